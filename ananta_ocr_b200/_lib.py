@@ -1,0 +1,193 @@
+"""ctypes binding of libdash_b200.so (the C ABI declared in include/dash_b200.h).
+
+The structures below mirror the header field by field; ``check_abi()`` compares
+their sizes with the library's own ``sizeof`` values.  Loading fails loudly:
+there is no CPU or eager fallback behind this module.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libdash_b200.so")
+
+DASH_OK = 0
+DASH_ERR_INVALID = 1
+DASH_ERR_UNSUPPORTED = 2
+DASH_ERR_CUDA = 3
+DASH_ERR_WORKSPACE = 4
+
+DASH_DEV_TIMEOUT = 1
+DASH_DEV_BAD_BLOCK = 2
+DASH_DEV_BAD_PAGE = 3
+
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
+DTYPE_F16 = 2
+
+_p = C.c_void_p
+_i32 = C.c_int32
+_i64 = C.c_int64
+_f32 = C.c_float
+
+
+class DashDeviceError(C.Structure):
+    _fields_ = [("code", _i32), ("where", _i32), ("info", _i64)]
+
+
+class DashSeqs(C.Structure):
+    _fields_ = [("n_seq", _i32), ("q_len_fixed", _i32), ("kv_len_fixed", _i32),
+                ("max_q_len", _i32), ("q_start", _p), ("pos0", _p), ("kv_len", _p)]
+
+
+class DashKV(C.Structure):
+    _fields_ = [("k", _p), ("v", _p), ("dtype", _i32), ("n_kv_heads", _i32),
+                ("head_dim", _i32), ("pad0", _i32), ("stride_seq", _i64),
+                ("stride_tok", _i64), ("stride_head", _i64), ("block_table", _p),
+                ("bt_stride", _i64), ("num_pages", _i64)]
+
+
+class DashRoutes(C.Structure):
+    _fields_ = [("idx", _p), ("bias", _p), ("row_stride", _i64), ("ihead_stride", _i64),
+                ("K", _i32), ("n_index_heads", _i32)]
+
+
+class DashQO(C.Structure):
+    _fields_ = [("q", _p), ("out", _p), ("q_stride_seq", _i64), ("q_stride_tok", _i64),
+                ("q_stride_head", _i64), ("o_stride_seq", _i64), ("o_stride_tok", _i64),
+                ("o_stride_head", _i64), ("n_heads", _i32), ("pad0", _i32), ("lse", _p),
+                ("lse_stride_seq", _i64), ("lse_stride_tok", _i64), ("lse_stride_head", _i64)]
+
+
+class DashKbarArgs(C.Structure):
+    _fields_ = [("keys", _p), ("dtype", _i32), ("d", _i32), ("block_size", _i32),
+                ("n_seq", _i32), ("seq_len", _i32), ("n_plan", _i32), ("tok_stride", _i64),
+                ("seq_stride", _i64), ("page_stride", _i64), ("kbar_seq_rows", _i64),
+                ("head_cls", _p), ("pages", _p), ("ntok", _p), ("kbar", _p),
+                ("kbar_row_stride", _i64)]
+
+
+class DashRouteArgs(C.Structure):
+    _fields_ = [("seqs", DashSeqs), ("idx_q", _p), ("q_row_stride", _i64), ("kbar", _p),
+                ("kbar_row_stride", _i64), ("block_table", _p), ("bt_stride", _i64),
+                ("kbar_seq_rows", _i64), ("num_kbar_rows", _i64), ("width", _i32),
+                ("d", _i32), ("scores_in", _p), ("scores_in_stride", _i64),
+                ("scores_out", _p), ("scores_out_stride", _i64), ("cand", _p),
+                ("cand_row_stride", _i64), ("cand_per_seq", _i32), ("block_size", _i32),
+                ("local_blocks", _i32), ("topm", _i32), ("K", _i32), ("out_width", _i32),
+                ("idx_scale", _f32), ("prior_floor", _f32), ("inv_sigma", _f32),
+                ("pad0", _i32), ("out_idx", _p), ("out_bias", _p), ("out_stride", _i64),
+                ("out_count", _p), ("device_error", _p)]
+
+
+class DashBlockMaxArgs(C.Structure):
+    _fields_ = [("q", _p), ("q_stride_b", _i64), ("q_stride_c", _i64), ("k", _p),
+                ("k_stride_b", _i64), ("k_stride_j", _i64), ("pos", _p),
+                ("pos_stride_b", _i64), ("pos_stride_c", _i64), ("seg", _p),
+                ("seg_stride_b", _i64), ("seg_stride_c", _i64), ("B", _i32), ("C", _i32),
+                ("Sk", _i32), ("d", _i32), ("block_size", _i32), ("nblk", _i32),
+                ("local_window", _i32), ("clamp", _i32), ("empty", _f32), ("pad0", _i32),
+                ("out", _p), ("out_stride_b", _i64), ("out_stride_c", _i64)]
+
+
+class DashPrefillArgs(C.Structure):
+    _fields_ = [("seqs", DashSeqs), ("kv", DashKV), ("routes", DashRoutes), ("qo", DashQO),
+                ("seg_start", _p), ("scale", _f32), ("block_size", _i32),
+                ("local_window", _i32), ("pad0", _i32), ("workspace", _p),
+                ("workspace_bytes", C.c_size_t), ("device_error", _p)]
+
+
+class DashDecodeArgs(C.Structure):
+    _fields_ = [("seqs", DashSeqs), ("kv", DashKV), ("routes", DashRoutes), ("qo", DashQO),
+                ("scale", _f32), ("block_size", _i32), ("local_window", _i32),
+                ("num_splits", _i32), ("workspace", _p), ("workspace_bytes", C.c_size_t),
+                ("device_error", _p)]
+
+
+ABI_ORDER = [DashSeqs, DashKV, DashRoutes, DashQO, DashKbarArgs, DashRouteArgs,
+             DashBlockMaxArgs, DashPrefillArgs, DashDecodeArgs, DashDeviceError]
+
+# every function the header declares
+EXPORTS = [
+    "dash_kbar_pool", "dash_route", "dash_block_max", "dash_prefill_workspace_size",
+    "dash_prefill_attn", "dash_decode_workspace_size", "dash_decode_attn", "dash_last_error",
+    "dash_library_version", "dash_count_launches", "dash_abi_sizes",
+]
+
+
+class DashError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"dash status {code}: {msg}")
+        self.code = code
+
+
+_lib = None
+
+
+def load(path: str = LIB_PATH):
+    """Load the library (once).  Raises if it is missing: no fallback exists."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise RuntimeError(
+            f"{path} is missing; build it with `python -m ananta_ocr_b200.build` "
+            "(the DASH kernels have no CPU or eager fallback)")
+    L = C.CDLL(path)
+    for name, args in [
+        ("dash_kbar_pool", [C.POINTER(DashKbarArgs), _p]),
+        ("dash_route", [C.POINTER(DashRouteArgs), _p]),
+        ("dash_block_max", [C.POINTER(DashBlockMaxArgs), _p]),
+        ("dash_prefill_attn", [C.POINTER(DashPrefillArgs), _p]),
+        ("dash_decode_attn", [C.POINTER(DashDecodeArgs), _p]),
+    ]:
+        f = getattr(L, name)
+        f.argtypes = args
+        f.restype = C.c_int
+    L.dash_prefill_workspace_size.argtypes = [C.POINTER(DashPrefillArgs)]
+    L.dash_prefill_workspace_size.restype = C.c_size_t
+    L.dash_decode_workspace_size.argtypes = [C.POINTER(DashDecodeArgs)]
+    L.dash_decode_workspace_size.restype = C.c_size_t
+    L.dash_last_error.argtypes = [C.c_char_p, C.c_int]
+    L.dash_last_error.restype = C.c_int
+    L.dash_library_version.restype = C.c_int
+    L.dash_count_launches.argtypes = [C.c_int]
+    L.dash_count_launches.restype = C.c_int
+    L.dash_abi_sizes.argtypes = [C.POINTER(_i64), C.c_int]
+    L.dash_abi_sizes.restype = C.c_int
+    _lib = L
+    check_abi()
+    return L
+
+
+def check_abi():
+    L = _lib
+    out = (_i64 * 10)()
+    n = L.dash_abi_sizes(out, 10)
+    for i, cls in enumerate(ABI_ORDER[:n]):
+        if C.sizeof(cls) != out[i]:
+            raise RuntimeError(f"ABI mismatch for {cls.__name__}: python {C.sizeof(cls)} "
+                               f"vs library {out[i]}")
+
+
+def last_error() -> str:
+    buf = C.create_string_buffer(512)
+    load().dash_last_error(buf, 512)
+    return buf.value.decode(errors="replace")
+
+
+def call(fn_name: str, args) -> None:
+    L = load()
+    rc = getattr(L, fn_name)(C.byref(args), current_stream())
+    if rc != DASH_OK:
+        raise DashError(rc, last_error())
+
+
+def current_stream():
+    import torch
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def launches(reset: bool = False) -> int:
+    return load().dash_count_launches(1 if reset else 0)

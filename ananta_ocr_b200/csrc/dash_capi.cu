@@ -1,0 +1,215 @@
+// dash_capi.cu -- the extern "C" boundary of libdash_b200.so: argument
+// validation (every malformed call returns a status and a message instead of
+// reaching a kernel), workspace sizing and kernel launches.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <atomic>
+
+#include "dash_internal.h"
+
+namespace dash {
+
+static thread_local char g_err[512] = {0};
+static std::atomic<int> g_launches{0};
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* kernel) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(DASH_ERR_CUDA, "%s launch failed: %s", kernel, cudaGetErrorString(e));
+  return DASH_OK;
+}
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+static int64_t seq_rows(const DashSeqs& q) {
+  // number of query rows; for the packed layout the host passes max_q_len and
+  // the row count through q_len_fixed = total rows (see DashSeqs contract)
+  return q.q_start ? (int64_t)q.q_len_fixed : (int64_t)q.n_seq * q.q_len_fixed;
+}
+
+static int check_seqs(const DashSeqs& q) {
+  if (q.n_seq < 0) return set_error(DASH_ERR_INVALID, "n_seq < 0");
+  if (q.q_len_fixed < 0) return set_error(DASH_ERR_INVALID, "q_len_fixed < 0");
+  if (q.q_start == nullptr && q.max_q_len < q.q_len_fixed)
+    return set_error(DASH_ERR_INVALID, "max_q_len < q_len_fixed");
+  if (q.kv_len == nullptr && q.kv_len_fixed < 0) return set_error(DASH_ERR_INVALID, "kv_len_fixed < 0");
+  return DASH_OK;
+}
+
+static int check_kv(const DashKV& kv, int n_heads, int block_size) {
+  if (!kv.k || !kv.v) return set_error(DASH_ERR_INVALID, "null K/V pointer");
+  if (kv.dtype != DASH_DTYPE_BF16 && kv.dtype != DASH_DTYPE_F16)
+    return set_error(DASH_ERR_UNSUPPORTED, "K/V dtype must be bf16 or fp16");
+  if (kv.head_dim != 128) return set_error(DASH_ERR_UNSUPPORTED, "head_dim %d != 128", kv.head_dim);
+  if (kv.n_kv_heads <= 0 || n_heads % kv.n_kv_heads != 0)
+    return set_error(DASH_ERR_INVALID, "n_heads %d not a multiple of n_kv_heads %d", n_heads, kv.n_kv_heads);
+  if (!aligned16(kv.k) || !aligned16(kv.v)) return set_error(DASH_ERR_INVALID, "K/V must be 16-byte aligned");
+  if (kv.stride_tok % 8 || kv.stride_head % 8 || kv.stride_seq % 8)
+    return set_error(DASH_ERR_INVALID, "K/V strides must be multiples of 8 elements");
+  if (kv.block_table && kv.num_pages <= 0) return set_error(DASH_ERR_INVALID, "num_pages must be > 0");
+  if (block_size <= 0) return set_error(DASH_ERR_INVALID, "block_size must be > 0");
+  return DASH_OK;
+}
+
+static int check_routes(const DashRoutes& r, int n_heads, int n_kv_heads) {
+  if (r.K < 0) return set_error(DASH_ERR_INVALID, "K < 0");
+  if (r.K > 0 && !r.idx) return set_error(DASH_ERR_INVALID, "null route idx");
+  if (r.K > 256) return set_error(DASH_ERR_UNSUPPORTED, "K %d > 256", r.K);
+  int nih = r.n_index_heads > 0 ? r.n_index_heads : 1;
+  if (n_heads % nih != 0 || n_kv_heads % nih != 0)
+    return set_error(DASH_ERR_INVALID, "n_index_heads %d must divide heads (%d) and kv heads (%d)", nih,
+                     n_heads, n_kv_heads);
+  return DASH_OK;
+}
+
+static int check_qo(const DashQO& qo) {
+  if (!qo.q || !qo.out) return set_error(DASH_ERR_INVALID, "null q/out");
+  if (!aligned16(qo.q) || !aligned16(qo.out)) return set_error(DASH_ERR_INVALID, "q/out must be 16-byte aligned");
+  if (qo.q_stride_tok % 8 || qo.q_stride_head % 8 || qo.q_stride_seq % 8 || qo.o_stride_tok % 8 ||
+      qo.o_stride_head % 8 || qo.o_stride_seq % 8)
+    return set_error(DASH_ERR_INVALID, "q/out strides must be multiples of 8 elements");
+  return DASH_OK;
+}
+
+}  // namespace dash
+
+using namespace dash;
+
+extern "C" {
+
+int dash_last_error(char* buf, int len) {
+  if (buf && len > 0) {
+    strncpy(buf, g_err, (size_t)len - 1);
+    buf[len - 1] = 0;
+  }
+  return (int)strlen(g_err);
+}
+
+int dash_library_version(void) { return (0 << 16) | 1; }
+
+int dash_count_launches(int reset) {
+  int v = g_launches.load();
+  if (reset) g_launches.store(0);
+  return v;
+}
+
+int dash_abi_sizes(int64_t* out, int n) {
+  const int64_t s[10] = {(int64_t)sizeof(DashSeqs),        (int64_t)sizeof(DashKV),
+                         (int64_t)sizeof(DashRoutes),      (int64_t)sizeof(DashQO),
+                         (int64_t)sizeof(DashKbarArgs),    (int64_t)sizeof(DashRouteArgs),
+                         (int64_t)sizeof(DashBlockMaxArgs), (int64_t)sizeof(DashPrefillArgs),
+                         (int64_t)sizeof(DashDecodeArgs),  (int64_t)sizeof(DashDeviceError)};
+  for (int i = 0; i < n && i < 10; ++i) out[i] = s[i];
+  return 10;
+}
+
+int dash_kbar_pool(const DashKbarArgs* a, dash_stream_t stream) {
+  if (!a) return set_error(DASH_ERR_INVALID, "null args");
+  if (!a->keys || !a->kbar) return set_error(DASH_ERR_INVALID, "null keys/kbar");
+  if (a->dtype != DASH_DTYPE_F32 && a->dtype != DASH_DTYPE_BF16)
+    return set_error(DASH_ERR_UNSUPPORTED, "k-bar keys must be fp32 or bf16");
+  if (a->d <= 0 || a->d > 256) return set_error(DASH_ERR_UNSUPPORTED, "index dim %d not in (0, 256]", a->d);
+  if (a->block_size <= 0 || a->block_size > 256)
+    return set_error(DASH_ERR_UNSUPPORTED, "block_size %d not in (0, 256]", a->block_size);
+  if (a->pages && !a->ntok) return set_error(DASH_ERR_INVALID, "paged plan needs ntok");
+  if (!a->pages && (a->n_seq < 0 || a->seq_len < 0)) return set_error(DASH_ERR_INVALID, "bad n_seq/seq_len");
+  return launch_kbar(*a, (cudaStream_t)stream);
+}
+
+int dash_route(const DashRouteArgs* a, dash_stream_t stream) {
+  if (!a) return set_error(DASH_ERR_INVALID, "null args");
+  int rc = check_seqs(a->seqs);
+  if (rc) return rc;
+  if (!a->out_idx || !a->out_bias) return set_error(DASH_ERR_INVALID, "null outputs");
+  if (a->width <= 0) return set_error(DASH_ERR_INVALID, "width must be > 0");
+  if (a->width > 8192) return set_error(DASH_ERR_UNSUPPORTED, "width %d > 8192", a->width);
+  if (a->K <= 0 || a->out_width < a->K) return set_error(DASH_ERR_INVALID, "need 0 < K <= out_width");
+  int M = a->topm > 0 ? (a->topm < a->width ? a->topm : a->width) : a->width;
+  if (M > 256) return set_error(DASH_ERR_UNSUPPORTED, "entmax window %d > 256 (set topm)", M);
+  if (!a->scores_in) {
+    if (!a->idx_q || !a->kbar) return set_error(DASH_ERR_INVALID, "null idx_q/kbar");
+    if (a->d != 128) return set_error(DASH_ERR_UNSUPPORTED, "index dim %d != 128", a->d);
+    if (!aligned16(a->kbar) || a->kbar_row_stride % 4) return set_error(DASH_ERR_INVALID, "k-bar must be 16-byte aligned rows");
+    if (a->num_kbar_rows <= 0) return set_error(DASH_ERR_INVALID, "num_kbar_rows must be > 0");
+    if (a->block_size <= 0) return set_error(DASH_ERR_INVALID, "block_size must be > 0");
+  }
+  return launch_route(*a, seq_rows(a->seqs), (cudaStream_t)stream);
+}
+
+int dash_block_max(const DashBlockMaxArgs* a, dash_stream_t stream) {
+  if (!a) return set_error(DASH_ERR_INVALID, "null args");
+  if (!a->q || !a->k || !a->pos || !a->out) return set_error(DASH_ERR_INVALID, "null pointer");
+  if (a->d <= 0 || a->d > 256) return set_error(DASH_ERR_UNSUPPORTED, "dim %d not in (0, 256]", a->d);
+  if (a->block_size <= 0 || a->block_size > 128)
+    return set_error(DASH_ERR_UNSUPPORTED, "block_size %d not in (0, 128]", a->block_size);
+  if (a->B < 0 || a->C < 0 || a->Sk < 0 || a->nblk < 0) return set_error(DASH_ERR_INVALID, "negative size");
+  return launch_block_max(*a, (cudaStream_t)stream);
+}
+
+size_t dash_prefill_workspace_size(const DashPrefillArgs* a) {
+  if (!a) return 0;
+  return prefill_workspace(*a, seq_rows(a->seqs));
+}
+
+int dash_prefill_attn(const DashPrefillArgs* a, dash_stream_t stream) {
+  if (!a) return set_error(DASH_ERR_INVALID, "null args");
+  int rc = check_seqs(a->seqs);
+  if (!rc) rc = check_kv(a->kv, a->qo.n_heads, a->block_size);
+  if (!rc) rc = check_routes(a->routes, a->qo.n_heads, a->kv.n_kv_heads);
+  if (!rc) rc = check_qo(a->qo);
+  if (rc) return rc;
+  const int G = a->qo.n_heads / a->kv.n_kv_heads;
+  if (G != 1 && G != 2 && G != 4 && G != 8 && G != 16)
+    return set_error(DASH_ERR_UNSUPPORTED, "query heads per kv head %d not in {1,2,4,8,16}", G);
+  if (a->block_size % 64 != 0 || a->block_size > 256)
+    return set_error(DASH_ERR_UNSUPPORTED, "prefill block_size %d not in {64,128,192,256}", a->block_size);
+  if (a->local_window < 0) return set_error(DASH_ERR_INVALID, "local_window must be >= 0");
+  if (a->kv.block_table == nullptr && a->seqs.kv_len_fixed <= 0)
+    return set_error(DASH_ERR_INVALID, "contiguous K/V needs kv_len_fixed (allocated length)");
+  int64_t rows = seq_rows(a->seqs);
+  size_t need = prefill_workspace(*a, rows);
+  if (need && (!a->workspace || a->workspace_bytes < need))
+    return set_error(DASH_ERR_WORKSPACE, "prefill workspace %zu bytes needed, %zu given", need,
+                     a->workspace_bytes);
+  return launch_prefill(*a, rows, (cudaStream_t)stream);
+}
+
+size_t dash_decode_workspace_size(const DashDecodeArgs* a) {
+  if (!a) return 0;
+  int64_t rows = seq_rows(a->seqs);
+  int sp = a->num_splits > 0 ? a->num_splits : decode_auto_splits(*a, rows);
+  return decode_workspace(*a, rows, sp);
+}
+
+int dash_decode_attn(const DashDecodeArgs* a, dash_stream_t stream) {
+  if (!a) return set_error(DASH_ERR_INVALID, "null args");
+  int rc = check_seqs(a->seqs);
+  if (!rc) rc = check_kv(a->kv, a->qo.n_heads, a->block_size);
+  if (!rc) rc = check_routes(a->routes, a->qo.n_heads, a->kv.n_kv_heads);
+  if (!rc) rc = check_qo(a->qo);
+  if (rc) return rc;
+  if (a->local_window < 0) return set_error(DASH_ERR_INVALID, "local_window must be >= 0");
+  if (a->routes.K + a->local_window / a->block_size + 2 > 480)
+    return set_error(DASH_ERR_UNSUPPORTED, "too many blocks per decode row");
+  int64_t rows = seq_rows(a->seqs);
+  int sp = a->num_splits > 0 ? a->num_splits : decode_auto_splits(*a, rows);
+  if (sp > 64) return set_error(DASH_ERR_UNSUPPORTED, "num_splits %d > 64", sp);
+  size_t need = decode_workspace(*a, rows, sp);
+  if (need && (!a->workspace || a->workspace_bytes < need))
+    return set_error(DASH_ERR_WORKSPACE, "decode workspace %zu bytes needed, %zu given", need,
+                     a->workspace_bytes);
+  return launch_decode(*a, rows, sp, (cudaStream_t)stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,23 @@
+// dash_internal.h -- host-side glue shared by the translation units of
+// libdash_b200.so (error reporting, launch accounting, kernel launchers).
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+#include "../../include/dash_b200.h"
+
+namespace dash {
+
+int set_error(int code, const char* fmt, ...);   // stores the message, returns code
+int check_launch(const char* kernel);            // cudaGetLastError -> status
+void count_launch();
+
+int launch_kbar(const DashKbarArgs& a, cudaStream_t st);
+int launch_route(const DashRouteArgs& a, int64_t n_rows, cudaStream_t st);
+int launch_block_max(const DashBlockMaxArgs& a, cudaStream_t st);
+int launch_decode(const DashDecodeArgs& a, int64_t n_rows, int splits, cudaStream_t st);
+int launch_prefill(const DashPrefillArgs& a, int64_t n_rows, cudaStream_t st);
+size_t prefill_workspace(const DashPrefillArgs& a, int64_t n_rows);
+size_t decode_workspace(const DashDecodeArgs& a, int64_t n_rows, int splits);
+int decode_auto_splits(const DashDecodeArgs& a, int64_t n_rows);
+
+}  // namespace dash

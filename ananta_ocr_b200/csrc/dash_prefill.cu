@@ -1,0 +1,634 @@
+// dash_prefill.cu -- DASH prefill gather attention on sm_100a tensor cores.
+//
+// Work unit: one CTA per (tile of 128 query rows, kv head).  A tile row is a
+// (query token, query head of this kv head) pair; with G query heads per kv
+// head a tile covers 128/G consecutive tokens.  The tile walks, in ascending
+// order, every 64-key tile of the blocks that any of its rows routed to (the
+// per-tile union built by plan_kernel) plus the blocks of its local windows.
+// Per key tile:
+//   TMA (warp 4)      K and V tiles -> shared memory (128-byte swizzle), 3 stages
+//   MMA (warp 5)      S = Q K^T   (tcgen05.mma M=128 N=64,  fp32 in TMEM, 2 buffers)
+//                     O += P V    (tcgen05.mma M=128 N=128, fp32 in TMEM)
+//   softmax (w0-3)    one thread per row: S from TMEM, per-row mask + bias
+//                     (local window: no bias; routed block: + bias; else -inf),
+//                     online softmax in the exp2 domain with lazy rescaling of
+//                     O (only when the row max grows by > 2^8), P -> shared
+//                     memory (bf16/fp16, swizzled) for the PV MMA.
+// Rows that did not route a block of the union simply get P = 0 there.
+//
+// Semantics: sparse_gather_e2e_triton.py:34-115 (_e2e_attn_fwd_kernel),
+// sparse_gather_triton.py:29-104 (_gather_attn_fwd_kernel, seg/packing),
+// WHL attend_triton.py:88-292 (_dash_sparse_fwd_kernel, paged).
+#include <cudaTypedefs.h>
+#include "dash_common.cuh"
+#include "dash_internal.h"
+
+namespace dash {
+
+constexpr int BM = 128;          // tile rows (M of both MMAs)
+constexpr int BN = 64;           // keys per key tile (N of QK, K of PV)
+constexpr int HD = 128;          // head dim
+constexpr int NSTAGE = 3;
+constexpr int OFF_Q = 0;                          // 2 x [128 x 128 B]
+constexpr int OFF_K = 32768;                      // NSTAGE x 2 x [64 x 128 B]
+constexpr int OFF_V = OFF_K + NSTAGE * 16384;     // NSTAGE x 2 x [64 x 128 B]
+constexpr int OFF_P = OFF_V + NSTAGE * 16384;     // 2 x [128 x 128 B]
+constexpr int OFF_MASK = OFF_P + 2 * 16384;       // block mask words
+constexpr int MAX_MASK_WORDS = 256;               // <= 8192 blocks
+constexpr int OFF_BAR = OFF_MASK + MAX_MASK_WORDS * 4;
+constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;  // + alignment slack
+constexpr int NTHREADS = 192;
+constexpr uint32_t TMEM_COLS = 256;               // S0 | S1 | O
+constexpr int kPlanMaxK = 256;                    // routed slots per row
+
+struct PrefillPlan {
+  const int32_t* cidx;     // canonical lists [nih][n_rows][K]
+  const float* cbias;
+  const uint32_t* tmask;   // per-tile unions [nih][n_tiles][nwords]
+  int64_t n_rows;
+  int32_t nwords;
+  int32_t tiles_per_seq;
+  int32_t G;               // query heads per kv head
+  int32_t TT;              // tokens per tile (= 128 / G)
+  int32_t paged;
+  int32_t nblk_cap;
+};
+
+__device__ __forceinline__ void seq_of_row(const DashSeqs& q, int64_t r, int& s, int& i) {
+  if (q.q_start == nullptr) {
+    s = (int)(r / q.q_len_fixed);
+    i = (int)(r - (int64_t)s * q.q_len_fixed);
+    return;
+  }
+  int lo = 0, hi = q.n_seq - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (q.q_start[mid] <= r) lo = mid; else hi = mid - 1;
+  }
+  s = lo;
+  i = (int)(r - q.q_start[lo]);
+}
+__device__ __forceinline__ int kv_len_of(const DashSeqs& q, int s) {
+  return q.kv_len ? q.kv_len[s] : q.kv_len_fixed;
+}
+__device__ __forceinline__ int q_len_of(const DashSeqs& q, int s) {
+  return q.q_start ? q.q_start[s + 1] - q.q_start[s] : q.q_len_fixed;
+}
+__device__ __forceinline__ int pos0_of(const DashSeqs& q, int s) {
+  return q.pos0 ? q.pos0[s] : kv_len_of(q, s) - q_len_of(q, s);
+}
+__device__ __forceinline__ int64_t row_base(const DashSeqs& q, int s) {
+  return q.q_start ? (int64_t)q.q_start[s] : (int64_t)s * q.q_len_fixed;
+}
+
+// ---------------------------------------------------------------------------
+// plan_kernel: one warp per (query row, index head).  Canonicalises the routed
+// list (drops -1, ids without a remote key for this row, later duplicates;
+// sorts ascending) and ORs the kept ids into the row's tile union.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) plan_kernel(DashPrefillArgs a, PrefillPlan p,
+                                                   int32_t* cidx, float* cbias,
+                                                   uint32_t* tmask) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * 4 + warp;
+  const int ih = blockIdx.y;
+  if (r >= p.n_rows) return;
+  int s, i;
+  seq_of_row(a.seqs, r, s, i);
+  const int kvl = kv_len_of(a.seqs, s);
+  const int64_t pos = (int64_t)pos0_of(a.seqs, s) + i;
+  const int64_t lstart = pos - a.local_window + 1;
+  const int nblk_seq = (kvl + a.block_size - 1) / a.block_size;
+  const int K = a.routes.K;
+  const int32_t* il = a.routes.idx + r * a.routes.row_stride + (int64_t)ih * a.routes.ihead_stride;
+  const float* bl = a.routes.bias ? a.routes.bias + r * a.routes.row_stride +
+                                        (int64_t)ih * a.routes.ihead_stride
+                                  : nullptr;
+  int32_t* oi = cidx + ((int64_t)ih * p.n_rows + r) * K;
+  float* ob = cbias + ((int64_t)ih * p.n_rows + r) * K;
+  const int tile = s * p.tiles_per_seq + i / p.TT;
+  uint32_t* tm = tmask + ((int64_t)ih * a.seqs.n_seq * p.tiles_per_seq + tile) * p.nwords;
+  __shared__ int32_t s_id[4][kPlanMaxK];   // kept id per slot, -1 when dropped
+  int32_t* sid = s_id[warp];
+  // pass 1: keep ids with a remote key for this row, drop later duplicates
+  for (int j = lane; j < K; j += 32) sid[j] = il[j];
+  __syncwarp();
+  for (int j = lane; j < K; j += 32) {
+    const int b = sid[j];
+    bool ok = b >= 0 && b < nblk_seq && b < p.nblk_cap && (int64_t)b * a.block_size < lstart;
+    if (b >= nblk_seq) record_error(a.device_error, DASH_DEV_BAD_BLOCK, 30, b);
+    if (ok)
+      for (int u = 0; u < j; ++u) ok &= sid[u] != b;
+    // Dropped slots become a distinct negative marker.  Validity depends only
+    // on the id, so a later duplicate of a dropped id is dropped by the same
+    // test, and a kept id is never rewritten: concurrent reads stay exact.
+    if (!ok) sid[j] = -1 - j;
+  }
+  __syncwarp();
+  // pass 2: rank the kept ids (distinct) and write the ascending list
+  int nk = 0;
+  for (int j0 = 0; j0 < K; j0 += 32) {
+    const int j = j0 + lane;
+    const int b = j < K ? sid[j] : -1;
+    const bool ok = b >= 0;
+    int rank = 0;
+    if (ok)
+      for (int u = 0; u < K; ++u) rank += sid[u] >= 0 && sid[u] < b;
+    if (ok) {
+      oi[rank] = b;
+      ob[rank] = bl ? bl[j] : 0.0f;
+      atomicOr(tm + (b >> 5), 1u << (b & 31));
+    }
+    nk += __popc(__ballot_sync(0xffffffffu, ok));
+  }
+  for (int j = nk + lane; j < K; j += 32) { oi[j] = -1; ob[j] = 0.0f; }
+}
+
+// ---------------------------------------------------------------------------
+// Key-tile iterator over the shared block mask (ascending).
+// ---------------------------------------------------------------------------
+struct TileIter {
+  int w, b, half;
+  uint32_t bits;
+};
+__device__ __forceinline__ int next_tile(TileIter& t, const uint32_t* mask, int nwords, int bs,
+                                         int64_t pmax, int kvl) {
+  const int halves = bs / BN;
+  while (true) {
+    if (t.half + 1 < halves && t.b >= 0) {
+      t.half++;
+    } else {
+      while (t.bits == 0) {
+        if (++t.w >= nwords) return -1;
+        t.bits = mask[t.w];
+      }
+      int bit = __ffs(t.bits) - 1;
+      t.bits &= t.bits - 1;
+      t.b = t.w * 32 + bit;
+      t.half = 0;
+    }
+    int64_t kt0 = (int64_t)t.b * bs + t.half * BN;
+    if (kt0 > pmax || kt0 >= kvl) continue;
+    return (int)kt0;
+  }
+}
+
+template <typename T, bool PAGED>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    prefill_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                   const DashPrefillArgs a, const PrefillPlan p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint32_t* smask = reinterpret_cast<uint32_t*>(sm + OFF_MASK);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
+  uint64_t* kv_full = bars + 0;      // [NSTAGE]
+  uint64_t* kv_empty = bars + 3;     // [NSTAGE]
+  uint64_t* s_full = bars + 6;       // [2]
+  uint64_t* s_free = bars + 8;       // [2]
+  uint64_t* p_full = bars + 10;      // [2]
+  uint64_t* pv_done = bars + 12;     // [2]
+  uint64_t* q_full = bars + 14;
+  uint64_t* mma_done = bars + 15;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 17);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_seq = a.seqs.n_seq;
+  // heaviest (last) tiles first
+  const int jj = blockIdx.x / n_seq;
+  const int s = blockIdx.x - jj * n_seq;
+  const int tj = p.tiles_per_seq - 1 - jj;
+  const int hk = blockIdx.y;
+  const int qlen = q_len_of(a.seqs, s);
+  const int i0 = tj * p.TT;
+  if (i0 >= qlen) return;
+  const int kvl = kv_len_of(a.seqs, s);
+  const int pos0 = pos0_of(a.seqs, s);
+  const int ntok = min(p.TT, qlen - i0);
+  const int64_t pmin = (int64_t)pos0 + i0, pmax = pmin + ntok - 1;
+  const int G = p.G;
+  const int H = a.qo.n_heads;
+  const int nih = a.routes.n_index_heads > 0 ? a.routes.n_index_heads : 1;
+  const int ih = (hk * G) / (H / nih);
+  const int bs = a.block_size;
+
+  // ---- setup: barriers, TMEM, block mask ----
+  if (tid == 0) {
+    for (int k = 0; k < NSTAGE; ++k) { mbar_init(kv_full + k, 1); mbar_init(kv_empty + k, 1); }
+    for (int k = 0; k < 2; ++k) {
+      mbar_init(s_full + k, 1); mbar_init(s_free + k, 128);
+      mbar_init(p_full + k, 128); mbar_init(pv_done + k, 1);
+    }
+    mbar_init(q_full, 128);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    mbar_init_fence();
+  }
+  if (warp == 5) { tmem_alloc(tmem_holder, TMEM_COLS); tmem_relinquish(); }
+  {
+    const uint32_t* um = p.tmask + ((int64_t)ih * n_seq * p.tiles_per_seq + (int64_t)s * p.tiles_per_seq + tj) * p.nwords;
+    const int64_t lb0 = max((int64_t)0, (pmin - a.local_window + 1) / bs);
+    const int64_t lb1 = pmax / bs;
+    for (int w = tid; w < p.nwords; w += NTHREADS) {
+      uint32_t m = um[w];
+      int64_t b0 = (int64_t)w * 32;
+      for (int k = 0; k < 32; ++k) {
+        int64_t b = b0 + k;
+        if (b >= lb0 && b <= lb1) m |= 1u << k;
+      }
+      smask[w] = m;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const uint32_t tS = tmem, tO = tmem + 128;
+  DeviceError* derr = a.device_error;
+
+  if (warp == 4) {
+    // =================== TMA producer ===================
+    if (lane == 0) {
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      TileIter itr{-1, -1, 0, 0u};
+      int it = 0;
+      while (true) {
+        int kt0 = next_tile(itr, smask, p.nwords, bs, pmax, kvl);
+        if (kt0 < 0) break;
+        const int st = it % NSTAGE;
+        if (it >= NSTAGE && !mbar_wait(kv_empty + st, ((it / NSTAGE) - 1) & 1, abort_flag, derr, 40)) break;
+        uint8_t* dK = sm + OFF_K + st * 16384;
+        uint8_t* dV = sm + OFF_V + st * 16384;
+        int c1, c3;
+        bool ok = true;
+        if (PAGED) {
+          int64_t page = a.kv.block_table[(int64_t)s * a.kv.bt_stride + kt0 / bs];
+          if (page < 0 || page >= a.kv.num_pages) {
+            record_error(derr, DASH_DEV_BAD_PAGE, 41, page);
+            ok = false;
+          }
+          c1 = kt0 % bs;
+          c3 = (int)page;
+        } else {
+          c1 = kt0;
+          c3 = s;
+        }
+        if (ok) {
+          mbar_arrive_expect_tx(kv_full + st, 4 * 8192);
+          tma_load_4d(dK, &tmK, kv_full + st, 0, c1, hk, c3);
+          tma_load_4d(dK + 8192, &tmK, kv_full + st, 64, c1, hk, c3);
+          tma_load_4d(dV, &tmV, kv_full + st, 0, c1, hk, c3);
+          tma_load_4d(dV + 8192, &tmV, kv_full + st, 64, c1, hk, c3);
+        } else {
+          mbar_arrive(kv_full + st);
+        }
+        ++it;
+      }
+      // drain: never leave the CTA with bulk copies in flight
+      for (int k = max(0, it - NSTAGE); k < it; ++k) {
+        volatile int no_abort = 0;
+        mbar_wait(kv_full + (k % NSTAGE), (k / NSTAGE) & 1, &no_abort, nullptr, 42);
+      }
+    }
+  } else if (warp == 5) {
+    // =================== MMA issuer ===================
+    if (lane == 0) {
+      constexpr uint32_t fmt = DType<T>::fmt;
+      constexpr uint32_t idesc_qk = make_idesc(fmt, 0, 0, BM, BN);
+      constexpr uint32_t idesc_pv = make_idesc(fmt, 0, 1, BM, HD);
+      const uint32_t sQ = smem_u32(sm + OFF_Q);
+      bool alive = mbar_wait(q_full, 0, abort_flag, derr, 50);
+      TileIter itr{-1, -1, 0, 0u};
+      int it = 0;
+      auto issue_pv = [&](int j) -> bool {
+        const int pb = j & 1;
+        if (!mbar_wait(p_full + pb, (j >> 1) & 1, abort_flag, derr, 51)) return false;
+        tc_fence_after();
+        const uint32_t sP = smem_u32(sm + OFF_P + pb * 16384);
+        const uint32_t sV = smem_u32(sm + OFF_V + (j % NSTAGE) * 16384);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          uint64_t ad = sw128_desc(sP + kk * 32, 16, 1024);
+          uint64_t bd = sw128_desc(sV + kk * 2048, 8192, 1024);
+          umma_ss(tO, ad, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(pv_done + pb);
+        umma_commit(kv_empty + (j % NSTAGE));
+        return true;
+      };
+      while (alive) {
+        int kt0 = next_tile(itr, smask, p.nwords, bs, pmax, kvl);
+        if (kt0 < 0) break;
+        const int st = it % NSTAGE, sb = it & 1;
+        if (!mbar_wait(kv_full + st, (it / NSTAGE) & 1, abort_flag, derr, 52)) { alive = false; break; }
+        if (it >= 2 && !mbar_wait(s_free + sb, ((it >> 1) - 1) & 1, abort_flag, derr, 53)) { alive = false; break; }
+        tc_fence_after();
+        const uint32_t sK = smem_u32(sm + OFF_K + st * 16384);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          uint64_t ad = sw128_desc(sQ + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+          uint64_t bd = sw128_desc(sK + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
+          umma_ss(tS + sb * BN, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full + sb);
+        if (it >= 1 && !issue_pv(it - 1)) { alive = false; break; }
+        ++it;
+      }
+      if (alive && it >= 1) issue_pv(it - 1);
+      // all MMAs of this CTA complete before TMEM is released
+      umma_commit(mma_done);
+      volatile int no_abort = 0;
+      mbar_wait(mma_done, 0, &no_abort, nullptr, 54);
+    }
+    __syncwarp();
+  } else {
+    // =================== softmax / epilogue (one thread per row) ===================
+    const int m = tid;                       // row 0..127
+    const int tok = i0 + m / G;
+    const int hq = hk * G + (m % G);
+    const bool row_ok = (m / G) < ntok;
+    const int64_t pos = row_ok ? (int64_t)pos0 + tok : -1;
+    const int64_t lstart = pos - a.local_window + 1;
+    const int64_t rglob = row_base(a.seqs, s) + tok;
+    const int64_t segs = (row_ok && a.seg_start) ? (int64_t)a.seg_start[rglob] : 0;
+    // ---- Q row -> shared (swizzled K-major) ----
+    {
+      const T* qp = reinterpret_cast<const T*>(a.qo.q) +
+                    (a.seqs.q_start ? rglob * a.qo.q_stride_tok
+                                    : (int64_t)s * a.qo.q_stride_seq + (int64_t)tok * a.qo.q_stride_tok) +
+                    (int64_t)hq * a.qo.q_stride_head;
+      uint8_t* sq = sm + OFF_Q;
+#pragma unroll
+      for (int cc = 0; cc < 16; ++cc) {
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (row_ok) v = *reinterpret_cast<const uint4*>(qp + cc * 8);
+        const int region = cc >> 3, c8 = cc & 7;
+        *reinterpret_cast<uint4*>(sq + region * 16384 + m * 128 + ((c8 ^ (m & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(q_full);
+    }
+    // routed list cursor
+    const int K = a.routes.K;
+    const int32_t* rl = p.cidx + ((int64_t)ih * p.n_rows + rglob) * K;
+    const float* rbl = p.cbias + ((int64_t)ih * p.n_rows + rglob) * K;
+    const bool has_bias = a.routes.bias != nullptr;
+    int cur_j = 0;
+    int cur_b = (row_ok && K > 0) ? rl[0] : -1;
+    float cur_bias = (row_ok && K > 0 && has_bias) ? rbl[0] : 0.0f;
+    const float sl2 = a.scale * 1.4426950408889634f;
+    const float LOG2E = 1.4426950408889634f;
+    float m_run = -INFINITY, l_run = 0.0f;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    TileIter itr{-1, -1, 0, 0u};
+    int it = 0;
+    bool alive = true;
+    while (alive) {
+      int kt0 = next_tile(itr, smask, p.nwords, bs, pmax, kvl);
+      if (kt0 < 0) break;
+      const int st = it % NSTAGE, sb = it & 1;
+      const int blk = kt0 / bs;
+      // zero V rows past the end of the sequence (never multiply garbage by P = 0)
+      if (kt0 + BN > kvl) {
+        if (!mbar_wait(kv_full + st, (it / NSTAGE) & 1, abort_flag, derr, 60)) { alive = false; break; }
+        const int r0 = kvl - kt0;
+        uint8_t* dV = sm + OFF_V + st * 16384;
+        for (int e = m; e < (BN - r0) * 16; e += 128) {
+          const int row = r0 + e / 16, ch = e % 16;
+          *reinterpret_cast<uint4*>(dV + (ch >> 3) * 8192 + row * 128 + ((ch & 7) << 4)) = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();
+      }
+      // advance the routed-list cursor to this block
+      while (cur_b >= 0 && cur_b < blk) {
+        ++cur_j;
+        cur_b = cur_j < K ? rl[cur_j] : -1;
+        cur_bias = (cur_j < K && has_bias) ? rbl[cur_j] : 0.0f;
+      }
+      const bool sel = cur_b == blk;
+      const float b2 = sel ? cur_bias * LOG2E : 0.0f;
+      if (!mbar_wait(s_full + sb, (it >> 1) & 1, abort_flag, derr, 61)) { alive = false; break; }
+      tc_fence_after();
+      uint32_t sr[64];
+      {
+        uint32_t (&r0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sr[0]);
+        uint32_t (&r1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sr[32]);
+        tmem_ld32(tS + sb * BN + lane_base, r0);
+        tmem_ld32(tS + sb * BN + 32 + lane_base, r1);
+        tmem_ld_wait();
+      }
+      tc_fence_before();
+      mbar_arrive(s_free + sb);
+      // logits (exp2 domain) with the DASH mask
+      const int64_t hi = pos - kt0;                 // last causal column
+      const int64_t lo_loc = lstart - kt0;          // first local column
+      const int64_t lo_seg = segs - kt0;
+      float x[64];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        float v = __uint_as_float(sr[c]) * sl2;
+        float lg = (c >= lo_loc) ? v : (sel ? v + b2 : -INFINITY);
+        lg = (c > hi || c < lo_seg) ? -INFINITY : lg;
+        x[c] = lg;
+        mx = fmaxf(mx, lg);
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const bool need = m_new > m_run + 8.0f || (m_run == -INFINITY && m_new != -INFINITY);
+      const bool warp_need = __any_sync(0xffffffffu, need);
+      if (warp_need) {
+        if (it > 0) {
+          if (!mbar_wait(pv_done + ((it - 1) & 1), ((it - 1) >> 1) & 1, abort_flag, derr, 62)) { alive = false; break; }
+          tc_fence_after();
+          const float f = need ? (m_run == -INFINITY ? 0.0f : fast_exp2(m_run - m_new)) : 1.0f;
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            uint32_t o[32];
+            tmem_ld32(tO + q4 * 32 + lane_base, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * f);
+            tmem_st32(tO + q4 * 32 + lane_base, o);
+          }
+          tmem_st_wait();
+          l_run *= f;
+        }
+        if (need) m_run = m_new;
+      }
+      const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
+      float ls = 0.0f;
+      uint32_t pk[32];
+#pragma unroll
+      for (int c = 0; c < 64; c += 2) {
+        float p0 = fast_exp2(x[c] - m_use);
+        float p1 = fast_exp2(x[c + 1] - m_use);
+        ls += p0 + p1;
+        pk[c >> 1] = pack2(p0, p1, (T*)nullptr);
+      }
+      l_run += ls;
+      // P buffer sb was last read by PV(it-2)
+      if (it >= 2 && !mbar_wait(pv_done + sb, ((it - 2) >> 1) & 1, abort_flag, derr, 63)) { alive = false; break; }
+      uint8_t* dP = sm + OFF_P + sb * 16384 + m * 128;
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8)
+        *reinterpret_cast<uint4*>(dP + ((c8 ^ (m & 7)) << 4)) =
+            make_uint4(pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full + sb);
+      ++it;
+    }
+    // ---- epilogue ----
+    float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+    bool have_o = alive && it > 0;
+    if (have_o && !mbar_wait(pv_done + ((it - 1) & 1), ((it - 1) >> 1) & 1, abort_flag, derr, 64)) have_o = false;
+    tc_fence_after();
+    T* op = reinterpret_cast<T*>(a.qo.out) +
+            (a.seqs.q_start ? rglob * a.qo.o_stride_tok
+                            : (int64_t)s * a.qo.o_stride_seq + (int64_t)tok * a.qo.o_stride_tok) +
+            (int64_t)hq * a.qo.o_stride_head;
+#pragma unroll
+    for (int q4 = 0; q4 < 4; ++q4) {
+      uint32_t o[32];
+      tmem_ld32(tO + q4 * 32 + lane_base, o);
+      tmem_ld_wait();
+      if (row_ok) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          float a0 = have_o ? __uint_as_float(o[c]) * inv_l : 0.0f;
+          float a1 = have_o ? __uint_as_float(o[c + 1]) * inv_l : 0.0f;
+          pk[c >> 1] = pack2(a0, a1, (T*)nullptr);
+        }
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          *reinterpret_cast<uint4*>(op + q4 * 32 + v * 8) = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+      }
+    }
+    if (row_ok && a.qo.lse) {
+      float lse = l_run > 0.0f ? (m_run + log2f(l_run)) * 0.6931471805599453f : -INFINITY;
+      a.qo.lse[(a.seqs.q_start ? rglob * a.qo.lse_stride_tok
+                               : (int64_t)s * a.qo.lse_stride_seq + (int64_t)tok * a.qo.lse_stride_tok) +
+               (int64_t)hq * a.qo.lse_stride_head] = lse;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 5) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+static int make_kv_map(CUtensorMap* map, const void* base, const DashPrefillArgs& a, bool paged) {
+  auto enc = get_encode();
+  if (!enc) return set_error(DASH_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  const int esz = 2;
+  cuuint64_t dims[4], strides[3];
+  dims[0] = HD;
+  dims[1] = paged ? (cuuint64_t)a.block_size : (cuuint64_t)a.seqs.kv_len_fixed;
+  dims[2] = (cuuint64_t)a.kv.n_kv_heads;
+  dims[3] = paged ? (cuuint64_t)a.kv.num_pages : (cuuint64_t)a.seqs.n_seq;
+  strides[0] = (cuuint64_t)a.kv.stride_tok * esz;
+  strides[1] = (cuuint64_t)a.kv.stride_head * esz;
+  strides[2] = (cuuint64_t)a.kv.stride_seq * esz;
+  cuuint32_t box[4] = {64, (cuuint32_t)BN, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  for (int k = 0; k < 3; ++k)
+    if (strides[k] % 16 != 0 || strides[k] == 0)
+      return set_error(DASH_ERR_INVALID, "K/V strides must be non-zero multiples of 16 bytes");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0)
+    return set_error(DASH_ERR_INVALID, "K/V base must be 16-byte aligned");
+  CUresult r = enc(map, a.kv.dtype == DASH_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                   4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(DASH_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return DASH_OK;
+}
+
+static void plan_geometry(const DashPrefillArgs& a, int64_t n_rows, PrefillPlan& p) {
+  const int G = a.qo.n_heads / a.kv.n_kv_heads;
+  p.G = G;
+  p.TT = BM / G;
+  p.tiles_per_seq = (a.seqs.max_q_len + p.TT - 1) / p.TT;
+  p.paged = a.kv.block_table != nullptr;
+  p.nblk_cap = p.paged ? (int)a.kv.bt_stride
+                       : (a.seqs.kv_len_fixed + a.block_size - 1) / a.block_size;
+  p.nwords = (p.nblk_cap + 31) / 32;
+  p.n_rows = n_rows;
+}
+
+size_t prefill_workspace(const DashPrefillArgs& a, int64_t n_rows) {
+  PrefillPlan p{};
+  plan_geometry(a, n_rows, p);
+  const int nih = a.routes.n_index_heads > 0 ? a.routes.n_index_heads : 1;
+  size_t lists = (size_t)nih * n_rows * a.routes.K * 4;
+  lists = (lists + 255) & ~(size_t)255;
+  size_t masks = (size_t)nih * a.seqs.n_seq * p.tiles_per_seq * p.nwords * 4;
+  return 2 * lists + ((masks + 255) & ~(size_t)255);
+}
+
+int launch_prefill(const DashPrefillArgs& a, int64_t n_rows, cudaStream_t st) {
+  if (n_rows == 0 || a.seqs.n_seq == 0) return DASH_OK;
+  PrefillPlan p{};
+  plan_geometry(a, n_rows, p);
+  if (p.nwords > MAX_MASK_WORDS)
+    return set_error(DASH_ERR_UNSUPPORTED, "too many blocks per sequence (%d > %d)", p.nblk_cap,
+                     MAX_MASK_WORDS * 32);
+  const int nih = a.routes.n_index_heads > 0 ? a.routes.n_index_heads : 1;
+  size_t lists = (size_t)nih * n_rows * a.routes.K * 4;
+  lists = (lists + 255) & ~(size_t)255;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(a.workspace);
+  int32_t* cidx = reinterpret_cast<int32_t*>(ws);
+  float* cbias = reinterpret_cast<float*>(ws + lists);
+  uint32_t* tmask = reinterpret_cast<uint32_t*>(ws + 2 * lists);
+  size_t masks = (size_t)nih * a.seqs.n_seq * p.tiles_per_seq * p.nwords * 4;
+  cudaError_t e = cudaMemsetAsync(tmask, 0, masks, st);
+  if (e != cudaSuccess) return set_error(DASH_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+  p.cidx = cidx;
+  p.cbias = cbias;
+  p.tmask = tmask;
+  if (a.routes.K > 0) {
+    dim3 g1((unsigned)((n_rows + 3) / 4), nih);
+    plan_kernel<<<g1, 128, 0, st>>>(a, p, cidx, cbias, tmask);
+    count_launch();
+    int rc = check_launch("plan_kernel");
+    if (rc) return rc;
+  }
+  CUtensorMap mk, mv;
+  int rc = make_kv_map(&mk, a.kv.k, a, p.paged);
+  if (rc) return rc;
+  rc = make_kv_map(&mv, a.kv.v, a, p.paged);
+  if (rc) return rc;
+  dim3 grid((unsigned)(a.seqs.n_seq * p.tiles_per_seq), a.kv.n_kv_heads);
+  auto launch = [&](auto kern) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    kern<<<grid, NTHREADS, SMEM_BYTES, st>>>(mk, mv, a, p);
+  };
+  if (a.kv.dtype == DASH_DTYPE_BF16) {
+    if (p.paged) launch(prefill_kernel<__nv_bfloat16, true>);
+    else launch(prefill_kernel<__nv_bfloat16, false>);
+  } else {
+    if (p.paged) launch(prefill_kernel<__half, true>);
+    else launch(prefill_kernel<__half, false>);
+  }
+  count_launch();
+  return check_launch("prefill_kernel");
+}
+
+}  // namespace dash

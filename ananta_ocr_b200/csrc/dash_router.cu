@@ -1,0 +1,481 @@
+// dash_router.cu -- DASH router kernels (CUDA cores, fp32):
+//   kbar_pool_kernel   stage-0 head_cls pooling of index keys (k-bar)
+//   route_rows_kernel  block scores + candidate mask + 1.5-entmax + top-K + bias
+//   block_max_kernel   indexer-mode stage-0 block-max scores
+//
+// Bit-exactness: every dot product is a sequential __fmaf_rn chain over the
+// feature index and every other rounding step is spelled out, in the same
+// order as oracle/dash_oracle.c, so k-bar, block scores and the selected block
+// lists are bitwise equal to the CPU oracle.
+#include "dash_common.cuh"
+#include "dash_internal.h"
+
+namespace dash {
+
+constexpr float kScoreNeg = -1.0e9f;
+constexpr float kEntmaxNeg = -1.0e4f;
+
+// ---------------------------------------------------------------------------
+// k-bar pooling: one CTA per block (contiguous) or plan entry (paged).
+// Restates dash_attention.py:863-888 / route_triton.py:36-72.
+// ---------------------------------------------------------------------------
+template <typename KT>
+__global__ void __launch_bounds__(128) kbar_pool_kernel(DashKbarArgs a) {
+  extern __shared__ float sm[];
+  const int d = a.d;
+  const int ld = d + 1;                       // padded row, conflict-free column reads
+  float* sk = sm;                             // [bs][d+1]
+  float* shc = sk + a.block_size * ld;        // [d]
+  float* se = shc + d;                        // [bs]
+  float* sred = se + a.block_size;            // [4]
+  const KT* keys = reinterpret_cast<const KT*>(a.keys);
+
+  int n;
+  int64_t base, out_row;
+  if (a.pages == nullptr) {
+    int b = blockIdx.x, s = blockIdx.y;
+    n = a.seq_len - b * a.block_size;
+    if (n > a.block_size) n = a.block_size;
+    base = (int64_t)s * a.seq_stride + (int64_t)b * a.block_size * a.tok_stride;
+    out_row = (int64_t)s * a.kbar_seq_rows + b;
+  } else {
+    int i = blockIdx.x;
+    n = a.ntok[i];
+    if (n <= 0) return;                        // not a page slot (route_triton.py:69-72)
+    if (n > a.block_size) n = a.block_size;
+    base = a.pages[i] * a.page_stride;
+    out_row = a.pages[i];
+  }
+  for (int e = threadIdx.x; e < n * d; e += blockDim.x) {
+    int j = e / d, c = e - j * d;
+    sk[j * ld + c] = (float)keys[base + (int64_t)j * a.tok_stride + c];
+  }
+  for (int c = threadIdx.x; c < d; c += blockDim.x) shc[c] = a.head_cls ? a.head_cls[c] : 0.0f;
+  __syncthreads();
+  const float inv_sqrt_d = (float)(1.0 / sqrt((double)d));
+  float lmax = -INFINITY;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    float acc = 0.0f;
+    for (int c = 0; c < d; ++c) acc = __fmaf_rn(sk[j * ld + c], shc[c], acc);
+    float aw = clamp_act(__fmul_rn(acc, inv_sqrt_d));
+    se[j] = aw;
+    lmax = fmaxf(lmax, aw);
+  }
+  for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+  if ((threadIdx.x & 31) == 0) sred[threadIdx.x >> 5] = lmax;
+  __syncthreads();
+  float rmax = fmaxf(fmaxf(sred[0], sred[1]), fmaxf(sred[2], sred[3]));
+  if (n <= 0) rmax = 0.0f;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) se[j] = det_expf(__fsub_rn(se[j], rmax));
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float sum = 0.0f;
+    for (int j = 0; j < n; ++j) sum = __fadd_rn(sum, se[j]);
+    sred[0] = sum > 1e-6f ? sum : 1e-6f;
+  }
+  __syncthreads();
+  const float den = sred[0];
+  for (int j = threadIdx.x; j < n; j += blockDim.x) se[j] = __fdiv_rn(se[j], den);
+  __syncthreads();
+  for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    float acc = 0.0f;
+    for (int j = 0; j < n; ++j) acc = __fmaf_rn(se[j], sk[j * ld + c], acc);
+    if (!(acc == acc) || isinf(acc)) acc = 0.0f;
+    a.kbar[out_row * a.kbar_row_stride + c] = acc;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Row -> (sequence, position) for the DashSeqs packing.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void row_to_seq(const DashSeqs& q, int64_t r, int& s, int& i) {
+  if (q.q_start == nullptr) {
+    s = (int)(r / q.q_len_fixed);
+    i = (int)(r - (int64_t)s * q.q_len_fixed);
+    return;
+  }
+  int lo = 0, hi = q.n_seq - 1;                 // last s with q_start[s] <= r
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (q.q_start[mid] <= r) lo = mid; else hi = mid - 1;
+  }
+  s = lo;
+  i = (int)(r - q.q_start[lo]);
+}
+__device__ __forceinline__ int seq_kv_len(const DashSeqs& q, int s) {
+  return q.kv_len ? q.kv_len[s] : q.kv_len_fixed;
+}
+__device__ __forceinline__ int seq_q_len(const DashSeqs& q, int s) {
+  return q.q_start ? (q.q_start[s + 1] - q.q_start[s]) : q.q_len_fixed;
+}
+__device__ __forceinline__ int64_t seq_pos(const DashSeqs& q, int s, int i) {
+  int p0 = q.pos0 ? q.pos0[s] : seq_kv_len(q, s) - seq_q_len(q, s);
+  return (int64_t)p0 + i;
+}
+
+__device__ __forceinline__ uint32_t order_key(float x) {
+  uint32_t u = __float_as_uint(x);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// ---------------------------------------------------------------------------
+// Routing: one warp per query row.
+// Restates modeling_deepseekv2.py:309-333 + 351-388 (and WHL dash_router.py
+// route_and_select): cand = remote & mask (fallback remote); x = cand ? z*scale
+// : -1e4; top-M by (x desc, id asc) via a radix select on the order-preserving
+// key; entmax tau by bisection over the top-M and a closed-form refinement on
+// the found support; first K by rank; bias = (log max(p,floor) - mean)/sigma
+// over the valid (candidate) slots; ascending pack with -1 tail.
+// ---------------------------------------------------------------------------
+constexpr int kRouteWarps = 4;
+constexpr int kMaxM = 256;
+
+__global__ void __launch_bounds__(kRouteWarps * 32) route_rows_kernel(DashRouteArgs a,
+                                                                     int64_t n_rows) {
+  extern __shared__ float smr[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int W = a.width;
+  const int Wp = (W + 31) & ~31;
+  // per-warp scratch: q [d] | x [Wp] | cand bits [Wp/32] | M items (id, x) | sel flags
+  float* sq = smr + warp * (a.d + Wp + Wp / 32 + 3 * kMaxM);
+  float* sx = sq + a.d;
+  uint32_t* scand = reinterpret_cast<uint32_t*>(sx + Wp);
+  int* mid_ = reinterpret_cast<int*>(scand + Wp / 32);
+  float* mx = reinterpret_cast<float*>(mid_ + kMaxM);
+  int* mrank = reinterpret_cast<int*>(mx + kMaxM);
+
+  const int64_t r = (int64_t)blockIdx.x * kRouteWarps + warp;
+  if (r >= n_rows) return;
+  int s, i;
+  row_to_seq(a.seqs, r, s, i);
+  const int64_t pos = seq_pos(a.seqs, s, i);
+  const int kvl = seq_kv_len(a.seqs, s);
+  const int64_t qblk = pos >= 0 ? pos / a.block_size : -1;
+
+  // ---- scores ----
+  if (a.scores_in) {
+    for (int b = lane; b < W; b += 32) sx[b] = a.scores_in[r * a.scores_in_stride + b];
+  } else {
+    for (int c = lane; c < a.d; c += 32) sq[c] = a.idx_q[r * a.q_row_stride + c];
+    __syncwarp();
+    const float inv_sqrt_d = (float)(1.0 / sqrt((double)a.d));
+    for (int b = lane; b < W; b += 32) {
+      float z = kScoreNeg;
+      if ((int64_t)b <= qblk - a.local_blocks && (int64_t)b * a.block_size < kvl) {
+        int64_t kr = a.block_table ? (int64_t)a.block_table[(int64_t)s * a.bt_stride + b]
+                                   : (int64_t)s * a.kbar_seq_rows + b;
+        if (kr < 0 || kr >= a.num_kbar_rows) {
+          record_error(a.device_error, DASH_DEV_BAD_PAGE, 10, kr);
+        } else {
+          const float4* kb = reinterpret_cast<const float4*>(a.kbar + kr * a.kbar_row_stride);
+          float acc = 0.0f;
+          for (int c4 = 0; c4 < a.d / 4; ++c4) {
+            float4 k4 = __ldg(kb + c4);
+            acc = __fmaf_rn(sq[4 * c4 + 0], k4.x, acc);
+            acc = __fmaf_rn(sq[4 * c4 + 1], k4.y, acc);
+            acc = __fmaf_rn(sq[4 * c4 + 2], k4.z, acc);
+            acc = __fmaf_rn(sq[4 * c4 + 3], k4.w, acc);
+          }
+          z = clamp_act(__fmul_rn(acc, inv_sqrt_d));
+        }
+      }
+      sx[b] = z;
+    }
+  }
+  __syncwarp();
+  if (a.scores_out)
+    for (int b = lane; b < W; b += 32) a.scores_out[r * a.scores_out_stride + b] = sx[b];
+
+  // ---- candidates (with per-row fallback) ----
+  const uint8_t* cm = nullptr;
+  if (a.cand) cm = a.cand + (a.cand_per_seq ? (int64_t)s : r) * a.cand_row_stride;
+  bool any = false;
+  for (int b0 = 0; b0 < Wp; b0 += 32) {
+    int b = b0 + lane;
+    bool remote = b < W && sx[b] > kScoreNeg * 0.5f;
+    bool c = remote && (!cm || cm[b] != 0);
+    uint32_t bal = __ballot_sync(0xffffffffu, c);
+    if (lane == 0) scand[b0 >> 5] = bal;
+    any |= bal != 0;
+  }
+  __syncwarp();
+  if (!any) {
+    for (int b0 = 0; b0 < Wp; b0 += 32) {
+      int b = b0 + lane;
+      bool remote = b < W && sx[b] > kScoreNeg * 0.5f;
+      uint32_t bal = __ballot_sync(0xffffffffu, remote);
+      if (lane == 0) scand[b0 >> 5] = bal;
+    }
+    __syncwarp();
+  }
+  for (int b = lane; b < W; b += 32) {
+    bool c = (scand[b >> 5] >> (b & 31)) & 1u;
+    float v = c ? __fmul_rn(sx[b], a.idx_scale) : kEntmaxNeg;
+    if (!(v == v) || isinf(v)) v = kEntmaxNeg;
+    sx[b] = v;
+  }
+  __syncwarp();
+
+  // ---- top-M threshold (radix select over the order-preserving key) ----
+  int M = a.topm > 0 ? min(a.topm, W) : W;
+  if (M < 1) M = 1;
+  uint32_t T = 0;
+  if (M < W) {
+    for (int bit = 31; bit >= 0; --bit) {
+      uint32_t trial = T | (1u << bit);
+      int cnt = 0;
+      for (int b = lane; b < W; b += 32) cnt += order_key(sx[b]) >= trial;
+      cnt = __reduce_add_sync(0xffffffffu, cnt);
+      if (cnt >= M) T = trial;
+    }
+  }
+  // gather the M items in ascending id order: keys > T, then the lowest-id ties
+  int n_gt = 0;
+  if (M < W) {
+    int c = 0;
+    for (int b = lane; b < W; b += 32) c += order_key(sx[b]) > T;
+    n_gt = __reduce_add_sync(0xffffffffu, c);
+  }
+  int ties_left = M - n_gt;
+  int n_items = 0;
+  for (int b0 = 0; b0 < Wp; b0 += 32) {
+    int b = b0 + lane;
+    bool in = false, tie = false;
+    if (b < W) {
+      uint32_t k = order_key(sx[b]);
+      if (M >= W) in = true;
+      else if (k > T) in = true;
+      else if (k == T) tie = true;
+    }
+    uint32_t tb = __ballot_sync(0xffffffffu, tie);
+    int tie_rank = __popc(tb & ((1u << lane) - 1u));
+    if (tie && tie_rank < ties_left) in = true;
+    ties_left -= min(ties_left, __popc(tb));
+    uint32_t ib = __ballot_sync(0xffffffffu, in);
+    if (in) {
+      int slot = n_items + __popc(ib & ((1u << lane) - 1u));
+      mid_[slot] = b;
+      mx[slot] = sx[b];
+    }
+    n_items += __popc(ib);
+  }
+  __syncwarp();
+  M = n_items;  // == M
+
+  // ---- rank of each item by (x desc, id asc) ----
+  for (int t = lane; t < M; t += 32) {
+    float xt = mx[t];
+    int it = mid_[t], rk = 0;
+    for (int u = 0; u < M; ++u) {
+      float xu = mx[u];
+      rk += (xu > xt) || (xu == xt && mid_[u] < it);
+    }
+    mrank[t] = rk;
+  }
+  __syncwarp();
+
+  // ---- 1.5-entmax over the M items: z = (x - max)/2; tau by bisection ----
+  float xmax = -INFINITY;
+  for (int t = lane; t < M; t += 32) xmax = fmaxf(xmax, mx[t]);
+  for (int o = 16; o > 0; o >>= 1) xmax = fmaxf(xmax, __shfl_xor_sync(0xffffffffu, xmax, o));
+  constexpr int PER = kMaxM / 32;
+  float zl[PER];
+#pragma unroll
+  for (int u = 0; u < PER; ++u) {
+    int t = lane + 32 * u;
+    zl[u] = t < M ? __fdiv_rn(__fsub_rn(mx[t], xmax), 2.0f) : -INFINITY;
+  }
+  float lo = -1.0f, hi = 0.0f;
+  for (int it = 0; it < 30; ++it) {
+    float m = 0.5f * (lo + hi);
+    float f = 0.0f;
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      float t = fmaxf(zl[u] - m, 0.0f);
+      f = __fmaf_rn(t, t, f);
+    }
+    for (int o = 16; o > 0; o >>= 1) f += __shfl_xor_sync(0xffffffffu, f, o);
+    if (f > 1.0f) lo = m; else hi = m;
+  }
+  float tau_b = 0.5f * (lo + hi);
+  // closed form on the support {z > tau_b}: tau = mean - sqrt(max((1-ss)/k, 0))
+  float s1 = 0.0f, s2 = 0.0f, kk = 0.0f;
+#pragma unroll
+  for (int u = 0; u < PER; ++u)
+    if (zl[u] > tau_b) { s1 += zl[u]; s2 = __fmaf_rn(zl[u], zl[u], s2); kk += 1.0f; }
+  for (int o = 16; o > 0; o >>= 1) {
+    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+    s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    kk += __shfl_xor_sync(0xffffffffu, kk, o);
+  }
+  if (kk < 1.0f) kk = 1.0f;
+  float mean = s1 / kk, mean_sq = s2 / kk;
+  float ss = kk * (mean_sq - mean * mean);
+  float delta = (1.0f - ss) / kk;
+  float tau = mean - sqrtf(fmaxf(delta, 0.0f));
+
+  // ---- first K by rank; bias over the valid (candidate) ones ----
+  int Kc = min(a.K, M);
+  if (Kc < 1) Kc = 1;
+  float lsum = 0.0f;
+  int cnt = 0;
+  float logp_l[PER];
+  bool valid_l[PER];
+#pragma unroll
+  for (int u = 0; u < PER; ++u) {
+    int t = lane + 32 * u;
+    valid_l[u] = false;
+    logp_l[u] = 0.0f;
+    if (t < M && mrank[t] < Kc) {
+      int b = mid_[t];
+      bool c = (scand[b >> 5] >> (b & 31)) & 1u;
+      float pz = fmaxf(zl[u] - tau, 0.0f);
+      float p = pz * pz;
+      logp_l[u] = logf(fmaxf(p, a.prior_floor));
+      valid_l[u] = c;
+      if (c) { lsum += logp_l[u]; cnt += 1; }
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+  cnt = __reduce_add_sync(0xffffffffu, cnt);
+  const float mu = lsum / (float)(cnt > 0 ? cnt : 1);
+
+  // ---- ascending pack ----
+  int32_t* oi = a.out_idx + r * a.out_stride;
+  float* ob = a.out_bias + r * a.out_stride;
+  for (int j = lane; j < a.out_width; j += 32) { oi[j] = -1; ob[j] = 0.0f; }
+  __syncwarp();
+#pragma unroll
+  for (int u = 0; u < PER; ++u) {
+    int t = lane + 32 * u;
+    if (valid_l[u]) {
+      int b = mid_[t];
+      // position = number of valid selected items with a smaller id
+      int p = 0;
+      for (int v = 0; v < M; ++v) {
+        if (mrank[v] < Kc) {
+          int bv = mid_[v];
+          bool cv = (scand[bv >> 5] >> (bv & 31)) & 1u;
+          p += cv && bv < b;
+        }
+      }
+      if (p < a.out_width) {
+        oi[p] = b;
+        ob[p] = (logp_l[u] - mu) * a.inv_sigma;
+      }
+    }
+  }
+  if (a.out_count && lane == 0) a.out_count[r] = min(cnt, a.out_width);
+}
+
+// ---------------------------------------------------------------------------
+// Indexer stage-0: block max of token scores over remote keys.
+// One CTA per (32 query rows, key block, batch); thread (row, key lane).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) block_max_kernel(DashBlockMaxArgs a) {
+  extern __shared__ float smb[];
+  const int d = a.d, ld = d + 1;
+  float* sq = smb;                 // [32][d+1]
+  float* sk = sq + 32 * ld;        // [bs][d+1]
+  float* sred = sk + a.block_size * ld;  // [4][32]
+  const int c0 = blockIdx.x * 32, blk = blockIdx.y, b = blockIdx.z;
+  const int j0 = blk * a.block_size;
+  for (int e = threadIdx.x; e < 32 * d; e += blockDim.x) {
+    int rr = e / d, c = e - rr * d;
+    int cc = c0 + rr;
+    sq[rr * ld + c] = cc < a.C ? a.q[b * a.q_stride_b + (int64_t)cc * a.q_stride_c + c] : 0.0f;
+  }
+  for (int e = threadIdx.x; e < a.block_size * d; e += blockDim.x) {
+    int jj = e / d, c = e - jj * d;
+    int j = j0 + jj;
+    sk[jj * ld + c] = j < a.Sk ? a.k[b * a.k_stride_b + (int64_t)j * a.k_stride_j + c] : 0.0f;
+  }
+  __syncthreads();
+  const int rr = threadIdx.x & 31, part = threadIdx.x >> 5;
+  const int cc = c0 + rr;
+  float m = a.empty;
+  bool any = false;
+  if (cc < a.C) {
+    int64_t pos = a.pos[b * a.pos_stride_b + (int64_t)cc * a.pos_stride_c];
+    int64_t seg = a.seg ? a.seg[b * a.seg_stride_b + (int64_t)cc * a.seg_stride_c] : 0;
+    int64_t hi = pos - a.local_window;
+    for (int jj = part; jj < a.block_size; jj += 4) {
+      int64_t j = j0 + jj;
+      if (j >= a.Sk || j > hi || j < seg) continue;
+      float acc = 0.0f;
+      for (int c = 0; c < d; ++c) acc = __fmaf_rn(sq[rr * ld + c], sk[jj * ld + c], acc);
+      if (a.clamp) acc = clamp_act(acc);
+      if (!any || acc > m || acc != acc) { m = acc; any = true; }
+    }
+  }
+  sred[part * 32 + rr] = m;
+  int* sany = reinterpret_cast<int*>(sred + 128);
+  sany[part * 32 + rr] = any ? 1 : 0;
+  __syncthreads();
+  if (part == 0 && cc < a.C) {
+    float best = a.empty;
+    bool got = false;
+    for (int p = 0; p < 4; ++p) {
+      if (!sany[p * 32 + rr]) continue;
+      float v = sred[p * 32 + rr];
+      if (!got || v > best || v != v) { best = v; got = true; }
+    }
+    a.out[b * a.out_stride_b + (int64_t)cc * a.out_stride_c + blk] = best;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host launchers
+// ---------------------------------------------------------------------------
+int launch_kbar(const DashKbarArgs& a, cudaStream_t st) {
+  dim3 grid;
+  if (a.pages == nullptr) {
+    int nblk = (a.seq_len + a.block_size - 1) / a.block_size;
+    grid = dim3(nblk, a.n_seq);
+  } else {
+    grid = dim3(a.n_plan);
+  }
+  if (grid.x == 0 || grid.y == 0) return DASH_OK;
+  size_t smem = sizeof(float) * ((size_t)a.block_size * (a.d + 1) + a.d + a.block_size + 4);
+  if (a.dtype == DASH_DTYPE_F32) {
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(kbar_pool_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem);
+    kbar_pool_kernel<float><<<grid, 128, smem, st>>>(a);
+  } else {
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(kbar_pool_kernel<__nv_bfloat16>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kbar_pool_kernel<__nv_bfloat16><<<grid, 128, smem, st>>>(a);
+  }
+  count_launch();
+  return check_launch("kbar_pool_kernel");
+}
+
+int launch_route(const DashRouteArgs& a, int64_t n_rows, cudaStream_t st) {
+  if (n_rows == 0) return DASH_OK;
+  int Wp = (a.width + 31) & ~31;
+  size_t per_warp = sizeof(float) * ((size_t)a.d + Wp + Wp / 32 + 3 * kMaxM);
+  size_t smem = per_warp * kRouteWarps;
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(route_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+  int64_t grid = (n_rows + kRouteWarps - 1) / kRouteWarps;
+  route_rows_kernel<<<(unsigned)grid, kRouteWarps * 32, smem, st>>>(a, n_rows);
+  count_launch();
+  return check_launch("route_rows_kernel");
+}
+
+int launch_block_max(const DashBlockMaxArgs& a, cudaStream_t st) {
+  dim3 grid((a.C + 31) / 32, a.nblk, a.B);
+  if (grid.x == 0 || grid.y == 0 || grid.z == 0) return DASH_OK;
+  size_t smem = sizeof(float) * ((size_t)(32 + a.block_size) * (a.d + 1) + 256);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(block_max_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+  block_max_kernel<<<grid, 128, smem, st>>>(a);
+  count_launch();
+  return check_launch("block_max_kernel");
+}
+
+}  // namespace dash

@@ -1,0 +1,337 @@
+"""Tensor-level wrappers around the C ABI (torch tensors in, kernels launched on
+the current CUDA stream).  Every function requires CUDA tensors and raises on
+any non-zero library status; there is no CPU path.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib as L
+
+_DT = {torch.bfloat16: L.DTYPE_BF16, torch.float16: L.DTYPE_F16, torch.float32: L.DTYPE_F32}
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("DASH B200 kernels need CUDA tensors (no CPU fallback)")
+
+
+@dataclass
+class Seqs:
+    """Query/sequence packing (mirrors DashSeqs).
+
+    fixed: ``n_seq`` sequences of ``q_len`` query rows each, keys ``kv_len``.
+    varlen: ``q_start`` int32 [n_seq+1] (cu_seqlens_q), optional ``pos0`` and
+    ``kv_len_t`` int32 [n_seq] device tensors, ``total_rows`` and ``max_q_len``
+    given by the caller (no host sync)."""
+    n_seq: int
+    q_len: int = 0
+    kv_len: int = 0
+    q_start: Optional[torch.Tensor] = None
+    pos0: Optional[torch.Tensor] = None
+    kv_len_t: Optional[torch.Tensor] = None
+    total_rows: int = 0
+    max_q_len: int = 0
+
+    @property
+    def rows(self) -> int:
+        return self.total_rows if self.q_start is not None else self.n_seq * self.q_len
+
+    def c(self) -> L.DashSeqs:
+        s = L.DashSeqs()
+        s.n_seq = self.n_seq
+        if self.q_start is not None:
+            s.q_len_fixed = self.total_rows
+            s.max_q_len = self.max_q_len
+        else:
+            s.q_len_fixed = self.q_len
+            s.max_q_len = max(self.max_q_len, self.q_len)
+        s.kv_len_fixed = self.kv_len
+        s.q_start = _ptr(self.q_start)
+        s.pos0 = _ptr(self.pos0)
+        s.kv_len = _ptr(self.kv_len_t)
+        return s
+
+
+class DeviceErrorWord:
+    """16 bytes of device memory the kernels write DASH_DEV_* codes into."""
+
+    def __init__(self, device):
+        self.t = torch.zeros(2, dtype=torch.int64, device=device)
+
+    @property
+    def ptr(self):
+        return self.t.data_ptr()
+
+    def read(self):
+        v = self.t.cpu()
+        code = int(v[0] & 0xFFFFFFFF)
+        where = int((v[0] >> 32) & 0xFFFFFFFF)
+        return code, where, int(v[1])
+
+    def check(self):
+        code, where, info = self.read()
+        if code:
+            raise RuntimeError(f"DASH device error {code} at site {where} (value {info})")
+
+    def clear(self):
+        self.t.zero_()
+
+
+# ---------------------------------------------------------------------------
+# stage-0 pooling
+# ---------------------------------------------------------------------------
+def kbar_pool_contig(idx_k: torch.Tensor, head_cls: Optional[torch.Tensor], block_size: int,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """idx_k [B,S,d] (fp32/bf16, unit inner stride) -> k-bar [B,nblk,d] fp32."""
+    _need_cuda(idx_k)
+    B, S, d = idx_k.shape
+    if idx_k.stride(2) != 1:
+        idx_k = idx_k.contiguous()
+    nblk = (S + block_size - 1) // block_size
+    if out is None:
+        out = torch.empty(B, nblk, d, dtype=torch.float32, device=idx_k.device)
+    hc = None if head_cls is None else head_cls.detach().to(idx_k.device, torch.float32).contiguous()
+    a = L.DashKbarArgs()
+    a.keys = idx_k.data_ptr()
+    a.dtype = _DT[idx_k.dtype]
+    a.d, a.block_size, a.n_seq, a.seq_len, a.n_plan = d, block_size, B, S, 0
+    a.tok_stride, a.seq_stride, a.page_stride = idx_k.stride(1), idx_k.stride(0), 0
+    a.kbar_seq_rows = out.stride(0) // out.stride(1)
+    a.head_cls = _ptr(hc)
+    a.pages = a.ntok = None
+    a.kbar = out.data_ptr()
+    a.kbar_row_stride = out.stride(1)
+    L.call("dash_kbar_pool", a)
+    return out
+
+
+def kbar_pool_paged(index_cache: torch.Tensor, pages: torch.Tensor, ntok: torch.Tensor,
+                    head_cls: Optional[torch.Tensor], kbar: torch.Tensor) -> torch.Tensor:
+    """Refresh kbar[page] from index_cache [P, bs, d] for each (page, ntok) entry."""
+    _need_cuda(index_cache, pages, ntok, kbar)
+    P, bs, d = index_cache.shape
+    pages = pages.to(torch.int64).contiguous()
+    ntok = ntok.to(torch.int32).contiguous()
+    hc = None if head_cls is None else head_cls.detach().to(index_cache.device, torch.float32).contiguous()
+    a = L.DashKbarArgs()
+    a.keys = index_cache.data_ptr()
+    a.dtype = _DT[index_cache.dtype]
+    a.d, a.block_size, a.n_seq, a.seq_len, a.n_plan = d, bs, 0, 0, int(pages.numel())
+    a.tok_stride, a.seq_stride, a.page_stride = index_cache.stride(1), 0, index_cache.stride(0)
+    a.kbar_seq_rows = 0
+    a.head_cls = _ptr(hc)
+    a.pages, a.ntok = pages.data_ptr(), ntok.data_ptr()
+    a.kbar, a.kbar_row_stride = kbar.data_ptr(), kbar.stride(0)
+    if a.n_plan:
+        L.call("dash_kbar_pool", a)
+    return kbar
+
+
+# ---------------------------------------------------------------------------
+# routing
+# ---------------------------------------------------------------------------
+def route(seqs: Seqs, *, width: int, block_size: int, local_blocks: int, idx_scale: float,
+          prior_floor: float, sigma: float, topm: int, K: int,
+          idx_q: Optional[torch.Tensor] = None, kbar: Optional[torch.Tensor] = None,
+          block_table: Optional[torch.Tensor] = None, scores_in: Optional[torch.Tensor] = None,
+          cand: Optional[torch.Tensor] = None, cand_per_seq: bool = False,
+          out_idx: Optional[torch.Tensor] = None, out_bias: Optional[torch.Tensor] = None,
+          out_width: Optional[int] = None, scores_out: Optional[torch.Tensor] = None,
+          out_count: Optional[torch.Tensor] = None, device_error: Optional[DeviceErrorWord] = None):
+    """Fused DASH routing for ``seqs.rows`` query rows.
+
+    Either ``scores_in`` [rows, width] (precomputed block scores) or ``idx_q``
+    [rows, d] + ``kbar`` (contiguous [n_seq, nblk, d] or a page cache [P, d]
+    addressed through ``block_table`` [n_seq, W]).  Returns (idx int32 [rows,
+    out_width] ascending with -1 tail, bias fp32 [rows, out_width])."""
+    ref = scores_in if scores_in is not None else idx_q
+    _need_cuda(ref, kbar, block_table, cand)
+    dev = ref.device
+    rows = seqs.rows
+    ow = out_width or K
+    if out_idx is None:
+        out_idx = torch.empty(rows, ow, dtype=torch.int32, device=dev)
+    if out_bias is None:
+        out_bias = torch.empty(rows, ow, dtype=torch.float32, device=dev)
+    a = L.DashRouteArgs()
+    a.seqs = seqs.c()
+    if scores_in is None:
+        if idx_q.dtype != torch.float32 or idx_q.stride(-1) != 1:
+            idx_q = idx_q.float().contiguous()
+        a.idx_q, a.q_row_stride = idx_q.data_ptr(), idx_q.stride(0)
+        a.d = idx_q.shape[-1]
+        if block_table is not None:
+            a.kbar, a.kbar_row_stride = kbar.data_ptr(), kbar.stride(0)
+            a.block_table, a.bt_stride = block_table.data_ptr(), block_table.stride(0)
+            a.num_kbar_rows = kbar.shape[0]
+        else:
+            a.kbar, a.kbar_row_stride = kbar.data_ptr(), kbar.stride(1)
+            a.kbar_seq_rows = kbar.stride(0) // kbar.stride(1)
+            a.num_kbar_rows = kbar.shape[0] * a.kbar_seq_rows
+    else:
+        scores_in = scores_in if scores_in.stride(-1) == 1 else scores_in.contiguous()
+        a.scores_in, a.scores_in_stride = scores_in.data_ptr(), scores_in.stride(0)
+        a.d = 128
+    a.width = width
+    if scores_out is not None:
+        a.scores_out, a.scores_out_stride = scores_out.data_ptr(), scores_out.stride(0)
+    if cand is not None:
+        cand = cand.to(torch.uint8).contiguous()
+        a.cand, a.cand_row_stride, a.cand_per_seq = cand.data_ptr(), cand.stride(0), int(cand_per_seq)
+    a.block_size, a.local_blocks, a.topm, a.K, a.out_width = block_size, local_blocks, topm, K, ow
+    a.idx_scale, a.prior_floor, a.inv_sigma = float(idx_scale), float(prior_floor), float(1.0 / sigma)
+    a.out_idx, a.out_bias, a.out_stride = out_idx.data_ptr(), out_bias.data_ptr(), out_idx.stride(0)
+    assert out_bias.stride(0) == out_idx.stride(0)
+    a.out_count = _ptr(out_count)
+    a.device_error = device_error.ptr if device_error is not None else None
+    L.call("dash_route", a)
+    return out_idx, out_bias
+
+
+def block_max(q: torch.Tensor, k: torch.Tensor, pos: torch.Tensor, seg: Optional[torch.Tensor],
+              block_size: int, nblk: int, local_window: int, clamp: bool, empty: float):
+    """Indexer stage-0 block-max scores: q [B,C,d], k [B,Sk,d] fp32 -> [B,C,nblk]."""
+    _need_cuda(q, k, pos, seg)
+    q = q.float().contiguous()
+    k = k.float().contiguous()
+    B, Cq, d = q.shape
+    pos = pos.to(torch.int32).contiguous()
+    seg = None if seg is None else seg.to(torch.int32).contiguous()
+    out = torch.empty(B, Cq, nblk, dtype=torch.float32, device=q.device)
+    a = L.DashBlockMaxArgs()
+    a.q, a.q_stride_b, a.q_stride_c = q.data_ptr(), q.stride(0), q.stride(1)
+    a.k, a.k_stride_b, a.k_stride_j = k.data_ptr(), k.stride(0), k.stride(1)
+    a.pos, a.pos_stride_b, a.pos_stride_c = pos.data_ptr(), pos.stride(0), pos.stride(1)
+    if seg is not None:
+        a.seg, a.seg_stride_b, a.seg_stride_c = seg.data_ptr(), seg.stride(0), seg.stride(1)
+    a.B, a.C, a.Sk, a.d = B, Cq, k.shape[1], d
+    a.block_size, a.nblk, a.local_window, a.clamp = block_size, nblk, local_window, int(clamp)
+    a.empty = float(empty)
+    a.out, a.out_stride_b, a.out_stride_c = out.data_ptr(), out.stride(0), out.stride(1)
+    L.call("dash_block_max", a)
+    return out
+
+
+# ---------------------------------------------------------------------------
+# attention
+# ---------------------------------------------------------------------------
+def _kv(k, v, block_table, n_kv_heads, paged_layout):
+    """DashKV from tensors.  contiguous: k/v indexable as [seq, tok, head, d] via
+    strides; paged: caches [P, page, Hkv, d]."""
+    kv = L.DashKV()
+    kv.k, kv.v = k.data_ptr(), v.data_ptr()
+    kv.dtype = _DT[k.dtype]
+    kv.n_kv_heads = n_kv_heads
+    kv.head_dim = k.shape[-1]
+    st = paged_layout
+    assert k.stride() == v.stride(), "K and V must share strides"
+    kv.stride_seq, kv.stride_tok, kv.stride_head = st
+    if block_table is not None:
+        kv.block_table, kv.bt_stride = block_table.data_ptr(), block_table.stride(0)
+        kv.num_pages = k.shape[0]
+    return kv
+
+
+def _routes(idx, bias, row_stride, ihead_stride, n_index_heads):
+    r = L.DashRoutes()
+    r.idx = _ptr(idx)
+    r.bias = _ptr(bias)
+    r.row_stride, r.ihead_stride = row_stride, ihead_stride
+    r.K = 0 if idx is None else idx.shape[-1]
+    r.n_index_heads = n_index_heads
+    return r
+
+
+def _qo(q, out, q_strides, o_strides, n_heads, lse=None, lse_strides=(0, 0, 0)):
+    qo = L.DashQO()
+    qo.q, qo.out = q.data_ptr(), out.data_ptr()
+    qo.q_stride_seq, qo.q_stride_tok, qo.q_stride_head = q_strides
+    qo.o_stride_seq, qo.o_stride_tok, qo.o_stride_head = o_strides
+    qo.n_heads = n_heads
+    qo.lse = _ptr(lse)
+    qo.lse_stride_seq, qo.lse_stride_tok, qo.lse_stride_head = lse_strides
+    return qo
+
+
+_WS = {}
+
+
+def _workspace(device, nbytes, key):
+    """Grow-only workspace cache per (device, key); callers that must not
+    allocate pass their own buffer instead."""
+    buf = _WS.get((device, key))
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+        _WS[(device, key)] = buf
+    return buf
+
+
+def prefill_attn(args: L.DashPrefillArgs, device, workspace: Optional[torch.Tensor] = None):
+    L.load()
+    need = L.load().dash_prefill_workspace_size(args)
+    if workspace is None:
+        workspace = _workspace(device, need, "prefill")
+    args.workspace, args.workspace_bytes = workspace.data_ptr(), workspace.numel()
+    L.call("dash_prefill_attn", args)
+
+
+def decode_attn(args: L.DashDecodeArgs, device, workspace: Optional[torch.Tensor] = None):
+    need = L.load().dash_decode_workspace_size(args)
+    if need:
+        if workspace is None:
+            workspace = _workspace(device, need, "decode")
+        args.workspace, args.workspace_bytes = workspace.data_ptr(), workspace.numel()
+    L.call("dash_decode_attn", args)
+
+
+def gather_attention(q, k, v, idx, bias, *, block_size: int, local_window: int, scale: float,
+                     out=None, lse=None, seg_start=None, n_index_heads: int = 1,
+                     device_error: Optional[DeviceErrorWord] = None, workspace=None):
+    """Contiguous prefill: q [B,HQ,T,D], k/v [B,Hkv,T,D] (any strides with unit
+    inner stride), idx/bias routes [B,HI,T,K] (or [B,T,K]).  Returns out
+    [B,HQ,T,D] (a new tensor unless ``out`` is given)."""
+    _need_cuda(q, k, v, idx)
+    B, HQ, T, D = q.shape
+    Hkv = k.shape[1]
+    if out is None:
+        out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    if idx.dim() == 3:
+        idx = idx[:, None]
+        bias = None if bias is None else bias[:, None]
+    HI = idx.shape[1]
+    # rows are (b, t) pairs addressed as row * row_stride + ih * ihead_stride:
+    # view the routes as [B, T, HI, K] with equally spaced rows
+    idx4 = idx.to(torch.int32).permute(0, 2, 1, 3)
+    bias4 = None if bias is None else bias.to(torch.float32).permute(0, 2, 1, 3)
+
+    def _rowable(t):
+        return t.stride(3) == 1 and t.stride(0) == T * t.stride(1)
+
+    if not _rowable(idx4) or (bias4 is not None and
+                              (not _rowable(bias4) or bias4.stride() != idx4.stride())):
+        idx4 = idx4.contiguous()
+        bias4 = None if bias4 is None else bias4.contiguous()
+    a = L.DashPrefillArgs()
+    a.seqs = Seqs(n_seq=B, q_len=T, kv_len=T, max_q_len=T).c()
+    a.kv = _kv(k, v, None, Hkv, (k.stride(0), k.stride(2), k.stride(1)))
+    a.routes = _routes(idx4, bias4, idx4.stride(1), idx4.stride(2), HI)
+    lse_strides = (0, 0, 0) if lse is None else (lse.stride(0), lse.stride(2), lse.stride(1))
+    a.qo = _qo(q, out, (q.stride(0), q.stride(2), q.stride(1)),
+               (out.stride(0), out.stride(2), out.stride(1)), HQ, lse, lse_strides)
+    if seg_start is not None:
+        seg_start = seg_start.to(torch.int32).contiguous()
+        a.seg_start = seg_start.data_ptr()
+    a.scale, a.block_size, a.local_window = float(scale), int(block_size), int(local_window)
+    a.device_error = device_error.ptr if device_error is not None else None
+    prefill_attn(a, q.device, workspace)
+    return out

@@ -1,0 +1,57 @@
+"""Drop-in for ANANTA_OCR ``sparse_gather_e2e_triton.py`` (forward only).
+
+``triton_gather_attention_e2e`` keeps the reference's name, signature, tensor
+layouts and "return None on unsupported shape" contract
+(sparse_gather_e2e_triton.py:342-391), but runs the B200 tcgen05 kernel of
+``libdash_b200.so`` instead of a Triton kernel.  Semantics
+(sparse_gather_e2e_triton.py:34-115): per query token t and head, keys in the
+routed blocks strictly below the local window get the slot's additive bias,
+keys in the window (t-LW, t] get none, everything is causal.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import ops
+
+SPARSE_E2E_SENTINEL = 1
+
+
+def _as_kernel_dtype(t: torch.Tensor) -> torch.Tensor:
+    # the tensor-core path computes in bf16/fp16 with fp32 accumulation
+    return t if t.dtype in (torch.bfloat16, torch.float16) else t.to(torch.bfloat16)
+
+
+def triton_gather_attention_e2e(query_states, key_states, value_states, block_indices,
+                                blk_bias_slots, position_ids, attention_mask, block_size, scale,
+                                local_window=None):
+    """Fused e2e gather attention.  query_states [B,HQ,T,D], key/value [B,Hkv,T,D],
+    block_indices [B,1,T,K] int (-1 pad), blk_bias_slots [B,T,K] fp32,
+    position_ids [B,T] (must be arange).  Returns [B,HQ,T,D] or None when the
+    reference would also decline (mask present, q_len != k_len, non-arange
+    positions, more than one index head)."""
+    if attention_mask is not None:
+        return None
+    if block_indices.shape[1] != 1:
+        return None
+    B, HQ, T, D = query_states.shape
+    if key_states.shape[2] != T:
+        return None
+    if position_ids is None or position_ids.dim() != 2 or position_ids.shape[-1] != T:
+        return None
+    ar = torch.arange(T, device=position_ids.device)
+    if not bool((position_ids == ar).all()):
+        return None
+    if D != 128 or value_states.shape[-1] != 128:
+        raise NotImplementedError(f"head_dim {D} not supported (B200 kernel: 128)")
+    if torch.is_grad_enabled() and any(
+            t.requires_grad for t in (query_states, key_states, value_states, blk_bias_slots)):
+        raise NotImplementedError("backward is not implemented by the B200 DASH kernels")
+    lw = int(block_size) if local_window is None else max(1, int(local_window))
+    dt = query_states.dtype
+    q = _as_kernel_dtype(query_states)
+    k = _as_kernel_dtype(key_states).to(q.dtype)
+    v = _as_kernel_dtype(value_states).to(q.dtype)
+    out = ops.gather_attention(q, k, v, block_indices, blk_bias_slots[:, None],
+                               block_size=int(block_size), local_window=lw, scale=float(scale))
+    return out if out.dtype == dt else out.to(dt)

@@ -1,0 +1,300 @@
+/*
+ * dash_b200.h -- C ABI of the B200 (sm_100a) DASH block-sparse attention library
+ * (libdash_b200.so).
+ *
+ * DASH is ANANTA_OCR's SR-SWA attention: every query token attends to a
+ * sliding window of `local_window` tokens plus up to K remote key blocks picked
+ * by a single-head 1.5-entmax router, each remote block carrying an additive
+ * log-prior bias.  The library implements the forward path:
+ *
+ *   dash_kbar_pool      stage-0 head_cls pooling of index keys into one
+ *                       summary key per block (k-bar)
+ *   dash_route          block scores + 1.5-entmax + top-K selection + bias,
+ *                       emitting compact ascending int32 block lists
+ *   dash_block_max      indexer-mode stage-0 scores (block max of token scores)
+ *   dash_prefill_attn   gather attention for many query tokens (tcgen05/TMEM)
+ *   dash_decode_attn    gather attention for decode tokens over a block-paged
+ *                       KV cache (split-KV with fused combine)
+ *
+ * Conventions
+ *  - All pointers are DEVICE pointers unless stated; strides are in ELEMENTS.
+ *  - Every entry point returns a DASH_* status; on failure dash_last_error()
+ *    holds a message.  Kernels never trap: a bounds check that fails on the
+ *    device records a DASH_DEV_* code in the optional DashDeviceError word
+ *    (device memory, zero-initialised by the caller) and skips the access.
+ *  - Work is enqueued on `stream` (a cudaStream_t); nothing synchronises.
+ *  - The routing of a query token is shared by all attention heads (the
+ *    reference router has one index head); `n_index_heads` > 1 selects the
+ *    multi-index-head layout of sparse_gather_triton.py.
+ */
+#ifndef DASH_B200_H
+#define DASH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DASH_OK 0
+#define DASH_ERR_INVALID 1     /* malformed argument (shape, null pointer, alignment)  */
+#define DASH_ERR_UNSUPPORTED 2 /* well formed but outside what the kernels implement   */
+#define DASH_ERR_CUDA 3        /* a CUDA runtime or driver call failed                  */
+#define DASH_ERR_WORKSPACE 4   /* workspace pointer missing or too small                */
+
+#define DASH_DEV_TIMEOUT 1     /* a bounded wait inside a kernel ran out               */
+#define DASH_DEV_BAD_BLOCK 2   /* routed block id outside [0, blocks of the sequence)   */
+#define DASH_DEV_BAD_PAGE 3    /* block-table page id outside [0, num_pages)            */
+
+#define DASH_DTYPE_F32 0
+#define DASH_DTYPE_BF16 1
+#define DASH_DTYPE_F16 2
+
+typedef void* dash_stream_t; /* cudaStream_t */
+
+/* Device-side error word (allocate 16 bytes of device memory, zero it). */
+typedef struct {
+  int32_t code;  /* first DASH_DEV_* code, 0 = none */
+  int32_t where; /* kernel site id */
+  int64_t info;  /* offending value */
+} DashDeviceError;
+
+/* Sequences of a batch.  Query row i of sequence s sits at position
+ * pos0[s] + i and attends keys [0, pos]; the sequence holds kv_len[s] tokens.
+ *   q_start  [n_seq+1] first query row of each sequence in a packed (varlen)
+ *            row layout (cu_seqlens_q); NULL: sequence s owns rows
+ *            [s*q_len_fixed, (s+1)*q_len_fixed) and strides use stride_seq.
+ *   pos0     [n_seq] position of the first query row; NULL: kv_len - q_len
+ *            (the queries are the last tokens: prefill without prefix, decode).
+ *   kv_len   [n_seq] live tokens (seq_lens); NULL: kv_len_fixed for all.
+ *   q_len_fixed  rows per sequence when q_start == NULL; the TOTAL number of
+ *            query rows (q_start[n_seq]) when q_start != NULL.
+ *   max_q_len    upper bound of any sequence's query rows.
+ *   kv_len_fixed also gives the allocated token extent of contiguous K/V.   */
+typedef struct {
+  int32_t n_seq;
+  int32_t q_len_fixed;
+  int32_t kv_len_fixed;
+  int32_t max_q_len;
+  const int32_t* q_start;
+  const int32_t* pos0;
+  const int32_t* kv_len;
+} DashSeqs;
+
+/* Key/value storage.
+ *  contiguous (block_table == NULL): element (seq s, token t, head h, dim c) at
+ *      base + s*stride_seq + t*stride_tok + h*stride_head + c
+ *  block-paged (block_table != NULL): token t of sequence s lives in page
+ *      p = block_table[s*bt_stride + t/page_size] at offset t%page_size:
+ *      base + p*stride_seq + (t%page_size)*stride_tok + h*stride_head + c
+ *  (page_size == block_size: one sparse block per page.)                     */
+typedef struct {
+  const void* k;
+  const void* v;
+  int32_t dtype; /* DASH_DTYPE_BF16 or DASH_DTYPE_F16 */
+  int32_t n_kv_heads;
+  int32_t head_dim;
+  int32_t pad0;
+  int64_t stride_seq, stride_tok, stride_head;
+  const int32_t* block_table;
+  int64_t bt_stride;
+  int64_t num_pages;
+} DashKV;
+
+/* Routed blocks per query row: idx[row*row_stride + ih*ihead_stride + j],
+ * j < K, -1 = unused slot; bias likewise (NULL = no bias).  Query head hq
+ * reads index head  hq / (n_heads / n_index_heads).  Lists need not be sorted
+ * or duplicate-free; ids outside the sequence's causal range are ignored.   */
+typedef struct {
+  const int32_t* idx;
+  const float* bias;
+  int64_t row_stride;
+  int64_t ihead_stride;
+  int32_t K;
+  int32_t n_index_heads;
+} DashRoutes;
+
+/* Queries and outputs: element (seq s, query row i, head h, dim c) at
+ *   q + (q_start ? (q_start[s]+i)*stride_tok : s*stride_seq + i*stride_tok)
+ *     + h*stride_head + c                                                    */
+typedef struct {
+  const void* q;
+  void* out;
+  int64_t q_stride_seq, q_stride_tok, q_stride_head;
+  int64_t o_stride_seq, o_stride_tok, o_stride_head;
+  int32_t n_heads;
+  int32_t pad0;
+  float* lse;                 /* optional natural-log LSE, same (s, i, h) addressing */
+  int64_t lse_stride_seq, lse_stride_tok, lse_stride_head;
+} DashQO;
+
+/* ---------------------------------------------------------------------- */
+/* Stage-0 head_cls pooling (k-bar).
+ * Replaces: dash_attention.py:863-888 (_block_scores_headcls pooling),
+ *           modeling_deepseekv2.py:362-379 (_block_scores_infer),
+ *           WHL sglang/srt/layers/attention/unlimited_dash_ops/route_triton.py:36-72
+ *           (_kbar_page_kernel) and :707-726 (kbar_refresh_tail_triton).
+ * contiguous (pages == NULL): summary of block b of sequence s (tokens
+ *   [b*block_size, min(seq_len, (b+1)*block_size))) -> kbar row s*kbar_seq_rows+b.
+ * paged: for each plan entry i with ntok[i] > 0, the first ntok[i] tokens of
+ *   page pages[i] -> kbar row pages[i].                                    */
+typedef struct {
+  const void* keys;
+  int32_t dtype;       /* DASH_DTYPE_F32 or DASH_DTYPE_BF16 */
+  int32_t d;           /* index dim, <= 256 */
+  int32_t block_size;  /* <= 256 */
+  int32_t n_seq;
+  int32_t seq_len;
+  int32_t n_plan;
+  int64_t tok_stride;  /* elements between consecutive tokens */
+  int64_t seq_stride;  /* contiguous: elements between sequences */
+  int64_t page_stride; /* paged: elements between pages */
+  int64_t kbar_seq_rows;
+  const float* head_cls; /* [d] or NULL (= zeros: block mean) */
+  const int64_t* pages;
+  const int32_t* ntok;
+  float* kbar;
+  int64_t kbar_row_stride;
+} DashKbarArgs;
+int dash_kbar_pool(const DashKbarArgs* args, dash_stream_t stream);
+
+/* ---------------------------------------------------------------------- */
+/* Routing: scores, candidates, 1.5-entmax prior, top-K selection, bias.
+ * Replaces: modeling_deepseekv2.py:351-388 (_block_scores_infer scoring) +
+ *           modeling_deepseekv2.py:309-333 (_infer_route_select),
+ *           WHL dash_router.py:131-174 (DashRouterMath.route_and_select),
+ *           WHL route_triton.py:624-678 (route_prefill_triton) and
+ *           :730-847 (route_decode_triton).
+ * Row r is query row r of `seqs` (same packing as the attention).  Block b
+ * of row r is a candidate iff b <= pos/block_size - local_blocks and
+ * b*block_size < kv_len (and cand[...] != 0 when a mask is given, with the
+ * per-row fallback to all remote blocks when the mask leaves none).
+ * Output: out_idx[r*out_stride + j], j < out_width: selected ids ascending,
+ * -1 tail; out_bias alongside (0 on unused slots).  Selection = top-K by
+ * score among candidates, ties to the lowest block id; the entmax prior is
+ * evaluated over the top-`topm` entries (topm <= 0: all blocks).            */
+typedef struct {
+  DashSeqs seqs;
+  const float* idx_q;     /* [rows, d] router queries */
+  int64_t q_row_stride;
+  const float* kbar;      /* k-bar rows */
+  int64_t kbar_row_stride;
+  const int32_t* block_table; /* paged k-bar cache: row = block_table[s*bt_stride+b] */
+  int64_t bt_stride;
+  int64_t kbar_seq_rows;  /* contiguous k-bar: row = s*kbar_seq_rows + b */
+  int64_t num_kbar_rows;  /* bounds check of k-bar rows */
+  int32_t width;          /* blocks scored per row (max_block) */
+  int32_t d;              /* == 128 */
+  const float* scores_in; /* optional [rows, width] precomputed scores (skips scoring) */
+  int64_t scores_in_stride;
+  float* scores_out;      /* optional [rows, width] */
+  int64_t scores_out_stride;
+  const uint8_t* cand;    /* optional candidate mask, [rows or n_seq, width] */
+  int64_t cand_row_stride;
+  int32_t cand_per_seq;   /* 1: one mask row per sequence */
+  int32_t block_size;
+  int32_t local_blocks;
+  int32_t topm;
+  int32_t K;
+  int32_t out_width;      /* >= K */
+  float idx_scale;        /* scaling_factor / sqrt(index_dim) */
+  float prior_floor;
+  float inv_sigma;
+  int32_t pad0;
+  int32_t* out_idx;
+  float* out_bias;
+  int64_t out_stride;
+  int32_t* out_count;     /* optional valid slots per row */
+  DashDeviceError* device_error;
+} DashRouteArgs;
+int dash_route(const DashRouteArgs* args, dash_stream_t stream);
+
+/* ---------------------------------------------------------------------- */
+/* Indexer stage-0 block scores (block max over remote keys).
+ * Replaces: sparse_gather_triton.py:431-467 (triton_block_max_score, clamp=0,
+ *           empty=-inf), modeling_deepseekv2.py:389-400 and
+ *           dash_attention.py:801-835 (clamp=1, empty=-1e9).
+ * out[b, c, blk] = max over keys j of block blk with seg[b,c] <= j <=
+ * pos[b,c] - local_window and j < Sk of <q[b,c], k[b,j]> (clamped to +-1e4
+ * when clamp != 0); `empty` when the block has no such key.                 */
+typedef struct {
+  const float* q; int64_t q_stride_b, q_stride_c;
+  const float* k; int64_t k_stride_b, k_stride_j;
+  const int32_t* pos; int64_t pos_stride_b, pos_stride_c;
+  const int32_t* seg; int64_t seg_stride_b, seg_stride_c; /* NULL = 0 */
+  int32_t B, C, Sk, d, block_size, nblk, local_window, clamp;
+  float empty;
+  int32_t pad0;
+  float* out; int64_t out_stride_b, out_stride_c;
+} DashBlockMaxArgs;
+int dash_block_max(const DashBlockMaxArgs* args, dash_stream_t stream);
+
+/* ---------------------------------------------------------------------- */
+/* Prefill gather attention (tcgen05 / TMEM / TMA).
+ * Replaces: sparse_gather_e2e_triton.py:342-391 (triton_gather_attention_e2e,
+ *           forward), sparse_gather_triton.py:343-392 (triton_gather_attention,
+ *           forward; bias = NULL), WHL attend_triton.py:523-596
+ *           (dash_sparse_attn).
+ * Query token at position p, head h: logits over keys j <= p, j >= seg,
+ *   local  (j > p - local_window): scale*<q,k_j>
+ *   remote (block j/block_size routed for the token, j <= p - local_window):
+ *          scale*<q,k_j> + bias of that slot
+ * out = softmax(logits) @ V.  head_dim 128, block_size 64 or 128,
+ * n_heads / n_kv_heads in {1,2,4,8,16}.  Workspace: dash_prefill_workspace_size. */
+typedef struct {
+  DashSeqs seqs;
+  DashKV kv;
+  DashRoutes routes;
+  DashQO qo;
+  const int32_t* seg_start; /* optional per query row first attendable key (packing) */
+  float scale;
+  int32_t block_size;
+  int32_t local_window;
+  int32_t pad0;
+  void* workspace;
+  size_t workspace_bytes;
+  DashDeviceError* device_error;
+} DashPrefillArgs;
+size_t dash_prefill_workspace_size(const DashPrefillArgs* args);
+int dash_prefill_attn(const DashPrefillArgs* args, dash_stream_t stream);
+
+/* ---------------------------------------------------------------------- */
+/* Decode gather attention over a block-paged (or contiguous) KV cache.
+ * Replaces: WHL attend_triton.py:600-715 (dash_sparse_attn_decode) with the
+ *           split-K merge of WHL common.py:40-89, and the decode attend of
+ *           modeling_deepseekv2.py:424-451 (_decode_attend).
+ * Same logit rule as prefill.  The selected blocks plus the local window are
+ * split across `num_splits` CTAs per (row, kv head) (0 = automatic); partial
+ * results go to the workspace and the last CTA of each (row, kv head) merges
+ * them (no CTA ever waits for another).  Workspace: dash_decode_workspace_size. */
+typedef struct {
+  DashSeqs seqs;
+  DashKV kv;
+  DashRoutes routes;
+  DashQO qo;
+  float scale;
+  int32_t block_size;
+  int32_t local_window;
+  int32_t num_splits;
+  void* workspace;
+  size_t workspace_bytes;
+  DashDeviceError* device_error;
+} DashDecodeArgs;
+size_t dash_decode_workspace_size(const DashDecodeArgs* args);
+int dash_decode_attn(const DashDecodeArgs* args, dash_stream_t stream);
+
+/* ---------------------------------------------------------------------- */
+/* Diagnostics */
+int dash_last_error(char* buf, int len);     /* copies the last host-side error message */
+int dash_library_version(void);              /* (major << 16) | minor */
+int dash_count_launches(int reset);          /* kernels launched by this library so far */
+/* sizeof() of the argument structs, in this order: DashSeqs, DashKV, DashRoutes,
+ * DashQO, DashKbarArgs, DashRouteArgs, DashBlockMaxArgs, DashPrefillArgs,
+ * DashDecodeArgs, DashDeviceError.  Lets a binding verify its struct layouts. */
+int dash_abi_sizes(int64_t* out, int n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DASH_B200_H */

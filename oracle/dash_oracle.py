@@ -330,6 +330,19 @@ def page_offsets(rng, S, n_heads, d, n_pages, page_tokens, std):
     return off
 
 
+def make_router_inputs(seed, B, S, n_pages, page_tokens, offset_std, d_idx=128, scale=0.5):
+    """Router idx_q/idx_k [B,S,d_idx] fp32 only (drawn like q/k, with page offsets)."""
+    rng = np.random.default_rng(seed)
+    iq = np.empty((B, S, d_idx), np.float32)
+    ik = np.empty((B, S, d_idx), np.float32)
+    for b in range(B):
+        ioff = (page_offsets(rng, S, 1, d_idx, n_pages, page_tokens, offset_std)[0]
+                if offset_std else 0.0)
+        iq[b] = rng.standard_normal((S, d_idx), dtype=np.float32) * scale + ioff
+        ik[b] = rng.standard_normal((S, d_idx), dtype=np.float32) * scale + ioff
+    return iq, ik
+
+
 def make_prefill_inputs(seed, B, H, S, D, n_pages, page_tokens, offset_std, d_idx=128,
                         scale=0.5):
     """q,k,v [B,H,S,D] and router idx_q/idx_k [B,S,d_idx] (fp32 numpy)."""

@@ -1,0 +1,130 @@
+"""C-ABI checks that need no GPU: the library loads, exports every function the
+header declares, its struct layouts match the Python binding, and malformed
+calls are rejected on the host with a status and a message."""
+import ctypes as C
+import os
+import re
+
+import pytest
+
+from ananta_ocr_b200 import _lib as L
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(__file__)), "include", "dash_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|size_t)\s+(dash_\w+)\s*\(", text, re.M)))
+
+
+def test_header_and_binding_agree():
+    assert declared_functions() == sorted(L.EXPORTS)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = L.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+
+
+def test_abi_struct_sizes():
+    L.load()
+    L.check_abi()
+
+
+def _call_status(fn, args):
+    lib = L.load()
+    return getattr(lib, fn)(C.byref(args), None)
+
+
+def test_route_rejects_bad_arguments():
+    a = L.DashRouteArgs()
+    assert _call_status("dash_route", a) == L.DASH_ERR_INVALID     # null outputs
+    assert "null" in L.last_error()
+    a.out_idx = a.out_bias = 16
+    a.width = 10
+    a.K, a.out_width = 4, 2
+    assert _call_status("dash_route", a) == L.DASH_ERR_INVALID     # K > out_width
+    a.out_width = 4
+    a.topm = 0
+    a.width = 1000
+    assert _call_status("dash_route", a) == L.DASH_ERR_UNSUPPORTED  # entmax window too wide
+
+
+def _prefill_args(head_dim=128, block_size=64, heads=10, kv_heads=10, K=4):
+    a = L.DashPrefillArgs()
+    a.seqs.n_seq, a.seqs.q_len_fixed, a.seqs.kv_len_fixed, a.seqs.max_q_len = 1, 256, 256, 256
+    a.kv.k = a.kv.v = 1 << 20
+    a.kv.dtype = L.DTYPE_BF16
+    a.kv.n_kv_heads, a.kv.head_dim = kv_heads, head_dim
+    a.kv.stride_seq, a.kv.stride_tok, a.kv.stride_head = 256 * kv_heads * 128, kv_heads * 128, 128
+    a.routes.idx = 1 << 21
+    a.routes.K = K
+    a.routes.row_stride = K
+    a.qo.q = a.qo.out = 1 << 22
+    a.qo.n_heads = heads
+    a.qo.q_stride_tok = a.qo.o_stride_tok = heads * 128
+    a.qo.q_stride_head = a.qo.o_stride_head = 128
+    a.block_size, a.local_window, a.scale = block_size, 256, 0.088
+    return a
+
+
+def test_prefill_rejects_unsupported_shapes():
+    assert _call_status("dash_prefill_attn", _prefill_args(head_dim=64)) == L.DASH_ERR_UNSUPPORTED
+    assert "head_dim" in L.last_error()
+    assert _call_status("dash_prefill_attn", _prefill_args(block_size=32)) == L.DASH_ERR_UNSUPPORTED
+    assert _call_status("dash_prefill_attn", _prefill_args(heads=12, kv_heads=8)) == L.DASH_ERR_INVALID
+    assert _call_status("dash_prefill_attn", _prefill_args(heads=24, kv_heads=8)) == L.DASH_ERR_UNSUPPORTED
+    assert _call_status("dash_prefill_attn", _prefill_args(K=300)) == L.DASH_ERR_UNSUPPORTED
+
+
+def test_prefill_requires_workspace():
+    a = _prefill_args()
+    lib = L.load()
+    need = lib.dash_prefill_workspace_size(C.byref(a))
+    assert need > 0
+    assert _call_status("dash_prefill_attn", a) == L.DASH_ERR_WORKSPACE
+    assert "workspace" in L.last_error()
+
+
+def test_decode_workspace_and_validation():
+    a = L.DashDecodeArgs()
+    a.seqs.n_seq, a.seqs.q_len_fixed, a.seqs.kv_len_fixed, a.seqs.max_q_len = 64, 1, 27556, 1
+    a.kv.k = a.kv.v = 1 << 20
+    a.kv.dtype = L.DTYPE_BF16
+    a.kv.n_kv_heads, a.kv.head_dim = 10, 128
+    a.kv.stride_seq, a.kv.stride_tok, a.kv.stride_head = 64 * 1280, 1280, 128
+    a.kv.block_table, a.kv.bt_stride, a.kv.num_pages = 1 << 23, 431, 27584
+    a.routes.idx, a.routes.K, a.routes.row_stride = 1 << 21, 32, 32
+    a.qo.q = a.qo.out = 1 << 22
+    a.qo.n_heads = 10
+    a.qo.q_stride_seq = a.qo.o_stride_seq = 1280
+    a.qo.q_stride_tok = a.qo.o_stride_tok = 1280
+    a.qo.q_stride_head = a.qo.o_stride_head = 128
+    a.block_size, a.local_window, a.scale = 64, 256, 0.088
+    lib = L.load()
+    a.num_splits = 4
+    assert lib.dash_decode_workspace_size(C.byref(a)) >= 64 * 10 * 4 * 130 * 4
+    assert _call_status("dash_decode_attn", a) == L.DASH_ERR_WORKSPACE
+    a.num_splits = 1
+    assert lib.dash_decode_workspace_size(C.byref(a)) == 0
+    a.kv.dtype = L.DTYPE_F32
+    assert _call_status("dash_decode_attn", a) == L.DASH_ERR_UNSUPPORTED
+
+
+def test_kbar_validation():
+    a = L.DashKbarArgs()
+    assert _call_status("dash_kbar_pool", a) == L.DASH_ERR_INVALID
+    a.keys = a.kbar = 1 << 20
+    a.dtype, a.d, a.block_size = L.DTYPE_F16, 128, 64
+    assert _call_status("dash_kbar_pool", a) == L.DASH_ERR_UNSUPPORTED
+
+
+def test_package_fails_loudly_without_library(tmp_path):
+    with pytest.raises(RuntimeError, match="no CPU or eager fallback"):
+        saved = L._lib
+        try:
+            L._lib = None
+            L.load(str(tmp_path / "missing.so"))
+        finally:
+            L._lib = saved
