@@ -136,6 +136,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// Warp-uniform variant: every lane waits, the warp proceeds only if all lanes
+// saw the phase complete (keeps the following .sync.aligned tcgen05 ops
+// converged even when the abort flag is raised mid-wait).
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity,
+                                               volatile int* abort_flag, DeviceError* err,
+                                               int where) {
+  bool ok = mbar_wait(bar, parity, abort_flag, err, where);
+  return __all_sync(0xffffffffu, ok);
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -192,11 +192,15 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_kernel(DashDecodeArgs a
   for (int it = it0 + warp; it < it1; it += kDecWarps) {
     const DecItem item = items[it];
     const float b2 = item.remote ? item.bias * 1.4426950408889634f : 0.0f;
-    // two keys per group per step (j, j+8): 16 loads of 16 B in flight per lane
-    for (int j = grp; j < item.nkeys; j += 16) {
+    // Two keys per group per step (j, j+8): 16 loads of 16 B in flight per lane.
+    // The trip count is the same for every lane of the warp (the shuffles
+    // below need all 32 lanes); lanes past the end use key 0 and mask it.
+    for (int j0 = 0; j0 < item.nkeys; j0 += 16) {
+      const int j = j0 + grp;
+      const bool one = j < item.nkeys;
       const bool two = j + 8 < item.nkeys;
-      const int64_t off0 = item.base + (int64_t)j * a.kv.stride_tok + sub * 32;
-      const int64_t off1 = two ? off0 + 8 * a.kv.stride_tok : off0;
+      const int64_t off0 = item.base + (int64_t)(one ? j : 0) * a.kv.stride_tok + sub * 32;
+      const int64_t off1 = item.base + (int64_t)(two ? j + 8 : 0) * a.kv.stride_tok + sub * 32;
       float k0[32], k1[32], v0[32], v1[32];
       load_row32(kbase + off0, k0);
       load_row32(kbase + off1, k1);
@@ -209,12 +213,13 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_kernel(DashDecodeArgs a
       s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
       s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
       s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-      s0 += b2;
+      s0 = one ? s0 + b2 : -INFINITY;
       s1 = two ? s1 + b2 : -INFINITY;
-      float mn = fmaxf(m, fmaxf(s0, s1));
-      float alpha = (m == -INFINITY) ? 0.0f : fast_exp2(m - mn);
-      float p0 = fast_exp2(s0 - mn);
-      float p1 = two ? fast_exp2(s1 - mn) : 0.0f;
+      const float mn = fmaxf(m, fmaxf(s0, s1));
+      if (mn == -INFINITY) continue;                  // nothing valid yet for this group
+      const float alpha = (m == -INFINITY) ? 0.0f : fast_exp2(m - mn);
+      const float p0 = one ? fast_exp2(s0 - mn) : 0.0f;
+      const float p1 = two ? fast_exp2(s1 - mn) : 0.0f;
       l = l * alpha + p0 + p1;
 #pragma unroll
       for (int c = 0; c < 32; ++c) o[c] = fmaf(p1, v1[c], fmaf(p0, v0[c], o[c] * alpha));

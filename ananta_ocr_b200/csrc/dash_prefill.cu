@@ -391,7 +391,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int blk = kt0 / bs;
       // zero V rows past the end of the sequence (never multiply garbage by P = 0)
       if (kt0 + BN > kvl) {
-        if (!mbar_wait(kv_full + st, (it / NSTAGE) & 1, abort_flag, derr, 60)) { alive = false; break; }
+        if (!mbar_wait_warp(kv_full + st, (it / NSTAGE) & 1, abort_flag, derr, 60)) { alive = false; break; }
         const int r0 = kvl - kt0;
         uint8_t* dV = sm + OFF_V + st * 16384;
         for (int e = m; e < (BN - r0) * 16; e += 128) {
@@ -408,7 +408,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       const bool sel = cur_b == blk;
       const float b2 = sel ? cur_bias * LOG2E : 0.0f;
-      if (!mbar_wait(s_full + sb, (it >> 1) & 1, abort_flag, derr, 61)) { alive = false; break; }
+      if (!mbar_wait_warp(s_full + sb, (it >> 1) & 1, abort_flag, derr, 61)) { alive = false; break; }
       tc_fence_after();
       uint32_t sr[64];
       {
@@ -439,7 +439,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const bool warp_need = __any_sync(0xffffffffu, need);
       if (warp_need) {
         if (it > 0) {
-          if (!mbar_wait(pv_done + ((it - 1) & 1), ((it - 1) >> 1) & 1, abort_flag, derr, 62)) { alive = false; break; }
+          if (!mbar_wait_warp(pv_done + ((it - 1) & 1), ((it - 1) >> 1) & 1, abort_flag, derr, 62)) { alive = false; break; }
           tc_fence_after();
           const float f = need ? (m_run == -INFINITY ? 0.0f : fast_exp2(m_run - m_new)) : 1.0f;
 #pragma unroll
@@ -468,7 +468,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       l_run += ls;
       // P buffer sb was last read by PV(it-2)
-      if (it >= 2 && !mbar_wait(pv_done + sb, ((it - 2) >> 1) & 1, abort_flag, derr, 63)) { alive = false; break; }
+      if (it >= 2 && !mbar_wait_warp(pv_done + sb, ((it - 2) >> 1) & 1, abort_flag, derr, 63)) { alive = false; break; }
       uint8_t* dP = sm + OFF_P + sb * 16384 + m * 128;
 #pragma unroll
       for (int c8 = 0; c8 < 8; ++c8)
@@ -482,7 +482,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // ---- epilogue ----
     float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
     bool have_o = alive && it > 0;
-    if (have_o && !mbar_wait(pv_done + ((it - 1) & 1), ((it - 1) >> 1) & 1, abort_flag, derr, 64)) have_o = false;
+    if (have_o && !mbar_wait_warp(pv_done + ((it - 1) & 1), ((it - 1) >> 1) & 1, abort_flag, derr, 64)) have_o = false;
     tc_fence_after();
     T* op = reinterpret_cast<T*>(a.qo.out) +
             (a.seqs.q_start ? rglob * a.qo.o_stride_tok
