@@ -113,6 +113,7 @@ EXPORTS = [
     "dash_kbar_pool", "dash_route", "dash_block_max", "dash_prefill_workspace_size",
     "dash_prefill_attn", "dash_decode_workspace_size", "dash_decode_attn", "dash_last_error",
     "dash_library_version", "dash_count_launches", "dash_abi_sizes",
+    "dash_decode_attn_noalloc", "dash_noalloc_scratch_bytes",
 ]
 
 
@@ -149,6 +150,10 @@ def load(path: str = LIB_PATH):
     L.dash_prefill_workspace_size.restype = C.c_size_t
     L.dash_decode_workspace_size.argtypes = [C.POINTER(DashDecodeArgs)]
     L.dash_decode_workspace_size.restype = C.c_size_t
+    L.dash_decode_attn_noalloc.argtypes = [C.POINTER(DashDecodeArgs), _p]
+    L.dash_decode_attn_noalloc.restype = C.c_int
+    L.dash_noalloc_scratch_bytes.argtypes = []
+    L.dash_noalloc_scratch_bytes.restype = C.c_size_t
     L.dash_last_error.argtypes = [C.c_char_p, C.c_int]
     L.dash_last_error.restype = C.c_int
     L.dash_library_version.restype = C.c_int

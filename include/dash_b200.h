@@ -284,6 +284,27 @@ typedef struct {
 size_t dash_decode_workspace_size(const DashDecodeArgs* args);
 int dash_decode_attn(const DashDecodeArgs* args, dash_stream_t stream);
 
+/* Allocation-free decode (no counterpart in the reference; the reference
+ * allocates its split scratch through PyTorch).  For callers that cannot call
+ * cudaMalloc or hand the library a workspace -- e.g. a host program whose
+ * device memory is owned by its own pool, or a bare FFI consumer without an
+ * allocator.  Same arguments and result as dash_decode_attn; `workspace` is
+ * ignored.  The split scratch is a fixed array of
+ * DASH_NOALLOC_SCRATCH_BYTES inside this library's device memory (each GPU
+ * that loads the library holds it until process exit); calls whose split
+ * scratch would exceed it return DASH_ERR_WORKSPACE with a message.  The
+ * first call on each device looks up the array's device address (with that
+ * device current), so make a first call on a device before any stream
+ * capture.  All calls share the one array, which keeps the last call's
+ * contents; every call first clears the arrival counters in it (an
+ * asynchronous memset on `stream`).  Calls that overlap on the GPU (other
+ * streams, other host threads) race on the array and must be serialised by
+ * the caller.  No cudaMalloc, cudaFree or allocating library routine is
+ * called. */
+#define DASH_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
+int dash_decode_attn_noalloc(const DashDecodeArgs* args, dash_stream_t stream);
+size_t dash_noalloc_scratch_bytes(void);
+
 /* ---------------------------------------------------------------------- */
 /* Diagnostics */
 int dash_last_error(char* buf, int len);     /* copies the last host-side error message */
