@@ -374,9 +374,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int32_t* rl = p.cidx + ((int64_t)ih * p.n_rows + rglob) * K;
     const float* rbl = p.cbias + ((int64_t)ih * p.n_rows + rglob) * K;
     const bool has_bias = a.routes.bias != nullptr;
+    // cursor = entry cur_j; the entry after it is kept prefetched in registers
+    // so an advance never waits on a global load inside the tile loop
     int cur_j = 0;
     int cur_b = (row_ok && K > 0) ? rl[0] : -1;
     float cur_bias = (row_ok && K > 0 && has_bias) ? rbl[0] : 0.0f;
+    int nxt_b = (row_ok && K > 1) ? rl[1] : -1;
+    float nxt_bias = (row_ok && K > 1 && has_bias) ? rbl[1] : 0.0f;
     const float sl2 = a.scale * 1.4426950408889634f;
     const float LOG2E = 1.4426950408889634f;
     float m_run = -INFINITY, l_run = 0.0f;
@@ -403,8 +407,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       // advance the routed-list cursor to this block
       while (cur_b >= 0 && cur_b < blk) {
         ++cur_j;
-        cur_b = cur_j < K ? rl[cur_j] : -1;
-        cur_bias = (cur_j < K && has_bias) ? rbl[cur_j] : 0.0f;
+        cur_b = nxt_b;
+        cur_bias = nxt_bias;
+        const int j2 = cur_j + 1;
+        nxt_b = (cur_b >= 0 && j2 < K) ? rl[j2] : -1;
+        nxt_bias = (cur_b >= 0 && j2 < K && has_bias) ? rbl[j2] : 0.0f;
       }
       const bool sel = cur_b == blk;
       const float b2 = sel ? cur_bias * LOG2E : 0.0f;

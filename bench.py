@@ -195,28 +195,75 @@ def prefill_flops(cfg, idx):
     return alg, executed
 
 
-def run_prefill(cfg, dev, steps, warmup, rank, world):
+class GraphStep:
+    """A step as two CUDA graphs (route part, attention part) replayed back to
+    back on the current stream, with CUDA events between them."""
+
+    def __init__(self, route_fn, attn_fn, use_graph=True):
+        import torch
+        self.route_fn, self.attn_fn = route_fn, attn_fn
+        self.graphs = None
+        if use_graph:
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):          # warm the capture stream
+                route_fn()
+                attn_fn()
+            torch.cuda.current_stream().wait_stream(s)
+            torch.cuda.synchronize()
+            g1, g2 = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g1):
+                route_fn()
+            with torch.cuda.graph(g2):
+                attn_fn()
+            self.graphs = (g1, g2)
+
+    def __call__(self, timers=None):
+        if timers:
+            timers[0].record()
+        self.graphs[0].replay() if self.graphs else self.route_fn()
+        if timers:
+            timers[1].record()
+        self.graphs[1].replay() if self.graphs else self.attn_fn()
+        if timers:
+            timers[2].record()
+
+
+def run_prefill(cfg, dev, steps, warmup, rank, world, use_graph=True):
     import torch
-    from ananta_ocr_b200 import _lib, ops
-    B, H, S, D, bs, K = (cfg[x] for x in ("B", "H", "S", "D", "bs", "K"))
+    from ananta_ocr_b200 import ops
+    B, H, S, D, bs, lb, K = (cfg[x] for x in ("B", "H", "S", "D", "bs", "lb", "K"))
     nblk = (S + bs - 1) // bs
     q, k, v, iq, ik = make_prefill(cfg, dev, 1234 + rank)
     ws = dict(kbar=torch.empty(B, nblk, 128, device=dev),
               idx=torch.empty(B * S, K, dtype=torch.int32, device=dev),
               bias=torch.empty(B * S, K, device=dev), out=torch.empty_like(q))
-    from ananta_ocr_b200 import _lib as L
-    probe = L.DashPrefillArgs()
     ws["attn_ws"] = None
     out, idx, bias = prefill_step(cfg, q, k, v, iq, ik, ws)
     ws["attn_ws"] = ops._WS.get((q.device, "prefill"))
+    torch.cuda.synchronize()
+    seqs = ops.Seqs(n_seq=B, q_len=S, kv_len=S, max_q_len=S)
+
+    def route_fn():
+        kb = ops.kbar_pool_contig(ik, None, bs, out=ws["kbar"])
+        ops.route(seqs, width=nblk, block_size=bs, local_blocks=lb, idx_scale=IDX_SCALE,
+                  prior_floor=1e-4, sigma=1.0, topm=K, K=K, idx_q=iq.view(B * S, 128), kbar=kb,
+                  out_idx=ws["idx"], out_bias=ws["bias"])
+
+    def attn_fn():
+        ops.gather_attention(q, k, v, ws["idx"].view(B, S, K), ws["bias"].view(B, S, K),
+                             block_size=bs, local_window=lb * bs, scale=1.0 / math.sqrt(D),
+                             out=ws["out"], workspace=ws["attn_ws"])
+
+    step = GraphStep(route_fn, attn_fn, use_graph)
     for _ in range(max(0, warmup - 1)):
-        prefill_step(cfg, q, k, v, iq, ik, ws)
+        step()
     torch.cuda.synchronize()
     alg, executed = prefill_flops(cfg, idx)
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     return dict(q=q, k=k, v=v, iq=iq, ik=ik, ws=ws, ev=ev, start=start, stop=stop, alg=alg,
-                executed=executed, idx=idx)
+                executed=executed, idx=idx, step=step)
 
 
 def run_decode_setup(cfg, dev, seed):
@@ -245,23 +292,33 @@ def run_decode_setup(cfg, dev, seed):
                 out=torch.empty(R, H, D, dtype=torch.bfloat16, device=dev), nb=nb)
 
 
-def decode_step(cfg, d, timers=None):
+def decode_route(cfg, d):
+    """k-bar refresh of each sequence's tail page + decode routing."""
     from ananta_ocr_b200.unlimited_dash_ops import route_triton as RT
-    from ananta_ocr_b200.unlimited_dash_ops.attend_triton import dash_sparse_attn_decode
-    R, H, S, D, bs, lb, K = (cfg[x] for x in ("R", "H", "S", "D", "bs", "lb", "K"))
-    if timers:
-        timers[0].record()
+    bs, lb, K = cfg["bs"], cfg["lb"], cfg["K"]
     RT.kbar_refresh_tail_triton(kv_cache=d["icache"], k_bar=d["kbar"], block_table=d["bt"],
                                 seq_lens=d["sl"], head_cls=None, block_size=bs, plan=d["tail"])
     RT.route_decode_triton(idx_q=d["iq"], k_bar=d["kbar"], block_table=d["bt"], seq_lens=d["sl"],
                            image_allow=None, out_idx=d["oi"], out_bias=d["ob"], max_block=d["nb"],
                            block_size=bs, local_blocks=lb, decode_query_len=1, idx_scale=IDX_SCALE,
                            prior_floor=1e-4, sigma=1.0, topm=K, budget=K, out_slots=K)
-    if timers:
-        timers[1].record()
+
+
+def decode_attend(cfg, d):
+    from ananta_ocr_b200.unlimited_dash_ops.attend_triton import dash_sparse_attn_decode
+    H, D, bs, lb = cfg["H"], cfg["D"], cfg["bs"], cfg["lb"]
     dash_sparse_attn_decode(d["q"], d["kc"], d["vc"], d["oi"][None].expand(H, -1, -1),
                             d["ob"][None].expand(H, -1, -1), d["bt"], d["sl"], H, 1.0 / math.sqrt(D),
                             d["out"], 1, local_blocks=lb, sparse_block_size=bs)
+
+
+def decode_step(cfg, d, timers=None):
+    if timers:
+        timers[0].record()
+    decode_route(cfg, d)
+    if timers:
+        timers[1].record()
+    decode_attend(cfg, d)
     if timers:
         timers[2].record()
 
@@ -327,6 +384,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="launch eagerly instead of replaying captured CUDA graphs")
     args = ap.parse_args()
     cfg = C2 if args.workload == "c2" else C4
     rank = int(os.environ.get("RANK", "0"))
@@ -366,12 +425,16 @@ def main():
     from ananta_ocr_b200 import _lib
     _lib.load()
 
-    st = run_prefill(cfg, dev, args.steps, args.warmup, rank, world)
+    st = run_prefill(cfg, dev, args.steps, args.warmup, rank, world, not args.no_graph)
     dec = None
     if not args.no_decode:
         dec = run_decode_setup(C3, dev, 77 + rank)
+        decode_step(C3, dec)
+        torch.cuda.synchronize()
+        dec["step"] = GraphStep(lambda: decode_route(C3, dec), lambda: decode_attend(C3, dec),
+                                not args.no_graph)
         for _ in range(args.warmup):
-            decode_step(C3, dec)
+            dec["step"]()
     torch.cuda.synchronize()
 
     # ---------------- timed prefill steps ----------------
@@ -381,13 +444,18 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    launches0 = _lib.launches()
     st["start"].record()
     for i in range(args.steps):
-        prefill_step(cfg, st["q"], st["k"], st["v"], st["iq"], st["ik"], st["ws"], st["ev"][i])
+        st["step"](st["ev"][i])
     st["stop"].record()
     torch.cuda.synchronize()
-    launches = _lib.launches() - launches0
+    # library kernels per step (counted on an eager step: graph replays re-launch
+    # the same captured kernels without passing through the library)
+    launches0 = _lib.launches()
+    st["step"].route_fn()
+    st["step"].attn_fn()
+    torch.cuda.synchronize()
+    launches = (_lib.launches() - launches0) * args.steps
     if world > 1:
         dist.barrier()
     total_ms = st["start"].elapsed_time(st["stop"])
@@ -400,7 +468,7 @@ def main():
         d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         d0.record()
         for i in range(args.steps):
-            decode_step(C3, dec, dev_ev[i])
+            dec["step"](dev_ev[i])
         d1.record()
         torch.cuda.synchronize()
         dec_total = d0.elapsed_time(d1) / args.steps
