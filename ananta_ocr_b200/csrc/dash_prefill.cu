@@ -383,7 +383,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     float nxt_bias = (row_ok && K > 1 && has_bias) ? rbl[1] : 0.0f;
     const float sl2 = a.scale * 1.4426950408889634f;
     const float LOG2E = 1.4426950408889634f;
-    float m_run = -INFINITY, l_run = 0.0f;
+    // Running max (exp2 domain) starts at the row's largest routed bias: the
+    // bias of the top entmax block is what makes a row's max jump, so starting
+    // there leaves rescaling of O for rows whose raw scores exceed it by > 2^8.
+    // Any start value is exact (O and l share the reference); a start above the
+    // true max only scales p by a power of two (no underflow for logits within
+    // ~100 of it).
+    float m_run = 0.0f, l_run = 0.0f;
+    if (row_ok && has_bias) {
+      for (int j = 0; j < K; ++j) {
+        if (rl[j] < 0) break;
+        m_run = fmaxf(m_run, rbl[j] * LOG2E);
+      }
+    }
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     TileIter itr{-1, -1, 0, 0u};
     int it = 0;
@@ -428,27 +440,30 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tc_fence_before();
       mbar_arrive(s_free + sb);
       // logits (exp2 domain) with the DASH mask
-      const int64_t hi = pos - kt0;                 // last causal column
-      const int64_t lo_loc = lstart - kt0;          // first local column
-      const int64_t lo_seg = segs - kt0;
+      // x = logit - m_run in the exp2 domain: one FFMA per element, the mask
+      // as selects; column c is kept iff lo <= c <= hi where lo is the first
+      // local column, or the first attendable column when the block is routed
+      const int hi = (int)max((int64_t)-1, min((int64_t)63, pos - kt0));
+      const int lo_seg = (int)max((int64_t)0, min((int64_t)64, segs - kt0));
+      const int lo_loc = (int)max((int64_t)0, min((int64_t)64, lstart - kt0));
+      const int lo = max(sel ? 0 : lo_loc, lo_seg);
+      const float add_loc = -m_run;
+      const float add_rem = b2 - m_run;
       float x[64];
-      float mx = -INFINITY;
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
-        float v = __uint_as_float(sr[c]) * sl2;
-        float lg = (c >= lo_loc) ? v : (sel ? v + b2 : -INFINITY);
-        lg = (c > hi || c < lo_seg) ? -INFINITY : lg;
-        x[c] = lg;
-        mx = fmaxf(mx, lg);
+        const float v = fmaf(__uint_as_float(sr[c]), sl2, c >= lo_loc ? add_loc : add_rem);
+        x[c] = (c >= lo && c <= hi) ? v : -INFINITY;
+        mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
       }
-      const float m_new = fmaxf(m_run, mx);
-      const bool need = m_new > m_run + 8.0f || (m_run == -INFINITY && m_new != -INFINITY);
-      const bool warp_need = __any_sync(0xffffffffu, need);
-      if (warp_need) {
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      const bool need = mx > 8.0f;               // row max grew by more than 2^8
+      if (__any_sync(0xffffffffu, need)) {
+        const float f = need ? fast_exp2(-mx) : 1.0f;
         if (it > 0) {
           if (!mbar_wait_warp(pv_done + ((it - 1) & 1), ((it - 1) >> 1) & 1, abort_flag, derr, 62)) { alive = false; break; }
           tc_fence_after();
-          const float f = need ? (m_run == -INFINITY ? 0.0f : fast_exp2(m_run - m_new)) : 1.0f;
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4) {
             uint32_t o[32];
@@ -459,21 +474,24 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             tmem_st32(tO + q4 * 32 + lane_base, o);
           }
           tmem_st_wait();
-          l_run *= f;
         }
-        if (need) m_run = m_new;
+        l_run *= f;
+        if (need) {
+          m_run += mx;
+#pragma unroll
+          for (int c = 0; c < 64; ++c) x[c] -= mx;
+        }
       }
-      const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-      float ls = 0.0f;
+      float ls4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       uint32_t pk[32];
 #pragma unroll
       for (int c = 0; c < 64; c += 2) {
-        float p0 = fast_exp2(x[c] - m_use);
-        float p1 = fast_exp2(x[c + 1] - m_use);
-        ls += p0 + p1;
+        const float p0 = fast_exp2(x[c]);
+        const float p1 = fast_exp2(x[c + 1]);
+        ls4[(c >> 1) & 3] += p0 + p1;
         pk[c >> 1] = pack2(p0, p1, (T*)nullptr);
       }
-      l_run += ls;
+      l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
       // P buffer sb was last read by PV(it-2)
       if (it >= 2 && !mbar_wait_warp(pv_done + sb, ((it - 2) >> 1) & 1, abort_flag, derr, 63)) { alive = false; break; }
       uint8_t* dP = sm + OFF_P + sb * 16384 + m * 128;

@@ -130,6 +130,57 @@ __device__ __forceinline__ uint32_t order_key(float x) {
 constexpr int kRouteWarps = 4;
 constexpr int kMaxM = 256;
 
+// Scores of blocks b = t0, t0+step, ... of one row into sx.  Four blocks are
+// in flight per thread (four independent accumulators); each dot product is
+// still one sequential __fmaf_rn chain over the feature index.
+__device__ __forceinline__ void score_blocks(const DashRouteArgs& a, const float* sq, float* sx,
+                                             int s, int64_t qblk, int kvl, int t0, int step) {
+  const int W = a.width;
+  const float inv_sqrt_d = (float)(1.0 / sqrt((double)a.d));
+  for (int b0 = t0; b0 < W; b0 += 4 * step) {
+    const float4* kb[4];
+    bool live[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int b = b0 + u * step;
+      live[u] = b < W && (int64_t)b <= qblk - a.local_blocks && (int64_t)b * a.block_size < kvl;
+      kb[u] = nullptr;
+      if (live[u]) {
+        int64_t kr = a.block_table ? (int64_t)a.block_table[(int64_t)s * a.bt_stride + b]
+                                   : (int64_t)s * a.kbar_seq_rows + b;
+        if (kr < 0 || kr >= a.num_kbar_rows) {
+          record_error(a.device_error, DASH_DEV_BAD_PAGE, 10, kr);
+          live[u] = false;
+        } else {
+          kb[u] = reinterpret_cast<const float4*>(a.kbar + kr * a.kbar_row_stride);
+        }
+      }
+    }
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int c4 = 0; c4 < a.d / 4; ++c4) {
+      const float q0 = sq[4 * c4 + 0], q1 = sq[4 * c4 + 1], q2 = sq[4 * c4 + 2], q3 = sq[4 * c4 + 3];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (!live[u]) continue;
+        const float4 k4 = __ldg(kb[u] + c4);
+        acc[u] = __fmaf_rn(q0, k4.x, acc[u]);
+        acc[u] = __fmaf_rn(q1, k4.y, acc[u]);
+        acc[u] = __fmaf_rn(q2, k4.z, acc[u]);
+        acc[u] = __fmaf_rn(q3, k4.w, acc[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int b = b0 + u * step;
+      if (b < W) sx[b] = live[u] ? clamp_act(__fmul_rn(acc[u], inv_sqrt_d)) : kScoreNeg;
+    }
+  }
+}
+
+// CTA_ROW = false: one warp per row (many rows).  CTA_ROW = true: one CTA per
+// row, all its threads score the row's blocks, warp 0 selects (few rows,
+// e.g. decode).
+template <bool CTA_ROW>
 __global__ void __launch_bounds__(kRouteWarps * 32) route_rows_kernel(DashRouteArgs a,
                                                                      int64_t n_rows) {
   extern __shared__ float smr[];
@@ -137,14 +188,15 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_rows_kernel(DashRouteA
   const int W = a.width;
   const int Wp = (W + 31) & ~31;
   // per-warp scratch: q [d] | x [Wp] | cand bits [Wp/32] | M items (id, x) | sel flags
-  float* sq = smr + warp * (a.d + Wp + Wp / 32 + 3 * kMaxM);
+  const int slot = CTA_ROW ? 0 : warp;
+  float* sq = smr + slot * (a.d + Wp + Wp / 32 + 3 * kMaxM);
   float* sx = sq + a.d;
   uint32_t* scand = reinterpret_cast<uint32_t*>(sx + Wp);
   int* mid_ = reinterpret_cast<int*>(scand + Wp / 32);
   float* mx = reinterpret_cast<float*>(mid_ + kMaxM);
   int* mrank = reinterpret_cast<int*>(mx + kMaxM);
 
-  const int64_t r = (int64_t)blockIdx.x * kRouteWarps + warp;
+  const int64_t r = CTA_ROW ? (int64_t)blockIdx.x : (int64_t)blockIdx.x * kRouteWarps + warp;
   if (r >= n_rows) return;
   int s, i;
   row_to_seq(a.seqs, r, s, i);
@@ -154,33 +206,18 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_rows_kernel(DashRouteA
 
   // ---- scores ----
   if (a.scores_in) {
+    if (CTA_ROW && warp != 0) return;
     for (int b = lane; b < W; b += 32) sx[b] = a.scores_in[r * a.scores_in_stride + b];
+  } else if (CTA_ROW) {
+    for (int c = threadIdx.x; c < a.d; c += blockDim.x) sq[c] = a.idx_q[r * a.q_row_stride + c];
+    __syncthreads();
+    score_blocks(a, sq, sx, s, qblk, kvl, threadIdx.x, blockDim.x);
+    __syncthreads();
+    if (warp != 0) return;
   } else {
     for (int c = lane; c < a.d; c += 32) sq[c] = a.idx_q[r * a.q_row_stride + c];
     __syncwarp();
-    const float inv_sqrt_d = (float)(1.0 / sqrt((double)a.d));
-    for (int b = lane; b < W; b += 32) {
-      float z = kScoreNeg;
-      if ((int64_t)b <= qblk - a.local_blocks && (int64_t)b * a.block_size < kvl) {
-        int64_t kr = a.block_table ? (int64_t)a.block_table[(int64_t)s * a.bt_stride + b]
-                                   : (int64_t)s * a.kbar_seq_rows + b;
-        if (kr < 0 || kr >= a.num_kbar_rows) {
-          record_error(a.device_error, DASH_DEV_BAD_PAGE, 10, kr);
-        } else {
-          const float4* kb = reinterpret_cast<const float4*>(a.kbar + kr * a.kbar_row_stride);
-          float acc = 0.0f;
-          for (int c4 = 0; c4 < a.d / 4; ++c4) {
-            float4 k4 = __ldg(kb + c4);
-            acc = __fmaf_rn(sq[4 * c4 + 0], k4.x, acc);
-            acc = __fmaf_rn(sq[4 * c4 + 1], k4.y, acc);
-            acc = __fmaf_rn(sq[4 * c4 + 2], k4.z, acc);
-            acc = __fmaf_rn(sq[4 * c4 + 3], k4.w, acc);
-          }
-          z = clamp_act(__fmul_rn(acc, inv_sqrt_d));
-        }
-      }
-      sx[b] = z;
-    }
+    score_blocks(a, sq, sx, s, qblk, kvl, lane, 32);
   }
   __syncwarp();
   if (a.scores_out)
@@ -456,12 +493,21 @@ int launch_route(const DashRouteArgs& a, int64_t n_rows, cudaStream_t st) {
   if (n_rows == 0) return DASH_OK;
   int Wp = (a.width + 31) & ~31;
   size_t per_warp = sizeof(float) * ((size_t)a.d + Wp + Wp / 32 + 3 * kMaxM);
-  size_t smem = per_warp * kRouteWarps;
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(route_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
-  int64_t grid = (n_rows + kRouteWarps - 1) / kRouteWarps;
-  route_rows_kernel<<<(unsigned)grid, kRouteWarps * 32, smem, st>>>(a, n_rows);
+  // few rows (decode): one CTA per row so all its threads score; else warp per row
+  const bool cta_row = n_rows < 148 * 16;
+  size_t smem = per_warp * (cta_row ? 1 : kRouteWarps);
+  if (cta_row) {
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(route_rows_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem);
+    route_rows_kernel<true><<<(unsigned)n_rows, kRouteWarps * 32, smem, st>>>(a, n_rows);
+  } else {
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(route_rows_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem);
+    int64_t grid = (n_rows + kRouteWarps - 1) / kRouteWarps;
+    route_rows_kernel<false><<<(unsigned)grid, kRouteWarps * 32, smem, st>>>(a, n_rows);
+  }
   count_launch();
   return check_launch("route_rows_kernel");
 }

@@ -164,6 +164,30 @@ def test_paged_prefill_with_prefix(bs, lb):
     assert_close_bf16(out.float().cpu().numpy(), ref)
 
 
+def test_prefill_config4_geometry_sampled_rows():
+    """BASELINE config 4 geometry (block 128, window 8 blocks = 1024 tokens,
+    k=64, 16 heads) on one 32,768-token sequence: router + attention on the GPU,
+    routes bit-exact, output vs the oracle on sampled rows."""
+    B, H, S, D, bs, lb, K = 1, 16, 32768, 128, 128, 8, 64
+    q, k, v, iq, ik = O.make_prefill_inputs(8, B, H, S, D, S // 273, 273, 0.2)
+    out, idx, bias = MD.dash_prefill_forward(
+        torch.from_numpy(q).cuda().bfloat16(), torch.from_numpy(k).cuda().bfloat16(),
+        torch.from_numpy(v).cuda().bfloat16(), torch.from_numpy(iq).cuda(),
+        torch.from_numpy(ik).cuda(), block_size=bs, local_blocks=lb, K=K,
+        idx_scale=128.0 / math.sqrt(128), prior_floor=1e-4, sigma=1.0, return_routes=True)
+    rows = sample_rows(np.random.default_rng(2), S, 40)
+    gi = idx.cpu().numpy()
+    kb = O.kbar_contig(ik, np.zeros(128, np.float32), bs)
+    nblk = kb.shape[1]
+    osc = O.scores_paged(iq[0, rows], rows, np.zeros(len(rows), np.int64), np.array([S]), kb[0],
+                         np.arange(nblk, dtype=np.int32)[None], bs, lb, nblk)
+    oi, _, _ = O.route_select(osc, None, 128.0 / math.sqrt(128), K, K, 1e-4, 1.0)
+    np.testing.assert_array_equal(gi[0, rows], oi)
+    ref = O.attend_contig(bf16_round(q), bf16_round(k), bf16_round(v), gi, bias.cpu().numpy(), bs,
+                          lb * bs, 1.0 / math.sqrt(D), rows=rows)
+    assert_close_bf16(out.float().cpu().numpy()[:, :, rows], ref)
+
+
 def test_prefill_config2_full_size_sampled_rows():
     """BASELINE config 2 (B=4, H=10, S=9248, bs=64, window 4, K=16, page
     offsets): router + attention on the GPU; routes checked bit-exact and the
