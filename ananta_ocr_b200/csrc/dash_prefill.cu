@@ -451,11 +451,27 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const float add_rem = b2 - m_run;
       float x[64];
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      // Pure tile for this row: all 64 columns kept with one additive term, or
+      // none kept.  When every row of the warp is pure (all tiles away from the
+      // window edge and the diagonal) a row costs one FFMA per column.
+      const bool empty = lo > hi;
+      const bool full = lo == 0 && hi == 63 && (lo_loc == 0 || lo_loc == 64);
+      if (__all_sync(0xffffffffu, empty || full)) {
+        const float add = lo_loc == 0 ? add_loc : add_rem;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float v = fmaf(__uint_as_float(sr[c]), sl2, c >= lo_loc ? add_loc : add_rem);
-        x[c] = (c >= lo && c <= hi) ? v : -INFINITY;
-        mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
+        for (int c = 0; c < 64; ++c) {
+          // an empty row may sit on key columns past the sequence end (garbage
+          // K): select, never add, the -inf
+          x[c] = empty ? -INFINITY : fmaf(__uint_as_float(sr[c]), sl2, add);
+          mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const float v = fmaf(__uint_as_float(sr[c]), sl2, c >= lo_loc ? add_loc : add_rem);
+          x[c] = (c >= lo && c <= hi) ? v : -INFINITY;
+          mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
+        }
       }
       const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       const bool need = mx > 8.0f;               // row max grew by more than 2^8
