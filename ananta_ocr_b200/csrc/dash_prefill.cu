@@ -29,16 +29,18 @@ constexpr int BM = 128;          // tile rows (M of both MMAs)
 constexpr int BN = 64;           // keys per key tile (N of QK, K of PV)
 constexpr int HD = 128;          // head dim
 constexpr int NSTAGE = 3;
-constexpr int OFF_Q = 0;                          // 2 x [128 x 128 B]
-constexpr int OFF_K = 32768;                      // NSTAGE x 2 x [64 x 128 B]
+// two query tiles (A, B) per CTA share the K/V stream
+constexpr int OFF_Q = 0;                          // 2 tiles x 2 x [128 x 128 B]
+constexpr int OFF_K = 65536;                      // NSTAGE x 2 x [64 x 128 B]
 constexpr int OFF_V = OFF_K + NSTAGE * 16384;     // NSTAGE x 2 x [64 x 128 B]
-constexpr int OFF_P = OFF_V + NSTAGE * 16384;     // 2 x [128 x 128 B]
-constexpr int OFF_MASK = OFF_P + 2 * 16384;       // block mask words
+constexpr int OFF_P = OFF_V + NSTAGE * 16384;     // 2 tiles x 2 buffers x [128 x 128 B]
+constexpr int OFF_MASK = OFF_P + 4 * 16384;       // block mask words
 constexpr int MAX_MASK_WORDS = 256;               // <= 8192 blocks
 constexpr int OFF_BAR = OFF_MASK + MAX_MASK_WORDS * 4;
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;  // + alignment slack
-constexpr int NTHREADS = 192;
-constexpr uint32_t TMEM_COLS = 256;               // S0 | S1 | O
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+constexpr int NTHREADS = 320;                     // 8 softmax warps, TMA warp, MMA warp
+constexpr uint32_t TMEM_COLS = 512;               // per tile: S0 | S1 | O
 constexpr int kPlanMaxK = 256;                    // routed slots per row
 
 struct PrefillPlan {
@@ -183,29 +185,29 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
   uint64_t* kv_full = bars + 0;      // [NSTAGE]
   uint64_t* kv_empty = bars + 3;     // [NSTAGE]
-  uint64_t* s_full = bars + 6;       // [2]
-  uint64_t* s_free = bars + 8;       // [2]
-  uint64_t* p_full = bars + 10;      // [2]
-  uint64_t* pv_done = bars + 12;     // [2]
-  uint64_t* q_full = bars + 14;
-  uint64_t* mma_done = bars + 15;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 16);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 17);
+  // per softmax group g (9 barriers each from bars + 6 + 9g):
+  //   s_full[2], s_free[2], p_full[2], pv_done[2], q_full
+  uint64_t* mma_done = bars + 24;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 25);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 26);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_seq = a.seqs.n_seq;
-  // heaviest (last) tiles first
+  // two consecutive query tiles per CTA; heaviest (last) pairs first
+  const int pairs = (p.tiles_per_seq + 1) >> 1;
   const int jj = blockIdx.x / n_seq;
   const int s = blockIdx.x - jj * n_seq;
-  const int tj = p.tiles_per_seq - 1 - jj;
+  const int pj = pairs - 1 - jj;
   const int hk = blockIdx.y;
   const int qlen = q_len_of(a.seqs, s);
-  const int i0 = tj * p.TT;
-  if (i0 >= qlen) return;
+  const int i0A = 2 * pj * p.TT;
+  if (i0A >= qlen) return;
+  const bool hasB = i0A + p.TT < qlen;
+  const int ngroups = hasB ? 2 : 1;
   const int kvl = kv_len_of(a.seqs, s);
   const int pos0 = pos0_of(a.seqs, s);
-  const int ntok = min(p.TT, qlen - i0);
-  const int64_t pmin = (int64_t)pos0 + i0, pmax = pmin + ntok - 1;
+  const int ntok_all = min(2 * p.TT, qlen - i0A);
+  const int64_t pmin = (int64_t)pos0 + i0A, pmax = pmin + ntok_all - 1;
   const int G = p.G;
   const int H = a.qo.n_heads;
   const int nih = a.routes.n_index_heads > 0 ? a.routes.n_index_heads : 1;
@@ -215,22 +217,29 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   // ---- setup: barriers, TMEM, block mask ----
   if (tid == 0) {
     for (int k = 0; k < NSTAGE; ++k) { mbar_init(kv_full + k, 1); mbar_init(kv_empty + k, 1); }
-    for (int k = 0; k < 2; ++k) {
-      mbar_init(s_full + k, 1); mbar_init(s_free + k, 128);
-      mbar_init(p_full + k, 128); mbar_init(pv_done + k, 1);
+    for (int g = 0; g < 2; ++g) {
+      uint64_t* gb = bars + 6 + 9 * g;
+      for (int k = 0; k < 2; ++k) {
+        mbar_init(gb + 0 + k, 1);      // s_full
+        mbar_init(gb + 2 + k, 128);    // s_free
+        mbar_init(gb + 4 + k, 128);    // p_full
+        mbar_init(gb + 6 + k, 1);      // pv_done
+      }
+      mbar_init(gb + 8, 128);          // q_full
     }
-    mbar_init(q_full, 128);
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     mbar_init_fence();
   }
-  if (warp == 5) { tmem_alloc(tmem_holder, TMEM_COLS); tmem_relinquish(); }
+  if (warp == 9) { tmem_alloc(tmem_holder, TMEM_COLS); tmem_relinquish(); }
   {
-    const uint32_t* um = p.tmask + ((int64_t)ih * n_seq * p.tiles_per_seq + (int64_t)s * p.tiles_per_seq + tj) * p.nwords;
+    const int64_t tbase = (int64_t)ih * n_seq * p.tiles_per_seq + (int64_t)s * p.tiles_per_seq + 2 * pj;
+    const uint32_t* umA = p.tmask + tbase * p.nwords;
+    const uint32_t* umB = hasB ? umA + p.nwords : nullptr;
     const int64_t lb0 = max((int64_t)0, (pmin - a.local_window + 1) / bs);
     const int64_t lb1 = pmax / bs;
     for (int w = tid; w < p.nwords; w += NTHREADS) {
-      uint32_t m = um[w];
+      uint32_t m = umA[w] | (umB ? umB[w] : 0u);
       int64_t b0 = (int64_t)w * 32;
       for (int k = 0; k < 32; ++k) {
         int64_t b = b0 + k;
@@ -243,10 +252,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const uint32_t tS = tmem, tO = tmem + 128;
   DeviceError* derr = a.device_error;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // =================== TMA producer ===================
     if (lane == 0) {
       prefetch_tmap(&tmK);
@@ -291,29 +299,34 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         mbar_wait(kv_full + (k % NSTAGE), (k / NSTAGE) & 1, &no_abort, nullptr, 42);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // =================== MMA issuer ===================
     if (lane == 0) {
       constexpr uint32_t fmt = DType<T>::fmt;
       constexpr uint32_t idesc_qk = make_idesc(fmt, 0, 0, BM, BN);
       constexpr uint32_t idesc_pv = make_idesc(fmt, 0, 1, BM, HD);
-      const uint32_t sQ = smem_u32(sm + OFF_Q);
-      bool alive = mbar_wait(q_full, 0, abort_flag, derr, 50);
+      bool alive = true;
+      for (int g = 0; g < ngroups && alive; ++g)
+        alive = mbar_wait(bars + 6 + 9 * g + 8, 0, abort_flag, derr, 50);
       TileIter itr{-1, -1, 0, 0u};
       int it = 0;
       auto issue_pv = [&](int j) -> bool {
         const int pb = j & 1;
-        if (!mbar_wait(p_full + pb, (j >> 1) & 1, abort_flag, derr, 51)) return false;
-        tc_fence_after();
-        const uint32_t sP = smem_u32(sm + OFF_P + pb * 16384);
         const uint32_t sV = smem_u32(sm + OFF_V + (j % NSTAGE) * 16384);
+        for (int g = 0; g < ngroups; ++g) {
+          uint64_t* gb = bars + 6 + 9 * g;
+          if (!mbar_wait(gb + 4 + pb, (j >> 1) & 1, abort_flag, derr, 51)) return false;
+          tc_fence_after();
+          const uint32_t sP = smem_u32(sm + OFF_P + (2 * g + pb) * 16384);
+          const uint32_t tO = tmem + g * 256 + 128;
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          uint64_t ad = sw128_desc(sP + kk * 32, 16, 1024);
-          uint64_t bd = sw128_desc(sV + kk * 2048, 8192, 1024);
-          umma_ss(tO, ad, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            uint64_t ad = sw128_desc(sP + kk * 32, 16, 1024);
+            uint64_t bd = sw128_desc(sV + kk * 2048, 8192, 1024);
+            umma_ss(tO, ad, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(gb + 6 + pb);
         }
-        umma_commit(pv_done + pb);
         umma_commit(kv_empty + (j % NSTAGE));
         return true;
       };
@@ -322,16 +335,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (kt0 < 0) break;
         const int st = it % NSTAGE, sb = it & 1;
         if (!mbar_wait(kv_full + st, (it / NSTAGE) & 1, abort_flag, derr, 52)) { alive = false; break; }
-        if (it >= 2 && !mbar_wait(s_free + sb, ((it >> 1) - 1) & 1, abort_flag, derr, 53)) { alive = false; break; }
-        tc_fence_after();
         const uint32_t sK = smem_u32(sm + OFF_K + st * 16384);
+        for (int g = 0; g < ngroups && alive; ++g) {
+          uint64_t* gb = bars + 6 + 9 * g;
+          if (it >= 2 && !mbar_wait(gb + 2 + sb, ((it >> 1) - 1) & 1, abort_flag, derr, 53)) { alive = false; break; }
+          tc_fence_after();
+          const uint32_t sQ = smem_u32(sm + OFF_Q + g * 32768);
+          const uint32_t tS = tmem + g * 256 + sb * BN;
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          uint64_t ad = sw128_desc(sQ + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-          uint64_t bd = sw128_desc(sK + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
-          umma_ss(tS + sb * BN, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            uint64_t ad = sw128_desc(sQ + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+            uint64_t bd = sw128_desc(sK + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
+            umma_ss(tS, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(gb + 0 + sb);
         }
-        umma_commit(s_full + sb);
+        if (!alive) break;
         if (it >= 1 && !issue_pv(it - 1)) { alive = false; break; }
         ++it;
       }
@@ -342,9 +361,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_wait(mma_done, 0, &no_abort, nullptr, 54);
     }
     __syncwarp();
-  } else {
-    // =================== softmax / epilogue (one thread per row) ===================
-    const int m = tid;                       // row 0..127
+  } else if (warp / 4 < ngroups) {
+    // ============ softmax / epilogue: group g, one thread per tile row ============
+    const int g = warp >> 2;
+    uint64_t* gb = bars + 6 + 9 * g;
+    uint64_t* s_full = gb + 0;
+    uint64_t* s_free = gb + 2;
+    uint64_t* p_full = gb + 4;
+    uint64_t* pv_done = gb + 6;
+    uint64_t* q_full = gb + 8;
+    const uint32_t tS = tmem + g * 256, tO = tmem + g * 256 + 128;
+    const int m = tid & 127;                 // row 0..127 of this group's tile
+    const int i0 = i0A + g * p.TT;
+    const int ntok = min(p.TT, qlen - i0);
     const int tok = i0 + m / G;
     const int hq = hk * G + (m % G);
     const bool row_ok = (m / G) < ntok;
@@ -358,7 +387,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     (a.seqs.q_start ? rglob * a.qo.q_stride_tok
                                     : (int64_t)s * a.qo.q_stride_seq + (int64_t)tok * a.qo.q_stride_tok) +
                     (int64_t)hq * a.qo.q_stride_head;
-      uint8_t* sq = sm + OFF_Q;
+      uint8_t* sq = sm + OFF_Q + g * 32768;
 #pragma unroll
       for (int cc = 0; cc < 16; ++cc) {
         uint4 v = make_uint4(0, 0, 0, 0);
@@ -396,7 +425,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         m_run = fmaxf(m_run, rbl[j] * LOG2E);
       }
     }
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     TileIter itr{-1, -1, 0, 0u};
     int it = 0;
     bool alive = true;
@@ -429,17 +458,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const float b2 = sel ? cur_bias * LOG2E : 0.0f;
       if (!mbar_wait_warp(s_full + sb, (it >> 1) & 1, abort_flag, derr, 61)) { alive = false; break; }
       tc_fence_after();
-      uint32_t sr[64];
-      {
-        uint32_t (&r0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sr[0]);
-        uint32_t (&r1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sr[32]);
-        tmem_ld32(tS + sb * BN + lane_base, r0);
-        tmem_ld32(tS + sb * BN + 32 + lane_base, r1);
-        tmem_ld_wait();
-      }
+      float x[64];                               // S, then logit - m_run in place
+      tmem_ld32f(tS + sb * BN + lane_base, x);
+      tmem_ld32f(tS + sb * BN + 32 + lane_base, x + 32);
+      tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(s_free + sb);
-      // logits (exp2 domain) with the DASH mask
       // x = logit - m_run in the exp2 domain: one FFMA per element, the mask
       // as selects; column c is kept iff lo <= c <= hi where lo is the first
       // local column, or the first attendable column when the block is routed
@@ -449,7 +473,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int lo = max(sel ? 0 : lo_loc, lo_seg);
       const float add_loc = -m_run;
       const float add_rem = b2 - m_run;
-      float x[64];
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       // Pure tile for this row: all 64 columns kept with one additive term, or
       // none kept.  When every row of the warp is pure (all tiles away from the
@@ -462,13 +485,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         for (int c = 0; c < 64; ++c) {
           // an empty row may sit on key columns past the sequence end (garbage
           // K): select, never add, the -inf
-          x[c] = empty ? -INFINITY : fmaf(__uint_as_float(sr[c]), sl2, add);
+          x[c] = empty ? -INFINITY : fmaf(x[c], sl2, add);
           mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
         }
       } else {
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
-          const float v = fmaf(__uint_as_float(sr[c]), sl2, c >= lo_loc ? add_loc : add_rem);
+          const float v = fmaf(x[c], sl2, c >= lo_loc ? add_loc : add_rem);
           x[c] = (c >= lo && c <= hi) ? v : -INFINITY;
           mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
         }
@@ -498,23 +521,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           for (int c = 0; c < 64; ++c) x[c] -= mx;
         }
       }
+      // P buffer sb was last read by PV(it-2) (long done by now in practice)
+      if (it >= 2 && !mbar_wait_warp(pv_done + sb, ((it - 2) >> 1) & 1, abort_flag, derr, 63)) { alive = false; break; }
+      uint8_t* dP = sm + OFF_P + (2 * g + sb) * 16384 + m * 128;
       float ls4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      uint32_t pk[32];
 #pragma unroll
-      for (int c = 0; c < 64; c += 2) {
-        const float p0 = fast_exp2(x[c]);
-        const float p1 = fast_exp2(x[c + 1]);
-        ls4[(c >> 1) & 3] += p0 + p1;
-        pk[c >> 1] = pack2(p0, p1, (T*)nullptr);
+      for (int c8 = 0; c8 < 8; ++c8) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = fast_exp2(x[8 * c8 + 2 * e]);
+          const float p1 = fast_exp2(x[8 * c8 + 2 * e + 1]);
+          ls4[e] += p0 + p1;
+          pk[e] = pack2(p0, p1, (T*)nullptr);
+        }
+        *reinterpret_cast<uint4*>(dP + ((c8 ^ (m & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
       l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
-      // P buffer sb was last read by PV(it-2)
-      if (it >= 2 && !mbar_wait_warp(pv_done + sb, ((it - 2) >> 1) & 1, abort_flag, derr, 63)) { alive = false; break; }
-      uint8_t* dP = sm + OFF_P + sb * 16384 + m * 128;
-#pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8)
-        *reinterpret_cast<uint4*>(dP + ((c8 ^ (m & 7)) << 4)) =
-            make_uint4(pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full + sb);
@@ -557,7 +580,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 5) tmem_dealloc(tmem, TMEM_COLS);
+  if (warp == 9) tmem_dealloc(tmem, TMEM_COLS);
 }
 
 // ---------------------------------------------------------------------------
@@ -656,7 +679,7 @@ int launch_prefill(const DashPrefillArgs& a, int64_t n_rows, cudaStream_t st) {
   if (rc) return rc;
   rc = make_kv_map(&mv, a.kv.v, a, p.paged);
   if (rc) return rc;
-  dim3 grid((unsigned)(a.seqs.n_seq * p.tiles_per_seq), a.kv.n_kv_heads);
+  dim3 grid((unsigned)(a.seqs.n_seq * ((p.tiles_per_seq + 1) / 2)), a.kv.n_kv_heads);
   auto launch = [&](auto kern) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     kern<<<grid, NTHREADS, SMEM_BYTES, st>>>(mk, mv, a, p);
