@@ -283,6 +283,26 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t ab_fmt, uint32_t a_mn
          ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
+// Packed fp32x2 arithmetic (sm_100): one instruction for two lanes of data.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t v;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(a), "f"(b));
+  return v;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 template <typename T> struct DType;
 template <> struct DType<__nv_bfloat16> { static constexpr uint32_t fmt = 1; };
 template <> struct DType<__half> { static constexpr uint32_t fmt = 0; };
@@ -294,6 +314,15 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, __nv_bfloat16*) {
 __device__ __forceinline__ uint32_t pack2(float a, float b, __half*) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+// elementwise max of two packed 16-bit pairs, and the larger half as fp32
+__device__ __forceinline__ uint32_t hmax2u(uint32_t a, uint32_t b, __nv_bfloat16*) {
+  __nv_bfloat162 r = __hmax2(*reinterpret_cast<__nv_bfloat162*>(&a), *reinterpret_cast<__nv_bfloat162*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t hmax2u(uint32_t a, uint32_t b, __half*) {
+  __half2 r = __hmax2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
 }
 __device__ __forceinline__ float2 unpack2(uint32_t u, __nv_bfloat16*) {
   __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&u);

@@ -473,71 +473,99 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int lo = max(sel ? 0 : lo_loc, lo_seg);
       const float add_loc = -m_run;
       const float add_rem = b2 - m_run;
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      // P buffer sb was last read by PV(it-2) (long done by now in practice)
+      if (it >= 2 && !mbar_wait_warp(pv_done + sb, ((it - 2) >> 1) & 1, abort_flag, derr, 63)) { alive = false; break; }
+      uint8_t* dP = sm + OFF_P + (2 * g + sb) * 16384 + m * 128;
       // Pure tile for this row: all 64 columns kept with one additive term, or
-      // none kept.  When every row of the warp is pure (all tiles away from the
-      // window edge and the diagonal) a row costs one FFMA per column.
+      // none kept.  When every row of the warp is pure and the tile lies inside
+      // the sequence (tiles away from the window edge and the diagonal), the
+      // logits take one packed FFMA per 2 columns (an empty row adds -inf), P is
+      // produced directly, and the rescale test runs on the packed P maximum.
       const bool empty = lo > hi;
       const bool full = lo == 0 && hi == 63 && (lo_loc == 0 || lo_loc == 64);
-      if (__all_sync(0xffffffffu, empty || full)) {
-        const float add = lo_loc == 0 ? add_loc : add_rem;
+      bool done = false;
+      float mx = -INFINITY;
+      if (__all_sync(0xffffffffu, empty || full) && kt0 + BN <= kvl) {
+        const float add = empty ? -INFINITY : (lo_loc == 0 ? add_loc : add_rem);
+        const uint64_t sl2v = f2_pack(sl2, sl2), addv = f2_pack(add, add);
+        uint64_t lsv = f2_pack(0.0f, 0.0f);
+        uint32_t pmax = 0;                         // packed +0.0 pair
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          // an empty row may sit on key columns past the sequence end (garbage
-          // K): select, never add, the -inf
-          x[c] = empty ? -INFINITY : fmaf(x[c], sl2, add);
-          mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
+        for (int c8 = 0; c8 < 8; ++c8) {
+          uint32_t pk[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int c = 8 * c8 + 2 * e;
+            f2_unpack(ffma2(f2_pack(x[c], x[c + 1]), sl2v, addv), x[c], x[c + 1]);
+            const float p0 = fast_exp2(x[c]);
+            const float p1 = fast_exp2(x[c + 1]);
+            lsv = fadd2(lsv, f2_pack(p0, p1));
+            pk[e] = pack2(p0, p1, (T*)nullptr);
+            pmax = hmax2u(pmax, pk[e], (T*)nullptr);
+          }
+          *reinterpret_cast<uint4*>(dP + ((c8 ^ (m & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+        const float2 pm = unpack2(pmax, (T*)nullptr);
+        const bool big = !(fmaxf(pm.x, pm.y) <= 256.0f);   // p > 2^8 (or inf/NaN)
+        if (!__any_sync(0xffffffffu, big)) {
+          float l0, l1;
+          f2_unpack(lsv, l0, l1);
+          l_run += l0 + l1;
+          done = true;
+        } else {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) mx = fmaxf(mx, x[c]);
         }
       } else {
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
           const float v = fmaf(x[c], sl2, c >= lo_loc ? add_loc : add_rem);
           x[c] = (c >= lo && c <= hi) ? v : -INFINITY;
           mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
         }
+        mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       }
-      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-      const bool need = mx > 8.0f;               // row max grew by more than 2^8
-      if (__any_sync(0xffffffffu, need)) {
-        const float f = need ? fast_exp2(-mx) : 1.0f;
-        if (it > 0) {
-          if (!mbar_wait_warp(pv_done + ((it - 1) & 1), ((it - 1) >> 1) & 1, abort_flag, derr, 62)) { alive = false; break; }
-          tc_fence_after();
+      if (!done) {
+        const bool need = mx > 8.0f;             // row max grew by more than 2^8
+        if (__any_sync(0xffffffffu, need)) {
+          const float f = need ? fast_exp2(-mx) : 1.0f;
+          if (it > 0) {
+            if (!mbar_wait_warp(pv_done + ((it - 1) & 1), ((it - 1) >> 1) & 1, abort_flag, derr, 62)) { alive = false; break; }
+            tc_fence_after();
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            uint32_t o[32];
-            tmem_ld32(tO + q4 * 32 + lane_base, o);
-            tmem_ld_wait();
+            for (int q4 = 0; q4 < 4; ++q4) {
+              uint32_t o[32];
+              tmem_ld32(tO + q4 * 32 + lane_base, o);
+              tmem_ld_wait();
 #pragma unroll
-            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * f);
-            tmem_st32(tO + q4 * 32 + lane_base, o);
+              for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * f);
+              tmem_st32(tO + q4 * 32 + lane_base, o);
+            }
+            tmem_st_wait();
           }
-          tmem_st_wait();
-        }
-        l_run *= f;
-        if (need) {
-          m_run += mx;
+          l_run *= f;
+          if (need) {
+            m_run += mx;
 #pragma unroll
-          for (int c = 0; c < 64; ++c) x[c] -= mx;
+            for (int c = 0; c < 64; ++c) x[c] -= mx;
+          }
         }
+        float ls4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          uint32_t pk[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float p0 = fast_exp2(x[8 * c8 + 2 * e]);
+            const float p1 = fast_exp2(x[8 * c8 + 2 * e + 1]);
+            ls4[e] += p0 + p1;
+            pk[e] = pack2(p0, p1, (T*)nullptr);
+          }
+          *reinterpret_cast<uint4*>(dP + ((c8 ^ (m & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+        l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
       }
-      // P buffer sb was last read by PV(it-2) (long done by now in practice)
-      if (it >= 2 && !mbar_wait_warp(pv_done + sb, ((it - 2) >> 1) & 1, abort_flag, derr, 63)) { alive = false; break; }
-      uint8_t* dP = sm + OFF_P + (2 * g + sb) * 16384 + m * 128;
-      float ls4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
-        uint32_t pk[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float p0 = fast_exp2(x[8 * c8 + 2 * e]);
-          const float p1 = fast_exp2(x[8 * c8 + 2 * e + 1]);
-          ls4[e] += p0 + p1;
-          pk[e] = pack2(p0, p1, (T*)nullptr);
-        }
-        *reinterpret_cast<uint4*>(dP + ((c8 ^ (m & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      }
-      l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full + sb);

@@ -177,52 +177,13 @@ __device__ __forceinline__ void score_blocks(const DashRouteArgs& a, const float
   }
 }
 
-// CTA_ROW = false: one warp per row (many rows).  CTA_ROW = true: one CTA per
-// row, all its threads score the row's blocks, warp 0 selects (few rows,
-// e.g. decode).
-template <bool CTA_ROW>
-__global__ void __launch_bounds__(kRouteWarps * 32) route_rows_kernel(DashRouteArgs a,
-                                                                     int64_t n_rows) {
-  extern __shared__ float smr[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// Selection for one row whose W scores are in sx (overwritten), by one warp:
+// candidates, x = score*scale, top-M radix select, ranks, entmax, bias, pack.
+__device__ __noinline__ void select_row(const DashRouteArgs& a, float* sx, uint32_t* scand,
+                                        int* mid_, float* mx, int* mrank, int64_t r, int s,
+                                        int lane) {
   const int W = a.width;
   const int Wp = (W + 31) & ~31;
-  // per-warp scratch: q [d] | x [Wp] | cand bits [Wp/32] | M items (id, x) | sel flags
-  const int slot = CTA_ROW ? 0 : warp;
-  float* sq = smr + slot * (a.d + Wp + Wp / 32 + 3 * kMaxM);
-  float* sx = sq + a.d;
-  uint32_t* scand = reinterpret_cast<uint32_t*>(sx + Wp);
-  int* mid_ = reinterpret_cast<int*>(scand + Wp / 32);
-  float* mx = reinterpret_cast<float*>(mid_ + kMaxM);
-  int* mrank = reinterpret_cast<int*>(mx + kMaxM);
-
-  const int64_t r = CTA_ROW ? (int64_t)blockIdx.x : (int64_t)blockIdx.x * kRouteWarps + warp;
-  if (r >= n_rows) return;
-  int s, i;
-  row_to_seq(a.seqs, r, s, i);
-  const int64_t pos = seq_pos(a.seqs, s, i);
-  const int kvl = seq_kv_len(a.seqs, s);
-  const int64_t qblk = pos >= 0 ? pos / a.block_size : -1;
-
-  // ---- scores ----
-  if (a.scores_in) {
-    if (CTA_ROW && warp != 0) return;
-    for (int b = lane; b < W; b += 32) sx[b] = a.scores_in[r * a.scores_in_stride + b];
-  } else if (CTA_ROW) {
-    for (int c = threadIdx.x; c < a.d; c += blockDim.x) sq[c] = a.idx_q[r * a.q_row_stride + c];
-    __syncthreads();
-    score_blocks(a, sq, sx, s, qblk, kvl, threadIdx.x, blockDim.x);
-    __syncthreads();
-    if (warp != 0) return;
-  } else {
-    for (int c = lane; c < a.d; c += 32) sq[c] = a.idx_q[r * a.q_row_stride + c];
-    __syncwarp();
-    score_blocks(a, sq, sx, s, qblk, kvl, lane, 32);
-  }
-  __syncwarp();
-  if (a.scores_out)
-    for (int b = lane; b < W; b += 32) a.scores_out[r * a.scores_out_stride + b] = sx[b];
-
   // ---- candidates (with per-row fallback) ----
   const uint8_t* cm = nullptr;
   if (a.cand) cm = a.cand + (a.cand_per_seq ? (int64_t)s : r) * a.cand_row_stride;
@@ -406,6 +367,162 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_rows_kernel(DashRouteA
 }
 
 // ---------------------------------------------------------------------------
+// Tiled routing for many rows: a CTA scores 32 consecutive query rows of one
+// sequence against 64-block chunks of k-bar staged in shared memory (each
+// k-bar row is read from L2 once per 32 rows), then each warp selects for 4
+// rows.  Every score is still one thread's sequential FMA chain.
+// ---------------------------------------------------------------------------
+constexpr int kTileRows = 32;
+constexpr int kChunk = 64;
+constexpr int kLd = 132;   // padded fp32 row (conflict-free 16-byte loads)
+
+__host__ __device__ inline size_t route_tile_smem_floats(int W) {
+  const int Wp = (W + 31) & ~31;
+  return (size_t)kTileRows * kLd + (size_t)kChunk * kLd + kChunk + (size_t)kTileRows * Wp +
+         8 * ((size_t)Wp / 32 + 3 * kMaxM);
+}
+
+__global__ void __launch_bounds__(256) route_tile_kernel(DashRouteArgs a, int tiles_per_seq) {
+  extern __shared__ float smt[];
+  const int W = a.width, Wp = (W + 31) & ~31;
+  float* qs = smt;                                  // [32][kLd]
+  float* kbs = qs + kTileRows * kLd;                // [64][kLd]
+  int* kbad = reinterpret_cast<int*>(kbs + kChunk * kLd);   // [64]
+  float* scs = reinterpret_cast<float*>(kbad + kChunk);     // [32][Wp]
+  float* selbase = scs + kTileRows * Wp;            // per warp: cand | ids | x | ranks
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int s = blockIdx.x / tiles_per_seq, tb = blockIdx.x - s * tiles_per_seq;
+  const int qlen = seq_q_len(a.seqs, s);
+  const int i0 = tb * kTileRows;
+  if (i0 >= qlen) return;
+  const int nr = min(kTileRows, qlen - i0);
+  const int kvl = seq_kv_len(a.seqs, s);
+  const int64_t rbase = (a.seqs.q_start ? (int64_t)a.seqs.q_start[s] : (int64_t)s * a.seqs.q_len_fixed) + i0;
+  const int64_t p0 = seq_pos(a.seqs, s, i0);
+  const int bs = a.block_size;
+  for (int e = tid; e < kTileRows * 32; e += 256) {
+    const int rr = e >> 5, c4 = e & 31;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (rr < nr) v = *reinterpret_cast<const float4*>(a.idx_q + (rbase + rr) * a.q_row_stride + 4 * c4);
+    *reinterpret_cast<float4*>(qs + rr * kLd + 4 * c4) = v;
+  }
+  for (int e = tid; e < kTileRows * Wp; e += 256) scs[e] = kScoreNeg;
+  int64_t bmax = (p0 + nr - 1) / bs - a.local_blocks;   // last block any row of the tile scores
+  bmax = min(bmax, (int64_t)W - 1);
+  bmax = min(bmax, (int64_t)(kvl - 1) / bs);
+  const int rr = tid & 31;
+  const int64_t qblk_r = (p0 + rr) / bs;
+  const float inv_sqrt_d = (float)(1.0 / sqrt((double)a.d));
+  __syncthreads();
+  for (int64_t cb0 = 0; cb0 <= bmax; cb0 += kChunk) {
+    for (int e = tid; e < kChunk * 32; e += 256) {
+      const int bb = e >> 5, c4 = e & 31;
+      const int64_t b = cb0 + bb;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      int bad = 1;
+      if (b <= bmax) {
+        const int64_t kr = a.block_table ? (int64_t)a.block_table[(int64_t)s * a.bt_stride + b]
+                                         : (int64_t)s * a.kbar_seq_rows + b;
+        if (kr < 0 || kr >= a.num_kbar_rows) {
+          if (c4 == 0) record_error(a.device_error, DASH_DEV_BAD_PAGE, 11, kr);
+        } else {
+          v = __ldg(reinterpret_cast<const float4*>(a.kbar + kr * a.kbar_row_stride) + c4);
+          bad = 0;
+        }
+      }
+      *reinterpret_cast<float4*>(kbs + bb * kLd + 4 * c4) = v;
+      if (c4 == 0) kbad[bb] = bad;
+    }
+    __syncthreads();
+    float acc[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] = 0.0f;
+    for (int c4 = 0; c4 < 32; ++c4) {
+      const float4 q4 = *reinterpret_cast<const float4*>(qs + rr * kLd + 4 * c4);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float4 k4 = *reinterpret_cast<const float4*>(kbs + (warp + 8 * k) * kLd + 4 * c4);
+        acc[k] = __fmaf_rn(q4.x, k4.x, acc[k]);
+        acc[k] = __fmaf_rn(q4.y, k4.y, acc[k]);
+        acc[k] = __fmaf_rn(q4.z, k4.z, acc[k]);
+        acc[k] = __fmaf_rn(q4.w, k4.w, acc[k]);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int bb = warp + 8 * k;
+      const int64_t b = cb0 + bb;
+      if (rr < nr && b <= bmax && !kbad[bb] && b <= qblk_r - a.local_blocks && b * bs < kvl)
+        scs[rr * Wp + b] = clamp_act(__fmul_rn(acc[k], inv_sqrt_d));
+    }
+    __syncthreads();
+  }
+  float* sel = selbase + warp * (Wp / 32 + 3 * kMaxM);
+  uint32_t* scand = reinterpret_cast<uint32_t*>(sel);
+  int* mid_ = reinterpret_cast<int*>(scand + Wp / 32);
+  float* mx = reinterpret_cast<float*>(mid_ + kMaxM);
+  int* mrank = reinterpret_cast<int*>(mx + kMaxM);
+  for (int r2 = warp; r2 < nr; r2 += 8) {
+    const int64_t r = rbase + r2;
+    float* sx = scs + r2 * Wp;
+    if (a.scores_out)
+      for (int b = lane; b < W; b += 32) a.scores_out[r * a.scores_out_stride + b] = sx[b];
+    __syncwarp();
+    select_row(a, sx, scand, mid_, mx, mrank, r, s, lane);
+    __syncwarp();
+  }
+}
+
+// CTA_ROW = false: one warp per row (many rows).  CTA_ROW = true: one CTA per
+// row, all its threads score the row's blocks, warp 0 selects (few rows,
+// e.g. decode).
+template <bool CTA_ROW>
+__global__ void __launch_bounds__(kRouteWarps * 32) route_rows_kernel(DashRouteArgs a,
+                                                                     int64_t n_rows) {
+  extern __shared__ float smr[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int W = a.width;
+  const int Wp = (W + 31) & ~31;
+  // per-warp scratch: q [d] | x [Wp] | cand bits [Wp/32] | M items (id, x) | sel flags
+  const int slot = CTA_ROW ? 0 : warp;
+  float* sq = smr + slot * (a.d + Wp + Wp / 32 + 3 * kMaxM);
+  float* sx = sq + a.d;
+  uint32_t* scand = reinterpret_cast<uint32_t*>(sx + Wp);
+  int* mid_ = reinterpret_cast<int*>(scand + Wp / 32);
+  float* mx = reinterpret_cast<float*>(mid_ + kMaxM);
+  int* mrank = reinterpret_cast<int*>(mx + kMaxM);
+
+  const int64_t r = CTA_ROW ? (int64_t)blockIdx.x : (int64_t)blockIdx.x * kRouteWarps + warp;
+  if (r >= n_rows) return;
+  int s, i;
+  row_to_seq(a.seqs, r, s, i);
+  const int64_t pos = seq_pos(a.seqs, s, i);
+  const int kvl = seq_kv_len(a.seqs, s);
+  const int64_t qblk = pos >= 0 ? pos / a.block_size : -1;
+
+  // ---- scores ----
+  if (a.scores_in) {
+    if (CTA_ROW && warp != 0) return;
+    for (int b = lane; b < W; b += 32) sx[b] = a.scores_in[r * a.scores_in_stride + b];
+  } else if (CTA_ROW) {
+    for (int c = threadIdx.x; c < a.d; c += blockDim.x) sq[c] = a.idx_q[r * a.q_row_stride + c];
+    __syncthreads();
+    score_blocks(a, sq, sx, s, qblk, kvl, threadIdx.x, blockDim.x);
+    __syncthreads();
+    if (warp != 0) return;
+  } else {
+    for (int c = lane; c < a.d; c += 32) sq[c] = a.idx_q[r * a.q_row_stride + c];
+    __syncwarp();
+    score_blocks(a, sq, sx, s, qblk, kvl, lane, 32);
+  }
+  __syncwarp();
+  if (a.scores_out)
+    for (int b = lane; b < W; b += 32) a.scores_out[r * a.scores_out_stride + b] = sx[b];
+
+  select_row(a, sx, scand, mid_, mx, mrank, r, s, lane);
+}
+
+// ---------------------------------------------------------------------------
 // Indexer stage-0: block max of token scores over remote keys.
 // One CTA per (32 query rows, key block, batch); thread (row, key lane).
 // ---------------------------------------------------------------------------
@@ -493,6 +610,15 @@ int launch_route(const DashRouteArgs& a, int64_t n_rows, cudaStream_t st) {
   if (n_rows == 0) return DASH_OK;
   int Wp = (a.width + 31) & ~31;
   size_t per_warp = sizeof(float) * ((size_t)a.d + Wp + Wp / 32 + 3 * kMaxM);
+  // many rows of few sequences: tiled kernel (k-bar chunks shared by 32 rows)
+  if (!a.scores_in && a.width <= 1024 && a.d == 128 && n_rows >= 148 * 16) {
+    const int tiles = (a.seqs.max_q_len + kTileRows - 1) / kTileRows;
+    const size_t sm = sizeof(float) * route_tile_smem_floats(a.width);
+    cudaFuncSetAttribute(route_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    route_tile_kernel<<<(unsigned)((int64_t)a.seqs.n_seq * tiles), 256, sm, st>>>(a, tiles);
+    count_launch();
+    return check_launch("route_tile_kernel");
+  }
   // few rows (decode): one CTA per row so all its threads score; else warp per row
   const bool cta_row = n_rows < 148 * 16;
   size_t smem = per_warp * (cta_row ? 1 : kRouteWarps);
