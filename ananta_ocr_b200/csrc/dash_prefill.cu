@@ -458,15 +458,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const float b2 = sel ? cur_bias * LOG2E : 0.0f;
       if (!mbar_wait_warp(s_full + sb, (it >> 1) & 1, abort_flag, derr, 61)) { alive = false; break; }
       tc_fence_after();
-      float x[64];                               // S, then logit - m_run in place
-      tmem_ld32f(tS + sb * BN + lane_base, x);
-      tmem_ld32f(tS + sb * BN + 32 + lane_base, x + 32);
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(s_free + sb);
-      // x = logit - m_run in the exp2 domain: one FFMA per element, the mask
-      // as selects; column c is kept iff lo <= c <= hi where lo is the first
-      // local column, or the first attendable column when the block is routed
+      // Column c of this key tile is kept iff lo <= c <= hi, where lo is the
+      // first local column, or the first attendable column when the block is
+      // routed; logits are x = s*scale*log2e + (local ? 0 : bias) - m_run.
       const int hi = (int)max((int64_t)-1, min((int64_t)63, pos - kt0));
       const int lo_seg = (int)max((int64_t)0, min((int64_t)64, segs - kt0));
       const int lo_loc = (int)max((int64_t)0, min((int64_t)64, lstart - kt0));
@@ -476,34 +470,43 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       // P buffer sb was last read by PV(it-2) (long done by now in practice)
       if (it >= 2 && !mbar_wait_warp(pv_done + sb, ((it - 2) >> 1) & 1, abort_flag, derr, 63)) { alive = false; break; }
       uint8_t* dP = sm + OFF_P + (2 * g + sb) * 16384 + m * 128;
+      const uint32_t tSb = tS + sb * BN + lane_base;
       // Pure tile for this row: all 64 columns kept with one additive term, or
       // none kept.  When every row of the warp is pure and the tile lies inside
       // the sequence (tiles away from the window edge and the diagonal), the
       // logits take one packed FFMA per 2 columns (an empty row adds -inf), P is
       // produced directly, and the rescale test runs on the packed P maximum.
+      // S is read from TMEM in two 32-column halves to keep registers low.
       const bool empty = lo > hi;
       const bool full = lo == 0 && hi == 63 && (lo_loc == 0 || lo_loc == 64);
       bool done = false;
-      float mx = -INFINITY;
       if (__all_sync(0xffffffffu, empty || full) && kt0 + BN <= kvl) {
         const float add = empty ? -INFINITY : (lo_loc == 0 ? add_loc : add_rem);
         const uint64_t sl2v = f2_pack(sl2, sl2), addv = f2_pack(add, add);
         uint64_t lsv = f2_pack(0.0f, 0.0f);
         uint32_t pmax = 0;                         // packed +0.0 pair
 #pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          uint32_t pk[4];
+        for (int h = 0; h < 2; ++h) {
+          float x[32];
+          tmem_ld32f(tSb + 32 * h, x);
+          tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int c = 8 * c8 + 2 * e;
-            f2_unpack(ffma2(f2_pack(x[c], x[c + 1]), sl2v, addv), x[c], x[c + 1]);
-            const float p0 = fast_exp2(x[c]);
-            const float p1 = fast_exp2(x[c + 1]);
-            lsv = fadd2(lsv, f2_pack(p0, p1));
-            pk[e] = pack2(p0, p1, (T*)nullptr);
-            pmax = hmax2u(pmax, pk[e], (T*)nullptr);
+          for (int c8 = 0; c8 < 4; ++c8) {
+            uint32_t pk[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int c = 8 * c8 + 2 * e;
+              float y0, y1;
+              f2_unpack(ffma2(f2_pack(x[c], x[c + 1]), sl2v, addv), y0, y1);
+              const float p0 = fast_exp2(y0);
+              const float p1 = fast_exp2(y1);
+              lsv = fadd2(lsv, f2_pack(p0, p1));
+              pk[e] = pack2(p0, p1, (T*)nullptr);
+              pmax = hmax2u(pmax, pk[e], (T*)nullptr);
+            }
+            const int cc = 4 * h + c8;
+            *reinterpret_cast<uint4*>(dP + ((cc ^ (m & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           }
-          *reinterpret_cast<uint4*>(dP + ((c8 ^ (m & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
         const float2 pm = unpack2(pmax, (T*)nullptr);
         const bool big = !(fmaxf(pm.x, pm.y) <= 256.0f);   // p > 2^8 (or inf/NaN)
@@ -512,22 +515,25 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           f2_unpack(lsv, l0, l1);
           l_run += l0 + l1;
           done = true;
-        } else {
-#pragma unroll
-          for (int c = 0; c < 64; ++c) mx = fmaxf(mx, x[c]);
         }
-      } else {
-        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const float v = fmaf(x[c], sl2, c >= lo_loc ? add_loc : add_rem);
-          x[c] = (c >= lo && c <= hi) ? v : -INFINITY;
-          mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
-        }
-        mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       }
       if (!done) {
+        // general path: pass 1 row max, optional rescale, pass 2 P
+        float mx = -INFINITY;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float x[32];
+          tmem_ld32f(tSb + 32 * h, x);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int c = 32 * h + j;
+            const float v = fmaf(x[j], sl2, c >= lo_loc ? add_loc : add_rem);
+            mx = fmaxf(mx, (c >= lo && c <= hi) ? v : -INFINITY);
+          }
+        }
         const bool need = mx > 8.0f;             // row max grew by more than 2^8
+        float shift = 0.0f;
         if (__any_sync(0xffffffffu, need)) {
           const float f = need ? fast_exp2(-mx) : 1.0f;
           if (it > 0) {
@@ -547,25 +553,38 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           l_run *= f;
           if (need) {
             m_run += mx;
-#pragma unroll
-            for (int c = 0; c < 64; ++c) x[c] -= mx;
+            shift = mx;
           }
         }
         float ls4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          uint32_t pk[4];
+        for (int h = 0; h < 2; ++h) {
+          float x[32];
+          tmem_ld32f(tSb + 32 * h, x);
+          tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float p0 = fast_exp2(x[8 * c8 + 2 * e]);
-            const float p1 = fast_exp2(x[8 * c8 + 2 * e + 1]);
-            ls4[e] += p0 + p1;
-            pk[e] = pack2(p0, p1, (T*)nullptr);
+          for (int c8 = 0; c8 < 4; ++c8) {
+            uint32_t pk[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float pp[2];
+#pragma unroll
+              for (int u = 0; u < 2; ++u) {
+                const int j = 8 * c8 + 2 * e + u, c = 32 * h + j;
+                const float v = fmaf(x[j], sl2, (c >= lo_loc ? add_loc : add_rem) - shift);
+                pp[u] = fast_exp2((c >= lo && c <= hi) ? v : -INFINITY);
+              }
+              ls4[e] += pp[0] + pp[1];
+              pk[e] = pack2(pp[0], pp[1], (T*)nullptr);
+            }
+            const int cc = 4 * h + c8;
+            *reinterpret_cast<uint4*>(dP + ((cc ^ (m & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           }
-          *reinterpret_cast<uint4*>(dP + ((c8 ^ (m & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
         l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
       }
+      tc_fence_before();
+      mbar_arrive(s_free + sb);                  // S buffer sb fully read
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full + sb);
