@@ -39,7 +39,7 @@ constexpr int MAX_MASK_WORDS = 256;               // <= 8192 blocks
 constexpr int OFF_BAR = OFF_MASK + MAX_MASK_WORDS * 4;
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;  // + alignment slack
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
-constexpr int NTHREADS = 320;                     // 8 softmax warps, TMA warp, MMA warp
+constexpr int NTHREADS = 352;                     // 8 softmax warps, TMA warp, 2 MMA warps
 constexpr uint32_t TMEM_COLS = 512;               // per tile: S0 | S1 | O
 constexpr int kPlanMaxK = 256;                    // routed slots per row
 
@@ -187,9 +187,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint64_t* kv_empty = bars + 3;     // [NSTAGE]
   // per softmax group g (9 barriers each from bars + 6 + 9g):
   //   s_full[2], s_free[2], p_full[2], pv_done[2], q_full
-  uint64_t* mma_done = bars + 24;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 25);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 26);
+  uint64_t* mma_done = bars + 24;    // [2], one per MMA warp
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 26);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 27);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_seq = a.seqs.n_seq;
@@ -216,7 +216,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   // ---- setup: barriers, TMEM, block mask ----
   if (tid == 0) {
-    for (int k = 0; k < NSTAGE; ++k) { mbar_init(kv_full + k, 1); mbar_init(kv_empty + k, 1); }
+    // a K/V stage is free once every group's PV of it completed
+    for (int k = 0; k < NSTAGE; ++k) { mbar_init(kv_full + k, 1); mbar_init(kv_empty + k, ngroups); }
     for (int g = 0; g < 2; ++g) {
       uint64_t* gb = bars + 6 + 9 * g;
       for (int k = 0; k < 2; ++k) {
@@ -228,6 +229,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_init(gb + 8, 128);          // q_full
     }
     mbar_init(mma_done, 1);
+    mbar_init(mma_done + 1, 1);
     *abort_flag = 0;
     mbar_init_fence();
   }
@@ -299,34 +301,33 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         mbar_wait(kv_full + (k % NSTAGE), (k / NSTAGE) & 1, &no_abort, nullptr, 42);
       }
     }
-  } else if (warp == 9) {
-    // =================== MMA issuer ===================
-    if (lane == 0) {
+  } else if (warp == 9 || warp == 10) {
+    // ============ MMA issuers: warp 9 for group 0, warp 10 for group 1 ============
+    // Each group has its own issuer so neither waits on the other's softmax.
+    const int g = warp - 9;
+    if (lane == 0 && g < ngroups) {
       constexpr uint32_t fmt = DType<T>::fmt;
       constexpr uint32_t idesc_qk = make_idesc(fmt, 0, 0, BM, BN);
       constexpr uint32_t idesc_pv = make_idesc(fmt, 0, 1, BM, HD);
-      bool alive = true;
-      for (int g = 0; g < ngroups && alive; ++g)
-        alive = mbar_wait(bars + 6 + 9 * g + 8, 0, abort_flag, derr, 50);
+      uint64_t* gb = bars + 6 + 9 * g;
+      const uint32_t sQ = smem_u32(sm + OFF_Q + g * 32768);
+      const uint32_t tSg = tmem + g * 256, tO = tmem + g * 256 + 128;
+      bool alive = mbar_wait(gb + 8, 0, abort_flag, derr, 50);
       TileIter itr{-1, -1, 0, 0u};
       int it = 0;
       auto issue_pv = [&](int j) -> bool {
         const int pb = j & 1;
+        if (!mbar_wait(gb + 4 + pb, (j >> 1) & 1, abort_flag, derr, 51)) return false;
+        tc_fence_after();
         const uint32_t sV = smem_u32(sm + OFF_V + (j % NSTAGE) * 16384);
-        for (int g = 0; g < ngroups; ++g) {
-          uint64_t* gb = bars + 6 + 9 * g;
-          if (!mbar_wait(gb + 4 + pb, (j >> 1) & 1, abort_flag, derr, 51)) return false;
-          tc_fence_after();
-          const uint32_t sP = smem_u32(sm + OFF_P + (2 * g + pb) * 16384);
-          const uint32_t tO = tmem + g * 256 + 128;
+        const uint32_t sP = smem_u32(sm + OFF_P + (2 * g + pb) * 16384);
 #pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk) {
-            uint64_t ad = sw128_desc(sP + kk * 32, 16, 1024);
-            uint64_t bd = sw128_desc(sV + kk * 2048, 8192, 1024);
-            umma_ss(tO, ad, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(gb + 6 + pb);
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          uint64_t ad = sw128_desc(sP + kk * 32, 16, 1024);
+          uint64_t bd = sw128_desc(sV + kk * 2048, 8192, 1024);
+          umma_ss(tO, ad, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         }
+        umma_commit(gb + 6 + pb);
         umma_commit(kv_empty + (j % NSTAGE));
         return true;
       };
@@ -335,30 +336,24 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (kt0 < 0) break;
         const int st = it % NSTAGE, sb = it & 1;
         if (!mbar_wait(kv_full + st, (it / NSTAGE) & 1, abort_flag, derr, 52)) { alive = false; break; }
+        if (it >= 2 && !mbar_wait(gb + 2 + sb, ((it >> 1) - 1) & 1, abort_flag, derr, 53)) { alive = false; break; }
+        tc_fence_after();
         const uint32_t sK = smem_u32(sm + OFF_K + st * 16384);
-        for (int g = 0; g < ngroups && alive; ++g) {
-          uint64_t* gb = bars + 6 + 9 * g;
-          if (it >= 2 && !mbar_wait(gb + 2 + sb, ((it >> 1) - 1) & 1, abort_flag, derr, 53)) { alive = false; break; }
-          tc_fence_after();
-          const uint32_t sQ = smem_u32(sm + OFF_Q + g * 32768);
-          const uint32_t tS = tmem + g * 256 + sb * BN;
 #pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk) {
-            uint64_t ad = sw128_desc(sQ + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-            uint64_t bd = sw128_desc(sK + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
-            umma_ss(tS, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
-          }
-          umma_commit(gb + 0 + sb);
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          uint64_t ad = sw128_desc(sQ + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+          uint64_t bd = sw128_desc(sK + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
+          umma_ss(tSg + sb * BN, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
         }
-        if (!alive) break;
+        umma_commit(gb + 0 + sb);
         if (it >= 1 && !issue_pv(it - 1)) { alive = false; break; }
         ++it;
       }
       if (alive && it >= 1) issue_pv(it - 1);
-      // all MMAs of this CTA complete before TMEM is released
-      umma_commit(mma_done);
+      // all MMAs of this group complete before TMEM is released
+      umma_commit(mma_done + g);
       volatile int no_abort = 0;
-      mbar_wait(mma_done, 0, &no_abort, nullptr, 54);
+      mbar_wait(mma_done + g, 0, &no_abort, nullptr, 54);
     }
     __syncwarp();
   } else if (warp / 4 < ngroups) {
