@@ -47,6 +47,7 @@ struct PrefillPlan {
   const int32_t* cidx;     // canonical lists [nih][n_rows][K]
   const float* cbias;
   const uint32_t* tmask;   // per-tile unions [nih][n_tiles][nwords]
+  const float* rowmax;     // largest kept bias per row [nih][n_rows] (-inf: none)
   int64_t n_rows;
   int32_t nwords;
   int32_t tiles_per_seq;
@@ -90,7 +91,7 @@ __device__ __forceinline__ int64_t row_base(const DashSeqs& q, int s) {
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(128) plan_kernel(DashPrefillArgs a, PrefillPlan p,
                                                    int32_t* cidx, float* cbias,
-                                                   uint32_t* tmask) {
+                                                   uint32_t* tmask, float* rowmax) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r = (int64_t)blockIdx.x * 4 + warp;
   const int ih = blockIdx.y;
@@ -129,6 +130,7 @@ __global__ void __launch_bounds__(128) plan_kernel(DashPrefillArgs a, PrefillPla
   __syncwarp();
   // pass 2: rank the kept ids (distinct) and write the ascending list
   int nk = 0;
+  float bmax = -INFINITY;
   for (int j0 = 0; j0 < K; j0 += 32) {
     const int j = j0 + lane;
     const int b = j < K ? sid[j] : -1;
@@ -142,8 +144,11 @@ __global__ void __launch_bounds__(128) plan_kernel(DashPrefillArgs a, PrefillPla
       atomicOr(tm + (b >> 5), 1u << (b & 31));
     }
     nk += __popc(__ballot_sync(0xffffffffu, ok));
+    bmax = fmaxf(bmax, (ok && bl) ? bl[j] : -INFINITY);
   }
   for (int j = nk + lane; j < K; j += 32) { oi[j] = -1; ob[j] = 0.0f; }
+  for (int o = 16; o > 0; o >>= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
+  if (lane == 0) rowmax[(int64_t)ih * p.n_rows + r] = bmax;
 }
 
 // ---------------------------------------------------------------------------
@@ -414,12 +419,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // true max only scales p by a power of two (no underflow for logits within
     // ~100 of it).
     float m_run = 0.0f, l_run = 0.0f;
-    if (row_ok && has_bias) {
-      for (int j = 0; j < K; ++j) {
-        if (rl[j] < 0) break;
-        m_run = fmaxf(m_run, rbl[j] * LOG2E);
-      }
-    }
+    if (row_ok && has_bias && K > 0)
+      m_run = fmaxf(0.0f, p.rowmax[(int64_t)ih * p.n_rows + rglob] * LOG2E);
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     TileIter itr{-1, -1, 0, 0u};
     int it = 0;
@@ -686,7 +687,7 @@ size_t prefill_workspace(const DashPrefillArgs& a, int64_t n_rows) {
   size_t lists = (size_t)nih * n_rows * a.routes.K * 4;
   lists = (lists + 255) & ~(size_t)255;
   size_t masks = (size_t)nih * a.seqs.n_seq * p.tiles_per_seq * p.nwords * 4;
-  return 2 * lists + ((masks + 255) & ~(size_t)255);
+  return 2 * lists + ((masks + 255) & ~(size_t)255) + (size_t)nih * n_rows * 4;
 }
 
 int launch_prefill(const DashPrefillArgs& a, int64_t n_rows, cudaStream_t st) {
@@ -709,9 +710,11 @@ int launch_prefill(const DashPrefillArgs& a, int64_t n_rows, cudaStream_t st) {
   p.cidx = cidx;
   p.cbias = cbias;
   p.tmask = tmask;
+  float* rowmax = reinterpret_cast<float*>(ws + 2 * lists + ((masks + 255) & ~(size_t)255));
+  p.rowmax = rowmax;
   if (a.routes.K > 0) {
     dim3 g1((unsigned)((n_rows + 3) / 4), nih);
-    plan_kernel<<<g1, 128, 0, st>>>(a, p, cidx, cbias, tmask);
+    plan_kernel<<<g1, 128, 0, st>>>(a, p, cidx, cbias, tmask, rowmax);
     count_launch();
     int rc = check_launch("plan_kernel");
     if (rc) return rc;
