@@ -6,14 +6,21 @@
 // order, every 64-key tile of the blocks that any of its rows routed to (the
 // per-tile union built by plan_kernel) plus the blocks of its local windows.
 // Per key tile:
-//   TMA (warp 4)      K and V tiles -> shared memory (128-byte swizzle), 3 stages
-//   MMA (warp 5)      S = Q K^T   (tcgen05.mma M=128 N=64,  fp32 in TMEM, 2 buffers)
-//                     O += P V    (tcgen05.mma M=128 N=128, fp32 in TMEM)
-//   softmax (w0-3)    one thread per row: S from TMEM, per-row mask + bias
-//                     (local window: no bias; routed block: + bias; else -inf),
-//                     online softmax in the exp2 domain with lazy rescaling of
-//                     O (only when the row max grows by > 2^8), P -> shared
-//                     memory (bf16/fp16, swizzled) for the PV MMA.
+//   TMA (warp 8)      K and V tiles -> shared memory (128-byte swizzle), 4 stages
+//   MMA (warps 9,10)  one issuer per query tile:
+//                     S = Q K^T   (tcgen05.mma M=128 N=64, Q and K from shared
+//                                  memory, fp32 in TMEM, 2 buffers)
+//                     O += P V    (tcgen05.mma M=128 N=128, P from TMEM, V from
+//                                  shared memory, fp32 in TMEM)
+//   softmax (w0-7)    one thread per row of one of the two query tiles: S from
+//                     TMEM, per-row mask + bias (local window: no bias; routed
+//                     block: + bias; else -inf), online softmax in the exp2
+//                     domain with lazy rescaling of O, P (bf16/fp16) written
+//                     back over the S buffer it came from.
+// Keeping P in TMEM removes the P round trip through shared memory, which
+// (with the Q operand re-read by every QK MMA) bounds this kernel.  The
+// softmax warpgroups take 208 registers each and the TMA/MMA warpgroup 88
+// (setmaxnreg), so a thread holds its whole 64-column S row.
 // Rows that did not route a block of the union simply get P = 0 there.
 //
 // Semantics: sparse_gather_e2e_triton.py:34-115 (_e2e_attn_fwd_kernel),
@@ -28,19 +35,32 @@ namespace dash {
 constexpr int BM = 128;          // tile rows (M of both MMAs)
 constexpr int BN = 64;           // keys per key tile (N of QK, K of PV)
 constexpr int HD = 128;          // head dim
-constexpr int NSTAGE = 3;
+constexpr int NSTAGE = 4;
 // two query tiles (A, B) per CTA share the K/V stream
 constexpr int OFF_Q = 0;                          // 2 tiles x 2 x [128 x 128 B]
 constexpr int OFF_K = 65536;                      // NSTAGE x 2 x [64 x 128 B]
 constexpr int OFF_V = OFF_K + NSTAGE * 16384;     // NSTAGE x 2 x [64 x 128 B]
-constexpr int OFF_P = OFF_V + NSTAGE * 16384;     // 2 tiles x 2 buffers x [128 x 128 B]
-constexpr int OFF_MASK = OFF_P + 4 * 16384;       // block mask words
+constexpr int OFF_MASK = OFF_V + NSTAGE * 16384;  // block mask words
 constexpr int MAX_MASK_WORDS = 256;               // <= 8192 blocks
 constexpr int OFF_BAR = OFF_MASK + MAX_MASK_WORDS * 4;
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;  // + alignment slack
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
-constexpr int NTHREADS = 352;                     // 8 softmax warps, TMA warp, 2 MMA warps
-constexpr uint32_t TMEM_COLS = 512;               // per tile: S0 | S1 | O
+// warps 0-7 softmax (two groups), 8 TMA, 9-10 MMA issuers, 11 idle
+constexpr int NTHREADS = 384;
+// Register split: launched at kLaunchRegs per thread (3 warps per SM
+// sub-partition), then 2 x 128 softmax threads grow to kSoftmaxRegs while the
+// 128 TMA/MMA threads shrink to kOtherRegs.  The host refuses to launch a
+// build whose register count does not cover the split (the growth would wait).
+constexpr int kLaunchRegs = 168;
+constexpr int kSoftmaxRegs = 208;
+constexpr int kOtherRegs = 88;
+static_assert(2 * 128 * kSoftmaxRegs + 128 * kOtherRegs <= NTHREADS * kLaunchRegs, "register split");
+static_assert(2 * kSoftmaxRegs + kOtherRegs <= 3 * kLaunchRegs, "register split per sub-partition");
+constexpr uint32_t TMEM_COLS = 512;               // per query tile: S0 | S1 | O
+// O is rescaled only when a row's logit exceeds its running max by more than
+// 2^kGrowLog2 (then p < 2^32: no bf16/fp32 overflow for any sequence length)
+constexpr float kGrowLog2 = 32.0f;
+constexpr float kGrowP = 4294967296.0f;
 constexpr int kPlanMaxK = 256;                    // routed slots per row
 
 struct PrefillPlan {
@@ -188,13 +208,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint32_t* smask = reinterpret_cast<uint32_t*>(sm + OFF_MASK);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
-  uint64_t* kv_full = bars + 0;      // [NSTAGE]
-  uint64_t* kv_empty = bars + 3;     // [NSTAGE]
-  // per softmax group g (9 barriers each from bars + 6 + 9g):
-  //   s_full[2], s_free[2], p_full[2], pv_done[2], q_full
-  uint64_t* mma_done = bars + 24;    // [2], one per MMA warp
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 26);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 27);
+  uint64_t* kv_full = bars + 0;            // [NSTAGE]
+  uint64_t* kv_empty = bars + NSTAGE;      // [NSTAGE]
+  // per softmax group g (7 barriers each from bars + 2*NSTAGE + 7g):
+  //   s_full[2], p_full[2], pv_done[2], q_full
+  uint64_t* mma_done = bars + 2 * NSTAGE + 14;   // [2], one per MMA warp
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * NSTAGE + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * NSTAGE + 17);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_seq = a.seqs.n_seq;
@@ -224,14 +244,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // a K/V stage is free once every group's PV of it completed
     for (int k = 0; k < NSTAGE; ++k) { mbar_init(kv_full + k, 1); mbar_init(kv_empty + k, ngroups); }
     for (int g = 0; g < 2; ++g) {
-      uint64_t* gb = bars + 6 + 9 * g;
+      uint64_t* gb = bars + 2 * NSTAGE + 7 * g;
       for (int k = 0; k < 2; ++k) {
-        mbar_init(gb + 0 + k, 1);      // s_full
-        mbar_init(gb + 2 + k, 128);    // s_free
-        mbar_init(gb + 4 + k, 128);    // p_full
-        mbar_init(gb + 6 + k, 1);      // pv_done
+        mbar_init(gb + 0 + k, 1);      // s_full   (MMA commit)
+        mbar_init(gb + 2 + k, 4);      // p_full   (one arrive per softmax warp)
+        mbar_init(gb + 4 + k, 1);      // pv_done  (MMA commit)
       }
-      mbar_init(gb + 8, 128);          // q_full
+      mbar_init(gb + 6, 4);            // q_full
     }
     mbar_init(mma_done, 1);
     mbar_init(mma_done + 1, 1);
@@ -260,364 +279,363 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
   DeviceError* derr = a.device_error;
+  // register split (inside each role's branch so that the compiler budgets
+  // each role's code with its own count): softmax warpgroups grow, the
+  // TMA/MMA warpgroup shrinks
 
-  if (warp == 8) {
-    // =================== TMA producer ===================
-    if (lane == 0) {
-      prefetch_tmap(&tmK);
-      prefetch_tmap(&tmV);
-      TileIter itr{-1, -1, 0, 0u};
-      int it = 0;
-      while (true) {
-        int kt0 = next_tile(itr, smask, p.nwords, bs, pmax, kvl);
-        if (kt0 < 0) break;
-        const int st = it % NSTAGE;
-        if (it >= NSTAGE && !mbar_wait(kv_empty + st, ((it / NSTAGE) - 1) & 1, abort_flag, derr, 40)) break;
-        uint8_t* dK = sm + OFF_K + st * 16384;
-        uint8_t* dV = sm + OFF_V + st * 16384;
-        int c1, c3;
-        bool ok = true;
-        if (PAGED) {
-          int64_t page = a.kv.block_table[(int64_t)s * a.kv.bt_stride + kt0 / bs];
-          if (page < 0 || page >= a.kv.num_pages) {
-            record_error(derr, DASH_DEV_BAD_PAGE, 41, page);
-            ok = false;
+  if (warp >= 8) {
+    regs_shrink<kOtherRegs>();
+    if (warp == 8) {
+      // =================== TMA producer ===================
+      if (lane == 0) {
+        prefetch_tmap(&tmK);
+        prefetch_tmap(&tmV);
+        TileIter itr{-1, -1, 0, 0u};
+        int it = 0;
+        while (true) {
+          int kt0 = next_tile(itr, smask, p.nwords, bs, pmax, kvl);
+          if (kt0 < 0) break;
+          const int st = it % NSTAGE;
+          if (it >= NSTAGE && !mbar_wait(kv_empty + st, ((it / NSTAGE) - 1) & 1, abort_flag, derr, 40)) break;
+          uint8_t* dK = sm + OFF_K + st * 16384;
+          uint8_t* dV = sm + OFF_V + st * 16384;
+          int c1, c3;
+          bool ok = true;
+          if (PAGED) {
+            int64_t page = a.kv.block_table[(int64_t)s * a.kv.bt_stride + kt0 / bs];
+            if (page < 0 || page >= a.kv.num_pages) {
+              record_error(derr, DASH_DEV_BAD_PAGE, 41, page);
+              ok = false;
+            }
+            c1 = kt0 % bs;
+            c3 = (int)page;
+          } else {
+            c1 = kt0;
+            c3 = s;
           }
-          c1 = kt0 % bs;
-          c3 = (int)page;
-        } else {
-          c1 = kt0;
-          c3 = s;
+          if (ok) {
+            mbar_arrive_expect_tx(kv_full + st, 4 * 8192);
+            tma_load_4d(dK, &tmK, kv_full + st, 0, c1, hk, c3);
+            tma_load_4d(dK + 8192, &tmK, kv_full + st, 64, c1, hk, c3);
+            tma_load_4d(dV, &tmV, kv_full + st, 0, c1, hk, c3);
+            tma_load_4d(dV + 8192, &tmV, kv_full + st, 64, c1, hk, c3);
+          } else {
+            mbar_arrive(kv_full + st);
+          }
+          ++it;
         }
-        if (ok) {
-          mbar_arrive_expect_tx(kv_full + st, 4 * 8192);
-          tma_load_4d(dK, &tmK, kv_full + st, 0, c1, hk, c3);
-          tma_load_4d(dK + 8192, &tmK, kv_full + st, 64, c1, hk, c3);
-          tma_load_4d(dV, &tmV, kv_full + st, 0, c1, hk, c3);
-          tma_load_4d(dV + 8192, &tmV, kv_full + st, 64, c1, hk, c3);
-        } else {
-          mbar_arrive(kv_full + st);
+        // drain: never leave the CTA with bulk copies in flight
+        for (int k = max(0, it - NSTAGE); k < it; ++k) {
+          volatile int no_abort = 0;
+          mbar_wait(kv_full + (k % NSTAGE), (k / NSTAGE) & 1, &no_abort, nullptr, 42);
         }
-        ++it;
       }
-      // drain: never leave the CTA with bulk copies in flight
-      for (int k = max(0, it - NSTAGE); k < it; ++k) {
+    } else if (warp == 9 || warp == 10) {
+      // ============ MMA issuers: warp 9 for group 0, warp 10 for group 1 ============
+      // Each group has its own issuer so neither waits on the other's softmax.
+      const int g = warp - 9;
+      if (lane == 0 && g < ngroups) {
+        constexpr uint32_t fmt = DType<T>::fmt;
+        constexpr uint32_t idesc_qk = make_idesc(fmt, 0, 0, BM, BN);
+        constexpr uint32_t idesc_pv = make_idesc(fmt, 0, 1, BM, HD);
+        uint64_t* gb = bars + 2 * NSTAGE + 7 * g;
+        const uint32_t sQ = smem_u32(sm + OFF_Q + g * 32768);
+        const uint32_t tSg = tmem + g * 256, tO = tmem + g * 256 + 128;
+        bool alive = mbar_wait(gb + 6, 0, abort_flag, derr, 50);
+        TileIter itr{-1, -1, 0, 0u};
+        int it = 0;
+        // O += P V with P (bf16, K-major) read from the first 32 columns of S buffer j&1
+        auto issue_pv = [&](int j) -> bool {
+          const int pb = j & 1;
+          if (!mbar_wait(gb + 2 + pb, (j >> 1) & 1, abort_flag, derr, 51)) return false;
+          tc_fence_after();
+          const uint32_t sV = smem_u32(sm + OFF_V + (j % NSTAGE) * 16384);
+          const uint32_t tP = tSg + pb * BN;
+  #pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            uint64_t bd = sw128_desc(sV + kk * 2048, 8192, 1024);
+            umma_ts(tO, tP + kk * 8, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(gb + 4 + pb);
+          umma_commit(kv_empty + (j % NSTAGE));
+          return true;
+        };
+        while (alive) {
+          int kt0 = next_tile(itr, smask, p.nwords, bs, pmax, kvl);
+          if (kt0 < 0) break;
+          const int st = it % NSTAGE, sb = it & 1;
+          if (!mbar_wait(kv_full + st, (it / NSTAGE) & 1, abort_flag, derr, 52)) { alive = false; break; }
+          // S buffer sb holds P(it-2) until PV(it-2) has completed
+          if (it >= 2 && !mbar_wait(gb + 4 + sb, ((it - 2) >> 1) & 1, abort_flag, derr, 53)) { alive = false; break; }
+          tc_fence_after();
+          const uint32_t sK = smem_u32(sm + OFF_K + st * 16384);
+  #pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            uint64_t ad = sw128_desc(sQ + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+            uint64_t bd = sw128_desc(sK + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
+            umma_ss(tSg + sb * BN, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(gb + 0 + sb);
+          if (it >= 1 && !issue_pv(it - 1)) { alive = false; break; }
+          ++it;
+        }
+        if (alive && it >= 1) issue_pv(it - 1);
+        // all MMAs of this group complete before TMEM is released
+        umma_commit(mma_done + g);
         volatile int no_abort = 0;
-        mbar_wait(kv_full + (k % NSTAGE), (k / NSTAGE) & 1, &no_abort, nullptr, 42);
+        mbar_wait(mma_done + g, 0, &no_abort, nullptr, 54);
       }
+      __syncwarp();
     }
-  } else if (warp == 9 || warp == 10) {
-    // ============ MMA issuers: warp 9 for group 0, warp 10 for group 1 ============
-    // Each group has its own issuer so neither waits on the other's softmax.
-    const int g = warp - 9;
-    if (lane == 0 && g < ngroups) {
-      constexpr uint32_t fmt = DType<T>::fmt;
-      constexpr uint32_t idesc_qk = make_idesc(fmt, 0, 0, BM, BN);
-      constexpr uint32_t idesc_pv = make_idesc(fmt, 0, 1, BM, HD);
-      uint64_t* gb = bars + 6 + 9 * g;
-      const uint32_t sQ = smem_u32(sm + OFF_Q + g * 32768);
-      const uint32_t tSg = tmem + g * 256, tO = tmem + g * 256 + 128;
-      bool alive = mbar_wait(gb + 8, 0, abort_flag, derr, 50);
+  } else {
+    regs_grow<kSoftmaxRegs>();
+    if ((warp >> 2) < ngroups) {
+      // ============ softmax / epilogue: group g, one thread per tile row ============
+      const int g = warp >> 2;
+      uint64_t* gb = bars + 2 * NSTAGE + 7 * g;
+      uint64_t* s_full = gb + 0;
+      uint64_t* p_full = gb + 2;
+      uint64_t* pv_done = gb + 4;
+      uint64_t* q_full = gb + 6;
+      const uint32_t tS = tmem + g * 256, tO = tmem + g * 256 + 128;
+      const int m = tid & 127;                 // row 0..127 of this group's tile
+      const int i0 = i0A + g * p.TT;
+      const int ntok = min(p.TT, qlen - i0);
+      const int tok = i0 + m / G;
+      const int hq = hk * G + (m % G);
+      const bool row_ok = (m / G) < ntok;
+      const int64_t pos = row_ok ? (int64_t)pos0 + tok : -1;
+      const int64_t lstart = pos - a.local_window + 1;
+      const int64_t rglob = row_base(a.seqs, s) + tok;
+      const int64_t segs = (row_ok && a.seg_start) ? (int64_t)a.seg_start[rglob] : 0;
+      // ---- Q row -> shared (swizzled K-major) ----
+      {
+        const T* qp = reinterpret_cast<const T*>(a.qo.q) +
+                      (a.seqs.q_start ? rglob * a.qo.q_stride_tok
+                                      : (int64_t)s * a.qo.q_stride_seq + (int64_t)tok * a.qo.q_stride_tok) +
+                      (int64_t)hq * a.qo.q_stride_head;
+        uint8_t* sq = sm + OFF_Q + g * 32768;
+  #pragma unroll
+        for (int cc = 0; cc < 16; ++cc) {
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (row_ok) v = *reinterpret_cast<const uint4*>(qp + cc * 8);
+          const int region = cc >> 3, c8 = cc & 7;
+          *reinterpret_cast<uint4*>(sq + region * 16384 + m * 128 + ((c8 ^ (m & 7)) << 4)) = v;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(q_full);
+      }
+      // routed list cursor
+      const int K = a.routes.K;
+      const int32_t* rl = p.cidx + ((int64_t)ih * p.n_rows + rglob) * K;
+      const float* rbl = p.cbias + ((int64_t)ih * p.n_rows + rglob) * K;
+      const bool has_bias = a.routes.bias != nullptr;
+      // cursor = entry cur_j; the raw entry after it is kept prefetched in
+      // registers.  The prefetch is unconditional (index clamped to the list) and
+      // its value is first used at the next advance, at least one key tile
+      // later, so no instruction of the tile loop waits on it.
+      int cur_j = 0;
+      int cur_b = (row_ok && K > 0) ? rl[0] : -1;
+      float cur_bias = (row_ok && K > 0 && has_bias) ? rbl[0] : 0.0f;
+      int nxt_raw = (row_ok && K > 1) ? rl[1] : -1;
+      float nxt_bias_raw = (row_ok && K > 1) ? rbl[1] : 0.0f;
+      const float sl2 = a.scale * 1.4426950408889634f;
+      const float LOG2E = 1.4426950408889634f;
+      // Running max (exp2 domain) starts at the row's largest routed bias: the
+      // bias of the top entmax block is what makes a row's max jump.  Any start
+      // value is exact (O and l share the reference).  O is rescaled only when a
+      // logit exceeds the running max by more than kGrowLog2: p stays below
+      // 2^kGrowLog2, far inside the bf16/fp32 range, and a start above the true
+      // max only scales p by a power of two.
+      float m_run = 0.0f, l_run = 0.0f;
+      if (row_ok && has_bias && K > 0)
+        m_run = fmaxf(0.0f, p.rowmax[(int64_t)ih * p.n_rows + rglob] * LOG2E);
+      const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
       TileIter itr{-1, -1, 0, 0u};
       int it = 0;
-      auto issue_pv = [&](int j) -> bool {
-        const int pb = j & 1;
-        if (!mbar_wait(gb + 4 + pb, (j >> 1) & 1, abort_flag, derr, 51)) return false;
-        tc_fence_after();
-        const uint32_t sV = smem_u32(sm + OFF_V + (j % NSTAGE) * 16384);
-        const uint32_t sP = smem_u32(sm + OFF_P + (2 * g + pb) * 16384);
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          uint64_t ad = sw128_desc(sP + kk * 32, 16, 1024);
-          uint64_t bd = sw128_desc(sV + kk * 2048, 8192, 1024);
-          umma_ss(tO, ad, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(gb + 6 + pb);
-        umma_commit(kv_empty + (j % NSTAGE));
-        return true;
-      };
+      bool alive = true;
       while (alive) {
         int kt0 = next_tile(itr, smask, p.nwords, bs, pmax, kvl);
         if (kt0 < 0) break;
         const int st = it % NSTAGE, sb = it & 1;
-        if (!mbar_wait(kv_full + st, (it / NSTAGE) & 1, abort_flag, derr, 52)) { alive = false; break; }
-        if (it >= 2 && !mbar_wait(gb + 2 + sb, ((it >> 1) - 1) & 1, abort_flag, derr, 53)) { alive = false; break; }
+        const int blk = kt0 / bs;
+        // zero V rows past the end of the sequence (never multiply garbage by P = 0)
+        if (kt0 + BN > kvl) {
+          if (!mbar_wait_warp(kv_full + st, (it / NSTAGE) & 1, abort_flag, derr, 60)) { alive = false; break; }
+          const int r0 = kvl - kt0;
+          uint8_t* dV = sm + OFF_V + st * 16384;
+          for (int e = m; e < (BN - r0) * 16; e += 128) {
+            const int row = r0 + e / 16, ch = e % 16;
+            *reinterpret_cast<uint4*>(dV + (ch >> 3) * 8192 + row * 128 + ((ch & 7) << 4)) = make_uint4(0, 0, 0, 0);
+          }
+          fence_proxy_async_smem();
+        }
+        // advance the routed-list cursor to this block (only rows with row_ok
+        // enter: their lists are in bounds)
+        while (cur_b >= 0 && cur_b < blk) {
+          ++cur_j;
+          cur_b = cur_j < K ? nxt_raw : -1;
+          cur_bias = has_bias ? nxt_bias_raw : 0.0f;
+          const int j2 = min(cur_j + 1, K - 1);
+          nxt_raw = rl[j2];
+          nxt_bias_raw = rbl[j2];
+        }
+        const bool sel = cur_b == blk;
+        const float b2 = sel ? cur_bias * LOG2E : 0.0f;
+        if (!mbar_wait_warp(s_full + sb, (it >> 1) & 1, abort_flag, derr, 61)) { alive = false; break; }
         tc_fence_after();
-        const uint32_t sK = smem_u32(sm + OFF_K + st * 16384);
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          uint64_t ad = sw128_desc(sQ + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-          uint64_t bd = sw128_desc(sK + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
-          umma_ss(tSg + sb * BN, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(gb + 0 + sb);
-        if (it >= 1 && !issue_pv(it - 1)) { alive = false; break; }
-        ++it;
-      }
-      if (alive && it >= 1) issue_pv(it - 1);
-      // all MMAs of this group complete before TMEM is released
-      umma_commit(mma_done + g);
-      volatile int no_abort = 0;
-      mbar_wait(mma_done + g, 0, &no_abort, nullptr, 54);
-    }
-    __syncwarp();
-  } else if (warp / 4 < ngroups) {
-    // ============ softmax / epilogue: group g, one thread per tile row ============
-    const int g = warp >> 2;
-    uint64_t* gb = bars + 6 + 9 * g;
-    uint64_t* s_full = gb + 0;
-    uint64_t* s_free = gb + 2;
-    uint64_t* p_full = gb + 4;
-    uint64_t* pv_done = gb + 6;
-    uint64_t* q_full = gb + 8;
-    const uint32_t tS = tmem + g * 256, tO = tmem + g * 256 + 128;
-    const int m = tid & 127;                 // row 0..127 of this group's tile
-    const int i0 = i0A + g * p.TT;
-    const int ntok = min(p.TT, qlen - i0);
-    const int tok = i0 + m / G;
-    const int hq = hk * G + (m % G);
-    const bool row_ok = (m / G) < ntok;
-    const int64_t pos = row_ok ? (int64_t)pos0 + tok : -1;
-    const int64_t lstart = pos - a.local_window + 1;
-    const int64_t rglob = row_base(a.seqs, s) + tok;
-    const int64_t segs = (row_ok && a.seg_start) ? (int64_t)a.seg_start[rglob] : 0;
-    // ---- Q row -> shared (swizzled K-major) ----
-    {
-      const T* qp = reinterpret_cast<const T*>(a.qo.q) +
-                    (a.seqs.q_start ? rglob * a.qo.q_stride_tok
-                                    : (int64_t)s * a.qo.q_stride_seq + (int64_t)tok * a.qo.q_stride_tok) +
-                    (int64_t)hq * a.qo.q_stride_head;
-      uint8_t* sq = sm + OFF_Q + g * 32768;
-#pragma unroll
-      for (int cc = 0; cc < 16; ++cc) {
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (row_ok) v = *reinterpret_cast<const uint4*>(qp + cc * 8);
-        const int region = cc >> 3, c8 = cc & 7;
-        *reinterpret_cast<uint4*>(sq + region * 16384 + m * 128 + ((c8 ^ (m & 7)) << 4)) = v;
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(q_full);
-    }
-    // routed list cursor
-    const int K = a.routes.K;
-    const int32_t* rl = p.cidx + ((int64_t)ih * p.n_rows + rglob) * K;
-    const float* rbl = p.cbias + ((int64_t)ih * p.n_rows + rglob) * K;
-    const bool has_bias = a.routes.bias != nullptr;
-    // cursor = entry cur_j; the entry after it is kept prefetched in registers
-    // so an advance never waits on a global load inside the tile loop
-    int cur_j = 0;
-    int cur_b = (row_ok && K > 0) ? rl[0] : -1;
-    float cur_bias = (row_ok && K > 0 && has_bias) ? rbl[0] : 0.0f;
-    int nxt_b = (row_ok && K > 1) ? rl[1] : -1;
-    float nxt_bias = (row_ok && K > 1 && has_bias) ? rbl[1] : 0.0f;
-    const float sl2 = a.scale * 1.4426950408889634f;
-    const float LOG2E = 1.4426950408889634f;
-    // Running max (exp2 domain) starts at the row's largest routed bias: the
-    // bias of the top entmax block is what makes a row's max jump, so starting
-    // there leaves rescaling of O for rows whose raw scores exceed it by > 2^8.
-    // Any start value is exact (O and l share the reference); a start above the
-    // true max only scales p by a power of two (no underflow for logits within
-    // ~100 of it).
-    float m_run = 0.0f, l_run = 0.0f;
-    if (row_ok && has_bias && K > 0)
-      m_run = fmaxf(0.0f, p.rowmax[(int64_t)ih * p.n_rows + rglob] * LOG2E);
-    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    TileIter itr{-1, -1, 0, 0u};
-    int it = 0;
-    bool alive = true;
-    while (alive) {
-      int kt0 = next_tile(itr, smask, p.nwords, bs, pmax, kvl);
-      if (kt0 < 0) break;
-      const int st = it % NSTAGE, sb = it & 1;
-      const int blk = kt0 / bs;
-      // zero V rows past the end of the sequence (never multiply garbage by P = 0)
-      if (kt0 + BN > kvl) {
-        if (!mbar_wait_warp(kv_full + st, (it / NSTAGE) & 1, abort_flag, derr, 60)) { alive = false; break; }
-        const int r0 = kvl - kt0;
-        uint8_t* dV = sm + OFF_V + st * 16384;
-        for (int e = m; e < (BN - r0) * 16; e += 128) {
-          const int row = r0 + e / 16, ch = e % 16;
-          *reinterpret_cast<uint4*>(dV + (ch >> 3) * 8192 + row * 128 + ((ch & 7) << 4)) = make_uint4(0, 0, 0, 0);
-        }
-        fence_proxy_async_smem();
-      }
-      // advance the routed-list cursor to this block
-      while (cur_b >= 0 && cur_b < blk) {
-        ++cur_j;
-        cur_b = nxt_b;
-        cur_bias = nxt_bias;
-        const int j2 = cur_j + 1;
-        nxt_b = (cur_b >= 0 && j2 < K) ? rl[j2] : -1;
-        nxt_bias = (cur_b >= 0 && j2 < K && has_bias) ? rbl[j2] : 0.0f;
-      }
-      const bool sel = cur_b == blk;
-      const float b2 = sel ? cur_bias * LOG2E : 0.0f;
-      if (!mbar_wait_warp(s_full + sb, (it >> 1) & 1, abort_flag, derr, 61)) { alive = false; break; }
-      tc_fence_after();
-      // Column c of this key tile is kept iff lo <= c <= hi, where lo is the
-      // first local column, or the first attendable column when the block is
-      // routed; logits are x = s*scale*log2e + (local ? 0 : bias) - m_run.
-      const int hi = (int)max((int64_t)-1, min((int64_t)63, pos - kt0));
-      const int lo_seg = (int)max((int64_t)0, min((int64_t)64, segs - kt0));
-      const int lo_loc = (int)max((int64_t)0, min((int64_t)64, lstart - kt0));
-      const int lo = max(sel ? 0 : lo_loc, lo_seg);
-      const float add_loc = -m_run;
-      const float add_rem = b2 - m_run;
-      // P buffer sb was last read by PV(it-2) (long done by now in practice)
-      if (it >= 2 && !mbar_wait_warp(pv_done + sb, ((it - 2) >> 1) & 1, abort_flag, derr, 63)) { alive = false; break; }
-      uint8_t* dP = sm + OFF_P + (2 * g + sb) * 16384 + m * 128;
-      const uint32_t tSb = tS + sb * BN + lane_base;
-      // Pure tile for this row: all 64 columns kept with one additive term, or
-      // none kept.  When every row of the warp is pure and the tile lies inside
-      // the sequence (tiles away from the window edge and the diagonal), the
-      // logits take one packed FFMA per 2 columns (an empty row adds -inf), P is
-      // produced directly, and the rescale test runs on the packed P maximum.
-      // S is read from TMEM in two 32-column halves to keep registers low.
-      const bool empty = lo > hi;
-      const bool full = lo == 0 && hi == 63 && (lo_loc == 0 || lo_loc == 64);
-      bool done = false;
-      if (__all_sync(0xffffffffu, empty || full) && kt0 + BN <= kvl) {
-        const float add = empty ? -INFINITY : (lo_loc == 0 ? add_loc : add_rem);
-        const uint64_t sl2v = f2_pack(sl2, sl2), addv = f2_pack(add, add);
-        uint64_t lsv = f2_pack(0.0f, 0.0f);
-        uint32_t pmax = 0;                         // packed +0.0 pair
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          float x[32];
-          tmem_ld32f(tSb + 32 * h, x);
+        // Column c of this key tile is kept iff lo <= c <= hi, where lo is the
+        // first local column, or the first attendable column when the block is
+        // routed; logits are x = s*scale*log2e + (local ? 0 : bias) - m_run.
+        const int hi = (int)max((int64_t)-1, min((int64_t)63, pos - kt0));
+        const int lo_seg = (int)max((int64_t)0, min((int64_t)64, segs - kt0));
+        const int lo_loc = (int)max((int64_t)0, min((int64_t)64, lstart - kt0));
+        const int lo = max(sel ? 0 : lo_loc, lo_seg);
+        const float add_loc = -m_run;
+        const float add_rem = b2 - m_run;
+        const uint32_t tSb = tS + sb * BN + lane_base;
+        uint32_t pk[32];
+        // Pure tile for this row: all 64 columns kept with one additive term, or
+        // none kept.  When every row of the warp is pure and the tile lies inside
+        // the sequence (tiles away from the window edge and the diagonal), the
+        // logits take one packed FFMA per 2 columns (an empty row adds -inf), P is
+        // produced directly, and the rescale test runs on the packed P maximum.
+        const bool empty = lo > hi;
+        const bool full = lo == 0 && hi == 63 && (lo_loc == 0 || lo_loc == 64);
+        bool done = false;
+        if (__all_sync(0xffffffffu, empty || full) && kt0 + BN <= kvl) {
+          float x[64];
+          tmem_ld32f(tSb, x);
+          tmem_ld32f(tSb + 32, x + 32);
           tmem_ld_wait();
-#pragma unroll
-          for (int c8 = 0; c8 < 4; ++c8) {
-            uint32_t pk[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int c = 8 * c8 + 2 * e;
-              float y0, y1;
-              f2_unpack(ffma2(f2_pack(x[c], x[c + 1]), sl2v, addv), y0, y1);
-              const float p0 = fast_exp2(y0);
-              const float p1 = fast_exp2(y1);
-              lsv = fadd2(lsv, f2_pack(p0, p1));
-              pk[e] = pack2(p0, p1, (T*)nullptr);
-              pmax = hmax2u(pmax, pk[e], (T*)nullptr);
+          const float add = empty ? -INFINITY : (lo_loc == 0 ? add_loc : add_rem);
+          const uint64_t sl2v = f2_pack(sl2, sl2), addv = f2_pack(add, add);
+          uint64_t lsv = f2_pack(0.0f, 0.0f);
+          uint32_t pmx = 0;                          // packed +0.0 pair
+  #pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            float y0, y1;
+            f2_unpack(ffma2(f2_pack(x[2 * e], x[2 * e + 1]), sl2v, addv), y0, y1);
+            const float p0 = fast_exp2(y0);
+            const float p1 = fast_exp2(y1);
+            lsv = fadd2(lsv, f2_pack(p0, p1));
+            pk[e] = pack2(p0, p1, (T*)nullptr);
+            pmx = hmax2u(pmx, pk[e], (T*)nullptr);
+          }
+          const float2 pm = unpack2(pmx, (T*)nullptr);
+          const bool big = !(fmaxf(pm.x, pm.y) <= kGrowP);   // p > 2^kGrowLog2 (or inf/NaN)
+          if (!__any_sync(0xffffffffu, big)) {
+            float l0, l1;
+            f2_unpack(lsv, l0, l1);
+            l_run += l0 + l1;
+            done = true;
+          }
+        }
+        if (!done) {
+          // general path: row max, optional rescale of O, then P.  S is read
+          // in 32-column halves, once per pass (it is intact until P is stored
+          // over it), which keeps the rare path inside the register budget.
+          float mx = -INFINITY;
+  #pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float x[32];
+            tmem_ld32f(tSb + 32 * h, x);
+            tmem_ld_wait();
+  #pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int c = 32 * h + j;
+              const float v = fmaf(x[j], sl2, c >= lo_loc ? add_loc : add_rem);
+              mx = fmaxf(mx, (c >= lo && c <= hi) ? v : -INFINITY);
             }
-            const int cc = 4 * h + c8;
-            *reinterpret_cast<uint4*>(dP + ((cc ^ (m & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           }
-        }
-        const float2 pm = unpack2(pmax, (T*)nullptr);
-        const bool big = !(fmaxf(pm.x, pm.y) <= 256.0f);   // p > 2^8 (or inf/NaN)
-        if (!__any_sync(0xffffffffu, big)) {
-          float l0, l1;
-          f2_unpack(lsv, l0, l1);
-          l_run += l0 + l1;
-          done = true;
-        }
-      }
-      if (!done) {
-        // general path: pass 1 row max, optional rescale, pass 2 P
-        float mx = -INFINITY;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          float x[32];
-          tmem_ld32f(tSb + 32 * h, x);
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int c = 32 * h + j;
-            const float v = fmaf(x[j], sl2, c >= lo_loc ? add_loc : add_rem);
-            mx = fmaxf(mx, (c >= lo && c <= hi) ? v : -INFINITY);
-          }
-        }
-        const bool need = mx > 8.0f;             // row max grew by more than 2^8
-        float shift = 0.0f;
-        if (__any_sync(0xffffffffu, need)) {
-          const float f = need ? fast_exp2(-mx) : 1.0f;
-          if (it > 0) {
-            if (!mbar_wait_warp(pv_done + ((it - 1) & 1), ((it - 1) >> 1) & 1, abort_flag, derr, 62)) { alive = false; break; }
-            tc_fence_after();
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
-              uint32_t o[32];
-              tmem_ld32(tO + q4 * 32 + lane_base, o);
-              tmem_ld_wait();
-#pragma unroll
-              for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * f);
-              tmem_st32(tO + q4 * 32 + lane_base, o);
+          const bool need = mx > kGrowLog2;
+          float shift = 0.0f;
+          if (__any_sync(0xffffffffu, need)) {
+            const float f = need ? fast_exp2(-mx) : 1.0f;
+            if (it > 0) {
+              if (!mbar_wait_warp(pv_done + ((it - 1) & 1), ((it - 1) >> 1) & 1, abort_flag, derr, 62)) { alive = false; break; }
+              tc_fence_after();
+  #pragma unroll 1
+              for (int q4 = 0; q4 < 4; ++q4) {
+                uint32_t o[32];
+                tmem_ld32(tO + q4 * 32 + lane_base, o);
+                tmem_ld_wait();
+  #pragma unroll
+                for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * f);
+                tmem_st32(tO + q4 * 32 + lane_base, o);
+              }
+              tmem_st_wait();
             }
-            tmem_st_wait();
+            l_run *= f;
+            if (need) {
+              m_run += mx;
+              shift = mx;
+            }
           }
-          l_run *= f;
-          if (need) {
-            m_run += mx;
-            shift = mx;
-          }
-        }
-        float ls4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          float x[32];
-          tmem_ld32f(tSb + 32 * h, x);
-          tmem_ld_wait();
-#pragma unroll
-          for (int c8 = 0; c8 < 4; ++c8) {
-            uint32_t pk[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
+          float ls4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  #pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float x[32];
+            tmem_ld32f(tSb + 32 * h, x);
+            tmem_ld_wait();
+  #pragma unroll
+            for (int e = 0; e < 16; ++e) {
               float pp[2];
-#pragma unroll
+  #pragma unroll
               for (int u = 0; u < 2; ++u) {
-                const int j = 8 * c8 + 2 * e + u, c = 32 * h + j;
+                const int j = 2 * e + u, c = 32 * h + j;
                 const float v = fmaf(x[j], sl2, (c >= lo_loc ? add_loc : add_rem) - shift);
                 pp[u] = fast_exp2((c >= lo && c <= hi) ? v : -INFINITY);
               }
-              ls4[e] += pp[0] + pp[1];
-              pk[e] = pack2(pp[0], pp[1], (T*)nullptr);
+              ls4[e & 3] += pp[0] + pp[1];
+              pk[16 * h + e] = pack2(pp[0], pp[1], (T*)nullptr);
             }
-            const int cc = 4 * h + c8;
-            *reinterpret_cast<uint4*>(dP + ((cc ^ (m & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           }
+          l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
         }
-        l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
+        // P(it) over the first 32 columns of S buffer sb (this thread's S reads
+        // completed above), then hand it to the MMA warp
+        tmem_st32(tSb, pk);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full + sb);
+        ++it;
       }
-      tc_fence_before();
-      mbar_arrive(s_free + sb);                  // S buffer sb fully read
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(p_full + sb);
-      ++it;
-    }
-    // ---- epilogue ----
-    float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
-    bool have_o = alive && it > 0;
-    if (have_o && !mbar_wait_warp(pv_done + ((it - 1) & 1), ((it - 1) >> 1) & 1, abort_flag, derr, 64)) have_o = false;
-    tc_fence_after();
-    T* op = reinterpret_cast<T*>(a.qo.out) +
-            (a.seqs.q_start ? rglob * a.qo.o_stride_tok
-                            : (int64_t)s * a.qo.o_stride_seq + (int64_t)tok * a.qo.o_stride_tok) +
-            (int64_t)hq * a.qo.o_stride_head;
-#pragma unroll
-    for (int q4 = 0; q4 < 4; ++q4) {
-      uint32_t o[32];
-      tmem_ld32(tO + q4 * 32 + lane_base, o);
-      tmem_ld_wait();
-      if (row_ok) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          float a0 = have_o ? __uint_as_float(o[c]) * inv_l : 0.0f;
-          float a1 = have_o ? __uint_as_float(o[c + 1]) * inv_l : 0.0f;
-          pk[c >> 1] = pack2(a0, a1, (T*)nullptr);
+      // ---- epilogue ----
+      float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+      bool have_o = alive && it > 0;
+      if (have_o && !mbar_wait_warp(pv_done + ((it - 1) & 1), ((it - 1) >> 1) & 1, abort_flag, derr, 64)) have_o = false;
+      tc_fence_after();
+      T* op = reinterpret_cast<T*>(a.qo.out) +
+              (a.seqs.q_start ? rglob * a.qo.o_stride_tok
+                              : (int64_t)s * a.qo.o_stride_seq + (int64_t)tok * a.qo.o_stride_tok) +
+              (int64_t)hq * a.qo.o_stride_head;
+  #pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint32_t o[32];
+        tmem_ld32(tO + q4 * 32 + lane_base, o);
+        tmem_ld_wait();
+        if (row_ok) {
+          uint32_t pko[16];
+  #pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            float a0 = have_o ? __uint_as_float(o[c]) * inv_l : 0.0f;
+            float a1 = have_o ? __uint_as_float(o[c + 1]) * inv_l : 0.0f;
+            pko[c >> 1] = pack2(a0, a1, (T*)nullptr);
+          }
+  #pragma unroll
+          for (int v = 0; v < 4; ++v)
+            *reinterpret_cast<uint4*>(op + q4 * 32 + v * 8) = make_uint4(pko[4 * v], pko[4 * v + 1], pko[4 * v + 2], pko[4 * v + 3]);
         }
-#pragma unroll
-        for (int v = 0; v < 4; ++v)
-          *reinterpret_cast<uint4*>(op + q4 * 32 + v * 8) = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
       }
-    }
-    if (row_ok && a.qo.lse) {
-      float lse = l_run > 0.0f ? (m_run + log2f(l_run)) * 0.6931471805599453f : -INFINITY;
-      a.qo.lse[(a.seqs.q_start ? rglob * a.qo.lse_stride_tok
-                               : (int64_t)s * a.qo.lse_stride_seq + (int64_t)tok * a.qo.lse_stride_tok) +
-               (int64_t)hq * a.qo.lse_stride_head] = lse;
+      if (row_ok && a.qo.lse) {
+        float lse = l_run > 0.0f ? (m_run + log2f(l_run)) * 0.6931471805599453f : -INFINITY;
+        a.qo.lse[(a.seqs.q_start ? rglob * a.qo.lse_stride_tok
+                                 : (int64_t)s * a.qo.lse_stride_seq + (int64_t)tok * a.qo.lse_stride_tok) +
+                 (int64_t)hq * a.qo.lse_stride_head] = lse;
+      }
     }
   }
   tc_fence_before();
@@ -725,17 +743,25 @@ int launch_prefill(const DashPrefillArgs& a, int64_t n_rows, cudaStream_t st) {
   rc = make_kv_map(&mv, a.kv.v, a, p.paged);
   if (rc) return rc;
   dim3 grid((unsigned)(a.seqs.n_seq * ((p.tiles_per_seq + 1) / 2)), a.kv.n_kv_heads);
-  auto launch = [&](auto kern) {
+  auto launch = [&](auto kern) -> int {
+    // the in-kernel register growth waits until the pool covers it: launch
+    // only a build whose per-thread count matches the split
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess)
+      return set_error(DASH_ERR_CUDA, "cudaFuncGetAttributes(prefill_kernel) failed");
+    if (fa.numRegs != kLaunchRegs)
+      return set_error(DASH_ERR_UNSUPPORTED, "prefill_kernel built with %d registers per thread, "
+                       "the register split needs %d", fa.numRegs, kLaunchRegs);
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     kern<<<grid, NTHREADS, SMEM_BYTES, st>>>(mk, mv, a, p);
+    return DASH_OK;
   };
   if (a.kv.dtype == DASH_DTYPE_BF16) {
-    if (p.paged) launch(prefill_kernel<__nv_bfloat16, true>);
-    else launch(prefill_kernel<__nv_bfloat16, false>);
+    rc = p.paged ? launch(prefill_kernel<__nv_bfloat16, true>) : launch(prefill_kernel<__nv_bfloat16, false>);
   } else {
-    if (p.paged) launch(prefill_kernel<__half, true>);
-    else launch(prefill_kernel<__half, false>);
+    rc = p.paged ? launch(prefill_kernel<__half, true>) : launch(prefill_kernel<__half, false>);
   }
+  if (rc) return rc;
   count_launch();
   return check_launch("prefill_kernel");
 }

@@ -46,9 +46,12 @@ __global__ void __launch_bounds__(128) kbar_pool_kernel(DashKbarArgs a) {
     base = a.pages[i] * a.page_stride;
     out_row = a.pages[i];
   }
+  // Stage the block's keys; non-coherent loads, eight in flight per thread
+  // (the loads do not wait on the shared-memory stores between them).
+#pragma unroll 8
   for (int e = threadIdx.x; e < n * d; e += blockDim.x) {
     int j = e / d, c = e - j * d;
-    sk[j * ld + c] = (float)keys[base + (int64_t)j * a.tok_stride + c];
+    sk[j * ld + c] = (float)__ldg(keys + base + (int64_t)j * a.tok_stride + c);
   }
   for (int c = threadIdx.x; c < d; c += blockDim.x) shc[c] = a.head_cls ? a.head_cls[c] : 0.0f;
   __syncthreads();
@@ -123,8 +126,8 @@ __device__ __forceinline__ uint32_t order_key(float x) {
 // Restates modeling_deepseekv2.py:309-333 + 351-388 (and WHL dash_router.py
 // route_and_select): cand = remote & mask (fallback remote); x = cand ? z*scale
 // : -1e4; top-M by (x desc, id asc) via a radix select on the order-preserving
-// key; entmax tau by bisection over the top-M and a closed-form refinement on
-// the found support; first K by rank; bias = (log max(p,floor) - mean)/sigma
+// key; entmax tau by the sort-based formula over the ranked top-M; first K by
+// rank; bias = (log max(p,floor) - mean)/sigma
 // over the valid (candidate) slots; ascending pack with -1 tail.
 // ---------------------------------------------------------------------------
 constexpr int kRouteWarps = 4;
@@ -177,13 +180,63 @@ __device__ __forceinline__ void score_blocks(const DashRouteArgs& a, const float
   }
 }
 
-// Selection for one row whose W scores are in sx (overwritten), by one warp:
-// candidates, x = score*scale, top-M radix select, ranks, entmax, bias, pack.
+// Largest T with #{key >= T} >= M, decided bit by bit from the top.  The scan
+// stops once exactly M keys are >= T: the top-M set is then fixed and has no
+// partial tie at its boundary.  Keys are order_key(x); padding keys are 0,
+// below every real key.
+template <int KW>
+__device__ __forceinline__ uint32_t radix_threshold(const uint32_t (&kr)[KW], int M) {
+  uint32_t T = 0;
+  for (int bit = 31; bit >= 0; --bit) {
+    const uint32_t trial = T | (1u << bit);
+    int c = 0;
+#pragma unroll
+    for (int u = 0; u < KW; ++u) c += kr[u] >= trial ? 1 : 0;
+    c = __reduce_add_sync(0xffffffffu, c);
+    if (c >= M) {
+      T = trial;
+      if (c == M) break;
+    }
+  }
+  return T;
+}
+
+__device__ __forceinline__ uint32_t radix_threshold_smem(const float* sx, int W, int M, int lane) {
+  uint32_t T = 0;
+  for (int bit = 31; bit >= 0; --bit) {
+    const uint32_t trial = T | (1u << bit);
+    int c = 0;
+    for (int b = lane; b < W; b += 32) c += order_key(sx[b]) >= trial ? 1 : 0;
+    c = __reduce_add_sync(0xffffffffu, c);
+    if (c >= M) {
+      T = trial;
+      if (c == M) break;
+    }
+  }
+  return T;
+}
+
+// Selection for one row whose W scores are in sx, by one warp: candidates,
+// x = score*scale, top-M (x desc, id asc), 1.5-entmax over the top-M, first K
+// by rank, bias, ascending pack.  KW > 0: W <= 32*KW and the x / keys of
+// block lane + 32u live in registers; KW == 0: they stay in sx (overwritten).
+//
+// The entmax threshold is the sort-based formula of
+// modeling_deepseekv2.py:_infer_route_select (via entmax15): for every rank k
+// of the sorted z = (x - max)/2, tau_k = mean_k - sqrt(max((1 - ss_k)/k, 0))
+// from prefix sums taken sequentially in rank order; support = #{k : tau_k <=
+// z_k}; tau = tau_support.  Each step is one correctly rounded operation in
+// the order of the CPU restatement, so tau is bitwise the restatement's.
+//
+// Per-warp scratch: mid_ (block id by slot; slots ascend by id), mx (x by
+// slot, then z by rank, then log-prior by rank), mval (valid flag by rank).
+template <int KW>
 __device__ __noinline__ void select_row(const DashRouteArgs& a, float* sx, uint32_t* scand,
-                                        int* mid_, float* mx, int* mrank, int64_t r, int s,
+                                        int* mid_, float* mx, int* mval, int64_t r, int s,
                                         int lane) {
   const int W = a.width;
   const int Wp = (W + 31) & ~31;
+  const uint32_t lt_mask = (1u << lane) - 1u;
   // ---- candidates (with per-row fallback) ----
   const uint8_t* cm = nullptr;
   if (a.cand) cm = a.cand + (a.cand_per_seq ? (int64_t)s : r) * a.cand_row_stride;
@@ -206,164 +259,206 @@ __device__ __noinline__ void select_row(const DashRouteArgs& a, float* sx, uint3
     }
     __syncwarp();
   }
-  for (int b = lane; b < W; b += 32) {
-    bool c = (scand[b >> 5] >> (b & 31)) & 1u;
-    float v = c ? __fmul_rn(sx[b], a.idx_scale) : kEntmaxNeg;
+  auto is_cand = [&](int b) -> bool { return (scand[b >> 5] >> (b & 31)) & 1u; };
+  auto xform = [&](int b) -> float {
+    float v = is_cand(b) ? __fmul_rn(sx[b], a.idx_scale) : kEntmaxNeg;
     if (!(v == v) || isinf(v)) v = kEntmaxNeg;
-    sx[b] = v;
-  }
-  __syncwarp();
+    return v;
+  };
 
-  // ---- top-M threshold (radix select over the order-preserving key) ----
+  // ---- top-M, gathered into slots in ascending id order ----
   int M = a.topm > 0 ? min(a.topm, W) : W;
   if (M < 1) M = 1;
-  uint32_t T = 0;
-  if (M < W) {
-    for (int bit = 31; bit >= 0; --bit) {
-      uint32_t trial = T | (1u << bit);
-      int cnt = 0;
-      for (int b = lane; b < W; b += 32) cnt += order_key(sx[b]) >= trial;
-      cnt = __reduce_add_sync(0xffffffffu, cnt);
-      if (cnt >= M) T = trial;
-    }
-  }
-  // gather the M items in ascending id order: keys > T, then the lowest-id ties
-  int n_gt = 0;
-  if (M < W) {
-    int c = 0;
-    for (int b = lane; b < W; b += 32) c += order_key(sx[b]) > T;
-    n_gt = __reduce_add_sync(0xffffffffu, c);
-  }
-  int ties_left = M - n_gt;
   int n_items = 0;
-  for (int b0 = 0; b0 < Wp; b0 += 32) {
-    int b = b0 + lane;
+  auto gather = [&](int b, float x, uint32_t k, uint32_t T, int& ties_left) {
     bool in = false, tie = false;
     if (b < W) {
-      uint32_t k = order_key(sx[b]);
-      if (M >= W) in = true;
-      else if (k > T) in = true;
+      if (M >= W || k > T) in = true;
       else if (k == T) tie = true;
     }
-    uint32_t tb = __ballot_sync(0xffffffffu, tie);
-    int tie_rank = __popc(tb & ((1u << lane) - 1u));
-    if (tie && tie_rank < ties_left) in = true;
+    const uint32_t tb = __ballot_sync(0xffffffffu, tie);
+    if (tie && __popc(tb & lt_mask) < ties_left) in = true;
     ties_left -= min(ties_left, __popc(tb));
-    uint32_t ib = __ballot_sync(0xffffffffu, in);
+    const uint32_t ib = __ballot_sync(0xffffffffu, in);
     if (in) {
-      int slot = n_items + __popc(ib & ((1u << lane) - 1u));
+      const int slot = n_items + __popc(ib & lt_mask);
       mid_[slot] = b;
-      mx[slot] = sx[b];
+      mx[slot] = x;
     }
     n_items += __popc(ib);
+  };
+  if constexpr (KW > 0) {
+    float xr[KW];
+    uint32_t kr[KW];
+#pragma unroll
+    for (int u = 0; u < KW; ++u) {
+      const int b = lane + 32 * u;
+      xr[u] = b < W ? xform(b) : 0.0f;
+      kr[u] = b < W ? order_key(xr[u]) : 0u;
+    }
+    uint32_t T = 0;
+    int n_gt = 0;
+    if (M < W) {
+      T = radix_threshold<KW>(kr, M);
+      int c = 0;
+#pragma unroll
+      for (int u = 0; u < KW; ++u) c += kr[u] > T ? 1 : 0;
+      n_gt = __reduce_add_sync(0xffffffffu, c);
+    }
+    int ties_left = M - n_gt;
+#pragma unroll
+    for (int u = 0; u < KW; ++u)
+      if (32 * u < W) gather(lane + 32 * u, xr[u], kr[u], T, ties_left);
+  } else {
+    for (int b = lane; b < W; b += 32) sx[b] = xform(b);
+    __syncwarp();
+    uint32_t T = 0;
+    int n_gt = 0;
+    if (M < W) {
+      T = radix_threshold_smem(sx, W, M, lane);
+      int c = 0;
+      for (int b = lane; b < W; b += 32) c += order_key(sx[b]) > T ? 1 : 0;
+      n_gt = __reduce_add_sync(0xffffffffu, c);
+    }
+    int ties_left = M - n_gt;
+    for (int b0 = 0; b0 < Wp; b0 += 32) {
+      const int b = b0 + lane;
+      const float x = b < W ? sx[b] : 0.0f;
+      gather(b, x, b < W ? order_key(x) : 0u, T, ties_left);
+    }
   }
   __syncwarp();
   M = n_items;  // == M
 
-  // ---- rank of each item by (x desc, id asc) ----
-  for (int t = lane; t < M; t += 32) {
-    float xt = mx[t];
-    int it = mid_[t], rk = 0;
-    for (int u = 0; u < M; ++u) {
-      float xu = mx[u];
-      rk += (xu > xt) || (xu == xt && mid_[u] < it);
-    }
-    mrank[t] = rk;
-  }
-  __syncwarp();
-
-  // ---- 1.5-entmax over the M items: z = (x - max)/2; tau by bisection ----
-  float xmax = -INFINITY;
-  for (int t = lane; t < M; t += 32) xmax = fmaxf(xmax, mx[t]);
-  for (int o = 16; o > 0; o >>= 1) xmax = fmaxf(xmax, __shfl_xor_sync(0xffffffffu, xmax, o));
+  // ---- rank of slot t = lane + 32u by (x desc, id asc) ----
   constexpr int PER = kMaxM / 32;
-  float zl[PER];
+  const int nper = (M + 31) >> 5;
+  float xt[PER];
+  int rk[PER];
 #pragma unroll
   for (int u = 0; u < PER; ++u) {
-    int t = lane + 32 * u;
-    zl[u] = t < M ? __fdiv_rn(__fsub_rn(mx[t], xmax), 2.0f) : -INFINITY;
+    const int t = lane + 32 * u;
+    xt[u] = (u < nper && t < M) ? mx[t] : -INFINITY;
+    rk[u] = 0;
   }
-  float lo = -1.0f, hi = 0.0f;
-  for (int it = 0; it < 30; ++it) {
-    float m = 0.5f * (lo + hi);
-    float f = 0.0f;
+  for (int v = 0; v < M; ++v) {
+    const float xv = mx[v];
 #pragma unroll
-    for (int u = 0; u < PER; ++u) {
-      float t = fmaxf(zl[u] - m, 0.0f);
-      f = __fmaf_rn(t, t, f);
-    }
-    for (int o = 16; o > 0; o >>= 1) f += __shfl_xor_sync(0xffffffffu, f, o);
-    if (f > 1.0f) lo = m; else hi = m;
+    for (int u = 0; u < PER; ++u)
+      if (u < nper) rk[u] += (xv > xt[u] || (xv == xt[u] && v < lane + 32 * u)) ? 1 : 0;
   }
-  float tau_b = 0.5f * (lo + hi);
-  // closed form on the support {z > tau_b}: tau = mean - sqrt(max((1-ss)/k, 0))
-  float s1 = 0.0f, s2 = 0.0f, kk = 0.0f;
+  float xmax = -INFINITY;
 #pragma unroll
-  for (int u = 0; u < PER; ++u)
-    if (zl[u] > tau_b) { s1 += zl[u]; s2 = __fmaf_rn(zl[u], zl[u], s2); kk += 1.0f; }
-  for (int o = 16; o > 0; o >>= 1) {
-    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-    s2 += __shfl_xor_sync(0xffffffffu, s2, o);
-    kk += __shfl_xor_sync(0xffffffffu, kk, o);
-  }
-  if (kk < 1.0f) kk = 1.0f;
-  float mean = s1 / kk, mean_sq = s2 / kk;
-  float ss = kk * (mean_sq - mean * mean);
-  float delta = (1.0f - ss) / kk;
-  float tau = mean - sqrtf(fmaxf(delta, 0.0f));
-
-  // ---- first K by rank; bias over the valid (candidate) ones ----
+  for (int u = 0; u < PER; ++u) xmax = fmaxf(xmax, xt[u]);
+  for (int o = 16; o > 0; o >>= 1) xmax = fmaxf(xmax, __shfl_xor_sync(0xffffffffu, xmax, o));
   int Kc = min(a.K, M);
   if (Kc < 1) Kc = 1;
-  float lsum = 0.0f;
-  int cnt = 0;
-  float logp_l[PER];
-  bool valid_l[PER];
+  bool valid[PER];
+  __syncwarp();  // every lane has read mx by slot
 #pragma unroll
   for (int u = 0; u < PER; ++u) {
-    int t = lane + 32 * u;
-    valid_l[u] = false;
-    logp_l[u] = 0.0f;
-    if (t < M && mrank[t] < Kc) {
-      int b = mid_[t];
-      bool c = (scand[b >> 5] >> (b & 31)) & 1u;
-      float pz = fmaxf(zl[u] - tau, 0.0f);
-      float p = pz * pz;
-      logp_l[u] = logf(fmaxf(p, a.prior_floor));
-      valid_l[u] = c;
-      if (c) { lsum += logp_l[u]; cnt += 1; }
+    const int t = lane + 32 * u;
+    valid[u] = false;
+    if (u < nper && t < M) {
+      valid[u] = rk[u] < Kc && is_cand(mid_[t]);
+      mx[rk[u]] = __fdiv_rn(__fsub_rn(xt[u], xmax), 2.0f);   // z by rank
+      mval[rk[u]] = valid[u] ? 1 : 0;
     }
   }
-  for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
-  cnt = __reduce_add_sync(0xffffffffu, cnt);
-  const float mu = lsum / (float)(cnt > 0 ? cnt : 1);
-
-  // ---- ascending pack ----
-  int32_t* oi = a.out_idx + r * a.out_stride;
-  float* ob = a.out_bias + r * a.out_stride;
-  for (int j = lane; j < a.out_width; j += 32) { oi[j] = -1; ob[j] = 0.0f; }
   __syncwarp();
+
+  // ---- tau_k for rank k = lane + 32u; support; tau ----
+  float cs = 0.0f, cs2 = 0.0f;
+  float tau_r[PER];
+  int support = 0;
 #pragma unroll
   for (int u = 0; u < PER; ++u) {
-    int t = lane + 32 * u;
-    if (valid_l[u]) {
-      int b = mid_[t];
-      // position = number of valid selected items with a smaller id
-      int p = 0;
-      for (int v = 0; v < M; ++v) {
-        if (mrank[v] < Kc) {
-          int bv = mid_[v];
-          bool cv = (scand[bv >> 5] >> (bv & 31)) & 1u;
-          p += cv && bv < b;
+    tau_r[u] = 0.0f;
+    if (u < nper) {
+      const int k = lane + 32 * u;
+      // add z_j for j = previous k + 1 .. k in ascending order (u = 0: 0 .. k)
+      const int jstart = u == 0 ? 32 - min(M, 32) : 0;
+      for (int jj = jstart; jj < 32; ++jj) {
+        const int j = k - 31 + jj;
+        if (j >= 0) {
+          const float zj = mx[j];
+          cs = __fadd_rn(cs, zj);
+          cs2 = __fadd_rn(cs2, __fmul_rn(zj, zj));
         }
       }
-      if (p < a.out_width) {
-        oi[p] = b;
-        ob[p] = (logp_l[u] - mu) * a.inv_sigma;
+      bool in_support = false;
+      if (k < M) {
+        const float rho = (float)(k + 1);
+        const float mean = __fdiv_rn(cs, rho);
+        const float mean_sq = __fdiv_rn(cs2, rho);
+        const float ss = __fmul_rn(rho, __fsub_rn(mean_sq, __fmul_rn(mean, mean)));
+        const float delta = __fdiv_rn(__fsub_rn(1.0f, ss), rho);
+        const float tau = __fsub_rn(mean, __fsqrt_rn(delta > 0.0f ? delta : 0.0f));
+        tau_r[u] = tau;
+        in_support = tau <= mx[k];
       }
+      support += __popc(__ballot_sync(0xffffffffu, in_support));
     }
   }
-  if (a.out_count && lane == 0) a.out_count[r] = min(cnt, a.out_width);
+  if (support < 1) support = 1;
+  float tsel = 0.0f;
+#pragma unroll
+  for (int u = 0; u < PER; ++u)
+    if (u == ((support - 1) >> 5)) tsel = tau_r[u];
+  const float tau = __shfl_sync(0xffffffffu, tsel, (support - 1) & 31);
+
+  // ---- log prior of the first Kc ranks; mean over the valid ones ----
+  __syncwarp();  // every lane has read z by rank
+  for (int k = lane; k < Kc; k += 32) {
+    float t = __fsub_rn(mx[k], tau);
+    t = t > 0.0f ? t : 0.0f;
+    const float p = __fmul_rn(t, t);
+    mx[k] = logf(p > a.prior_floor ? p : a.prior_floor);
+  }
+  __syncwarp();
+  float lsum = 0.0f;
+  int cnt = 0;
+  for (int k = 0; k < Kc; ++k)
+    if (mval[k]) {
+      lsum = __fadd_rn(lsum, mx[k]);
+      ++cnt;
+    }
+  const float mu = __fdiv_rn(lsum, (float)(cnt > 0 ? cnt : 1));
+
+  // ---- ascending pack (slots ascend by id) ----
+  int32_t* oi = a.out_idx + r * a.out_stride;
+  float* ob = a.out_bias + r * a.out_stride;
+  int npos = 0;
+#pragma unroll
+  for (int u = 0; u < PER; ++u) {
+    if (u < nper) {
+      const uint32_t vb = __ballot_sync(0xffffffffu, valid[u]);
+      if (valid[u]) {
+        const int p = npos + __popc(vb & lt_mask);
+        if (p < a.out_width) {
+          oi[p] = mid_[lane + 32 * u];
+          ob[p] = __fmul_rn(__fsub_rn(mx[rk[u]], mu), a.inv_sigma);
+        }
+      }
+      npos += __popc(vb);
+    }
+  }
+  for (int j = npos + lane; j < a.out_width; j += 32) {
+    oi[j] = -1;
+    ob[j] = 0.0f;
+  }
+  if (a.out_count && lane == 0) a.out_count[r] = min(npos, a.out_width);
+}
+
+__device__ __forceinline__ void select_row_any(const DashRouteArgs& a, float* sx,
+                                               uint32_t* scand, int* mid_, float* mx, int* mval,
+                                               int64_t r, int s, int lane) {
+  const int W = a.width;
+  if (W <= 160) select_row<5>(a, sx, scand, mid_, mx, mval, r, s, lane);
+  else if (W <= 256) select_row<8>(a, sx, scand, mid_, mx, mval, r, s, lane);
+  else if (W <= 512) select_row<16>(a, sx, scand, mid_, mx, mval, r, s, lane);
+  else if (W <= 1024) select_row<32>(a, sx, scand, mid_, mx, mval, r, s, lane);
+  else select_row<0>(a, sx, scand, mid_, mx, mval, r, s, lane);
 }
 
 // ---------------------------------------------------------------------------
@@ -468,7 +563,7 @@ __global__ void __launch_bounds__(256) route_tile_kernel(DashRouteArgs a, int ti
     if (a.scores_out)
       for (int b = lane; b < W; b += 32) a.scores_out[r * a.scores_out_stride + b] = sx[b];
     __syncwarp();
-    select_row(a, sx, scand, mid_, mx, mrank, r, s, lane);
+    select_row_any(a, sx, scand, mid_, mx, mrank, r, s, lane);
     __syncwarp();
   }
 }
@@ -519,7 +614,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_rows_kernel(DashRouteA
   if (a.scores_out)
     for (int b = lane; b < W; b += 32) a.scores_out[r * a.scores_out_stride + b] = sx[b];
 
-  select_row(a, sx, scand, mid_, mx, mrank, r, s, lane);
+  select_row_any(a, sx, scand, mid_, mx, mrank, r, s, lane);
 }
 
 // ---------------------------------------------------------------------------

@@ -386,8 +386,12 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch eagerly instead of replaying captured CUDA graphs")
+    ap.add_argument("--decode-rows", type=int, default=0,
+                    help="decode batch override (small cases for profiler captures)")
     args = ap.parse_args()
     cfg = C2 if args.workload == "c2" else C4
+    if args.decode_rows > 0:
+        C3["R"] = args.decode_rows
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
