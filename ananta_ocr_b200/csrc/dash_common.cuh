@@ -67,7 +67,7 @@ __device__ __forceinline__ float det_expf(float x) {
 
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
-  asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
@@ -323,6 +323,41 @@ __device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
+}
+
+__device__ __forceinline__ uint64_t fadd2_rn(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// 2^y for a pair of values on the FMA pipe (offloads the MUFU unit).
+// Cody-Waite split y = j + f with j = round(y) taken by adding and removing
+// 1.5 * 2^23, |f| <= 1/2 exact, then 2^f from a degree-3 polynomial whose
+// constant term is fixed to 1; c1..c3 are a relative-error least-squares fit
+// made for this kernel on [-1/2, 1/2] (max relative error 1.0e-4, under a
+// tenth of a bf16 ulp), and 2^j enters through the exponent field.  y is
+// clamped to [-127, 64]: at -127 the result is exactly +0 (the exponent of
+// 1.0 minus 127), above 64 it stays >= 2^64, which callers treat as overflow.
+__device__ __forceinline__ uint64_t exp2_poly2(float y0, float y1) {
+  constexpr float kShift = 12582912.0f;   // 1.5 * 2^23
+  constexpr float c1 = 0.6932829022407532f, c2 = 0.24220998585224152f, c3 = 0.055008433759212494f;
+  y0 = fminf(fmaxf(y0, -127.0f), 64.0f);
+  y1 = fminf(fmaxf(y1, -127.0f), 64.0f);
+  const uint64_t yv = f2_pack(y0, y1);
+  const uint64_t t = fadd2_rn(yv, f2_pack(kShift, kShift));
+  const uint64_t jf = fadd2_rn(t, f2_pack(-kShift, -kShift));
+  const uint64_t fr = ffma2(jf, f2_pack(-1.0f, -1.0f), yv);
+  uint64_t pv = ffma2(fr, f2_pack(c3, c3), f2_pack(c2, c2));
+  pv = ffma2(pv, fr, f2_pack(c1, c1));
+  pv = ffma2(pv, fr, f2_pack(1.0f, 1.0f));
+  float p0, p1, t0, t1;
+  f2_unpack(pv, p0, p1);
+  f2_unpack(t, t0, t1);
+  // low bits of t hold j (the shifter's own bits vanish in the shift)
+  const uint32_t r0 = __float_as_uint(p0) + (__float_as_uint(t0) << 23);
+  const uint32_t r1 = __float_as_uint(p1) + (__float_as_uint(t1) << 23);
+  return f2_pack(__uint_as_float(r0), __uint_as_float(r1));
 }
 
 template <typename T> struct DType;

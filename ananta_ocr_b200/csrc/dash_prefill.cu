@@ -19,7 +19,7 @@
 //                     back over the S buffer it came from.
 // Keeping P in TMEM removes the P round trip through shared memory, which
 // (with the Q operand re-read by every QK MMA) bounds this kernel.  The
-// softmax warpgroups take 208 registers each and the TMA/MMA warpgroup 88
+// softmax warpgroups take 200 registers each and the TMA/MMA warpgroup 104
 // (setmaxnreg), so a thread holds its whole 64-column S row.
 // Rows that did not route a block of the union simply get P = 0 there.
 //
@@ -52,8 +52,8 @@ constexpr int NTHREADS = 384;
 // 128 TMA/MMA threads shrink to kOtherRegs.  The host refuses to launch a
 // build whose register count does not cover the split (the growth would wait).
 constexpr int kLaunchRegs = 168;
-constexpr int kSoftmaxRegs = 208;
-constexpr int kOtherRegs = 88;
+constexpr int kSoftmaxRegs = 200;
+constexpr int kOtherRegs = 104;
 static_assert(2 * 128 * kSoftmaxRegs + 128 * kOtherRegs <= NTHREADS * kLaunchRegs, "register split");
 static_assert(2 * kSoftmaxRegs + kOtherRegs <= 3 * kLaunchRegs, "register split per sub-partition");
 constexpr uint32_t TMEM_COLS = 512;               // per query tile: S0 | S1 | O
@@ -172,7 +172,9 @@ __global__ void __launch_bounds__(128) plan_kernel(DashPrefillArgs a, PrefillPla
 }
 
 // ---------------------------------------------------------------------------
-// Key-tile iterator over the shared block mask (ascending).
+// Key-tile iterator over the shared block mask (ascending).  After a call that
+// returned kt0 >= 0, b is the block of the tile and half its 64-key part, so
+// callers need no division by the block size.
 // ---------------------------------------------------------------------------
 struct TileIter {
   int w, b, half;
@@ -302,12 +304,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           int c1, c3;
           bool ok = true;
           if (PAGED) {
-            int64_t page = a.kv.block_table[(int64_t)s * a.kv.bt_stride + kt0 / bs];
+            int64_t page = a.kv.block_table[(int64_t)s * a.kv.bt_stride + itr.b];
             if (page < 0 || page >= a.kv.num_pages) {
               record_error(derr, DASH_DEV_BAD_PAGE, 41, page);
               ok = false;
             }
-            c1 = kt0 % bs;
+            c1 = itr.half * BN;
             c3 = (int)page;
           } else {
             c1 = kt0;
@@ -408,6 +410,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int64_t lstart = pos - a.local_window + 1;
       const int64_t rglob = row_base(a.seqs, s) + tok;
       const int64_t segs = (row_ok && a.seg_start) ? (int64_t)a.seg_start[rglob] : 0;
+      // positions inside one sequence fit in 32 bits (kv lengths are int32)
+      const int pos_i = (int)pos, lstart_i = (int)lstart, seg_i = (int)segs;
       // ---- Q row -> shared (swizzled K-major) ----
       {
         const T* qp = reinterpret_cast<const T*>(a.qo.q) +
@@ -428,8 +432,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       // routed list cursor
       const int K = a.routes.K;
-      const int32_t* rl = p.cidx + ((int64_t)ih * p.n_rows + rglob) * K;
-      const float* rbl = p.cbias + ((int64_t)ih * p.n_rows + rglob) * K;
+      // rows past the end of the tile read row 0's list (never used)
+      const int64_t lrow = (int64_t)ih * p.n_rows + (row_ok ? rglob : 0);
+      const int32_t* rl = p.cidx + lrow * K;
+      const float* rbl = p.cbias + lrow * K;
       const bool has_bias = a.routes.bias != nullptr;
       // cursor = entry cur_j; the raw entry after it is kept prefetched in
       // registers.  The prefetch is unconditional (index clamped to the list) and
@@ -455,11 +461,39 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       TileIter itr{-1, -1, 0, 0u};
       int it = 0;
       bool alive = true;
-      while (alive) {
-        int kt0 = next_tile(itr, smask, p.nwords, bs, pmax, kvl);
-        if (kt0 < 0) break;
+      // Advance the routed-list cursor to block blk; sel / b2 describe the
+      // block for this row.  Every kept routed block has a key tile of its
+      // own, so the cursor moves at most one entry per tile and takes the
+      // prefetched entry; the refill is unconditional (same address while the
+      // cursor stays) and first read a tile later.  The inner walk only serves
+      // lists that skip a tile, which plan_kernel never writes.
+      auto cursor_to = [&](int blk, bool& sel, float& b2) {
+        if (K > 0) {
+          if (cur_b >= 0 && cur_b < blk) {
+            ++cur_j;
+            cur_b = cur_j < K ? nxt_raw : -1;
+            cur_bias = has_bias ? nxt_bias_raw : 0.0f;
+            while (cur_b >= 0 && cur_b < blk) {
+              ++cur_j;
+              cur_b = cur_j < K ? rl[cur_j] : -1;
+              cur_bias = (cur_j < K && has_bias) ? rbl[cur_j] : 0.0f;
+            }
+          }
+          const int j2 = min(cur_j + 1, K - 1);
+          nxt_raw = rl[j2];
+          nxt_bias_raw = rbl[j2];
+        }
+        sel = cur_b == blk;
+        b2 = sel ? cur_bias * LOG2E : 0.0f;
+      };
+      // The iterator and the cursor run one tile ahead: the next tile's
+      // bookkeeping is done while this tile's S load is in flight.
+      int kt0 = next_tile(itr, smask, p.nwords, bs, pmax, kvl);
+      bool sel = false;
+      float b2 = 0.0f;
+      if (kt0 >= 0) cursor_to(itr.b, sel, b2);
+      while (alive && kt0 >= 0) {
         const int st = it % NSTAGE, sb = it & 1;
-        const int blk = kt0 / bs;
         // zero V rows past the end of the sequence (never multiply garbage by P = 0)
         if (kt0 + BN > kvl) {
           if (!mbar_wait_warp(kv_full + st, (it / NSTAGE) & 1, abort_flag, derr, 60)) { alive = false; break; }
@@ -471,31 +505,29 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
           fence_proxy_async_smem();
         }
-        // advance the routed-list cursor to this block (only rows with row_ok
-        // enter: their lists are in bounds)
-        while (cur_b >= 0 && cur_b < blk) {
-          ++cur_j;
-          cur_b = cur_j < K ? nxt_raw : -1;
-          cur_bias = has_bias ? nxt_bias_raw : 0.0f;
-          const int j2 = min(cur_j + 1, K - 1);
-          nxt_raw = rl[j2];
-          nxt_bias_raw = rbl[j2];
-        }
-        const bool sel = cur_b == blk;
-        const float b2 = sel ? cur_bias * LOG2E : 0.0f;
         if (!mbar_wait_warp(s_full + sb, (it >> 1) & 1, abort_flag, derr, 61)) { alive = false; break; }
         tc_fence_after();
         // Column c of this key tile is kept iff lo <= c <= hi, where lo is the
         // first local column, or the first attendable column when the block is
         // routed; logits are x = s*scale*log2e + (local ? 0 : bias) - m_run.
-        const int hi = (int)max((int64_t)-1, min((int64_t)63, pos - kt0));
-        const int lo_seg = (int)max((int64_t)0, min((int64_t)64, segs - kt0));
-        const int lo_loc = (int)max((int64_t)0, min((int64_t)64, lstart - kt0));
+        // S(it) -> registers; the row's mask terms are computed while the
+        // load is in flight (the wait comes before any branch on them)
+        const uint32_t tSb = tS + sb * BN + lane_base;
+        float x[64];
+        tmem_ld32f(tSb, x);
+        tmem_ld32f(tSb + 32, x + 32);
+        const int hi = min(63, max(-1, pos_i - kt0));
+        const int lo_seg = min(64, max(0, seg_i - kt0));
+        const int lo_loc = min(64, max(0, lstart_i - kt0));
         const int lo = max(sel ? 0 : lo_loc, lo_seg);
         const float add_loc = -m_run;
         const float add_rem = b2 - m_run;
-        const uint32_t tSb = tS + sb * BN + lane_base;
+        const int kt_next = next_tile(itr, smask, p.nwords, bs, pmax, kvl);
+        bool sel_next = false;
+        float b2_next = 0.0f;
+        if (kt_next >= 0) cursor_to(itr.b, sel_next, b2_next);
         uint32_t pk[32];
+        tmem_ld_wait();
         // Pure tile for this row: all 64 columns kept with one additive term, or
         // none kept.  When every row of the warp is pure and the tile lies inside
         // the sequence (tiles away from the window edge and the diagonal), the
@@ -505,10 +537,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const bool full = lo == 0 && hi == 63 && (lo_loc == 0 || lo_loc == 64);
         bool done = false;
         if (__all_sync(0xffffffffu, empty || full) && kt0 + BN <= kvl) {
-          float x[64];
-          tmem_ld32f(tSb, x);
-          tmem_ld32f(tSb + 32, x + 32);
-          tmem_ld_wait();
           const float add = empty ? -INFINITY : (lo_loc == 0 ? add_loc : add_rem);
           const uint64_t sl2v = f2_pack(sl2, sl2), addv = f2_pack(add, add);
           uint64_t lsv = f2_pack(0.0f, 0.0f);
@@ -517,8 +545,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           for (int e = 0; e < 32; ++e) {
             float y0, y1;
             f2_unpack(ffma2(f2_pack(x[2 * e], x[2 * e + 1]), sl2v, addv), y0, y1);
-            const float p0 = fast_exp2(y0);
-            const float p1 = fast_exp2(y1);
+            // one pair in four on the FMA pipe, the rest on the MUFU unit
+            float p0, p1;
+            if ((e & 3) == 3) {
+              f2_unpack(exp2_poly2(y0, y1), p0, p1);
+            } else {
+              p0 = fast_exp2(y0);
+              p1 = fast_exp2(y1);
+            }
             lsv = fadd2(lsv, f2_pack(p0, p1));
             pk[e] = pack2(p0, p1, (T*)nullptr);
             pmx = hmax2u(pmx, pk[e], (T*)nullptr);
@@ -602,6 +636,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full + sb);
         ++it;
+        kt0 = kt_next;
+        sel = sel_next;
+        b2 = b2_next;
       }
       // ---- epilogue ----
       float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
