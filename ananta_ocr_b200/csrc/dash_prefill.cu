@@ -27,6 +27,7 @@
 // sparse_gather_triton.py:29-104 (_gather_attn_fwd_kernel, seg/packing),
 // WHL attend_triton.py:88-292 (_dash_sparse_fwd_kernel, paged).
 #include <cudaTypedefs.h>
+#include <climits>
 #include "dash_common.cuh"
 #include "dash_internal.h"
 
@@ -77,20 +78,6 @@ struct PrefillPlan {
   int32_t nblk_cap;
 };
 
-__device__ __forceinline__ void seq_of_row(const DashSeqs& q, int64_t r, int& s, int& i) {
-  if (q.q_start == nullptr) {
-    s = (int)(r / q.q_len_fixed);
-    i = (int)(r - (int64_t)s * q.q_len_fixed);
-    return;
-  }
-  int lo = 0, hi = q.n_seq - 1;
-  while (lo < hi) {
-    int mid = (lo + hi + 1) >> 1;
-    if (q.q_start[mid] <= r) lo = mid; else hi = mid - 1;
-  }
-  s = lo;
-  i = (int)(r - q.q_start[lo]);
-}
 __device__ __forceinline__ int kv_len_of(const DashSeqs& q, int s) {
   return q.kv_len ? q.kv_len[s] : q.kv_len_fixed;
 }
@@ -105,70 +92,113 @@ __device__ __forceinline__ int64_t row_base(const DashSeqs& q, int s) {
 }
 
 // ---------------------------------------------------------------------------
-// plan_kernel: one warp per (query row, index head).  Canonicalises the routed
-// list (drops -1, ids without a remote key for this row, later duplicates;
-// sorts ascending) and ORs the kept ids into the row's tile union.
+// plan_kernel: one CTA per (query tile, index head), one warp per token row
+// (strided).  Canonicalises each row's routed list (drops -1, ids without a
+// remote key for the row, later duplicates; ascending order), records the
+// row's largest kept bias, and builds the tile's block union in shared memory;
+// the union words are written once, so no global atomics and no pre-zeroing.
+// Slot j of a row lives in lane j % 32, register j / 32 (PER registers);
+// duplicate and rank tests run over warp shuffles.  The next row's slots are
+// loaded before the current row is processed.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(128) plan_kernel(DashPrefillArgs a, PrefillPlan p,
-                                                   int32_t* cidx, float* cbias,
-                                                   uint32_t* tmask, float* rowmax) {
+constexpr int kPlanWarps = 16;
+
+template <int PER>
+__global__ void __launch_bounds__(kPlanWarps * 32) plan_kernel(DashPrefillArgs a, PrefillPlan p,
+                                                               int32_t* cidx, float* cbias,
+                                                               uint32_t* tmask, float* rowmax) {
+  __shared__ uint32_t s_mask[MAX_MASK_WORDS];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t r = (int64_t)blockIdx.x * 4 + warp;
-  const int ih = blockIdx.y;
-  if (r >= p.n_rows) return;
-  int s, i;
-  seq_of_row(a.seqs, r, s, i);
+  const int tile = blockIdx.x, ih = blockIdx.y;
+  const int s = tile / p.tiles_per_seq, t = tile - s * p.tiles_per_seq;
+  for (int w = threadIdx.x; w < p.nwords; w += kPlanWarps * 32) s_mask[w] = 0u;
+  __syncthreads();
+  const int qlen = q_len_of(a.seqs, s);
+  const int i_end = min(qlen, (t + 1) * p.TT);
   const int kvl = kv_len_of(a.seqs, s);
-  const int64_t pos = (int64_t)pos0_of(a.seqs, s) + i;
-  const int64_t lstart = pos - a.local_window + 1;
+  const int pos0 = pos0_of(a.seqs, s);
   const int nblk_seq = (kvl + a.block_size - 1) / a.block_size;
   const int K = a.routes.K;
-  const int32_t* il = a.routes.idx + r * a.routes.row_stride + (int64_t)ih * a.routes.ihead_stride;
-  const float* bl = a.routes.bias ? a.routes.bias + r * a.routes.row_stride +
-                                        (int64_t)ih * a.routes.ihead_stride
-                                  : nullptr;
-  int32_t* oi = cidx + ((int64_t)ih * p.n_rows + r) * K;
-  float* ob = cbias + ((int64_t)ih * p.n_rows + r) * K;
-  const int tile = s * p.tiles_per_seq + i / p.TT;
-  uint32_t* tm = tmask + ((int64_t)ih * a.seqs.n_seq * p.tiles_per_seq + tile) * p.nwords;
-  __shared__ int32_t s_id[4][kPlanMaxK];   // kept id per slot, -1 when dropped
-  int32_t* sid = s_id[warp];
-  // pass 1: keep ids with a remote key for this row, drop later duplicates
-  for (int j = lane; j < K; j += 32) sid[j] = il[j];
-  __syncwarp();
-  for (int j = lane; j < K; j += 32) {
-    const int b = sid[j];
-    bool ok = b >= 0 && b < nblk_seq && b < p.nblk_cap && (int64_t)b * a.block_size < lstart;
-    if (b >= nblk_seq) record_error(a.device_error, DASH_DEV_BAD_BLOCK, 30, b);
-    if (ok)
-      for (int u = 0; u < j; ++u) ok &= sid[u] != b;
-    // Dropped slots become a distinct negative marker.  Validity depends only
-    // on the id, so a later duplicate of a dropped id is dropped by the same
-    // test, and a kept id is never rewritten: concurrent reads stay exact.
-    if (!ok) sid[j] = -1 - j;
-  }
-  __syncwarp();
-  // pass 2: rank the kept ids (distinct) and write the ascending list
-  int nk = 0;
-  float bmax = -INFINITY;
-  for (int j0 = 0; j0 < K; j0 += 32) {
-    const int j = j0 + lane;
-    const int b = j < K ? sid[j] : -1;
-    const bool ok = b >= 0;
-    int rank = 0;
-    if (ok)
-      for (int u = 0; u < K; ++u) rank += sid[u] >= 0 && sid[u] < b;
-    if (ok) {
-      oi[rank] = b;
-      ob[rank] = bl ? bl[j] : 0.0f;
-      atomicOr(tm + (b >> 5), 1u << (b & 31));
+  const int64_t rb = row_base(a.seqs, s);
+  auto load_row = [&](int i, int (&b)[PER], float (&bias)[PER]) {
+    const int64_t r = rb + i;
+    const int32_t* il = a.routes.idx + r * a.routes.row_stride + (int64_t)ih * a.routes.ihead_stride;
+    const float* bl = a.routes.bias ? a.routes.bias + r * a.routes.row_stride +
+                                          (int64_t)ih * a.routes.ihead_stride
+                                    : nullptr;
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      const int j = lane + 32 * q;
+      b[q] = j < K ? il[j] : -1;
+      bias[q] = (j < K && bl) ? bl[j] : 0.0f;
     }
-    nk += __popc(__ballot_sync(0xffffffffu, ok));
-    bmax = fmaxf(bmax, (ok && bl) ? bl[j] : -INFINITY);
+  };
+  int b_nx[PER];
+  float bias_nx[PER];
+  int i = t * p.TT + warp;
+  if (i < i_end) load_row(i, b_nx, bias_nx);
+  for (; i < i_end; i += kPlanWarps) {
+    int b[PER];
+    float bias[PER];
+#pragma unroll
+    for (int q = 0; q < PER; ++q) { b[q] = b_nx[q]; bias[q] = bias_nx[q]; }
+    if (i + kPlanWarps < i_end) load_row(i + kPlanWarps, b_nx, bias_nx);
+    const int64_t r = rb + i;
+    const int lstart = pos0 + i - a.local_window + 1;
+    // keep ids with a remote key for this row; drop later duplicates (the
+    // validity test depends only on the id, so a duplicate of a dropped id is
+    // dropped by the same test)
+    bool keep[PER];
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      const int bb = b[q];
+      keep[q] = bb >= 0 && bb < nblk_seq && bb < p.nblk_cap && (int64_t)bb * a.block_size < lstart;
+      if (bb >= nblk_seq) record_error(a.device_error, DASH_DEV_BAD_BLOCK, 30, bb);
+    }
+#pragma unroll
+    for (int qs = 0; qs < PER; ++qs) {
+      for (int src = 0; src < 32; ++src) {
+        const int bu = __shfl_sync(0xffffffffu, b[qs], src);
+        const int u = src + 32 * qs;
+#pragma unroll
+        for (int q = 0; q < PER; ++q)
+          if (u < lane + 32 * q && bu == b[q]) keep[q] = false;
+      }
+    }
+    // rank of each kept id among the kept ids (distinct): ascending position
+    int rank[PER];
+#pragma unroll
+    for (int q = 0; q < PER; ++q) rank[q] = 0;
+#pragma unroll
+    for (int qs = 0; qs < PER; ++qs) {
+      const int key = keep[qs] ? b[qs] : INT_MAX;
+      for (int src = 0; src < 32; ++src) {
+        const int ku = __shfl_sync(0xffffffffu, key, src);
+#pragma unroll
+        for (int q = 0; q < PER; ++q) rank[q] += ku < b[q] ? 1 : 0;
+      }
+    }
+    int32_t* oi = cidx + ((int64_t)ih * p.n_rows + r) * K;
+    float* ob = cbias + ((int64_t)ih * p.n_rows + r) * K;
+    int nk = 0;
+    float bmax = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      if (keep[q]) {
+        oi[rank[q]] = b[q];
+        ob[rank[q]] = bias[q];
+        atomicOr(s_mask + (b[q] >> 5), 1u << (b[q] & 31));
+        if (a.routes.bias) bmax = fmaxf(bmax, bias[q]);
+      }
+      nk += __popc(__ballot_sync(0xffffffffu, keep[q]));
+    }
+    for (int j = nk + lane; j < K; j += 32) { oi[j] = -1; ob[j] = 0.0f; }
+    for (int o = 16; o > 0; o >>= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
+    if (lane == 0) rowmax[(int64_t)ih * p.n_rows + r] = bmax;
   }
-  for (int j = nk + lane; j < K; j += 32) { oi[j] = -1; ob[j] = 0.0f; }
-  for (int o = 16; o > 0; o >>= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
-  if (lane == 0) rowmax[(int64_t)ih * p.n_rows + r] = bmax;
+  __syncthreads();
+  uint32_t* tm = tmask + ((int64_t)ih * a.seqs.n_seq * p.tiles_per_seq + tile) * p.nwords;
+  for (int w = threadIdx.x; w < p.nwords; w += kPlanWarps * 32) tm[w] = s_mask[w];
 }
 
 // ---------------------------------------------------------------------------
@@ -760,16 +790,18 @@ int launch_prefill(const DashPrefillArgs& a, int64_t n_rows, cudaStream_t st) {
   float* cbias = reinterpret_cast<float*>(ws + lists);
   uint32_t* tmask = reinterpret_cast<uint32_t*>(ws + 2 * lists);
   size_t masks = (size_t)nih * a.seqs.n_seq * p.tiles_per_seq * p.nwords * 4;
-  cudaError_t e = cudaMemsetAsync(tmask, 0, masks, st);
-  if (e != cudaSuccess) return set_error(DASH_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
   p.cidx = cidx;
   p.cbias = cbias;
   p.tmask = tmask;
   float* rowmax = reinterpret_cast<float*>(ws + 2 * lists + ((masks + 255) & ~(size_t)255));
   p.rowmax = rowmax;
-  if (a.routes.K > 0) {
-    dim3 g1((unsigned)((n_rows + 3) / 4), nih);
-    plan_kernel<<<g1, 128, 0, st>>>(a, p, cidx, cbias, tmask, rowmax);
+  {
+    // every tile's union words are written (also with no routed lists)
+    dim3 g1((unsigned)(a.seqs.n_seq * p.tiles_per_seq), nih);
+    const int K = a.routes.K;
+    if (K <= 32) plan_kernel<1><<<g1, kPlanWarps * 32, 0, st>>>(a, p, cidx, cbias, tmask, rowmax);
+    else if (K <= 64) plan_kernel<2><<<g1, kPlanWarps * 32, 0, st>>>(a, p, cidx, cbias, tmask, rowmax);
+    else plan_kernel<kPlanMaxK / 32><<<g1, kPlanWarps * 32, 0, st>>>(a, p, cidx, cbias, tmask, rowmax);
     count_launch();
     int rc = check_launch("plan_kernel");
     if (rc) return rc;

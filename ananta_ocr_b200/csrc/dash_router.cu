@@ -18,11 +18,14 @@ constexpr float kEntmaxNeg = -1.0e4f;
 // ---------------------------------------------------------------------------
 // k-bar pooling: one CTA per block (contiguous) or plan entry (paged).
 // Restates dash_attention.py:863-888 / route_triton.py:36-72.
+// DC > 0 fixes the index dim at compile time (loops unroll, shared-memory
+// operands are fetched ahead of the fixed-order FMA chains); VEC stages the
+// keys with 16-byte loads.  The arithmetic order is the same in every form.
 // ---------------------------------------------------------------------------
-template <typename KT>
+template <typename KT, int DC, bool VEC>
 __global__ void __launch_bounds__(128) kbar_pool_kernel(DashKbarArgs a) {
   extern __shared__ float sm[];
-  const int d = a.d;
+  const int d = DC > 0 ? DC : a.d;
   const int ld = d + 1;                       // padded row, conflict-free column reads
   float* sk = sm;                             // [bs][d+1]
   float* shc = sk + a.block_size * ld;        // [d]
@@ -46,12 +49,26 @@ __global__ void __launch_bounds__(128) kbar_pool_kernel(DashKbarArgs a) {
     base = a.pages[i] * a.page_stride;
     out_row = a.pages[i];
   }
-  // Stage the block's keys; non-coherent loads, eight in flight per thread
-  // (the loads do not wait on the shared-memory stores between them).
+  if constexpr (VEC) {
+    // 16-byte vectors of W elements; every load of a thread is issued before
+    // its first shared-memory store
+    constexpr int W = 16 / (int)sizeof(KT);
+    const int dv = d / W;
+    const int tot = n * dv;
+#pragma unroll 16
+    for (int e = threadIdx.x; e < tot; e += 128) {
+      const int j = e / dv, cv = e - j * dv;
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(keys + base + (int64_t)j * a.tok_stride) + cv);
+      const KT* v = reinterpret_cast<const KT*>(&raw);
+#pragma unroll
+      for (int k = 0; k < W; ++k) sk[j * ld + cv * W + k] = (float)v[k];
+    }
+  } else {
 #pragma unroll 8
-  for (int e = threadIdx.x; e < n * d; e += blockDim.x) {
-    int j = e / d, c = e - j * d;
-    sk[j * ld + c] = (float)__ldg(keys + base + (int64_t)j * a.tok_stride + c);
+    for (int e = threadIdx.x; e < n * d; e += 128) {
+      int j = e / d, c = e - j * d;
+      sk[j * ld + c] = (float)__ldg(keys + base + (int64_t)j * a.tok_stride + c);
+    }
   }
   for (int c = threadIdx.x; c < d; c += blockDim.x) shc[c] = a.head_cls ? a.head_cls[c] : 0.0f;
   __syncthreads();
@@ -59,6 +76,7 @@ __global__ void __launch_bounds__(128) kbar_pool_kernel(DashKbarArgs a) {
   float lmax = -INFINITY;
   for (int j = threadIdx.x; j < n; j += blockDim.x) {
     float acc = 0.0f;
+#pragma unroll 16
     for (int c = 0; c < d; ++c) acc = __fmaf_rn(sk[j * ld + c], shc[c], acc);
     float aw = clamp_act(__fmul_rn(acc, inv_sqrt_d));
     se[j] = aw;
@@ -73,6 +91,7 @@ __global__ void __launch_bounds__(128) kbar_pool_kernel(DashKbarArgs a) {
   __syncthreads();
   if (threadIdx.x == 0) {
     float sum = 0.0f;
+#pragma unroll 16
     for (int j = 0; j < n; ++j) sum = __fadd_rn(sum, se[j]);
     sred[0] = sum > 1e-6f ? sum : 1e-6f;
   }
@@ -82,6 +101,7 @@ __global__ void __launch_bounds__(128) kbar_pool_kernel(DashKbarArgs a) {
   __syncthreads();
   for (int c = threadIdx.x; c < d; c += blockDim.x) {
     float acc = 0.0f;
+#pragma unroll 16
     for (int j = 0; j < n; ++j) acc = __fmaf_rn(se[j], sk[j * ld + c], acc);
     if (!(acc == acc) || isinf(acc)) acc = 0.0f;
     a.kbar[out_row * a.kbar_row_stride + c] = acc;
@@ -686,16 +706,24 @@ int launch_kbar(const DashKbarArgs& a, cudaStream_t st) {
   }
   if (grid.x == 0 || grid.y == 0) return DASH_OK;
   size_t smem = sizeof(float) * ((size_t)a.block_size * (a.d + 1) + a.d + a.block_size + 4);
+  // 16-byte staging needs every row start 16-byte aligned
+  const int w = a.dtype == DASH_DTYPE_F32 ? 4 : 8;
+  const bool vec = (reinterpret_cast<uintptr_t>(a.keys) & 15) == 0 && a.d % w == 0 &&
+                   a.tok_stride % w == 0 &&
+                   (a.pages == nullptr ? a.seq_stride % w == 0 : a.page_stride % w == 0);
+  auto go = [&](auto kern) {
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<grid, 128, smem, st>>>(a);
+  };
   if (a.dtype == DASH_DTYPE_F32) {
-    if (smem > 48 * 1024)
-      cudaFuncSetAttribute(kbar_pool_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem);
-    kbar_pool_kernel<float><<<grid, 128, smem, st>>>(a);
+    if (a.d == 128 && vec) go(kbar_pool_kernel<float, 128, true>);
+    else if (vec) go(kbar_pool_kernel<float, 0, true>);
+    else go(kbar_pool_kernel<float, 0, false>);
   } else {
-    if (smem > 48 * 1024)
-      cudaFuncSetAttribute(kbar_pool_kernel<__nv_bfloat16>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kbar_pool_kernel<__nv_bfloat16><<<grid, 128, smem, st>>>(a);
+    if (a.d == 128 && vec) go(kbar_pool_kernel<__nv_bfloat16, 128, true>);
+    else if (vec) go(kbar_pool_kernel<__nv_bfloat16, 0, true>);
+    else go(kbar_pool_kernel<__nv_bfloat16, 0, false>);
   }
   count_launch();
   return check_launch("kbar_pool_kernel");
