@@ -562,7 +562,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // none kept.  When every row of the warp is pure and the tile lies inside
         // the sequence (tiles away from the window edge and the diagonal), the
         // logits take one packed FFMA per 2 columns (an empty row adds -inf), P is
-        // produced directly, and the rescale test runs on the packed P maximum.
+        // produced directly, and the rescale test runs on the row's partial sums.
         const bool empty = lo > hi;
         const bool full = lo == 0 && hi == 63 && (lo_loc == 0 || lo_loc == 64);
         bool done = false;
@@ -570,7 +570,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const float add = empty ? -INFINITY : (lo_loc == 0 ? add_loc : add_rem);
           const uint64_t sl2v = f2_pack(sl2, sl2), addv = f2_pack(add, add);
           uint64_t lsv = f2_pack(0.0f, 0.0f);
-          uint32_t pmx = 0;                          // packed +0.0 pair
   #pragma unroll
           for (int e = 0; e < 32; ++e) {
             float y0, y1;
@@ -585,13 +584,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             lsv = fadd2(lsv, f2_pack(p0, p1));
             pk[e] = pack2(p0, p1, (T*)nullptr);
-            pmx = hmax2u(pmx, pk[e], (T*)nullptr);
           }
-          const float2 pm = unpack2(pmx, (T*)nullptr);
-          const bool big = !(fmaxf(pm.x, pm.y) <= kGrowP);   // p > 2^kGrowLog2 (or inf/NaN)
+          // every p <= 2^kGrowLog2 when both partial sums are (sums of
+          // non-negative terms; inf / NaN fail the test too)
+          float l0, l1;
+          f2_unpack(lsv, l0, l1);
+          const bool big = !(fmaxf(l0, l1) <= kGrowP);
           if (!__any_sync(0xffffffffu, big)) {
-            float l0, l1;
-            f2_unpack(lsv, l0, l1);
             l_run += l0 + l1;
             done = true;
           }
