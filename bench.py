@@ -579,7 +579,7 @@ def main():
                                        "peak_source": f"{peak_kind} hbm_gbs"}}
     if e2e is not None:
         line["e2e"] = e2e
-    if not args.no_cpu:
+    if not args.no_cpu and world == 1:   # the CPU baseline is timed at N = 1 only
         line["cpu_baseline"] = cpu_baseline(cfg, n_tokens=256)
         line["cpu_baseline"].pop("seconds", None)
     print(json.dumps(line))
