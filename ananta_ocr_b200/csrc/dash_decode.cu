@@ -91,6 +91,20 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_kernel(DashDecodeArgs a
   const int64_t lstart = pos - a.local_window + 1 > 0 ? pos - a.local_window + 1 : 0;
   const int nblk_seq = (kvl + bs - 1) / bs;
 
+  // ---- query (pre-scaled into the exp2 domain); loaded by every warp while
+  // warp 0 builds the work list ----
+  const int grp = lane >> 2, sub = lane & 3;
+  const float sl2 = a.scale * 1.4426950408889634f;
+  float q[32];
+  {
+    const T* qp = reinterpret_cast<const T*>(a.qo.q) +
+                  (a.seqs.q_start ? (int64_t)(a.seqs.q_start[s] + i) * a.qo.q_stride_tok
+                                  : (int64_t)s * a.qo.q_stride_seq + (int64_t)i * a.qo.q_stride_tok) +
+                  (int64_t)hq * a.qo.q_stride_head + sub * 32;
+    load_row32(qp, q);
+#pragma unroll
+    for (int c = 0; c < 32; ++c) q[c] *= sl2;
+  }
   // ---- build the work list (warp 0, one routed slot per lane) ----
   if (warp == 0) {
     const int nih = a.routes.n_index_heads > 0 ? a.routes.n_index_heads : 1;
@@ -105,6 +119,7 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_kernel(DashDecodeArgs a
       bool ok = b >= 0;
       if (ok && b >= nblk_seq) { record_error(a.device_error, DASH_DEV_BAD_BLOCK, 21, b); ok = false; }
       if (ok) {                                   // first occurrence of a duplicated id wins
+#pragma unroll 8
         for (int u = 0; u < j; ++u) ok &= il[u] != b;
       }
       int64_t k0 = (int64_t)b * bs;
@@ -170,19 +185,6 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_kernel(DashDecodeArgs a
   const int per = (n_items + splits - 1) / splits;
   const int it0 = split * per, it1 = min(n_items, it0 + per);
 
-  // ---- query (pre-scaled into the exp2 domain) ----
-  const int grp = lane >> 2, sub = lane & 3;
-  const float sl2 = a.scale * 1.4426950408889634f;
-  float q[32];
-  {
-    const T* qp = reinterpret_cast<const T*>(a.qo.q) +
-                  (a.seqs.q_start ? (int64_t)(a.seqs.q_start[s] + i) * a.qo.q_stride_tok
-                                  : (int64_t)s * a.qo.q_stride_seq + (int64_t)i * a.qo.q_stride_tok) +
-                  (int64_t)hq * a.qo.q_stride_head + sub * 32;
-    load_row32(qp, q);
-#pragma unroll
-    for (int c = 0; c < 32; ++c) q[c] *= sl2;
-  }
   float m = -INFINITY, l = 0.0f, o[32];
 #pragma unroll
   for (int c = 0; c < 32; ++c) o[c] = 0.0f;
@@ -295,16 +297,36 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_kernel(DashDecodeArgs a
   if (threadIdx.x == 0) counters[unit] = 0;
 }
 
+// CTA slots of the whole GPU for decode_kernel (resident CTAs per SM x SMs).
+static int decode_slots() {
+  static int slots[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148 * 4;
+  if (slots[dev] == 0) {
+    int sms = 0, per = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, decode_kernel<__nv_bfloat16>, kDecWarps * 32, 0);
+    slots[dev] = (sms > 0 && per > 0) ? sms * per : 148 * 4;
+  }
+  return slots[dev];
+}
+
+// Split count minimising (waves of CTAs) x (per-CTA work): a row's work is its
+// routed blocks plus window blocks; every CTA also pays a fixed prologue
+// (work list, query) worth about 1.5 blocks.  Waves are counted whole, so the
+// choice avoids a nearly empty last wave.
 int decode_auto_splits(const DashDecodeArgs& a, int64_t n_rows) {
-  // aim for >= ~4 CTAs per SM in flight; at most K+window blocks per split of 1
-  int64_t units = n_rows * a.qo.n_heads;
-  int items = a.routes.K + a.local_window / a.block_size + 1;
-  int target = 148 * 8;
-  int sp = (int)((target + units - 1) / units);
-  if (sp < 1) sp = 1;
-  if (sp > items) sp = items;
-  if (sp > 16) sp = 16;
-  return sp;
+  const int64_t units = n_rows * a.qo.n_heads;
+  const int items = a.routes.K + a.local_window / a.block_size + 1;
+  const int64_t slots = decode_slots();
+  int best = 1;
+  double best_cost = 1e300;
+  for (int sp = 1; sp <= 16 && sp <= items; ++sp) {
+    const double waves = (double)((units * sp + slots - 1) / slots);
+    const double cost = waves * ((double)items / sp + 1.5);
+    if (cost < best_cost * 0.999) { best_cost = cost; best = sp; }
+  }
+  return best;
 }
 
 size_t decode_workspace(const DashDecodeArgs& a, int64_t n_rows, int splits) {
