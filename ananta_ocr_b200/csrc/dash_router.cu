@@ -250,7 +250,7 @@ __device__ __forceinline__ uint32_t radix_threshold_smem(const float* sx, int W,
 //
 // Per-warp scratch: mid_ (block id by slot; slots ascend by id), mx (x by
 // slot, then z by rank, then log-prior by rank), mval (valid flag by rank).
-template <int KW>
+template <int KW, int PER>
 __device__ __noinline__ void select_row(const DashRouteArgs& a, float* sx, uint32_t* scand,
                                         int* mid_, float* mx, int* mval, int64_t r, int s,
                                         int lane) {
@@ -350,8 +350,7 @@ __device__ __noinline__ void select_row(const DashRouteArgs& a, float* sx, uint3
   __syncwarp();
   M = n_items;  // == M
 
-  // ---- rank of slot t = lane + 32u by (x desc, id asc) ----
-  constexpr int PER = kMaxM / 32;
+  // ---- rank of slot t = lane + 32u by (x desc, id asc); PER >= ceil(M / 32) ----
   const int nper = (M + 31) >> 5;
   float xt[PER];
   int rk[PER];
@@ -361,6 +360,7 @@ __device__ __noinline__ void select_row(const DashRouteArgs& a, float* sx, uint3
     xt[u] = (u < nper && t < M) ? mx[t] : -INFINITY;
     rk[u] = 0;
   }
+#pragma unroll 8
   for (int v = 0; v < M; ++v) {
     const float xv = mx[v];
 #pragma unroll
@@ -398,10 +398,11 @@ __device__ __noinline__ void select_row(const DashRouteArgs& a, float* sx, uint3
       const int k = lane + 32 * u;
       // add z_j for j = previous k + 1 .. k in ascending order (u = 0: 0 .. k)
       const int jstart = u == 0 ? 32 - min(M, 32) : 0;
+#pragma unroll 8
       for (int jj = jstart; jj < 32; ++jj) {
         const int j = k - 31 + jj;
+        const float zj = mx[max(j, 0)];
         if (j >= 0) {
-          const float zj = mx[j];
           cs = __fadd_rn(cs, zj);
           cs2 = __fadd_rn(cs2, __fmul_rn(zj, zj));
         }
@@ -438,6 +439,7 @@ __device__ __noinline__ void select_row(const DashRouteArgs& a, float* sx, uint3
   __syncwarp();
   float lsum = 0.0f;
   int cnt = 0;
+#pragma unroll 8
   for (int k = 0; k < Kc; ++k)
     if (mval[k]) {
       lsum = __fadd_rn(lsum, mx[k]);
@@ -470,15 +472,26 @@ __device__ __noinline__ void select_row(const DashRouteArgs& a, float* sx, uint3
   if (a.out_count && lane == 0) a.out_count[r] = min(npos, a.out_width);
 }
 
+template <int KW>
+__device__ __forceinline__ void select_row_m(const DashRouteArgs& a, float* sx, uint32_t* scand,
+                                             int* mid_, float* mx, int* mval, int64_t r, int s,
+                                             int lane) {
+  const int W = a.width;
+  const int M = a.topm > 0 ? min(a.topm, W) : W;
+  if (M <= 32) select_row<KW, 1>(a, sx, scand, mid_, mx, mval, r, s, lane);
+  else if (M <= 64) select_row<KW, 2>(a, sx, scand, mid_, mx, mval, r, s, lane);
+  else select_row<KW, kMaxM / 32>(a, sx, scand, mid_, mx, mval, r, s, lane);
+}
+
 __device__ __forceinline__ void select_row_any(const DashRouteArgs& a, float* sx,
                                                uint32_t* scand, int* mid_, float* mx, int* mval,
                                                int64_t r, int s, int lane) {
   const int W = a.width;
-  if (W <= 160) select_row<5>(a, sx, scand, mid_, mx, mval, r, s, lane);
-  else if (W <= 256) select_row<8>(a, sx, scand, mid_, mx, mval, r, s, lane);
-  else if (W <= 512) select_row<16>(a, sx, scand, mid_, mx, mval, r, s, lane);
-  else if (W <= 1024) select_row<32>(a, sx, scand, mid_, mx, mval, r, s, lane);
-  else select_row<0>(a, sx, scand, mid_, mx, mval, r, s, lane);
+  if (W <= 160) select_row_m<5>(a, sx, scand, mid_, mx, mval, r, s, lane);
+  else if (W <= 256) select_row_m<8>(a, sx, scand, mid_, mx, mval, r, s, lane);
+  else if (W <= 512) select_row_m<16>(a, sx, scand, mid_, mx, mval, r, s, lane);
+  else if (W <= 1024) select_row_m<32>(a, sx, scand, mid_, mx, mval, r, s, lane);
+  else select_row_m<0>(a, sx, scand, mid_, mx, mval, r, s, lane);
 }
 
 // ---------------------------------------------------------------------------
