@@ -267,12 +267,15 @@ _WS = {}
 
 
 def _workspace(device, nbytes, key):
-    """Grow-only workspace cache per (device, key); callers that must not
-    allocate pass their own buffer instead."""
-    buf = _WS.get((device, key))
+    """Grow-only workspace cache per (device, current stream, key): kernels on
+    different streams may run at the same time, so each stream has its own
+    scratch (a buffer is only ever reused in its stream's order).  Callers that
+    must not allocate pass their own buffer instead."""
+    sid = torch.cuda.current_stream(device).cuda_stream
+    buf = _WS.get((device, sid, key))
     if buf is None or buf.numel() < nbytes:
         buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
-        _WS[(device, key)] = buf
+        _WS[(device, sid, key)] = buf
     return buf
 
 
