@@ -7,10 +7,13 @@
 // feature index and every other rounding step is spelled out, in the same
 // order as oracle/dash_oracle.c, so k-bar, block scores and the selected block
 // lists are bitwise equal to the CPU oracle.
+#include <cooperative_groups.h>
 #include "dash_common.cuh"
 #include "dash_internal.h"
 
 namespace dash {
+
+namespace cg = cooperative_groups;
 
 constexpr float kScoreNeg = -1.0e9f;
 constexpr float kEntmaxNeg = -1.0e4f;
@@ -651,6 +654,98 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_rows_kernel(DashRouteA
 }
 
 // ---------------------------------------------------------------------------
+// Few rows (decode): a cluster of kClusterCtas CTAs per row.  CTA c scores a
+// contiguous slice of the row's blocks, one thread per block (its k-bar row is
+// loaded whole, then the same sequential FMA chain as score_blocks, so scores
+// are bitwise those of the other kernels); CTA 0 gathers the slices through
+// distributed shared memory and selects.  Every CTA reaches both cluster
+// barriers (no early exit).
+// ---------------------------------------------------------------------------
+constexpr int kClusterCtas = 8;
+
+__host__ __device__ inline int cluster_slice(int W) { return (W + kClusterCtas - 1) / kClusterCtas; }
+__host__ __device__ inline size_t route_cluster_smem_floats(int W) {
+  const int Wp = (W + 31) & ~31;
+  const int per = (cluster_slice(W) + 31) & ~31;
+  return (size_t)128 + per + Wp + Wp / 32 + 3 * kMaxM;
+}
+
+__global__ void __launch_bounds__(128) route_cluster_kernel(DashRouteArgs a) {
+  extern __shared__ __align__(16) float smc[];
+  cg::cluster_group cl = cg::this_cluster();
+  const int rank = (int)cl.block_rank();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int W = a.width;
+  const int Wp = (W + 31) & ~31;
+  const int per = cluster_slice(W);
+  float* sq = smc;                                   // [128] router query
+  float* ssc = sq + 128;                             // [per] this CTA's slice of scores
+  float* sx = ssc + ((per + 31) & ~31);              // CTA 0: the row's W scores
+  uint32_t* scand = reinterpret_cast<uint32_t*>(sx + Wp);
+  int* mid_ = reinterpret_cast<int*>(scand + Wp / 32);
+  float* mx = reinterpret_cast<float*>(mid_ + kMaxM);
+  int* mval = reinterpret_cast<int*>(mx + kMaxM);
+
+  const int64_t r = (int64_t)(blockIdx.x / kClusterCtas);
+  int s, i;
+  row_to_seq(a.seqs, r, s, i);
+  const int64_t pos = seq_pos(a.seqs, s, i);
+  const int kvl = seq_kv_len(a.seqs, s);
+  const int64_t qblk = pos >= 0 ? pos / a.block_size : -1;
+  sq[threadIdx.x] = a.idx_q[r * a.q_row_stride + threadIdx.x];
+  __syncthreads();
+  const float inv_sqrt_d = (float)(1.0 / sqrt((double)a.d));
+  const float4* sq4 = reinterpret_cast<const float4*>(sq);
+  for (int t = threadIdx.x; t < per; t += 128) {
+    const int b = rank * per + t;
+    float sc = kScoreNeg;
+    bool live = b < W && (int64_t)b <= qblk - a.local_blocks && (int64_t)b * a.block_size < kvl;
+    int64_t kr = 0;
+    if (live) {
+      kr = a.block_table ? (int64_t)a.block_table[(int64_t)s * a.bt_stride + b]
+                         : (int64_t)s * a.kbar_seq_rows + b;
+      if (kr < 0 || kr >= a.num_kbar_rows) {
+        record_error(a.device_error, DASH_DEV_BAD_PAGE, 12, kr);
+        live = false;
+      }
+    }
+    if (live) {
+      const float4* kb = reinterpret_cast<const float4*>(a.kbar + kr * a.kbar_row_stride);
+      float4 kv[32];
+#pragma unroll
+      for (int c4 = 0; c4 < 32; ++c4) kv[c4] = __ldg(kb + c4);
+      float acc = 0.0f;
+#pragma unroll
+      for (int c4 = 0; c4 < 32; ++c4) {
+        const float4 q4 = sq4[c4];
+        acc = __fmaf_rn(q4.x, kv[c4].x, acc);
+        acc = __fmaf_rn(q4.y, kv[c4].y, acc);
+        acc = __fmaf_rn(q4.z, kv[c4].z, acc);
+        acc = __fmaf_rn(q4.w, kv[c4].w, acc);
+      }
+      sc = clamp_act(__fmul_rn(acc, inv_sqrt_d));
+    }
+    ssc[t] = sc;
+  }
+  cl.sync();                                  // every slice written
+  if (rank == 0) {
+    for (int b = threadIdx.x; b < W; b += 128) {
+      const int src = b / per;
+      const float* remote = cl.map_shared_rank(ssc, src);
+      sx[b] = remote[b - src * per];
+    }
+    __syncthreads();
+    if (warp == 0) {
+      if (a.scores_out)
+        for (int b = lane; b < W; b += 32) a.scores_out[r * a.scores_out_stride + b] = sx[b];
+      __syncwarp();
+      select_row_any(a, sx, scand, mid_, mx, mval, r, s, lane);
+    }
+  }
+  cl.sync();                                  // slices stay alive until CTA 0 has read them
+}
+
+// ---------------------------------------------------------------------------
 // Indexer stage-0: block max of token scores over remote keys.
 // One CTA per (32 query rows, key block, batch); thread (row, key lane).
 // ---------------------------------------------------------------------------
@@ -755,7 +850,29 @@ int launch_route(const DashRouteArgs& a, int64_t n_rows, cudaStream_t st) {
     count_launch();
     return check_launch("route_tile_kernel");
   }
-  // few rows (decode): one CTA per row so all its threads score; else warp per row
+  // few rows (decode): a cluster of CTAs per row scores the blocks in parallel
+  if (!a.scores_in && a.d == 128 && n_rows < 148 * 16) {
+    const size_t smem = sizeof(float) * route_cluster_smem_floats(a.width);
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(route_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(n_rows * kClusterCtas));
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kClusterCtas;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, route_cluster_kernel, a);
+    if (e != cudaSuccess) return set_error(DASH_ERR_CUDA, "route_cluster_kernel launch: %s", cudaGetErrorString(e));
+    count_launch();
+    return check_launch("route_cluster_kernel");
+  }
+  // few rows otherwise: one CTA per row so all its threads score; else warp per row
   const bool cta_row = n_rows < 148 * 16;
   size_t smem = per_warp * (cta_row ? 1 : kRouteWarps);
   if (cta_row) {

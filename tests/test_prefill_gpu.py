@@ -209,3 +209,39 @@ def test_prefill_config2_full_size_sampled_rows():
     ref = O.attend_contig(bf16_round(q), bf16_round(k), bf16_round(v), gi, bias.cpu().numpy(),
                           bs, lb * bs, 1.0 / math.sqrt(D), rows=rows)
     assert_close_bf16(out.float().cpu().numpy()[:, :, rows], ref)
+
+
+def test_two_streams_share_no_scratch():
+    """Two prefills issued on two streams at once (each library call takes
+    its cached scratch from its own stream) give exactly the single-stream
+    outputs."""
+    torch.manual_seed(5)
+    B, H, T, D, bs = 2, 2, 1500, 128, 64
+    ins = []
+    for _ in range(2):
+        q = (torch.randn(B, H, T, D, device="cuda") * 0.5).bfloat16()
+        k = (torch.randn(B, H, T, D, device="cuda") * 0.5).bfloat16()
+        v = (torch.randn(B, H, T, D, device="cuda") * 0.5).bfloat16()
+        iq = torch.randn(B, T, 128, device="cuda") * 0.5
+        ik = torch.randn(B, T, 128, device="cuda") * 0.5
+        ins.append((q, k, v, iq, ik))
+
+    def run(x):
+        return MD.dash_prefill_forward(*x, block_size=bs, local_blocks=4, K=4,
+                                       idx_scale=128.0 / math.sqrt(128), prior_floor=1e-4, sigma=1.0)
+
+    ref = [run(x) for x in ins]
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream() for _ in range(2)]
+    outs = [None, None]
+    for _ in range(3):
+        for s in streams:
+            s.wait_stream(torch.cuda.current_stream())
+        for j in range(2):
+            with torch.cuda.stream(streams[j]):
+                outs[j] = run(ins[j])
+        for s in streams:
+            torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        for j in range(2):
+            assert torch.equal(outs[j], ref[j])
