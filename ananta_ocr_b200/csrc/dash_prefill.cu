@@ -397,8 +397,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           if (kt0 < 0) break;
           const int st = it % NSTAGE, sb = it & 1;
           if (!mbar_wait(kv_full + st, (it / NSTAGE) & 1, abort_flag, derr, 52)) { alive = false; break; }
-          // S buffer sb holds P(it-2) until PV(it-2) has completed
-          if (it >= 2 && !mbar_wait(gb + 4 + sb, ((it - 2) >> 1) & 1, abort_flag, derr, 53)) { alive = false; break; }
+          // S buffer sb holds P(it-2), read by PV(it-2).  This thread issued
+          // PV(it-2) (after the softmax had released S(it-2)) before this QK,
+          // and tcgen05.mma ops of one thread execute in issue order, so the
+          // QK below cannot overwrite P before PV(it-2) has read it: no wait.
           tc_fence_after();
           const uint32_t sK = smem_u32(sm + OFF_K + st * 16384);
   #pragma unroll
