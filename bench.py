@@ -425,7 +425,19 @@ def main():
     dev = torch.device("cuda", local_rank)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        # NCCL may print a banner on stdout when its communicator is created;
+        # keep stdout for the one JSON line by sending it to stderr meanwhile
+        sys.stdout.flush()
+        saved_fd = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+            dist.barrier()
+            torch.cuda.synchronize()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved_fd, 1)
+            os.close(saved_fd)
     from ananta_ocr_b200 import _lib
     _lib.load()
 
@@ -490,6 +502,28 @@ def main():
         t_step, attn_ms = float(tt[0]), float(tt[1])
     tokens_per_rank = cfg["B"] * cfg["S"]
     value = tokens_per_rank * world / (t_step / 1e3)
+
+    # ---------------- the one collective: all-gather of the output shards -------------
+    # (outside the timed step, reported on its own; NCCL over NVLink)
+    gather = None
+    if world > 1:
+        shard = st["ws"]["out"]
+        full = torch.empty((world,) + tuple(shard.shape), dtype=shard.dtype, device=dev)
+        for _ in range(2):
+            dist.all_gather_into_tensor(full, shard)
+        torch.cuda.synchronize()
+        dist.barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        dist.all_gather_into_tensor(full, shard)
+        g1.record()
+        torch.cuda.synchronize()
+        gt = torch.tensor([g0.elapsed_time(g1)], device=dev, dtype=torch.float64)
+        dist.all_reduce(gt, op=dist.ReduceOp.MAX)
+        gbytes = full.numel() * full.element_size()
+        gather = {"ms": float(gt[0]), "bytes": gbytes, "bus_gbs": gbytes * (world - 1) / world / float(gt[0]) / 1e6,
+                  "op": "all_gather_into_tensor (NCCL)"}
+        del full
 
     # ---------------- e2e through the public API (pinned host buffers) -------------
     e2e = None
@@ -576,6 +610,7 @@ def main():
                      "kernel": "prefill_kernel (+plan_kernel), algorithmic FLOPs / CUDA-event time",
                      "peak_source": f"{peak_kind} bf16_tflops"},
         "gpu_launches": launches,
+        "output_gather": gather,
         "clocks": clk,
     }
     if dec_res is not None:
