@@ -52,8 +52,11 @@ def dash_sparse_attn(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
                      block_table: torch.Tensor, cu_seqlens_q: torch.Tensor, seq_lens: torch.Tensor,
                      prefix_lens: torch.Tensor, max_query_len: int, num_kv_heads: int,
                      sm_scale: float, output: torch.Tensor, local_blocks: int = 0,
-                     sparse_block_size: int = SPARSE_BLOCK_SIZE) -> None:
-    """Bias-aware block-sparse prefill attention over the paged cache (in place)."""
+                     sparse_block_size: int = SPARSE_BLOCK_SIZE,
+                     device_error: Optional["ops.DeviceErrorWord"] = None) -> None:
+    """Bias-aware block-sparse prefill attention over the paged cache (in place).
+    ``device_error`` (extension) receives the first out-of-range block or page
+    id the kernels met (they skip it and carry on)."""
     ops._need_cuda(q, k_cache, topk_idx, block_table)
     total_q, H, D = q.shape
     batch = cu_seqlens_q.shape[0] - 1
@@ -69,6 +72,7 @@ def dash_sparse_attn(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     a.qo = ops._qo(q, output, (0, q.stride(0), q.stride(1)), (0, output.stride(0), output.stride(1)), H)
     a.scale, a.block_size = float(sm_scale), int(sparse_block_size)
     a.local_window = int(local_blocks) * int(sparse_block_size)
+    a.device_error = device_error.ptr if device_error is not None else None
     keep = (seqs, idx_keep, bias_keep, bt)
     ops.prefill_attn(a, q.device)
     del keep
@@ -81,12 +85,14 @@ def dash_sparse_attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
                             sm_scale: float, output: torch.Tensor, decode_query_len: int,
                             local_blocks: int = 0, sparse_block_size: int = SPARSE_BLOCK_SIZE,
                             chunk_width: Optional[int] = None, cg_rows: Optional[int] = None,
-                            num_splits: int = 0, workspace: Optional[torch.Tensor] = None) -> None:
+                            num_splits: int = 0, workspace: Optional[torch.Tensor] = None,
+                            device_error: Optional["ops.DeviceErrorWord"] = None) -> None:
     """Bias-aware block-sparse decode with split-KV and fused combine (in place).
 
     ``chunk_width``/``cg_rows`` are accepted for signature compatibility; the
-    split count is chosen from the grid (``num_splits`` overrides it) and the
-    split scratch comes from ``workspace`` (or a grow-only cache)."""
+    split count is chosen from the grid (``num_splits`` overrides it), the
+    split scratch comes from ``workspace`` (or a grow-only cache), and
+    ``device_error`` receives the first out-of-range block or page id."""
     ops._need_cuda(q, k_cache, topk_idx, block_table, seq_lens)
     total_q, H, D = q.shape
     dql = int(decode_query_len)
@@ -105,6 +111,7 @@ def dash_sparse_attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
     a.scale, a.block_size = float(sm_scale), int(sparse_block_size)
     a.local_window = int(local_blocks) * int(sparse_block_size)
     a.num_splits = int(num_splits)
+    a.device_error = device_error.ptr if device_error is not None else None
     keep = (seqs, idx_keep, bias_keep, bt, sl)
     ops.decode_attn(a, q.device, workspace)
     del keep
