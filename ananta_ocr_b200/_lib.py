@@ -113,7 +113,7 @@ EXPORTS = [
     "dash_kbar_pool", "dash_route", "dash_block_max", "dash_prefill_workspace_size",
     "dash_prefill_attn", "dash_decode_workspace_size", "dash_decode_attn", "dash_last_error",
     "dash_library_version", "dash_count_launches", "dash_abi_sizes",
-    "dash_decode_attn_noalloc", "dash_noalloc_scratch_bytes",
+    "dash_decode_attn_noalloc", "dash_noalloc_scratch_bytes", "dash_selftest_bounded_wait",
 ]
 
 
@@ -161,6 +161,8 @@ def load(path: str = LIB_PATH):
     L.dash_count_launches.restype = C.c_int
     L.dash_abi_sizes.argtypes = [C.POINTER(_i64), C.c_int]
     L.dash_abi_sizes.restype = C.c_int
+    L.dash_selftest_bounded_wait.argtypes = [C.c_uint64, _p, _p]
+    L.dash_selftest_bounded_wait.restype = C.c_int
     _lib = L
     check_abi()
     return L

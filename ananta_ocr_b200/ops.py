@@ -87,6 +87,15 @@ class DeviceErrorWord:
         self.t.zero_()
 
 
+def selftest_bounded_wait(device_error: DeviceErrorWord, limit_ms: float = 50.0) -> None:
+    """Runs the library's bounded-wait self-test on the current stream: a
+    kernel waits for a barrier phase that never completes and must give up
+    after ``limit_ms`` with DASH_DEV_TIMEOUT in ``device_error``."""
+    rc = L.load().dash_selftest_bounded_wait(int(limit_ms * 1e6), device_error.ptr, L.current_stream())
+    if rc != L.DASH_OK:
+        raise L.DashError(rc, L.last_error())
+
+
 # ---------------------------------------------------------------------------
 # stage-0 pooling
 # ---------------------------------------------------------------------------

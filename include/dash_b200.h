@@ -314,6 +314,12 @@ int dash_count_launches(int reset);          /* kernels launched by this library
  * DashQO, DashKbarArgs, DashRouteArgs, DashBlockMaxArgs, DashPrefillArgs,
  * DashDecodeArgs, DashDeviceError.  Lets a binding verify its struct layouts. */
 int dash_abi_sizes(int64_t* out, int n);
+/* Self-test of the bounded waits every kernel uses (no reference counterpart):
+ * one thread waits on an mbarrier that nothing arrives on, with a limit of
+ * `limit_ns` (1 ms .. 1 s); the wait gives up, records DASH_DEV_TIMEOUT in
+ * `err` and the kernel returns.  Lets a host check the failure path without
+ * hanging or faulting a GPU. */
+int dash_selftest_bounded_wait(uint64_t limit_ns, DashDeviceError* err, dash_stream_t stream);
 
 #ifdef __cplusplus
 }

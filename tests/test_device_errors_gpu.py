@@ -92,3 +92,20 @@ def test_decode_out_of_range_page_is_reported_and_skipped():
     assert code == L.DASH_DEV_BAD_PAGE and info == P + 40
     diff = (out_bad.float() - out_clean.float()).abs()
     assert float(diff.max()) <= 2e-2 and float(diff.mean()) <= 2e-3
+
+
+def test_bounded_wait_gives_up_and_reports():
+    """A kernel waiting on a barrier phase that never completes gives up after
+    its limit, records DASH_DEV_TIMEOUT, and the context stays usable."""
+    import time
+    err = ops.DeviceErrorWord("cuda")
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ops.selftest_bounded_wait(err, limit_ms=50.0)
+    torch.cuda.synchronize()
+    elapsed = time.perf_counter() - t0
+    code, where, _ = err.read()
+    assert code == L.DASH_DEV_TIMEOUT and where == 90
+    assert 0.04 <= elapsed < 5.0
+    x = torch.arange(8, device="cuda", dtype=torch.float32)
+    assert float(x.sum()) == 28.0
