@@ -78,7 +78,9 @@ class DashRouteArgs(C.Structure):
                 ("local_blocks", _i32), ("topm", _i32), ("K", _i32), ("out_width", _i32),
                 ("idx_scale", _f32), ("prior_floor", _f32), ("inv_sigma", _f32),
                 ("pad0", _i32), ("out_idx", _p), ("out_bias", _p), ("out_stride", _i64),
-                ("out_count", _p), ("device_error", _p)]
+                ("out_count", _p), ("device_error", _p), ("page_q", _p), ("page_lo", _p),
+                ("page_hi", _p), ("page_bits", _p), ("page_seq_rows", _i64),
+                ("num_page_desc", _i64), ("page_bits_words", _i32), ("pad1", _i32)]
 
 
 class DashBlockMaxArgs(C.Structure):
@@ -105,8 +107,62 @@ class DashDecodeArgs(C.Structure):
                 ("device_error", _p)]
 
 
+class DashPageIdsArgs(C.Structure):
+    _fields_ = [("token_ids", _p), ("ids_stride", _i64), ("n_seq", _i32), ("ids_len", _i32),
+                ("key_length", _i32), ("per_page", _i32), ("image_token_id", _i64),
+                ("page_token_id", _i64), ("mm_pad_shift", _i64), ("has_page_token", _i32),
+                ("rule", _i32), ("page_scope_prefill", _i32), ("block_size", _i32),
+                ("n_blocks", _i32), ("page_elem_bytes", _i32), ("image_mask", _p),
+                ("image_mask_stride", _i64), ("image_page", _p), ("image_page_stride", _i64),
+                ("query_page", _p), ("query_page_stride", _i64), ("blk_lo", _p),
+                ("blk_hi", _p), ("blk_bits", _p), ("blk_has_image", _p),
+                ("prompt_pages", _p), ("marker_count", _p), ("n_image", _p),
+                ("n_query", _p), ("device_error", _p)]
+
+
+class DashPageStateArgs(C.Structure):
+    _fields_ = [("input_ids", _p), ("q_start", _p), ("start_pos", _p), ("seq_lens", _p),
+                ("gen_start", _p), ("block_table", _p), ("bt_stride", _i64),
+                ("slot_mapping", _p), ("num_slots", _i64), ("image_token_id", _i64),
+                ("page_token_id", _i64), ("mm_pad_shift", _i64), ("num_tokens", _i32),
+                ("num_reqs", _i32), ("num_decode_tokens", _i32), ("bt_width", _i32),
+                ("block_size", _i32), ("per_page", _i32), ("has_page_token", _i32),
+                ("pad0", _i32), ("slot_img_page", _p), ("slot_marker_cum", _p),
+                ("slot_img_run", _p), ("slot_prompt_pages", _p), ("q_page", _p),
+                ("blk_lo", _p), ("blk_hi", _p), ("device_error", _p)]
+
+
+class DashPageAllowArgs(C.Structure):
+    _fields_ = [("rows", _i32), ("width", _i32), ("out", _p), ("out_stride", _i64),
+                ("q_page", _p), ("q_elem_bytes", _i32), ("q_len", _i32), ("q_pos", _p),
+                ("q_stride", _i64), ("row_seq", _p), ("rows_per_seq", _i32), ("desc_width", _i32),
+                ("page_lo", _p), ("page_hi", _p), ("page_bits", _p), ("page_bits_words", _i32),
+                ("block_size", _i32), ("num_desc", _i64), ("block_table", _p),
+                ("bt_stride", _i64), ("desc_seq_rows", _i64), ("seq_lens", _p),
+                ("fallback", _i32), ("pad0", _i32)]
+
+
+class DashPageDecodeArgs(C.Structure):
+    _fields_ = [("last_ids", _p), ("ids_stride", _i64), ("n_seq", _i32),
+                ("has_page_token", _i32), ("page_token_id", _i64), ("marker_count", _p),
+                ("prompt_pages", _p), ("q_page", _p)]
+
+
+class DashBlockAnyArgs(C.Structure):
+    _fields_ = [("mask", _p), ("mask_stride", _i64), ("rows", _i32), ("len", _i32),
+                ("block_size", _i32), ("n_blocks", _i32), ("out", _p), ("out_stride", _i64)]
+
+
+class DashPageBlocksArgs(C.Structure):
+    _fields_ = [("pages", _p), ("stride", _i64), ("elem_bytes", _i32), ("rows", _i32),
+                ("len", _i32), ("block_size", _i32), ("n_blocks", _i32), ("pad0", _i32),
+                ("lo", _p), ("hi", _p), ("bits", _p)]
+
+
 ABI_ORDER = [DashSeqs, DashKV, DashRoutes, DashQO, DashKbarArgs, DashRouteArgs,
-             DashBlockMaxArgs, DashPrefillArgs, DashDecodeArgs, DashDeviceError]
+             DashBlockMaxArgs, DashPrefillArgs, DashDecodeArgs, DashDeviceError,
+             DashPageIdsArgs, DashPageStateArgs, DashPageAllowArgs, DashPageDecodeArgs,
+             DashBlockAnyArgs, DashPageBlocksArgs]
 
 # every function the header declares
 EXPORTS = [
@@ -114,6 +170,8 @@ EXPORTS = [
     "dash_prefill_attn", "dash_decode_workspace_size", "dash_decode_attn", "dash_last_error",
     "dash_library_version", "dash_count_launches", "dash_abi_sizes",
     "dash_decode_attn_noalloc", "dash_noalloc_scratch_bytes", "dash_selftest_bounded_wait",
+    "dash_page_ids", "dash_page_state_step", "dash_page_allow", "dash_page_decode_query",
+    "dash_block_any", "dash_page_blocks",
 ]
 
 
@@ -142,6 +200,12 @@ def load(path: str = LIB_PATH):
         ("dash_block_max", [C.POINTER(DashBlockMaxArgs), _p]),
         ("dash_prefill_attn", [C.POINTER(DashPrefillArgs), _p]),
         ("dash_decode_attn", [C.POINTER(DashDecodeArgs), _p]),
+        ("dash_page_ids", [C.POINTER(DashPageIdsArgs), _p]),
+        ("dash_page_state_step", [C.POINTER(DashPageStateArgs), _p]),
+        ("dash_page_allow", [C.POINTER(DashPageAllowArgs), _p]),
+        ("dash_page_decode_query", [C.POINTER(DashPageDecodeArgs), _p]),
+        ("dash_block_any", [C.POINTER(DashBlockAnyArgs), _p]),
+        ("dash_page_blocks", [C.POINTER(DashPageBlocksArgs), _p]),
     ]:
         f = getattr(L, name)
         f.argtypes = args
@@ -170,8 +234,10 @@ def load(path: str = LIB_PATH):
 
 def check_abi():
     L = _lib
-    out = (_i64 * 10)()
-    n = L.dash_abi_sizes(out, 10)
+    out = (_i64 * len(ABI_ORDER))()
+    n = L.dash_abi_sizes(out, len(ABI_ORDER))
+    if n != len(ABI_ORDER):
+        raise RuntimeError(f"ABI mismatch: library reports {n} structs, python {len(ABI_ORDER)}")
     for i, cls in enumerate(ABI_ORDER[:n]):
         if C.sizeof(cls) != out[i]:
             raise RuntimeError(f"ABI mismatch for {cls.__name__}: python {C.sizeof(cls)} "

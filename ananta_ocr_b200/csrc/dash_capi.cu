@@ -105,13 +105,16 @@ int dash_count_launches(int reset) {
 }
 
 int dash_abi_sizes(int64_t* out, int n) {
-  const int64_t s[10] = {(int64_t)sizeof(DashSeqs),        (int64_t)sizeof(DashKV),
-                         (int64_t)sizeof(DashRoutes),      (int64_t)sizeof(DashQO),
-                         (int64_t)sizeof(DashKbarArgs),    (int64_t)sizeof(DashRouteArgs),
-                         (int64_t)sizeof(DashBlockMaxArgs), (int64_t)sizeof(DashPrefillArgs),
-                         (int64_t)sizeof(DashDecodeArgs),  (int64_t)sizeof(DashDeviceError)};
-  for (int i = 0; i < n && i < 10; ++i) out[i] = s[i];
-  return 10;
+  const int64_t s[16] = {(int64_t)sizeof(DashSeqs),           (int64_t)sizeof(DashKV),
+                         (int64_t)sizeof(DashRoutes),         (int64_t)sizeof(DashQO),
+                         (int64_t)sizeof(DashKbarArgs),       (int64_t)sizeof(DashRouteArgs),
+                         (int64_t)sizeof(DashBlockMaxArgs),   (int64_t)sizeof(DashPrefillArgs),
+                         (int64_t)sizeof(DashDecodeArgs),     (int64_t)sizeof(DashDeviceError),
+                         (int64_t)sizeof(DashPageIdsArgs),    (int64_t)sizeof(DashPageStateArgs),
+                         (int64_t)sizeof(DashPageAllowArgs),  (int64_t)sizeof(DashPageDecodeArgs),
+                         (int64_t)sizeof(DashBlockAnyArgs),   (int64_t)sizeof(DashPageBlocksArgs)};
+  for (int i = 0; i < n && i < 16; ++i) out[i] = s[i];
+  return 16;
 }
 
 int dash_kbar_pool(const DashKbarArgs* a, dash_stream_t stream) {
@@ -143,6 +146,15 @@ int dash_route(const DashRouteArgs* a, dash_stream_t stream) {
     if (!aligned16(a->kbar) || a->kbar_row_stride % 4) return set_error(DASH_ERR_INVALID, "k-bar must be 16-byte aligned rows");
     if (a->num_kbar_rows <= 0) return set_error(DASH_ERR_INVALID, "num_kbar_rows must be > 0");
     if (a->block_size <= 0) return set_error(DASH_ERR_INVALID, "block_size must be > 0");
+  }
+  if (a->page_q) {
+    if (!a->page_lo || !a->page_hi) return set_error(DASH_ERR_INVALID, "page mode needs page_lo/page_hi");
+    if (a->page_bits && (a->page_bits_words <= 0 || a->page_bits_words > 8))
+      return set_error(DASH_ERR_INVALID, "page_bits_words %d not in [1, 8]", a->page_bits_words);
+    if (a->num_page_desc <= 0) return set_error(DASH_ERR_INVALID, "num_page_desc must be > 0");
+    if (!a->block_table && a->page_seq_rows < a->width)
+      return set_error(DASH_ERR_INVALID, "page_seq_rows %lld < width %d", (long long)a->page_seq_rows,
+                       a->width);
   }
   return launch_route(*a, seq_rows(a->seqs), (cudaStream_t)stream);
 }
@@ -210,6 +222,89 @@ int dash_decode_attn(const DashDecodeArgs* a, dash_stream_t stream) {
     return set_error(DASH_ERR_WORKSPACE, "decode workspace %zu bytes needed, %zu given", need,
                      a->workspace_bytes);
   return launch_decode(*a, rows, sp, (cudaStream_t)stream);
+}
+
+static bool pow2_block(int bs) { return bs >= 16 && bs <= 256 && (bs & (bs - 1)) == 0; }
+
+int dash_page_ids(const DashPageIdsArgs* a, dash_stream_t stream) {
+  if (!a) return set_error(DASH_ERR_INVALID, "null args");
+  if (a->n_seq < 0 || a->key_length < 0 || a->ids_len < 0) return set_error(DASH_ERR_INVALID, "negative size");
+  if (a->n_seq > 0 && a->key_length > 0 && a->ids_len > 0 && !a->token_ids)
+    return set_error(DASH_ERR_INVALID, "null token_ids");
+  if (a->per_page < 1) return set_error(DASH_ERR_INVALID, "per_page must be >= 1");
+  if (a->rule != 0 && a->rule != 1) return set_error(DASH_ERR_INVALID, "rule must be 0 or 1");
+  if (a->rule == 1 && a->query_page) return set_error(DASH_ERR_INVALID, "rule 1 produces no query pages");
+  if ((a->image_page || a->query_page) && a->page_elem_bytes != 4 && a->page_elem_bytes != 8)
+    return set_error(DASH_ERR_INVALID, "page_elem_bytes must be 4 or 8");
+  const bool blocks = a->blk_lo || a->blk_hi || a->blk_bits || a->blk_has_image;
+  if (blocks) {
+    if (!pow2_block(a->block_size))
+      return set_error(DASH_ERR_UNSUPPORTED, "block_size %d: block outputs need a power of two in [16, 256]",
+                       a->block_size);
+    if (a->n_blocks < 0) return set_error(DASH_ERR_INVALID, "n_blocks < 0");
+  }
+  return launch_page_ids(*a, (cudaStream_t)stream);
+}
+
+int dash_page_state_step(const DashPageStateArgs* a, dash_stream_t stream) {
+  if (!a) return set_error(DASH_ERR_INVALID, "null args");
+  if (a->num_reqs < 0 || a->num_tokens < 0) return set_error(DASH_ERR_INVALID, "negative size");
+  if (a->num_reqs == 0) return DASH_OK;
+  if (!a->input_ids || !a->block_table || !a->slot_mapping || !a->q_page)
+    return set_error(DASH_ERR_INVALID, "null ids/block_table/slot_mapping/q_page");
+  if (!a->slot_img_page || !a->slot_marker_cum || !a->slot_img_run || !a->slot_prompt_pages)
+    return set_error(DASH_ERR_INVALID, "null slot state");
+  if (!a->q_start && a->num_tokens != a->num_reqs)
+    return set_error(DASH_ERR_INVALID, "without q_start every request owns one token");
+  if (!a->start_pos && !a->seq_lens) return set_error(DASH_ERR_INVALID, "need start_pos or seq_lens");
+  if (a->num_slots <= 0 || a->block_size <= 0 || a->bt_width <= 0 || a->per_page < 1)
+    return set_error(DASH_ERR_INVALID, "num_slots, block_size, bt_width and per_page must be > 0");
+  if (!a->blk_lo != !a->blk_hi) return set_error(DASH_ERR_INVALID, "blk_lo and blk_hi go together");
+  return launch_page_state(*a, (cudaStream_t)stream);
+}
+
+int dash_page_allow(const DashPageAllowArgs* a, dash_stream_t stream) {
+  if (!a) return set_error(DASH_ERR_INVALID, "null args");
+  if (a->rows < 0 || a->width < 0 || a->desc_width < 0) return set_error(DASH_ERR_INVALID, "negative size");
+  if (a->rows == 0 || a->width == 0) return DASH_OK;
+  if (!a->out || !a->q_page || !a->page_lo || !a->page_hi)
+    return set_error(DASH_ERR_INVALID, "null out/q_page/page_lo/page_hi");
+  if (!a->row_seq && a->rows_per_seq <= 0) return set_error(DASH_ERR_INVALID, "rows_per_seq must be > 0");
+  if (a->q_elem_bytes != 4 && a->q_elem_bytes != 8) return set_error(DASH_ERR_INVALID, "q_elem_bytes must be 4 or 8");
+  if (a->q_pos && a->q_len <= 0) return set_error(DASH_ERR_INVALID, "q_len must be > 0 with q_pos");
+  if (a->page_bits && (a->page_bits_words <= 0 || a->page_bits_words > 8))
+    return set_error(DASH_ERR_INVALID, "page_bits_words %d not in [1, 8]", a->page_bits_words);
+  if (a->num_desc <= 0) return set_error(DASH_ERR_INVALID, "num_desc must be > 0");
+  if (a->seq_lens && a->block_size <= 0) return set_error(DASH_ERR_INVALID, "block_size must be > 0");
+  return launch_page_allow(*a, (cudaStream_t)stream);
+}
+
+int dash_page_blocks(const DashPageBlocksArgs* a, dash_stream_t stream) {
+  if (!a) return set_error(DASH_ERR_INVALID, "null args");
+  if (a->rows < 0 || a->len < 0 || a->n_blocks < 0) return set_error(DASH_ERR_INVALID, "negative size");
+  if (a->block_size <= 0 || a->block_size > 256)
+    return set_error(DASH_ERR_UNSUPPORTED, "block_size %d not in (0, 256]", a->block_size);
+  if (a->elem_bytes != 4 && a->elem_bytes != 8) return set_error(DASH_ERR_INVALID, "elem_bytes must be 4 or 8");
+  if (a->rows > 0 && a->n_blocks > 0 && (!a->lo || !a->hi || (a->len > 0 && !a->pages)))
+    return set_error(DASH_ERR_INVALID, "null pages/lo/hi");
+  return launch_page_blocks(*a, (cudaStream_t)stream);
+}
+
+int dash_page_decode_query(const DashPageDecodeArgs* a, dash_stream_t stream) {
+  if (!a) return set_error(DASH_ERR_INVALID, "null args");
+  if (a->n_seq < 0) return set_error(DASH_ERR_INVALID, "n_seq < 0");
+  if (a->n_seq > 0 && (!a->last_ids || !a->marker_count || !a->prompt_pages || !a->q_page))
+    return set_error(DASH_ERR_INVALID, "null pointer");
+  return launch_page_decode(*a, (cudaStream_t)stream);
+}
+
+int dash_block_any(const DashBlockAnyArgs* a, dash_stream_t stream) {
+  if (!a) return set_error(DASH_ERR_INVALID, "null args");
+  if (a->rows < 0 || a->len < 0 || a->n_blocks < 0) return set_error(DASH_ERR_INVALID, "negative size");
+  if (a->block_size <= 0) return set_error(DASH_ERR_INVALID, "block_size must be > 0");
+  if (a->rows > 0 && a->n_blocks > 0 && (!a->out || (a->len > 0 && !a->mask)))
+    return set_error(DASH_ERR_INVALID, "null mask/out");
+  return launch_block_any(*a, (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -30,6 +30,21 @@ __device__ __forceinline__ void record_error(DeviceError* e, int code, int where
 }
 
 // ---------------------------------------------------------------------------
+// Image-page membership of block descriptor i: page q lies in [lo, hi] and,
+// with a page bit set, bit (q - lo) is set (exact set instead of range).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ bool page_desc_holds(const int32_t* lo_a, const int32_t* hi_a,
+                                                const uint32_t* bits, int words, int64_t i,
+                                                int q) {
+  const int lo = lo_a[i];
+  if (q < 0 || lo < 0 || q < lo || q > hi_a[i]) return false;
+  if (!bits) return true;
+  const int k = q - lo;
+  if (k >= 32 * words) return false;
+  return (bits[i * words + (k >> 5)] >> (k & 31)) & 1u;
+}
+
+// ---------------------------------------------------------------------------
 // Fixed-order fp32 arithmetic shared with oracle/dash_oracle.c
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float clamp_act(float z) {

@@ -19,5 +19,11 @@ int launch_prefill(const DashPrefillArgs& a, int64_t n_rows, cudaStream_t st);
 size_t prefill_workspace(const DashPrefillArgs& a, int64_t n_rows);
 size_t decode_workspace(const DashDecodeArgs& a, int64_t n_rows, int splits);
 int decode_auto_splits(const DashDecodeArgs& a, int64_t n_rows);
+int launch_page_ids(const DashPageIdsArgs& a, cudaStream_t st);
+int launch_page_state(const DashPageStateArgs& a, cudaStream_t st);
+int launch_page_allow(const DashPageAllowArgs& a, cudaStream_t st);
+int launch_page_decode(const DashPageDecodeArgs& a, cudaStream_t st);
+int launch_block_any(const DashBlockAnyArgs& a, cudaStream_t st);
+int launch_page_blocks(const DashPageBlocksArgs& a, cudaStream_t st);
 
 }  // namespace dash

@@ -253,6 +253,20 @@ __device__ __forceinline__ uint32_t radix_threshold_smem(const float* sx, int W,
 //
 // Per-warp scratch: mid_ (block id by slot; slots ascend by id), mx (x by
 // slot, then z by rank, then log-prior by rank), mval (valid flag by rank).
+// Page-aware candidacy of block b for a row of sequence s whose query page is
+// qp (descriptor of a physical block through the block table, or row-major
+// per sequence).
+__device__ __forceinline__ bool page_block_holds(const DashRouteArgs& a, int qp, int s, int b) {
+  if (qp < 0) return false;
+  const int64_t i = a.block_table ? (int64_t)a.block_table[(int64_t)s * a.bt_stride + b]
+                                  : (int64_t)s * a.page_seq_rows + b;
+  if (i < 0 || i >= a.num_page_desc) {
+    record_error(a.device_error, DASH_DEV_BAD_PAGE, 13, i);
+    return false;
+  }
+  return page_desc_holds(a.page_lo, a.page_hi, a.page_bits, a.page_bits_words, i, qp);
+}
+
 template <int KW, int PER>
 __device__ __noinline__ void select_row(const DashRouteArgs& a, float* sx, uint32_t* scand,
                                         int* mid_, float* mx, int* mval, int64_t r, int s,
@@ -262,12 +276,15 @@ __device__ __noinline__ void select_row(const DashRouteArgs& a, float* sx, uint3
   const uint32_t lt_mask = (1u << lane) - 1u;
   // ---- candidates (with per-row fallback) ----
   const uint8_t* cm = nullptr;
-  if (a.cand) cm = a.cand + (a.cand_per_seq ? (int64_t)s : r) * a.cand_row_stride;
+  if (a.cand && !a.page_q) cm = a.cand + (a.cand_per_seq ? (int64_t)s : r) * a.cand_row_stride;
+  const int qp = a.page_q ? a.page_q[r] : -1;
   bool any = false;
   for (int b0 = 0; b0 < Wp; b0 += 32) {
     int b = b0 + lane;
     bool remote = b < W && sx[b] > kScoreNeg * 0.5f;
-    bool c = remote && (!cm || cm[b] != 0);
+    bool c = remote;
+    if (a.page_q) c = remote && page_block_holds(a, qp, s, b);
+    else if (cm) c = remote && cm[b] != 0;
     uint32_t bal = __ballot_sync(0xffffffffu, c);
     if (lane == 0) scand[b0 >> 5] = bal;
     any |= bal != 0;

@@ -10,7 +10,14 @@ libdash_b200.so:
   over a contiguous cache.
 * ``dash_prefill_forward``: the ``_infer_prefill_attend`` flow
   (modeling_deepseekv2.py:403-421) after the router projections: scores ->
-  selection -> gather attention, with the routed lists kept on the device.
+  selection -> gather attention, with the routed lists kept on the device;
+  with ``page_domain`` the page-aware candidates of ``_dash_block_cand`` are
+  applied inside the router from their compact form (no [B, S, nblk] mask).
+* ``_dash_page_ids`` / ``_dash_block_cand`` (modeling_deepseekv2.py:87-114):
+  page-aware ids and the per-query candidate domain through the indexer's
+  builders (``_sparse_base_impl.DeepseekV2IndexerPages``).
+* ``page_domain_from_ids``: token ids -> the compact domain for
+  ``dash_prefill_forward`` in one kernel pass.
 
 ``router`` arguments only need the attributes the reference reads
 (stage0, block_size, local_blocks, local_window, head_cls, _infer_params).
@@ -26,6 +33,42 @@ from .sparse_gather_e2e_triton import _as_kernel_dtype
 
 _SCORE_NEG = -1.0e9
 _MASK_NEG = -1.0e9
+
+
+def _dash_page_ids(self, idx, src_ids, key_length):
+    """modeling_deepseekv2.py:87-96: (image mask, image page ids, query page ids)."""
+    if idx.image_bucket_constraint:
+        return idx._build_page_aware_ids(src_ids, idx.image_token_id, idx.page_token_id,
+                                         key_length)
+    itm = idx._build_flat_image_token_mask(src_ids, idx.image_token_id, key_length)
+    return itm, None, None
+
+
+def _dash_block_cand(self, idx, router, pos_ids, itm, ipi, qpi, nblk, bsz, q_len):
+    """modeling_deepseekv2.py:99-114: [B, S, nblk] bool per-query candidate
+    domain, or None.  One pass: the kernels never build the [B, S, nblk,
+    block_size] comparison, so ``router.q_chunk`` slicing is not needed."""
+    if itm is None and (ipi is None or qpi is None):
+        return None
+    cm = idx._build_kl_candidate_mask(pos_ids, nblk, itm, bsz, q_len,
+                                      image_token_page_ids=ipi, query_token_page_ids=qpi)
+    return cm[:, 0]
+
+
+@torch.no_grad()
+def page_domain_from_ids(token_ids, *, image_token_id, page_token_id, per_page, block_size,
+                         nblk, page_scope_prefill=False):
+    """Compact page-aware domain of a fresh contiguous prefill (query row t of
+    sequence b at position t): query page per row + exact page descriptors per
+    block, from one ``dash_page_ids`` pass.  Same candidates as
+    ``_dash_block_cand`` with ``image_bucket_constraint``."""
+    from .pages import PageDomain, page_ids
+    B, S = token_ids.shape
+    r = page_ids(token_ids, image_token_id=image_token_id, page_token_id=page_token_id,
+                 per_page=per_page, key_length=S, rule=0, page_scope_prefill=page_scope_prefill,
+                 block_size=block_size, n_blocks=nblk)
+    return PageDomain(q_page=r["query_page"].view(-1), lo=r["lo"], hi=r["hi"], bits=r["bits"],
+                      seq_rows=nblk)
 
 
 @torch.no_grad()
@@ -99,7 +142,7 @@ def _decode_attend(q, k_all, v_all, topi, bias, valid, q_pos, block_size, local_
 @torch.no_grad()
 def dash_prefill_forward(q, k, v, idx_q, idx_k, *, block_size, local_blocks, head_cls=None,
                          K, topm=None, idx_scale, prior_floor, sigma, scale=None,
-                         return_routes=False):
+                         return_routes=False, page_domain=None):
     """Router + gather attention for a contiguous prefill.
 
     q [B,H,S,D], k/v [B,Hkv,S,D] (bf16/fp16), idx_q/idx_k [B,S,d] fp32 router
@@ -111,7 +154,8 @@ def dash_prefill_forward(q, k, v, idx_q, idx_k, *, block_size, local_blocks, hea
     seqs = ops.Seqs(n_seq=B, q_len=S, kv_len=S, max_q_len=S)
     idx, bias = ops.route(seqs, width=nblk, block_size=block_size, local_blocks=local_blocks,
                           idx_scale=idx_scale, prior_floor=prior_floor, sigma=sigma,
-                          topm=int(topm or K), K=K, idx_q=idx_q.reshape(B * S, d), kbar=kbar)
+                          topm=int(topm or K), K=K, idx_q=idx_q.reshape(B * S, d), kbar=kbar,
+                          page=page_domain)
     out = ops.gather_attention(q, k, v, idx.view(B, S, K), bias.view(B, S, K),
                                block_size=block_size, local_window=local_blocks * block_size,
                                scale=float(scale if scale is not None else 1.0 / math.sqrt(D)))

@@ -156,12 +156,15 @@ def route(seqs: Seqs, *, width: int, block_size: int, local_blocks: int, idx_sca
           cand: Optional[torch.Tensor] = None, cand_per_seq: bool = False,
           out_idx: Optional[torch.Tensor] = None, out_bias: Optional[torch.Tensor] = None,
           out_width: Optional[int] = None, scores_out: Optional[torch.Tensor] = None,
-          out_count: Optional[torch.Tensor] = None, device_error: Optional[DeviceErrorWord] = None):
+          out_count: Optional[torch.Tensor] = None, device_error: Optional[DeviceErrorWord] = None,
+          page=None):
     """Fused DASH routing for ``seqs.rows`` query rows.
 
     Either ``scores_in`` [rows, width] (precomputed block scores) or ``idx_q``
     [rows, d] + ``kbar`` (contiguous [n_seq, nblk, d] or a page cache [P, d]
-    addressed through ``block_table`` [n_seq, W]).  Returns (idx int32 [rows,
+    addressed through ``block_table`` [n_seq, W]).  ``page`` (a
+    ``pages.PageDomain``) restricts the candidates to the blocks holding image
+    tokens of each row's page (instead of ``cand``).  Returns (idx int32 [rows,
     out_width] ascending with -1 tail, bias fp32 [rows, out_width])."""
     ref = scores_in if scores_in is not None else idx_q
     _need_cuda(ref, kbar, block_table, cand)
@@ -203,6 +206,16 @@ def route(seqs: Seqs, *, width: int, block_size: int, local_blocks: int, idx_sca
     assert out_bias.stride(0) == out_idx.stride(0)
     a.out_count = _ptr(out_count)
     a.device_error = device_error.ptr if device_error is not None else None
+    if page is not None:
+        _need_cuda(page.q_page, page.lo, page.hi, page.bits)
+        for t in (page.q_page, page.lo, page.hi):
+            if t.dtype != torch.int32 or not t.is_contiguous():
+                raise ValueError("page domain tensors must be contiguous int32")
+        a.page_q, a.page_lo, a.page_hi = page.q_page.data_ptr(), page.lo.data_ptr(), page.hi.data_ptr()
+        if page.bits is not None:
+            a.page_bits, a.page_bits_words = page.bits.data_ptr(), page.bits.shape[-1]
+        a.page_seq_rows = page.seq_rows if block_table is None else 0
+        a.num_page_desc = page.lo.numel()
     L.call("dash_route", a)
     return out_idx, out_bias
 

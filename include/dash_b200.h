@@ -207,8 +207,225 @@ typedef struct {
   int64_t out_stride;
   int32_t* out_count;     /* optional valid slots per row */
   DashDeviceError* device_error;
+  /* Page-aware candidates (optional; when page_q is set, cand is ignored).
+   * Block b of row r is a candidate iff it is remote and the image-page set
+   * of its descriptor i holds q = page_q[r]: q >= 0, page_lo[i] >= 0,
+   * page_lo[i] <= q <= page_hi[i] and, when page_bits is given, bit
+   * (q - page_lo[i]) of page_bits[i*page_bits_words ...] is set.
+   * i = block_table[s*bt_stride + b] when block_table is set (descriptors of
+   * physical blocks), else s*page_seq_rows + b.  Rows left without a
+   * candidate fall back to all remote blocks.  Replaces the `image_allow`
+   * input of WHL route_triton.py:159-167 built by page_state.py:330-371 /
+   * decode_meta_triton.py:107-163, and the `block_cand` of
+   * modeling_deepseekv2.py:310-319 built by _sparse_base_impl.py:2383-2484. */
+  const int32_t* page_q;
+  const int32_t* page_lo;
+  const int32_t* page_hi;
+  const uint32_t* page_bits;
+  int64_t page_seq_rows;
+  int64_t num_page_desc;   /* descriptors addressable (bounds check) */
+  int32_t page_bits_words;
+  int32_t pad1;
 } DashRouteArgs;
 int dash_route(const DashRouteArgs* args, dash_stream_t stream);
+
+/* ---------------------------------------------------------------------- */
+/* Page-aware candidate domain (image pages of an OCR document).
+ *
+ * Token ids mark image placeholders (image_token_id, or any id >=
+ * mm_pad_shift when mm_pad_shift > 0) and page starts (page_token_id when
+ * has_page_token).  Per row, cum(t) = page markers at positions <= t and
+ * run(t) = image tokens at positions <= t.
+ *
+ * dash_page_ids -- one pass over contiguous rows of token ids.
+ * Replaces: _sparse_base_impl.py:2189-2260 (_build_page_aware_ids, rule 0),
+ *           :2363-2381 (_build_flat_image_token_mask), :2177-2187
+ *           (_build_image_block_allow_mask) and the prefill branch of
+ *           modeling_anantaocr.py:468-481 (_uocr_dash_decode_allow, rule 1).
+ *   rule 0: pp = cum at the row's last image token (0 without one); the row
+ *           is in marker mode iff pp > 0; image page = marker mode ? cum - 1
+ *           : (run - 1) / per_page; query page = cum - 1 at positions <= the
+ *           last image token (-1 unless page_scope_prefill), cum - 1 - pp
+ *           after it in marker mode, cum - 1 otherwise; negative -> -1.
+ *   rule 1: image page = cum > 0 ? cum - 1 : (run - 1) / per_page (per
+ *           token); query pages are not produced.
+ * Image pages are -1 at non-image tokens.  Tokens at t >= ids_len read as id
+ * -1.  Block outputs cover n_blocks blocks of block_size tokens per row
+ * (tokens past key_length count as non-image): lo/hi = min/max image page >=
+ * 0 in the block (-1 when none), bits = set of pages present (bit k: page
+ * lo + k; exact for rule 0, where a block spans fewer than block_size
+ * pages), has_image = any image token.  block_size: power of two in
+ * [16, 256] (block outputs only).  Per-row outputs: prompt_pages = pp,
+ * marker_count = cum at key_length - 1, n_image / n_query = image tokens /
+ * tokens with a query page >= 0.  Every output pointer is optional.       */
+typedef struct {
+  const int64_t* token_ids;   /* [n_seq, ids_stride] */
+  int64_t ids_stride;
+  int32_t n_seq;
+  int32_t ids_len;            /* columns present in token_ids */
+  int32_t key_length;         /* tokens per row processed */
+  int32_t per_page;           /* >= 1 */
+  int64_t image_token_id;
+  int64_t page_token_id;
+  int64_t mm_pad_shift;       /* 0: off */
+  int32_t has_page_token;
+  int32_t rule;               /* 0 or 1 */
+  int32_t page_scope_prefill;
+  int32_t block_size;
+  int32_t n_blocks;           /* blocks per row of the block outputs */
+  int32_t page_elem_bytes;    /* 4 (int32) or 8 (int64) for image_page / query_page */
+  uint8_t* image_mask;  int64_t image_mask_stride;   /* [n_seq, key_length] */
+  void* image_page;     int64_t image_page_stride;   /* [n_seq, key_length] */
+  void* query_page;     int64_t query_page_stride;   /* [n_seq, key_length] */
+  int32_t* blk_lo;                                   /* [n_seq, n_blocks] */
+  int32_t* blk_hi;
+  uint32_t* blk_bits;                                /* [n_seq, n_blocks, max(1, block_size/32)] */
+  uint8_t* blk_has_image;
+  int32_t* prompt_pages;                             /* [n_seq] */
+  int32_t* marker_count;
+  int32_t* n_image;
+  int32_t* n_query;
+  DashDeviceError* device_error;
+} DashPageIdsArgs;
+int dash_page_ids(const DashPageIdsArgs* args, dash_stream_t stream);
+
+/* dash_page_state_step -- per-slot page bookkeeping of a block-paged KV
+ * cache for one serving step (a mixed batch of requests, tokens packed).
+ * Replaces: page_state.py:217-313 (PageIsolationState.step) and the page
+ * part of decode_meta_triton.py:18-87 (_decode_meta_kernel).
+ * Request r owns tokens [q_start[r], q_start[r+1]) at positions
+ * start_pos[r] + i (q_start NULL: request r owns token r; start_pos NULL:
+ * start_pos[r] = seq_lens[r] - 1).  Carry-in (marker count, image run,
+ * prompt pages) is read from the slot of position start_pos - 1.  Per token:
+ * marker_cum, img_run, image page (rule 1 of dash_page_ids), pp = max(carry,
+ * marker_cum at the latest image token of this step), query page = image
+ * page at image tokens, else (generated token ? marker_cum - 1 - pp (-1 if
+ * negative) : (marker_cum > pp ? marker_cum - 1 : -1)).  A token is
+ * generated iff its index < num_decode_tokens, or its position >=
+ * gen_start[r] (gen_start optional).  The four slot arrays are written at
+ * slot_mapping (clamped to [0, num_slots)); then slots past the last token
+ * in each request's last block get image page -1.  When blk_lo/blk_hi are
+ * given, the image-page bounds of every physical block written in this step
+ * are recomputed from the slot array (page_state.py:315-328).            */
+typedef struct {
+  const int64_t* input_ids;   /* [num_tokens] */
+  const int64_t* q_start;     /* [num_reqs+1] or NULL */
+  const int64_t* start_pos;   /* [num_reqs] or NULL */
+  const int32_t* seq_lens;    /* [num_reqs], used when start_pos is NULL */
+  const int64_t* gen_start;   /* [num_reqs] or NULL */
+  const int32_t* block_table; int64_t bt_stride;
+  const int64_t* slot_mapping;/* [num_tokens] */
+  int64_t num_slots;
+  int64_t image_token_id;
+  int64_t page_token_id;
+  int64_t mm_pad_shift;
+  int32_t num_tokens;
+  int32_t num_reqs;
+  int32_t num_decode_tokens;
+  int32_t bt_width;
+  int32_t block_size;
+  int32_t per_page;
+  int32_t has_page_token;
+  int32_t pad0;
+  int32_t* slot_img_page;     /* [num_slots] state, in/out */
+  int32_t* slot_marker_cum;
+  int32_t* slot_img_run;
+  int32_t* slot_prompt_pages;
+  int32_t* q_page;            /* [num_tokens] out */
+  int32_t* blk_lo;            /* [num_slots / block_size] or NULL */
+  int32_t* blk_hi;
+  DashDeviceError* device_error;
+} DashPageStateArgs;
+int dash_page_state_step(const DashPageStateArgs* args, dash_stream_t stream);
+
+/* dash_page_allow -- dense per-row candidate mask out[r, b] (uint8), b <
+ * width, from a query page per row and block page descriptors.
+ * Replaces: page_state.py:330-371 (build_query_allow), decode_meta_triton.py
+ * :107-163 (_decode_allow_kernel), _sparse_base_impl.py:2383-2402 +
+ * :2457-2484 (_build_page_aware_image_block_mask + _build_kl_candidate_mask
+ * fallback) and the decode branch of modeling_anantaocr.py:482-496.
+ * Row r belongs to sequence s = row_seq ? row_seq[r] : r / rows_per_seq.
+ * Block b < desc_width has descriptor i = block_table[s*bt_stride + b]
+ * (clamped to [0, num_desc)) or s*desc_seq_rows + b; blocks >= desc_width
+ * and (seq_lens given) blocks with b*block_size >= seq_lens[s] never match.
+ * same = match as in dash_route's page mode; out = same, or 1 everywhere
+ * when fallback != 0 and the row has no match.                             */
+typedef struct {
+  int32_t rows;
+  int32_t width;
+  uint8_t* out; int64_t out_stride;
+  const void* q_page;         /* [rows], or [n_seq, q_stride] when q_pos is set */
+  int32_t q_elem_bytes;       /* 4 (int32) or 8 (int64) */
+  int32_t q_len;              /* q_pos set: query page of row r = q_page[s*q_stride +
+                                 clamp(q_pos[r], 0, q_len - 1)] */
+  const int64_t* q_pos;       /* [rows] or NULL */
+  int64_t q_stride;
+  const int32_t* row_seq;     /* [rows] or NULL */
+  int32_t rows_per_seq;
+  int32_t desc_width;
+  const int32_t* page_lo;
+  const int32_t* page_hi;
+  const uint32_t* page_bits;  /* or NULL: range test only */
+  int32_t page_bits_words;
+  int32_t block_size;
+  int64_t num_desc;
+  const int32_t* block_table; int64_t bt_stride;
+  int64_t desc_seq_rows;
+  const int32_t* seq_lens;    /* or NULL */
+  int32_t fallback;
+  int32_t pad0;
+} DashPageAllowArgs;
+int dash_page_allow(const DashPageAllowArgs* args, dash_stream_t stream);
+
+/* dash_page_blocks -- block page descriptors from image page ids (-1 = no
+ * image page): for block b < n_blocks of row s, over tokens t < min(len,
+ * (b+1)*block_size): lo/hi = min/max page >= 0 (-1 when none), bits = pages
+ * present relative to lo (words = max(1, block_size/32); a page beyond
+ * 32*words of lo sets no bit).
+ * Replaces the per-block test of _sparse_base_impl.py:2390-2401 and
+ * page_state.py:315-328 (block_page_bounds, via a [num_blocks, block_size]
+ * view of the slot pages).                                                 */
+typedef struct {
+  const void* pages; int64_t stride;   /* [rows, stride] */
+  int32_t elem_bytes;                  /* 4 or 8 */
+  int32_t rows;
+  int32_t len;
+  int32_t block_size;
+  int32_t n_blocks;
+  int32_t pad0;
+  int32_t* lo;                         /* [rows, n_blocks] */
+  int32_t* hi;
+  uint32_t* bits;                      /* [rows, n_blocks, words] or NULL */
+} DashPageBlocksArgs;
+int dash_page_blocks(const DashPageBlocksArgs* args, dash_stream_t stream);
+
+/* dash_page_decode_query -- decode-step query page of the contiguous decoder.
+ * Replaces: modeling_anantaocr.py:482-486 (_uocr_dash_decode_allow decode
+ * branch): marker_count[s] += (last_ids[s*ids_stride] == page_token_id);
+ * q_page[s] = marker_count[s] - 1 - prompt_pages[s], -1 when negative.     */
+typedef struct {
+  const int64_t* last_ids; int64_t ids_stride;
+  int32_t n_seq;
+  int32_t has_page_token;
+  int64_t page_token_id;
+  int32_t* marker_count;      /* in/out */
+  const int32_t* prompt_pages;
+  int32_t* q_page;            /* out */
+} DashPageDecodeArgs;
+int dash_page_decode_query(const DashPageDecodeArgs* args, dash_stream_t stream);
+
+/* dash_block_any -- out[s, b] = any(mask[s, t]) over the tokens t <
+ * min(len, (b+1)*block_size) of block b, b < n_blocks.
+ * Replaces: _sparse_base_impl.py:2177-2187 (_build_image_block_allow_mask). */
+typedef struct {
+  const uint8_t* mask; int64_t mask_stride;
+  int32_t rows;
+  int32_t len;
+  int32_t block_size;
+  int32_t n_blocks;
+  uint8_t* out; int64_t out_stride;
+} DashBlockAnyArgs;
+int dash_block_any(const DashBlockAnyArgs* args, dash_stream_t stream);
 
 /* ---------------------------------------------------------------------- */
 /* Indexer stage-0 block scores (block max over remote keys).
@@ -312,7 +529,9 @@ int dash_library_version(void);              /* (major << 16) | minor */
 int dash_count_launches(int reset);          /* kernels launched by this library so far */
 /* sizeof() of the argument structs, in this order: DashSeqs, DashKV, DashRoutes,
  * DashQO, DashKbarArgs, DashRouteArgs, DashBlockMaxArgs, DashPrefillArgs,
- * DashDecodeArgs, DashDeviceError.  Lets a binding verify its struct layouts. */
+ * DashDecodeArgs, DashDeviceError, DashPageIdsArgs, DashPageStateArgs,
+ * DashPageAllowArgs, DashPageDecodeArgs, DashBlockAnyArgs, DashPageBlocksArgs.  Lets a binding
+ * verify its struct layouts; returns the number of sizes available. */
 int dash_abi_sizes(int64_t* out, int n);
 /* Self-test of the bounded waits every kernel uses (no reference counterpart):
  * one thread waits on an mbarrier that nothing arrives on, with a limit of

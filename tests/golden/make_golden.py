@@ -68,6 +68,17 @@ def import_reference():
     for p in ["sglang", "sglang/srt", "sglang/srt/layers", "sglang/srt/layers/attention"]:
         open(os.path.join(tmp, p, "__init__.py"), "w").close()
     sys.path.insert(0, tmp)
+    # modules the reference imports but this path never uses
+    rt = types.ModuleType("sglang.srt.runtime_context")
+    rt.get_buffer = lambda key, factory: factory()
+    sys.modules["sglang.srt.runtime_context"] = rt
+
+    class _AttrDict(dict):
+        __getattr__ = dict.__getitem__
+    for mod, attr in (("easydict", "EasyDict"), ("addict", "Dict")):
+        m = types.ModuleType(mod)
+        setattr(m, attr, _AttrDict)
+        sys.modules.setdefault(mod, m)
     import ananta_ref.dash_attention as da
     import ananta_ref.modeling_deepseekv2 as md
     return da, md
@@ -239,6 +250,198 @@ def triton_interp_case(da, md, name, seed):
     print(name, "saved")
 
 
+def page_aware_case(name, seed):
+    """Page-aware candidate domain: the indexer's id builders and candidate mask
+    (_sparse_base_impl.py), _dash_block_cand (modeling_deepseekv2.py), the
+    contiguous decoder's decode allow (modeling_anantaocr.py) and the sglang
+    PageIsolationState / decode_allow_fused / local_union_fused (Triton
+    interpreted) over a short serving trace."""
+    import ananta_ref._sparse_base_impl as sb
+    import ananta_ref.modeling_deepseekv2 as mdl
+    import ananta_ref.modeling_anantaocr as ma
+    from sglang.srt.layers.attention.unlimited_dash_ops import page_state as ps
+    from sglang.srt.layers.attention.unlimited_dash_ops import decode_meta_triton as dm
+    from oracle.page_oracle import (make_document_ids, IMAGE_TOKEN_ID as IMG,
+                                    PAGE_TOKEN_ID as PG, MM_PAD_SHIFT)
+    torch.cuda.is_current_stream_capturing = lambda: False
+    rng = np.random.default_rng(seed)
+    res = {}
+
+    # ---- contiguous documents ----
+    S, bs = 1500, 64
+    docs = [
+        make_document_ids(rng, S, n_pages=4, page_tokens=273, text_in_page=3, empty_pages=1,
+                          response_pages=2),
+        make_document_ids(rng, S, n_pages=5, page_tokens=200, markers=False),
+        make_document_ids(rng, S, n_pages=30, page_tokens=20, empty_pages=6, lead_images=10,
+                          response_pages=3),
+    ]
+    ids = np.stack(docs)
+    B = ids.shape[0]
+    nblk = -(-S // bs)
+    dev = torch.device("cpu")
+    idx = types.SimpleNamespace(q_proj=types.SimpleNamespace(weight=torch.zeros(1, device=dev)),
+                                per_page_image_tokens=100, block_size=bs, layer_idx=0,
+                                _page_aware_diag_logged=True, image_bucket_constraint=True,
+                                image_token_id=IMG, page_token_id=PG)
+    for m in ("_build_page_aware_image_block_mask", "_build_image_block_allow_mask",
+              "_build_page_aware_ids", "_build_flat_image_token_mask",
+              "_build_kl_candidate_mask", "_log_image_mask"):
+        setattr(idx, m, types.MethodType(getattr(sb.DeepseekV2Indexer, m), idx))
+    idx._diag_due = lambda key: False                       # no diagnostic prints
+    tid = torch.tensor(ids)
+    pos = torch.arange(S)[None].expand(B, -1)
+    for scope in (False, True):
+        sb._PAGE_SCOPE_PREFILL = scope
+        itm, ipi, qpi = sb.DeepseekV2Indexer._build_page_aware_ids(idx, tid, IMG, PG, S)
+        res[f"itm_{int(scope)}"] = itm.numpy()
+        res[f"ipi_{int(scope)}"] = ipi.numpy()
+        res[f"qpi_{int(scope)}"] = qpi.numpy()
+        cm = sb.DeepseekV2Indexer._build_kl_candidate_mask(idx, pos, nblk, itm, B, S, ipi, qpi)
+        res[f"cand_page_{int(scope)}"] = np.packbits(cm[:, 0].numpy(), axis=-1)
+    sb._PAGE_SCOPE_PREFILL = False
+    # a truncated key length (ids longer than the keys) and a padded one
+    for kl in (1000, 1700):
+        itm, ipi, qpi = sb.DeepseekV2Indexer._build_page_aware_ids(idx, tid, IMG, PG, kl)
+        res[f"ipi_kl{kl}"] = ipi.numpy()
+        res[f"qpi_kl{kl}"] = qpi.numpy()
+    flat = sb.DeepseekV2Indexer._build_flat_image_token_mask(idx, tid, IMG, S)
+    res["img_blk"] = sb.DeepseekV2Indexer._build_image_block_allow_mask(idx, flat, nblk).numpy()
+    res["img_blk_short"] = sb.DeepseekV2Indexer._build_image_block_allow_mask(
+        idx, flat, nblk - 5).numpy()
+    idx.image_bucket_constraint = False
+    cm = sb.DeepseekV2Indexer._build_kl_candidate_mask(idx, pos[:, :300], nblk, flat, B, 300)
+    res["cand_flat"] = np.packbits(cm[:, 0].numpy(), axis=-1)
+    idx.image_bucket_constraint = True
+    router = types.SimpleNamespace(q_chunk=512)
+    itm, ipi, qpi = mdl._dash_page_ids(None, idx, tid, S)
+    bc = mdl._dash_block_cand(None, idx, router, pos, itm, ipi, qpi, nblk, B, S)
+    res["block_cand"] = np.packbits(bc.numpy(), axis=-1)
+    # positions that differ from the token index (a shifted window of queries)
+    pos2 = torch.clamp(torch.arange(S)[None].expand(B, -1) + 37, max=S + 20)
+    cm = sb.DeepseekV2Indexer._build_kl_candidate_mask(idx, pos2, nblk, itm, B, S, ipi, qpi)
+    res["cand_pos_shift"] = np.packbits(cm[:, 0].numpy(), axis=-1)
+
+    # ---- contiguous decoder: decode allow over a few decode steps ----
+    class _Cache:
+        def __init__(self):
+            self.n = 0
+
+        def get_seq_length(self):
+            return self.n
+    cache = _Cache()
+    L0 = 1300
+    ma._uocr_dash_decode_allow(idx, tid[:, :L0], cache)
+    st = cache._uocr_pg
+    res["dec_bmin"], res["dec_bmax"] = st["bmin"].numpy(), st["bmax"].numpy()
+    res["dec_pp"], res["dec_mcum"] = st["pp"].numpy(), st["mcum"].numpy()
+    cache.n = L0
+    steps = []
+    dec_ids = rng.integers(0, 1000, size=(6, B))
+    dec_ids[1, 0] = PG
+    dec_ids[3, :] = PG
+    dec_ids[4, 2] = PG
+    for k in range(dec_ids.shape[0]):
+        allow = ma._uocr_dash_decode_allow(idx, torch.tensor(dec_ids[k][:, None]), cache)
+        steps.append(np.packbits(allow.numpy(), axis=-1))
+        cache.n += 1
+    res["dec_ids"] = dec_ids
+    assert len({a.shape for a in steps}) == 1
+    res["dec_allow"] = np.stack(steps)
+
+    # ---- sglang serving trace ----
+    sbs, per = 16, 24
+    cfg = {"image_token_id": IMG, "page_token_id": PG, "per_page_image_tokens": per}
+    pst = ps.PageIsolationState(cfg, sbs)
+    P = 96
+    num_slots = P * sbs
+    perm = rng.permutation(P)
+    W = 24
+    R = 3
+    bt = np.zeros((R, W), np.int64)
+    for r in range(R):
+        bt[r] = perm[r * W:(r + 1) * W]
+    doc = [make_document_ids(rng, 200, n_pages=4, page_tokens=30, text_in_page=2,
+                             response_pages=0),
+           make_document_ids(rng, 170, n_pages=3, page_tokens=40, markers=False),
+           make_document_ids(rng, 190, n_pages=5, page_tokens=25, empty_pages=1,
+                             lead_images=7, response_pages=0)]
+    seg = doc[1][5:60]                                      # multimodal pad ids
+    seg[seg == IMG] = MM_PAD_SHIFT + 5
+    # steps: (per request: (start, n_tokens, ids)); extend steps first, then decodes
+    trace = []
+    lens = [0, 0, 0]
+    plan = [[120, 170, 150], [80, 0, 40], [1, 1, 1], [1, 1, 1], [1, 1, 1], [1, 1, 1]]
+    gen_ids = rng.integers(0, 1000, size=(4, R))
+    gen_ids[0, 0] = PG
+    gen_ids[1, 2] = PG
+    gen_ids[2, 1] = IMG
+    gen_ids[3, 0] = PG
+    for si, q_lens in enumerate(plan):
+        toks, starts, qs, rows = [], [], [0], []
+        n_dec = 0
+        for r in range(R):
+            n = q_lens[r]
+            if n == 0:
+                continue
+            if si >= 2:
+                t = [int(gen_ids[si - 2, r])]
+            else:
+                t = doc[r][lens[r]:lens[r] + n].tolist()
+            toks += t
+            starts.append(lens[r])
+            rows.append(r)
+            qs.append(qs[-1] + n)
+        nr = len(rows)
+        q_start = torch.tensor(qs, dtype=torch.int64)
+        start_pos = torch.tensor(starts, dtype=torch.int64)
+        btab = torch.tensor(bt[rows])
+        T = qs[-1]
+        gen_start = None
+        if si >= 2:
+            n_dec = T
+        layout = ps.BatchLayout(num_tokens=T, num_reqs=nr, q_start=q_start, start_pos=start_pos,
+                                block_table=btab, req_of_token=ps._req_of_token(q_start, T),
+                                num_decode_tokens=n_dec, gen_start=gen_start)
+        slots = []
+        for j, r in enumerate(rows):
+            for i in range(qs[j + 1] - qs[j]):
+                p = starts[j] + i
+                slots.append(int(bt[r, p // sbs]) * sbs + p % sbs)
+        slot_mapping = torch.tensor(slots, dtype=torch.int64)
+        ids_t = torch.tensor(toks, dtype=torch.int64)
+        q_page = pst.step(ids_t, layout, slot_mapping, num_slots).clone()
+        allow = pst.build_query_allow(layout, q_page, W, P).clone()
+        rec = {"rows": np.array(rows), "q_start": np.array(qs), "start_pos": np.array(starts),
+               "ids": np.array(toks), "slots": np.array(slots), "n_dec": n_dec,
+               "q_page": q_page.numpy(), "allow": allow.numpy(),
+               "slot_img_page": pst._slot_img_page.numpy().copy(),
+               "slot_marker_cum": pst._slot_marker_cum.numpy().copy(),
+               "slot_img_run": pst._slot_img_run.numpy().copy(),
+               "slot_prompt_pages": pst._slot_prompt_pages.numpy().copy()}
+        for j, r in enumerate(rows):
+            lens[r] += qs[j + 1] - qs[j]
+        if si >= 2:
+            seq_lens = torch.tensor([lens[r] for r in rows], dtype=torch.int32)
+            da_ = dm.decode_allow_fused(block_table=btab, page_state=pst, q_page=q_page,
+                                        seq_lens=seq_lens, max_block=W, num_blocks=P,
+                                        block_size=sbs)
+            rec["decode_allow"] = da_.numpy().copy()
+            lu = dm.local_union_fused(allow=da_, seq_lens=seq_lens,
+                                      out=torch.zeros(nr, W, dtype=torch.int8), max_block=W,
+                                      block_size=sbs, local_blocks=2)
+            rec["local_union"] = lu.numpy().copy()
+            rec["seq_lens"] = seq_lens.numpy()
+        trace.append(rec)
+    for i, rec in enumerate(trace):
+        for k, v in rec.items():
+            res[f"sg{i}_{k}"] = np.asarray(v)
+    np.savez_compressed(os.path.join(HERE, name + ".npz"), seed=seed, ids=ids, S=S, bs=bs,
+                        nblk=nblk, per_page=100, sg_bs=sbs, sg_per=per, sg_P=P, sg_W=W,
+                        sg_bt=bt, sg_steps=len(trace), **res)
+    print(name, "saved")
+
+
 def main():
     da, md = import_reference()
     torch.set_num_threads(os.cpu_count())
@@ -254,6 +457,7 @@ def main():
     decode_case(da, md, "decode_small", seed=3, B=4, H=2, S=1000, bs=64, lb=4, K=8, topm=8)
     paged_router_case("paged_router", seed=4)
     triton_interp_case(da, md, "triton_interp", seed=5)
+    page_aware_case("page_aware", seed=6)
 
 
 if __name__ == "__main__":
