@@ -117,11 +117,11 @@ __device__ __forceinline__ int block_excl_max(int v, int* swarp, int& total) {
 // Restates _sparse_base_impl.py:2189-2260 (rule 0) and
 // modeling_anantaocr.py:468-481 (rule 1).
 // ---------------------------------------------------------------------------
-constexpr int kIdThreads = 512;
+constexpr int kIdThreads = 256;
 constexpr int kIdPer = 8;
-constexpr int kIdTile = kIdThreads * kIdPer;   // 4096 tokens
+constexpr int kIdTile = kIdThreads * kIdPer;   // 2048 tokens
 constexpr int kIdCluster = 8;
-constexpr int kIdMaxTilesPerCta = 256;         // rows up to 8 * 256 * 4096 tokens
+constexpr int kIdMaxTilesPerCta = 512;         // rows up to 8 * 512 * 2048 tokens
 
 struct PgTile {
   int n_mark, n_img, last_img, mark_upto;      // last_img: position in the row or -1

@@ -270,7 +270,7 @@ __device__ __forceinline__ bool page_block_holds(const DashRouteArgs& a, int qp,
 template <int KW, int PER>
 __device__ __noinline__ void select_row(const DashRouteArgs& a, float* sx, uint32_t* scand,
                                         int* mid_, float* mx, int* mval, int64_t r, int s,
-                                        int lane) {
+                                        int lane, uint32_t* pc_cache) {
   const int W = a.width;
   const int Wp = (W + 31) & ~31;
   const uint32_t lt_mask = (1u << lane) - 1u;
@@ -278,12 +278,35 @@ __device__ __noinline__ void select_row(const DashRouteArgs& a, float* sx, uint3
   const uint8_t* cm = nullptr;
   if (a.cand && !a.page_q) cm = a.cand + (a.cand_per_seq ? (int64_t)s : r) * a.cand_row_stride;
   const int qp = a.page_q ? a.page_q[r] : -1;
+  // KW > 0: page candidacy of block lane + 32u in bit u, computed with
+  // independent loads and, with a cache (rows of one sequence handled by this
+  // warp), reused while the query page stays the same
+  uint32_t pcm = 0;
+  if constexpr (KW > 0) {
+    if (a.page_q) {
+      if (pc_cache && (int)pc_cache[32] == qp) {
+        pcm = pc_cache[lane];
+      } else {
+#pragma unroll
+        for (int u = 0; u < KW; ++u) {
+          const int b = lane + 32 * u;
+          if (b < W && page_block_holds(a, qp, s, b)) pcm |= 1u << u;
+        }
+        if (pc_cache) {
+          __syncwarp();
+          pc_cache[lane] = pcm;
+          if (lane == 0) pc_cache[32] = (uint32_t)qp;
+          __syncwarp();
+        }
+      }
+    }
+  }
   bool any = false;
   for (int b0 = 0; b0 < Wp; b0 += 32) {
     int b = b0 + lane;
     bool remote = b < W && sx[b] > kScoreNeg * 0.5f;
     bool c = remote;
-    if (a.page_q) c = remote && page_block_holds(a, qp, s, b);
+    if (a.page_q) c = remote && (KW > 0 ? ((pcm >> (b0 >> 5)) & 1u) != 0 : page_block_holds(a, qp, s, b));
     else if (cm) c = remote && cm[b] != 0;
     uint32_t bal = __ballot_sync(0xffffffffu, c);
     if (lane == 0) scand[b0 >> 5] = bal;
@@ -339,11 +362,32 @@ __device__ __noinline__ void select_row(const DashRouteArgs& a, float* sx, uint3
     uint32_t T = 0;
     int n_gt = 0;
     if (M < W) {
-      T = radix_threshold<KW>(kr, M);
-      int c = 0;
+      // Every non-candidate has x = kEntmaxNeg.  When the candidates fit the
+      // window and all lie above that value, the top-M is the candidates plus
+      // the lowest-id non-candidates: the threshold is that value's key (no
+      // select; rows restricted to a few blocks would otherwise resolve the
+      // long tie digit by digit).
+      int nc = 0;
+      bool low = false;
 #pragma unroll
-      for (int u = 0; u < KW; ++u) c += kr[u] > T ? 1 : 0;
-      n_gt = __reduce_add_sync(0xffffffffu, c);
+      for (int u = 0; u < KW; ++u) {
+        const int b = lane + 32 * u;
+        if (b < W && is_cand(b)) {
+          ++nc;
+          low |= !(xr[u] > kEntmaxNeg);
+        }
+      }
+      nc = __reduce_add_sync(0xffffffffu, nc);
+      if (nc <= M && !__any_sync(0xffffffffu, low)) {
+        T = order_key(kEntmaxNeg);
+        n_gt = nc;
+      } else {
+        T = radix_threshold<KW>(kr, M);
+        int c = 0;
+#pragma unroll
+        for (int u = 0; u < KW; ++u) c += kr[u] > T ? 1 : 0;
+        n_gt = __reduce_add_sync(0xffffffffu, c);
+      }
     }
     int ties_left = M - n_gt;
 #pragma unroll
@@ -495,23 +539,24 @@ __device__ __noinline__ void select_row(const DashRouteArgs& a, float* sx, uint3
 template <int KW>
 __device__ __forceinline__ void select_row_m(const DashRouteArgs& a, float* sx, uint32_t* scand,
                                              int* mid_, float* mx, int* mval, int64_t r, int s,
-                                             int lane) {
+                                             int lane, uint32_t* pc_cache) {
   const int W = a.width;
   const int M = a.topm > 0 ? min(a.topm, W) : W;
-  if (M <= 32) select_row<KW, 1>(a, sx, scand, mid_, mx, mval, r, s, lane);
-  else if (M <= 64) select_row<KW, 2>(a, sx, scand, mid_, mx, mval, r, s, lane);
-  else select_row<KW, kMaxM / 32>(a, sx, scand, mid_, mx, mval, r, s, lane);
+  if (M <= 32) select_row<KW, 1>(a, sx, scand, mid_, mx, mval, r, s, lane, pc_cache);
+  else if (M <= 64) select_row<KW, 2>(a, sx, scand, mid_, mx, mval, r, s, lane, pc_cache);
+  else select_row<KW, kMaxM / 32>(a, sx, scand, mid_, mx, mval, r, s, lane, pc_cache);
 }
 
 __device__ __forceinline__ void select_row_any(const DashRouteArgs& a, float* sx,
                                                uint32_t* scand, int* mid_, float* mx, int* mval,
-                                               int64_t r, int s, int lane) {
+                                               int64_t r, int s, int lane,
+                                               uint32_t* pc_cache = nullptr) {
   const int W = a.width;
-  if (W <= 160) select_row_m<5>(a, sx, scand, mid_, mx, mval, r, s, lane);
-  else if (W <= 256) select_row_m<8>(a, sx, scand, mid_, mx, mval, r, s, lane);
-  else if (W <= 512) select_row_m<16>(a, sx, scand, mid_, mx, mval, r, s, lane);
-  else if (W <= 1024) select_row_m<32>(a, sx, scand, mid_, mx, mval, r, s, lane);
-  else select_row_m<0>(a, sx, scand, mid_, mx, mval, r, s, lane);
+  if (W <= 160) select_row_m<5>(a, sx, scand, mid_, mx, mval, r, s, lane, pc_cache);
+  else if (W <= 256) select_row_m<8>(a, sx, scand, mid_, mx, mval, r, s, lane, pc_cache);
+  else if (W <= 512) select_row_m<16>(a, sx, scand, mid_, mx, mval, r, s, lane, pc_cache);
+  else if (W <= 1024) select_row_m<32>(a, sx, scand, mid_, mx, mval, r, s, lane, pc_cache);
+  else select_row_m<0>(a, sx, scand, mid_, mx, mval, r, s, lane, pc_cache);
 }
 
 // ---------------------------------------------------------------------------
@@ -521,13 +566,14 @@ __device__ __forceinline__ void select_row_any(const DashRouteArgs& a, float* sx
 // rows.  Every score is still one thread's sequential FMA chain.
 // ---------------------------------------------------------------------------
 constexpr int kTileRows = 32;
+constexpr int kPcCache = 33;   // per warp: page-candidacy mask per lane + the query page
 constexpr int kChunk = 64;
 constexpr int kLd = 132;   // padded fp32 row (conflict-free 16-byte loads)
 
 __host__ __device__ inline size_t route_tile_smem_floats(int W) {
   const int Wp = (W + 31) & ~31;
   return (size_t)kTileRows * kLd + (size_t)kChunk * kLd + kChunk + (size_t)kTileRows * Wp +
-         8 * ((size_t)Wp / 32 + 3 * kMaxM);
+         8 * ((size_t)Wp / 32 + 3 * kMaxM) + 8 * kPcCache;
 }
 
 __global__ void __launch_bounds__(256) route_tile_kernel(DashRouteArgs a, int tiles_per_seq) {
@@ -606,6 +652,9 @@ __global__ void __launch_bounds__(256) route_tile_kernel(DashRouteArgs a, int ti
     __syncthreads();
   }
   float* sel = selbase + warp * (Wp / 32 + 3 * kMaxM);
+  uint32_t* pc_cache = reinterpret_cast<uint32_t*>(selbase + 8 * (Wp / 32 + 3 * kMaxM)) + warp * kPcCache;
+  if (lane == 0) pc_cache[32] = 0x80000000u;   // no page cached (pages are >= -1)
+  __syncwarp();
   uint32_t* scand = reinterpret_cast<uint32_t*>(sel);
   int* mid_ = reinterpret_cast<int*>(scand + Wp / 32);
   float* mx = reinterpret_cast<float*>(mid_ + kMaxM);
@@ -616,7 +665,7 @@ __global__ void __launch_bounds__(256) route_tile_kernel(DashRouteArgs a, int ti
     if (a.scores_out)
       for (int b = lane; b < W; b += 32) a.scores_out[r * a.scores_out_stride + b] = sx[b];
     __syncwarp();
-    select_row_any(a, sx, scand, mid_, mx, mrank, r, s, lane);
+    select_row_any(a, sx, scand, mid_, mx, mrank, r, s, lane, pc_cache);
     __syncwarp();
   }
 }

@@ -66,7 +66,7 @@ def page_domain_from_ids(token_ids, *, image_token_id, page_token_id, per_page, 
     B, S = token_ids.shape
     r = page_ids(token_ids, image_token_id=image_token_id, page_token_id=page_token_id,
                  per_page=per_page, key_length=S, rule=0, page_scope_prefill=page_scope_prefill,
-                 block_size=block_size, n_blocks=nblk)
+                 block_size=block_size, n_blocks=nblk, want_image=False)
     return PageDomain(q_page=r["query_page"].view(-1), lo=r["lo"], hi=r["hi"], bits=r["bits"],
                       seq_rows=nblk)
 

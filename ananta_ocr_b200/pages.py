@@ -13,6 +13,7 @@ raises.
 """
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
 from typing import Optional
 
@@ -51,11 +52,12 @@ def page_ids(token_ids: torch.Tensor, *, image_token_id: int, page_token_id: Opt
              per_page: int, key_length: int, rule: int = 0, page_scope_prefill: bool = False,
              mm_pad_shift: int = 0, block_size: int = 0, n_blocks: int = 0,
              token_outputs: bool = True, page_dtype=torch.int32, bits: bool = True,
-             has_image: bool = False):
+             has_image: bool = False, want_image: bool = True):
     """One pass of ``dash_page_ids`` over token ids [B, >=0] (int64).
 
     Returns a dict: ``image_mask`` bool, ``image_page`` / ``query_page``
-    (``page_dtype``) [B, key_length] when ``token_outputs``; ``lo``/``hi``
+    (``page_dtype``) [B, key_length] when ``token_outputs`` (the first two
+    only with ``want_image``); ``lo``/``hi``
     int32 [B, n_blocks], ``bits`` int32 [B, n_blocks, words] and ``has_image``
     bool [B, n_blocks] when ``block_size``; ``prompt_pages``, ``marker_count``,
     ``n_image``, ``n_query`` int32 [B]."""
@@ -77,34 +79,52 @@ def page_ids(token_ids: torch.Tensor, *, image_token_id: int, page_token_id: Opt
     a.page_token_id = int(page_token_id) if page_token_id is not None else -1
     a.mm_pad_shift = int(mm_pad_shift)
     a.rule, a.page_scope_prefill = int(rule), int(bool(page_scope_prefill))
+    if token_outputs and page_dtype not in (torch.int32, torch.int64):
+        raise ValueError("page_dtype must be int32 or int64")
+    # every int32 output in one allocation: [query_page | image_page | lo | hi |
+    # bits | per-row x4] (int64 pages get their own)
+    w32 = page_dtype == torch.int32
+    words = _words(block_size) if block_size else 0
+    parts = []
+    if token_outputs and rule == 0 and w32:
+        parts.append(("query_page", (B, key_length)))
+    if token_outputs and want_image and w32:
+        parts.append(("image_page", (B, key_length)))
+    if block_size:
+        parts += [("lo", (B, n_blocks)), ("hi", (B, n_blocks))]
+        if bits:
+            parts.append(("bits", (B, n_blocks, words)))
+    parts.append(("rows", (4, B)))
+    n32 = sum(math.prod(sh) for _, sh in parts)
+    buf = torch.empty(n32, dtype=torch.int32, device=dev)
+    o = 0
+    for name, sh in parts:
+        n = math.prod(sh)
+        out[name] = buf[o:o + n].view(sh)
+        o += n
     if token_outputs:
-        if page_dtype not in (torch.int32, torch.int64):
-            raise ValueError("page_dtype must be int32 or int64")
-        a.page_elem_bytes = 8 if page_dtype == torch.int64 else 4
-        im = torch.empty(B, key_length, dtype=torch.bool, device=dev)
-        ip = torch.empty(B, key_length, dtype=page_dtype, device=dev)
-        a.image_mask, a.image_mask_stride = im.data_ptr(), key_length
-        a.image_page, a.image_page_stride = ip.data_ptr(), key_length
-        out["image_mask"], out["image_page"] = im, ip
+        a.page_elem_bytes = 4 if w32 else 8
+        if want_image:
+            im = torch.empty(B, key_length, dtype=torch.bool, device=dev)
+            if not w32:
+                out["image_page"] = torch.empty(B, key_length, dtype=page_dtype, device=dev)
+            a.image_mask, a.image_mask_stride = im.data_ptr(), key_length
+            a.image_page, a.image_page_stride = out["image_page"].data_ptr(), key_length
+            out["image_mask"] = im
         if rule == 0:
-            qp = torch.empty(B, key_length, dtype=page_dtype, device=dev)
-            a.query_page, a.query_page_stride = qp.data_ptr(), key_length
-            out["query_page"] = qp
+            if not w32:
+                out["query_page"] = torch.empty(B, key_length, dtype=page_dtype, device=dev)
+            a.query_page, a.query_page_stride = out["query_page"].data_ptr(), key_length
     if block_size:
         a.block_size, a.n_blocks = int(block_size), int(n_blocks)
-        lo = torch.empty(B, n_blocks, dtype=torch.int32, device=dev)
-        hi = torch.empty(B, n_blocks, dtype=torch.int32, device=dev)
-        a.blk_lo, a.blk_hi = lo.data_ptr(), hi.data_ptr()
-        out["lo"], out["hi"] = lo, hi
+        a.blk_lo, a.blk_hi = out["lo"].data_ptr(), out["hi"].data_ptr()
         if bits:
-            bt = torch.empty(B, n_blocks, _words(block_size), dtype=torch.int32, device=dev)
-            a.blk_bits = bt.data_ptr()
-            out["bits"] = bt
+            a.blk_bits = out["bits"].data_ptr()
         if has_image:
             hb = torch.empty(B, n_blocks, dtype=torch.bool, device=dev)
             a.blk_has_image = hb.data_ptr()
             out["has_image"] = hb
-    rows = torch.empty(4, B, dtype=torch.int32, device=dev)
+    rows = out.pop("rows")
     a.prompt_pages, a.marker_count = rows[0].data_ptr(), rows[1].data_ptr()
     a.n_image, a.n_query = rows[2].data_ptr(), rows[3].data_ptr()
     out["prompt_pages"], out["marker_count"], out["n_image"], out["n_query"] = rows.unbind(0)

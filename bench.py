@@ -43,6 +43,7 @@ C4 = dict(name="config4_longdoc_prefill_bf16", B=8, H=16, S=131072, D=128, bs=12
           n_pages=480, page_tokens=273, off_std=0.2)
 C3 = dict(name="config3_decode_bf16", R=64, H=10, S=27556, D=128, bs=64, lb=4, K=32)
 IDX_SCALE = 128.0 / math.sqrt(128)
+IMAGE_TOKEN_ID, PAGE_TOKEN_ID = 128815, 128827   # config.json:156,160
 
 
 def load_peaks():
@@ -103,6 +104,131 @@ class ClockSampler:
                         reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
                 "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def page_cpu_baseline(cfg, threads=None):
+    """Reference candidate-domain path (page ids + per-query same-page block
+    mask, the numpy restatement in oracle/page_oracle.py) for one sequence."""
+    import numpy as np
+    from oracle import page_oracle as PO
+    ids = document_ids_np(cfg, 0)[:1]
+    S, bs = cfg["S"], cfg["bs"]
+    nblk = -(-S // bs)
+    t0 = time.perf_counter()
+    itm, ipi, qpi, _, _ = PO.page_aware_ids(ids, IMAGE_TOKEN_ID, PAGE_TOKEN_ID,
+                                            cfg["page_tokens"], S, True)
+    PO.kl_candidate_mask(np.arange(S)[None], nblk, itm, bs, True, ipi, qpi)
+    dt = time.perf_counter() - t0
+    return dict(value=S / dt, unit="tokens/s", cores=1, kind="port",
+                sample=f"1 sequence x {S} query tokens of {cfg['name']} (page ids + same-page "
+                       f"candidate mask), oracle/page_oracle.py", seconds=dt)
+
+
+# ---------------------------------------------------------------------------
+# synthetic OCR documents: pages of [<PAGE>] + image tokens, then a text tail
+# carrying two response-page markers
+# ---------------------------------------------------------------------------
+def _doc_layout(cfg):
+    P, pt, S = cfg["n_pages"], cfg["page_tokens"], cfg["S"]
+    tail = P * pt
+    return P, pt, S, [tail + o for o in (64, 256) if tail + o < S]
+
+
+def document_ids(cfg, dev, seed):
+    import torch
+    P, pt, S, marks = _doc_layout(cfg)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    ids = torch.randint(0, 100_000, (cfg["B"], S), generator=g, device=dev)
+    for p in range(P):
+        a = p * pt
+        if a >= S:
+            break
+        ids[:, a] = PAGE_TOKEN_ID
+        ids[:, a + 1:min(S, a + pt)] = IMAGE_TOKEN_ID
+    for m in marks:
+        ids[:, m] = PAGE_TOKEN_ID
+    return ids
+
+
+def document_ids_np(cfg, seed):
+    import numpy as np
+    P, pt, S, marks = _doc_layout(cfg)
+    ids = np.random.default_rng(seed).integers(0, 100_000, (cfg["B"], S))
+    for p in range(P):
+        a = p * pt
+        if a >= S:
+            break
+        ids[:, a] = PAGE_TOKEN_ID
+        ids[:, a + 1:min(S, a + pt)] = IMAGE_TOKEN_ID
+    for m in marks:
+        ids[:, m] = PAGE_TOKEN_ID
+    return ids
+
+
+def run_page_aware(cfg, st, dev, steps, warmup):
+    """Page-aware routing of the prefill workload (every query on its own
+    page): the page-id pass, the router with the compact domain, the router
+    without candidates, and the dense-mask alternative, each timed alone."""
+    import torch
+    from ananta_ocr_b200 import ops, pages
+    from ananta_ocr_b200 import modeling_deepseekv2 as MD
+    B, S, bs, lb, K = (cfg[x] for x in ("B", "S", "bs", "lb", "K"))
+    nblk = -(-S // bs)
+    ids = document_ids(cfg, dev, 99)
+    seqs = ops.Seqs(n_seq=B, q_len=S, kv_len=S, max_q_len=S)
+    oi = torch.empty(B * S, K, dtype=torch.int32, device=dev)
+    ob = torch.empty(B * S, K, dtype=torch.float32, device=dev)
+    kw = dict(width=nblk, block_size=bs, local_blocks=lb, idx_scale=IDX_SCALE, prior_floor=1e-4,
+              sigma=1.0, topm=K, K=K, idx_q=st["iq"].view(B * S, 128), kbar=st["ws"]["kbar"],
+              out_idx=oi, out_bias=ob)
+
+    def ids_fn():
+        return MD.page_domain_from_ids(ids, image_token_id=IMAGE_TOKEN_ID,
+                                       page_token_id=PAGE_TOKEN_ID, per_page=cfg["page_tokens"],
+                                       block_size=bs, nblk=nblk, page_scope_prefill=True)
+    dom = ids_fn()
+    cand = pages.page_allow(dom.q_page, dom.lo, dom.hi, bits=dom.bits, width=nblk, rows=B * S,
+                            rows_per_seq=S, fallback=True)
+    fns = {
+        "page_ids": ids_fn,
+        "route_page": lambda: ops.route(seqs, page=dom, **kw),
+        "route_plain": lambda: ops.route(seqs, **kw),
+        "dense_mask": lambda: pages.page_allow(dom.q_page, dom.lo, dom.hi, bits=dom.bits,
+                                               width=nblk, rows=B * S, rows_per_seq=S,
+                                               fallback=True, out=cand),
+        "route_dense": lambda: ops.route(seqs, cand=cand, **kw),
+    }
+    res = {}
+    for name, fn in fns.items():
+        # replayed from a CUDA graph so the figure is device time, not the
+        # host's launch cost
+        for _ in range(max(3, warmup)):
+            fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        res[name] = e0.elapsed_time(e1) / steps
+        del graph
+    # the routes the page domain gives are those of the dense mask
+    ops.route(seqs, page=dom, **kw)
+    i1, b1 = oi.clone(), ob.clone()
+    ops.route(seqs, cand=cand, **kw)
+    same = bool(torch.equal(i1, oi) and torch.equal(b1, ob))
+    constrained = int((dom.q_page >= 0).sum())
+    words = dom.bits.shape[-1]
+    ids_bytes = B * S * (8 + 4) + B * nblk * (8 + 4 * words) + 16 * B
+    return dict(ms=res, equal_to_dense=same, rows=B * S, rows_with_page=constrained,
+                page_ids_bytes=ids_bytes)
 
 
 # ---------------------------------------------------------------------------
@@ -384,6 +510,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-pages", action="store_true",
+                    help="skip the page-aware routing measurement")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch eagerly instead of replaying captured CUDA graphs")
     ap.add_argument("--decode-rows", type=int, default=0,
@@ -580,6 +708,10 @@ def main():
         e2e = {"value": tokens_per_rank * world / (e2e_ms / 1e3), "unit": "tokens/s",
                "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
+    page_res = None
+    if not args.no_pages and args.workload == "c2":
+        page_res = run_page_aware(cfg, st, dev, args.steps, args.warmup)
+
     peaks, peak_kind = load_peaks()
     if rank != 0:
         if world > 1:
@@ -624,6 +756,26 @@ def main():
                                        "unit": "GB/s", "frac": attn_gbs / hbm,
                                        "kernel": "decode_kernel, K+V bytes of attended keys",
                                        "peak_source": f"{peak_kind} hbm_gbs"}}
+    if page_res is not None:
+        hbm = peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
+        ms = page_res["ms"]
+        gbs = page_res["page_ids_bytes"] / ms["page_ids"] / 1e6
+        line["page_aware"] = {
+            "workload": cfg["name"] + " + page-aware candidates (page_scope_prefill)",
+            "ms": ms, "route_overhead_ms": ms["route_page"] - ms["route_plain"],
+            "dense_path_ms": ms["dense_mask"] + ms["route_dense"],
+            "compact_path_ms": ms["page_ids"] + ms["route_page"],
+            "rows": page_res["rows"], "rows_with_page": page_res["rows_with_page"],
+            "routes_equal_dense": page_res["equal_to_dense"],
+            "l2": "inputs L2-resident (token ids 0.3 MB)",
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                         "frac": gbs / hbm, "kernel": "page_ids_kernel, ids in + pages out",
+                         "bytes_per_launch": page_res["page_ids_bytes"],
+                         "peak_source": f"{peak_kind} hbm_gbs"}}
+        if not args.no_cpu and world == 1:
+            pc = page_cpu_baseline(cfg)
+            pc.pop("seconds", None)
+            line["page_aware"]["cpu_baseline"] = pc
     if e2e is not None:
         line["e2e"] = e2e
     if not args.no_cpu and world == 1:   # the CPU baseline is timed at N = 1 only

@@ -111,11 +111,11 @@ def page_aware_image_block_mask(image_token_page_ids, query_token_page_ids, pos_
     qp = np.take_along_axis(qp_all, pos, 1)
     kp = page_blocks(image_token_page_ids, num_key_blocks, block_size)
     out = np.zeros(qp.shape + (num_key_blocks,), bool)
-    for b in range(qp.shape[0]):
-        for c in range(qp.shape[1]):
-            q = qp[b, c]
-            if q >= 0:
-                out[b, c] = (kp[b] == q).any(-1)
+    step = 256                                   # query chunks, as the reference's q_chunk
+    for c0 in range(0, qp.shape[1], step):
+        q = qp[:, c0:c0 + step]
+        out[:, c0:c0 + step] = ((kp[:, None] == q[:, :, None, None]).any(-1)
+                                & (q >= 0)[:, :, None])
     return out
 
 
