@@ -159,10 +159,19 @@ class DashPageBlocksArgs(C.Structure):
                 ("lo", _p), ("hi", _p), ("bits", _p)]
 
 
+class DashIndexProjArgs(C.Structure):
+    _fields_ = [("hidden", _p), ("hidden_stride", _i64), ("w_q", _p), ("w_k", _p),
+                ("w_stride", _i64), ("norm_q", _p), ("norm_k", _p), ("cos", _p), ("sin", _p),
+                ("cs_stride", _i64), ("eps", _f32), ("norm_clamp", _i32), ("T", _i32),
+                ("hidden_dim", _i32), ("d", _i32), ("k_dtype", _i32), ("idx_q", _p),
+                ("q_stride", _i64), ("idx_k", _p), ("k_stride", _i64), ("slot_mapping", _p),
+                ("k_rows", _i64), ("device_error", _p)]
+
+
 ABI_ORDER = [DashSeqs, DashKV, DashRoutes, DashQO, DashKbarArgs, DashRouteArgs,
              DashBlockMaxArgs, DashPrefillArgs, DashDecodeArgs, DashDeviceError,
              DashPageIdsArgs, DashPageStateArgs, DashPageAllowArgs, DashPageDecodeArgs,
-             DashBlockAnyArgs, DashPageBlocksArgs]
+             DashBlockAnyArgs, DashPageBlocksArgs, DashIndexProjArgs]
 
 # every function the header declares
 EXPORTS = [
@@ -171,7 +180,7 @@ EXPORTS = [
     "dash_library_version", "dash_count_launches", "dash_abi_sizes",
     "dash_decode_attn_noalloc", "dash_noalloc_scratch_bytes", "dash_selftest_bounded_wait",
     "dash_page_ids", "dash_page_state_step", "dash_page_allow", "dash_page_decode_query",
-    "dash_block_any", "dash_page_blocks",
+    "dash_block_any", "dash_page_blocks", "dash_index_proj",
 ]
 
 
@@ -206,6 +215,7 @@ def load(path: str = LIB_PATH):
         ("dash_page_decode_query", [C.POINTER(DashPageDecodeArgs), _p]),
         ("dash_block_any", [C.POINTER(DashBlockAnyArgs), _p]),
         ("dash_page_blocks", [C.POINTER(DashPageBlocksArgs), _p]),
+        ("dash_index_proj", [C.POINTER(DashIndexProjArgs), _p]),
     ]:
         f = getattr(L, name)
         f.argtypes = args

@@ -105,16 +105,17 @@ int dash_count_launches(int reset) {
 }
 
 int dash_abi_sizes(int64_t* out, int n) {
-  const int64_t s[16] = {(int64_t)sizeof(DashSeqs),           (int64_t)sizeof(DashKV),
+  const int64_t s[17] = {(int64_t)sizeof(DashSeqs),           (int64_t)sizeof(DashKV),
                          (int64_t)sizeof(DashRoutes),         (int64_t)sizeof(DashQO),
                          (int64_t)sizeof(DashKbarArgs),       (int64_t)sizeof(DashRouteArgs),
                          (int64_t)sizeof(DashBlockMaxArgs),   (int64_t)sizeof(DashPrefillArgs),
                          (int64_t)sizeof(DashDecodeArgs),     (int64_t)sizeof(DashDeviceError),
                          (int64_t)sizeof(DashPageIdsArgs),    (int64_t)sizeof(DashPageStateArgs),
                          (int64_t)sizeof(DashPageAllowArgs),  (int64_t)sizeof(DashPageDecodeArgs),
-                         (int64_t)sizeof(DashBlockAnyArgs),   (int64_t)sizeof(DashPageBlocksArgs)};
-  for (int i = 0; i < n && i < 16; ++i) out[i] = s[i];
-  return 16;
+                         (int64_t)sizeof(DashBlockAnyArgs),   (int64_t)sizeof(DashPageBlocksArgs),
+                         (int64_t)sizeof(DashIndexProjArgs)};
+  for (int i = 0; i < n && i < 17; ++i) out[i] = s[i];
+  return 17;
 }
 
 int dash_kbar_pool(const DashKbarArgs* a, dash_stream_t stream) {
@@ -288,6 +289,33 @@ int dash_page_blocks(const DashPageBlocksArgs* a, dash_stream_t stream) {
   if (a->rows > 0 && a->n_blocks > 0 && (!a->lo || !a->hi || (a->len > 0 && !a->pages)))
     return set_error(DASH_ERR_INVALID, "null pages/lo/hi");
   return launch_page_blocks(*a, (cudaStream_t)stream);
+}
+
+int dash_index_proj(const DashIndexProjArgs* a, dash_stream_t stream) {
+  if (!a) return set_error(DASH_ERR_INVALID, "null args");
+  if (a->T < 0) return set_error(DASH_ERR_INVALID, "T < 0");
+  if (a->T == 0) return DASH_OK;
+  if (a->d != 128) return set_error(DASH_ERR_UNSUPPORTED, "index dim %d != 128", a->d);
+  if (a->hidden_dim <= 0 || a->hidden_dim % 64)
+    return set_error(DASH_ERR_UNSUPPORTED, "hidden_dim %d must be a positive multiple of 64", a->hidden_dim);
+  if (!a->hidden || !a->w_q || !a->w_k || !a->norm_q || !a->norm_k || !a->idx_q || !a->idx_k)
+    return set_error(DASH_ERR_INVALID, "null pointer");
+  if (!aligned16(a->hidden) || !aligned16(a->w_q) || !aligned16(a->w_k))
+    return set_error(DASH_ERR_INVALID, "hidden and weights must be 16-byte aligned");
+  if (a->hidden_stride < a->hidden_dim || a->hidden_stride % 8 || a->w_stride < a->hidden_dim || a->w_stride % 8)
+    return set_error(DASH_ERR_INVALID, "hidden / weight row strides must cover hidden_dim and be multiples of 8");
+  if (!a->cos != !a->sin) return set_error(DASH_ERR_INVALID, "cos and sin go together");
+  if (a->cos && (!aligned16(a->cos) || !aligned16(a->sin) || a->cs_stride % 8 || a->cs_stride < a->d))
+    return set_error(DASH_ERR_INVALID, "cos/sin must be 16-byte aligned with a row stride multiple of 8 >= d");
+  if (a->k_dtype != DASH_DTYPE_F32 && a->k_dtype != DASH_DTYPE_BF16)
+    return set_error(DASH_ERR_UNSUPPORTED, "idx_k dtype must be fp32 or bf16");
+  if (a->slot_mapping && a->k_rows <= 0) return set_error(DASH_ERR_INVALID, "k_rows must be > 0 with slot_mapping");
+  if (!aligned16(a->idx_q) || a->q_stride % 4 || a->q_stride < a->d)
+    return set_error(DASH_ERR_INVALID, "idx_q must be 16-byte aligned with a row stride multiple of 4 >= d");
+  if ((reinterpret_cast<uintptr_t>(a->idx_k) & (a->k_dtype == DASH_DTYPE_BF16 ? 7 : 15)) || a->k_stride % 4 ||
+      a->k_stride < a->d)
+    return set_error(DASH_ERR_INVALID, "idx_k rows must be aligned for vector stores (row stride multiple of 4 >= d)");
+  return launch_index_proj(*a, (cudaStream_t)stream);
 }
 
 int dash_page_decode_query(const DashPageDecodeArgs* a, dash_stream_t stream) {

@@ -8,6 +8,8 @@ libdash_b200.so:
   1.5-entmax over the top-``topm`` scores, top-K selection, centred bias.
 * ``_decode_attend`` (modeling_deepseekv2.py:424-451): decode gather attention
   over a contiguous cache.
+* ``_router_qk`` (modeling_deepseekv2.py:336-348): the router's index
+  projections + RMSNorm + RoPE as one tcgen05 GEMM with a fused epilogue.
 * ``dash_prefill_forward``: the ``_infer_prefill_attend`` flow
   (modeling_deepseekv2.py:403-421) after the router projections: scores ->
   selection -> gather attention, with the routed lists kept on the device;
@@ -69,6 +71,27 @@ def page_domain_from_ids(token_ids, *, image_token_id, page_token_id, per_page, 
                  block_size=block_size, n_blocks=nblk, want_image=False)
     return PageDomain(q_page=r["query_page"].view(-1), lo=r["lo"], hi=r["hi"], bits=r["bits"],
                       seq_rows=nblk)
+
+
+@torch.no_grad()
+def _router_qk(router, hidden_states, pe):
+    """modeling_deepseekv2.py:336-348: router index q/k [B, S, d] fp32 =
+    RoPE(_RMSNorm(W hidden)) in one tcgen05 kernel (bf16 GEMM, fp32
+    accumulate, the reference's bf16 roundings in the epilogue).  Non-finite
+    hidden values are not zeroed before the GEMM (rows holding them come out
+    zeroed by the norm instead)."""
+    B, S, Hd = hidden_states.shape
+    d = router.index_dim
+    cos = sin = None
+    if pe is not None:
+        cos, sin = pe
+        cos = cos.expand(B, S, cos.shape[-1]).reshape(B * S, cos.shape[-1])[:, :d]
+        sin = sin.expand(B, S, sin.shape[-1]).reshape(B * S, sin.shape[-1])[:, :d]
+    idx_q, idx_k = ops.index_proj(hidden_states.reshape(B * S, Hd), router.q_proj.weight,
+                                  router.k_proj.weight, router.q_norm.weight,
+                                  router.k_norm.weight, float(router.q_norm.eps), cos=cos,
+                                  sin=sin, norm_clamp=True)
+    return idx_q.view(B, S, d), idx_k.view(B, S, d)
 
 
 @torch.no_grad()

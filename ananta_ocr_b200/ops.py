@@ -360,3 +360,61 @@ def gather_attention(q, k, v, idx, bias, *, block_size: int, local_window: int, 
     a.device_error = device_error.ptr if device_error is not None else None
     prefill_attn(a, q.device, workspace)
     return out
+
+
+# ---------------------------------------------------------------------------
+# router front end
+# ---------------------------------------------------------------------------
+def index_proj(hidden: torch.Tensor, w_q: torch.Tensor, w_k: torch.Tensor,
+               norm_q: torch.Tensor, norm_k: torch.Tensor, eps: float, *,
+               cos: Optional[torch.Tensor] = None, sin: Optional[torch.Tensor] = None,
+               norm_clamp: bool = False, idx_q: Optional[torch.Tensor] = None,
+               idx_k: Optional[torch.Tensor] = None, slot_mapping: Optional[torch.Tensor] = None,
+               device_error: Optional[DeviceErrorWord] = None):
+    """Index projections + RMSNorm + RoPE on tcgen05 (``dash_index_proj``).
+
+    hidden [T, hidden_dim] bf16; w_q/w_k [128, hidden_dim] bf16 (nn.Linear
+    weights); norm_q/norm_k [128] (Gemma weights, scale 1 + w); cos/sin
+    [T, >=128] bf16 or None.  Returns (idx_q [T, 128] fp32, idx_k): idx_k is
+    [T, 128] fp32 unless ``idx_k`` is given -- with ``slot_mapping`` [T] int64
+    it is a cache of rows [num_slots, 128] (fp32 or bf16) written at the
+    tokens' slots."""
+    _need_cuda(hidden, w_q, w_k, cos, sin, idx_k, slot_mapping)
+    if hidden.dtype != torch.bfloat16 or w_q.dtype != torch.bfloat16 or w_k.dtype != torch.bfloat16:
+        raise NotImplementedError("index projections run on bf16 hidden states and weights")
+    T, Hd = hidden.shape
+    dev = hidden.device
+    if hidden.stride(-1) != 1:
+        hidden = hidden.contiguous()
+    w_q = w_q if w_q.stride(-1) == 1 else w_q.contiguous()
+    w_k = w_k if w_k.stride(-1) == 1 else w_k.contiguous()
+    if w_q.stride(0) != w_k.stride(0):
+        w_k = w_k.contiguous()
+        w_q = w_q.contiguous()
+    nq = norm_q.to(device=dev, dtype=torch.float32).contiguous()
+    nk = norm_k.to(device=dev, dtype=torch.float32).contiguous()
+    if idx_q is None:
+        idx_q = torch.empty(T, w_q.shape[0], dtype=torch.float32, device=dev)
+    if idx_k is None:
+        idx_k = torch.empty(T, w_k.shape[0], dtype=torch.float32, device=dev)
+    a = L.DashIndexProjArgs()
+    a.hidden, a.hidden_stride = hidden.data_ptr(), hidden.stride(0)
+    a.w_q, a.w_k, a.w_stride = w_q.data_ptr(), w_k.data_ptr(), w_q.stride(0)
+    a.norm_q, a.norm_k = nq.data_ptr(), nk.data_ptr()
+    if cos is not None:
+        if cos.dtype != torch.bfloat16 or sin.dtype != torch.bfloat16:
+            raise NotImplementedError("cos/sin must be bf16 (the model dtype)")
+        if cos.stride(-1) != 1 or sin.stride(-1) != 1 or cos.stride(0) != sin.stride(0):
+            cos, sin = cos.contiguous(), sin.contiguous()
+        a.cos, a.sin, a.cs_stride = cos.data_ptr(), sin.data_ptr(), cos.stride(0)
+    a.eps, a.norm_clamp = float(eps), int(bool(norm_clamp))
+    a.T, a.hidden_dim, a.d = T, Hd, w_q.shape[0]
+    a.k_dtype = _DT[idx_k.dtype]
+    a.idx_q, a.q_stride = idx_q.data_ptr(), idx_q.stride(0)
+    a.idx_k, a.k_stride = idx_k.data_ptr(), idx_k.stride(0)
+    if slot_mapping is not None:
+        sm = slot_mapping if slot_mapping.dtype == torch.int64 else slot_mapping.to(torch.int64)
+        a.slot_mapping, a.k_rows = sm.contiguous().data_ptr(), idx_k.shape[0]
+    a.device_error = device_error.ptr if device_error is not None else None
+    L.call("dash_index_proj", a)
+    return idx_q, idx_k

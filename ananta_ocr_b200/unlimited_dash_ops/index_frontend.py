@@ -1,0 +1,38 @@
+"""Serving-side router front end, backed by libdash_b200.so.
+
+``index_qk_fused`` is the index branch of WHL unlimited_ocr_v2.py:145-162
+(``index_q_proj`` / ``index_k_proj`` + ``GemmaRMSNorm`` x2 +
+``apply_page2d_rope_pair`` on the index cos/sin table) followed by the index-K
+store of WHL memory_pool.py:5573-5591 (``set_index_k_buffer``), as one tcgen05
+kernel: the GEMM accumulates in TMEM and the epilogue normalises, rotates and
+writes idx_q (fp32, the router's input) and idx_k straight into the paged index
+cache at ``slot_mapping``.  The k-bar tail refresh stays a separate launch
+(``route_triton.kbar_refresh_tail_triton``): a page's summary depends on tokens
+other CTAs write.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from .. import ops
+
+
+@torch.no_grad()
+def index_qk_fused(hidden_states: torch.Tensor, index_q_weight: torch.Tensor,
+                   index_k_weight: torch.Tensor, q_norm_weight: torch.Tensor,
+                   k_norm_weight: torch.Tensor, eps: float, cos: Optional[torch.Tensor] = None,
+                   sin: Optional[torch.Tensor] = None, *, index_cache: Optional[torch.Tensor] = None,
+                   slot_mapping: Optional[torch.Tensor] = None, idx_q_out=None):
+    """Returns (idx_q [T, 128] fp32, idx_k).  With ``index_cache`` ([pages,
+    page_size, 128] or [slots, 128], fp32 or bf16) and ``slot_mapping``, idx_k
+    is written into the cache rows and the cache is returned."""
+    T = hidden_states.shape[0]
+    kout = None
+    if index_cache is not None:
+        kout = index_cache.view(-1, index_cache.shape[-1])
+    q, k = ops.index_proj(hidden_states.reshape(T, -1), index_q_weight, index_k_weight,
+                          q_norm_weight, k_norm_weight, eps, cos=cos, sin=sin, norm_clamp=False,
+                          idx_q=idx_q_out, idx_k=kout, slot_mapping=slot_mapping)
+    return q, (index_cache if index_cache is not None else k)

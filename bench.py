@@ -231,6 +231,69 @@ def run_page_aware(cfg, st, dev, steps, warmup):
                 page_ids_bytes=ids_bytes)
 
 
+def run_frontend(cfg, dev, steps, warmup):
+    """Router front end of the prefill workload: index projections (hidden
+    1280 -> 2 x 128) + RMSNorm + RoPE for every token, one tcgen05 kernel,
+    against the same computation as PyTorch ops (cuBLAS GEMMs + elementwise).
+    Device time of CUDA-graph replays; L2 is flushed before every timed
+    replay (the 95 MB hidden input would otherwise stay in the 126 MB L2)."""
+    import torch
+    from ananta_ocr_b200 import ops
+    T, Hd, d = cfg["B"] * cfg["S"], 1280, 128
+    g = torch.Generator(device=dev).manual_seed(123)
+    h = torch.randn(T, Hd, generator=g, device=dev).to(torch.bfloat16)
+    wq = (torch.randn(d, Hd, generator=g, device=dev) / math.sqrt(Hd)).to(torch.bfloat16)
+    wk = (torch.randn(d, Hd, generator=g, device=dev) / math.sqrt(Hd)).to(torch.bfloat16)
+    nq = torch.randn(d, generator=g, device=dev) * 0.1
+    nk = torch.randn(d, generator=g, device=dev) * 0.1
+    pos = torch.arange(T, device=dev, dtype=torch.float32)[:, None] % cfg["S"]
+    inv = 1.0 / (10000.0 ** (torch.arange(0, d // 2, device=dev).float() / (d // 2)))
+    emb = torch.cat([pos * inv, pos * inv], -1)
+    cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+    iq = torch.empty(T, d, device=dev)
+    ik = torch.empty(T, d, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def ours():
+        ops.index_proj(h, wq, wk, nq, nk, 1e-6, cos=cos, sin=sin, idx_q=iq, idx_k=ik)
+
+    def torch_path():
+        hq = torch.nn.functional.linear(h, wq)
+        hk = torch.nn.functional.linear(h, wk)
+        outs = []
+        for x, w in ((hq, nq), (hk, nk)):
+            x32 = x.float()
+            x32 = x32 * torch.rsqrt(x32.pow(2).mean(-1, keepdim=True) + 1e-6)
+            y = (x32 * (1.0 + w)).to(torch.bfloat16)
+            rot = torch.cat((-y[:, d // 2:], y[:, :d // 2]), -1)
+            outs.append((y * cos + rot * sin).float())
+        return outs
+
+    res = {}
+    for name, fn in (("index_proj", ours), ("torch_ops", torch_path)):
+        for _ in range(max(3, warmup)):
+            fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        times = []
+        for i in range(3 + steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            if i >= 3:
+                times.append(e0.elapsed_time(e1))
+        res[name] = statistics.median(times)
+        del graph
+    nbytes = T * Hd * 2 + 2 * d * Hd * 2 + 2 * T * d * 4 + 2 * T * d * 2
+    flops = 2.0 * T * Hd * 2 * d
+    return dict(ms=res, tokens=T, bytes=nbytes, flops=flops)
+
+
 # ---------------------------------------------------------------------------
 # workload construction (device-side, seeded)
 # ---------------------------------------------------------------------------
@@ -512,6 +575,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-pages", action="store_true",
                     help="skip the page-aware routing measurement")
+    ap.add_argument("--no-frontend", action="store_true",
+                    help="skip the router front-end measurement")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch eagerly instead of replaying captured CUDA graphs")
     ap.add_argument("--decode-rows", type=int, default=0,
@@ -711,6 +776,9 @@ def main():
     page_res = None
     if not args.no_pages and args.workload == "c2":
         page_res = run_page_aware(cfg, st, dev, args.steps, args.warmup)
+    fe_res = None
+    if not args.no_frontend and args.workload == "c2":
+        fe_res = run_frontend(cfg, dev, args.steps, args.warmup)
 
     peaks, peak_kind = load_peaks()
     if rank != 0:
@@ -776,6 +844,20 @@ def main():
             pc = page_cpu_baseline(cfg)
             pc.pop("seconds", None)
             line["page_aware"]["cpu_baseline"] = pc
+    if fe_res is not None:
+        hbm = peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
+        ms = fe_res["ms"]["index_proj"]
+        gbs = fe_res["bytes"] / ms / 1e6
+        line["frontend"] = {
+            "workload": cfg["name"] + " router front end (hidden 1280 -> index q, k; RMSNorm; RoPE)",
+            "ms": fe_res["ms"], "tokens_per_s": fe_res["tokens"] / (ms / 1e3),
+            "tflops": fe_res["flops"] / (ms / 1e3) / 1e12,
+            "l2": "flushed before every timed replay",
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                         "frac": gbs / hbm, "kernel": "index_proj_kernel, hidden + weights in, "
+                                                      "q/k fp32 out, cos/sin in",
+                         "bytes_per_launch": fe_res["bytes"],
+                         "peak_source": f"{peak_kind} hbm_gbs"}}
     if e2e is not None:
         line["e2e"] = e2e
     if not args.no_cpu and world == 1:   # the CPU baseline is timed at N = 1 only

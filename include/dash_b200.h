@@ -523,6 +523,45 @@ int dash_decode_attn_noalloc(const DashDecodeArgs* args, dash_stream_t stream);
 size_t dash_noalloc_scratch_bytes(void);
 
 /* ---------------------------------------------------------------------- */
+/* Router front end: index projections + RMSNorm + RoPE (+ index-K write).
+ * Replaces: modeling_deepseekv2.py:336-348 (_router_qk) with the _RMSNorm of
+ *           dash_attention.py:680-700 (norm_clamp = 1), and WHL
+ *           unlimited_ocr_v2.py:145-162 (index_q/k_proj + GemmaRMSNorm +
+ *           apply_page2d_rope_pair of WHL page2d_rope.py:130-141 / :233-257,
+ *           norm_clamp = 0) with the index-K store of WHL
+ *           memory_pool.py:5573-5591 (set_index_k_buffer).
+ * Per token t (row of hidden [T, hidden_dim] bf16):
+ *   xq = bf16(hidden[t] . w_q^T), xk likewise (bf16 GEMM, fp32 accumulate);
+ *   y = bf16((x * rsqrt(mean(x^2) + eps)) * (1 + norm_w))      (norm_clamp = 0)
+ *       with x non-finite -> 0 and clamps to +-1e4 after each product when
+ *       norm_clamp = 1;
+ *   RoPE (cos/sin [T, d] bf16, optional), rotate-half pairs (j, j + d/2),
+ *   each product and the sum rounded to bf16 (the reference's bf16 ops):
+ *       o_j = bf16(bf16(y_j cos_j) + bf16(rot_j sin_j)), rot = (-y_hi, y_lo);
+ *   idx_q[t] = o_q (fp32); idx_k row (slot_mapping ? slot_mapping[t] : t) = o_k
+ *   (fp32 or bf16).  d = 128, hidden_dim a multiple of 64 (>= 64).           */
+typedef struct {
+  const void* hidden; int64_t hidden_stride;   /* bf16, elements */
+  const void* w_q; const void* w_k;            /* bf16 [d, hidden_dim] (nn.Linear weights) */
+  int64_t w_stride;
+  const float* norm_q; const float* norm_k;    /* [d] */
+  const void* cos; const void* sin;            /* bf16 [T, cs_stride] or NULL (no RoPE) */
+  int64_t cs_stride;
+  float eps;
+  int32_t norm_clamp;
+  int32_t T;
+  int32_t hidden_dim;
+  int32_t d;
+  int32_t k_dtype;                             /* DASH_DTYPE_F32 or DASH_DTYPE_BF16 */
+  float* idx_q; int64_t q_stride;              /* [T, d] fp32 */
+  void* idx_k; int64_t k_stride;               /* rows of d */
+  const int64_t* slot_mapping;                 /* optional [T] */
+  int64_t k_rows;                              /* rows addressable through slot_mapping */
+  DashDeviceError* device_error;
+} DashIndexProjArgs;
+int dash_index_proj(const DashIndexProjArgs* args, dash_stream_t stream);
+
+/* ---------------------------------------------------------------------- */
 /* Diagnostics */
 int dash_last_error(char* buf, int len);     /* copies the last host-side error message */
 int dash_library_version(void);              /* (major << 16) | minor */
@@ -530,7 +569,8 @@ int dash_count_launches(int reset);          /* kernels launched by this library
 /* sizeof() of the argument structs, in this order: DashSeqs, DashKV, DashRoutes,
  * DashQO, DashKbarArgs, DashRouteArgs, DashBlockMaxArgs, DashPrefillArgs,
  * DashDecodeArgs, DashDeviceError, DashPageIdsArgs, DashPageStateArgs,
- * DashPageAllowArgs, DashPageDecodeArgs, DashBlockAnyArgs, DashPageBlocksArgs.  Lets a binding
+ * DashPageAllowArgs, DashPageDecodeArgs, DashBlockAnyArgs, DashPageBlocksArgs,
+ * DashIndexProjArgs.  Lets a binding
  * verify its struct layouts; returns the number of sizes available. */
 int dash_abi_sizes(int64_t* out, int n);
 /* Self-test of the bounded waits every kernel uses (no reference counterpart):

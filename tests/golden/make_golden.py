@@ -442,6 +442,77 @@ def page_aware_case(name, seed):
     print(name, "saved")
 
 
+def _gemma_forward_native():
+    """GemmaRMSNorm.forward_native of the sglang wheel (WHL layernorm.py:1113-1131),
+    compiled from the wheel's own source (the module's imports need a full
+    sglang runtime)."""
+    import ast
+    whl = glob.glob(os.path.join(REF, "wheel", "*.whl"))[0]
+    src = zipfile.ZipFile(whl).read("sglang/srt/layers/layernorm.py").decode()
+    tree = ast.parse(src)
+    cls = next(n for n in tree.body if isinstance(n, ast.ClassDef) and n.name == "GemmaRMSNorm")
+    fn = next(n for n in cls.body if isinstance(n, ast.FunctionDef) and n.name == "forward_native")
+    mod = ast.Module(body=[fn], type_ignores=[])
+    import typing
+    ns = {"torch": torch, "Optional": typing.Optional, "Union": typing.Union,
+          "Tuple": typing.Tuple}
+    exec(compile(mod, "layernorm.py", "exec"), ns)
+    return ns["forward_native"]
+
+
+def frontend_case(name, seed):
+    """Router front end: the reference's _router_qk (index projections +
+    _RMSNorm + RoPE, modeling_deepseekv2.py:336-348) and the sglang index branch
+    (Linear + GemmaRMSNorm.forward_native + _rope2d_torch), bf16 on CPU."""
+    import ananta_ref.dash_attention as da
+    import ananta_ref.modeling_deepseekv2 as mdl
+    from sglang.srt.layers.attention.unlimited_dash_ops import page2d_rope as pr
+    gemma = _gemma_forward_native()
+    rng = np.random.default_rng(seed)
+    B, S, Hd, d, eps = 2, 83, 192, 128, 1e-6
+    bf = torch.bfloat16
+    hidden = torch.tensor(rng.standard_normal((B, S, Hd)), dtype=torch.float32).to(bf)
+    wq = torch.tensor(rng.standard_normal((d, Hd)) / math.sqrt(Hd), dtype=torch.float32).to(bf)
+    wk = torch.tensor(rng.standard_normal((d, Hd)) / math.sqrt(Hd), dtype=torch.float32).to(bf)
+    nq = torch.tensor(rng.standard_normal(d) * 0.1, dtype=torch.float32).to(bf)
+    nk = torch.tensor(rng.standard_normal(d) * 0.1, dtype=torch.float32).to(bf)
+    pos = torch.tensor(rng.integers(0, 5000, size=(B, S)), dtype=torch.float32)
+    inv = 1.0 / (10000.0 ** (torch.arange(0, d // 2, dtype=torch.float32) / (d // 2)))
+    ang = pos[..., None] * inv
+    emb = torch.cat([ang, ang], -1)
+    cos, sin = emb.cos().to(bf), emb.sin().to(bf)
+
+    def lin(w):
+        m = torch.nn.Linear(Hd, d, bias=False, dtype=bf)
+        m.weight.data.copy_(w)
+        return m
+
+    def hf_norm(w):
+        m = da._RMSNorm(d, eps=eps).to(bf)
+        m.weight.data.copy_(w)
+        return m
+    router = types.SimpleNamespace(index_dim=d, q_proj=lin(wq), k_proj=lin(wk),
+                                   q_norm=hf_norm(nq), k_norm=hf_norm(nk))
+    with torch.no_grad():
+        hq, hk = mdl._router_qk(router, hidden, (cos, sin))
+        hq0, hk0 = mdl._router_qk(router, hidden, None)
+        T = B * S
+        x = hidden.view(T, Hd)
+        out = {}
+        for tag, w, nw in (("q", wq, nq), ("k", wk, nk)):
+            y = torch.nn.functional.linear(x, w)
+            stub = types.SimpleNamespace(weight=nw, variance_epsilon=eps)
+            y = gemma(stub, y.view(-1, 1, d)).view(T, d)
+            out[tag] = pr._rope2d_torch(y, cos.view(T, d), sin.view(T, d), d).float()
+    u16 = lambda t: t.contiguous().view(torch.int16).numpy()
+    np.savez_compressed(
+        os.path.join(HERE, name + ".npz"), seed=seed, B=B, S=S, Hd=Hd, d=d, eps=eps,
+        hidden=u16(hidden), wq=u16(wq), wk=u16(wk), nq=u16(nq), nk=u16(nk), cos=u16(cos),
+        sin=u16(sin), hf_q=hq.numpy(), hf_k=hk.numpy(), hf_q_norope=hq0.numpy(),
+        hf_k_norope=hk0.numpy(), sg_q=out["q"].numpy(), sg_k=out["k"].numpy())
+    print(name, "saved")
+
+
 def main():
     da, md = import_reference()
     torch.set_num_threads(os.cpu_count())
@@ -458,6 +529,7 @@ def main():
     paged_router_case("paged_router", seed=4)
     triton_interp_case(da, md, "triton_interp", seed=5)
     page_aware_case("page_aware", seed=6)
+    frontend_case("frontend", seed=7)
 
 
 if __name__ == "__main__":
