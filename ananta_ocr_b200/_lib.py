@@ -168,10 +168,19 @@ class DashIndexProjArgs(C.Structure):
                 ("k_rows", _i64), ("device_error", _p)]
 
 
+class DashRopeKVArgs(C.Structure):
+    _fields_ = [("q", _p), ("q_stride", _i64), ("q_out", _p), ("q_out_stride", _i64),
+                ("k", _p), ("k_stride", _i64), ("v", _p), ("v_stride", _i64), ("cos", _p),
+                ("sin", _p), ("cs_stride", _i64), ("k_cache", _p), ("v_cache", _p),
+                ("cache_row_stride", _i64), ("slot_mapping", _p), ("num_slots", _i64),
+                ("T", _i32), ("n_q_heads", _i32), ("n_kv_heads", _i32), ("head_dim", _i32),
+                ("device_error", _p)]
+
+
 ABI_ORDER = [DashSeqs, DashKV, DashRoutes, DashQO, DashKbarArgs, DashRouteArgs,
              DashBlockMaxArgs, DashPrefillArgs, DashDecodeArgs, DashDeviceError,
              DashPageIdsArgs, DashPageStateArgs, DashPageAllowArgs, DashPageDecodeArgs,
-             DashBlockAnyArgs, DashPageBlocksArgs, DashIndexProjArgs]
+             DashBlockAnyArgs, DashPageBlocksArgs, DashIndexProjArgs, DashRopeKVArgs]
 
 # every function the header declares
 EXPORTS = [
@@ -180,7 +189,7 @@ EXPORTS = [
     "dash_library_version", "dash_count_launches", "dash_abi_sizes",
     "dash_decode_attn_noalloc", "dash_noalloc_scratch_bytes", "dash_selftest_bounded_wait",
     "dash_page_ids", "dash_page_state_step", "dash_page_allow", "dash_page_decode_query",
-    "dash_block_any", "dash_page_blocks", "dash_index_proj",
+    "dash_block_any", "dash_page_blocks", "dash_index_proj", "dash_rope_kv_write",
 ]
 
 
@@ -216,6 +225,7 @@ def load(path: str = LIB_PATH):
         ("dash_block_any", [C.POINTER(DashBlockAnyArgs), _p]),
         ("dash_page_blocks", [C.POINTER(DashPageBlocksArgs), _p]),
         ("dash_index_proj", [C.POINTER(DashIndexProjArgs), _p]),
+        ("dash_rope_kv_write", [C.POINTER(DashRopeKVArgs), _p]),
     ]:
         f = getattr(L, name)
         f.argtypes = args

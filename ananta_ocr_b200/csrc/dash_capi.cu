@@ -105,7 +105,7 @@ int dash_count_launches(int reset) {
 }
 
 int dash_abi_sizes(int64_t* out, int n) {
-  const int64_t s[17] = {(int64_t)sizeof(DashSeqs),           (int64_t)sizeof(DashKV),
+  const int64_t s[18] = {(int64_t)sizeof(DashSeqs),           (int64_t)sizeof(DashKV),
                          (int64_t)sizeof(DashRoutes),         (int64_t)sizeof(DashQO),
                          (int64_t)sizeof(DashKbarArgs),       (int64_t)sizeof(DashRouteArgs),
                          (int64_t)sizeof(DashBlockMaxArgs),   (int64_t)sizeof(DashPrefillArgs),
@@ -113,9 +113,9 @@ int dash_abi_sizes(int64_t* out, int n) {
                          (int64_t)sizeof(DashPageIdsArgs),    (int64_t)sizeof(DashPageStateArgs),
                          (int64_t)sizeof(DashPageAllowArgs),  (int64_t)sizeof(DashPageDecodeArgs),
                          (int64_t)sizeof(DashBlockAnyArgs),   (int64_t)sizeof(DashPageBlocksArgs),
-                         (int64_t)sizeof(DashIndexProjArgs)};
-  for (int i = 0; i < n && i < 17; ++i) out[i] = s[i];
-  return 17;
+                         (int64_t)sizeof(DashIndexProjArgs),  (int64_t)sizeof(DashRopeKVArgs)};
+  for (int i = 0; i < n && i < 18; ++i) out[i] = s[i];
+  return 18;
 }
 
 int dash_kbar_pool(const DashKbarArgs* a, dash_stream_t stream) {
@@ -316,6 +316,28 @@ int dash_index_proj(const DashIndexProjArgs* a, dash_stream_t stream) {
       a->k_stride < a->d)
     return set_error(DASH_ERR_INVALID, "idx_k rows must be aligned for vector stores (row stride multiple of 4 >= d)");
   return launch_index_proj(*a, (cudaStream_t)stream);
+}
+
+int dash_rope_kv_write(const DashRopeKVArgs* a, dash_stream_t stream) {
+  if (!a) return set_error(DASH_ERR_INVALID, "null args");
+  if (a->T < 0 || a->n_q_heads < 0 || a->n_kv_heads < 0) return set_error(DASH_ERR_INVALID, "negative size");
+  if (a->T == 0) return DASH_OK;
+  if (a->head_dim != 128) return set_error(DASH_ERR_UNSUPPORTED, "head_dim %d != 128", a->head_dim);
+  if ((a->n_q_heads && (!a->q || !a->q_out)) || (a->n_kv_heads && (!a->k || !a->k_cache)) ||
+      (a->v && !a->v_cache))
+    return set_error(DASH_ERR_INVALID, "null pointer");
+  if (!a->cos != !a->sin) return set_error(DASH_ERR_INVALID, "cos and sin go together");
+  const void* ptrs[7] = {a->q, a->q_out, a->k, a->v, a->k_cache, a->v_cache, a->cos};
+  for (const void* p : ptrs)
+    if (p && !aligned16(p)) return set_error(DASH_ERR_INVALID, "tensors must be 16-byte aligned");
+  if (a->sin && !aligned16(a->sin)) return set_error(DASH_ERR_INVALID, "tensors must be 16-byte aligned");
+  if (a->q_stride % 8 || a->q_out_stride % 8 || a->k_stride % 8 || a->v_stride % 8 || a->cache_row_stride % 8 ||
+      (a->cos && a->cs_stride % 8))
+    return set_error(DASH_ERR_INVALID, "row strides must be multiples of 8 elements");
+  if (a->cache_row_stride < (int64_t)a->n_kv_heads * a->head_dim)
+    return set_error(DASH_ERR_INVALID, "cache rows shorter than n_kv_heads * head_dim");
+  if (a->n_kv_heads && a->num_slots <= 0) return set_error(DASH_ERR_INVALID, "num_slots must be > 0");
+  return launch_rope_kv(*a, (cudaStream_t)stream);
 }
 
 int dash_page_decode_query(const DashPageDecodeArgs* a, dash_stream_t stream) {

@@ -363,3 +363,86 @@ int launch_index_proj(const DashIndexProjArgs& a, cudaStream_t st) {
 }
 
 }  // namespace dash
+
+namespace dash {
+
+// ---------------------------------------------------------------------------
+// rope_kv_kernel: one CTA per token; thread work item = 8 columns of a head
+// row plus their rotate-half partners (q and k), or 8 columns of v.  HBM-bound
+// elementwise pass: q read + written, k and v read and written once into the
+// cache rows, cos/sin read once per token.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint4 rope8(uint4 x, uint4 xp, uint4 c, uint4 s, bool lo_half) {
+  // lo_half: x holds columns j < 64 (rot = -x_partner), else rot = +x_partner
+  const uint32_t xv[4] = {x.x, x.y, x.z, x.w}, pv[4] = {xp.x, xp.y, xp.z, xp.w};
+  const uint32_t cv[4] = {c.x, c.y, c.z, c.w}, sv[4] = {s.x, s.y, s.z, s.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    float r[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float xf = h ? bf_hi(xv[e]) : bf_lo(xv[e]);
+      float pf = h ? bf_hi(pv[e]) : bf_lo(pv[e]);
+      if (lo_half) pf = -pf;
+      const float cf = h ? bf_hi(cv[e]) : bf_lo(cv[e]);
+      const float sf = h ? bf_hi(sv[e]) : bf_lo(sv[e]);
+      r[h] = __fadd_rn(bf16r(__fmul_rn(xf, cf)), bf16r(__fmul_rn(pf, sf)));
+    }
+    const __nv_bfloat162 b2 = __floats2bfloat162_rn(r[0], r[1]);
+    o[e] = *reinterpret_cast<const uint32_t*>(&b2);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__global__ void __launch_bounds__(256) rope_kv_kernel(DashRopeKVArgs a) {
+  const int64_t t = blockIdx.x;
+  const int nq = a.n_q_heads, nkv = a.n_kv_heads;
+  const uint4* cs = a.cos ? reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.cos) + t * a.cs_stride) : nullptr;
+  const uint4* sn = a.cos ? reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.sin) + t * a.cs_stride) : nullptr;
+  const int64_t slot = a.slot_mapping ? a.slot_mapping[t] : t;
+  const bool slot_ok = slot >= 0 && slot < a.num_slots;
+  if (!slot_ok && threadIdx.x == 0) record_error(a.device_error, DASH_DEV_BAD_PAGE, 80, slot);
+  // work items: q pair-chunks (nq * 8), k pair-chunks (nkv * 8), v chunks (nkv * 16)
+  const int n_items = nq * 8 + nkv * 8 + (a.v ? nkv * 16 : 0);
+  for (int it = threadIdx.x; it < n_items; it += blockDim.x) {
+    if (it < nq * 8 + nkv * 8) {
+      const bool is_q = it < nq * 8;
+      const int i = is_q ? it : it - nq * 8;
+      const int head = i >> 3, ch = i & 7;                 // columns [8ch, 8ch+8) and +64
+      const uint4* src = reinterpret_cast<const uint4*>(
+          reinterpret_cast<const __nv_bfloat16*>(is_q ? a.q : a.k) + t * (is_q ? a.q_stride : a.k_stride)) + head * 16;
+      const uint4 lo = src[ch], hi = src[8 + ch];
+      uint4 olo = lo, ohi = hi;
+      if (cs) {
+        olo = rope8(lo, hi, __ldg(cs + ch), __ldg(sn + ch), true);
+        ohi = rope8(hi, lo, __ldg(cs + 8 + ch), __ldg(sn + 8 + ch), false);
+      }
+      uint4* dst;
+      if (is_q) {
+        dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.q_out) + t * a.q_out_stride) + head * 16;
+      } else {
+        if (!slot_ok) continue;
+        dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.k_cache) + slot * a.cache_row_stride) + head * 16;
+      }
+      dst[ch] = olo;
+      dst[8 + ch] = ohi;
+    } else {
+      if (!slot_ok) continue;
+      const int i = it - nq * 8 - nkv * 8;                  // v: head i / 16, chunk i % 16
+      const uint4* src = reinterpret_cast<const uint4*>(
+          reinterpret_cast<const __nv_bfloat16*>(a.v) + t * a.v_stride);
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.v_cache) + slot * a.cache_row_stride);
+      dst[i] = src[i];
+    }
+  }
+}
+
+int launch_rope_kv(const DashRopeKVArgs& a, cudaStream_t st) {
+  if (a.T == 0) return DASH_OK;
+  rope_kv_kernel<<<(unsigned)a.T, 256, 0, st>>>(a);
+  count_launch();
+  return check_launch("rope_kv_kernel");
+}
+
+}  // namespace dash

@@ -26,5 +26,6 @@ int launch_page_decode(const DashPageDecodeArgs& a, cudaStream_t st);
 int launch_block_any(const DashBlockAnyArgs& a, cudaStream_t st);
 int launch_page_blocks(const DashPageBlocksArgs& a, cudaStream_t st);
 int launch_index_proj(const DashIndexProjArgs& a, cudaStream_t st);
+int launch_rope_kv(const DashRopeKVArgs& a, cudaStream_t st);
 
 }  // namespace dash

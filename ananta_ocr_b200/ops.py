@@ -418,3 +418,52 @@ def index_proj(hidden: torch.Tensor, w_q: torch.Tensor, w_k: torch.Tensor,
     a.device_error = device_error.ptr if device_error is not None else None
     L.call("dash_index_proj", a)
     return idx_q, idx_k
+
+
+def rope_kv_write(q: Optional[torch.Tensor], k: Optional[torch.Tensor], cos: Optional[torch.Tensor],
+                  sin: Optional[torch.Tensor], *, v: Optional[torch.Tensor] = None,
+                  q_out: Optional[torch.Tensor] = None, k_cache: Optional[torch.Tensor] = None,
+                  v_cache: Optional[torch.Tensor] = None, slot_mapping: Optional[torch.Tensor] = None,
+                  head_dim: int = 128, device_error: Optional[DeviceErrorWord] = None):
+    """Rotate-half RoPE of q [T, Hq*D] and k [T, Hkv*D] (bf16, every product and
+    the sum rounded to bf16) with k (rotated) and v written to the cache rows
+    ``slot_mapping`` (``dash_rope_kv_write``).  Without caches, k goes to a
+    new [T, Hkv*D] tensor.  Returns (q_out, k_dest)."""
+    _need_cuda(q, k, v, cos, sin, k_cache, v_cache, slot_mapping)
+    ref = q if q is not None else k
+    T = ref.shape[0]
+    a = L.DashRopeKVArgs()
+    a.T, a.head_dim = T, head_dim
+    if q is not None:
+        if q.stride(-1) != 1:
+            q = q.contiguous()
+        if q_out is None:
+            q_out = torch.empty_like(q)
+        a.q, a.q_stride, a.q_out, a.q_out_stride = q.data_ptr(), q.stride(0), q_out.data_ptr(), q_out.stride(0)
+        a.n_q_heads = q.shape[1] // head_dim
+    if k is not None:
+        if k.stride(-1) != 1:
+            k = k.contiguous()
+        a.k, a.k_stride, a.n_kv_heads = k.data_ptr(), k.stride(0), k.shape[1] // head_dim
+        if k_cache is None:
+            k_cache = torch.empty_like(k)
+        kc = k_cache.view(-1, k_cache.shape[-2] * k_cache.shape[-1]) if k_cache.dim() == 3 else k_cache
+        kc = kc if kc.dim() == 2 else kc.reshape(-1, a.n_kv_heads * head_dim)
+        a.k_cache, a.cache_row_stride, a.num_slots = kc.data_ptr(), kc.stride(0), kc.shape[0]
+        if v is not None:
+            if v.stride(-1) != 1:
+                v = v.contiguous()
+            vc = v_cache.reshape(kc.shape) if v_cache.dim() != 2 else v_cache
+            if vc.stride(0) != kc.stride(0):
+                raise ValueError("k_cache and v_cache rows must share a stride")
+            a.v, a.v_stride, a.v_cache = v.data_ptr(), v.stride(0), vc.data_ptr()
+    if cos is not None:
+        if cos.stride(-1) != 1 or sin.stride(-1) != 1 or cos.stride(0) != sin.stride(0):
+            cos, sin = cos.contiguous(), sin.contiguous()
+        a.cos, a.sin, a.cs_stride = cos.data_ptr(), sin.data_ptr(), cos.stride(0)
+    if slot_mapping is not None:
+        sm = slot_mapping if slot_mapping.dtype == torch.int64 else slot_mapping.to(torch.int64)
+        a.slot_mapping = sm.contiguous().data_ptr()
+    a.device_error = device_error.ptr if device_error is not None else None
+    L.call("dash_rope_kv_write", a)
+    return q_out, k_cache

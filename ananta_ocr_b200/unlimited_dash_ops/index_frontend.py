@@ -1,4 +1,4 @@
-"""Serving-side router front end, backed by libdash_b200.so.
+"""Serving-side attention front end, backed by libdash_b200.so.
 
 ``index_qk_fused`` is the index branch of WHL unlimited_ocr_v2.py:145-162
 (``index_q_proj`` / ``index_k_proj`` + ``GemmaRMSNorm`` x2 +
@@ -36,3 +36,32 @@ def index_qk_fused(hidden_states: torch.Tensor, index_q_weight: torch.Tensor,
                           q_norm_weight, k_norm_weight, eps, cos=cos, sin=sin, norm_clamp=False,
                           idx_q=idx_q_out, idx_k=kout, slot_mapping=slot_mapping)
     return q, (index_cache if index_cache is not None else k)
+
+
+@torch.no_grad()
+def apply_page2d_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                      head_dim: int) -> torch.Tensor:
+    """WHL page2d_rope.py:192-223: NeoX (rotate-half) RoPE of [T, H * head_dim]
+    bf16 with every product and the sum rounded to bf16."""
+    out, _ = ops.rope_kv_write(x, None, cos, sin, head_dim=head_dim)
+    return out
+
+
+@torch.no_grad()
+def apply_page2d_rope_pair(x: torch.Tensor, y: torch.Tensor, cos: torch.Tensor,
+                           sin: torch.Tensor, head_dim: int):
+    """WHL page2d_rope.py:301-323: both tensors in one launch."""
+    return ops.rope_kv_write(x, y, cos, sin, head_dim=head_dim)
+
+
+@torch.no_grad()
+def rope_and_store_kv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Tensor,
+                      sin: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                      slot_mapping: torch.Tensor, head_dim: int = 128) -> torch.Tensor:
+    """``apply_page2d_rope_pair(q, k)`` (main branch, WHL unlimited_ocr_v2.py:156-158)
+    followed by ``set_kv_buffer(loc, k, v)`` (WHL memory_pool.py:5524-5545) in one
+    pass: q is rotated in place, rotated k and v land in the cache rows.
+    Returns q."""
+    ops.rope_kv_write(q, k, cos, sin, v=v, q_out=q, k_cache=k_cache, v_cache=v_cache,
+                      slot_mapping=slot_mapping, head_dim=head_dim)
+    return q

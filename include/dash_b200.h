@@ -561,6 +561,34 @@ typedef struct {
 } DashIndexProjArgs;
 int dash_index_proj(const DashIndexProjArgs* args, dash_stream_t stream);
 
+/* dash_rope_kv_write -- main-branch RoPE + paged K/V store for one step.
+ * Replaces: WHL page2d_rope.py:301-323 (apply_page2d_rope_pair on q and k:
+ *           rotate-half RoPE, each product and the sum rounded to bf16) and
+ *           WHL memory_pool.py:5524-5545 (set_kv_buffer).
+ * Token t: q[t] (n_q_heads x head_dim bf16) is rotated into q_out[t] (may be
+ * q itself); k[t] rotated and v[t] copied into k_cache / v_cache rows
+ * slot_mapping[t] (n_kv_heads x head_dim each, cache row stride in elements).
+ * cos/sin [T, head_dim] bf16 (NULL: no rotation).  v NULL: k is only rotated
+ * (into k_cache rows; slot_mapping NULL: row t), which is
+ * apply_page2d_rope_pair itself.  head_dim = 128.                           */
+typedef struct {
+  const void* q; int64_t q_stride;          /* [T, n_q_heads * head_dim] bf16 */
+  void* q_out; int64_t q_out_stride;
+  const void* k; int64_t k_stride;          /* [T, n_kv_heads * head_dim] */
+  const void* v; int64_t v_stride;
+  const void* cos; const void* sin; int64_t cs_stride;
+  void* k_cache; void* v_cache;             /* rows of n_kv_heads * head_dim */
+  int64_t cache_row_stride;
+  const int64_t* slot_mapping;              /* [T] */
+  int64_t num_slots;
+  int32_t T;
+  int32_t n_q_heads;
+  int32_t n_kv_heads;
+  int32_t head_dim;
+  DashDeviceError* device_error;
+} DashRopeKVArgs;
+int dash_rope_kv_write(const DashRopeKVArgs* args, dash_stream_t stream);
+
 /* ---------------------------------------------------------------------- */
 /* Diagnostics */
 int dash_last_error(char* buf, int len);     /* copies the last host-side error message */
@@ -570,7 +598,7 @@ int dash_count_launches(int reset);          /* kernels launched by this library
  * DashQO, DashKbarArgs, DashRouteArgs, DashBlockMaxArgs, DashPrefillArgs,
  * DashDecodeArgs, DashDeviceError, DashPageIdsArgs, DashPageStateArgs,
  * DashPageAllowArgs, DashPageDecodeArgs, DashBlockAnyArgs, DashPageBlocksArgs,
- * DashIndexProjArgs.  Lets a binding
+ * DashIndexProjArgs, DashRopeKVArgs.  Lets a binding
  * verify its struct layouts; returns the number of sizes available. */
 int dash_abi_sizes(int64_t* out, int n);
 /* Self-test of the bounded waits every kernel uses (no reference counterpart):

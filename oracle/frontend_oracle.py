@@ -57,3 +57,10 @@ def index_qk(hidden, wq, wk, nq, nk, eps, cos=None, sin=None):
     if cos is not None:
         q, k = rope(q, cos, sin), rope(k, cos, sin)
     return q.float(), k.float()
+
+
+def rope_rows(x, cos, sin, head_dim=128):
+    """WHL page2d_rope.py:130-141 (_rope2d_torch): [T, H * head_dim] rows."""
+    T = x.shape[0]
+    v = x.view(T, -1, head_dim)
+    return rope(v, cos[:, None, :], sin[:, None, :]).view_as(x)

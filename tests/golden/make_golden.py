@@ -504,9 +504,17 @@ def frontend_case(name, seed):
             stub = types.SimpleNamespace(weight=nw, variance_epsilon=eps)
             y = gemma(stub, y.view(-1, 1, d)).view(T, d)
             out[tag] = pr._rope2d_torch(y, cos.view(T, d), sin.view(T, d), d).float()
+    # main-branch RoPE of a 2-head q and a 1-head k (apply_page2d_rope's torch path)
+    T = B * S
+    rx = torch.tensor(rng.standard_normal((T, 2 * d)), dtype=torch.float32).to(bf)
+    ry = torch.tensor(rng.standard_normal((T, d)), dtype=torch.float32).to(bf)
+    with torch.no_grad():
+        ox = pr._rope2d_torch(rx, cos.view(T, d), sin.view(T, d), d)
+        oy = pr._rope2d_torch(ry, cos.view(T, d), sin.view(T, d), d)
     u16 = lambda t: t.contiguous().view(torch.int16).numpy()
     np.savez_compressed(
         os.path.join(HERE, name + ".npz"), seed=seed, B=B, S=S, Hd=Hd, d=d, eps=eps,
+        rope_x=u16(rx), rope_y=u16(ry), rope_ox=u16(ox), rope_oy=u16(oy),
         hidden=u16(hidden), wq=u16(wq), wk=u16(wk), nq=u16(nq), nk=u16(nk), cos=u16(cos),
         sin=u16(sin), hf_q=hq.numpy(), hf_k=hk.numpy(), hf_q_norope=hq0.numpy(),
         hf_k_norope=hk0.numpy(), sg_q=out["q"].numpy(), sg_k=out["k"].numpy())

@@ -139,3 +139,45 @@ def test_bad_slot_is_recorded_and_skipped():
     keep[17] = False
     check(cache[slots[keep]].cpu().numpy(), rk[keep].cpu().numpy())
     check(q.cpu().numpy(), rq.cpu().numpy())
+
+
+# ---------------------------------------------------------------------------
+# main-branch RoPE + paged K/V store: bf16 products and sums, bit-exact
+# ---------------------------------------------------------------------------
+from ananta_ocr_b200.unlimited_dash_ops import index_frontend as IF  # noqa: E402
+
+
+def test_rope_pair_matches_reference_golden_bitwise():
+    g = golden()
+    T, d = int(g["B"]) * int(g["S"]), int(g["d"])
+    cos, sin = bf("cos").view(T, d), bf("sin").view(T, d)
+    ox, oy = IF.apply_page2d_rope_pair(bf("rope_x"), bf("rope_y"), cos, sin, d)
+    assert torch.equal(ox, bf("rope_ox")) and torch.equal(oy, bf("rope_oy"))
+    assert torch.equal(IF.apply_page2d_rope(bf("rope_x"), cos, sin, d), bf("rope_ox"))
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(10, 10), (16, 2)])
+def test_rope_and_store_kv_bitwise(Hq, Hkv):
+    T, D, P, bs = 777, 128, 128, 16
+    gen = torch.Generator(device="cpu").manual_seed(Hq * 31 + Hkv)
+    q = torch.randn(T, Hq * D, generator=gen).to(torch.bfloat16).cuda()
+    k = torch.randn(T, Hkv * D, generator=gen).to(torch.bfloat16).cuda()
+    v = torch.randn(T, Hkv * D, generator=gen).to(torch.bfloat16).cuda()
+    pos = torch.randint(0, 20000, (T, 1), generator=gen).float()
+    inv = 1.0 / (10000.0 ** (torch.arange(0, D // 2).float() / (D // 2)))
+    emb = torch.cat([pos * inv, pos * inv], -1)
+    cos, sin = emb.cos().to(torch.bfloat16).cuda(), emb.sin().to(torch.bfloat16).cuda()
+    k_cache = torch.full((P, bs, Hkv, D), 3.0, dtype=torch.bfloat16, device="cuda")
+    v_cache = torch.full_like(k_cache, 5.0)
+    slots = torch.randperm(P * bs, device="cuda")[:T]
+    rq = F.rope_rows(q, cos, sin, D)
+    rk = F.rope_rows(k, cos, sin, D)
+    q2 = q.clone()
+    IF.rope_and_store_kv(q2, k, v, cos, sin, k_cache, v_cache, slots, D)
+    assert torch.equal(q2, rq)
+    kc = k_cache.view(P * bs, Hkv * D)
+    vc = v_cache.view(P * bs, Hkv * D)
+    assert torch.equal(kc[slots], rk) and torch.equal(vc[slots], v)
+    untouched = torch.ones(P * bs, dtype=torch.bool, device="cuda")
+    untouched[slots] = False
+    assert torch.all(kc[untouched] == 3.0) and torch.all(vc[untouched] == 5.0)

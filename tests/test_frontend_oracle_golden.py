@@ -35,3 +35,11 @@ def test_index_branch_matches_reference():
                       bf("cos").view(T, d), bf("sin").view(T, d))
     assert np.array_equal(q.numpy(), G["sg_q"])
     assert np.array_equal(k.numpy(), G["sg_k"])
+
+
+def test_rope_rows_match_reference():
+    T, d = int(G["B"]) * int(G["S"]), int(G["d"])
+    cos, sin = bf("cos").view(T, d), bf("sin").view(T, d)
+    for x, o in (("rope_x", "rope_ox"), ("rope_y", "rope_oy")):
+        got = F.rope_rows(bf(x), cos, sin, d)
+        assert torch.equal(got, bf(o))
