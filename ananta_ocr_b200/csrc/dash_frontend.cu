@@ -52,9 +52,14 @@ static_assert(4 * UNIT_BYTES <= OFF_NORM, "epilogue staging must fit the stage b
 // fp32 -> bf16 -> fp32, round to nearest even, on the integer pipe (the
 // rounding the reference's bf16 tensors apply; non-finite values keep their
 // class: inf stays inf, a quiet NaN stays NaN)
-__device__ __forceinline__ float bf16r(float x) {
+__device__ __forceinline__ uint32_t bf16r_bits(float x) {
   const uint32_t u = __float_as_uint(x);
-  return __uint_as_float((u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u);
+  return (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
+}
+__device__ __forceinline__ float bf16r(float x) { return __uint_as_float(bf16r_bits(x)); }
+// two fp32 -> packed bf16x2 (lo, hi), rounded to nearest even on the integer pipe
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  return __byte_perm(bf16r_bits(lo), bf16r_bits(hi), 0x7632);
 }
 
 // y = bf16(x * inv * w1) (w1 = 1 + w); the clamped variant zeroes non-finite x
@@ -90,76 +95,81 @@ __device__ __forceinline__ float bf_lo(uint32_t u) { return __uint_as_float(u <<
 __device__ __forceinline__ float bf_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
 
 // One projection of this thread's row: TMEM columns [tcol, tcol + 128) hold
-// x.  Outputs (bf16-exact) go to the staging row `srow` (bf16, 128 wide).
+// x.  Pass 1 reads TMEM once, stores the bf16-rounded row in the staging row
+// `srow` and sums the squares; pass 2 reads the row back from shared memory and
+// overwrites it with the (bf16-exact) outputs.
 __device__ __forceinline__ void epilogue_unit(uint32_t tcol, const float* w1s,
                                               const uint4* cos_row, const uint4* sin_row,
                                               float eps, bool clamp, __nv_bfloat16* srow) {
-  // pass 1: mean square of the bf16-rounded row (four partial sums, added in order)
   float ss[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll 1
   for (int c = 0; c < 2; ++c) {
     float v[64];
-    tmem_ld32f(tcol + c * 32, v);
-    tmem_ld32f(tcol + 64 + c * 32, v + 32);
+    tmem_ld32f(tcol + c * 64, v);
+    tmem_ld32f(tcol + c * 64 + 32, v + 32);
     tmem_ld_wait();
 #pragma unroll
-    for (int j = 0; j < 64; ++j) {
-      float x = bf16r(v[j]);
-      if (clamp && !isfinite(x)) x = 0.0f;
-      ss[j & 3] = __fadd_rn(ss[j & 3], __fmul_rn(x, x));
+    for (int j = 0; j < 64; j += 8) {
+      uint32_t p[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float x0 = bf16r(v[j + 2 * e]), x1 = bf16r(v[j + 2 * e + 1]);
+        if (clamp) {
+          if (!isfinite(x0)) x0 = 0.0f;
+          if (!isfinite(x1)) x1 = 0.0f;
+        }
+        ss[e] = __fadd_rn(ss[e], __fmul_rn(x0, x0));
+        ss[e] = __fadd_rn(ss[e], __fmul_rn(x1, x1));
+        p[e] = __byte_perm(__float_as_uint(x0), __float_as_uint(x1), 0x7632);
+      }
+      *reinterpret_cast<uint4*>(srow + c * 64 + j) = make_uint4(p[0], p[1], p[2], p[3]);
     }
   }
   const float tot = __fadd_rn(__fadd_rn(ss[0], ss[1]), __fadd_rn(ss[2], ss[3]));
   const float inv = rsqrtf(__fadd_rn(__fmul_rn(tot, 1.0f / 128.0f), eps));
-  // pass 2: columns j and j + 64 together (rotate-half partners)
-#pragma unroll 1
-  for (int c = 0; c < 2; ++c) {
-    float va[32], vb[32];
-    tmem_ld32f(tcol + c * 32, va);
-    tmem_ld32f(tcol + 64 + c * 32, vb);
-    tmem_ld_wait();
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      uint4 ca, sa, cb, sb;
-      if (cos_row) {
-        ca = __ldg(cos_row + c * 4 + g);
-        sa = __ldg(sin_row + c * 4 + g);
-        cb = __ldg(cos_row + 8 + c * 4 + g);
-        sb = __ldg(sin_row + 8 + c * 4 + g);
-      }
-      const uint32_t cav[4] = {ca.x, ca.y, ca.z, ca.w}, sav[4] = {sa.x, sa.y, sa.z, sa.w};
-      const uint32_t cbv[4] = {cb.x, cb.y, cb.z, cb.w}, sbv[4] = {sb.x, sb.y, sb.z, sb.w};
-      uint32_t pa[4], pb[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float oa[2], ob[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int i = g * 8 + 2 * e + h;
-          const int j = c * 32 + i;
-          const float ya = rms_scale(bf16r(va[i]), inv, w1s[j], clamp);
-          const float yb = rms_scale(bf16r(vb[i]), inv, w1s[j + 64], clamp);
-          oa[h] = ya;
-          ob[h] = yb;
-          if (cos_row) {
-            const float c_a = h ? bf_hi(cav[e]) : bf_lo(cav[e]);
-            const float s_a = h ? bf_hi(sav[e]) : bf_lo(sav[e]);
-            const float c_b = h ? bf_hi(cbv[e]) : bf_lo(cbv[e]);
-            const float s_b = h ? bf_hi(sbv[e]) : bf_lo(sbv[e]);
-            // rot = (-y_hi, y_lo); every product and the sum rounded to bf16
-            oa[h] = __fadd_rn(bf16r(__fmul_rn(ya, c_a)), -bf16r(__fmul_rn(yb, s_a)));
-            ob[h] = __fadd_rn(bf16r(__fmul_rn(yb, c_b)), bf16r(__fmul_rn(ya, s_b)));
-          }
-        }
-        // the final bf16 rounding of both outputs, packed
-        const __nv_bfloat162 a2 = __floats2bfloat162_rn(oa[0], oa[1]);
-        const __nv_bfloat162 b2 = __floats2bfloat162_rn(ob[0], ob[1]);
-        pa[e] = *reinterpret_cast<const uint32_t*>(&a2);
-        pb[e] = *reinterpret_cast<const uint32_t*>(&b2);
-      }
-      *reinterpret_cast<uint4*>(srow + c * 32 + g * 8) = make_uint4(pa[0], pa[1], pa[2], pa[3]);
-      *reinterpret_cast<uint4*>(srow + 64 + c * 32 + g * 8) = make_uint4(pb[0], pb[1], pb[2], pb[3]);
+  // pass 2: columns j and j + 64 together (rotate-half partners), 8 at a time
+#pragma unroll 2
+  for (int g = 0; g < 8; ++g) {
+    const uint4 xa4 = *reinterpret_cast<const uint4*>(srow + g * 8);
+    const uint4 xb4 = *reinterpret_cast<const uint4*>(srow + 64 + g * 8);
+    uint4 ca, sa, cb, sb;
+    if (cos_row) {
+      ca = __ldg(cos_row + g);
+      sa = __ldg(sin_row + g);
+      cb = __ldg(cos_row + 8 + g);
+      sb = __ldg(sin_row + 8 + g);
     }
+    const uint32_t xav[4] = {xa4.x, xa4.y, xa4.z, xa4.w}, xbv[4] = {xb4.x, xb4.y, xb4.z, xb4.w};
+    const uint32_t cav[4] = {ca.x, ca.y, ca.z, ca.w}, sav[4] = {sa.x, sa.y, sa.z, sa.w};
+    const uint32_t cbv[4] = {cb.x, cb.y, cb.z, cb.w}, sbv[4] = {sb.x, sb.y, sb.z, sb.w};
+    uint32_t pa[4], pb[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float oa[2], ob[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int j = g * 8 + 2 * e + h;
+        const float xa = h ? bf_hi(xav[e]) : bf_lo(xav[e]);
+        const float xb = h ? bf_hi(xbv[e]) : bf_lo(xbv[e]);
+        const float ya = rms_scale(xa, inv, w1s[j], clamp);
+        const float yb = rms_scale(xb, inv, w1s[j + 64], clamp);
+        oa[h] = ya;
+        ob[h] = yb;
+        if (cos_row) {
+          const float c_a = h ? bf_hi(cav[e]) : bf_lo(cav[e]);
+          const float s_a = h ? bf_hi(sav[e]) : bf_lo(sav[e]);
+          const float c_b = h ? bf_hi(cbv[e]) : bf_lo(cbv[e]);
+          const float s_b = h ? bf_hi(sbv[e]) : bf_lo(sbv[e]);
+          // rot = (-y_hi, y_lo); every product and the sum rounded to bf16
+          oa[h] = __fadd_rn(bf16r(__fmul_rn(ya, c_a)), -bf16r(__fmul_rn(yb, s_a)));
+          ob[h] = __fadd_rn(bf16r(__fmul_rn(yb, c_b)), bf16r(__fmul_rn(ya, s_b)));
+        }
+      }
+      pa[e] = pack_bf16x2(oa[0], oa[1]);
+      pb[e] = pack_bf16x2(ob[0], ob[1]);
+    }
+    *reinterpret_cast<uint4*>(srow + g * 8) = make_uint4(pa[0], pa[1], pa[2], pa[3]);
+    *reinterpret_cast<uint4*>(srow + 64 + g * 8) = make_uint4(pb[0], pb[1], pb[2], pb[3]);
   }
 }
 
@@ -389,8 +399,7 @@ __device__ __forceinline__ uint4 rope8(uint4 x, uint4 xp, uint4 c, uint4 s, bool
       const float sf = h ? bf_hi(sv[e]) : bf_lo(sv[e]);
       r[h] = __fadd_rn(bf16r(__fmul_rn(xf, cf)), bf16r(__fmul_rn(pf, sf)));
     }
-    const __nv_bfloat162 b2 = __floats2bfloat162_rn(r[0], r[1]);
-    o[e] = *reinterpret_cast<const uint32_t*>(&b2);
+    o[e] = pack_bf16x2(r[0], r[1]);
   }
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
