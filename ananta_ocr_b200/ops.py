@@ -447,8 +447,7 @@ def rope_kv_write(q: Optional[torch.Tensor], k: Optional[torch.Tensor], cos: Opt
         a.k, a.k_stride, a.n_kv_heads = k.data_ptr(), k.stride(0), k.shape[1] // head_dim
         if k_cache is None:
             k_cache = torch.empty_like(k)
-        kc = k_cache.view(-1, k_cache.shape[-2] * k_cache.shape[-1]) if k_cache.dim() == 3 else k_cache
-        kc = kc if kc.dim() == 2 else kc.reshape(-1, a.n_kv_heads * head_dim)
+        kc = k_cache if k_cache.dim() == 2 else k_cache.reshape(-1, a.n_kv_heads * head_dim)
         a.k_cache, a.cache_row_stride, a.num_slots = kc.data_ptr(), kc.stride(0), kc.shape[0]
         if v is not None:
             if v.stride(-1) != 1:

@@ -124,6 +124,53 @@ def page_cpu_baseline(cfg, threads=None):
                        f"candidate mask), oracle/page_oracle.py", seconds=dt)
 
 
+def run_c5(dev, decode_steps, warmup):
+    """the 12-layer decoder of ananta_ocr_b200/e2e_decoder.py
+    (random init, bf16), a prefill of 8 x 27,556 tokens of visual embeddings
+    ~N(0, 0.02), then ``decode_steps`` greedy decode steps replayed from a
+    CUDA graph.  Device time with CUDA events."""
+    import torch
+    from ananta_ocr_b200.e2e_decoder import DashDecoder, DecoderConfig
+    cfg = DecoderConfig()
+    B, S = 8, 27556
+    dec = DashDecoder(cfg, B, S + decode_steps + warmup + 4, dev, seed=0)
+    g = torch.Generator(device=dev).manual_seed(1)
+    emb = (torch.randn(B, S, cfg.hidden, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    dec.prefill(emb)                       # warm-up (the timed prefill rewrites the caches)
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(cfg.layers)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    logits = dec.prefill(emb, attn_events=ev)
+    e1.record()
+    torch.cuda.synchronize()
+    t_prefill = e0.elapsed_time(e1)
+    t_attn = sum(a.elapsed_time(b) for a, b in ev)
+    dec.tok.copy_(logits.argmax(-1))
+    for _ in range(warmup):
+        dec.decode_step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph):
+            dec.decode_step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize()
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record()
+    for _ in range(decode_steps):
+        graph.replay()
+    d1.record()
+    torch.cuda.synchronize()
+    t_dec = d0.elapsed_time(d1) / decode_steps
+    ok = bool(torch.isfinite(logits).all())
+    del graph
+    return dict(B=B, S=S, prefill_ms=t_prefill, attn_ms=t_attn, decode_ms=t_dec,
+                decode_steps=decode_steps, finite=ok)
+
+
 # ---------------------------------------------------------------------------
 # synthetic OCR documents: pages of [<PAGE>] + image tokens, then a text tail
 # carrying two response-page markers
@@ -569,7 +616,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c2", choices=["c2", "c4"])
+    ap.add_argument("--workload", default="c2", choices=["c2", "c4", "c5"],
+                    help="c2 (default, the headline), c4 long-document prefill, c5 end-to-end decoder")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -633,6 +681,34 @@ def main():
             os.close(saved_fd)
     from ananta_ocr_b200 import _lib
     _lib.load()
+
+    if args.workload == "c5":
+        # one model per GPU: ranks other than 0 run nothing (replicas only)
+        if rank != 0:
+            return
+        clocks = ClockSampler(local_rank)
+        clocks.start()
+        r = run_c5(dev, 512, max(3, args.warmup))
+        clk = clocks.stop()
+        line = {"metric": "C5 e2e prefill tokens/s", "value": r["B"] * r["S"] / (r["prefill_ms"] / 1e3),
+                "unit": "tokens/s", "n_gpus": 1, "steps": 1, "warmup": 1,
+                "ms_per_step": r["prefill_ms"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (random-init weights, visual embeddings ~N(0,0.02))",
+                "config": {"workload": "config5_e2e_decoder", "layers": 12, "hidden": 1280,
+                           "heads": 10, "experts": "64 routed top-6 + 2 shared", "batch": r["B"],
+                           "prompt_tokens": r["S"], "decode_steps": r["decode_steps"],
+                           "block_size": 64, "local_blocks": 4, "routed_k": 16},
+                "prefill": {"ms": r["prefill_ms"], "attention_ms": r["attn_ms"],
+                            "attention_fraction": r["attn_ms"] / r["prefill_ms"],
+                            "attention_scope": "per layer: RoPE + K/V store, index front end, "
+                                               "k-bar, routing, paged attention"},
+                "decode": {"ms_per_step": r["decode_ms"],
+                           "tokens_per_s": r["B"] / (r["decode_ms"] / 1e3),
+                           "graph": "one CUDA graph per step, 512 replays"},
+                "finite_logits": r["finite"], "clocks": clk}
+        print(json.dumps(line))
+        return
 
     st = run_prefill(cfg, dev, args.steps, args.warmup, rank, world, not args.no_graph)
     dec = None
