@@ -15,7 +15,9 @@ Attention per layer, all through libdash_b200:
   index_qk_fused      index projections + RMSNorm + RoPE; idx_k into the paged
                       index cache
   kbar refresh        k-bar summaries of the pages written this step
-  route_*_triton      scores + 1.5-entmax + top-K over the paged k-bar
+  route_*_triton      scores + 1.5-entmax + top-K over the paged k-bar, with
+                      page-aware candidates when the token ids are given
+                      (PageIsolationState, once per forward for all layers)
   dash_sparse_attn*   paged prefill (tcgen05) / decode (split-KV) attention
 The GEMMs and the MoE are PyTorch (cuBLAS).  ``decode_step`` allocates nothing
 that changes between steps and is captured in a CUDA graph by the caller.
@@ -30,7 +32,9 @@ import torch
 import torch.nn.functional as F
 
 from .unlimited_dash_ops import attend_triton as AT
+from .unlimited_dash_ops import decode_meta_triton as DM
 from .unlimited_dash_ops import index_frontend as IF
+from .unlimited_dash_ops import page_state as PS
 from .unlimited_dash_ops import route_triton as RT
 
 
@@ -69,7 +73,8 @@ class DashDecoder:
     """Random-init bf16 decoder with paged caches for ``batch`` sequences of
     up to ``max_len`` tokens."""
 
-    def __init__(self, cfg: DecoderConfig, batch: int, max_len: int, device, seed: int = 0):
+    def __init__(self, cfg: DecoderConfig, batch: int, max_len: int, device, seed: int = 0,
+                 page_cfg=None, page_mask: bool = False):
         self.cfg = c = cfg
         self.B = batch
         self.dev = device
@@ -124,6 +129,12 @@ class DashDecoder:
         self.attn_out = torch.empty(batch, c.heads, c.head_dim, dtype=bf, device=device)
         self.dec_ws = torch.empty(16 << 20, dtype=torch.uint8, device=device)
         self.idx_scale = c.scaling / math.sqrt(c.index_dim)
+        # page-aware candidates (image_token_id / page_token_id / per_page_image_tokens)
+        self.pst = PS.PageIsolationState(page_cfg, bs) if page_cfg is not None else None
+        # page_mask: pass the reference's dense [rows, max_block] allow mask
+        # (build_query_allow / decode_allow_fused) instead of the compact domain
+        self.page_mask = page_mask
+        self.qpage = torch.empty(batch, dtype=torch.int32, device=device)
 
     # ---------------------------------------------------------------- pieces
     def rope_tables(self, pos):
@@ -184,9 +195,13 @@ class DashDecoder:
 
     # ---------------------------------------------------------------- prefill
     @torch.no_grad()
-    def prefill(self, embeds: torch.Tensor, attn_events=None):
+    def prefill(self, embeds: torch.Tensor, attn_events=None, token_ids=None, gen_start=None):
         """embeds [B, S, hidden] bf16 -> logits [B, vocab] of each sequence's
-        last token; fills the caches (positions 0..S-1)."""
+        last token; fills the caches (positions 0..S-1).  With ``token_ids``
+        [B, S] and a page configuration, routing is restricted to the blocks of
+        each query's own image page; ``gen_start`` [B] marks the positions from
+        which tokens count as generated (text pages numbered as responses, as a
+        decode step numbers them)."""
         c = self.cfg
         B, S, H = embeds.shape
         T = B * S
@@ -203,6 +218,20 @@ class DashDecoder:
         plan = RT.kbar_all_plan(block_table=self.block_table, seq_lens=self.seq_lens,
                                 context_lens=ctx, block_size=c.block_size, max_block=self.pps,
                                 max_query_len=S, device=dev)
+        domain = allow = None
+        if self.pst is not None and token_ids is not None:
+            layout = PS.BatchLayout(num_tokens=T, num_reqs=B,
+                                    q_start=torch.arange(B + 1, device=dev) * S,
+                                    start_pos=torch.zeros(B, dtype=torch.int64, device=dev),
+                                    block_table=self.block_table, req_of_token=req,
+                                    gen_start=gen_start)
+            q_page = self.pst.step(token_ids.reshape(T), layout, slots,
+                                   self.num_pages * c.block_size)
+            domain = self.pst.candidate_domain(q_page)
+            self.last_q_page = q_page
+            if self.page_mask:
+                allow = self.pst.build_query_allow(layout, q_page, self.pps, self.num_pages)
+                domain = None
         oi = torch.empty(T, c.K, dtype=torch.int32, device=dev)
         ob = torch.empty(T, c.K, dtype=torch.float32, device=dev)
         attn = torch.empty(T, c.heads, c.head_dim, dtype=torch.bfloat16, device=dev)
@@ -220,11 +249,11 @@ class DashDecoder:
                                         head_cls=L["head_cls"], block_size=c.block_size, plan=plan)
             RT.route_prefill_triton(idx_q=idx_q, k_bar=self.kbar[li], block_table=self.block_table,
                                     seq_lens=self.seq_lens, cu_seqlens_q=cu, context_lens=ctx,
-                                    row2req=row2req, image_allow=None, out_idx=oi, out_bias=ob,
+                                    row2req=row2req, image_allow=allow, out_idx=oi, out_bias=ob,
                                     max_block=self.pps, block_size=c.block_size,
                                     local_blocks=c.local_blocks, idx_scale=self.idx_scale,
                                     prior_floor=c.prior_floor, sigma=c.sigma, topm=c.K, budget=c.K,
-                                    out_slots=c.K)
+                                    out_slots=c.K, page_domain=domain)
             AT.dash_sparse_attn(q.view(T, c.heads, c.head_dim), self.kc[li], self.vc[li],
                                 oi[None].expand(c.kv_heads, T, c.K), ob[None].expand(c.kv_heads, T, c.K),
                                 self.block_table, cu, self.seq_lens, ctx, S, c.kv_heads,
@@ -234,6 +263,7 @@ class DashDecoder:
                 attn_events[li][1].record()
             x = x + F.linear(attn.view(T, H), L["wo"])
             x = x + self.ffn_prefill(L, rmsnorm(x, L["ln2"], c.eps))
+        self.last_route = (oi, ob)         # the last layer's routes (tests read them)
         last = x.view(B, S, H)[:, -1]
         return F.linear(rmsnorm(last, self.final_norm, c.eps), self.lm_head)
 
@@ -254,6 +284,18 @@ class DashDecoder:
         sl = self.seq_lens + 1
         tail = RT.kbar_tail_plan(block_table=self.block_table, seq_lens=sl,
                                  block_size=c.block_size, tail_pages=1, device=dev)
+        domain = allow = None
+        if self.pst is not None:
+            q_page, _ = DM.decode_meta_fused(input_ids=self.tok, block_table=self.block_table,
+                                             seq_lens=sl, slot_mapping=slots, page_state=self.pst,
+                                             num_slots=self.num_pages * c.block_size,
+                                             block_size=c.block_size, out_q_page=self.qpage)
+            domain = self.pst.candidate_domain(q_page)
+            if self.page_mask:
+                allow = DM.decode_allow_fused(block_table=self.block_table, page_state=self.pst,
+                                              q_page=q_page, seq_lens=sl, max_block=self.pps,
+                                              num_blocks=self.num_pages, block_size=c.block_size)
+                domain = None
         for li, L in enumerate(self.layers):
             h = rmsnorm(x, L["ln1"], c.eps)
             qkv = F.linear(h, L["wqkv"])
@@ -265,11 +307,12 @@ class DashDecoder:
                                         block_table=self.block_table, seq_lens=sl,
                                         head_cls=L["head_cls"], block_size=c.block_size, plan=tail)
             RT.route_decode_triton(idx_q=idx_q, k_bar=self.kbar[li], block_table=self.block_table,
-                                   seq_lens=sl, image_allow=None, out_idx=self.oi, out_bias=self.ob,
+                                   seq_lens=sl, image_allow=allow, out_idx=self.oi, out_bias=self.ob,
                                    max_block=self.pps, block_size=c.block_size,
                                    local_blocks=c.local_blocks, decode_query_len=1,
                                    idx_scale=self.idx_scale, prior_floor=c.prior_floor,
-                                   sigma=c.sigma, topm=c.K, budget=c.K, out_slots=c.K)
+                                   sigma=c.sigma, topm=c.K, budget=c.K, out_slots=c.K,
+                                   page_domain=domain)
             AT.dash_sparse_attn_decode(q.view(B, c.heads, c.head_dim), self.kc[li], self.vc[li],
                                        self.oi[None].expand(c.kv_heads, B, c.K),
                                        self.ob[None].expand(c.kv_heads, B, c.K), self.block_table,

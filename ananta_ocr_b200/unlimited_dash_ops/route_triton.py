@@ -102,9 +102,12 @@ def route_prefill_triton(*, idx_q, k_bar, block_table, seq_lens, cu_seqlens_q, c
                          row2req, image_allow, out_idx, out_bias, max_block: int,
                          block_size: int, local_blocks: int, idx_scale: float,
                          prior_floor: float, sigma: float, topm: int, budget=None,
-                         q_chunk: int = 2048, out_slots=None, score_buf=None):
+                         q_chunk: int = 2048, out_slots=None, score_buf=None, page_domain=None):
     """Prefill routing into caller-owned ``out_idx``/``out_bias`` [total_q, slots].
-    Returns (M, None, 0): the slot width, no diagnostic score chunk."""
+    ``page_domain`` (extension: a ``pages.PageDomain`` of the page state's
+    bounds, e.g. ``PageIsolationState.candidate_domain``) replaces the dense
+    ``image_allow``.  Returns (M, None, 0): the slot width, no diagnostic score
+    chunk."""
     total_q = int(idx_q.shape[0])
     W = min(int(max_block), int(block_table.shape[1]))
     M = _out_slots(out_idx, topm, out_slots)
@@ -117,7 +120,8 @@ def route_prefill_triton(*, idx_q, k_bar, block_table, seq_lens, cu_seqlens_q, c
     ops.route(seqs, width=W, block_size=block_size, local_blocks=local_blocks,
               idx_scale=idx_scale, prior_floor=prior_floor, sigma=sigma, topm=int(topm), K=K,
               idx_q=idx_q, kbar=k_bar, block_table=bt, cand=cand,
-              out_idx=out_idx[:total_q], out_bias=out_bias[:total_q], out_width=M)
+              out_idx=out_idx[:total_q], out_bias=out_bias[:total_q], out_width=M,
+              page=page_domain)
     return M, None, 0
 
 
@@ -127,11 +131,12 @@ def route_decode_triton(*, idx_q, k_bar, block_table, seq_lens, image_allow, out
                         decode_query_len: int, idx_scale: float, prior_floor: float,
                         sigma: float, topm: int, score_buf=None, budget=None, out_slots=None,
                         entmax_base=None, entmax_fit=None, entmax_width: int = 0,
-                        score_buf_win=None, bounds=None):
+                        score_buf_win=None, bounds=None, page_domain=None):
     """Decode routing for ``nd = R * decode_query_len`` rows (the last
     ``decode_query_len`` tokens of each request).  The window-narrowing
     arguments of the reference are accepted; the fused kernel scans all
-    ``max_block`` columns of a row in one pass.  Returns the slot width M."""
+    ``max_block`` columns of a row in one pass.  ``page_domain`` as in
+    ``route_prefill_triton``.  Returns the slot width M."""
     nd = int(idx_q.shape[0])
     dql = max(1, int(decode_query_len))
     W = min(int(max_block), int(block_table.shape[1]))
@@ -145,5 +150,5 @@ def route_decode_triton(*, idx_q, k_bar, block_table, seq_lens, image_allow, out
     ops.route(seqs, width=W, block_size=block_size, local_blocks=local_blocks,
               idx_scale=idx_scale, prior_floor=prior_floor, sigma=sigma, topm=int(topm), K=K,
               idx_q=idx_q, kbar=k_bar, block_table=bt, cand=cand,
-              out_idx=out_idx[:nd], out_bias=out_bias[:nd], out_width=M)
+              out_idx=out_idx[:nd], out_bias=out_bias[:nd], out_width=M, page=page_domain)
     return M

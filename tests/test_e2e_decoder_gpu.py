@@ -63,3 +63,75 @@ def test_graph_decode_equals_eager():
     for e, r in zip(eager, replay):
         assert torch.equal(e, r)
     assert torch.equal(a.tok, b.tok) and torch.equal(a.seq_lens, b.seq_lens)
+
+
+# ---------------------------------------------------------------------------
+# page-aware candidates (the model's image_bucket_constraint): token ids lay
+# out pages of [marker] + image tokens followed by text
+# ---------------------------------------------------------------------------
+IMG, PG, PER = 900, 901, 41
+PAGE_CFG = dict(image_token_id=IMG, page_token_id=PG, per_page_image_tokens=PER)
+
+
+def doc_ids(S, n_pages, seed, per=PER):
+    """n_pages pages of ``per`` tokens (marker + image tokens), text after,
+    with one response-page marker 20 tokens into the text."""
+    ids = torch.randint(0, 800, (2, S), generator=torch.Generator().manual_seed(seed))
+    for p in range(n_pages):
+        ids[:, p * per] = PG
+        ids[:, p * per + 1:(p + 1) * per] = IMG
+    ids[:, n_pages * per + 20] = PG
+    return ids.cuda()
+
+
+def make_paged(seed=3, max_len=420):
+    return DashDecoder(CFG, batch=2, max_len=max_len, device=torch.device("cuda"), seed=seed,
+                       page_cfg=PAGE_CFG)
+
+
+def test_page_aware_prefill_plus_decode_equals_longer_prefill():
+    S = 333
+    ids = doc_ids(S + 1, 6, 4)
+    full = make_paged()
+    # the decode step numbers its text page as a response page: the longer
+    # prefill marks its last token as generated to match
+    ref = full.prefill(full.embed[ids], token_ids=ids,
+                       gen_start=torch.full((2,), S, dtype=torch.int64, device="cuda"))
+    part = make_paged()
+    part.prefill(part.embed[ids[:, :S]], token_ids=ids[:, :S])
+    part.tok.copy_(ids[:, S])
+    got = part.decode_step()
+    assert torch.isfinite(got).all() and torch.isfinite(ref).all()
+    err = (got.float() - ref.float()).abs().max().item()
+    assert err <= 0.02 * ref.float().abs().max().item(), err
+    # the page state after prefill + decode equals the state of the longer prefill
+    for a, b in zip(part.pst._slots, full.pst._slots):
+        assert torch.equal(a, b)
+    assert torch.equal(part.pst._blk_lo, full.pst._blk_lo)
+    assert torch.equal(part.pst._blk_hi, full.pst._blk_hi)
+
+
+def test_page_domain_equals_reference_allow_mask():
+    """The compact page domain routes exactly as the reference's dense allow
+    masks (``build_query_allow`` in prefill, ``decode_allow_fused`` in decode)
+    through the whole model: equal routes, equal logits; and the page-aware
+    routes differ from the unconstrained ones.  Pages of 200 tokens span
+    blocks outside the 2-block local window, and a query has more remote
+    blocks than K, so the page restriction changes what is routed."""
+    S = 1000
+    ids = doc_ids(S, 4, 5, per=200)
+    dom, ref = make_paged(max_len=1100), make_paged(max_len=1100)
+    dense = DashDecoder(CFG, batch=2, max_len=1100, device=torch.device("cuda"), seed=3)
+    dom.page_mask, ref.page_mask = False, True
+    a = dom.prefill(dom.embed[ids], token_ids=ids)
+    b = ref.prefill(ref.embed[ids], token_ids=ids)
+    dense.prefill(dense.embed[ids])
+    assert torch.equal(dom.last_route[0], ref.last_route[0])
+    assert torch.equal(dom.last_route[1], ref.last_route[1])
+    assert torch.equal(a, b)
+    assert not torch.equal(dom.last_route[0], dense.last_route[0])
+    for d in (dom, ref):
+        d.tok.fill_(IMG)
+    for _ in range(3):
+        assert torch.equal(dom.decode_step(), ref.decode_step())
+        assert torch.equal(dom.oi, ref.oi) and torch.equal(dom.ob, ref.ob)
