@@ -177,10 +177,25 @@ class DashRopeKVArgs(C.Structure):
                 ("device_error", _p)]
 
 
+class DashAttnBwdArgs(C.Structure):
+    _fields_ = [("q", _p), ("k", _p), ("v", _p), ("o", _p), ("dout", _p), ("dq", _p),
+                ("dk", _p), ("dv", _p), ("lse", _p), ("idx", _p), ("bias", _p), ("d_bias", _p),
+                ("delta", _p), ("flags", _p), ("n_seq", _i32), ("seq_len", _i32),
+                ("n_heads", _i32), ("n_kv_heads", _i32), ("head_dim", _i32), ("dtype", _i32),
+                ("block_size", _i32), ("local_window", _i32), ("K", _i32), ("pad0", _i32),
+                ("scale", _f32), ("pad1", _f32), ("device_error", _p)]
+
+
+class DashEntmaxArgs(C.Structure):
+    _fields_ = [("x", _p), ("y", _p), ("dy", _p), ("dx", _p), ("rows", _i64), ("stride", _i64),
+                ("n", _i32), ("pad0", _i32)]
+
+
 ABI_ORDER = [DashSeqs, DashKV, DashRoutes, DashQO, DashKbarArgs, DashRouteArgs,
              DashBlockMaxArgs, DashPrefillArgs, DashDecodeArgs, DashDeviceError,
              DashPageIdsArgs, DashPageStateArgs, DashPageAllowArgs, DashPageDecodeArgs,
-             DashBlockAnyArgs, DashPageBlocksArgs, DashIndexProjArgs, DashRopeKVArgs]
+             DashBlockAnyArgs, DashPageBlocksArgs, DashIndexProjArgs, DashRopeKVArgs,
+             DashAttnBwdArgs, DashEntmaxArgs]
 
 # every function the header declares
 EXPORTS = [
@@ -190,6 +205,7 @@ EXPORTS = [
     "dash_decode_attn_noalloc", "dash_noalloc_scratch_bytes", "dash_selftest_bounded_wait",
     "dash_page_ids", "dash_page_state_step", "dash_page_allow", "dash_page_decode_query",
     "dash_block_any", "dash_page_blocks", "dash_index_proj", "dash_rope_kv_write",
+    "dash_attn_bwd", "dash_attn_bwd_flag_words", "dash_entmax15_fwd", "dash_entmax15_bwd",
 ]
 
 
@@ -226,6 +242,9 @@ def load(path: str = LIB_PATH):
         ("dash_page_blocks", [C.POINTER(DashPageBlocksArgs), _p]),
         ("dash_index_proj", [C.POINTER(DashIndexProjArgs), _p]),
         ("dash_rope_kv_write", [C.POINTER(DashRopeKVArgs), _p]),
+        ("dash_attn_bwd", [C.POINTER(DashAttnBwdArgs), _p]),
+        ("dash_entmax15_fwd", [C.POINTER(DashEntmaxArgs), _p]),
+        ("dash_entmax15_bwd", [C.POINTER(DashEntmaxArgs), _p]),
     ]:
         f = getattr(L, name)
         f.argtypes = args
@@ -245,6 +264,8 @@ def load(path: str = LIB_PATH):
     L.dash_count_launches.restype = C.c_int
     L.dash_abi_sizes.argtypes = [C.POINTER(_i64), C.c_int]
     L.dash_abi_sizes.restype = C.c_int
+    L.dash_attn_bwd_flag_words.argtypes = [C.POINTER(DashAttnBwdArgs)]
+    L.dash_attn_bwd_flag_words.restype = C.c_int64
     L.dash_selftest_bounded_wait.argtypes = [C.c_uint64, _p, _p]
     L.dash_selftest_bounded_wait.restype = C.c_int
     _lib = L

@@ -105,7 +105,7 @@ int dash_count_launches(int reset) {
 }
 
 int dash_abi_sizes(int64_t* out, int n) {
-  const int64_t s[18] = {(int64_t)sizeof(DashSeqs),           (int64_t)sizeof(DashKV),
+  const int64_t s[20] = {(int64_t)sizeof(DashSeqs),           (int64_t)sizeof(DashKV),
                          (int64_t)sizeof(DashRoutes),         (int64_t)sizeof(DashQO),
                          (int64_t)sizeof(DashKbarArgs),       (int64_t)sizeof(DashRouteArgs),
                          (int64_t)sizeof(DashBlockMaxArgs),   (int64_t)sizeof(DashPrefillArgs),
@@ -113,9 +113,10 @@ int dash_abi_sizes(int64_t* out, int n) {
                          (int64_t)sizeof(DashPageIdsArgs),    (int64_t)sizeof(DashPageStateArgs),
                          (int64_t)sizeof(DashPageAllowArgs),  (int64_t)sizeof(DashPageDecodeArgs),
                          (int64_t)sizeof(DashBlockAnyArgs),   (int64_t)sizeof(DashPageBlocksArgs),
-                         (int64_t)sizeof(DashIndexProjArgs),  (int64_t)sizeof(DashRopeKVArgs)};
-  for (int i = 0; i < n && i < 18; ++i) out[i] = s[i];
-  return 18;
+                         (int64_t)sizeof(DashIndexProjArgs),  (int64_t)sizeof(DashRopeKVArgs),
+                         (int64_t)sizeof(DashAttnBwdArgs),    (int64_t)sizeof(DashEntmaxArgs)};
+  for (int i = 0; i < n && i < 20; ++i) out[i] = s[i];
+  return 20;
 }
 
 int dash_kbar_pool(const DashKbarArgs* a, dash_stream_t stream) {
@@ -355,6 +356,62 @@ int dash_block_any(const DashBlockAnyArgs* a, dash_stream_t stream) {
   if (a->rows > 0 && a->n_blocks > 0 && (!a->out || (a->len > 0 && !a->mask)))
     return set_error(DASH_ERR_INVALID, "null mask/out");
   return launch_block_any(*a, (cudaStream_t)stream);
+}
+
+static int check_attn_bwd(const DashAttnBwdArgs* a) {
+  if (!a) return set_error(DASH_ERR_INVALID, "null args");
+  if (a->n_seq < 0 || a->seq_len < 0) return set_error(DASH_ERR_INVALID, "negative size");
+  if (a->head_dim != 128) return set_error(DASH_ERR_UNSUPPORTED, "head_dim %d != 128", a->head_dim);
+  if (a->block_size <= 0 || a->block_size % 64)
+    return set_error(DASH_ERR_UNSUPPORTED, "block_size %d must be a positive multiple of 64", a->block_size);
+  if (a->local_window <= 0) return set_error(DASH_ERR_INVALID, "local_window must be > 0");
+  if (a->K < 0 || a->K > 256) return set_error(DASH_ERR_UNSUPPORTED, "K %d not in [0, 256]", a->K);
+  if (a->n_kv_heads <= 0 || a->n_heads % a->n_kv_heads)
+    return set_error(DASH_ERR_INVALID, "n_heads must be a multiple of n_kv_heads");
+  const int G = a->n_heads / a->n_kv_heads;
+  if (G != 1 && G != 2 && G != 4 && G != 8)
+    return set_error(DASH_ERR_UNSUPPORTED, "query heads per kv head %d not in {1,2,4,8}", G);
+  if (a->dtype != DASH_DTYPE_BF16 && a->dtype != DASH_DTYPE_F16 && a->dtype != DASH_DTYPE_F32)
+    return set_error(DASH_ERR_UNSUPPORTED, "dtype must be bf16, fp16 or fp32");
+  return DASH_OK;
+}
+
+int64_t dash_attn_bwd_flag_words(const DashAttnBwdArgs* a) {
+  if (check_attn_bwd(a)) return -1;
+  return (int64_t)attn_bwd_flag_words(*a);
+}
+
+int dash_attn_bwd(const DashAttnBwdArgs* a, dash_stream_t stream) {
+  int rc = check_attn_bwd(a);
+  if (rc) return rc;
+  if ((int64_t)a->n_seq * a->seq_len == 0) return DASH_OK;
+  if (!a->q || !a->k || !a->v || !a->o || !a->dout || !a->dq || !a->dk || !a->dv || !a->lse ||
+      !a->delta || !a->flags || (a->K > 0 && !a->idx))
+    return set_error(DASH_ERR_INVALID, "null pointer");
+  const void* vec[] = {a->q, a->k, a->v, a->o, a->dout, a->dq, a->dk, a->dv};
+  for (const void* p : vec)
+    if (!aligned16(p)) return set_error(DASH_ERR_INVALID, "q/k/v/o/dout/dq/dk/dv must be 16-byte aligned");
+  if (a->scale <= 0.f) return set_error(DASH_ERR_INVALID, "scale must be > 0");
+  return launch_attn_bwd(*a, (cudaStream_t)stream);
+}
+
+static int check_entmax(const DashEntmaxArgs* a, bool bwd) {
+  if (!a) return set_error(DASH_ERR_INVALID, "null args");
+  if (a->rows < 0 || a->n < 0) return set_error(DASH_ERR_INVALID, "negative size");
+  if (a->rows > 0 && a->stride < a->n) return set_error(DASH_ERR_INVALID, "row stride < n");
+  if (a->rows > 0 && a->n > 0 && (bwd ? (!a->y || !a->dy || !a->dx) : (!a->x || !a->y)))
+    return set_error(DASH_ERR_INVALID, "null pointer");
+  return DASH_OK;
+}
+
+int dash_entmax15_fwd(const DashEntmaxArgs* a, dash_stream_t stream) {
+  int rc = check_entmax(a, false);
+  return rc ? rc : launch_entmax15(*a, false, (cudaStream_t)stream);
+}
+
+int dash_entmax15_bwd(const DashEntmaxArgs* a, dash_stream_t stream) {
+  int rc = check_entmax(a, true);
+  return rc ? rc : launch_entmax15(*a, true, (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -27,5 +27,8 @@ int launch_block_any(const DashBlockAnyArgs& a, cudaStream_t st);
 int launch_page_blocks(const DashPageBlocksArgs& a, cudaStream_t st);
 int launch_index_proj(const DashIndexProjArgs& a, cudaStream_t st);
 int launch_rope_kv(const DashRopeKVArgs& a, cudaStream_t st);
+int launch_attn_bwd(const DashAttnBwdArgs& a, cudaStream_t st);
+size_t attn_bwd_flag_words(const DashAttnBwdArgs& a);
+int launch_entmax15(const DashEntmaxArgs& a, bool backward, cudaStream_t st);
 
 }  // namespace dash

@@ -4,6 +4,7 @@ any non-zero library status; there is no CPU path.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 from dataclasses import dataclass
 from typing import Optional
@@ -360,6 +361,73 @@ def gather_attention(q, k, v, idx, bias, *, block_size: int, local_window: int, 
     a.device_error = device_error.ptr if device_error is not None else None
     prefill_attn(a, q.device, workspace)
     return out
+
+
+# ---------------------------------------------------------------------------
+# training backward
+# ---------------------------------------------------------------------------
+def gather_attention_bwd(q, k, v, o, dout, lse, idx, bias, *, block_size: int,
+                         local_window: int, scale: float, want_d_bias: bool = True,
+                         device_error: Optional[DeviceErrorWord] = None):
+    """Backward of the contiguous gather attention (``dash_attn_bwd``).
+
+    q, o, dout [B, T, HQ, D]; k, v [B, T, Hkv, D] (made contiguous, one dtype);
+    lse [B, T, HQ] fp32 (natural log, from the forward); idx [B, T, K] int
+    (-1 unused), bias [B, T, K] fp32 or None.  Returns (dq, dk, dv, d_bias)
+    with d_bias [B, T, K] fp32 (None unless ``want_d_bias``)."""
+    _need_cuda(q, k, v, o, dout, lse, idx)
+    dt = q.dtype
+    q, o, dout = (t.to(dt).contiguous() for t in (q, o, dout))
+    k, v = k.to(dt).contiguous(), v.to(dt).contiguous()
+    B, T, HQ, D = q.shape
+    Hkv = k.shape[2]
+    idx = idx.to(torch.int32).contiguous()
+    K = idx.shape[-1]
+    bias = None if bias is None else bias.to(torch.float32).contiguous()
+    lse = lse.to(torch.float32).contiguous()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    d_bias = torch.empty(B, T, K, dtype=torch.float32, device=q.device) if want_d_bias else None
+    delta = torch.empty(B, T, HQ, dtype=torch.float32, device=q.device)
+    a = L.DashAttnBwdArgs()
+    a.n_seq, a.seq_len, a.n_heads, a.n_kv_heads, a.head_dim = B, T, HQ, Hkv, D
+    a.dtype, a.block_size, a.local_window, a.K = _DT[dt], int(block_size), int(local_window), K
+    a.scale = float(scale)
+    words = L.load().dash_attn_bwd_flag_words(ctypes.byref(a))
+    if words < 0:
+        raise L.DashError(L.DASH_ERR_UNSUPPORTED, L.last_error())
+    flags = torch.empty(max(1, words), dtype=torch.int32, device=q.device)
+    a.q, a.k, a.v, a.o, a.dout = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), dout.data_ptr()
+    a.dq, a.dk, a.dv = dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
+    a.lse, a.idx, a.bias = lse.data_ptr(), idx.data_ptr(), _ptr(bias)
+    a.d_bias, a.delta, a.flags = _ptr(d_bias), delta.data_ptr(), flags.data_ptr()
+    a.device_error = device_error.ptr if device_error is not None else None
+    L.call("dash_attn_bwd", a)
+    return dq, dk, dv, d_bias
+
+
+def entmax15(x: torch.Tensor) -> torch.Tensor:
+    """1.5-entmax over the last dim (``dash_entmax15_fwd``), fp32."""
+    _need_cuda(x)
+    x = x.to(torch.float32).contiguous()
+    y = torch.empty_like(x)
+    a = L.DashEntmaxArgs()
+    n = x.shape[-1] if x.dim() else 1
+    a.x, a.y, a.rows, a.n, a.stride = x.data_ptr(), y.data_ptr(), x.numel() // max(1, n), n, n
+    L.call("dash_entmax15_fwd", a)
+    return y
+
+
+def entmax15_backward(y: torch.Tensor, dy: torch.Tensor) -> torch.Tensor:
+    """Jacobian-vector product of 1.5-entmax (``dash_entmax15_bwd``), fp32."""
+    _need_cuda(y, dy)
+    y = y.to(torch.float32).contiguous()
+    dy = dy.to(torch.float32).contiguous()
+    dx = torch.empty_like(y)
+    a = L.DashEntmaxArgs()
+    n = y.shape[-1]
+    a.y, a.dy, a.dx, a.rows, a.n, a.stride = y.data_ptr(), dy.data_ptr(), dx.data_ptr(), y.numel() // max(1, n), n, n
+    L.call("dash_entmax15_bwd", a)
+    return dx
 
 
 # ---------------------------------------------------------------------------

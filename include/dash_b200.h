@@ -590,6 +590,59 @@ typedef struct {
 int dash_rope_kv_write(const DashRopeKVArgs* args, dash_stream_t stream);
 
 /* ---------------------------------------------------------------------- */
+/* dash_attn_bwd -- training backward of the contiguous gather attention.
+ * Replaces: sparse_gather_e2e_triton.py:118-189 (_e2e_attn_bwd_dq_kernel,
+ *           with the d_bias atomics), :192-262 (_e2e_attn_bwd_dkv_kernel)
+ *           and :319-337 (_E2EGatherAttnFn.backward: delta, block mask).
+ * q, o, dout, dq: [n_seq, seq_len, n_heads, head_dim]; k, v, dk, dv:
+ * [n_seq, seq_len, n_kv_heads, head_dim]; all contiguous, one dtype, 16-byte
+ * aligned.  lse [n_seq, seq_len, n_heads] (natural log, as the forward
+ * writes it).  idx / bias [n_seq, seq_len, K]: one routed list per token
+ * shared by all heads (-1 unused; later duplicates and ids outside the
+ * sequence's blocks are ignored; bias NULL = 0).  d_bias (optional)
+ * [n_seq, seq_len, K]: gradient of each slot's bias (0 on ignored slots),
+ * summed over all heads.  Scratch: delta [n_seq, seq_len, n_heads] fp32 and
+ * flags (dash_attn_bwd_flag_words() uint32 words).  head_dim 128, block_size
+ * a multiple of 64, n_heads / n_kv_heads in {1, 2, 4, 8}, K <= 256.          */
+typedef struct {
+  const void* q; const void* k; const void* v; const void* o; const void* dout;
+  void* dq; void* dk; void* dv;
+  const float* lse;
+  const int32_t* idx;
+  const float* bias;
+  float* d_bias;
+  float* delta;
+  uint32_t* flags;
+  int32_t n_seq, seq_len, n_heads, n_kv_heads;
+  int32_t head_dim, dtype, block_size, local_window;
+  int32_t K, pad0;
+  float scale, pad1;
+  DashDeviceError* device_error;
+} DashAttnBwdArgs;
+int dash_attn_bwd(const DashAttnBwdArgs* args, dash_stream_t stream);
+int64_t dash_attn_bwd_flag_words(const DashAttnBwdArgs* args);
+
+/* dash_entmax15_fwd / dash_entmax15_bwd -- dense 1.5-entmax over rows of n
+ * and its Jacobian-vector product (training prior).
+ * Replaces: dash_attention.py:623-658 (_entmax_threshold_and_support,
+ *           _Entmax15.forward / backward).
+ * fwd: x -> y = relu((x - max x)/2 - tau)^2 with sum y... = 1 at tau.
+ * bwd: y, dy -> dx = dy*g - g * sum(dy*g) / max(sum g, 1e-12), g = sqrt(y).
+ * All fp32 with a common row stride (elements).                             */
+typedef struct {
+  const float* x;
+  float* y;
+  const float* dy;
+  float* dx;
+  int64_t rows;
+  int64_t stride;
+  int32_t n;
+  int32_t pad0;
+} DashEntmaxArgs;
+int dash_entmax15_fwd(const DashEntmaxArgs* args, dash_stream_t stream);
+int dash_entmax15_bwd(const DashEntmaxArgs* args, dash_stream_t stream);
+
+/* ---------------------------------------------------------------------- */
 /* Diagnostics */
 int dash_last_error(char* buf, int len);     /* copies the last host-side error message */
 int dash_library_version(void);              /* (major << 16) | minor */
@@ -598,7 +651,7 @@ int dash_count_launches(int reset);          /* kernels launched by this library
  * DashQO, DashKbarArgs, DashRouteArgs, DashBlockMaxArgs, DashPrefillArgs,
  * DashDecodeArgs, DashDeviceError, DashPageIdsArgs, DashPageStateArgs,
  * DashPageAllowArgs, DashPageDecodeArgs, DashBlockAnyArgs, DashPageBlocksArgs,
- * DashIndexProjArgs, DashRopeKVArgs.  Lets a binding
+ * DashIndexProjArgs, DashRopeKVArgs, DashAttnBwdArgs, DashEntmaxArgs.  Lets a binding
  * verify its struct layouts; returns the number of sizes available. */
 int dash_abi_sizes(int64_t* out, int n);
 /* Self-test of the bounded waits every kernel uses (no reference counterpart):

@@ -521,6 +521,69 @@ def frontend_case(name, seed):
     print(name, "saved")
 
 
+def backward_case(name, seed):
+    """The reference's training backward (_E2EGatherAttnFn.backward: the Triton
+    dq/d_bias and dk/dv kernels, interpreted on the CPU, fp32) and its entmax
+    Jacobian (_Entmax15) on small shapes.  Routed lists hold -1 slots and ids
+    of blocks inside the local window; no duplicate ids (the reference's
+    dedup keeps an unspecified one of equal ids)."""
+    import ananta_ref.sparse_gather_e2e_triton as e2e
+    import ananta_ref.dash_attention as da
+    rng = np.random.default_rng(seed)
+    out = {}
+
+    def bf16_exact(a):
+        # inputs representable in bf16 (stored as uint16): the same values drive
+        # the fp32 and the bf16 kernels
+        return torch.tensor(a).to(torch.bfloat16).float().numpy()
+
+    def as_u16(a):
+        return torch.tensor(a).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+
+    for c, (B, HQ, H, T, bs, LW, K) in enumerate([(1, 1, 1, 128, 64, 64, 2),
+                                                   (1, 2, 1, 192, 64, 64, 2)]):
+        D = 128
+        q = bf16_exact(rng.standard_normal((B, HQ, T, D)) * 0.5)
+        k = bf16_exact(rng.standard_normal((B, H, T, D)) * 0.5)
+        v = bf16_exact(rng.standard_normal((B, H, T, D)) * 0.5)
+        do = bf16_exact(rng.standard_normal((B, HQ, T, D)))
+        nblk = (T + bs - 1) // bs
+        idx = np.full((B, T, K), -1, np.int32)
+        for b in range(B):
+            for t in range(T):
+                pool = list(range(0, t // bs + 1))        # remote and window blocks
+                n = min(K, len(pool), int(rng.integers(0, K + 1)))
+                if n:
+                    idx[b, t, :n] = rng.choice(pool, size=n, replace=False)
+        bias = (rng.standard_normal((B, T, K)) * 0.5).astype(np.float32)
+        tq, tk, tv = (torch.tensor(a, requires_grad=True) for a in (q, k, v))
+        tb = torch.tensor(bias, requires_grad=True)
+        o = e2e.triton_gather_attention_e2e(tq, tk, tv, torch.tensor(idx)[:, None], tb,
+                                            torch.arange(T)[None].expand(B, T), None, bs,
+                                            1.0 / math.sqrt(D), LW)
+        node = o.grad_fn.next_functions[0][0]
+        lse = node.saved_tensors[-1].detach().numpy()              # [B, T, HQ]
+        o.backward(torch.tensor(do))
+        tr = lambda a: np.ascontiguousarray(a.transpose(0, 2, 1, 3))   # -> [B, T, heads, D]
+        out.update({f"c{c}_q": as_u16(tr(q)), f"c{c}_k": as_u16(tr(k)), f"c{c}_v": as_u16(tr(v)),
+                    f"c{c}_do": as_u16(tr(do)),
+                    f"c{c}_idx": idx, f"c{c}_bias": bias, f"c{c}_o": tr(o.detach().numpy()),
+                    f"c{c}_lse": lse, f"c{c}_dq": tr(tq.grad.numpy()), f"c{c}_dk": tr(tk.grad.numpy()),
+                    f"c{c}_dv": tr(tv.grad.numpy()), f"c{c}_dbias": tb.grad.numpy(),
+                    f"c{c}_cfg": np.array([B, HQ, H, T, bs, LW, K])})
+    # entmax: rows like _route's input (masked entries at -1e4, scaled scores)
+    x = (rng.standard_normal((40, 37)) * 3).astype(np.float32)
+    x[rng.random(x.shape) < 0.3] = -1e4
+    x[:, 0] = rng.standard_normal(40) * 3
+    tx = torch.tensor(x, requires_grad=True)
+    y = da.entmax15(tx, -1)
+    dy = rng.standard_normal(x.shape).astype(np.float32)
+    y.backward(torch.tensor(dy))
+    out.update(ent_x=x, ent_y=y.detach().numpy(), ent_dy=dy, ent_dx=tx.grad.numpy())
+    np.savez_compressed(os.path.join(HERE, name + ".npz"), **out)
+    print(name, "saved")
+
+
 def main():
     da, md = import_reference()
     torch.set_num_threads(os.cpu_count())
@@ -538,6 +601,7 @@ def main():
     triton_interp_case(da, md, "triton_interp", seed=5)
     page_aware_case("page_aware", seed=6)
     frontend_case("frontend", seed=7)
+    backward_case("backward", seed=8)
 
 
 if __name__ == "__main__":

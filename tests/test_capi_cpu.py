@@ -14,7 +14,7 @@ HEADER = os.path.join(os.path.dirname(os.path.dirname(__file__)), "include", "da
 
 def declared_functions():
     text = open(HEADER).read()
-    return sorted(set(re.findall(r"^\s*(?:int|size_t)\s+(dash_\w+)\s*\(", text, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|int64_t|size_t)\s+(dash_\w+)\s*\(", text, re.M)))
 
 
 def test_header_and_binding_agree():
@@ -128,3 +128,29 @@ def test_package_fails_loudly_without_library(tmp_path):
             L.load(str(tmp_path / "missing.so"))
         finally:
             L._lib = saved
+
+
+def test_attn_bwd_rejects_bad_arguments():
+    a = L.DashAttnBwdArgs()
+    a.n_seq, a.seq_len, a.n_heads, a.n_kv_heads, a.head_dim = 1, 128, 4, 2, 128
+    a.dtype, a.block_size, a.local_window, a.K, a.scale = L.DTYPE_BF16, 64, 64, 4, 0.1
+    assert L.load().dash_attn_bwd_flag_words(C.byref(a)) == 2 * 4
+    for field, bad in (("head_dim", 64), ("block_size", 32), ("K", 300), ("n_heads", 3),
+                       ("n_heads", 32), ("dtype", 9)):
+        old = getattr(a, field)
+        setattr(a, field, bad)
+        assert _call_status("dash_attn_bwd", a) != 0, field
+        assert L.load().dash_attn_bwd_flag_words(C.byref(a)) == -1
+        setattr(a, field, old)
+    assert _call_status("dash_attn_bwd", a) == L.DASH_ERR_INVALID     # null pointers
+    assert "null" in L.last_error()
+
+
+def test_entmax_rejects_bad_arguments():
+    a = L.DashEntmaxArgs()
+    a.rows, a.n, a.stride = 4, 10, 5
+    assert _call_status("dash_entmax15_fwd", a) == L.DASH_ERR_INVALID
+    a.stride = 10
+    assert _call_status("dash_entmax15_bwd", a) == L.DASH_ERR_INVALID
+    a.rows = 0
+    assert _call_status("dash_entmax15_fwd", a) == 0
