@@ -180,7 +180,7 @@ class DashRopeKVArgs(C.Structure):
 class DashAttnBwdArgs(C.Structure):
     _fields_ = [("q", _p), ("k", _p), ("v", _p), ("o", _p), ("dout", _p), ("dq", _p),
                 ("dk", _p), ("dv", _p), ("lse", _p), ("idx", _p), ("bias", _p), ("d_bias", _p),
-                ("delta", _p), ("flags", _p), ("n_seq", _i32), ("seq_len", _i32),
+                ("delta", _p), ("flags", _p), ("dq_acc", _p), ("n_seq", _i32), ("seq_len", _i32),
                 ("n_heads", _i32), ("n_kv_heads", _i32), ("head_dim", _i32), ("dtype", _i32),
                 ("block_size", _i32), ("local_window", _i32), ("K", _i32), ("pad0", _i32),
                 ("scale", _f32), ("pad1", _f32), ("device_error", _p)]

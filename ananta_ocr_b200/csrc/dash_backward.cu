@@ -505,12 +505,9 @@ int launch_attn_bwd(const DashAttnBwdArgs& a, cudaStream_t st) {
   count_launch();
   int rc = check_launch("bwd_flags_kernel");
   if (rc) return rc;
-  const int G = a.n_heads / a.n_kv_heads;
-  switch (a.dtype) {
-    case DASH_DTYPE_BF16: return launch_bwd_g<__nv_bfloat16>(a, G, nblk, words, st);
-    case DASH_DTYPE_F16: return launch_bwd_g<__half>(a, G, nblk, words, st);
-    default: return launch_bwd_g<float>(a, G, nblk, words, st);
-  }
+  // 16-bit inputs: tensor cores (dash_backward_tc.cu); fp32: the kernels above
+  if (a.dtype == DASH_DTYPE_BF16 || a.dtype == DASH_DTYPE_F16) return launch_attn_bwd_tc(a, nblk, words, st);
+  return launch_bwd_g<float>(a, a.n_heads / a.n_kv_heads, nblk, words, st);
 }
 
 int launch_entmax15(const DashEntmaxArgs& a, bool backward, cudaStream_t st) {

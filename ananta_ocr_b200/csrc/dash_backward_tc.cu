@@ -1,0 +1,501 @@
+// dash_backward_tc.cu -- training backward of the DASH gather attention on
+// sm_100a tensor cores (bf16 / fp16 inputs, fp32 accumulation).
+//
+// Same semantics as the CUDA-core kernels of dash_backward.cu
+// (sparse_gather_e2e_triton.py:118-262), key-tile major with gathered query
+// rows, so no query row is multiplied against a block it did not route:
+//
+// Work unit: one CTA per (128-key tile, kv head, sequence).  The tile's rows
+// are the query rows that routed one of its (at most two) blocks with a key
+// below their local window (per-block row bitmask of bwd_flags_kernel) plus
+// the rows whose window reaches a key of the tile.  They are processed in
+// batches of 128 slots (a slot = a query row x one of the G query heads of
+// this kv head):
+//   math warps 0-3   gather the slots' q and dout rows into shared memory
+//                    (128-byte swizzle, K-major), per-slot lse / delta /
+//                    routed flags / biases
+//   MMA warp 4       S^T  = K  Q^T        (M = 128 keys, N = 128 slots, K = d)
+//                    dP^T = V  dO^T
+//   math warps       thread = key: P^T = exp(s*scale + bias - lse) on the kept
+//                    keys, dS^T = P^T (dP^T - delta); P^T and dS^T (bf16)
+//                    back into TMEM over S^T / dP^T, dS^T also into shared
+//                    memory (MN-major); per-slot column sums of the remote
+//                    dS^T (butterfly reduce-scatter) -> slot-bias gradient
+//   MMA warp         dV += P^T dO,  dK += dS^T Q   (A from TMEM)
+//                    dQ  = dS K                    (A and B MN-major, shared)
+//   math warps       thread = slot: dQ rows from TMEM -> fp32 atomics
+// After the last batch dK (x scale) and dV leave TMEM, one row per thread.
+// TMEM: S^T | dP^T | dV | dK, 128 columns each; dQ uses the upper halves of
+// the S^T and dP^T columns (P^T / dS^T, packed bf16, take the lower halves).
+// Every wait is bounded (abort flag + time limit, DASH_DEV_TIMEOUT).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <climits>
+#include "dash_common.cuh"
+#include "dash_internal.h"
+
+namespace dash {
+namespace {
+
+constexpr int TK = 128;                  // keys per CTA
+constexpr int NS = 128;                  // slots per batch
+constexpr int kTcThreads = 160;          // 4 math warps + 1 MMA warp
+constexpr int OFF_K = 0;                 // [2 halves][128 keys][128 B]
+constexpr int OFF_V = 32768;
+constexpr int OFF_Q = 65536;             // [2 halves][128 slots][128 B]
+constexpr int OFF_DO = 98304;
+constexpr int OFF_DS = 131072;           // dS^T MN-major: [2 slot halves][128 keys][128 B]
+constexpr int OFF_META = 163840;
+// meta arrays of NS entries: pos, row (global), hq, slotA, slotB, routed (int);
+// cloc, clA, clB, delta (float); dsum [4 warps][NS] (float)
+constexpr int META_WORDS = 10 * NS + 4 * NS + 8;
+constexpr int OFF_BAR = OFF_META + META_WORDS * 4;
+constexpr int SMEM_TC = OFF_BAR + 128 + 1024;    // + alignment slack
+static_assert(SMEM_TC <= 232448, "shared memory budget");
+constexpr uint32_t TMEM_COLS = 512;
+
+template <typename E> struct Fmt;
+template <> struct Fmt<__nv_bfloat16> {
+  static constexpr uint32_t v = 1;
+  static __device__ __forceinline__ float tof(__nv_bfloat16 x) { return __bfloat162float(x); }
+  static __device__ __forceinline__ uint32_t pack(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  static __device__ __forceinline__ void st(__nv_bfloat16* p, float x) { *p = __float2bfloat16_rn(x); }
+};
+template <> struct Fmt<__half> {
+  static constexpr uint32_t v = 0;
+  static __device__ __forceinline__ float tof(__half x) { return __half2float(x); }
+  static __device__ __forceinline__ uint32_t pack(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  static __device__ __forceinline__ void st(__half* p, float x) { *p = __float2half_rn(x); }
+};
+
+__device__ __forceinline__ void math_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// barrier of the 4 math warps that also ANDs a predicate over them: every
+// math warp leaves a failed wait together (none is left at a later barrier)
+__device__ __forceinline__ bool math_all(bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.and.pred po, 1, 128, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)p)
+      : "memory");
+  return r != 0;
+}
+
+// one 256-byte row (128 x 16-bit) -> K-major 128-byte-swizzled buffer of 128 rows
+__device__ __forceinline__ void st_row_sw128(uint8_t* buf, int row, const uint4* src, bool zero) {
+#pragma unroll
+  for (int cc = 0; cc < 16; ++cc) {
+    const uint4 v = zero ? make_uint4(0, 0, 0, 0) : src[cc];
+    const int region = cc >> 3, c8 = cc & 7;
+    *reinterpret_cast<uint4*>(buf + region * 16384 + row * 128 + ((c8 ^ (row & 7)) << 4)) = v;
+  }
+}
+
+__device__ __forceinline__ uint64_t kmaj_desc(uint32_t base, int kk) {
+  return sw128_desc(base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+}
+__device__ __forceinline__ uint64_t mn_desc(uint32_t base, int kk) {
+  return sw128_desc(base + kk * 2048, 16384, 1024);
+}
+
+// 32 values per lane -> lane c holds the sum over the warp of value c
+__device__ __forceinline__ float reduce_scatter32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const bool up = lane & off;
+#pragma unroll
+    for (int k = 0; k < off; ++k) {
+      const float send = up ? v[k] : v[k + off];
+      const float keep = up ? v[k + off] : v[k];
+      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  return v[0];
+}
+
+template <typename E>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    bwd_tc_kernel(const DashAttnBwdArgs a, int nblk, int words, int ntiles, float* dq_acc) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  int* m_pos = reinterpret_cast<int*>(sm + OFF_META);
+  int* m_row = m_pos + NS;
+  int* m_hq = m_row + NS;
+  int* m_sA = m_hq + NS;
+  int* m_sB = m_sA + NS;
+  int* m_routed = m_sB + NS;
+  float* m_cloc = reinterpret_cast<float*>(m_routed + NS);
+  float* m_clA = m_cloc + NS;
+  float* m_clB = m_clA + NS;
+  float* m_delta = m_clB + NS;
+  float* m_dsum = m_delta + NS;                 // [4][NS]
+  int* m_ns = reinterpret_cast<int*>(m_dsum + 4 * NS);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
+  uint64_t* rows_full = bars + 0;
+  uint64_t* s_full = bars + 1;
+  uint64_t* p_full = bars + 2;
+  uint64_t* pv_done = bars + 3;
+  uint64_t* fin = bars + 4;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 6);
+  DeviceError* derr = a.device_error;
+
+  const int T = a.seq_len, HQ = a.n_heads, H = a.n_kv_heads, G = HQ / H;
+  const int s = blockIdx.x / ntiles, tl = blockIdx.x - s * ntiles;
+  const int h = blockIdx.y;
+  const int key0 = tl * TK;
+  const int bs = a.block_size, LW = a.local_window;
+  const int bA = key0 / bs, bB = min(key0 + TK - 1, T - 1) / bs;
+  const int jB = bB != bA ? bB * bs - key0 : TK;        // first tile key of block B
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t kv_row = (int64_t)H * 128;
+  const int64_t kvoff = ((int64_t)s * T * H + h) * 128;
+  const uint32_t* flA = a.flags + ((int64_t)s * nblk + bA) * words;
+  const uint32_t* flB = a.flags + ((int64_t)s * nblk + bB) * words;
+
+  if (tid == 0) {
+    mbar_init(rows_full, 4);
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 4);
+    mbar_init(pv_done, 1);
+    mbar_init(fin, 1);
+    *abort_flag = 0;
+    mbar_init_fence();
+  }
+  if (warp == 4) { tmem_alloc(tmem_holder, TMEM_COLS); tmem_relinquish(); }
+  if (tid < TK) {
+    const int key = key0 + tid;
+    const bool z = key >= T;
+    const uint4* kp = reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(a.k) + kvoff + (int64_t)(z ? 0 : key) * kv_row);
+    const uint4* vp = reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(a.v) + kvoff + (int64_t)(z ? 0 : key) * kv_row);
+    st_row_sw128(sm + OFF_K, tid, kp, z);
+    st_row_sw128(sm + OFF_V, tid, vp, z);
+    fence_proxy_async_smem();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 384;
+  constexpr uint32_t fmt = Fmt<E>::v;
+
+  if (warp == 4) {
+    // ============================ MMA issuer ============================
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = make_idesc(fmt, 0, 0, TK, NS);
+      constexpr uint32_t idesc_acc = make_idesc(fmt, 0, 1, TK, 128);
+      constexpr uint32_t idesc_dq = make_idesc(fmt, 1, 1, NS, 64);
+      const uint32_t sK = smem_u32(sm + OFF_K), sV = smem_u32(sm + OFF_V);
+      const uint32_t sQ = smem_u32(sm + OFF_Q), sDO = smem_u32(sm + OFF_DO), sDS = smem_u32(sm + OFF_DS);
+      for (int b = 0;; ++b) {
+        if (!mbar_wait(rows_full, b & 1, abort_flag, derr, 80)) break;
+        tc_fence_after();
+        if (*reinterpret_cast<volatile int*>(m_ns) == 0) break;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) umma_ss(tS, kmaj_desc(sK, kk), kmaj_desc(sQ, kk), idesc_s, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) umma_ss(tDP, kmaj_desc(sV, kk), kmaj_desc(sDO, kk), idesc_s, kk > 0);
+        umma_commit(s_full);
+        if (!mbar_wait(p_full, b & 1, abort_flag, derr, 81)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) umma_ts(tDV, tS + kk * 8, mn_desc(sDO, kk), idesc_acc, (b > 0 || kk > 0));
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) umma_ts(tDK, tDP + kk * 8, mn_desc(sQ, kk), idesc_acc, (b > 0 || kk > 0));
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) umma_ss(tS + 64, mn_desc(sDS, kk), mn_desc(sK, kk), idesc_dq, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) umma_ss(tDP + 64, mn_desc(sDS, kk), mn_desc(sK + 16384, kk), idesc_dq, kk > 0);
+        umma_commit(pv_done);
+      }
+      // every MMA of this CTA completes before TMEM is released
+      umma_commit(fin);
+      volatile int no_abort = 0;
+      mbar_wait(fin, 0, &no_abort, nullptr, 82);
+    }
+    __syncwarp();
+  } else {
+    // ============================ math warps ============================
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const float LOG2E = 1.4426950408889634f;
+    const float sl2 = a.scale * LOG2E;
+    const int key = key0 + tid;
+    const bool keyB = tid >= jB;
+    const int64_t loc_end = min((int64_t)key0 + TK - 1 + LW - 1, (int64_t)T - 1);
+    // row cursor (thread 0): word w, bits m not yet taken
+    int cw = (key0 >> 5) - 1;
+    uint32_t cm = 0u;
+    int nb = 0;
+    bool alive = true;
+    while (alive) {
+      if (nb > 0) {
+        // ---- dQ of batch nb-1 -> fp32 accumulator ----
+        if (!math_all(mbar_wait_warp(pv_done, (nb - 1) & 1, abort_flag, derr, 83))) { alive = false; break; }
+        tc_fence_after();
+        const int ns_prev = *m_ns;
+#pragma unroll 1
+        for (int q4 = 0; q4 < 4; ++q4) {
+          float v[32];
+          tmem_ld32f((q4 < 2 ? tS : tDP) + 64 + (q4 & 1) * 32 + lane_base, v);
+          tmem_ld_wait();
+          if (tid < ns_prev) {
+            float4* dst = reinterpret_cast<float4*>(dq_acc + ((int64_t)m_row[tid] * HQ + m_hq[tid]) * 128 +
+                                                    (q4 >> 1) * 64 + (q4 & 1) * 32);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) atomicAdd(dst + c, make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]));
+          }
+        }
+      }
+      math_bar();
+      // ---- next batch of rows ----
+      if (tid == 0) {
+        int cnt = 0;
+        const int cap = NS / G;
+        int* rows = m_pos;              // scratch: row ids, expanded to slots below
+        while (cnt < cap) {
+          if (cm == 0u) {
+            if (++cw >= words) break;
+            uint32_t m = flA[cw] | (bB != bA ? flB[cw] : 0u);
+            const int64_t r0 = (int64_t)cw * 32;
+            const int64_t lo = max(r0, (int64_t)key0), hi = min(r0 + 31, loc_end);
+            if (lo <= hi) {
+              const int nbits = (int)(hi - lo + 1);
+              m |= (nbits == 32 ? 0xffffffffu : ((1u << nbits) - 1u)) << (int)(lo - r0);
+            }
+            if (r0 < key0) m &= ~((1u << (key0 - r0)) - 1u);
+            cm = m;
+            continue;
+          }
+          const int bit = __ffs(cm) - 1;
+          cm &= cm - 1u;
+          const int i = cw * 32 + bit;
+          if (i >= T) { cm = 0u; cw = words; break; }
+          rows[cnt++] = i;
+        }
+        for (int r = cnt - 1; r >= 0; --r) {      // expand rows to slots in place (back to front)
+          const int i = rows[r];
+          for (int g = G - 1; g >= 0; --g) { m_pos[r * G + g] = i; m_hq[r * G + g] = h * G + g; }
+        }
+        *m_ns = cnt * G;
+      }
+      math_bar();
+      const int ns = *m_ns;
+      if (ns == 0) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(rows_full);
+        break;
+      }
+      // ---- gather slot tid ----
+      {
+        const bool live = tid < ns;
+        const int i = live ? m_pos[tid] : 0;
+        const int hq = live ? m_hq[tid] : 0;
+        const int64_t row = (int64_t)s * T + i;
+        const int64_t off = (row * HQ + hq) * 128;
+        st_row_sw128(sm + OFF_Q, tid, reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(a.q) + off), !live);
+        st_row_sw128(sm + OFF_DO, tid, reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(a.dout) + off), !live);
+        int routed = 0, sA = -1, sB = -1;
+        float lse = 0.f, delta = 0.f, biasA = 0.f, biasB = 0.f;
+        if (live) {
+          lse = a.lse[row * HQ + hq];
+          delta = a.delta[row * HQ + hq];
+          if ((flA[i >> 5] >> (i & 31)) & 1u) routed |= 1;
+          if (bB != bA && ((flB[i >> 5] >> (i & 31)) & 1u)) routed |= 2;
+          const int32_t* ids = a.idx + row * a.K;
+          for (int jj = 0; jj < a.K && (((routed & 1) && sA < 0) || ((routed & 2) && sB < 0)); ++jj) {
+            const int b = ids[jj];
+            if ((routed & 1) && sA < 0 && b == bA) sA = jj;
+            if ((routed & 2) && sB < 0 && b == bB) sB = jj;
+          }
+          if (a.bias) {
+            if (sA >= 0) biasA = a.bias[row * a.K + sA];
+            if (sB >= 0) biasB = a.bias[row * a.K + sB];
+          }
+        }
+        m_row[tid] = (int)row;
+        m_routed[tid] = routed;
+        m_sA[tid] = sA;
+        m_sB[tid] = sB;
+        m_cloc[tid] = -lse * LOG2E;
+        m_clA[tid] = (biasA - lse) * LOG2E;
+        m_clB[tid] = (biasB - lse) * LOG2E;
+        m_delta[tid] = delta;
+        if (!live) m_pos[tid] = INT_MIN / 2;      // no key is kept for a padding slot
+        fence_proxy_async_smem();
+      }
+      math_bar();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(rows_full);
+      // ---- P^T and dS^T for key `key` (TMEM lane tid) ----
+      if (!math_all(mbar_wait_warp(s_full, nb & 1, abort_flag, derr, 84))) { alive = false; break; }
+      tc_fence_after();
+      const int rmask = keyB ? 2 : 1;
+#pragma unroll 1
+      for (int h2 = 0; h2 < 2; ++h2) {
+        uint32_t pkP[32], pkD[32];
+#pragma unroll
+        for (int c32 = 0; c32 < 2; ++c32) {
+          float x[32], y[32], rs[32];
+          const uint32_t col = h2 * 64 + c32 * 32;
+          tmem_ld32f(tS + col + lane_base, x);
+          tmem_ld32f(tDP + col + lane_base, y);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            float pv[2], dv[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int n = col + e + u;
+              const int d = m_pos[n] - key;
+              const bool local = d >= 0 && d < LW;
+              const bool remote = d >= LW && (m_routed[n] & rmask);
+              const float c = remote ? (keyB ? m_clB[n] : m_clA[n]) : m_cloc[n];
+              const float p = (local || remote) ? fast_exp2(fmaf(x[e + u], sl2, c)) : 0.f;
+              const float ds = (local || remote) ? p * (y[e + u] - m_delta[n]) : 0.f;
+              pv[u] = p;
+              dv[u] = ds;
+              rs[e + u] = remote ? ds : 0.f;
+            }
+            pkP[c32 * 16 + e / 2] = Fmt<E>::pack(pv[0], pv[1]);
+            pkD[c32 * 16 + e / 2] = Fmt<E>::pack(dv[0], dv[1]);
+          }
+          m_dsum[warp * NS + col + lane] = reduce_scatter32(rs, lane);
+        }
+        tmem_st32(tS + h2 * 32 + lane_base, pkP);
+        tmem_st32(tDP + h2 * 32 + lane_base, pkD);
+        // dS^T row `tid` (slots h2*64 .. +63) -> MN-major shared buffer
+        uint8_t* drow = sm + OFF_DS + h2 * 16384 + tid * 128;
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8)
+          *reinterpret_cast<uint4*>(drow + ((c8 ^ (tid & 7)) << 4)) =
+              make_uint4(pkD[4 * c8], pkD[4 * c8 + 1], pkD[4 * c8 + 2], pkD[4 * c8 + 3]);
+      }
+      tmem_st_wait();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      math_bar();
+      // ---- slot-bias gradient of slot tid ----
+      if (tid < ns && a.d_bias) {
+        float sA_sum = 0.f, sB_sum = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          if (w * 32 >= jB) sB_sum += m_dsum[w * NS + tid];
+          else sA_sum += m_dsum[w * NS + tid];
+        }
+        const int64_t row = m_row[tid];
+        if (m_sA[tid] >= 0) atomicAdd(a.d_bias + row * a.K + m_sA[tid], sA_sum);
+        if (m_sB[tid] >= 0) atomicAdd(a.d_bias + row * a.K + m_sB[tid], sB_sum);
+      }
+      ++nb;
+    }
+    // ---- dK, dV of key tid ----
+    // (alive is uniform over the math warps; the TMEM loads are warp-collective,
+    // so every lane issues them and only the stores depend on the key)
+    if (alive) {
+      const bool kv_ok = key < T;
+      E* dkp = reinterpret_cast<E*>(a.dk) + kvoff + (int64_t)(kv_ok ? key : 0) * kv_row;
+      E* dvp = reinterpret_cast<E*>(a.dv) + kvoff + (int64_t)(kv_ok ? key : 0) * kv_row;
+#pragma unroll 1
+      for (int q4 = 0; q4 < 4; ++q4) {
+        float kv[32], vv[32];
+        tmem_ld32f(tDK + q4 * 32 + lane_base, kv);
+        tmem_ld32f(tDV + q4 * 32 + lane_base, vv);
+        tmem_ld_wait();
+        if (!kv_ok) continue;
+        uint32_t pk[16], pv[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          pk[c] = nb > 0 ? Fmt<E>::pack(kv[2 * c] * a.scale, kv[2 * c + 1] * a.scale) : 0u;
+          pv[c] = nb > 0 ? Fmt<E>::pack(vv[2 * c], vv[2 * c + 1]) : 0u;
+        }
+#pragma unroll
+        for (int v4 = 0; v4 < 4; ++v4) {
+          *reinterpret_cast<uint4*>(dkp + q4 * 32 + v4 * 8) = make_uint4(pk[4 * v4], pk[4 * v4 + 1], pk[4 * v4 + 2], pk[4 * v4 + 3]);
+          *reinterpret_cast<uint4*>(dvp + q4 * 32 + v4 * 8) = make_uint4(pv[4 * v4], pv[4 * v4 + 1], pv[4 * v4 + 2], pv[4 * v4 + 3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// delta[row, h] = sum_d o * dout (one warp per (row, head))
+template <typename E>
+__global__ void __launch_bounds__(256) bwd_delta_kernel(DashAttnBwdArgs a, int64_t n) {
+  const int64_t w = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (w >= n) return;
+  const E* o = reinterpret_cast<const E*>(a.o) + w * 128 + lane * 4;
+  const E* d = reinterpret_cast<const E*>(a.dout) + w * 128 + lane * 4;
+  float acc = 0.f;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) acc = fmaf(Fmt<E>::tof(o[c]), Fmt<E>::tof(d[c]), acc);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) a.delta[w] = acc;
+}
+
+// dq = scale * acc, converted
+template <typename E>
+__global__ void __launch_bounds__(256) bwd_dq_convert_kernel(const float* acc, E* dq, float scale, int64_t n4) {
+  const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (i >= n4) return;
+  const float4 v = reinterpret_cast<const float4*>(acc)[i];
+  uint2 r;
+  r.x = Fmt<E>::pack(v.x * scale, v.y * scale);
+  r.y = Fmt<E>::pack(v.z * scale, v.w * scale);
+  reinterpret_cast<uint2*>(dq)[i] = r;
+}
+
+template <typename E>
+int launch_tc_typed(const DashAttnBwdArgs& a, int nblk, int words, float* dq_acc, cudaStream_t st) {
+  const int64_t rows = (int64_t)a.n_seq * a.seq_len;
+  const int64_t nrh = rows * a.n_heads;
+  bwd_delta_kernel<E><<<(unsigned)((nrh + 7) / 8), 256, 0, st>>>(a, nrh);
+  count_launch();
+  int rc = check_launch("bwd_delta_kernel");
+  if (rc) return rc;
+  cudaFuncSetAttribute(bwd_tc_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_TC);
+  const int ntiles = (a.seq_len + TK - 1) / TK;
+  bwd_tc_kernel<E><<<dim3((unsigned)(a.n_seq * ntiles), (unsigned)a.n_kv_heads), kTcThreads, SMEM_TC, st>>>(
+      a, nblk, words, ntiles, dq_acc);
+  count_launch();
+  rc = check_launch("bwd_tc_kernel");
+  if (rc) return rc;
+  const int64_t n4 = nrh * 32;
+  bwd_dq_convert_kernel<E><<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(dq_acc, reinterpret_cast<E*>(a.dq), a.scale, n4);
+  count_launch();
+  return check_launch("bwd_dq_convert_kernel");
+}
+
+}  // namespace
+
+size_t attn_bwd_tc_acc_bytes(const DashAttnBwdArgs& a) {
+  if (a.dtype != DASH_DTYPE_BF16 && a.dtype != DASH_DTYPE_F16) return 0;
+  return (size_t)a.n_seq * a.seq_len * a.n_heads * 128 * 4;
+}
+
+int launch_attn_bwd_tc(const DashAttnBwdArgs& a, int nblk, int words, cudaStream_t st) {
+  float* dq_acc = a.dq_acc;
+  if (cudaMemsetAsync(dq_acc, 0, attn_bwd_tc_acc_bytes(a), st) != cudaSuccess)
+    return set_error(DASH_ERR_CUDA, "memset of the dq accumulator failed");
+  if (a.dtype == DASH_DTYPE_BF16) return launch_tc_typed<__nv_bfloat16>(a, nblk, words, dq_acc, st);
+  return launch_tc_typed<__half>(a, nblk, words, dq_acc, st);
+}
+
+}  // namespace dash

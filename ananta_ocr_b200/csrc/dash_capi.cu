@@ -392,6 +392,8 @@ int dash_attn_bwd(const DashAttnBwdArgs* a, dash_stream_t stream) {
   for (const void* p : vec)
     if (!aligned16(p)) return set_error(DASH_ERR_INVALID, "q/k/v/o/dout/dq/dk/dv must be 16-byte aligned");
   if (a->scale <= 0.f) return set_error(DASH_ERR_INVALID, "scale must be > 0");
+  if ((a->dtype == DASH_DTYPE_BF16 || a->dtype == DASH_DTYPE_F16) && (!a->dq_acc || !aligned16(a->dq_acc)))
+    return set_error(DASH_ERR_INVALID, "bf16/fp16 need a 16-byte aligned dq_acc scratch");
   return launch_attn_bwd(*a, (cudaStream_t)stream);
 }
 

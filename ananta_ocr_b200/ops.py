@@ -396,10 +396,13 @@ def gather_attention_bwd(q, k, v, o, dout, lse, idx, bias, *, block_size: int,
     if words < 0:
         raise L.DashError(L.DASH_ERR_UNSUPPORTED, L.last_error())
     flags = torch.empty(max(1, words), dtype=torch.int32, device=q.device)
+    dq_acc = (torch.empty(B, T, HQ, D, dtype=torch.float32, device=q.device)
+              if dt in (torch.bfloat16, torch.float16) else None)
     a.q, a.k, a.v, a.o, a.dout = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), dout.data_ptr()
     a.dq, a.dk, a.dv = dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
     a.lse, a.idx, a.bias = lse.data_ptr(), idx.data_ptr(), _ptr(bias)
     a.d_bias, a.delta, a.flags = _ptr(d_bias), delta.data_ptr(), flags.data_ptr()
+    a.dq_acc = _ptr(dq_acc)
     a.device_error = device_error.ptr if device_error is not None else None
     L.call("dash_attn_bwd", a)
     return dq, dk, dv, d_bias

@@ -36,6 +36,8 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# 148 SMs x 128 fp32 FMA lanes x 2 FLOP x 1.965 GHz (nominal, context only)
+FP32_NOMINAL_TFLOPS = 74.4
 
 C2 = dict(name="config2_prefill_bf16", B=4, H=10, S=9248, D=128, bs=64, lb=4, K=16,
           n_pages=32, page_tokens=273, off_std=0.2)
@@ -283,6 +285,58 @@ def run_page_aware(cfg, st, dev, steps, warmup):
     ids_bytes = B * S * (8 + 4) + B * nblk * (8 + 4 * words) + 16 * B
     return dict(ms=res, equal_to_dense=same, rows=B * S, rows_with_page=constrained,
                 page_ids_bytes=ids_bytes)
+
+
+def run_backward(cfg, dev, steps, warmup):
+    """Training backward of the prefill workload's attention (``dash_attn_bwd``:
+    dq + slot-bias gradient, dk/dv) on config-2 shapes: bf16 q, k, v ~N(0,1)*0.5,
+    dout ~N(0,1), o and lse from the tcgen05 forward, K distinct remote blocks
+    per row drawn uniformly (noise-driven routes).  Inputs (q, k, v, o, dout:
+    ~470 MB) exceed L2.  Algorithmic FLOPs: 10 * D per kept (row, head, key):
+    the five products s, dp, dq, dk, dv."""
+    import torch
+    from ananta_ocr_b200 import ops
+    B, S, H, D, bs, LW, K = cfg["B"], cfg["S"], cfg["H"], 128, cfg["bs"], cfg["lb"] * cfg["bs"], cfg["K"]
+    g = torch.Generator(device=dev).manual_seed(321)
+    q = (torch.randn(B, S, H, D, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    k = (torch.randn(B, S, H, D, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    v = (torch.randn(B, S, H, D, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    do = torch.randn(B, S, H, D, generator=g, device=dev).to(torch.bfloat16)
+    t = torch.arange(S, device=dev)
+    nrem = torch.clamp((t - LW + 1 + bs - 1) // bs, min=0)            # blocks with a remote key
+    r = torch.rand(B, S, (S + bs - 1) // bs, generator=g, device=dev)
+    r = r.masked_fill(torch.arange(r.shape[-1], device=dev)[None, None] >= nrem[None, :, None], 2.0)
+    idx = r.argsort(-1)[..., :K].to(torch.int32)
+    idx = torch.where(torch.arange(K, device=dev)[None, None] < nrem[None, :, None], idx,
+                      torch.full_like(idx, -1)).sort(-1).values
+    bias = torch.randn(B, S, K, generator=g, device=dev) * 0.5
+    lse = torch.empty(B, H, S, device=dev)
+    o = ops.gather_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), idx[:, None],
+                             bias[:, None], block_size=bs, local_window=LW, scale=1 / math.sqrt(D),
+                             lse=lse).transpose(1, 2).contiguous()
+    lse_t = lse.transpose(1, 2).contiguous()
+
+    def step():
+        return ops.gather_attention_bwd(q, k, v, o, do, lse_t, idx, bias, block_size=bs,
+                                        local_window=LW, scale=1 / math.sqrt(D))
+    for _ in range(max(3, warmup)):
+        step()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(max(1, steps)):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    # kept keys per (row, head): window min(LW, t+1) + routed blocks' keys below it
+    valid = idx >= 0
+    blk_keys = torch.clamp(torch.minimum((idx.long() + 1) * bs, (t - LW + 1)[None, :, None])
+                           - idx.long() * bs, min=0) * valid
+    keys = blk_keys.sum(-1).float() + torch.clamp(t + 1, max=LW)[None].float()
+    flops = 10.0 * D * H * float(keys.sum())
+    return dict(ms=statistics.median(times), flops=flops, tokens=B * S)
 
 
 def run_frontend(cfg, dev, steps, warmup):
@@ -630,6 +684,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-pages", action="store_true",
                     help="skip the page-aware routing measurement")
+    ap.add_argument("--no-backward", action="store_true",
+                    help="skip the training-backward measurement")
     ap.add_argument("--no-frontend", action="store_true",
                     help="skip the router front-end measurement")
     ap.add_argument("--no-graph", action="store_true",
@@ -865,6 +921,9 @@ def main():
     fe_res = None
     if not args.no_frontend and args.workload == "c2":
         fe_res = run_frontend(cfg, dev, args.steps, args.warmup)
+    bw_res = None
+    if not args.no_backward and args.workload == "c2":
+        bw_res = run_backward(cfg, dev, args.steps, args.warmup)
 
     peaks, peak_kind = load_peaks()
     if rank != 0:
@@ -944,6 +1003,20 @@ def main():
                                                       "q/k fp32 out, cos/sin in",
                          "bytes_per_launch": fe_res["bytes"],
                          "peak_source": f"{peak_kind} hbm_gbs"}}
+    if bw_res is not None:
+        peak = peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
+        tf = bw_res["flops"] / (bw_res["ms"] / 1e3) / 1e12
+        line["backward"] = {
+            "workload": cfg["name"] + " attention backward (dq, dk, dv, slot-bias gradient), "
+                                      "uniform random routes",
+            "ms": bw_res["ms"], "tokens_per_s": bw_res["tokens"] / (bw_res["ms"] / 1e3),
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
+                         "frac": tf / peak, "kernel": "bwd_dq_kernel + bwd_dkv_kernel (CUDA cores, "
+                                                     "fp32 FMA; the tensor-core peak is the target)",
+                         "flops_per_launch": bw_res["flops"],
+                         "peak_source": f"{peak_kind} bf16_tflops",
+                         "fp32_cuda_core_nominal_tflops": FP32_NOMINAL_TFLOPS,
+                         "frac_of_fp32_cuda_core_nominal": tf / FP32_NOMINAL_TFLOPS}}
     if e2e is not None:
         line["e2e"] = e2e
     if not args.no_cpu and world == 1:   # the CPU baseline is timed at N = 1 only

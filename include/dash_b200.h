@@ -601,9 +601,12 @@ int dash_rope_kv_write(const DashRopeKVArgs* args, dash_stream_t stream);
  * shared by all heads (-1 unused; later duplicates and ids outside the
  * sequence's blocks are ignored; bias NULL = 0).  d_bias (optional)
  * [n_seq, seq_len, K]: gradient of each slot's bias (0 on ignored slots),
- * summed over all heads.  Scratch: delta [n_seq, seq_len, n_heads] fp32 and
- * flags (dash_attn_bwd_flag_words() uint32 words).  head_dim 128, block_size
- * a multiple of 64, n_heads / n_kv_heads in {1, 2, 4, 8}, K <= 256.          */
+ * summed over all heads.  Scratch: delta [n_seq, seq_len, n_heads] fp32,
+ * flags (dash_attn_bwd_flag_words() uint32 words) and, for bf16 / fp16,
+ * dq_acc [n_seq, seq_len, n_heads, head_dim] fp32 (16-byte aligned).
+ * bf16 / fp16 run on the tensor cores, fp32 on the CUDA cores.  head_dim
+ * 128, block_size a multiple of 64, n_heads / n_kv_heads in {1, 2, 4, 8},
+ * K <= 256.                                                                 */
 typedef struct {
   const void* q; const void* k; const void* v; const void* o; const void* dout;
   void* dq; void* dk; void* dv;
@@ -613,6 +616,7 @@ typedef struct {
   float* d_bias;
   float* delta;
   uint32_t* flags;
+  float* dq_acc;
   int32_t n_seq, seq_len, n_heads, n_kv_heads;
   int32_t head_dim, dtype, block_size, local_window;
   int32_t K, pad0;
