@@ -46,9 +46,9 @@ constexpr int OFF_Q = 65536;             // [2 halves][128 slots][128 B]
 constexpr int OFF_DO = 98304;
 constexpr int OFF_DS = 131072;           // dS^T MN-major: [2 slot halves][128 keys][128 B]
 constexpr int OFF_META = 163840;
-// meta arrays of NS entries: pos, row (global), hq, slotA, slotB, routed (int);
-// cloc, clA, clB, delta (float); dsum [4 warps][NS] (float)
-constexpr int META_WORDS = 10 * NS + 4 * NS + 8;
+// per-slot meta: int4 {pos, routed, cloc, delta} and float2 {clA, clB} read
+// by the softmax; row (global), hq, slotA, slotB; dsum [4 warps][NS]
+constexpr int META_WORDS = 4 * NS + 2 * NS + 4 * NS + 4 * NS + 8;
 constexpr int OFF_BAR = OFF_META + META_WORDS * 4;
 constexpr int SMEM_TC = OFF_BAR + 128 + 1024;    // + alignment slack
 static_assert(SMEM_TC <= 232448, "shared memory budget");
@@ -127,17 +127,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     bwd_tc_kernel(const DashAttnBwdArgs a, int nblk, int words, int ntiles, float* dq_acc) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  int* m_pos = reinterpret_cast<int*>(sm + OFF_META);
-  int* m_row = m_pos + NS;
+  int4* m_a = reinterpret_cast<int4*>(sm + OFF_META);            // {pos, routed, cloc, delta}
+  float2* m_b = reinterpret_cast<float2*>(m_a + NS);              // {clA, clB}
+  int* m_row = reinterpret_cast<int*>(m_b + NS);
   int* m_hq = m_row + NS;
   int* m_sA = m_hq + NS;
   int* m_sB = m_sA + NS;
-  int* m_routed = m_sB + NS;
-  float* m_cloc = reinterpret_cast<float*>(m_routed + NS);
-  float* m_clA = m_cloc + NS;
-  float* m_clB = m_clA + NS;
-  float* m_delta = m_clB + NS;
-  float* m_dsum = m_delta + NS;                 // [4][NS]
+  float* m_dsum = reinterpret_cast<float*>(m_sB + NS);           // [4][NS]
   int* m_ns = reinterpret_cast<int*>(m_dsum + 4 * NS);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
   uint64_t* rows_full = bars + 0;
@@ -231,9 +227,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int key = key0 + tid;
     const bool keyB = tid >= jB;
     const int64_t loc_end = min((int64_t)key0 + TK - 1 + LW - 1, (int64_t)T - 1);
-    // row cursor (thread 0): word w, bits m not yet taken
-    int cw = (key0 >> 5) - 1;
-    uint32_t cm = 0u;
+    // row cursor (warp 0, uniform): first row not yet taken
+    int next_row = key0;
     int nb = 0;
     bool alive = true;
     while (alive) {
@@ -256,36 +251,55 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
       math_bar();
-      // ---- next batch of rows ----
-      if (tid == 0) {
+      // ---- next batch of rows (warp 0: 32 bitmask words per step, one per lane) ----
+      if (warp == 0) {
         int cnt = 0;
         const int cap = NS / G;
-        int* rows = m_pos;              // scratch: row ids, expanded to slots below
-        while (cnt < cap) {
-          if (cm == 0u) {
-            if (++cw >= words) break;
-            uint32_t m = flA[cw] | (bB != bA ? flB[cw] : 0u);
-            const int64_t r0 = (int64_t)cw * 32;
+        while (cnt < cap && next_row < T) {
+          const int w = (next_row >> 5) + lane;
+          uint32_t m = 0u;
+          if (w < words) {
+            m = flA[w] | (bB != bA ? flB[w] : 0u);
+            const int64_t r0 = (int64_t)w * 32;
             const int64_t lo = max(r0, (int64_t)key0), hi = min(r0 + 31, loc_end);
             if (lo <= hi) {
               const int nbits = (int)(hi - lo + 1);
               m |= (nbits == 32 ? 0xffffffffu : ((1u << nbits) - 1u)) << (int)(lo - r0);
             }
-            if (r0 < key0) m &= ~((1u << (key0 - r0)) - 1u);
-            cm = m;
-            continue;
+            if (lane == 0) m &= 0xffffffffu << (next_row & 31);
+            if (r0 + 32 > T) m &= (T - r0 >= 32) ? 0xffffffffu : ((1u << (T - r0)) - 1u);
           }
-          const int bit = __ffs(cm) - 1;
-          cm &= cm - 1u;
-          const int i = cw * 32 + bit;
-          if (i >= T) { cm = 0u; cw = words; break; }
-          rows[cnt++] = i;
+          const int c = __popc(m);
+          int incl = c;
+#pragma unroll
+          for (int off = 1; off < 32; off <<= 1) {
+            const int o = __shfl_up_sync(0xffffffffu, incl, off);
+            if (lane >= off) incl += o;
+          }
+          const int excl = incl - c;
+          const int tot = __shfl_sync(0xffffffffu, incl, 31);
+          const int room = cap - cnt;
+          const int take = max(0, min(c, room - excl));
+          uint32_t mm = m;
+          for (int k = 0; k < take; ++k) {
+            const int bit = __ffs(mm) - 1;
+            mm &= mm - 1u;
+            const int r = cnt + excl + k;
+            for (int g = 0; g < G; ++g) { m_row[r * G + g] = w * 32 + bit; m_hq[r * G + g] = h * G + g; }
+          }
+          if (tot <= room) {
+            cnt += tot;
+            next_row = ((next_row >> 5) + 32) * 32;
+          } else {
+            // the lane holding the boundary: its first untaken row resumes the next batch
+            const bool bnd = excl <= room && excl + c > room;
+            const int src = __ffs(__ballot_sync(0xffffffffu, bnd)) - 1;
+            const int resume = w * 32 + (__ffs(mm) - 1);
+            next_row = __shfl_sync(0xffffffffu, resume, src);
+            cnt = cap;
+          }
         }
-        for (int r = cnt - 1; r >= 0; --r) {      // expand rows to slots in place (back to front)
-          const int i = rows[r];
-          for (int g = G - 1; g >= 0; --g) { m_pos[r * G + g] = i; m_hq[r * G + g] = h * G + g; }
-        }
-        *m_ns = cnt * G;
+        if (lane == 0) *m_ns = cnt * G;
       }
       math_bar();
       const int ns = *m_ns;
@@ -298,7 +312,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // ---- gather slot tid ----
       {
         const bool live = tid < ns;
-        const int i = live ? m_pos[tid] : 0;
+        const int i = live ? m_row[tid] : 0;
         const int hq = live ? m_hq[tid] : 0;
         const int64_t row = (int64_t)s * T + i;
         const int64_t off = (row * HQ + hq) * 128;
@@ -311,11 +325,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           delta = a.delta[row * HQ + hq];
           if ((flA[i >> 5] >> (i & 31)) & 1u) routed |= 1;
           if (bB != bA && ((flB[i >> 5] >> (i & 31)) & 1u)) routed |= 2;
+          // first slot of bA / bB: 16 independent loads per step
           const int32_t* ids = a.idx + row * a.K;
-          for (int jj = 0; jj < a.K && (((routed & 1) && sA < 0) || ((routed & 2) && sB < 0)); ++jj) {
-            const int b = ids[jj];
-            if ((routed & 1) && sA < 0 && b == bA) sA = jj;
-            if ((routed & 2) && sB < 0 && b == bB) sB = jj;
+          for (int j0 = 0; j0 < a.K && (((routed & 1) && sA < 0) || ((routed & 2) && sB < 0)); j0 += 16) {
+            int v[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) v[u] = j0 + u < a.K ? ids[j0 + u] : -1;
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+              if ((routed & 1) && sA < 0 && v[u] == bA) sA = j0 + u;
+              if ((routed & 2) && sB < 0 && v[u] == bB) sB = j0 + u;
+            }
           }
           if (a.bias) {
             if (sA >= 0) biasA = a.bias[row * a.K + sA];
@@ -323,14 +343,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
         }
         m_row[tid] = (int)row;
-        m_routed[tid] = routed;
         m_sA[tid] = sA;
         m_sB[tid] = sB;
-        m_cloc[tid] = -lse * LOG2E;
-        m_clA[tid] = (biasA - lse) * LOG2E;
-        m_clB[tid] = (biasB - lse) * LOG2E;
-        m_delta[tid] = delta;
-        if (!live) m_pos[tid] = INT_MIN / 2;      // no key is kept for a padding slot
+        // a padding slot's position keeps every key out
+        m_a[tid] = make_int4(live ? i : INT_MIN / 2, routed, __float_as_int(-lse * LOG2E), __float_as_int(delta));
+        m_b[tid] = make_float2((biasA - lse) * LOG2E, (biasB - lse) * LOG2E);
         fence_proxy_async_smem();
       }
       math_bar();
@@ -357,12 +374,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
               const int n = col + e + u;
-              const int d = m_pos[n] - key;
+              const int4 ma = m_a[n];
+              const float2 mb = m_b[n];
+              const int d = ma.x - key;
               const bool local = d >= 0 && d < LW;
-              const bool remote = d >= LW && (m_routed[n] & rmask);
-              const float c = remote ? (keyB ? m_clB[n] : m_clA[n]) : m_cloc[n];
+              const bool remote = d >= LW && (ma.y & rmask);
+              const float c = remote ? (keyB ? mb.y : mb.x) : __int_as_float(ma.z);
               const float p = (local || remote) ? fast_exp2(fmaf(x[e + u], sl2, c)) : 0.f;
-              const float ds = (local || remote) ? p * (y[e + u] - m_delta[n]) : 0.f;
+              const float ds = (local || remote) ? p * (y[e + u] - __int_as_float(ma.w)) : 0.f;
               pv[u] = p;
               dv[u] = ds;
               rs[e + u] = remote ? ds : 0.f;
