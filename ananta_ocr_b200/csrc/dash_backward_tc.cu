@@ -11,12 +11,12 @@
 // the rows whose window reaches a key of the tile.  They are processed in
 // batches of 128 slots (a slot = a query row x one of the G query heads of
 // this kv head):
-//   math warps 0-3   gather the slots' q and dout rows into shared memory
+//   math warps 0-7   gather the slots' q and dout rows into shared memory
 //                    (128-byte swizzle, K-major), per-slot lse / delta /
 //                    routed flags / biases
-//   MMA warp 4       S^T  = K  Q^T        (M = 128 keys, N = 128 slots, K = d)
+//   MMA warp 8       S^T  = K  Q^T        (M = 128 keys, N = 128 slots, K = d)
 //                    dP^T = V  dO^T
-//   math warps       thread = key: P^T = exp(s*scale + bias - lse) on the kept
+//   math warps       thread = (key, slot half): P^T = exp(s*scale + bias - lse) on the kept
 //                    keys, dS^T = P^T (dP^T - delta); P^T and dS^T (bf16)
 //                    back into TMEM over S^T / dP^T, dS^T also into shared
 //                    memory (MN-major); per-slot column sums of the remote
@@ -39,7 +39,8 @@ namespace {
 
 constexpr int TK = 128;                  // keys per CTA
 constexpr int NS = 128;                  // slots per batch
-constexpr int kTcThreads = 160;          // 4 math warps + 1 MMA warp
+constexpr int kMath = 256;               // 8 math warps (two warpgroups)
+constexpr int kTcThreads = kMath + 32;   // + 1 MMA warp (warp 8)
 constexpr int OFF_K = 0;                 // [2 halves][128 keys][128 B]
 constexpr int OFF_V = 32768;
 constexpr int OFF_Q = 65536;             // [2 halves][128 slots][128 B]
@@ -74,15 +75,15 @@ template <> struct Fmt<__half> {
   static __device__ __forceinline__ void st(__half* p, float x) { *p = __float2half_rn(x); }
 };
 
-__device__ __forceinline__ void math_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-// barrier of the 4 math warps that also ANDs a predicate over them: every
+__device__ __forceinline__ void math_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// barrier of the 8 math warps that also ANDs a predicate over them: every
 // math warp leaves a failed wait together (none is left at a later barrier)
 __device__ __forceinline__ bool math_all(bool p) {
   uint32_t r;
   asm volatile(
       "{\n\t.reg .pred pi, po;\n\t"
       "setp.ne.u32 pi, %1, 0;\n\t"
-      "bar.red.and.pred po, 1, 128, pi;\n\t"
+      "bar.red.and.pred po, 1, 256, pi;\n\t"
       "selp.u32 %0, 1, 0, po;\n\t}"
       : "=r"(r)
       : "r"((uint32_t)p)
@@ -159,22 +160,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t* flB = a.flags + ((int64_t)s * nblk + bB) * words;
 
   if (tid == 0) {
-    mbar_init(rows_full, 4);
+    mbar_init(rows_full, 8);
     mbar_init(s_full, 1);
-    mbar_init(p_full, 4);
+    mbar_init(p_full, 8);
     mbar_init(pv_done, 1);
     mbar_init(fin, 1);
     *abort_flag = 0;
     mbar_init_fence();
   }
-  if (warp == 4) { tmem_alloc(tmem_holder, TMEM_COLS); tmem_relinquish(); }
-  if (tid < TK) {
-    const int key = key0 + tid;
+  if (warp == 8) { tmem_alloc(tmem_holder, TMEM_COLS); tmem_relinquish(); }
+  if (tid < 2 * TK) {            // threads 0-127: K rows, 128-255: V rows
+    const int r = tid & (TK - 1);
+    const int key = key0 + r;
     const bool z = key >= T;
-    const uint4* kp = reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(a.k) + kvoff + (int64_t)(z ? 0 : key) * kv_row);
-    const uint4* vp = reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(a.v) + kvoff + (int64_t)(z ? 0 : key) * kv_row);
-    st_row_sw128(sm + OFF_K, tid, kp, z);
-    st_row_sw128(sm + OFF_V, tid, vp, z);
+    const void* base = tid < TK ? a.k : a.v;
+    const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(base) + kvoff + (int64_t)(z ? 0 : key) * kv_row);
+    st_row_sw128(sm + (tid < TK ? OFF_K : OFF_V), r, src, z);
     fence_proxy_async_smem();
   }
   tc_fence_before();
@@ -184,7 +185,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 384;
   constexpr uint32_t fmt = Fmt<E>::v;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ============================ MMA issuer ============================
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc(fmt, 0, 0, TK, NS);
@@ -221,11 +222,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncwarp();
   } else {
     // ============================ math warps ============================
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    // warp w: TMEM lane quarter wq (keys, or slots for dQ) and column half sh
+    const int wq = warp & 3, sh = warp >> 2;
+    const int kl = wq * 32 + lane;               // this thread's TMEM lane
+    const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
     const float LOG2E = 1.4426950408889634f;
     const float sl2 = a.scale * LOG2E;
-    const int key = key0 + tid;
-    const bool keyB = tid >= jB;
+    const int key = key0 + kl;
+    const bool keyB = kl >= jB;
     const int64_t loc_end = min((int64_t)key0 + TK - 1 + LW - 1, (int64_t)T - 1);
     // row cursor (warp 0, uniform): first row not yet taken
     int next_row = key0;
@@ -237,14 +241,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (!math_all(mbar_wait_warp(pv_done, (nb - 1) & 1, abort_flag, derr, 83))) { alive = false; break; }
         tc_fence_after();
         const int ns_prev = *m_ns;
+        // lanes = slots; warpgroup sh takes d half sh (columns 64.. of S^T or dP^T)
 #pragma unroll 1
-        for (int q4 = 0; q4 < 4; ++q4) {
+        for (int q2 = 0; q2 < 2; ++q2) {
           float v[32];
-          tmem_ld32f((q4 < 2 ? tS : tDP) + 64 + (q4 & 1) * 32 + lane_base, v);
+          tmem_ld32f((sh == 0 ? tS : tDP) + 64 + q2 * 32 + lane_base, v);
           tmem_ld_wait();
-          if (tid < ns_prev) {
-            float4* dst = reinterpret_cast<float4*>(dq_acc + ((int64_t)m_row[tid] * HQ + m_hq[tid]) * 128 +
-                                                    (q4 >> 1) * 64 + (q4 & 1) * 32);
+          if (kl < ns_prev) {
+            float4* dst = reinterpret_cast<float4*>(dq_acc + ((int64_t)m_row[kl] * HQ + m_hq[kl]) * 128 +
+                                                    sh * 64 + q2 * 32);
 #pragma unroll
             for (int c = 0; c < 8; ++c) atomicAdd(dst + c, make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]));
           }
@@ -309,18 +314,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0) mbar_arrive(rows_full);
         break;
       }
-      // ---- gather slot tid ----
+      // ---- gather slot n: threads 0-127 its q row and meta, 128-255 its dout row ----
       {
-        const bool live = tid < ns;
-        const int i = live ? m_row[tid] : 0;
-        const int hq = live ? m_hq[tid] : 0;
+        const int n = tid & (NS - 1);
+        const bool live = n < ns;
+        const int i = live ? m_row[n] : 0;
+        const int hq = live ? m_hq[n] : 0;
         const int64_t row = (int64_t)s * T + i;
         const int64_t off = (row * HQ + hq) * 128;
-        st_row_sw128(sm + OFF_Q, tid, reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(a.q) + off), !live);
-        st_row_sw128(sm + OFF_DO, tid, reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(a.dout) + off), !live);
+        if (tid >= NS)
+          st_row_sw128(sm + OFF_DO, n, reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(a.dout) + off), !live);
+        else
+          st_row_sw128(sm + OFF_Q, n, reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(a.q) + off), !live);
         int routed = 0, sA = -1, sB = -1;
         float lse = 0.f, delta = 0.f, biasA = 0.f, biasB = 0.f;
-        if (live) {
+        if (live && tid < NS) {
           lse = a.lse[row * HQ + hq];
           delta = a.delta[row * HQ + hq];
           if ((flA[i >> 5] >> (i & 31)) & 1u) routed |= 1;
@@ -342,13 +350,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (sB >= 0) biasB = a.bias[row * a.K + sB];
           }
         }
-        m_row[tid] = (int)row;
-        m_sA[tid] = sA;
-        m_sB[tid] = sB;
-        // a padding slot's position keeps every key out
-        m_a[tid] = make_int4(live ? i : INT_MIN / 2, routed, __float_as_int(-lse * LOG2E), __float_as_int(delta));
-        m_b[tid] = make_float2((biasA - lse) * LOG2E, (biasB - lse) * LOG2E);
         fence_proxy_async_smem();
+        math_bar();                 // every thread has read m_row / m_hq of the batch
+        if (tid < NS) {
+          m_row[n] = (int)row;
+          m_sA[n] = sA;
+          m_sB[n] = sB;
+          // a padding slot's position keeps every key out
+          m_a[n] = make_int4(live ? i : INT_MIN / 2, routed, __float_as_int(-lse * LOG2E), __float_as_int(delta));
+          m_b[n] = make_float2((biasA - lse) * LOG2E, (biasB - lse) * LOG2E);
+        }
       }
       math_bar();
       tc_fence_before();
@@ -359,7 +370,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc_fence_after();
       const int rmask = keyB ? 2 : 1;
 #pragma unroll 1
-      for (int h2 = 0; h2 < 2; ++h2) {
+      {
+        // warpgroup sh: slots sh*64 .. +63 of key kl
+        const int h2 = sh;
         uint32_t pkP[32], pkD[32];
 #pragma unroll
         for (int c32 = 0; c32 < 2; ++c32) {
@@ -389,15 +402,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             pkP[c32 * 16 + e / 2] = Fmt<E>::pack(pv[0], pv[1]);
             pkD[c32 * 16 + e / 2] = Fmt<E>::pack(dv[0], dv[1]);
           }
-          m_dsum[warp * NS + col + lane] = reduce_scatter32(rs, lane);
+          m_dsum[wq * NS + col + lane] = reduce_scatter32(rs, lane);
         }
+        // P^T / dS^T of slot half h2 go over S^T / dP^T columns h2*32 .. +31,
+        // which the other warpgroup reads (slots 32-63): store after both read
+        tmem_ld_wait();
+        math_bar();
         tmem_st32(tS + h2 * 32 + lane_base, pkP);
         tmem_st32(tDP + h2 * 32 + lane_base, pkD);
-        // dS^T row `tid` (slots h2*64 .. +63) -> MN-major shared buffer
-        uint8_t* drow = sm + OFF_DS + h2 * 16384 + tid * 128;
+        // dS^T row kl (slots h2*64 .. +63) -> MN-major shared buffer
+        uint8_t* drow = sm + OFF_DS + h2 * 16384 + kl * 128;
 #pragma unroll
         for (int c8 = 0; c8 < 8; ++c8)
-          *reinterpret_cast<uint4*>(drow + ((c8 ^ (tid & 7)) << 4)) =
+          *reinterpret_cast<uint4*>(drow + ((c8 ^ (kl & 7)) << 4)) =
               make_uint4(pkD[4 * c8], pkD[4 * c8 + 1], pkD[4 * c8 + 2], pkD[4 * c8 + 3]);
       }
       tmem_st_wait();
@@ -420,18 +437,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       ++nb;
     }
-    // ---- dK, dV of key tid ----
+    // ---- dK, dV of key kl, d half sh ----
     // (alive is uniform over the math warps; the TMEM loads are warp-collective,
     // so every lane issues them and only the stores depend on the key)
     if (alive) {
       const bool kv_ok = key < T;
-      E* dkp = reinterpret_cast<E*>(a.dk) + kvoff + (int64_t)(kv_ok ? key : 0) * kv_row;
-      E* dvp = reinterpret_cast<E*>(a.dv) + kvoff + (int64_t)(kv_ok ? key : 0) * kv_row;
+      E* dkp = reinterpret_cast<E*>(a.dk) + kvoff + (int64_t)(kv_ok ? key : 0) * kv_row + sh * 64;
+      E* dvp = reinterpret_cast<E*>(a.dv) + kvoff + (int64_t)(kv_ok ? key : 0) * kv_row + sh * 64;
 #pragma unroll 1
-      for (int q4 = 0; q4 < 4; ++q4) {
+      for (int q4 = 0; q4 < 2; ++q4) {
         float kv[32], vv[32];
-        tmem_ld32f(tDK + q4 * 32 + lane_base, kv);
-        tmem_ld32f(tDV + q4 * 32 + lane_base, vv);
+        tmem_ld32f(tDK + sh * 64 + q4 * 32 + lane_base, kv);
+        tmem_ld32f(tDV + sh * 64 + q4 * 32 + lane_base, vv);
         tmem_ld_wait();
         if (!kv_ok) continue;
         uint32_t pk[16], pv[16];
@@ -450,7 +467,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) tmem_dealloc(tmem, TMEM_COLS);
+  if (warp == 8) tmem_dealloc(tmem, TMEM_COLS);
 }
 
 // delta[row, h] = sum_d o * dout (one warp per (row, head))

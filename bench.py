@@ -675,8 +675,9 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c2", choices=["c2", "c4", "c5"],
-                    help="c2 (default, the headline), c4 long-document prefill, c5 end-to-end decoder")
+    ap.add_argument("--workload", default="c2", choices=["c2", "c4", "c5", "bwd"],
+                    help="c2 (default, the headline), c4 long-document prefill, c5 end-to-end decoder, "
+                         "bwd the config-2 training backward alone")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -743,6 +744,23 @@ def main():
     from ananta_ocr_b200 import _lib
     _lib.load()
 
+    if args.workload == "bwd":
+        # the training backward alone (one GPU; ranks other than 0 run nothing)
+        if rank != 0:
+            return
+        r = run_backward(C2, dev, args.steps, args.warmup)
+        peaks, peak_kind = load_peaks()
+        peak = peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
+        tf = r["flops"] / (r["ms"] / 1e3) / 1e12
+        print(json.dumps({"metric": "DASH attn backward tokens/s", "value": r["tokens"] / (r["ms"] / 1e3),
+                          "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": r["ms"], "higher_is_better": True, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                          "config": {"workload": "config2_backward_bf16"},
+                          "roofline": {"bound": "tensor", "achieved": tf, "peak": peak,
+                                       "unit": "TFLOP/s", "frac": tf / peak,
+                                       "peak_source": f"{peak_kind} bf16_tflops"}}))
+        return
     if args.workload == "c5":
         # one model per GPU: ranks other than 0 run nothing (replicas only)
         if rank != 0:
