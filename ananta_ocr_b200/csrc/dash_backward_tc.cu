@@ -11,9 +11,10 @@
 // the rows whose window reaches a key of the tile.  They are processed in
 // batches of 128 slots (a slot = a query row x one of the G query heads of
 // this kv head):
+//   producer warp 9  enumerates the next batch's rows and loads its per-slot
+//                    lse / delta / routed flags / biases (double-buffered)
 //   math warps 0-7   gather the slots' q and dout rows into shared memory
-//                    (128-byte swizzle, K-major), per-slot lse / delta /
-//                    routed flags / biases
+//                    (128-byte swizzle, K-major)
 //   MMA warp 8       S^T  = K  Q^T        (M = 128 keys, N = 128 slots, K = d)
 //                    dP^T = V  dO^T
 //   math warps       thread = (key, slot half): P^T = exp(s*scale + bias - lse) on the kept
@@ -40,17 +41,30 @@ namespace {
 constexpr int TK = 128;                  // keys per CTA
 constexpr int NS = 128;                  // slots per batch
 constexpr int kMath = 256;               // 8 math warps (two warpgroups)
-constexpr int kTcThreads = kMath + 32;   // + 1 MMA warp (warp 8)
+constexpr int kMmaWarp = 8;
+constexpr int kProdWarp = 9;
+constexpr int kTcThreads = kMath + 64;   // + MMA warp + producer warp
 constexpr int OFF_K = 0;                 // [2 halves][128 keys][128 B]
 constexpr int OFF_V = 32768;
 constexpr int OFF_Q = 65536;             // [2 halves][128 slots][128 B]
 constexpr int OFF_DO = 98304;
 constexpr int OFF_DS = 131072;           // dS^T MN-major: [2 slot halves][128 keys][128 B]
 constexpr int OFF_META = 163840;
-// per-slot meta: int4 {pos, routed, cloc, delta} and float2 {clA, clB} read
-// by the softmax; row (global), hq, slotA, slotB; dsum [4 warps][NS]
-constexpr int META_WORDS = 4 * NS + 2 * NS + 4 * NS + 4 * NS + 8;
-constexpr int OFF_BAR = OFF_META + META_WORDS * 4;
+// Per-batch slot meta, double-buffered (the producer fills batch b+1 while
+// batch b is computed): a = {pos, routed flags, cloc, delta} and b = {clA, clB}
+// (read by the softmax), global row, query head, slot of block A / B.
+struct SlotMeta {
+  int4 a[NS];
+  float2 b[NS];
+  int row[NS];
+  int hq[NS];
+  int sA[NS];
+  int sB[NS];
+  int ns;
+  int pad[3];
+};
+constexpr int META_BYTES = 2 * (int)sizeof(SlotMeta) + 4 * NS * 4;   // + dsum [4][NS]
+constexpr int OFF_BAR = (OFF_META + META_BYTES + 15) & ~15;
 constexpr int SMEM_TC = OFF_BAR + 128 + 1024;    // + alignment slack
 static_assert(SMEM_TC <= 232448, "shared memory budget");
 constexpr uint32_t TMEM_COLS = 512;
@@ -128,22 +142,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     bwd_tc_kernel(const DashAttnBwdArgs a, int nblk, int words, int ntiles, float* dq_acc) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  int4* m_a = reinterpret_cast<int4*>(sm + OFF_META);            // {pos, routed, cloc, delta}
-  float2* m_b = reinterpret_cast<float2*>(m_a + NS);              // {clA, clB}
-  int* m_row = reinterpret_cast<int*>(m_b + NS);
-  int* m_hq = m_row + NS;
-  int* m_sA = m_hq + NS;
-  int* m_sB = m_sA + NS;
-  float* m_dsum = reinterpret_cast<float*>(m_sB + NS);           // [4][NS]
-  int* m_ns = reinterpret_cast<int*>(m_dsum + 4 * NS);
+  SlotMeta* meta = reinterpret_cast<SlotMeta*>(sm + OFF_META);   // [2], batch b uses meta[b & 1]
+  float* m_dsum = reinterpret_cast<float*>(meta + 2);            // [4][NS]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
   uint64_t* rows_full = bars + 0;
   uint64_t* s_full = bars + 1;
   uint64_t* p_full = bars + 2;
   uint64_t* pv_done = bars + 3;
   uint64_t* fin = bars + 4;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 5);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 6);
+  uint64_t* meta_full = bars + 5;      // [2]
+  uint64_t* meta_empty = bars + 7;     // [2]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 9);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 10);
   DeviceError* derr = a.device_error;
 
   const int T = a.seq_len, HQ = a.n_heads, H = a.n_kv_heads, G = HQ / H;
@@ -156,8 +166,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t kv_row = (int64_t)H * 128;
   const int64_t kvoff = ((int64_t)s * T * H + h) * 128;
-  const uint32_t* flA = a.flags + ((int64_t)s * nblk + bA) * words;
-  const uint32_t* flB = a.flags + ((int64_t)s * nblk + bB) * words;
+  const float LOG2E = 1.4426950408889634f;
 
   if (tid == 0) {
     mbar_init(rows_full, 8);
@@ -165,10 +174,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     mbar_init(p_full, 8);
     mbar_init(pv_done, 1);
     mbar_init(fin, 1);
+    mbar_init(meta_full + 0, 1);
+    mbar_init(meta_full + 1, 1);
+    mbar_init(meta_empty + 0, 8);
+    mbar_init(meta_empty + 1, 8);
     *abort_flag = 0;
     mbar_init_fence();
   }
-  if (warp == 8) { tmem_alloc(tmem_holder, TMEM_COLS); tmem_relinquish(); }
+  if (warp == kMmaWarp) { tmem_alloc(tmem_holder, TMEM_COLS); tmem_relinquish(); }
   if (tid < 2 * TK) {            // threads 0-127: K rows, 128-255: V rows
     const int r = tid & (TK - 1);
     const int key = key0 + r;
@@ -185,7 +198,111 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 384;
   constexpr uint32_t fmt = Fmt<E>::v;
 
-  if (warp == 8) {
+  if (warp == kProdWarp) {
+    // ===================== producer: slot lists + per-slot meta =====================
+    const uint32_t* flA = a.flags + ((int64_t)s * nblk + bA) * words;
+    const uint32_t* flB = a.flags + ((int64_t)s * nblk + bB) * words;
+    const int64_t loc_end = min((int64_t)key0 + TK - 1 + LW - 1, (int64_t)T - 1);
+    int next_row = key0;                 // first row not yet taken (uniform)
+    for (int b = 0;; ++b) {
+      SlotMeta& M = meta[b & 1];
+      if (b >= 2 && !mbar_wait_warp(meta_empty + (b & 1), ((b >> 1) - 1) & 1, abort_flag, derr, 85)) break;
+      // rows: 32 bitmask words per step, one per lane
+      int cnt = 0;
+      const int cap = NS / G;
+      while (cnt < cap && next_row < T) {
+        const int w = (next_row >> 5) + lane;
+        uint32_t m = 0u;
+        if (w < words) {
+          m = flA[w] | (bB != bA ? flB[w] : 0u);
+          const int64_t r0 = (int64_t)w * 32;
+          const int64_t lo = max(r0, (int64_t)key0), hi = min(r0 + 31, loc_end);
+          if (lo <= hi) {
+            const int nbits = (int)(hi - lo + 1);
+            m |= (nbits == 32 ? 0xffffffffu : ((1u << nbits) - 1u)) << (int)(lo - r0);
+          }
+          if (lane == 0) m &= 0xffffffffu << (next_row & 31);
+          if (r0 + 32 > T) m &= (T - r0 >= 32) ? 0xffffffffu : ((1u << (T - r0)) - 1u);
+        }
+        const int c = __popc(m);
+        int incl = c;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const int o = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += o;
+        }
+        const int excl = incl - c;
+        const int tot = __shfl_sync(0xffffffffu, incl, 31);
+        const int room = cap - cnt;
+        const int take = max(0, min(c, room - excl));
+        uint32_t mm = m;
+        for (int k = 0; k < take; ++k) {
+          const int bit = __ffs(mm) - 1;
+          mm &= mm - 1u;
+          const int r = cnt + excl + k;
+          for (int g = 0; g < G; ++g) { M.row[r * G + g] = w * 32 + bit; M.hq[r * G + g] = h * G + g; }
+        }
+        if (tot <= room) {
+          cnt += tot;
+          next_row = ((next_row >> 5) + 32) * 32;
+        } else {
+          // the lane holding the boundary: its first untaken row resumes the next batch
+          const bool bnd = excl <= room && excl + c > room;
+          const int src = __ffs(__ballot_sync(0xffffffffu, bnd)) - 1;
+          const int resume = w * 32 + (__ffs(mm) - 1);
+          next_row = __shfl_sync(0xffffffffu, resume, src);
+          cnt = cap;
+        }
+      }
+      const int ns = cnt * G;
+      __syncwarp();
+      // per-slot meta, four slots per lane
+#pragma unroll 1
+      for (int q = 0; q < NS / 32; ++q) {
+        const int n = lane + 32 * q;
+        const bool live = n < ns;
+        const int i = live ? M.row[n] : 0;
+        const int hq = live ? M.hq[n] : 0;
+        const int64_t row = (int64_t)s * T + i;
+        int routed = 0, sA = -1, sB = -1;
+        float lse = 0.f, delta = 0.f, biasA = 0.f, biasB = 0.f;
+        if (live) {
+          lse = a.lse[row * HQ + hq];
+          delta = a.delta[row * HQ + hq];
+          if ((flA[i >> 5] >> (i & 31)) & 1u) routed |= 1;
+          if (bB != bA && ((flB[i >> 5] >> (i & 31)) & 1u)) routed |= 2;
+          // first slot of bA / bB: 16 independent loads per step
+          const int32_t* ids = a.idx + row * a.K;
+          for (int j0 = 0; j0 < a.K && (((routed & 1) && sA < 0) || ((routed & 2) && sB < 0)); j0 += 16) {
+            int v[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) v[u] = j0 + u < a.K ? ids[j0 + u] : -1;
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+              if ((routed & 1) && sA < 0 && v[u] == bA) sA = j0 + u;
+              if ((routed & 2) && sB < 0 && v[u] == bB) sB = j0 + u;
+            }
+          }
+          if (a.bias) {
+            if (sA >= 0) biasA = a.bias[row * a.K + sA];
+            if (sB >= 0) biasB = a.bias[row * a.K + sB];
+          }
+        }
+        M.row[n] = (int)row;
+        M.hq[n] = hq;
+        M.sA[n] = sA;
+        M.sB[n] = sB;
+        // a padding slot's position keeps every key out
+        M.a[n] = make_int4(live ? i : INT_MIN / 2, routed, __float_as_int(-lse * LOG2E), __float_as_int(delta));
+        M.b[n] = make_float2((biasA - lse) * LOG2E, (biasB - lse) * LOG2E);
+      }
+      if (lane == 0) M.ns = ns;
+      __threadfence_block();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(meta_full + (b & 1));
+      if (ns == 0) break;
+    }
+  } else if (warp == kMmaWarp) {
     // ============================ MMA issuer ============================
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc(fmt, 0, 0, TK, NS);
@@ -196,7 +313,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int b = 0;; ++b) {
         if (!mbar_wait(rows_full, b & 1, abort_flag, derr, 80)) break;
         tc_fence_after();
-        if (*reinterpret_cast<volatile int*>(m_ns) == 0) break;
+        if (*reinterpret_cast<volatile int*>(&meta[b & 1].ns) == 0) break;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) umma_ss(tS, kmaj_desc(sK, kk), kmaj_desc(sQ, kk), idesc_s, kk > 0);
 #pragma unroll
@@ -226,152 +343,63 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int wq = warp & 3, sh = warp >> 2;
     const int kl = wq * 32 + lane;               // this thread's TMEM lane
     const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
-    const float LOG2E = 1.4426950408889634f;
     const float sl2 = a.scale * LOG2E;
     const int key = key0 + kl;
     const bool keyB = kl >= jB;
-    const int64_t loc_end = min((int64_t)key0 + TK - 1 + LW - 1, (int64_t)T - 1);
-    // row cursor (warp 0, uniform): first row not yet taken
-    int next_row = key0;
+    const int rmask = keyB ? 2 : 1;
     int nb = 0;
     bool alive = true;
     while (alive) {
       if (nb > 0) {
-        // ---- dQ of batch nb-1 -> fp32 accumulator ----
+        // ---- dQ of batch nb-1 -> fp32 accumulator (lanes = slots, d half sh) ----
         if (!math_all(mbar_wait_warp(pv_done, (nb - 1) & 1, abort_flag, derr, 83))) { alive = false; break; }
         tc_fence_after();
-        const int ns_prev = *m_ns;
-        // lanes = slots; warpgroup sh takes d half sh (columns 64.. of S^T or dP^T)
+        const SlotMeta& P = meta[(nb - 1) & 1];
+        const int ns_prev = P.ns;
 #pragma unroll 1
         for (int q2 = 0; q2 < 2; ++q2) {
           float v[32];
           tmem_ld32f((sh == 0 ? tS : tDP) + 64 + q2 * 32 + lane_base, v);
           tmem_ld_wait();
           if (kl < ns_prev) {
-            float4* dst = reinterpret_cast<float4*>(dq_acc + ((int64_t)m_row[kl] * HQ + m_hq[kl]) * 128 +
+            float4* dst = reinterpret_cast<float4*>(dq_acc + ((int64_t)P.row[kl] * HQ + P.hq[kl]) * 128 +
                                                     sh * 64 + q2 * 32);
 #pragma unroll
             for (int c = 0; c < 8; ++c) atomicAdd(dst + c, make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]));
           }
         }
+        // the producer may refill this meta buffer
+        __syncwarp();
+        if (lane == 0) mbar_arrive(meta_empty + ((nb - 1) & 1));
       }
-      math_bar();
-      // ---- next batch of rows (warp 0: 32 bitmask words per step, one per lane) ----
-      if (warp == 0) {
-        int cnt = 0;
-        const int cap = NS / G;
-        while (cnt < cap && next_row < T) {
-          const int w = (next_row >> 5) + lane;
-          uint32_t m = 0u;
-          if (w < words) {
-            m = flA[w] | (bB != bA ? flB[w] : 0u);
-            const int64_t r0 = (int64_t)w * 32;
-            const int64_t lo = max(r0, (int64_t)key0), hi = min(r0 + 31, loc_end);
-            if (lo <= hi) {
-              const int nbits = (int)(hi - lo + 1);
-              m |= (nbits == 32 ? 0xffffffffu : ((1u << nbits) - 1u)) << (int)(lo - r0);
-            }
-            if (lane == 0) m &= 0xffffffffu << (next_row & 31);
-            if (r0 + 32 > T) m &= (T - r0 >= 32) ? 0xffffffffu : ((1u << (T - r0)) - 1u);
-          }
-          const int c = __popc(m);
-          int incl = c;
-#pragma unroll
-          for (int off = 1; off < 32; off <<= 1) {
-            const int o = __shfl_up_sync(0xffffffffu, incl, off);
-            if (lane >= off) incl += o;
-          }
-          const int excl = incl - c;
-          const int tot = __shfl_sync(0xffffffffu, incl, 31);
-          const int room = cap - cnt;
-          const int take = max(0, min(c, room - excl));
-          uint32_t mm = m;
-          for (int k = 0; k < take; ++k) {
-            const int bit = __ffs(mm) - 1;
-            mm &= mm - 1u;
-            const int r = cnt + excl + k;
-            for (int g = 0; g < G; ++g) { m_row[r * G + g] = w * 32 + bit; m_hq[r * G + g] = h * G + g; }
-          }
-          if (tot <= room) {
-            cnt += tot;
-            next_row = ((next_row >> 5) + 32) * 32;
-          } else {
-            // the lane holding the boundary: its first untaken row resumes the next batch
-            const bool bnd = excl <= room && excl + c > room;
-            const int src = __ffs(__ballot_sync(0xffffffffu, bnd)) - 1;
-            const int resume = w * 32 + (__ffs(mm) - 1);
-            next_row = __shfl_sync(0xffffffffu, resume, src);
-            cnt = cap;
-          }
-        }
-        if (lane == 0) *m_ns = cnt * G;
-      }
-      math_bar();
-      const int ns = *m_ns;
+      if (!math_all(mbar_wait_warp(meta_full + (nb & 1), (nb >> 1) & 1, abort_flag, derr, 86))) { alive = false; break; }
+      const SlotMeta& M = meta[nb & 1];
+      const int ns = M.ns;
       if (ns == 0) {
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(rows_full);
         break;
       }
-      // ---- gather slot n: threads 0-127 its q row and meta, 128-255 its dout row ----
+      // ---- gather slot n: threads 0-127 its q row, 128-255 its dout row ----
       {
         const int n = tid & (NS - 1);
         const bool live = n < ns;
-        const int i = live ? m_row[n] : 0;
-        const int hq = live ? m_hq[n] : 0;
-        const int64_t row = (int64_t)s * T + i;
-        const int64_t off = (row * HQ + hq) * 128;
+        const int64_t off = ((int64_t)(live ? M.row[n] : 0) * HQ + (live ? M.hq[n] : 0)) * 128;
         if (tid >= NS)
           st_row_sw128(sm + OFF_DO, n, reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(a.dout) + off), !live);
         else
           st_row_sw128(sm + OFF_Q, n, reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(a.q) + off), !live);
-        int routed = 0, sA = -1, sB = -1;
-        float lse = 0.f, delta = 0.f, biasA = 0.f, biasB = 0.f;
-        if (live && tid < NS) {
-          lse = a.lse[row * HQ + hq];
-          delta = a.delta[row * HQ + hq];
-          if ((flA[i >> 5] >> (i & 31)) & 1u) routed |= 1;
-          if (bB != bA && ((flB[i >> 5] >> (i & 31)) & 1u)) routed |= 2;
-          // first slot of bA / bB: 16 independent loads per step
-          const int32_t* ids = a.idx + row * a.K;
-          for (int j0 = 0; j0 < a.K && (((routed & 1) && sA < 0) || ((routed & 2) && sB < 0)); j0 += 16) {
-            int v[16];
-#pragma unroll
-            for (int u = 0; u < 16; ++u) v[u] = j0 + u < a.K ? ids[j0 + u] : -1;
-#pragma unroll
-            for (int u = 0; u < 16; ++u) {
-              if ((routed & 1) && sA < 0 && v[u] == bA) sA = j0 + u;
-              if ((routed & 2) && sB < 0 && v[u] == bB) sB = j0 + u;
-            }
-          }
-          if (a.bias) {
-            if (sA >= 0) biasA = a.bias[row * a.K + sA];
-            if (sB >= 0) biasB = a.bias[row * a.K + sB];
-          }
-        }
         fence_proxy_async_smem();
-        math_bar();                 // every thread has read m_row / m_hq of the batch
-        if (tid < NS) {
-          m_row[n] = (int)row;
-          m_sA[n] = sA;
-          m_sB[n] = sB;
-          // a padding slot's position keeps every key out
-          m_a[n] = make_int4(live ? i : INT_MIN / 2, routed, __float_as_int(-lse * LOG2E), __float_as_int(delta));
-          m_b[n] = make_float2((biasA - lse) * LOG2E, (biasB - lse) * LOG2E);
-        }
       }
       math_bar();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(rows_full);
-      // ---- P^T and dS^T for key `key` (TMEM lane tid) ----
+      // ---- P^T and dS^T for key `key` (TMEM lane kl), slots sh*64 .. +63 ----
       if (!math_all(mbar_wait_warp(s_full, nb & 1, abort_flag, derr, 84))) { alive = false; break; }
       tc_fence_after();
-      const int rmask = keyB ? 2 : 1;
-#pragma unroll 1
       {
-        // warpgroup sh: slots sh*64 .. +63 of key kl
         const int h2 = sh;
         uint32_t pkP[32], pkD[32];
 #pragma unroll
@@ -387,8 +415,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
               const int n = col + e + u;
-              const int4 ma = m_a[n];
-              const float2 mb = m_b[n];
+              const int4 ma = M.a[n];
+              const float2 mb = M.b[n];
               const int d = ma.x - key;
               const bool local = d >= 0 && d < LW;
               const bool remote = d >= LW && (ma.y & rmask);
@@ -406,7 +434,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         // P^T / dS^T of slot half h2 go over S^T / dP^T columns h2*32 .. +31,
         // which the other warpgroup reads (slots 32-63): store after both read
-        tmem_ld_wait();
         math_bar();
         tmem_st32(tS + h2 * 32 + lane_base, pkP);
         tmem_st32(tDP + h2 * 32 + lane_base, pkD);
@@ -431,9 +458,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (w * 32 >= jB) sB_sum += m_dsum[w * NS + tid];
           else sA_sum += m_dsum[w * NS + tid];
         }
-        const int64_t row = m_row[tid];
-        if (m_sA[tid] >= 0) atomicAdd(a.d_bias + row * a.K + m_sA[tid], sA_sum);
-        if (m_sB[tid] >= 0) atomicAdd(a.d_bias + row * a.K + m_sB[tid], sB_sum);
+        const int64_t row = M.row[tid];
+        if (M.sA[tid] >= 0) atomicAdd(a.d_bias + row * a.K + M.sA[tid], sA_sum);
+        if (M.sB[tid] >= 0) atomicAdd(a.d_bias + row * a.K + M.sB[tid], sB_sum);
       }
       ++nb;
     }
@@ -467,7 +494,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 8) tmem_dealloc(tmem, TMEM_COLS);
+  if (warp == kMmaWarp) tmem_dealloc(tmem, TMEM_COLS);
 }
 
 // delta[row, h] = sum_d o * dout (one warp per (row, head))
