@@ -116,6 +116,38 @@ def test_bf16_forward_backward_matches_oracle(B, HQ, H, T, bs, LW, K):
     assert torch.all(db[~keep] == 0)
 
 
+@pytest.mark.parametrize("dt,B,HQ,H,T,bs,LW,K", [
+    (torch.float16, 1, 4, 2, 700, 64, 128, 5),     # fp16 tensor-core path
+    (torch.bfloat16, 2, 2, 2, 100, 64, 64, 3),     # shorter than one 128-key tile
+    (torch.bfloat16, 1, 2, 1, 333, 64, 128, 0),    # no routed slots: local window only
+    (torch.bfloat16, 1, 2, 2, 520, 192, 192, 4),   # blocks straddling the 128-key tiles
+])
+def test_backward_edge_cases_match_oracle(dt, B, HQ, H, T, bs, LW, K):
+    g = torch.Generator().manual_seed(T * 7 + K)
+    q = (torch.randn(B, T, HQ, 128, generator=g) * 0.5).to(dt).cuda()
+    k = (torch.randn(B, T, H, 128, generator=g) * 0.5).to(dt).cuda()
+    v = (torch.randn(B, T, H, 128, generator=g) * 0.5).to(dt).cuda()
+    do = torch.randn(B, T, HQ, 128, generator=g).to(dt).cuda()
+    if K > 0:
+        idx, bias = routes(B, T, K, bs, LW, T + 1, dup=False)
+    else:
+        idx = torch.zeros(B, T, 0, dtype=torch.int32, device="cuda")
+        bias = torch.zeros(B, T, 0, device="cuda")
+    scale = 1.0 / math.sqrt(128)
+    lse = torch.empty(B, HQ, T, device="cuda")
+    o = ops.gather_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), idx[:, None],
+                             bias[:, None], block_size=bs, local_window=LW, scale=scale, lse=lse)
+    o = o.transpose(1, 2).contiguous()
+    dq, dk, dv, db = ops.gather_attention_bwd(q, k, v, o, do, lse.transpose(1, 2), idx, bias,
+                                              block_size=bs, local_window=LW, scale=scale)
+    _, _, rdq, rdk, rdv, rdb = BO.gather_attention_grads(q, k, v, idx, bias, do, bs, LW, scale)
+    for got, ref in ((dq, rdq), (dk, rdk), (dv, rdv)):
+        assert got.dtype == dt
+        close(got, ref, 0.02, 0.015)
+    if K > 0:
+        close(db, rdb, 0.02, 0.015)
+
+
 def test_autograd_mirror_matches_oracle():
     """triton_gather_attention_e2e with requires_grad: gradients of q, k, v and
     the slot biases through the reference-named autograd Function."""
