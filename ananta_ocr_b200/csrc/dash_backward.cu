@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(kThreads) bwd_dq_kernel(DashAttnBwdArgs a, int
       }
       if (slot >= 0 && a.d_bias) {
         dsum = warp_sum(dsum);
-        if (lane == 0) atomicAdd(a.d_bias + row * a.K + slot, dsum);
+        if (lane == 0) red_add(a.d_bias + row * a.K + slot, dsum);
       }
     }
     __syncthreads();

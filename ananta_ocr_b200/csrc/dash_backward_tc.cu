@@ -24,7 +24,8 @@
 //                    dS^T (butterfly reduce-scatter) -> slot-bias gradient
 //   MMA warp         dV += P^T dO,  dK += dS^T Q   (A from TMEM)
 //                    dQ  = dS K                    (A and B MN-major, shared)
-//   math warps       thread = slot: dQ rows from TMEM -> fp32 atomics
+//   math warps       thread = slot: dQ rows from TMEM -> fp32 reductions
+//                    (red.global.add.v4.f32, nothing returned)
 // After the last batch dK (x scale) and dV leave TMEM, one row per thread.
 // TMEM: S^T | dP^T | dV | dK, 128 columns each; dQ uses the upper halves of
 // the S^T and dP^T columns (P^T / dS^T, packed bf16, take the lower halves).
@@ -362,10 +363,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tmem_ld32f((sh == 0 ? tS : tDP) + 64 + q2 * 32 + lane_base, v);
           tmem_ld_wait();
           if (kl < ns_prev) {
-            float4* dst = reinterpret_cast<float4*>(dq_acc + ((int64_t)P.row[kl] * HQ + P.hq[kl]) * 128 +
-                                                    sh * 64 + q2 * 32);
+            float* dst = dq_acc + ((int64_t)P.row[kl] * HQ + P.hq[kl]) * 128 + sh * 64 + q2 * 32;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) atomicAdd(dst + c, make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]));
+            for (int c = 0; c < 8; ++c) red_add_v4(dst + 4 * c, v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
           }
         }
         // the producer may refill this meta buffer
@@ -459,8 +459,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           else sA_sum += m_dsum[w * NS + tid];
         }
         const int64_t row = M.row[tid];
-        if (M.sA[tid] >= 0) atomicAdd(a.d_bias + row * a.K + M.sA[tid], sA_sum);
-        if (M.sB[tid] >= 0) atomicAdd(a.d_bias + row * a.K + M.sB[tid], sB_sum);
+        if (M.sA[tid] >= 0) red_add(a.d_bias + row * a.K + M.sA[tid], sA_sum);
+        if (M.sB[tid] >= 0) red_add(a.d_bias + row * a.K + M.sB[tid], sB_sum);
       }
       ++nb;
     }
