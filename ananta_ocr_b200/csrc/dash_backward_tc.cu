@@ -27,8 +27,8 @@
 //   math warps       thread = slot: dQ rows from TMEM -> fp32 reductions
 //                    (red.global.add.v4.f32, nothing returned)
 // After the last batch dK (x scale) and dV leave TMEM, one row per thread.
-// TMEM: S^T | dP^T | dV | dK, 128 columns each; dQ uses the upper halves of
-// the S^T and dP^T columns (P^T / dS^T, packed bf16, take the lower halves).
+// TMEM: S^T | dP^T | dV | dK, 128 columns each; after the softmax P^T and
+// dS^T (packed bf16) take the S^T columns and dQ the dP^T columns.
 // Every wait is bounded (abort flag + time limit, DASH_DEV_TIMEOUT).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -308,7 +308,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc(fmt, 0, 0, TK, NS);
       constexpr uint32_t idesc_acc = make_idesc(fmt, 0, 1, TK, 128);
-      constexpr uint32_t idesc_dq = make_idesc(fmt, 1, 1, NS, 64);
+      constexpr uint32_t idesc_dq = make_idesc(fmt, 1, 1, NS, 128);
       const uint32_t sK = smem_u32(sm + OFF_K), sV = smem_u32(sm + OFF_V);
       const uint32_t sQ = smem_u32(sm + OFF_Q), sDO = smem_u32(sm + OFF_DO), sDS = smem_u32(sm + OFF_DS);
       for (int b = 0;; ++b) {
@@ -325,11 +325,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) umma_ts(tDV, tS + kk * 8, mn_desc(sDO, kk), idesc_acc, (b > 0 || kk > 0));
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) umma_ts(tDK, tDP + kk * 8, mn_desc(sQ, kk), idesc_acc, (b > 0 || kk > 0));
+        for (int kk = 0; kk < 8; ++kk) umma_ts(tDK, tS + 64 + kk * 8, mn_desc(sQ, kk), idesc_acc, (b > 0 || kk > 0));
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) umma_ss(tS + 64, mn_desc(sDS, kk), mn_desc(sK, kk), idesc_dq, kk > 0);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) umma_ss(tDP + 64, mn_desc(sDS, kk), mn_desc(sK + 16384, kk), idesc_dq, kk > 0);
+        for (int kk = 0; kk < 8; ++kk) umma_ss(tDP, mn_desc(sDS, kk), mn_desc(sK, kk), idesc_dq, kk > 0);
         umma_commit(pv_done);
       }
       // every MMA of this CTA completes before TMEM is released
@@ -360,7 +358,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll 1
         for (int q2 = 0; q2 < 2; ++q2) {
           float v[32];
-          tmem_ld32f((sh == 0 ? tS : tDP) + 64 + q2 * 32 + lane_base, v);
+          tmem_ld32f(tDP + sh * 64 + q2 * 32 + lane_base, v);
           tmem_ld_wait();
           if (kl < ns_prev) {
             float* dst = dq_acc + ((int64_t)P.row[kl] * HQ + P.hq[kl]) * 128 + sh * 64 + q2 * 32;
@@ -432,11 +430,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
           m_dsum[wq * NS + col + lane] = reduce_scatter32(rs, lane);
         }
-        // P^T / dS^T of slot half h2 go over S^T / dP^T columns h2*32 .. +31,
-        // which the other warpgroup reads (slots 32-63): store after both read
+        // P^T / dS^T of slot half h2 go to S^T columns h2*32 / 64 + h2*32,
+        // which both warpgroups read as S^T: store after both have read
         math_bar();
         tmem_st32(tS + h2 * 32 + lane_base, pkP);
-        tmem_st32(tDP + h2 * 32 + lane_base, pkD);
+        tmem_st32(tS + 64 + h2 * 32 + lane_base, pkD);
         // dS^T row kl (slots h2*64 .. +63) -> MN-major shared buffer
         uint8_t* drow = sm + OFF_DS + h2 * 16384 + kl * 128;
 #pragma unroll
