@@ -14,7 +14,7 @@
 //   producer warp 9  enumerates the next batch's rows and loads its per-slot
 //                    lse / delta / routed flags / biases (double-buffered)
 //   math warps 0-7   gather the slots' q and dout rows into shared memory
-//                    (128-byte swizzle, K-major)
+//                    (cp.async, 128-byte swizzle, K-major)
 //   MMA warp 8       S^T  = K  Q^T        (M = 128 keys, N = 128 slots, K = d)
 //                    dP^T = V  dO^T
 //   math warps       thread = (key, slot half): P^T = exp(s*scale + bias - lse) on the kept
@@ -114,6 +114,23 @@ __device__ __forceinline__ void st_row_sw128(uint8_t* buf, int row, const uint4*
     const int region = cc >> 3, c8 = cc & 7;
     *reinterpret_cast<uint4*>(buf + region * 16384 + row * 128 + ((c8 ^ (row & 7)) << 4)) = v;
   }
+}
+
+// the same row copied with cp.async (no register staging); the caller waits
+// with cp_async_wait_all() before handing the buffer to the tensor cores
+__device__ __forceinline__ void cp_row_sw128(uint8_t* buf, int row, const uint4* src, bool zero) {
+#pragma unroll
+  for (int cc = 0; cc < 16; ++cc) {
+    const int region = cc >> 3, c8 = cc & 7;
+    uint8_t* dst = buf + region * 16384 + row * 128 + ((c8 ^ (row & 7)) << 4);
+    if (zero)
+      *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+    else
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src + cc) : "memory");
+  }
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
 }
 
 __device__ __forceinline__ uint64_t kmaj_desc(uint32_t base, int kk) {
@@ -385,9 +402,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const bool live = n < ns;
         const int64_t off = ((int64_t)(live ? M.row[n] : 0) * HQ + (live ? M.hq[n] : 0)) * 128;
         if (tid >= NS)
-          st_row_sw128(sm + OFF_DO, n, reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(a.dout) + off), !live);
+          cp_row_sw128(sm + OFF_DO, n, reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(a.dout) + off), !live);
         else
-          st_row_sw128(sm + OFF_Q, n, reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(a.q) + off), !live);
+          cp_row_sw128(sm + OFF_Q, n, reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(a.q) + off), !live);
+        cp_async_wait_all();
         fence_proxy_async_smem();
       }
       math_bar();
