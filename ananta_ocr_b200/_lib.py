@@ -183,7 +183,8 @@ class DashAttnBwdArgs(C.Structure):
                 ("delta", _p), ("flags", _p), ("dq_acc", _p), ("n_seq", _i32), ("seq_len", _i32),
                 ("n_heads", _i32), ("n_kv_heads", _i32), ("head_dim", _i32), ("dtype", _i32),
                 ("block_size", _i32), ("local_window", _i32), ("K", _i32), ("pad0", _i32),
-                ("scale", _f32), ("pad1", _f32), ("device_error", _p)]
+                ("scale", _f32), ("pad1", _f32), ("device_error", _p), ("seg_start", _p),
+                ("n_index_heads", _i32), ("pad2", _i32)]
 
 
 class DashEntmaxArgs(C.Structure):

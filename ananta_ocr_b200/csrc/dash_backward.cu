@@ -122,20 +122,27 @@ __device__ __forceinline__ void partial_scores(const float* Ks, const float* Vs,
 }
 
 // ---------------------------------------------------------------------------
+// (with several index heads: one bitmask per (sequence, index head, block);
+// with segment starts: blocks holding a key in [seg_start, remote bound))
 __global__ void __launch_bounds__(kThreads) bwd_flags_kernel(DashAttnBwdArgs a, int nblk, int words) {
   const int64_t row = (int64_t)blockIdx.x * kThreads + threadIdx.x;
   const int T = a.seq_len;
   if (row >= (int64_t)a.n_seq * T) return;
   const int s = (int)(row / T), t = (int)(row - (int64_t)s * T);
-  const int64_t ls = (int64_t)t - a.local_window + 1;
-  const int32_t* ids = a.idx + row * a.K;
-  for (int j = 0; j < a.K; ++j) {
-    const int b = ids[j];
-    if (b < 0 || b >= nblk || (int64_t)b * a.block_size >= ls) continue;
-    bool dup = false;
-    for (int j2 = 0; j2 < j && !dup; ++j2) dup = ids[j2] == b;
-    if (dup) continue;
-    atomicOr(a.flags + ((int64_t)s * nblk + b) * words + (t >> 5), 1u << (t & 31));
+  const int HI = a.n_index_heads > 1 ? a.n_index_heads : 1;
+  const int64_t seg = a.seg_start ? (int64_t)a.seg_start[row] : 0;
+  const int64_t ls = max((int64_t)t - a.local_window + 1, seg);
+  for (int ih = 0; ih < HI; ++ih) {
+    const int64_t rr = ((int64_t)s * HI + ih) * T + t;
+    const int32_t* ids = a.idx + rr * a.K;
+    for (int j = 0; j < a.K; ++j) {
+      const int b = ids[j];
+      if (b < 0 || b >= nblk || (int64_t)b * a.block_size >= ls || (int64_t)(b + 1) * a.block_size <= seg) continue;
+      bool dup = false;
+      for (int j2 = 0; j2 < j && !dup; ++j2) dup = ids[j2] == b;
+      if (dup) continue;
+      atomicOr(a.flags + (((int64_t)s * HI + ih) * nblk + b) * words + (t >> 5), 1u << (t & 31));
+    }
   }
 }
 
@@ -489,7 +496,8 @@ int launch_bwd_g(const DashAttnBwdArgs& a, int G, int nblk, int words, cudaStrea
 size_t attn_bwd_flag_words(const DashAttnBwdArgs& a) {
   const int64_t nblk = (a.seq_len + a.block_size - 1) / a.block_size;
   const int64_t words = (a.seq_len + 31) / 32;
-  return (size_t)(a.n_seq * nblk * words);
+  const int64_t HI = a.n_index_heads > 1 ? a.n_index_heads : 1;
+  return (size_t)(a.n_seq * HI * nblk * words);
 }
 
 int launch_attn_bwd(const DashAttnBwdArgs& a, cudaStream_t st) {
@@ -499,7 +507,7 @@ int launch_attn_bwd(const DashAttnBwdArgs& a, cudaStream_t st) {
   const int words = (a.seq_len + 31) / 32;
   if (cudaMemsetAsync(a.flags, 0, attn_bwd_flag_words(a) * 4, st) != cudaSuccess)
     return set_error(DASH_ERR_CUDA, "memset of the row flags failed");
-  if (a.d_bias && cudaMemsetAsync(a.d_bias, 0, (size_t)rows * a.K * 4, st) != cudaSuccess)
+  if (a.d_bias && cudaMemsetAsync(a.d_bias, 0, (size_t)rows * (a.n_index_heads > 1 ? a.n_index_heads : 1) * a.K * 4, st) != cudaSuccess)
     return set_error(DASH_ERR_CUDA, "memset of d_bias failed");
   bwd_flags_kernel<<<(unsigned)((rows + kThreads - 1) / kThreads), kThreads, 0, st>>>(a, nblk, words);
   count_launch();

@@ -155,7 +155,9 @@ __device__ __forceinline__ float reduce_scatter32(float (&v)[32], int lane) {
   return v[0];
 }
 
-template <typename E>
+// SEG: rows carry segment starts (packed sequences); without them the key >=
+// segment test is compiled out
+template <typename E, bool SEG>
 __global__ void __launch_bounds__(kTcThreads, 1)
     bwd_tc_kernel(const DashAttnBwdArgs a, int nblk, int words, int ntiles, float* dq_acc) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -181,6 +183,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int bs = a.block_size, LW = a.local_window;
   const int bA = key0 / bs, bB = min(key0 + TK - 1, T - 1) / bs;
   const int jB = bB != bA ? bB * bs - key0 : TK;        // first tile key of block B
+  // index head of this kv head; its routes are rows (s*HI + ih)*T + t
+  const int HI = a.n_index_heads > 1 ? a.n_index_heads : 1;
+  const int ih = h * HI / H;
+  const int64_t rr_shift = ((int64_t)s * (HI - 1) + ih) * T;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t kv_row = (int64_t)H * 128;
   const int64_t kvoff = ((int64_t)s * T * H + h) * 128;
@@ -218,8 +224,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (warp == kProdWarp) {
     // ===================== producer: slot lists + per-slot meta =====================
-    const uint32_t* flA = a.flags + ((int64_t)s * nblk + bA) * words;
-    const uint32_t* flB = a.flags + ((int64_t)s * nblk + bB) * words;
+    const uint32_t* flA = a.flags + (((int64_t)s * HI + ih) * nblk + bA) * words;
+    const uint32_t* flB = a.flags + (((int64_t)s * HI + ih) * nblk + bB) * words;
     const int64_t loc_end = min((int64_t)key0 + TK - 1 + LW - 1, (int64_t)T - 1);
     int next_row = key0;                 // first row not yet taken (uniform)
     for (int b = 0;; ++b) {
@@ -282,6 +288,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int i = live ? M.row[n] : 0;
         const int hq = live ? M.hq[n] : 0;
         const int64_t row = (int64_t)s * T + i;
+        const int64_t rr = row + rr_shift;     // row of this index head's routes
         int routed = 0, sA = -1, sB = -1;
         float lse = 0.f, delta = 0.f, biasA = 0.f, biasB = 0.f;
         if (live) {
@@ -290,7 +297,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if ((flA[i >> 5] >> (i & 31)) & 1u) routed |= 1;
           if (bB != bA && ((flB[i >> 5] >> (i & 31)) & 1u)) routed |= 2;
           // first slot of bA / bB: 16 independent loads per step
-          const int32_t* ids = a.idx + row * a.K;
+          const int32_t* ids = a.idx + rr * a.K;
           for (int j0 = 0; j0 < a.K && (((routed & 1) && sA < 0) || ((routed & 2) && sB < 0)); j0 += 16) {
             int v[16];
 #pragma unroll
@@ -302,8 +309,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
           }
           if (a.bias) {
-            if (sA >= 0) biasA = a.bias[row * a.K + sA];
-            if (sB >= 0) biasB = a.bias[row * a.K + sB];
+            if (sA >= 0) biasA = a.bias[rr * a.K + sA];
+            if (sB >= 0) biasB = a.bias[rr * a.K + sB];
           }
         }
         M.row[n] = (int)row;
@@ -311,7 +318,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         M.sA[n] = sA;
         M.sB[n] = sB;
         // a padding slot's position keeps every key out
-        M.a[n] = make_int4(live ? i : INT_MIN / 2, routed, __float_as_int(-lse * LOG2E), __float_as_int(delta));
+        const int seg = (live && a.seg_start) ? a.seg_start[row] : 0;
+        M.a[n] = make_int4(live ? i : INT_MIN / 2, routed | (seg << 2), __float_as_int(-lse * LOG2E),
+                           __float_as_int(delta));
         M.b[n] = make_float2((biasA - lse) * LOG2E, (biasB - lse) * LOG2E);
       }
       if (lane == 0) M.ns = ns;
@@ -434,8 +443,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               const int4 ma = M.a[n];
               const float2 mb = M.b[n];
               const int d = ma.x - key;
-              const bool local = d >= 0 && d < LW;
-              const bool remote = d >= LW && (ma.y & rmask);
+              const bool inseg = !SEG || key >= (ma.y >> 2);
+              const bool local = d >= 0 && d < LW && inseg;
+              const bool remote = d >= LW && (ma.y & rmask) && inseg;
               const float c = remote ? (keyB ? mb.y : mb.x) : __int_as_float(ma.z);
               const float p = (local || remote) ? fast_exp2(fmaf(x[e + u], sl2, c)) : 0.f;
               const float ds = (local || remote) ? p * (y[e + u] - __int_as_float(ma.w)) : 0.f;
@@ -474,7 +484,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (w * 32 >= jB) sB_sum += m_dsum[w * NS + tid];
           else sA_sum += m_dsum[w * NS + tid];
         }
-        const int64_t row = M.row[tid];
+        const int64_t row = M.row[tid] + rr_shift;
         if (M.sA[tid] >= 0) red_add(a.d_bias + row * a.K + M.sA[tid], sA_sum);
         if (M.sB[tid] >= 0) red_add(a.d_bias + row * a.K + M.sB[tid], sB_sum);
       }
@@ -549,10 +559,15 @@ int launch_tc_typed(const DashAttnBwdArgs& a, int nblk, int words, float* dq_acc
   count_launch();
   int rc = check_launch("bwd_delta_kernel");
   if (rc) return rc;
-  cudaFuncSetAttribute(bwd_tc_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_TC);
   const int ntiles = (a.seq_len + TK - 1) / TK;
-  bwd_tc_kernel<E><<<dim3((unsigned)(a.n_seq * ntiles), (unsigned)a.n_kv_heads), kTcThreads, SMEM_TC, st>>>(
-      a, nblk, words, ntiles, dq_acc);
+  const dim3 grid((unsigned)(a.n_seq * ntiles), (unsigned)a.n_kv_heads);
+  if (a.seg_start) {
+    cudaFuncSetAttribute(bwd_tc_kernel<E, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_TC);
+    bwd_tc_kernel<E, true><<<grid, kTcThreads, SMEM_TC, st>>>(a, nblk, words, ntiles, dq_acc);
+  } else {
+    cudaFuncSetAttribute(bwd_tc_kernel<E, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_TC);
+    bwd_tc_kernel<E, false><<<grid, kTcThreads, SMEM_TC, st>>>(a, nblk, words, ntiles, dq_acc);
+  }
   count_launch();
   rc = check_launch("bwd_tc_kernel");
   if (rc) return rc;

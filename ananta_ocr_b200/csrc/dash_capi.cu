@@ -373,6 +373,11 @@ static int check_attn_bwd(const DashAttnBwdArgs* a) {
     return set_error(DASH_ERR_UNSUPPORTED, "query heads per kv head %d not in {1,2,4,8}", G);
   if (a->dtype != DASH_DTYPE_BF16 && a->dtype != DASH_DTYPE_F16 && a->dtype != DASH_DTYPE_F32)
     return set_error(DASH_ERR_UNSUPPORTED, "dtype must be bf16, fp16 or fp32");
+  const int HI = a->n_index_heads > 1 ? a->n_index_heads : 1;
+  if (a->n_kv_heads % HI)
+    return set_error(DASH_ERR_INVALID, "n_index_heads %d must divide n_kv_heads %d", HI, a->n_kv_heads);
+  if ((HI > 1 || a->seg_start) && a->dtype == DASH_DTYPE_F32)
+    return set_error(DASH_ERR_UNSUPPORTED, "several index heads / segment starts need bf16 or fp16");
   return DASH_OK;
 }
 

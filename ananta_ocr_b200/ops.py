@@ -368,13 +368,16 @@ def gather_attention(q, k, v, idx, bias, *, block_size: int, local_window: int, 
 # ---------------------------------------------------------------------------
 def gather_attention_bwd(q, k, v, o, dout, lse, idx, bias, *, block_size: int,
                          local_window: int, scale: float, want_d_bias: bool = True,
+                         seg_start: Optional[torch.Tensor] = None,
                          device_error: Optional[DeviceErrorWord] = None):
     """Backward of the contiguous gather attention (``dash_attn_bwd``).
 
     q, o, dout [B, T, HQ, D]; k, v [B, T, Hkv, D] (made contiguous, one dtype);
     lse [B, T, HQ] fp32 (natural log, from the forward); idx [B, T, K] int
-    (-1 unused), bias [B, T, K] fp32 or None.  Returns (dq, dk, dv, d_bias)
-    with d_bias [B, T, K] fp32 (None unless ``want_d_bias``)."""
+    (-1 unused) or [B, HI, T, K] for HI index heads, bias of the same shape
+    fp32 or None; seg_start [B, T] int (packed sequences: row t sees keys
+    [seg_start, t]) or None.  Returns (dq, dk, dv, d_bias) with d_bias shaped
+    like idx, fp32 (None unless ``want_d_bias``)."""
     _need_cuda(q, k, v, o, dout, lse, idx)
     dt = q.dtype
     q, o, dout = (t.to(dt).contiguous() for t in (q, o, dout))
@@ -383,15 +386,19 @@ def gather_attention_bwd(q, k, v, o, dout, lse, idx, bias, *, block_size: int,
     Hkv = k.shape[2]
     idx = idx.to(torch.int32).contiguous()
     K = idx.shape[-1]
+    HI = idx.shape[1] if idx.dim() == 4 else 1
+    seg_start = None if seg_start is None else seg_start.to(torch.int32).contiguous()
     bias = None if bias is None else bias.to(torch.float32).contiguous()
     lse = lse.to(torch.float32).contiguous()
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    d_bias = torch.empty(B, T, K, dtype=torch.float32, device=q.device) if want_d_bias else None
+    d_bias = torch.empty(idx.shape, dtype=torch.float32, device=q.device) if want_d_bias else None
     delta = torch.empty(B, T, HQ, dtype=torch.float32, device=q.device)
     a = L.DashAttnBwdArgs()
     a.n_seq, a.seq_len, a.n_heads, a.n_kv_heads, a.head_dim = B, T, HQ, Hkv, D
     a.dtype, a.block_size, a.local_window, a.K = _DT[dt], int(block_size), int(local_window), K
     a.scale = float(scale)
+    a.n_index_heads = HI
+    a.seg_start = _ptr(seg_start)
     words = L.load().dash_attn_bwd_flag_words(ctypes.byref(a))
     if words < 0:
         raise L.DashError(L.DASH_ERR_UNSUPPORTED, L.last_error())

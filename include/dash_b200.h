@@ -622,6 +622,16 @@ typedef struct {
   int32_t K, pad0;
   float scale, pad1;
   DashDeviceError* device_error;
+  /* Several index heads and packed sequences (bf16 / fp16 only):
+   * n_index_heads HI > 1 gives routes idx / bias / d_bias as
+   * [n_seq, HI, seq_len, K], kv head h reading index head h * HI / n_kv_heads
+   * (HI divides n_kv_heads); seg_start [n_seq, seq_len] int32 (or NULL = 0)
+   * limits row t to keys in [seg_start, t].
+   * Replaces: sparse_gather_triton.py:107-316 (_gather_attn_bwd_dq/dkv,
+   *           HI index heads and segment starts).                          */
+  const int32_t* seg_start;
+  int32_t n_index_heads;
+  int32_t pad2;
 } DashAttnBwdArgs;
 int dash_attn_bwd(const DashAttnBwdArgs* args, dash_stream_t stream);
 int64_t dash_attn_bwd_flag_words(const DashAttnBwdArgs* args);

@@ -90,3 +90,47 @@ def entmax15_backward(y: torch.Tensor, dy: torch.Tensor) -> torch.Tensor:
     dx = dy * g
     q = dx.sum(-1, keepdim=True) / g.sum(-1, keepdim=True).clamp_min(1e-12)
     return dx - q * g
+
+
+def gather_attention_heads(q, k, v, idx, seg, block_size: int, local_window: int, scale: float):
+    """sparse_gather_triton.py restated densely: HI index heads (idx
+    [B, HI, T, K], query head hq reads index head hq // (HQ / HI)), packed
+    sequences (seg [B, T]: row t sees keys in [seg, t]), no bias.  Keys of a
+    routed block below max(t - LW + 1, seg) and the window [that bound, t]
+    are kept.  Returns (o [B,T,HQ,D], lse [B,T,HQ]); differentiable in q, k, v."""
+    B, T, HQ, D = q.shape
+    H = k.shape[2]
+    G = HQ // H
+    HI = idx.shape[1]
+    nblk = (T + block_size - 1) // block_size
+    dev = q.device
+    kb = torch.arange(T, device=dev) // block_size
+    ti = torch.arange(T, device=dev).view(1, T, 1)
+    kj = torch.arange(T, device=dev).view(1, 1, T)
+    sg = seg.long().view(B, T, 1)
+    ls = torch.maximum(ti - local_window + 1, sg)
+    local = (kj <= ti) & (kj >= ls)                                       # [B, T, T]
+    outs, lses = [], []
+    for hq in range(HQ):
+        ih = hq // (HQ // HI)
+        ids = idx[:, ih].long()                                           # [B, T, K]
+        valid = (ids >= 0) & (ids < nblk)          # no bias: duplicates change nothing
+        dump = torch.where(valid, ids, torch.full_like(ids, nblk))
+        sel = torch.zeros(B, T, nblk + 1, dtype=torch.bool, device=dev).scatter(-1, dump, True)
+        remote = (kj < ls) & (kj >= sg) & sel[:, :, :nblk][:, :, kb]
+        allowed = local | remote
+        s = scale * q[:, :, hq].float() @ k[:, :, hq // G].float().transpose(-1, -2)   # [B, T, T]
+        s = s.masked_fill(~allowed, float("-inf"))
+        lses.append(torch.logsumexp(s, -1))
+        outs.append(torch.softmax(s, -1) @ v[:, :, hq // G].float())
+    return torch.stack(outs, 2), torch.stack(lses, 2)
+
+
+def gather_attention_heads_grads(q, k, v, idx, seg, dout, block_size, local_window, scale):
+    """(o, lse, dq, dk, dv) of gather_attention_heads in fp32 via autograd."""
+    q = q.float().detach().requires_grad_(True)
+    k = k.float().detach().requires_grad_(True)
+    v = v.float().detach().requires_grad_(True)
+    o, lse = gather_attention_heads(q, k, v, idx, seg, block_size, local_window, scale)
+    o.backward(dout.float())
+    return o.detach(), lse.detach(), q.grad, k.grad, v.grad

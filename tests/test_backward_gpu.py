@@ -197,3 +197,92 @@ def test_entmax_autograd_matches_oracle(rows, n):
     # another dim than the last
     y2 = entmax15(x.detach().t().contiguous(), 0)
     torch.testing.assert_close(y2.t(), yr.detach(), rtol=1e-5, atol=1e-6)
+
+
+# ---------------------------------------------------------------------------
+# several index heads + packed sequences (sparse_gather_triton's path, no bias)
+# ---------------------------------------------------------------------------
+from ananta_ocr_b200 import sparse_gather_triton as SG  # noqa: E402
+from ananta_ocr_b200 import _lib as L  # noqa: E402
+
+
+def packed(B, T, seed):
+    """position_ids of packed sequences (random segment lengths) and the
+    matching segment starts arange(T) - position_ids."""
+    g = torch.Generator().manual_seed(seed)
+    pos = torch.empty(B, T, dtype=torch.int64)
+    for b in range(B):
+        t = 0
+        while t < T:
+            n = int(torch.randint(40, 300, (1,), generator=g))
+            pos[b, t:t + n] = torch.arange(min(n, T - t))
+            t += n
+    return pos.cuda(), (torch.arange(T)[None] - pos.cpu()).to(torch.int32).cuda()
+
+
+def heads_routes(B, HI, T, K, bs, seed):
+    g = torch.Generator().manual_seed(seed)
+    idx = torch.full((B, HI, T, K), -1, dtype=torch.int32)
+    for t in range(T):
+        n = int(torch.randint(0, K + 1, (1,), generator=g))
+        if n:
+            idx[:, :, t, :n] = torch.randint(0, t // bs + 1, (B, HI, n), generator=g, dtype=torch.int32)
+    return idx.cuda()
+
+
+@pytest.mark.parametrize("B,HQ,H,HI,T,bs,LW,K", [(2, 8, 4, 2, 600, 64, 128, 5),
+                                                  (1, 4, 2, 1, 450, 128, 128, 3)])
+def test_multi_index_head_packed_backward_matches_oracle(B, HQ, H, HI, T, bs, LW, K):
+    g = torch.Generator().manual_seed(T + HI)
+    q = (torch.randn(B, T, HQ, 128, generator=g) * 0.5).to(torch.bfloat16).cuda()
+    k = (torch.randn(B, T, H, 128, generator=g) * 0.5).to(torch.bfloat16).cuda()
+    v = (torch.randn(B, T, H, 128, generator=g) * 0.5).to(torch.bfloat16).cuda()
+    do = torch.randn(B, T, HQ, 128, generator=g).to(torch.bfloat16).cuda()
+    _, seg = packed(B, T, T)
+    idx = heads_routes(B, HI, T, K, bs, T + 1)
+    scale = 1.0 / math.sqrt(128)
+    lse = torch.empty(B, HQ, T, device="cuda")
+    o = ops.gather_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), idx, None,
+                             block_size=bs, local_window=LW, scale=scale, seg_start=seg,
+                             n_index_heads=HI, lse=lse)
+    o = o.transpose(1, 2).contiguous()
+    dq, dk, dv, _ = ops.gather_attention_bwd(q, k, v, o, do, lse.transpose(1, 2), idx, None,
+                                             block_size=bs, local_window=LW, scale=scale,
+                                             want_d_bias=False, seg_start=seg)
+    ro, rlse, rdq, rdk, rdv = BO.gather_attention_heads_grads(q, k, v, idx, seg, do, bs, LW, scale)
+    close(o, ro, 0.02, 0.01)
+    close(lse.transpose(1, 2), rlse, 1e-3)
+    for got, ref in ((dq, rdq), (dk, rdk), (dv, rdv)):
+        close(got, ref, 0.02, 0.015)
+
+
+def test_gather_attention_mirror_gradients_match_oracle():
+    """sparse_gather_triton.triton_gather_attention with requires_grad (two
+    index heads, packed sequences) through the reference-named autograd
+    Function."""
+    B, HQ, H, HI, T, bs, LW, K = 1, 4, 2, 2, 520, 64, 128, 4
+    g = torch.Generator().manual_seed(11)
+    q = (torch.randn(B, HQ, T, 128, generator=g) * 0.5).to(torch.bfloat16).cuda().requires_grad_()
+    k = (torch.randn(B, H, T, 128, generator=g) * 0.5).to(torch.bfloat16).cuda().requires_grad_()
+    v = (torch.randn(B, H, T, 128, generator=g) * 0.5).to(torch.bfloat16).cuda().requires_grad_()
+    do = torch.randn(B, HQ, T, 128, generator=g).to(torch.bfloat16).cuda()
+    pos, seg = packed(B, T, 5)
+    idx = heads_routes(B, HI, T, K, bs, 6)
+    o = SG.triton_gather_attention(q, k, v, idx, pos, None, bs, 1.0 / math.sqrt(128), LW)
+    o.backward(do)
+    tr = lambda t: t.detach().transpose(1, 2)     # noqa: E731
+    ro, _, rdq, rdk, rdv = BO.gather_attention_heads_grads(tr(q), tr(k), tr(v), idx, seg, tr(do), bs, LW,
+                                                           1.0 / math.sqrt(128))
+    close(o.detach().transpose(1, 2), ro, 0.02, 0.01)
+    for got, ref in ((q.grad, rdq), (k.grad, rdk), (v.grad, rdv)):
+        close(got.transpose(1, 2), ref, 0.02, 0.015)
+
+
+def test_fp32_with_segments_is_rejected():
+    T = 128
+    x = torch.zeros(1, T, 2, 128, device="cuda")
+    idx = torch.full((1, T, 2), -1, dtype=torch.int32, device="cuda")
+    seg = torch.zeros(1, T, dtype=torch.int32, device="cuda")
+    with pytest.raises(L.DashError):
+        ops.gather_attention_bwd(x, x, x, x, x, torch.zeros(1, T, 2, device="cuda"), idx, None,
+                                 block_size=64, local_window=64, scale=0.1, seg_start=seg)

@@ -51,3 +51,25 @@ def test_entmax_matches_reference():
     np.testing.assert_allclose(y.sum(-1).numpy(), 1.0, rtol=1e-5)
     dx = BO.entmax15_backward(t("ent_y"), t("ent_dy"))
     np.testing.assert_allclose(dx.numpy(), G["ent_dx"], rtol=1e-5, atol=1e-6)
+
+
+def test_multi_index_head_restatement_reduces_to_the_pinned_one():
+    """gather_attention_heads (several index heads, packed sequences, no bias)
+    with one index head and no packing equals gather_attention with zero
+    biases, which the reference's e2e goldens pin; with two index heads each
+    query head follows its own index head's routes."""
+    g = torch.Generator().manual_seed(4)
+    B, HQ, H, T, bs, LW, K = 1, 4, 2, 200, 64, 64, 3
+    q = torch.randn(B, T, HQ, 128, generator=g) * 0.5
+    k = torch.randn(B, T, H, 128, generator=g) * 0.5
+    v = torch.randn(B, T, H, 128, generator=g) * 0.5
+    idx = torch.randint(-1, 4, (B, 2, T, K), generator=g, dtype=torch.int32)
+    seg = torch.zeros(B, T, dtype=torch.int32)
+    o1, l1 = BO.gather_attention_heads(q, k, v, idx[:, :1], seg, bs, LW, 1.0 / math.sqrt(128))
+    o2, l2 = BO.gather_attention(q, k, v, idx[:, 0], torch.zeros(B, T, K), bs, LW, 1.0 / math.sqrt(128))
+    torch.testing.assert_close(o1, o2, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(l1, l2, rtol=1e-5, atol=1e-5)
+    oh, _ = BO.gather_attention_heads(q, k, v, idx, seg, bs, LW, 1.0 / math.sqrt(128))
+    ob, _ = BO.gather_attention(q[:, :, 2:], k[:, :, 1:], v[:, :, 1:], idx[:, 1], torch.zeros(B, T, K),
+                                bs, LW, 1.0 / math.sqrt(128))
+    torch.testing.assert_close(oh[:, :, 2:], ob, rtol=1e-5, atol=1e-5)
