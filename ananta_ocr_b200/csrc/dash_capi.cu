@@ -84,6 +84,32 @@ static int check_qo(const DashQO& qo) {
 
 }  // namespace dash
 
+namespace dash {
+
+// Every check of a decode call that does not depend on the workspace, and the
+// split count it will run with.  Shared by dash_decode_attn, the workspace
+// query and the allocation-free entry point, so a malformed call is rejected
+// before anything is sized (no division by a zero block size, no size from a
+// negative row count).
+int validate_decode(const DashDecodeArgs* a, int* splits) {
+  if (!a) return set_error(DASH_ERR_INVALID, "null args");
+  int rc = check_seqs(a->seqs);
+  if (!rc) rc = check_kv(a->kv, a->qo.n_heads, a->block_size);
+  if (!rc) rc = check_routes(a->routes, a->qo.n_heads, a->kv.n_kv_heads);
+  if (!rc) rc = check_qo(a->qo);
+  if (rc) return rc;
+  if (a->local_window < 0) return set_error(DASH_ERR_INVALID, "local_window must be >= 0");
+  if (a->routes.K + a->local_window / a->block_size + 2 > 480)
+    return set_error(DASH_ERR_UNSUPPORTED, "too many blocks per decode row");
+  if (a->num_splits < 0) return set_error(DASH_ERR_INVALID, "num_splits must be >= 0");
+  const int sp = a->num_splits > 0 ? a->num_splits : decode_auto_splits(*a, seq_rows(a->seqs));
+  if (sp > 64) return set_error(DASH_ERR_UNSUPPORTED, "num_splits %d > 64", sp);
+  *splits = sp;
+  return DASH_OK;
+}
+
+}  // namespace dash
+
 using namespace dash;
 
 extern "C" {
@@ -186,8 +212,8 @@ int dash_prefill_attn(const DashPrefillArgs* a, dash_stream_t stream) {
   const int G = a->qo.n_heads / a->kv.n_kv_heads;
   if (G != 1 && G != 2 && G != 4 && G != 8 && G != 16)
     return set_error(DASH_ERR_UNSUPPORTED, "query heads per kv head %d not in {1,2,4,8,16}", G);
-  if (a->block_size % 64 != 0 || a->block_size > 256)
-    return set_error(DASH_ERR_UNSUPPORTED, "prefill block_size %d not in {64,128,192,256}", a->block_size);
+  if (a->block_size != 32 && (a->block_size % 64 != 0 || a->block_size > 256))
+    return set_error(DASH_ERR_UNSUPPORTED, "prefill block_size %d not in {32,64,128,192,256}", a->block_size);
   if (a->local_window < 0) return set_error(DASH_ERR_INVALID, "local_window must be >= 0");
   if (a->kv.block_table == nullptr && a->seqs.kv_len_fixed <= 0)
     return set_error(DASH_ERR_INVALID, "contiguous K/V needs kv_len_fixed (allocated length)");
@@ -200,25 +226,16 @@ int dash_prefill_attn(const DashPrefillArgs* a, dash_stream_t stream) {
 }
 
 size_t dash_decode_workspace_size(const DashDecodeArgs* a) {
-  if (!a) return 0;
-  int64_t rows = seq_rows(a->seqs);
-  int sp = a->num_splits > 0 ? a->num_splits : decode_auto_splits(*a, rows);
-  return decode_workspace(*a, rows, sp);
+  int sp = 0;
+  if (validate_decode(a, &sp)) return 0;
+  return decode_workspace(*a, seq_rows(a->seqs), sp);
 }
 
 int dash_decode_attn(const DashDecodeArgs* a, dash_stream_t stream) {
-  if (!a) return set_error(DASH_ERR_INVALID, "null args");
-  int rc = check_seqs(a->seqs);
-  if (!rc) rc = check_kv(a->kv, a->qo.n_heads, a->block_size);
-  if (!rc) rc = check_routes(a->routes, a->qo.n_heads, a->kv.n_kv_heads);
-  if (!rc) rc = check_qo(a->qo);
+  int sp = 0;
+  int rc = validate_decode(a, &sp);
   if (rc) return rc;
-  if (a->local_window < 0) return set_error(DASH_ERR_INVALID, "local_window must be >= 0");
-  if (a->routes.K + a->local_window / a->block_size + 2 > 480)
-    return set_error(DASH_ERR_UNSUPPORTED, "too many blocks per decode row");
   int64_t rows = seq_rows(a->seqs);
-  int sp = a->num_splits > 0 ? a->num_splits : decode_auto_splits(*a, rows);
-  if (sp > 64) return set_error(DASH_ERR_UNSUPPORTED, "num_splits %d > 64", sp);
   size_t need = decode_workspace(*a, rows, sp);
   if (need && (!a->workspace || a->workspace_bytes < need))
     return set_error(DASH_ERR_WORKSPACE, "decode workspace %zu bytes needed, %zu given", need,

@@ -19,6 +19,7 @@ int launch_prefill(const DashPrefillArgs& a, int64_t n_rows, cudaStream_t st);
 size_t prefill_workspace(const DashPrefillArgs& a, int64_t n_rows);
 size_t decode_workspace(const DashDecodeArgs& a, int64_t n_rows, int splits);
 int decode_auto_splits(const DashDecodeArgs& a, int64_t n_rows);
+int validate_decode(const DashDecodeArgs* a, int* splits);   // DASH_OK or a status with message
 int launch_page_ids(const DashPageIdsArgs& a, cudaStream_t st);
 int launch_page_state(const DashPageStateArgs& a, cudaStream_t st);
 int launch_page_allow(const DashPageAllowArgs& a, cudaStream_t st);

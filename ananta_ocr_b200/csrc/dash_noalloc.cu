@@ -46,7 +46,9 @@ int scratch_address(void** out) {
 extern "C" size_t dash_noalloc_scratch_bytes(void) { return kScratchBytes; }
 
 extern "C" int dash_decode_attn_noalloc(const DashDecodeArgs* args, dash_stream_t stream) {
-  if (!args) return dash::set_error(DASH_ERR_INVALID, "null args");
+  int splits = 0;
+  const int rc0 = dash::validate_decode(args, &splits);
+  if (rc0) return rc0;
   const size_t need = dash_decode_workspace_size(args);
   if (need > kScratchBytes)
     return dash::set_error(DASH_ERR_WORKSPACE,

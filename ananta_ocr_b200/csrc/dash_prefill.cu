@@ -100,10 +100,14 @@ __device__ __forceinline__ int64_t row_base(const DashSeqs& q, int s) {
 // Slot j of a row lives in lane j % 32, register j / 32 (PER registers);
 // duplicate and rank tests run over warp shuffles.  The next row's slots are
 // loaded before the current row is processed.
+// With 32-token blocks (PAIR) a 64-key tile holds blocks 2p and 2p+1, and the
+// list is written per tile instead of per block: entry = (p << 2) | routed
+// bits (bit h: block 2p+h routed), biases [2j + h], ascending in p, so the
+// attention kernel's cursor still moves at most one entry per key tile.
 // ---------------------------------------------------------------------------
 constexpr int kPlanWarps = 16;
 
-template <int PER>
+template <int PER, bool PAIR>
 __global__ void __launch_bounds__(kPlanWarps * 32) plan_kernel(DashPrefillArgs a, PrefillPlan p,
                                                                int32_t* cidx, float* cbias,
                                                                uint32_t* tmask, float* rowmax) {
@@ -179,20 +183,70 @@ __global__ void __launch_bounds__(kPlanWarps * 32) plan_kernel(DashPrefillArgs a
       }
     }
     int32_t* oi = cidx + ((int64_t)ih * p.n_rows + r) * K;
-    float* ob = cbias + ((int64_t)ih * p.n_rows + r) * K;
+    float* ob = cbias + ((int64_t)ih * p.n_rows + r) * K * (PAIR ? 2 : 1);
     int nk = 0;
     float bmax = -INFINITY;
+    if constexpr (!PAIR) {
+#pragma unroll
+      for (int q = 0; q < PER; ++q) {
+        if (keep[q]) {
+          oi[rank[q]] = b[q];
+          ob[rank[q]] = bias[q];
+        }
+        nk += __popc(__ballot_sync(0xffffffffu, keep[q]));
+      }
+      for (int j = nk + lane; j < K; j += 32) { oi[j] = -1; ob[j] = 0.0f; }
+    } else {
+      // partner = the other block of the same 64-key tile (ids are distinct
+      // after the duplicate test, so at most one kept slot matches)
+      bool pk[PER];
+      float pbias[PER];
+#pragma unroll
+      for (int q = 0; q < PER; ++q) { pk[q] = false; pbias[q] = 0.0f; }
+#pragma unroll
+      for (int qs = 0; qs < PER; ++qs) {
+        const int key = keep[qs] ? b[qs] : -2;
+        for (int src = 0; src < 32; ++src) {
+          const int ku = __shfl_sync(0xffffffffu, key, src);
+          const float bu = __shfl_sync(0xffffffffu, bias[qs], src);
+#pragma unroll
+          for (int q = 0; q < PER; ++q)
+            if (keep[q] && ku == (b[q] ^ 1)) { pk[q] = true; pbias[q] = bu; }
+        }
+      }
+      // the lower kept block of a tile leads its entry; entries ranked by tile
+      bool lead[PER];
+      int prank[PER];
+#pragma unroll
+      for (int q = 0; q < PER; ++q) { lead[q] = keep[q] && (!(b[q] & 1) || !pk[q]); prank[q] = 0; }
+#pragma unroll
+      for (int qs = 0; qs < PER; ++qs) {
+        const int key = lead[qs] ? (b[qs] >> 1) : INT_MAX;
+        for (int src = 0; src < 32; ++src) {
+          const int ku = __shfl_sync(0xffffffffu, key, src);
+#pragma unroll
+          for (int q = 0; q < PER; ++q) prank[q] += ku < (b[q] >> 1) ? 1 : 0;
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < PER; ++q) {
+        if (lead[q]) {
+          const int hb = b[q] & 1;
+          oi[prank[q]] = ((b[q] >> 1) << 2) | (1 << hb) | (pk[q] ? (1 << (hb ^ 1)) : 0);
+          ob[2 * prank[q] + hb] = bias[q];
+          ob[2 * prank[q] + (hb ^ 1)] = pk[q] ? pbias[q] : 0.0f;
+        }
+        nk += __popc(__ballot_sync(0xffffffffu, lead[q]));
+      }
+      for (int j = nk + lane; j < K; j += 32) { oi[j] = -1; ob[2 * j] = 0.0f; ob[2 * j + 1] = 0.0f; }
+    }
 #pragma unroll
     for (int q = 0; q < PER; ++q) {
       if (keep[q]) {
-        oi[rank[q]] = b[q];
-        ob[rank[q]] = bias[q];
         atomicOr(s_mask + (b[q] >> 5), 1u << (b[q] & 31));
         if (a.routes.bias) bmax = fmaxf(bmax, bias[q]);
       }
-      nk += __popc(__ballot_sync(0xffffffffu, keep[q]));
     }
-    for (int j = nk + lane; j < K; j += 32) { oi[j] = -1; ob[j] = 0.0f; }
     for (int o = 16; o > 0; o >>= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
     if (lane == 0) rowmax[(int64_t)ih * p.n_rows + r] = bmax;
   }
@@ -204,14 +258,31 @@ __global__ void __launch_bounds__(kPlanWarps * 32) plan_kernel(DashPrefillArgs a
 // ---------------------------------------------------------------------------
 // Key-tile iterator over the shared block mask (ascending).  After a call that
 // returned kt0 >= 0, b is the block of the tile and half its 64-key part, so
-// callers need no division by the block size.
+// callers need no division by the block size.  With 32-token blocks (PAIR) a
+// tile is kept when either of its blocks 2p, 2p+1 is set and b = 2p.
 // ---------------------------------------------------------------------------
 struct TileIter {
   int w, b, half;
   uint32_t bits;
 };
+template <bool PAIR>
 __device__ __forceinline__ int next_tile(TileIter& t, const uint32_t* mask, int nwords, int bs,
                                          int64_t pmax, int kvl) {
+  if constexpr (PAIR) {
+    while (true) {
+      while (t.bits == 0) {
+        if (++t.w >= nwords) return -1;
+        const uint32_t m = mask[t.w];
+        t.bits = (m | (m >> 1)) & 0x55555555u;
+      }
+      const int bit = __ffs(t.bits) - 1;
+      t.bits &= t.bits - 1;
+      t.b = t.w * 32 + bit;
+      const int64_t kt0 = (int64_t)t.b * 32;
+      if (kt0 > pmax || kt0 >= kvl) continue;
+      return (int)kt0;
+    }
+  }
   const int halves = bs / BN;
   while (true) {
     if (t.half + 1 < halves && t.b >= 0) {
@@ -232,7 +303,7 @@ __device__ __forceinline__ int next_tile(TileIter& t, const uint32_t* mask, int 
   }
 }
 
-template <typename T, bool PAGED>
+template <typename T, bool PAGED, bool PAIR>
 __global__ void __launch_bounds__(NTHREADS, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                    const DashPrefillArgs a, const PrefillPlan p) {
@@ -325,12 +396,44 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         TileIter itr{-1, -1, 0, 0u};
         int it = 0;
         while (true) {
-          int kt0 = next_tile(itr, smask, p.nwords, bs, pmax, kvl);
+          int kt0 = next_tile<PAIR>(itr, smask, p.nwords, bs, pmax, kvl);
           if (kt0 < 0) break;
           const int st = it % NSTAGE;
           if (it >= NSTAGE && !mbar_wait(kv_empty + st, ((it / NSTAGE) - 1) & 1, abort_flag, derr, 40)) break;
           uint8_t* dK = sm + OFF_K + st * 16384;
           uint8_t* dV = sm + OFF_V + st * 16384;
+          if constexpr (PAGED && PAIR) {
+            // two 32-token pages per key tile (32-row boxes at rows 0 and 32 of
+            // each swizzled half; 4096 B keeps the 1024 B swizzle atom); the
+            // second page exists only when the tile reaches past the first
+            const int64_t brow = (int64_t)s * a.kv.bt_stride + itr.b;
+            const int page0 = a.kv.block_table[brow];
+            const bool two = kt0 + 32 < kvl;
+            const int page1 = two ? a.kv.block_table[brow + 1] : 0;
+            const bool ok0 = page0 >= 0 && (int64_t)page0 < a.kv.num_pages;
+            const bool ok1 = two && page1 >= 0 && (int64_t)page1 < a.kv.num_pages;
+            if (!ok0) record_error(derr, DASH_DEV_BAD_PAGE, 43, page0);
+            if (two && !ok1) record_error(derr, DASH_DEV_BAD_PAGE, 44, page1);
+            const uint32_t bytes = (ok0 ? 16384u : 0u) + (ok1 ? 16384u : 0u);
+            if (bytes) {
+              mbar_arrive_expect_tx(kv_full + st, bytes);
+#pragma unroll
+              for (int dh = 0; dh < 2; ++dh) {
+                if (ok0) {
+                  tma_load_4d(dK + dh * 8192, &tmK, kv_full + st, dh * 64, 0, hk, page0);
+                  tma_load_4d(dV + dh * 8192, &tmV, kv_full + st, dh * 64, 0, hk, page0);
+                }
+                if (ok1) {
+                  tma_load_4d(dK + dh * 8192 + 4096, &tmK, kv_full + st, dh * 64, 0, hk, page1);
+                  tma_load_4d(dV + dh * 8192 + 4096, &tmV, kv_full + st, dh * 64, 0, hk, page1);
+                }
+              }
+            } else {
+              mbar_arrive(kv_full + st);
+            }
+            ++it;
+            continue;
+          }
           int c1, c3;
           bool ok = true;
           if (PAGED) {
@@ -393,7 +496,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           return true;
         };
         while (alive) {
-          int kt0 = next_tile(itr, smask, p.nwords, bs, pmax, kvl);
+          int kt0 = next_tile<PAIR>(itr, smask, p.nwords, bs, pmax, kvl);
           if (kt0 < 0) break;
           const int st = it % NSTAGE, sb = it & 1;
           if (!mbar_wait(kv_full + st, (it / NSTAGE) & 1, abort_flag, derr, 52)) { alive = false; break; }
@@ -467,17 +570,29 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       // rows past the end of the tile read row 0's list (never used)
       const int64_t lrow = (int64_t)ih * p.n_rows + (row_ok ? rglob : 0);
       const int32_t* rl = p.cidx + lrow * K;
-      const float* rbl = p.cbias + lrow * K;
+      const float* rbl = p.cbias + lrow * K * (PAIR ? 2 : 1);
       const bool has_bias = a.routes.bias != nullptr;
+      // An entry's biases for the two 32-column halves of its key tile (PAIR:
+      // the tile's two blocks; otherwise the block's bias for both).  plan_kernel
+      // zero-fills the bias lists when there is no bias.
+      auto ld_bias = [&](int j) -> float2 {
+        if constexpr (PAIR) {
+          return reinterpret_cast<const float2*>(rbl)[j];
+        } else {
+          const float v = rbl[j];
+          return make_float2(v, v);
+        }
+      };
+      auto key_of = [](int raw) -> int { return PAIR ? (raw >= 0 ? raw >> 2 : -1) : raw; };
       // cursor = entry cur_j; the raw entry after it is kept prefetched in
       // registers.  The prefetch is unconditional (index clamped to the list) and
       // its value is first used at the next advance, at least one key tile
       // later, so no instruction of the tile loop waits on it.
       int cur_j = 0;
-      int cur_b = (row_ok && K > 0) ? rl[0] : -1;
-      float cur_bias = (row_ok && K > 0 && has_bias) ? rbl[0] : 0.0f;
+      int cur_raw = (row_ok && K > 0) ? rl[0] : -1;
+      float2 cur_bias = (row_ok && K > 0) ? ld_bias(0) : make_float2(0.0f, 0.0f);
       int nxt_raw = (row_ok && K > 1) ? rl[1] : -1;
-      float nxt_bias_raw = (row_ok && K > 1) ? rbl[1] : 0.0f;
+      float2 nxt_bias_raw = (row_ok && K > 1) ? ld_bias(1) : make_float2(0.0f, 0.0f);
       const float sl2 = a.scale * 1.4426950408889634f;
       const float LOG2E = 1.4426950408889634f;
       // Running max (exp2 domain) starts at the row's largest routed bias: the
@@ -493,37 +608,45 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       TileIter itr{-1, -1, 0, 0u};
       int it = 0;
       bool alive = true;
-      // Advance the routed-list cursor to block blk; sel / b2 describe the
-      // block for this row.  Every kept routed block has a key tile of its
-      // own, so the cursor moves at most one entry per tile and takes the
-      // prefetched entry; the refill is unconditional (same address while the
-      // cursor stays) and first read a tile later.  The inner walk only serves
-      // lists that skip a tile, which plan_kernel never writes.
-      auto cursor_to = [&](int blk, bool& sel, float& b2) {
+      // Advance the routed-list cursor to the entry of key tile `key` (block
+      // id, or tile index with PAIR); sel0/sel1 and b20/b21 describe the two
+      // 32-column halves of the tile for this row.  Every kept entry has a key
+      // tile of its own, so the cursor moves at most one entry per tile and
+      // takes the prefetched entry; the refill is unconditional (same address
+      // while the cursor stays) and first read a tile later.  The inner walk
+      // only serves lists that skip a tile, which plan_kernel never writes.
+      auto cursor_to = [&](int key, bool& sel0, bool& sel1, float& b20, float& b21) {
+        int cur = key_of(cur_raw);
         if (K > 0) {
-          if (cur_b >= 0 && cur_b < blk) {
+          if (cur >= 0 && cur < key) {
             ++cur_j;
-            cur_b = cur_j < K ? nxt_raw : -1;
-            cur_bias = has_bias ? nxt_bias_raw : 0.0f;
-            while (cur_b >= 0 && cur_b < blk) {
+            cur_raw = cur_j < K ? nxt_raw : -1;
+            cur_bias = nxt_bias_raw;
+            cur = key_of(cur_raw);
+            while (cur >= 0 && cur < key) {
               ++cur_j;
-              cur_b = cur_j < K ? rl[cur_j] : -1;
-              cur_bias = (cur_j < K && has_bias) ? rbl[cur_j] : 0.0f;
+              cur_raw = cur_j < K ? rl[cur_j] : -1;
+              cur_bias = cur_j < K ? ld_bias(cur_j) : make_float2(0.0f, 0.0f);
+              cur = key_of(cur_raw);
             }
           }
           const int j2 = min(cur_j + 1, K - 1);
           nxt_raw = rl[j2];
-          nxt_bias_raw = rbl[j2];
+          nxt_bias_raw = ld_bias(j2);
         }
-        sel = cur_b == blk;
-        b2 = sel ? cur_bias * LOG2E : 0.0f;
+        const bool on = cur == key;
+        sel0 = on && (!PAIR || (cur_raw & 1));
+        sel1 = on && (!PAIR || (cur_raw & 2));
+        b20 = sel0 ? cur_bias.x * LOG2E : 0.0f;
+        b21 = sel1 ? cur_bias.y * LOG2E : 0.0f;
       };
+      auto tile_key = [&]() -> int { return PAIR ? (itr.b >> 1) : itr.b; };
       // The iterator and the cursor run one tile ahead: the next tile's
       // bookkeeping is done while this tile's S load is in flight.
-      int kt0 = next_tile(itr, smask, p.nwords, bs, pmax, kvl);
-      bool sel = false;
-      float b2 = 0.0f;
-      if (kt0 >= 0) cursor_to(itr.b, sel, b2);
+      int kt0 = next_tile<PAIR>(itr, smask, p.nwords, bs, pmax, kvl);
+      bool sel0 = false, sel1 = false;
+      float b20 = 0.0f, b21 = 0.0f;
+      if (kt0 >= 0) cursor_to(tile_key(), sel0, sel1, b20, b21);
       while (alive && kt0 >= 0) {
         const int st = it % NSTAGE, sb = it & 1;
         // zero V rows past the end of the sequence (never multiply garbage by P = 0)
@@ -539,9 +662,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         if (!mbar_wait_warp(s_full + sb, (it >> 1) & 1, abort_flag, derr, 61)) { alive = false; break; }
         tc_fence_after();
-        // Column c of this key tile is kept iff lo <= c <= hi, where lo is the
-        // first local column, or the first attendable column when the block is
-        // routed; logits are x = s*scale*log2e + (local ? 0 : bias) - m_run.
+        // Column c (half h = c / 32) of this key tile is kept iff
+        // lo_h <= c <= hi, where lo_h is the first local column, or the first
+        // attendable column when half h's block is routed; logits are
+        // x = s*scale*log2e + (local ? 0 : bias of half h) - m_run.
         // S(it) -> registers; the row's mask terms are computed while the
         // load is in flight (the wait comes before any branch on them)
         const uint32_t tSb = tS + sb * BN + lane_base;
@@ -551,31 +675,38 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int hi = min(63, max(-1, pos_i - kt0));
         const int lo_seg = min(64, max(0, seg_i - kt0));
         const int lo_loc = min(64, max(0, lstart_i - kt0));
-        const int lo = max(sel ? 0 : lo_loc, lo_seg);
+        const int lo0 = max(sel0 ? 0 : lo_loc, lo_seg);
+        const int lo1 = PAIR ? max(sel1 ? 0 : lo_loc, lo_seg) : lo0;
         const float add_loc = -m_run;
-        const float add_rem = b2 - m_run;
-        const int kt_next = next_tile(itr, smask, p.nwords, bs, pmax, kvl);
-        bool sel_next = false;
-        float b2_next = 0.0f;
-        if (kt_next >= 0) cursor_to(itr.b, sel_next, b2_next);
+        const float add_rem0 = b20 - m_run;
+        const float add_rem1 = PAIR ? b21 - m_run : add_rem0;
+        const int kt_next = next_tile<PAIR>(itr, smask, p.nwords, bs, pmax, kvl);
+        bool sel0_next = false, sel1_next = false;
+        float b20_next = 0.0f, b21_next = 0.0f;
+        if (kt_next >= 0) cursor_to(tile_key(), sel0_next, sel1_next, b20_next, b21_next);
         uint32_t pk[32];
         tmem_ld_wait();
-        // Pure tile for this row: all 64 columns kept with one additive term, or
-        // none kept.  When every row of the warp is pure and the tile lies inside
-        // the sequence (tiles away from the window edge and the diagonal), the
-        // logits take one packed FFMA per 2 columns (an empty row adds -inf), P is
-        // produced directly, and the rescale test runs on the row's partial sums.
-        const bool empty = lo > hi;
-        const bool full = lo == 0 && hi == 63 && (lo_loc == 0 || lo_loc == 64);
+        // Pure halves for this row: all 32 columns of a half kept with one
+        // additive term, or none kept.  When both halves of every row of the
+        // warp are pure and the tile lies inside the sequence (tiles away from
+        // the window edge and the diagonal), the logits take one packed FFMA
+        // per 2 columns (an empty half adds -inf), P is produced directly, and
+        // the rescale test runs on the row's partial sums.
+        const bool empty0 = lo0 > min(hi, 31);
+        const bool full0 = lo0 == 0 && hi >= 31 && (lo_loc == 0 || lo_loc >= 32);
+        const bool empty1 = max(lo1, 32) > hi;
+        const bool full1 = lo1 <= 32 && hi == 63 && (lo_loc <= 32 || lo_loc == 64);
         bool done = false;
-        if (__all_sync(0xffffffffu, empty || full) && kt0 + BN <= kvl) {
-          const float add = empty ? -INFINITY : (lo_loc == 0 ? add_loc : add_rem);
-          const uint64_t sl2v = f2_pack(sl2, sl2), addv = f2_pack(add, add);
+        if (__all_sync(0xffffffffu, (empty0 || full0) && (empty1 || full1)) && kt0 + BN <= kvl) {
+          const float add0 = empty0 ? -INFINITY : (lo_loc == 0 ? add_loc : add_rem0);
+          const float add1 = empty1 ? -INFINITY : (lo_loc <= 32 ? add_loc : add_rem1);
+          const uint64_t sl2v = f2_pack(sl2, sl2), addv0 = f2_pack(add0, add0),
+                         addv1 = f2_pack(add1, add1);
           uint64_t lsv = f2_pack(0.0f, 0.0f);
   #pragma unroll
           for (int e = 0; e < 32; ++e) {
             float y0, y1;
-            f2_unpack(ffma2(f2_pack(x[2 * e], x[2 * e + 1]), sl2v, addv), y0, y1);
+            f2_unpack(ffma2(f2_pack(x[2 * e], x[2 * e + 1]), sl2v, e < 16 ? addv0 : addv1), y0, y1);
             // one pair in four on the FMA pipe, the rest on the MUFU unit
             float p0, p1;
             if ((e & 3) == 3) {
@@ -610,8 +741,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const int c = 32 * h + j;
-              const float v = fmaf(x[j], sl2, c >= lo_loc ? add_loc : add_rem);
-              mx = fmaxf(mx, (c >= lo && c <= hi) ? v : -INFINITY);
+              const float v = fmaf(x[j], sl2, c >= lo_loc ? add_loc : (h ? add_rem1 : add_rem0));
+              mx = fmaxf(mx, (c >= (h ? lo1 : lo0) && c <= hi) ? v : -INFINITY);
             }
           }
           const bool need = mx > kGrowLog2;
@@ -650,8 +781,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   #pragma unroll
               for (int u = 0; u < 2; ++u) {
                 const int j = 2 * e + u, c = 32 * h + j;
-                const float v = fmaf(x[j], sl2, (c >= lo_loc ? add_loc : add_rem) - shift);
-                pp[u] = fast_exp2((c >= lo && c <= hi) ? v : -INFINITY);
+                const float v = fmaf(x[j], sl2, (c >= lo_loc ? add_loc : (h ? add_rem1 : add_rem0)) - shift);
+                pp[u] = fast_exp2((c >= (h ? lo1 : lo0) && c <= hi) ? v : -INFINITY);
               }
               ls4[e & 3] += pp[0] + pp[1];
               pk[16 * h + e] = pack2(pp[0], pp[1], (T*)nullptr);
@@ -668,8 +799,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (lane == 0) mbar_arrive(p_full + sb);
         ++it;
         kt0 = kt_next;
-        sel = sel_next;
-        b2 = b2_next;
+        sel0 = sel0_next;
+        sel1 = sel1_next;
+        b20 = b20_next;
+        b21 = b21_next;
       }
       // ---- epilogue ----
       float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
@@ -739,7 +872,9 @@ static int make_kv_map(CUtensorMap* map, const void* base, const DashPrefillArgs
   strides[0] = (cuuint64_t)a.kv.stride_tok * esz;
   strides[1] = (cuuint64_t)a.kv.stride_head * esz;
   strides[2] = (cuuint64_t)a.kv.stride_seq * esz;
-  cuuint32_t box[4] = {64, (cuuint32_t)BN, 1, 1};
+  // 32-token pages are loaded as two 32-row boxes per key tile
+  const cuuint32_t rows = (paged && a.block_size < BN) ? (cuuint32_t)a.block_size : (cuuint32_t)BN;
+  cuuint32_t box[4] = {64, rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   for (int k = 0; k < 3; ++k)
     if (strides[k] % 16 != 0 || strides[k] == 0)
@@ -766,14 +901,18 @@ static void plan_geometry(const DashPrefillArgs& a, int64_t n_rows, PrefillPlan&
   p.n_rows = n_rows;
 }
 
+// Workspace: canonical block lists, their biases (two per entry with
+// 32-token blocks), per-tile unions, per-row largest bias.
+static size_t round256(size_t x) { return (x + 255) & ~(size_t)255; }
+
 size_t prefill_workspace(const DashPrefillArgs& a, int64_t n_rows) {
   PrefillPlan p{};
   plan_geometry(a, n_rows, p);
   const int nih = a.routes.n_index_heads > 0 ? a.routes.n_index_heads : 1;
-  size_t lists = (size_t)nih * n_rows * a.routes.K * 4;
-  lists = (lists + 255) & ~(size_t)255;
+  const size_t lists = round256((size_t)nih * n_rows * a.routes.K * 4);
+  const size_t blists = a.block_size == 32 ? 2 * lists : lists;
   size_t masks = (size_t)nih * a.seqs.n_seq * p.tiles_per_seq * p.nwords * 4;
-  return 2 * lists + ((masks + 255) & ~(size_t)255) + (size_t)nih * n_rows * 4;
+  return lists + blists + round256(masks) + (size_t)nih * n_rows * 4;
 }
 
 int launch_prefill(const DashPrefillArgs& a, int64_t n_rows, cudaStream_t st) {
@@ -784,25 +923,33 @@ int launch_prefill(const DashPrefillArgs& a, int64_t n_rows, cudaStream_t st) {
     return set_error(DASH_ERR_UNSUPPORTED, "too many blocks per sequence (%d > %d)", p.nblk_cap,
                      MAX_MASK_WORDS * 32);
   const int nih = a.routes.n_index_heads > 0 ? a.routes.n_index_heads : 1;
-  size_t lists = (size_t)nih * n_rows * a.routes.K * 4;
-  lists = (lists + 255) & ~(size_t)255;
+  const bool pair = a.block_size == 32;
+  const size_t lists = round256((size_t)nih * n_rows * a.routes.K * 4);
+  const size_t blists = pair ? 2 * lists : lists;
   uint8_t* ws = reinterpret_cast<uint8_t*>(a.workspace);
   int32_t* cidx = reinterpret_cast<int32_t*>(ws);
   float* cbias = reinterpret_cast<float*>(ws + lists);
-  uint32_t* tmask = reinterpret_cast<uint32_t*>(ws + 2 * lists);
+  uint32_t* tmask = reinterpret_cast<uint32_t*>(ws + lists + blists);
   size_t masks = (size_t)nih * a.seqs.n_seq * p.tiles_per_seq * p.nwords * 4;
   p.cidx = cidx;
   p.cbias = cbias;
   p.tmask = tmask;
-  float* rowmax = reinterpret_cast<float*>(ws + 2 * lists + ((masks + 255) & ~(size_t)255));
+  float* rowmax = reinterpret_cast<float*>(ws + lists + blists + round256(masks));
   p.rowmax = rowmax;
   {
     // every tile's union words are written (also with no routed lists)
     dim3 g1((unsigned)(a.seqs.n_seq * p.tiles_per_seq), nih);
     const int K = a.routes.K;
-    if (K <= 32) plan_kernel<1><<<g1, kPlanWarps * 32, 0, st>>>(a, p, cidx, cbias, tmask, rowmax);
-    else if (K <= 64) plan_kernel<2><<<g1, kPlanWarps * 32, 0, st>>>(a, p, cidx, cbias, tmask, rowmax);
-    else plan_kernel<kPlanMaxK / 32><<<g1, kPlanWarps * 32, 0, st>>>(a, p, cidx, cbias, tmask, rowmax);
+    auto plan = [&](auto kern) { kern<<<g1, kPlanWarps * 32, 0, st>>>(a, p, cidx, cbias, tmask, rowmax); };
+    if (pair) {
+      if (K <= 32) plan(plan_kernel<1, true>);
+      else if (K <= 64) plan(plan_kernel<2, true>);
+      else plan(plan_kernel<kPlanMaxK / 32, true>);
+    } else {
+      if (K <= 32) plan(plan_kernel<1, false>);
+      else if (K <= 64) plan(plan_kernel<2, false>);
+      else plan(plan_kernel<kPlanMaxK / 32, false>);
+    }
     count_launch();
     int rc = check_launch("plan_kernel");
     if (rc) return rc;
@@ -827,9 +974,15 @@ int launch_prefill(const DashPrefillArgs& a, int64_t n_rows, cudaStream_t st) {
     return DASH_OK;
   };
   if (a.kv.dtype == DASH_DTYPE_BF16) {
-    rc = p.paged ? launch(prefill_kernel<__nv_bfloat16, true>) : launch(prefill_kernel<__nv_bfloat16, false>);
+    if (pair)
+      rc = p.paged ? launch(prefill_kernel<__nv_bfloat16, true, true>) : launch(prefill_kernel<__nv_bfloat16, false, true>);
+    else
+      rc = p.paged ? launch(prefill_kernel<__nv_bfloat16, true, false>) : launch(prefill_kernel<__nv_bfloat16, false, false>);
   } else {
-    rc = p.paged ? launch(prefill_kernel<__half, true>) : launch(prefill_kernel<__half, false>);
+    if (pair)
+      rc = p.paged ? launch(prefill_kernel<__half, true, true>) : launch(prefill_kernel<__half, false, true>);
+    else
+      rc = p.paged ? launch(prefill_kernel<__half, true, false>) : launch(prefill_kernel<__half, false, false>);
   }
   if (rc) return rc;
   count_launch();

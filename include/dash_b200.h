@@ -457,8 +457,10 @@ int dash_block_max(const DashBlockMaxArgs* args, dash_stream_t stream);
  *   local  (j > p - local_window): scale*<q,k_j>
  *   remote (block j/block_size routed for the token, j <= p - local_window):
  *          scale*<q,k_j> + bias of that slot
- * out = softmax(logits) @ V.  head_dim 128, block_size 64 or 128,
- * n_heads / n_kv_heads in {1,2,4,8,16}.  Workspace: dash_prefill_workspace_size. */
+ * out = softmax(logits) @ V.  head_dim 128,
+ * n_heads / n_kv_heads in {1,2,4,8,16}; block_size 32 (two blocks per 64-key
+ * tile; paged: 32-token pages) or a multiple of 64 up to 256.  Workspace:
+ * dash_prefill_workspace_size. */
 typedef struct {
   DashSeqs seqs;
   DashKV kv;
@@ -498,6 +500,9 @@ typedef struct {
   size_t workspace_bytes;
   DashDeviceError* device_error;
 } DashDecodeArgs;
+/* Bytes of split scratch dash_decode_attn needs for these arguments; 0 when it
+ * needs none (one split) or when the arguments are malformed (dash_decode_attn
+ * then returns the status and dash_last_error says why). */
 size_t dash_decode_workspace_size(const DashDecodeArgs* args);
 int dash_decode_attn(const DashDecodeArgs* args, dash_stream_t stream);
 

@@ -1,9 +1,10 @@
 """Generate the golden vectors that pin the CPU oracle to the reference.
 
-Run in a container that has the reference checkout (default ``/root/reference``,
-override with ``DASH_REFERENCE``):
+Run in a container that has the reference checkout, naming it with
+``DASH_REFERENCE`` (no default path); optional arguments name the cases to
+regenerate (default: all):
 
-    python tests/golden/make_golden.py
+    DASH_REFERENCE=<checkout> python tests/golden/make_golden.py [case ...]
 
 It imports the reference's OWN PyTorch functions and runs them on seeded
 inputs built by ``oracle.dash_oracle.make_prefill_inputs`` (numpy PCG64, so the
@@ -43,7 +44,7 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 from oracle.dash_oracle import make_prefill_inputs  # noqa: E402
 
-REF = os.environ.get("DASH_REFERENCE", "/root/reference")
+REF = os.environ.get("DASH_REFERENCE", "")
 
 
 def sha(*arrays):
@@ -54,6 +55,8 @@ def sha(*arrays):
 
 
 def import_reference():
+    if not REF or not os.path.isdir(REF):
+        raise SystemExit("set DASH_REFERENCE to the reference checkout")
     import transformers.utils.import_utils as iu
     if not hasattr(iu, "is_torch_fx_available"):
         iu.is_torch_fx_available = lambda: False
@@ -196,7 +199,7 @@ def paged_router_case(name, seed):
     print(name, "saved")
 
 
-def triton_interp_case(da, md, name, seed):
+def triton_interp_case(da, md, name, seed, T=96, bs=16, lb=2, K=3):
     """Reference Triton kernels, interpreted on CPU, on tiny shapes."""
     import ananta_ref.sparse_gather_e2e_triton as e2e
     from sglang.srt.layers.attention.unlimited_dash_ops import attend_triton as at
@@ -204,7 +207,7 @@ def triton_interp_case(da, md, name, seed):
     # CPU-only interpreter run nothing is
     torch.cuda.is_current_stream_capturing = lambda: False
     rng = np.random.default_rng(seed)
-    B, H, T, D, bs, lb, K = 1, 2, 96, 128, 16, 2, 3
+    B, H, D = 1, 2, 128
     q = (rng.standard_normal((B, H, T, D)) * 0.5).astype(np.float32)
     k = (rng.standard_normal((B, H, T, D)) * 0.5).astype(np.float32)
     v = (rng.standard_normal((B, H, T, D)) * 0.5).astype(np.float32)
@@ -584,25 +587,43 @@ def backward_case(name, seed):
     print(name, "saved")
 
 
-def main():
+def main(names=None):
     da, md = import_reference()
     torch.set_num_threads(os.cpu_count())
-    # C1: BASELINE config 1 (fp32, B=1, 10 heads, S=1348, bs=64, window 4 blocks, k=8)
-    prefill_case(da, md, "c1_headcls", seed=0, B=1, H=10, S=1348, bs=64, lb=4, K=8, topm=8,
-                 stage0="head_cls", hc_std=0.0, n_pages=0, page_tokens=273, off_std=0.0,
-                 sample_rows=np.linspace(0, 1347, 48).astype(np.int64))
-    # small cases: learned head_cls, topm > K, page offsets; indexer stage-0
-    prefill_case(da, md, "small_headcls", seed=1, B=2, H=2, S=300, bs=16, lb=2, K=4, topm=6,
-                 stage0="head_cls", hc_std=1.0, n_pages=5, page_tokens=50, off_std=0.3)
-    prefill_case(da, md, "small_indexer", seed=2, B=1, H=2, S=400, bs=32, lb=2, K=5, topm=5,
-                 stage0="indexer", hc_std=0.0, n_pages=6, page_tokens=60, off_std=0.3)
-    decode_case(da, md, "decode_small", seed=3, B=4, H=2, S=1000, bs=64, lb=4, K=8, topm=8)
-    paged_router_case("paged_router", seed=4)
-    triton_interp_case(da, md, "triton_interp", seed=5)
-    page_aware_case("page_aware", seed=6)
-    frontend_case("frontend", seed=7)
-    backward_case("backward", seed=8)
+    cases = {
+        # C1: BASELINE config 1 (fp32, B=1, 10 heads, S=1348, bs=64, window 4 blocks, k=8)
+        "c1_headcls": lambda: prefill_case(
+            da, md, "c1_headcls", seed=0, B=1, H=10, S=1348, bs=64, lb=4, K=8, topm=8,
+            stage0="head_cls", hc_std=0.0, n_pages=0, page_tokens=273, off_std=0.0,
+            sample_rows=np.linspace(0, 1347, 48).astype(np.int64)),
+        # the checkpoint's own DASH settings (config.json: sparse_block_size 32,
+        # sparse_local_block 4, dash_topk_blocks 12) on the config-1 shape with
+        # page offsets
+        "c1_bs32": lambda: prefill_case(
+            da, md, "c1_bs32", seed=10, B=1, H=10, S=1348, bs=32, lb=4, K=12, topm=12,
+            stage0="head_cls", hc_std=0.0, n_pages=4, page_tokens=273, off_std=0.2,
+            sample_rows=np.linspace(0, 1347, 64).astype(np.int64)),
+        # small cases: learned head_cls, topm > K, page offsets; indexer stage-0
+        "small_headcls": lambda: prefill_case(
+            da, md, "small_headcls", seed=1, B=2, H=2, S=300, bs=16, lb=2, K=4, topm=6,
+            stage0="head_cls", hc_std=1.0, n_pages=5, page_tokens=50, off_std=0.3),
+        "small_indexer": lambda: prefill_case(
+            da, md, "small_indexer", seed=2, B=1, H=2, S=400, bs=32, lb=2, K=5, topm=5,
+            stage0="indexer", hc_std=0.0, n_pages=6, page_tokens=60, off_std=0.3),
+        "decode_small": lambda: decode_case(da, md, "decode_small", seed=3, B=4, H=2, S=1000,
+                                            bs=64, lb=4, K=8, topm=8),
+        "paged_router": lambda: paged_router_case("paged_router", seed=4),
+        "triton_interp": lambda: triton_interp_case(da, md, "triton_interp", seed=5),
+        # 32-token blocks (one page per block) with a 4-block window
+        "triton_interp_bs32": lambda: triton_interp_case(da, md, "triton_interp_bs32", seed=9,
+                                                         T=256, bs=32, lb=4, K=3),
+        "page_aware": lambda: page_aware_case("page_aware", seed=6),
+        "frontend": lambda: frontend_case("frontend", seed=7),
+        "backward": lambda: backward_case("backward", seed=8),
+    }
+    for n in (names or list(cases)):
+        cases[n]()
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1:])

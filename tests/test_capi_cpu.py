@@ -72,7 +72,9 @@ def _prefill_args(head_dim=128, block_size=64, heads=10, kv_heads=10, K=4):
 def test_prefill_rejects_unsupported_shapes():
     assert _call_status("dash_prefill_attn", _prefill_args(head_dim=64)) == L.DASH_ERR_UNSUPPORTED
     assert "head_dim" in L.last_error()
-    assert _call_status("dash_prefill_attn", _prefill_args(block_size=32)) == L.DASH_ERR_UNSUPPORTED
+    assert _call_status("dash_prefill_attn", _prefill_args(block_size=16)) == L.DASH_ERR_UNSUPPORTED
+    assert _call_status("dash_prefill_attn", _prefill_args(block_size=96)) == L.DASH_ERR_UNSUPPORTED
+    assert "32" in L.last_error()
     assert _call_status("dash_prefill_attn", _prefill_args(heads=12, kv_heads=8)) == L.DASH_ERR_INVALID
     assert _call_status("dash_prefill_attn", _prefill_args(heads=24, kv_heads=8)) == L.DASH_ERR_UNSUPPORTED
     assert _call_status("dash_prefill_attn", _prefill_args(K=300)) == L.DASH_ERR_UNSUPPORTED
@@ -110,6 +112,20 @@ def test_decode_workspace_and_validation():
     assert lib.dash_decode_workspace_size(C.byref(a)) == 0
     a.kv.dtype = L.DTYPE_F32
     assert _call_status("dash_decode_attn", a) == L.DASH_ERR_UNSUPPORTED
+    a.kv.dtype = L.DTYPE_BF16
+    # malformed calls are rejected before anything is sized, by the workspace
+    # query (0), the workspace entry point and the allocation-free one alike
+    for field, bad in (("block_size", 0), ("num_splits", -1), ("n_seq", -1)):
+        saved = getattr(a.seqs if field == "n_seq" else a, field)
+        setattr(a.seqs if field == "n_seq" else a, field, bad)
+        a.num_splits = -1 if field == "num_splits" else 0
+        assert lib.dash_decode_workspace_size(C.byref(a)) == 0, field
+        for fn in ("dash_decode_attn", "dash_decode_attn_noalloc"):
+            assert _call_status(fn, a) == L.DASH_ERR_INVALID, (fn, field, L.last_error())
+        setattr(a.seqs if field == "n_seq" else a, field, saved)
+    a.num_splits = 65
+    for fn in ("dash_decode_attn", "dash_decode_attn_noalloc"):
+        assert _call_status(fn, a) == L.DASH_ERR_UNSUPPORTED
 
 
 def test_kbar_validation():

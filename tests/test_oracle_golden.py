@@ -48,7 +48,7 @@ def near_tie_rows(scores, K):
     return np.isfinite(b) & (gap <= 4 * np.spacing(np.abs(a).astype(np.float32)))
 
 
-PREFILL = ["c1_headcls", "small_headcls", "small_indexer"]
+PREFILL = ["c1_headcls", "c1_bs32", "small_headcls", "small_indexer"]
 
 
 def regen_prefill(g):
@@ -176,9 +176,10 @@ def test_paged_router_matches_sglang_torch_path():
     np.testing.assert_allclose(ob, rb[:, :budget], atol=1e-4)
 
 
-def test_triton_kernels_semantics():
+@pytest.mark.parametrize("name", ["triton_interp", "triton_interp_bs32"])
+def test_triton_kernels_semantics(name):
     """The reference Triton kernels (interpreted) and the oracle agree."""
-    g = load("triton_interp")
+    g = load(name)
     q, k, v, idx, bias = g["q"], g["k"], g["v"], g["idx"], g["bias"]
     bs, lb = int(g["bs"]), int(g["lb"])
     scale = 1.0 / math.sqrt(128)

@@ -37,6 +37,72 @@ def test_c1_golden_e2e():
     assert_close_bf16(out.float().cpu().numpy()[:, :, rows], g["out_rows"])
 
 
+def test_checkpoint_block_size_golden():
+    """The checkpoint's DASH settings (block 32, window 4 blocks, K=12) on the
+    config-1 shape with page offsets: router + attention on the GPU against the
+    reference's own _infer_route_select routes and _forward_dense output."""
+    g = np.load(os.path.join(GOLD, "c1_bs32.npz"))
+    B, H, S, bs, lb, K = (int(g[x]) for x in ("B", "H", "S", "bs", "lb", "K"))
+    q, k, v, iq, ik = O.make_prefill_inputs(int(g["seed"]), B, H, S, 128, int(g["n_pages"]),
+                                            int(g["page_tokens"]), float(g["off_std"]))
+    out, idx, bias = MD.dash_prefill_forward(
+        torch.from_numpy(q).cuda().bfloat16(), torch.from_numpy(k).cuda().bfloat16(),
+        torch.from_numpy(v).cuda().bfloat16(), torch.from_numpy(iq).cuda(),
+        torch.from_numpy(ik).cuda(), block_size=bs, local_blocks=lb, K=K,
+        idx_scale=float(g["idx_scale"]), prior_floor=float(g["floor"]), sigma=float(g["sigma"]),
+        return_routes=True)
+    topi, valid = g["topi"], g["valid"]
+    ri = np.sort(np.where(valid, topi, np.iinfo(np.int32).max), -1)
+    ri = np.where(ri == np.iinfo(np.int32).max, -1, ri).astype(np.int32)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    rows = g["rows"]
+    assert_close_bf16(out.float().cpu().numpy()[:, :, rows], g["out_rows"])
+
+
+@pytest.mark.parametrize("name", ["triton_interp", "triton_interp_bs32"])
+def test_reference_triton_golden(name):
+    """The reference's Triton kernels (interpreted on the CPU, fp32) against the
+    B200 kernels on the same inputs: e2e contiguous, paged prefill, decode.
+    The 16-token-block golden exercises decode only (the tensor-core prefill
+    takes blocks of 32 tokens or multiples of 64; it refuses 16)."""
+    g = np.load(os.path.join(GOLD, name + ".npz"))
+    q, k, v, idx, bias = g["q"], g["k"], g["v"], g["idx"], g["bias"]
+    bs, lb = int(g["bs"]), int(g["lb"])
+    B, H, T, D = q.shape
+    prefill = bs == 32 or bs % 64 == 0
+    bf = lambda x: torch.from_numpy(np.ascontiguousarray(x)).cuda().bfloat16()   # noqa: E731
+    if prefill:
+        out = triton_gather_attention_e2e(bf(q), bf(k), bf(v),
+                                          torch.from_numpy(idx).cuda()[:, None],
+                                          torch.from_numpy(bias).cuda(),
+                                          torch.arange(T, device="cuda")[None], None, bs,
+                                          1.0 / math.sqrt(D), lb * bs)
+        assert_close_bf16(out.float().cpu().numpy(), g["out_e2e"])
+    bt = g["block_table"]
+    P = int(bt.max()) + 1
+    kc = np.zeros((P, bs, H, D), np.float32)
+    vc = np.zeros_like(kc)
+    for b, pg in enumerate(bt[0]):
+        kc[pg] = k[0, :, b * bs:(b + 1) * bs].transpose(1, 0, 2)
+        vc[pg] = v[0, :, b * bs:(b + 1) * bs].transpose(1, 0, 2)
+    qp = q[0].transpose(1, 0, 2)
+    ti = torch.from_numpy(idx[0]).cuda()[None].expand(H, -1, -1)
+    tb = torch.from_numpy(bias[0]).cuda()[None].expand(H, -1, -1)
+    i32 = lambda x: torch.tensor(x, dtype=torch.int32, device="cuda")        # noqa: E731
+    if prefill:
+        outp = torch.zeros(T, H, D, dtype=torch.bfloat16, device="cuda")
+        dash_sparse_attn(bf(qp), bf(kc), bf(vc), ti, tb, torch.from_numpy(bt).cuda(),
+                         i32([0, T]), i32([T]), i32([0]), T, H, 1.0 / math.sqrt(D), outp,
+                         local_blocks=lb, sparse_block_size=bs)
+        assert_close_bf16(outp.float().cpu().numpy(), g["out_paged"])
+    from ananta_ocr_b200.unlimited_dash_ops.attend_triton import dash_sparse_attn_decode
+    outd = torch.zeros(1, H, D, dtype=torch.bfloat16, device="cuda")
+    dash_sparse_attn_decode(bf(qp[-1:]), bf(kc), bf(vc), ti[:, -1:], tb[:, -1:],
+                            torch.from_numpy(bt).cuda(), i32([T]), H, 1.0 / math.sqrt(D), outd, 1,
+                            local_blocks=lb, sparse_block_size=bs)
+    assert_close_bf16(outd.float().cpu().numpy(), g["out_decode"])
+
+
 def test_e2e_declines_like_reference():
     x = torch.zeros(1, 2, 64, 128, device="cuda", dtype=torch.bfloat16)
     bi = torch.zeros(1, 1, 64, 2, dtype=torch.int32, device="cuda")
@@ -55,6 +121,12 @@ CASES = [
     (1, 2, 2, 100, 64, 256, 4),       # window longer than the sequence
     (1, 8, 1, 600, 64, 128, 5),       # G=8
     (2, 3, 3, 777, 64, 192, 6),       # window not a multiple of ... 64-aligned but 3 blocks
+    # 32-token blocks (the checkpoint's sparse_block_size): two blocks per key tile
+    (2, 2, 2, 700, 32, 128, 12),
+    (1, 4, 2, 1000, 32, 128, 16),     # GQA G=2
+    (1, 1, 1, 129, 32, 128, 3),       # tiny, ragged tail
+    (1, 8, 1, 600, 32, 96, 5),        # G=8, window of 3 blocks
+    (2, 3, 3, 777, 32, 100, 12),      # window ends inside a block
 ]
 
 
@@ -121,7 +193,7 @@ def test_multi_index_head_and_packing():
         assert_close_bf16(got[:, hs], ref)
 
 
-@pytest.mark.parametrize("bs,lb", [(64, 4), (128, 2)])
+@pytest.mark.parametrize("bs,lb", [(64, 4), (128, 2), (32, 4), (32, 1)])
 def test_paged_prefill_with_prefix(bs, lb):
     rng = np.random.default_rng(bs)
     D, H, Hkv, K = 128, 4, 2, 4

@@ -16,6 +16,7 @@ import torch
 from ananta_ocr_b200 import _lib as L
 from ananta_ocr_b200 import ops
 from dash_testutil import assert_close_bf16
+from oracle import dash_oracle as O
 
 pytestmark = pytest.mark.gpu
 
@@ -53,16 +54,30 @@ def _problem():
     return q, kc, vc, bt, seq, idx, bias, H, bs, lb * bs
 
 
-def test_noalloc_decode_matches_workspace_entry_point():
+def _oracle(q, kc, vc, bt, sl, idx, bias, bs, lw):
+    """The CPU restatement of the reference's paged decode on the same inputs."""
+    R = q.shape[0]
+    return O.attend_paged(q.float().cpu().numpy(), kc.float().cpu().numpy(),
+                          vc.float().cpu().numpy(), idx.cpu().numpy(), bias.cpu().numpy(),
+                          bt.cpu().numpy(), np.arange(R), sl.cpu().numpy().astype(np.int64) - 1,
+                          bs, lw, 1.0 / math.sqrt(128))
+
+
+@pytest.mark.parametrize("splits", [4, 0])
+def test_noalloc_decode_matches_workspace_entry_point(splits):
+    """Two allocation-free calls in a row (the second sees the first one's
+    leftovers in the shared scratch) against the workspace entry point and the
+    oracle; splits 0 lets the library choose the split count."""
     lib = L.load()
     stream = L.current_stream()
     q, kc, vc, bt, sl, idx, bias, H, bs, lw = _problem()
-    splits = 4
     ref = torch.empty_like(q)
     a = _decode_args(q, kc, vc, bt, sl, idx, bias, ref, H, H, bs, lw, splits)
     need = lib.dash_decode_workspace_size(C.byref(a))
-    assert 0 < need <= lib.dash_noalloc_scratch_bytes()
-    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    assert need <= lib.dash_noalloc_scratch_bytes()
+    if splits:
+        assert need > 0
+    ws = torch.empty(max(need, 256), dtype=torch.uint8, device="cuda")
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     assert lib.dash_decode_attn(C.byref(a), stream) == L.DASH_OK, L.last_error()
     outs = []
@@ -72,8 +87,11 @@ def test_noalloc_decode_matches_workspace_entry_point():
         assert lib.dash_decode_attn_noalloc(C.byref(b), stream) == L.DASH_OK, L.last_error()
         outs.append(out)
     torch.cuda.synchronize()
+    want = _oracle(q, kc, vc, bt, sl, idx, bias, bs, lw)
+    assert_close_bf16(ref.float().cpu().numpy(), want)
     for out in outs:
         assert_close_bf16(out.float().cpu().numpy(), ref.float().cpu().numpy())
+        assert_close_bf16(out.float().cpu().numpy(), want)
 
 
 def test_noalloc_rejects_requests_beyond_the_fixed_scratch():
