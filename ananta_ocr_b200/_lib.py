@@ -192,11 +192,18 @@ class DashEntmaxArgs(C.Structure):
                 ("n", _i32), ("pad0", _i32)]
 
 
+class DashServingPlanArgs(C.Structure):
+    _fields_ = [("block_table", _p), ("bt_stride", _i64), ("seq_lens", _p), ("context_lens", _p),
+                ("cu_seqlens_q", _p), ("n_req", _i32), ("block_size", _i32), ("width", _i32),
+                ("mode", _i32), ("bt_width", _i32), ("pad0", _i32), ("pages", _p), ("ntok", _p),
+                ("row2req", _p)]
+
+
 ABI_ORDER = [DashSeqs, DashKV, DashRoutes, DashQO, DashKbarArgs, DashRouteArgs,
              DashBlockMaxArgs, DashPrefillArgs, DashDecodeArgs, DashDeviceError,
              DashPageIdsArgs, DashPageStateArgs, DashPageAllowArgs, DashPageDecodeArgs,
              DashBlockAnyArgs, DashPageBlocksArgs, DashIndexProjArgs, DashRopeKVArgs,
-             DashAttnBwdArgs, DashEntmaxArgs]
+             DashAttnBwdArgs, DashEntmaxArgs, DashServingPlanArgs]
 
 # every function the header declares
 EXPORTS = [
@@ -207,6 +214,7 @@ EXPORTS = [
     "dash_page_ids", "dash_page_state_step", "dash_page_allow", "dash_page_decode_query",
     "dash_block_any", "dash_page_blocks", "dash_index_proj", "dash_rope_kv_write",
     "dash_attn_bwd", "dash_attn_bwd_flag_words", "dash_entmax15_fwd", "dash_entmax15_bwd",
+    "dash_serving_plan",
 ]
 
 
@@ -246,6 +254,7 @@ def load(path: str = LIB_PATH):
         ("dash_attn_bwd", [C.POINTER(DashAttnBwdArgs), _p]),
         ("dash_entmax15_fwd", [C.POINTER(DashEntmaxArgs), _p]),
         ("dash_entmax15_bwd", [C.POINTER(DashEntmaxArgs), _p]),
+        ("dash_serving_plan", [C.POINTER(DashServingPlanArgs), _p]),
     ]:
         f = getattr(L, name)
         f.argtypes = args

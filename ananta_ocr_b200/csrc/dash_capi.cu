@@ -131,7 +131,7 @@ int dash_count_launches(int reset) {
 }
 
 int dash_abi_sizes(int64_t* out, int n) {
-  const int64_t s[20] = {(int64_t)sizeof(DashSeqs),           (int64_t)sizeof(DashKV),
+  const int64_t s[21] = {(int64_t)sizeof(DashSeqs),           (int64_t)sizeof(DashKV),
                          (int64_t)sizeof(DashRoutes),         (int64_t)sizeof(DashQO),
                          (int64_t)sizeof(DashKbarArgs),       (int64_t)sizeof(DashRouteArgs),
                          (int64_t)sizeof(DashBlockMaxArgs),   (int64_t)sizeof(DashPrefillArgs),
@@ -140,9 +140,10 @@ int dash_abi_sizes(int64_t* out, int n) {
                          (int64_t)sizeof(DashPageAllowArgs),  (int64_t)sizeof(DashPageDecodeArgs),
                          (int64_t)sizeof(DashBlockAnyArgs),   (int64_t)sizeof(DashPageBlocksArgs),
                          (int64_t)sizeof(DashIndexProjArgs),  (int64_t)sizeof(DashRopeKVArgs),
-                         (int64_t)sizeof(DashAttnBwdArgs),    (int64_t)sizeof(DashEntmaxArgs)};
-  for (int i = 0; i < n && i < 20; ++i) out[i] = s[i];
-  return 20;
+                         (int64_t)sizeof(DashAttnBwdArgs),    (int64_t)sizeof(DashEntmaxArgs),
+                         (int64_t)sizeof(DashServingPlanArgs)};
+  for (int i = 0; i < n && i < 21; ++i) out[i] = s[i];
+  return 21;
 }
 
 int dash_kbar_pool(const DashKbarArgs* a, dash_stream_t stream) {
@@ -426,6 +427,24 @@ static int check_entmax(const DashEntmaxArgs* a, bool bwd) {
   if (a->rows > 0 && a->n > 0 && (bwd ? (!a->y || !a->dy || !a->dx) : (!a->x || !a->y)))
     return set_error(DASH_ERR_INVALID, "null pointer");
   return DASH_OK;
+}
+
+int dash_serving_plan(const DashServingPlanArgs* a, dash_stream_t stream) {
+  if (!a) return set_error(DASH_ERR_INVALID, "null args");
+  if (a->n_req < 0) return set_error(DASH_ERR_INVALID, "n_req < 0");
+  if (a->n_req == 0) return DASH_OK;
+  if (!a->seq_lens) return set_error(DASH_ERR_INVALID, "null seq_lens");
+  if (a->pages || a->ntok) {
+    if (!a->pages || !a->ntok || !a->block_table)
+      return set_error(DASH_ERR_INVALID, "a page plan needs pages, ntok and block_table");
+    if (a->block_size <= 0 || a->width < 0 || a->bt_width <= 0 || a->bt_stride < a->bt_width)
+      return set_error(DASH_ERR_INVALID, "block_size and bt_width must be > 0, width >= 0, "
+                       "bt_stride >= bt_width");
+    if (a->mode != 0 && a->mode != 1) return set_error(DASH_ERR_INVALID, "mode must be 0 or 1");
+    if (a->mode == 0 && !a->context_lens) return set_error(DASH_ERR_INVALID, "mode 0 needs context_lens");
+  }
+  if (a->row2req && !a->cu_seqlens_q) return set_error(DASH_ERR_INVALID, "row2req needs cu_seqlens_q");
+  return launch_serving_plan(*a, (cudaStream_t)stream);
 }
 
 int dash_entmax15_fwd(const DashEntmaxArgs* a, dash_stream_t stream) {

@@ -7,13 +7,16 @@ of the same package (dash_router.py:131-174, DashRouterMath.route_and_select):
 top-``budget`` blocks by score (ties to the lowest id), entmax prior over the
 top-``topm`` candidates, centred log-prior bias; ids packed ascending with -1 /
 0.0 in unused slots.  The planning helpers (``kbar_tail_plan``,
-``kbar_all_plan``, ``prefill_row2req``) are the same small torch index
-computations as route_triton.py:576-620, 682-703.
+``kbar_all_plan``, ``prefill_row2req``) keep the reference's names and
+results (route_triton.py:576-620, 682-703) and run as one library kernel
+(``dash_serving_plan``) with the sizes given by the caller, so they need no
+host sync.
 """
 from __future__ import annotations
 
 import torch
 
+from .. import _lib as L
 from .. import ops
 
 SCORE_NEG = -1.0e9
@@ -22,60 +25,86 @@ ACT_CLAMP = 1.0e4
 SCAN_TILE = 128
 
 
+def _plan_buffers(n_entries, device, out):
+    if out is not None and out[0].shape[0] >= n_entries and out[1].shape[0] >= n_entries:
+        return out[0][:n_entries], out[1][:n_entries]
+    return (torch.empty(n_entries, dtype=torch.int64, device=device),
+            torch.empty(n_entries, dtype=torch.int32, device=device))
+
+
+def _i32(t, device):
+    return t.to(device=device, dtype=torch.int32).contiguous()
+
+
+def _serving_plan(*, block_table, seq_lens, block_size, width, mode, bt_width, context_lens=None,
+                  pages=None, ntok=None, cu_seqlens_q=None, row2req=None):
+    """One ``dash_serving_plan`` launch on the current stream."""
+    device = seq_lens.device
+    a = L.DashServingPlanArgs()
+    keep = []
+    if pages is not None:
+        bt = block_table if block_table.dtype == torch.int32 else block_table.to(torch.int32)
+        if bt.stride(-1) != 1:
+            bt = bt.contiguous()
+        keep.append(bt)
+        a.block_table, a.bt_stride = bt.data_ptr(), bt.stride(0)
+        a.pages, a.ntok = pages.data_ptr(), ntok.data_ptr()
+    sl = _i32(seq_lens, device)
+    keep.append(sl)
+    a.seq_lens = sl.data_ptr()
+    if context_lens is not None:
+        ctx = _i32(context_lens, device)
+        keep.append(ctx)
+        a.context_lens = ctx.data_ptr()
+    if row2req is not None:
+        cu = _i32(cu_seqlens_q, device)
+        keep.append(cu)
+        a.cu_seqlens_q, a.row2req = cu.data_ptr(), row2req.data_ptr()
+    a.n_req, a.block_size, a.width, a.mode = int(sl.shape[0]), int(block_size), int(width), int(mode)
+    a.bt_width = int(bt_width)
+    L.call("dash_serving_plan", a)
+    del keep
+
+
 @torch.no_grad()
 def kbar_all_plan(*, block_table, seq_lens, context_lens, block_size: int, max_block: int,
                   max_query_len: int, device, out=None):
-    """Pages changed by a prefill step: the boundary page plus the pages of the
-    query span (route_triton.py:576-601)."""
-    sl = seq_lens.to(device=device, dtype=torch.int64)
-    ctx = context_lens.to(device=device, dtype=torch.int64)
-    W = min(int(max_block), int(block_table.shape[1]))
-    width = min(W, -(-int(max_query_len) // int(block_size)) + 1)
-    p0 = ctx // block_size
-    blk = p0[:, None] + torch.arange(width, device=device)[None, :]
-    pages = block_table[:, :W].to(torch.int64).gather(1, blk.clamp(max=W - 1))
-    tok = (sl[:, None] - blk * block_size).clamp(0, block_size)
-    n = sl.shape[0] * width
-    if out is not None:
-        pages_buf, tok_buf = out
-        pages_buf[:n].copy_(pages.reshape(-1))
-        tok_buf[:n].copy_(tok.reshape(-1).to(torch.int32))
-        return pages_buf[:n], tok_buf[:n]
-    return pages.reshape(-1).contiguous(), tok.reshape(-1).to(torch.int32).contiguous()
+    """Pages a prefill step changed, per request: the block holding its first
+    new token and the following ones up to the longest query span
+    (route_triton.py:576-601), with their live token counts; one device launch.
+    Returns flat (pages int64, ntok int32) of ``n_req * width`` entries."""
+    bt_width = min(int(max_block), int(block_table.shape[1]))
+    width = min(bt_width, -(-int(max_query_len) // int(block_size)) + 1)
+    pages, ntok = _plan_buffers(int(seq_lens.shape[0]) * width, device, out)
+    _serving_plan(block_table=block_table, seq_lens=seq_lens.to(device), block_size=block_size,
+                  width=width, mode=0, bt_width=bt_width, context_lens=context_lens,
+                  pages=pages, ntok=ntok)
+    return pages, ntok
 
 
 @torch.no_grad()
 def prefill_row2req(*, cu_seqlens_q, device, out=None, total_q=None):
-    """Query row -> request index (route_triton.py:605-620)."""
-    cu = cu_seqlens_q.to(device=device, dtype=torch.int64)
-    q_lens = cu[1:] - cu[:-1]
-    r = torch.arange(q_lens.numel(), device=device)
-    row2req = torch.repeat_interleave(r, q_lens).to(torch.int32)
-    if out is not None:
-        out[:row2req.shape[0]].copy_(row2req)
-        return out[:row2req.shape[0]]
-    return row2req.contiguous()
+    """Request index of every query row (route_triton.py:605-620), filled on the
+    device.  ``total_q`` (the row count) avoids reading ``cu_seqlens_q[-1]``
+    back to the host; without it that one value is read."""
+    cu = cu_seqlens_q.to(device)
+    n = int(total_q) if total_q is not None else int(cu[-1])
+    row2req = out[:n] if out is not None else torch.empty(n, dtype=torch.int32, device=device)
+    _serving_plan(block_table=None, seq_lens=cu[1:] - cu[:-1], block_size=1, width=0, mode=1,
+                  bt_width=1, cu_seqlens_q=cu, row2req=row2req)
+    return row2req
 
 
 @torch.no_grad()
 def kbar_tail_plan(*, block_table, seq_lens, block_size: int, tail_pages: int, device, out=None):
-    """Mutable tail pages of every request and their live token counts
-    (route_triton.py:682-703)."""
-    sl = seq_lens.to(device=device, dtype=torch.int64)
-    nb = (sl + block_size - 1) // block_size
-    last = (nb - 1).clamp(min=0)
-    offs = torch.arange(tail_pages, device=device)
-    blk = (last[:, None] - offs[None, :]).clamp(min=0)
-    w = int(block_table.shape[1])
-    pages = block_table[:, :w].to(torch.int64).gather(1, blk.clamp(max=w - 1))
-    tok = (sl[:, None] - blk * block_size).clamp(0, block_size)
-    n = pages.numel()
-    if out is None or out[0].shape[0] < n:
-        return pages.reshape(-1).contiguous(), tok.reshape(-1).to(torch.int32).contiguous()
-    p_buf, t_buf = out[0][:n], out[1][:n]
-    p_buf.copy_(pages.reshape(-1))
-    t_buf.copy_(tok.reshape(-1))
-    return p_buf, t_buf
+    """The ``tail_pages`` newest blocks of every request (the ones a decode step
+    can still change) and their live token counts (route_triton.py:682-703);
+    one device launch.  Returns flat (pages int64, ntok int32)."""
+    pages, ntok = _plan_buffers(int(seq_lens.shape[0]) * int(tail_pages), device, out)
+    _serving_plan(block_table=block_table, seq_lens=seq_lens.to(device), block_size=block_size,
+                  width=int(tail_pages), mode=1, bt_width=int(block_table.shape[1]),
+                  pages=pages, ntok=ntok)
+    return pages, ntok
 
 
 @torch.no_grad()

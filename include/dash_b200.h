@@ -479,6 +479,31 @@ size_t dash_prefill_workspace_size(const DashPrefillArgs* args);
 int dash_prefill_attn(const DashPrefillArgs* args, dash_stream_t stream);
 
 /* ---------------------------------------------------------------------- */
+/* Serving-step plans, computed on the device in one launch (no host sync).
+ * Replaces: WHL route_triton.py:576-601 (kbar_all_plan), :605-620
+ *           (prefill_row2req), :682-703 (kbar_tail_plan).
+ * pages/ntok (optional, [n_req * width]): request r owns entries
+ *   [r*width, (r+1)*width); entry j names block
+ *     mode 0 (blocks a prefill chunk wrote): b = context_lens[r]/block_size + j
+ *     mode 1 (mutable tail, newest first):   b = max(last_r - j, 0),
+ *            last_r = max(ceil(seq_lens[r]/block_size) - 1, 0)
+ *   pages[e] = block_table[r, min(b, bt_width - 1)],
+ *   ntok[e]  = clamp(seq_lens[r] - b*block_size, 0, block_size)
+ *   (an entry with ntok 0 is skipped by dash_kbar_pool).
+ * row2req (optional, [cu_seqlens_q[n_req]]): rows [cu[r], cu[r+1]) get r.   */
+typedef struct {
+  const int32_t* block_table; int64_t bt_stride;
+  const int32_t* seq_lens;      /* [n_req] */
+  const int32_t* context_lens;  /* [n_req], mode 0 */
+  const int32_t* cu_seqlens_q;  /* [n_req + 1], for row2req */
+  int32_t n_req, block_size, width, mode, bt_width, pad0;
+  int64_t* pages;
+  int32_t* ntok;
+  int32_t* row2req;
+} DashServingPlanArgs;
+int dash_serving_plan(const DashServingPlanArgs* args, dash_stream_t stream);
+
+/* ---------------------------------------------------------------------- */
 /* Decode gather attention over a block-paged (or contiguous) KV cache.
  * Replaces: WHL attend_triton.py:600-715 (dash_sparse_attn_decode) with the
  *           split-K merge of WHL common.py:40-89, and the decode attend of
@@ -670,7 +695,8 @@ int dash_count_launches(int reset);          /* kernels launched by this library
  * DashQO, DashKbarArgs, DashRouteArgs, DashBlockMaxArgs, DashPrefillArgs,
  * DashDecodeArgs, DashDeviceError, DashPageIdsArgs, DashPageStateArgs,
  * DashPageAllowArgs, DashPageDecodeArgs, DashBlockAnyArgs, DashPageBlocksArgs,
- * DashIndexProjArgs, DashRopeKVArgs, DashAttnBwdArgs, DashEntmaxArgs.  Lets a binding
+ * DashIndexProjArgs, DashRopeKVArgs, DashAttnBwdArgs, DashEntmaxArgs,
+ * DashServingPlanArgs.  Lets a binding
  * verify its struct layouts; returns the number of sizes available. */
 int dash_abi_sizes(int64_t* out, int n);
 /* Self-test of the bounded waits every kernel uses (no reference counterpart):

@@ -355,6 +355,55 @@ def local_union(allow, seq_lens, max_block, block_size, local_blocks):
 
 
 # ---------------------------------------------------------------------------
+# serving-step plans (which k-bar pages to refresh; row -> request)
+# ---------------------------------------------------------------------------
+def _plan_entry(bt_row, seq_len, blk, block_size, bt_width):
+    page = int(bt_row[min(blk, bt_width - 1)])
+    live = min(max(int(seq_len) - blk * block_size, 0), block_size)
+    return page, live
+
+
+def plan_prefill_pages(block_table, seq_lens, context_lens, block_size, max_block, max_query_len):
+    """WHL route_triton.py:576-601 (kbar_all_plan): per request, ``width``
+    consecutive blocks from the one holding its first new token; a block past
+    the usable table width names the last column (with 0 live tokens)."""
+    R = len(seq_lens)
+    bt_width = min(int(max_block), block_table.shape[1])
+    width = min(bt_width, -(-int(max_query_len) // block_size) + 1)
+    pages = np.zeros(R * width, np.int64)
+    ntok = np.zeros(R * width, np.int32)
+    for r in range(R):
+        first = int(context_lens[r]) // block_size
+        for j in range(width):
+            pages[r * width + j], ntok[r * width + j] = _plan_entry(
+                block_table[r], seq_lens[r], first + j, block_size, bt_width)
+    return pages, ntok
+
+
+def plan_tail_pages(block_table, seq_lens, block_size, tail_pages):
+    """WHL route_triton.py:682-703 (kbar_tail_plan): the ``tail_pages`` newest
+    blocks of every request, newest first, clamped at block 0."""
+    R = len(seq_lens)
+    pages = np.zeros(R * tail_pages, np.int64)
+    ntok = np.zeros(R * tail_pages, np.int32)
+    for r in range(R):
+        n_blocks = -(-int(seq_lens[r]) // block_size)
+        last = max(n_blocks - 1, 0)
+        for j in range(tail_pages):
+            pages[r * tail_pages + j], ntok[r * tail_pages + j] = _plan_entry(
+                block_table[r], seq_lens[r], max(last - j, 0), block_size, block_table.shape[1])
+    return pages, ntok
+
+
+def rows_to_requests(cu_seqlens_q):
+    """WHL route_triton.py:605-620 (prefill_row2req): request of every query row."""
+    out = []
+    for r in range(len(cu_seqlens_q) - 1):
+        out += [r] * int(cu_seqlens_q[r + 1] - cu_seqlens_q[r])
+    return np.asarray(out, np.int32)
+
+
+# ---------------------------------------------------------------------------
 # synthetic documents
 # ---------------------------------------------------------------------------
 def make_document_ids(rng, length, *, n_pages, page_tokens=PER_PAGE_IMAGE_TOKENS,

@@ -253,6 +253,40 @@ def triton_interp_case(da, md, name, seed, T=96, bs=16, lb=2, K=3):
     print(name, "saved")
 
 
+def serving_plan_case(name, seed):
+    """The serving step's planning helpers of the sglang wheel (route_triton.py:
+    kbar_all_plan, prefill_row2req, kbar_tail_plan) on seeded block tables,
+    including empty requests, prefixes not on a block boundary and blocks past
+    the table width."""
+    from sglang.srt.layers.attention.unlimited_dash_ops import route_triton as rt
+    rng = np.random.default_rng(seed)
+    res = {}
+    for bs in (16, 32, 64):
+        R = 7
+        seq = rng.integers(0, 700, R)
+        seq[2] = 0
+        ctx = np.minimum(seq, rng.integers(0, 400, R))
+        ctx[3] = seq[3]
+        W = int(-(-seq.max() // bs)) + 2
+        bt = rng.integers(0, 5000, (R, W)).astype(np.int32)
+        q_lens = seq - ctx
+        cu = np.concatenate([[0], np.cumsum(q_lens)]).astype(np.int32)
+        for mb in (W, W - 3):
+            p, t = rt.kbar_all_plan(block_table=torch.tensor(bt), seq_lens=torch.tensor(seq),
+                                    context_lens=torch.tensor(ctx), block_size=bs, max_block=mb,
+                                    max_query_len=int(q_lens.max()), device="cpu")
+            res[f"all_{bs}_{mb == W}_pages"], res[f"all_{bs}_{mb == W}_ntok"] = p.numpy(), t.numpy()
+        for tp in (1, 3):
+            p, t = rt.kbar_tail_plan(block_table=torch.tensor(bt), seq_lens=torch.tensor(seq),
+                                     block_size=bs, tail_pages=tp, device="cpu")
+            res[f"tail_{bs}_{tp}_pages"], res[f"tail_{bs}_{tp}_ntok"] = p.numpy(), t.numpy()
+        res[f"row2req_{bs}"] = rt.prefill_row2req(cu_seqlens_q=torch.tensor(cu),
+                                                  device="cpu").numpy()
+        res[f"seq_{bs}"], res[f"ctx_{bs}"], res[f"bt_{bs}"], res[f"cu_{bs}"] = seq, ctx, bt, cu
+    np.savez_compressed(os.path.join(HERE, name + ".npz"), **res)
+    print(name, "saved")
+
+
 def page_aware_case(name, seed):
     """Page-aware candidate domain: the indexer's id builders and candidate mask
     (_sparse_base_impl.py), _dash_block_cand (modeling_deepseekv2.py), the
@@ -618,6 +652,7 @@ def main(names=None):
         "triton_interp_bs32": lambda: triton_interp_case(da, md, "triton_interp_bs32", seed=9,
                                                          T=256, bs=32, lb=4, K=3),
         "page_aware": lambda: page_aware_case("page_aware", seed=6),
+        "serving_plan": lambda: serving_plan_case("serving_plan", seed=11),
         "frontend": lambda: frontend_case("frontend", seed=7),
         "backward": lambda: backward_case("backward", seed=8),
     }

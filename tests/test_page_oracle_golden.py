@@ -110,3 +110,21 @@ def test_serving_trace_matches_reference():
             np.testing.assert_array_equal(lu, g["local_union"] != 0)
         for j, r in enumerate(rows):
             lens[r] = int(g["start_pos"][j]) + int(g["q_start"][j + 1] - g["q_start"][j])
+
+
+def test_serving_plans_match_reference_golden():
+    """kbar_all_plan / kbar_tail_plan / prefill_row2req restated in the oracle
+    against the sglang wheel's own outputs."""
+    g = np.load(os.path.join(GOLD, "serving_plan.npz"))
+    for bs in (16, 32, 64):
+        seq, ctx, bt, cu = g[f"seq_{bs}"], g[f"ctx_{bs}"], g[f"bt_{bs}"], g[f"cu_{bs}"]
+        W = bt.shape[1]
+        for full, mb in ((True, W), (False, W - 3)):
+            p, t = P.plan_prefill_pages(bt, seq, ctx, bs, mb, int((seq - ctx).max()))
+            np.testing.assert_array_equal(p, g[f"all_{bs}_{full}_pages"])
+            np.testing.assert_array_equal(t, g[f"all_{bs}_{full}_ntok"])
+        for tp in (1, 3):
+            p, t = P.plan_tail_pages(bt, seq, bs, tp)
+            np.testing.assert_array_equal(p, g[f"tail_{bs}_{tp}_pages"])
+            np.testing.assert_array_equal(t, g[f"tail_{bs}_{tp}_ntok"])
+        np.testing.assert_array_equal(P.rows_to_requests(cu), g[f"row2req_{bs}"])

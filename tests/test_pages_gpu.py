@@ -377,3 +377,47 @@ def test_cpu_tensors_raise():
     with pytest.raises(RuntimeError):
         pages.page_ids(torch.zeros(1, 10, dtype=torch.int64), image_token_id=IMG,
                        page_token_id=PG, per_page=1, key_length=10)
+
+
+def test_serving_plans_match_reference_golden_and_oracle():
+    """The serving-plan kernel behind kbar_all_plan / kbar_tail_plan /
+    prefill_row2req against the sglang wheel's outputs, plus a larger random
+    case against the oracle; the caller's out buffers are filled in place."""
+    from ananta_ocr_b200.unlimited_dash_ops import route_triton as RT
+    g = np.load(os.path.join(GOLD, "serving_plan.npz"))
+    dev = torch.device("cuda")
+    for bs in (16, 32, 64):
+        seq, ctx, bt, cu = g[f"seq_{bs}"], g[f"ctx_{bs}"], g[f"bt_{bs}"], g[f"cu_{bs}"]
+        tbt, tsl, tctx = (torch.from_numpy(x).to(dev) for x in (bt, seq, ctx))
+        W = bt.shape[1]
+        for full, mb in ((True, W), (False, W - 3)):
+            p, t = RT.kbar_all_plan(block_table=tbt, seq_lens=tsl, context_lens=tctx, block_size=bs,
+                                    max_block=mb, max_query_len=int((seq - ctx).max()), device=dev)
+            np.testing.assert_array_equal(p.cpu().numpy(), g[f"all_{bs}_{full}_pages"])
+            np.testing.assert_array_equal(t.cpu().numpy(), g[f"all_{bs}_{full}_ntok"])
+        for tp in (1, 3):
+            buf = (torch.full((64,), -7, dtype=torch.int64, device=dev),
+                   torch.full((64,), -7, dtype=torch.int32, device=dev))
+            p, t = RT.kbar_tail_plan(block_table=tbt, seq_lens=tsl, block_size=bs, tail_pages=tp,
+                                     device=dev, out=buf)
+            assert p.data_ptr() == buf[0].data_ptr()
+            np.testing.assert_array_equal(p.cpu().numpy(), g[f"tail_{bs}_{tp}_pages"])
+            np.testing.assert_array_equal(t.cpu().numpy(), g[f"tail_{bs}_{tp}_ntok"])
+        r2r = RT.prefill_row2req(cu_seqlens_q=torch.from_numpy(cu).to(dev), device=dev,
+                                 total_q=int(cu[-1]))
+        np.testing.assert_array_equal(r2r.cpu().numpy(), g[f"row2req_{bs}"])
+    rng = np.random.default_rng(3)
+    R, bs = 300, 32
+    seq = rng.integers(0, 30000, R)
+    ctx = np.minimum(seq, rng.integers(0, 30000, R))
+    bt = rng.integers(0, 1 << 20, (R, 1000)).astype(np.int32)
+    cu = np.concatenate([[0], np.cumsum(seq - ctx)]).astype(np.int32)
+    p, t = RT.kbar_all_plan(block_table=torch.from_numpy(bt).to(dev),
+                            seq_lens=torch.from_numpy(seq).to(dev),
+                            context_lens=torch.from_numpy(ctx).to(dev), block_size=bs,
+                            max_block=1000, max_query_len=int((seq - ctx).max()), device=dev)
+    rp, rt_ = P.plan_prefill_pages(bt, seq, ctx, bs, 1000, int((seq - ctx).max()))
+    np.testing.assert_array_equal(p.cpu().numpy(), rp)
+    np.testing.assert_array_equal(t.cpu().numpy(), rt_)
+    r2r = RT.prefill_row2req(cu_seqlens_q=torch.from_numpy(cu).to(dev), device=dev)
+    np.testing.assert_array_equal(r2r.cpu().numpy(), P.rows_to_requests(cu))
