@@ -97,7 +97,13 @@ class DashPrefillArgs(C.Structure):
     _fields_ = [("seqs", DashSeqs), ("kv", DashKV), ("routes", DashRoutes), ("qo", DashQO),
                 ("seg_start", _p), ("scale", _f32), ("block_size", _i32),
                 ("local_window", _i32), ("pad0", _i32), ("workspace", _p),
-                ("workspace_bytes", C.c_size_t), ("device_error", _p)]
+                ("workspace_bytes", C.c_size_t), ("device_error", _p), ("out_peers", _p),
+                ("n_peers", _i32), ("pad1", _i32)]
+
+
+class DashPeerHandle(C.Structure):
+    # unsigned bytes: a c_char array field would read back as NUL-truncated bytes
+    _fields_ = [("handle", C.c_ubyte * 64), ("offset", _i64), ("alloc_bytes", _i64)]
 
 
 class DashDecodeArgs(C.Structure):
@@ -203,7 +209,7 @@ ABI_ORDER = [DashSeqs, DashKV, DashRoutes, DashQO, DashKbarArgs, DashRouteArgs,
              DashBlockMaxArgs, DashPrefillArgs, DashDecodeArgs, DashDeviceError,
              DashPageIdsArgs, DashPageStateArgs, DashPageAllowArgs, DashPageDecodeArgs,
              DashBlockAnyArgs, DashPageBlocksArgs, DashIndexProjArgs, DashRopeKVArgs,
-             DashAttnBwdArgs, DashEntmaxArgs, DashServingPlanArgs]
+             DashAttnBwdArgs, DashEntmaxArgs, DashServingPlanArgs, DashPeerHandle]
 
 # every function the header declares
 EXPORTS = [
@@ -214,7 +220,7 @@ EXPORTS = [
     "dash_page_ids", "dash_page_state_step", "dash_page_allow", "dash_page_decode_query",
     "dash_block_any", "dash_page_blocks", "dash_index_proj", "dash_rope_kv_write",
     "dash_attn_bwd", "dash_attn_bwd_flag_words", "dash_entmax15_fwd", "dash_entmax15_bwd",
-    "dash_serving_plan",
+    "dash_serving_plan", "dash_peer_export", "dash_peer_import", "dash_peer_close",
 ]
 
 
@@ -276,6 +282,12 @@ def load(path: str = LIB_PATH):
     L.dash_abi_sizes.restype = C.c_int
     L.dash_attn_bwd_flag_words.argtypes = [C.POINTER(DashAttnBwdArgs)]
     L.dash_attn_bwd_flag_words.restype = C.c_int64
+    L.dash_peer_export.argtypes = [_p, C.POINTER(DashPeerHandle)]
+    L.dash_peer_export.restype = C.c_int
+    L.dash_peer_import.argtypes = [C.POINTER(DashPeerHandle), C.POINTER(_p)]
+    L.dash_peer_import.restype = C.c_int
+    L.dash_peer_close.argtypes = [_p]
+    L.dash_peer_close.restype = C.c_int
     L.dash_selftest_bounded_wait.argtypes = [C.c_uint64, _p, _p]
     L.dash_selftest_bounded_wait.restype = C.c_int
     _lib = L

@@ -131,7 +131,7 @@ int dash_count_launches(int reset) {
 }
 
 int dash_abi_sizes(int64_t* out, int n) {
-  const int64_t s[21] = {(int64_t)sizeof(DashSeqs),           (int64_t)sizeof(DashKV),
+  const int64_t s[22] = {(int64_t)sizeof(DashSeqs),           (int64_t)sizeof(DashKV),
                          (int64_t)sizeof(DashRoutes),         (int64_t)sizeof(DashQO),
                          (int64_t)sizeof(DashKbarArgs),       (int64_t)sizeof(DashRouteArgs),
                          (int64_t)sizeof(DashBlockMaxArgs),   (int64_t)sizeof(DashPrefillArgs),
@@ -141,9 +141,9 @@ int dash_abi_sizes(int64_t* out, int n) {
                          (int64_t)sizeof(DashBlockAnyArgs),   (int64_t)sizeof(DashPageBlocksArgs),
                          (int64_t)sizeof(DashIndexProjArgs),  (int64_t)sizeof(DashRopeKVArgs),
                          (int64_t)sizeof(DashAttnBwdArgs),    (int64_t)sizeof(DashEntmaxArgs),
-                         (int64_t)sizeof(DashServingPlanArgs)};
-  for (int i = 0; i < n && i < 21; ++i) out[i] = s[i];
-  return 21;
+                         (int64_t)sizeof(DashServingPlanArgs), (int64_t)sizeof(DashPeerHandle)};
+  for (int i = 0; i < n && i < 22; ++i) out[i] = s[i];
+  return 22;
 }
 
 int dash_kbar_pool(const DashKbarArgs* a, dash_stream_t stream) {
@@ -218,6 +218,8 @@ int dash_prefill_attn(const DashPrefillArgs* a, dash_stream_t stream) {
   if (a->local_window < 0) return set_error(DASH_ERR_INVALID, "local_window must be >= 0");
   if (a->kv.block_table == nullptr && a->seqs.kv_len_fixed <= 0)
     return set_error(DASH_ERR_INVALID, "contiguous K/V needs kv_len_fixed (allocated length)");
+  if (a->n_peers < 0 || a->n_peers > 64 || (a->n_peers > 0 && !a->out_peers))
+    return set_error(DASH_ERR_INVALID, "n_peers must be in [0, 64] with an out_peers array");
   int64_t rows = seq_rows(a->seqs);
   size_t need = prefill_workspace(*a, rows);
   if (need && (!a->workspace || a->workspace_bytes < need))

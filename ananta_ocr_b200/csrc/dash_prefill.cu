@@ -829,8 +829,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   #pragma unroll
           for (int v = 0; v < 4; ++v)
             *reinterpret_cast<uint4*>(op + q4 * 32 + v * 8) = make_uint4(pko[4 * v], pko[4 * v + 1], pko[4 * v + 2], pko[4 * v + 3]);
+          // fused output gather: the same row into every peer rank's copy of
+          // the output (P2P stores over NVLink; same strides, same offset)
+          for (int pr = 0; pr < a.n_peers; ++pr) {
+            T* pop = reinterpret_cast<T*>(a.out_peers[pr]) + (op - reinterpret_cast<T*>(a.qo.out));
+  #pragma unroll
+            for (int v = 0; v < 4; ++v)
+              *reinterpret_cast<uint4*>(pop + q4 * 32 + v * 8) = make_uint4(pko[4 * v], pko[4 * v + 1], pko[4 * v + 2], pko[4 * v + 3]);
+          }
         }
       }
+      // The peer stores are posted: no fence here, so an SM takes its next
+      // tile while they drain over NVLink.  The grid completes only once all
+      // of its writes are performed, and the caller's completion step is
+      // stream-ordered after the grid, so it sees every row in place.
       if (row_ok && a.qo.lse) {
         float lse = l_run > 0.0f ? (m_run + log2f(l_run)) * 0.6931471805599453f : -INFINITY;
         a.qo.lse[(a.seqs.q_start ? rglob * a.qo.lse_stride_tok

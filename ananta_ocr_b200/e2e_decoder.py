@@ -54,9 +54,15 @@ class DecoderConfig:
     first_dense: int = 1
     eps: float = 1e-6
     rope_theta: float = 500000.0
-    block_size: int = 64
+    # the checkpoint's DASH settings (config.json: sparse_block_size 32,
+    # sparse_local_block 4, dash_topk_blocks 12) and the serving router's
+    # defaults (WHL dash_router.py:16,101-105: entmax window 16, 16 output
+    # slots, the last 4 of them -1)
+    block_size: int = 32
     local_blocks: int = 4
-    K: int = 16
+    K: int = 12
+    topm: int = 16
+    slots: int = 16
     index_dim: int = 128
     scaling: float = 128.0
     prior_floor: float = 1e-4
@@ -124,8 +130,8 @@ class DashDecoder:
         self.inv_freq = inv
         # decode-step buffers (fixed addresses for graph replay)
         self.tok = torch.zeros(batch, dtype=torch.int64, device=device)
-        self.oi = torch.empty(batch, c.K, dtype=torch.int32, device=device)
-        self.ob = torch.empty(batch, c.K, dtype=torch.float32, device=device)
+        self.oi = torch.empty(batch, c.slots, dtype=torch.int32, device=device)
+        self.ob = torch.empty(batch, c.slots, dtype=torch.float32, device=device)
         self.attn_out = torch.empty(batch, c.heads, c.head_dim, dtype=bf, device=device)
         self.dec_ws = torch.empty(16 << 20, dtype=torch.uint8, device=device)
         self.idx_scale = c.scaling / math.sqrt(c.index_dim)
@@ -232,8 +238,8 @@ class DashDecoder:
             if self.page_mask:
                 allow = self.pst.build_query_allow(layout, q_page, self.pps, self.num_pages)
                 domain = None
-        oi = torch.empty(T, c.K, dtype=torch.int32, device=dev)
-        ob = torch.empty(T, c.K, dtype=torch.float32, device=dev)
+        oi = torch.empty(T, c.slots, dtype=torch.int32, device=dev)
+        ob = torch.empty(T, c.slots, dtype=torch.float32, device=dev)
         attn = torch.empty(T, c.heads, c.head_dim, dtype=torch.bfloat16, device=dev)
         for li, L in enumerate(self.layers):
             if attn_events is not None:
@@ -252,10 +258,10 @@ class DashDecoder:
                                     row2req=row2req, image_allow=allow, out_idx=oi, out_bias=ob,
                                     max_block=self.pps, block_size=c.block_size,
                                     local_blocks=c.local_blocks, idx_scale=self.idx_scale,
-                                    prior_floor=c.prior_floor, sigma=c.sigma, topm=c.K, budget=c.K,
-                                    out_slots=c.K, page_domain=domain)
+                                    prior_floor=c.prior_floor, sigma=c.sigma, topm=c.topm, budget=c.K,
+                                    out_slots=c.slots, page_domain=domain)
             AT.dash_sparse_attn(q.view(T, c.heads, c.head_dim), self.kc[li], self.vc[li],
-                                oi[None].expand(c.kv_heads, T, c.K), ob[None].expand(c.kv_heads, T, c.K),
+                                oi[None].expand(c.kv_heads, T, c.slots), ob[None].expand(c.kv_heads, T, c.slots),
                                 self.block_table, cu, self.seq_lens, ctx, S, c.kv_heads,
                                 1.0 / math.sqrt(c.head_dim), attn, local_blocks=c.local_blocks,
                                 sparse_block_size=c.block_size)
@@ -311,11 +317,11 @@ class DashDecoder:
                                    max_block=self.pps, block_size=c.block_size,
                                    local_blocks=c.local_blocks, decode_query_len=1,
                                    idx_scale=self.idx_scale, prior_floor=c.prior_floor,
-                                   sigma=c.sigma, topm=c.K, budget=c.K, out_slots=c.K,
+                                   sigma=c.sigma, topm=c.topm, budget=c.K, out_slots=c.slots,
                                    page_domain=domain)
             AT.dash_sparse_attn_decode(q.view(B, c.heads, c.head_dim), self.kc[li], self.vc[li],
-                                       self.oi[None].expand(c.kv_heads, B, c.K),
-                                       self.ob[None].expand(c.kv_heads, B, c.K), self.block_table,
+                                       self.oi[None].expand(c.kv_heads, B, c.slots),
+                                       self.ob[None].expand(c.kv_heads, B, c.slots), self.block_table,
                                        sl, c.kv_heads, 1.0 / math.sqrt(c.head_dim), self.attn_out, 1,
                                        local_blocks=c.local_blocks, sparse_block_size=c.block_size,
                                        workspace=self.dec_ws)

@@ -165,11 +165,12 @@ def _decode_attend(q, k_all, v_all, topi, bias, valid, q_pos, block_size, local_
 @torch.no_grad()
 def dash_prefill_forward(q, k, v, idx_q, idx_k, *, block_size, local_blocks, head_cls=None,
                          K, topm=None, idx_scale, prior_floor, sigma, scale=None,
-                         return_routes=False, page_domain=None):
+                         return_routes=False, page_domain=None, out=None, peers=None):
     """Router + gather attention for a contiguous prefill.
 
     q [B,H,S,D], k/v [B,Hkv,S,D] (bf16/fp16), idx_q/idx_k [B,S,d] fp32 router
-    queries/keys.  Returns out [B,H,S,D] (and the routed lists if asked)."""
+    queries/keys.  Returns out [B,H,S,D] (and the routed lists if asked);
+    ``out``/``peers`` as in ``ops.gather_attention`` (fused output gather)."""
     B, H, S, D = q.shape
     d = idx_q.shape[-1]
     nblk = (S + block_size - 1) // block_size
@@ -181,7 +182,8 @@ def dash_prefill_forward(q, k, v, idx_q, idx_k, *, block_size, local_blocks, hea
                           page=page_domain)
     out = ops.gather_attention(q, k, v, idx.view(B, S, K), bias.view(B, S, K),
                                block_size=block_size, local_window=local_blocks * block_size,
-                               scale=float(scale if scale is not None else 1.0 / math.sqrt(D)))
+                               scale=float(scale if scale is not None else 1.0 / math.sqrt(D)),
+                               out=out, peers=peers)
     if return_routes:
         return out, idx.view(B, S, K), bias.view(B, S, K)
     return out

@@ -322,10 +322,13 @@ def decode_attn(args: L.DashDecodeArgs, device, workspace: Optional[torch.Tensor
 
 def gather_attention(q, k, v, idx, bias, *, block_size: int, local_window: int, scale: float,
                      out=None, lse=None, seg_start=None, n_index_heads: int = 1,
-                     device_error: Optional[DeviceErrorWord] = None, workspace=None):
+                     device_error: Optional[DeviceErrorWord] = None, workspace=None,
+                     peers: Optional[torch.Tensor] = None):
     """Contiguous prefill: q [B,HQ,T,D], k/v [B,Hkv,T,D] (any strides with unit
     inner stride), idx/bias routes [B,HI,T,K] (or [B,T,K]).  Returns out
-    [B,HQ,T,D] (a new tensor unless ``out`` is given)."""
+    [B,HQ,T,D] (a new tensor unless ``out`` is given).  ``peers`` (int64 device
+    array, ``peer.PeerGather.peers_for(out)``) also stores every output row
+    into the other ranks' copies of ``out``."""
     _need_cuda(q, k, v, idx)
     B, HQ, T, D = q.shape
     Hkv = k.shape[1]
@@ -359,6 +362,8 @@ def gather_attention(q, k, v, idx, bias, *, block_size: int, local_window: int, 
         a.seg_start = seg_start.data_ptr()
     a.scale, a.block_size, a.local_window = float(scale), int(block_size), int(local_window)
     a.device_error = device_error.ptr if device_error is not None else None
+    if peers is not None and peers.numel():
+        a.out_peers, a.n_peers = peers.data_ptr(), int(peers.numel())
     prefill_attn(a, q.device, workspace)
     return out
 

@@ -5,8 +5,11 @@ single head per sequence, so the batch is split across ranks sequence-major;
 when there are more ranks than sequences, a sequence's kv heads are split
 across ranks and each of those ranks recomputes that sequence's (cheap) route.
 Nothing crosses NVLink inside attention.  The one collective is the final
-gather of the output shards (NCCL all-gather over NVLink/NVSwitch on GPUs,
-gloo on CPU in the tests).
+gather of the output shards: either fused into the attention kernel
+(``run_sharded_fused``: each output row is stored into every rank's gathered
+tensor over NVLink as soon as it is computed, then one stream-ordered NCCL
+word marks completion) or an NCCL all-gather after it (``run_sharded``; gloo
+on CPU in the tests).
 """
 from __future__ import annotations
 
@@ -82,3 +85,25 @@ def run_sharded(attn: Callable, q: torch.Tensor, k: torch.Tensor, v: torch.Tenso
         chunk = recv[r * max_units * per_unit: r * max_units * per_unit + n]
         full[s.b0:s.b1, s.h0 * G:s.h1 * G] = chunk.view(s.b1 - s.b0, (s.h1 - s.h0) * G, S, D)
     return full
+
+
+def run_sharded_fused(attn: Callable, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                      idx_q: torch.Tensor, idx_k: torch.Tensor, gather, *, rank: int,
+                      world: int, complete: bool = True) -> torch.Tensor:
+    """This rank's shard of a [B, H, S, D] problem with the gather fused into
+    the attention: ``attn(q, k, v, idx_q, idx_k, out=, peers=)`` writes the
+    shard's rows into ``out`` (this rank's slice of ``gather.full``, a
+    ``peer.PeerGather`` over a [B, H, S, D] tensor every rank holds) and into
+    the peers' copies.  Returns ``gather.full``, complete on every rank once
+    the stream reaches the end of the call (``complete``)."""
+    B, H, S, D = q.shape
+    Hkv = k.shape[1]
+    G = H // Hkv
+    sh = plan_shards(B, Hkv, world)[rank]
+    view = gather.full[sh.b0:sh.b1, sh.h0 * G:sh.h1 * G]
+    attn(q[sh.b0:sh.b1, sh.h0 * G:sh.h1 * G], k[sh.b0:sh.b1, sh.h0:sh.h1],
+         v[sh.b0:sh.b1, sh.h0:sh.h1], idx_q[sh.b0:sh.b1], idx_k[sh.b0:sh.b1],
+         out=view, peers=gather.peers_for(view))
+    if complete:
+        gather.complete()
+    return gather.full

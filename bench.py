@@ -15,11 +15,14 @@ the same run.  With N GPUs every rank runs its own shard of sequences (weak
 scaling, no collective inside the step); value = tokens of all ranks / max
 rank time.
 
-`--impl reference` times the reference algorithm on the host CPU: the
-reference is Python/PyTorch+Triton and cannot travel to the GPU box, so the
-arm runs the C restatement of it (oracle/dash_oracle.c, pinned to the
-reference's own outputs by tests/test_oracle_golden.py) with every host core,
-on a bounded sample of the same workload.
+`--impl reference` times the reference's own CPU inference path on the host:
+the reference is Python/PyTorch+Triton and cannot travel to the GPU box, so
+the arm runs a torch fp32 restatement of it (oracle/torch_path.py: head_cls
+k-bar, scores, canonical selection and the dense masked attention of
+dash_attention.py:980-1006, checked against the reference's own outputs by
+tests/test_torch_path.py) with every host thread, on a bounded sample of the
+same workload (query tokens of one sequence; every token of the dense form
+costs the same).
 """
 from __future__ import annotations
 
@@ -42,6 +45,10 @@ C2 = dict(name="config2_prefill_bf16", B=4, H=10, S=9248, D=128, bs=64, lb=4, K=
 C4 = dict(name="config4_longdoc_prefill_bf16", B=8, H=16, S=131072, D=128, bs=128, lb=8, K=64,
           n_pages=480, page_tokens=273, off_std=0.2)
 C3 = dict(name="config3_decode_bf16", R=64, H=10, S=27556, D=128, bs=64, lb=4, K=32)
+# the config-2 inputs under the checkpoint's own DASH settings (config.json:
+# sparse_block_size 32, sparse_local_block 4, dash_topk_blocks 12; the serving
+# router's entmax window of 16, WHL dash_router.py:16)
+C2_BS32 = dict(C2, name="config2_prefill_bf16_block32", bs=32, lb=4, K=12, topm=16)
 IDX_SCALE = 128.0 / math.sqrt(128)
 IMAGE_TOKEN_ID, PAGE_TOKEN_ID = 128815, 128827   # config.json:156,160
 
@@ -66,12 +73,13 @@ class ClockSampler:
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
-        self.path = os.path.join(REPO, "gpurun_out", f"clocks_rank{gpu_index}.csv")
+        self.path = None
 
     def start(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
-            self.f = open(self.path, "w")
+            import tempfile
+            fd, self.path = tempfile.mkstemp(prefix=f"dash_clocks_gpu{self.gpu}_", suffix=".csv")
+            self.f = os.fdopen(fd, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}", "--format=csv",
                  "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
@@ -102,6 +110,7 @@ class ClockSampler:
                 for n, v in zip(names, parts[5:9]):
                     if v.lower().startswith("active"):
                         reasons.add(n)
+        os.unlink(self.path)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
                 "reasons": sorted(reasons), "samples": len(sm)}
 
@@ -176,6 +185,30 @@ def run_c5(dev, decode_steps, warmup):
     del graph
     return dict(B=B, S=S, prefill_ms=t_prefill, attn_ms=t_attn, decode_ms=t_dec,
                 decode_steps=decode_steps, finite=ok)
+
+
+def c5_summary(r):
+    """The config-5 figures of ``run_c5`` as a JSON object."""
+    from ananta_ocr_b200.e2e_decoder import DecoderConfig
+    c = DecoderConfig()
+    return {
+        "config": {"workload": "config5_e2e_decoder", "layers": c.layers, "hidden": c.hidden,
+                   "heads": c.heads, "experts": "64 routed top-6 + 2 shared", "batch": r["B"],
+                   "prompt_tokens": r["S"], "decode_steps": r["decode_steps"],
+                   "block_size": c.block_size, "local_blocks": c.local_blocks, "routed_k": c.K,
+                   "entmax_window": c.topm,
+                   "document": "100 pages x (marker + 272 image tokens) + 256 text",
+                   "candidates": "page-aware (PageIsolationState, once per forward)",
+                   "weights": "random init (the checkpoint is absent)"},
+        "prefill": {"ms": r["prefill_ms"], "tokens_per_s": r["B"] * r["S"] / (r["prefill_ms"] / 1e3),
+                    "attention_ms": r["attn_ms"],
+                    "attention_fraction": r["attn_ms"] / r["prefill_ms"],
+                    "attention_scope": "per layer: RoPE + K/V store, index front end, "
+                                       "k-bar, routing, paged attention; page state "
+                                       "once per forward outside the layer events"},
+        "decode": {"ms_per_step": r["decode_ms"], "tokens_per_s": r["B"] / (r["decode_ms"] / 1e3),
+                   "graph": f"one CUDA graph per step, {r['decode_steps']} replays"},
+        "finite_logits": r["finite"]}
 
 
 # ---------------------------------------------------------------------------
@@ -434,6 +467,140 @@ def make_prefill(cfg, dev, seed):
     return q, k, v, iq, ik
 
 
+def make_prefill_seqs(cfg, dev, seqs, seed):
+    """Sequences ``seqs`` of a prefill workload, each from its own seeded
+    generator, so a rank holding any subset draws what one GPU holding all
+    would (the strong-scaling runs compare like with like)."""
+    import torch
+    H, S, D = cfg["H"], cfg["S"], cfg["D"]
+    P, pt = cfg["n_pages"], cfg["page_tokens"]
+    n = len(seqs)
+    q = torch.empty(n, H, S, D, device=dev, dtype=torch.bfloat16)
+    k, v = torch.empty_like(q), torch.empty_like(q)
+    iq = torch.empty(n, S, 128, device=dev)
+    ik = torch.empty(n, S, 128, device=dev)
+    for j, b in enumerate(seqs):
+        g = torch.Generator(device=dev).manual_seed(seed * 1000 + b)
+        off = torch.zeros(H, S, D, device=dev)
+        ioff = torch.zeros(S, 128, device=dev)
+        pages = torch.randn(P, H, 1, D, generator=g, device=dev) * cfg["off_std"]
+        ipages = torch.randn(P, 128, generator=g, device=dev) * cfg["off_std"]
+        for p in range(P):
+            a0, a1 = p * pt, min(S, (p + 1) * pt)
+            if a0 >= S:
+                break
+            off[:, a0:a1] = pages[p]
+            ioff[a0:a1] = ipages[p]
+        q[j] = (torch.randn(H, S, D, generator=g, device=dev) * 0.5 + off).bfloat16()
+        k[j] = (torch.randn(H, S, D, generator=g, device=dev) * 0.5 + off).bfloat16()
+        v[j] = (torch.randn(H, S, D, generator=g, device=dev) * 0.5).bfloat16()
+        iq[j] = torch.randn(S, 128, generator=g, device=dev) * 0.5 + ioff
+        ik[j] = torch.randn(S, 128, generator=g, device=dev) * 0.5 + ioff
+    return q, k, v, iq, ik
+
+
+def run_c4(dev, rank, world, steps, warmup, mode):
+    """BASELINE config 4 (B=8 long documents of 131,072 tokens, 16 heads, block
+    128, window 8 blocks, K=64) split over the ranks by sequence x kv head
+    (sharding.plan_shards): every rank routes and attends its shard, and the
+    step ends with the whole output on every rank (``mode`` "fused": gather in
+    the attention kernel; "nccl": in-place NCCL all-gather after it).  Strong
+    scaling: the total work is fixed.  Device time per step, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from ananta_ocr_b200 import ops
+    from ananta_ocr_b200.sharding import plan_shards
+    cfg = C4
+    B, H, S, D, bs, lb, K = (cfg[x] for x in ("B", "H", "S", "D", "bs", "lb", "K"))
+    sh = plan_shards(B, H, world)[rank]
+    nb = sh.b1 - sh.b0
+    q, k, v, iq, ik = make_prefill_seqs(cfg, dev, list(range(sh.b0, sh.b1)), 4)
+    if sh.h1 - sh.h0 < H:
+        q, k, v = (t[:, sh.h0:sh.h1].contiguous() for t in (q, k, v))
+    full = torch.empty(B, H, S, D, dtype=torch.bfloat16, device=dev)
+    out = full[sh.b0:sh.b1, sh.h0:sh.h1]
+    gather = None
+    if world > 1 and mode == "fused":
+        from ananta_ocr_b200.peer import PeerGather
+        gather = PeerGather(full)
+    peers = gather.peers_for(out) if gather is not None else None
+    nblk = -(-S // bs)
+    lcfg = dict(cfg, B=nb, H=sh.h1 - sh.h0)
+    ws = dict(kbar=torch.empty(nb, nblk, 128, device=dev),
+              idx=torch.empty(nb * S, K, dtype=torch.int32, device=dev),
+              bias=torch.empty(nb * S, K, device=dev),
+              attn_ws=torch.empty(_prefill_ws_bytes(lcfg), dtype=torch.uint8, device=dev))
+    seqs = ops.Seqs(n_seq=nb, q_len=S, kv_len=S, max_q_len=S)
+
+    def route_fn():
+        kb = ops.kbar_pool_contig(ik, None, bs, out=ws["kbar"])
+        ops.route(seqs, width=nblk, block_size=bs, local_blocks=lb, idx_scale=IDX_SCALE,
+                  prior_floor=1e-4, sigma=1.0, topm=K, K=K, idx_q=iq.view(nb * S, 128), kbar=kb,
+                  out_idx=ws["idx"], out_bias=ws["bias"])
+
+    def attn_fn():
+        ops.gather_attention(q, k, v, ws["idx"].view(nb, S, K), ws["bias"].view(nb, S, K),
+                             block_size=bs, local_window=lb * bs, scale=1.0 / math.sqrt(D),
+                             out=out, workspace=ws["attn_ws"], peers=peers)
+
+    post = None
+    if gather is not None:
+        post = gather.complete
+    elif world > 1 and mode == "nccl":
+        assert sh.h1 - sh.h0 == H, "the NCCL form gathers whole sequences"
+        post = lambda: dist.all_gather_into_tensor(full.view(-1), out.reshape(-1))  # noqa: E731
+    step = GraphStep(route_fn, attn_fn, True, post=post)
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        step(ev[i])
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / steps,
+                      statistics.mean(e[1].elapsed_time(e[2]) for e in ev)], device=dev,
+                     dtype=torch.float64)
+    alg, executed = prefill_flops(lcfg, ws["idx"])
+    fl = torch.tensor([alg, executed], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(fl)
+    if gather is not None:
+        gather.close()
+    del step
+    return dict(ms=float(t[0]), attn_gather_ms=float(t[1]), alg=float(fl[0]),
+                executed=float(fl[1]), tokens=B * S, shard=(sh.b0, sh.b1, sh.h0, sh.h1))
+
+
+def c4_summary(r, world, gather, peaks, peak_kind):
+    """The config-4 figures of ``run_c4`` as a JSON object."""
+    peak = peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
+    tf = r["alg"] / (r["ms"] / 1e3) / 1e12
+    return {
+        "workload": C4["name"], "scaling": "strong", "n_gpus": world,
+        "sequences": C4["B"], "seq_len": C4["S"], "heads": C4["H"], "block_size": C4["bs"],
+        "local_blocks": C4["lb"], "routed_k": C4["K"],
+        "split": "sequence x kv head (sharding.plan_shards); this run's rank-0 shard "
+                 f"seqs {r['shard'][0]}:{r['shard'][1]} heads {r['shard'][2]}:{r['shard'][3]}",
+        "output_gather_in_step": ("none (one GPU)" if world == 1 else
+                                  "fused into the attention kernel + NCCL completion word"
+                                  if gather != "nccl" else "in-place NCCL all-gather"),
+        "ms_per_step": r["ms"], "tokens_per_s": r["tokens"] / (r["ms"] / 1e3),
+        "attn_and_gather_ms": r["attn_gather_ms"],
+        "alg_tflops": tf, "executed_tflops": r["executed"] / (r["ms"] / 1e3) / 1e12,
+        "alg_flops_per_step": r["alg"], "executed_flops_per_step": r["executed"],
+        "roofline": {"bound": "tensor", "achieved": tf, "peak": peak * world, "unit": "TFLOP/s",
+                     "frac": tf / (peak * world),
+                     "kernel": "whole step (routing + prefill_kernel + gather), algorithmic FLOPs, "
+                               "all GPUs", "peak_source": f"{peak_kind} bf16_tflops x {world}"},
+        "steps": 3, "warmup": 3}
+
+
 def prefill_step(cfg, q, k, v, iq, ik, ws, timers=None):
     """One DASH prefill step through the public API; returns (out, idx, bias)."""
     from ananta_ocr_b200 import ops
@@ -485,7 +652,13 @@ def prefill_flops(cfg, idx):
     pmin, pmax = tiles * 128, torch.clamp(tiles * 128 + 127, max=S - 1)
     blk = torch.arange(nblk, device=idx.device)
     loc = (blk[None] >= torch.clamp((pmin[:, None] - LW + 1), min=0) // bs) & (blk[None] <= pmax[:, None] // bs)
-    ktiles = (uni | loc[None]).sum() * (bs // 64)
+    walked = uni | loc[None]
+    if bs >= 64:
+        ktiles = walked.sum() * (bs // 64)
+    else:
+        # 64-key tiles of two 32-token blocks: walked when either block is
+        walked = torch.nn.functional.pad(walked, (0, nblk % 2))
+        ktiles = walked.view(B, ntile, -1, 2).any(-1).sum()
     executed = float(ktiles) * H * 128 * 64 * D * 4
     return alg, executed
 
@@ -494,9 +667,9 @@ class GraphStep:
     """A step as two CUDA graphs (route part, attention part) replayed back to
     back on the current stream, with CUDA events between them."""
 
-    def __init__(self, route_fn, attn_fn, use_graph=True):
+    def __init__(self, route_fn, attn_fn, use_graph=True, post=None):
         import torch
-        self.route_fn, self.attn_fn = route_fn, attn_fn
+        self.route_fn, self.attn_fn, self.post = route_fn, attn_fn, post
         self.graphs = None
         if use_graph:
             s = torch.cuda.Stream()
@@ -520,37 +693,45 @@ class GraphStep:
         if timers:
             timers[1].record()
         self.graphs[1].replay() if self.graphs else self.attn_fn()
+        if self.post is not None:
+            self.post()          # stream-ordered, outside the graphs (an NCCL call)
         if timers:
             timers[2].record()
 
 
-def run_prefill(cfg, dev, steps, warmup, rank, world, use_graph=True):
+def run_prefill(cfg, dev, steps, warmup, rank, world, use_graph=True, gather=None):
+    """The headline step on this rank's B sequences.  With ``gather`` (a
+    ``peer.PeerGather`` over [world * B, H, S, D]) the attention also stores
+    every output row into the other ranks' gathered tensors (the fused output
+    gather) and the step ends with its stream-ordered completion."""
     import torch
     from ananta_ocr_b200 import ops
     B, H, S, D, bs, lb, K = (cfg[x] for x in ("B", "H", "S", "D", "bs", "lb", "K"))
     nblk = (S + bs - 1) // bs
     q, k, v, iq, ik = make_prefill(cfg, dev, 1234 + rank)
+    out = gather.full[rank * B:(rank + 1) * B] if gather is not None else torch.empty_like(q)
+    peers = gather.peers_for(out) if gather is not None else None
     ws = dict(kbar=torch.empty(B, nblk, 128, device=dev),
               idx=torch.empty(B * S, K, dtype=torch.int32, device=dev),
-              bias=torch.empty(B * S, K, device=dev), out=torch.empty_like(q))
-    ws["attn_ws"] = None
+              bias=torch.empty(B * S, K, device=dev), out=out,
+              attn_ws=torch.empty(_prefill_ws_bytes(cfg), dtype=torch.uint8, device=dev))
     out, idx, bias = prefill_step(cfg, q, k, v, iq, ik, ws)
-    ws["attn_ws"] = ops._WS.get((q.device, "prefill"))
     torch.cuda.synchronize()
     seqs = ops.Seqs(n_seq=B, q_len=S, kv_len=S, max_q_len=S)
 
     def route_fn():
         kb = ops.kbar_pool_contig(ik, None, bs, out=ws["kbar"])
         ops.route(seqs, width=nblk, block_size=bs, local_blocks=lb, idx_scale=IDX_SCALE,
-                  prior_floor=1e-4, sigma=1.0, topm=K, K=K, idx_q=iq.view(B * S, 128), kbar=kb,
-                  out_idx=ws["idx"], out_bias=ws["bias"])
+                  prior_floor=1e-4, sigma=1.0, topm=cfg.get("topm", K), K=K,
+                  idx_q=iq.view(B * S, 128), kbar=kb, out_idx=ws["idx"], out_bias=ws["bias"])
 
     def attn_fn():
         ops.gather_attention(q, k, v, ws["idx"].view(B, S, K), ws["bias"].view(B, S, K),
                              block_size=bs, local_window=lb * bs, scale=1.0 / math.sqrt(D),
-                             out=ws["out"], workspace=ws["attn_ws"])
+                             out=ws["out"], workspace=ws["attn_ws"], peers=peers)
 
-    step = GraphStep(route_fn, attn_fn, use_graph)
+    step = GraphStep(route_fn, attn_fn, use_graph,
+                     post=gather.complete if gather is not None else None)
     for _ in range(max(0, warmup - 1)):
         step()
     torch.cuda.synchronize()
@@ -559,6 +740,60 @@ def run_prefill(cfg, dev, steps, warmup, rank, world, use_graph=True):
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     return dict(q=q, k=k, v=v, iq=iq, ik=ik, ws=ws, ev=ev, start=start, stop=stop, alg=alg,
                 executed=executed, idx=idx, step=step)
+
+
+def run_prefill_on(cfg, st, dev, steps, warmup):
+    """The headline's prefill inputs (``st``) routed and attended under another
+    DASH configuration ``cfg`` (block size, window, K): k-bar + routing and the
+    attention replayed from CUDA graphs, device time per part with CUDA events."""
+    import torch
+    from ananta_ocr_b200 import ops
+    B, H, S, D, bs, lb, K = (cfg[x] for x in ("B", "H", "S", "D", "bs", "lb", "K"))
+    nblk = (S + bs - 1) // bs
+    q, k, v, iq, ik = (st[x] for x in ("q", "k", "v", "iq", "ik"))
+    ws = dict(kbar=torch.empty(B, nblk, 128, device=dev),
+              idx=torch.empty(B * S, K, dtype=torch.int32, device=dev),
+              bias=torch.empty(B * S, K, device=dev), out=torch.empty_like(q))
+    seqs = ops.Seqs(n_seq=B, q_len=S, kv_len=S, max_q_len=S)
+    # the attention scratch is sized once here, outside the graph capture
+    attn_ws = torch.empty(_prefill_ws_bytes(cfg), dtype=torch.uint8, device=dev)
+
+    def route_fn():
+        kb = ops.kbar_pool_contig(ik, None, bs, out=ws["kbar"])
+        ops.route(seqs, width=nblk, block_size=bs, local_blocks=lb, idx_scale=IDX_SCALE,
+                  prior_floor=1e-4, sigma=1.0, topm=cfg.get("topm", K), K=K,
+                  idx_q=iq.view(B * S, 128), kbar=kb, out_idx=ws["idx"], out_bias=ws["bias"])
+
+    def attn_fn():
+        ops.gather_attention(q, k, v, ws["idx"].view(B, S, K), ws["bias"].view(B, S, K),
+                             block_size=bs, local_window=lb * bs, scale=1.0 / math.sqrt(D),
+                             out=ws["out"], workspace=attn_ws)
+
+    route_fn()
+    step = GraphStep(route_fn, attn_fn)
+    for _ in range(max(3, warmup)):
+        step()
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    for i in range(steps):
+        step(ev[i])
+    torch.cuda.synchronize()
+    route_ms = statistics.median(e[0].elapsed_time(e[1]) for e in ev)
+    attn_ms = statistics.median(e[1].elapsed_time(e[2]) for e in ev)
+    alg, executed = prefill_flops(cfg, ws["idx"])
+    return dict(route_ms=route_ms, attn_ms=attn_ms, alg=alg, executed=executed, tokens=B * S)
+
+
+def _prefill_ws_bytes(cfg):
+    """Bytes of attention scratch (canonical lists, two biases per entry for
+    32-token blocks, per-tile unions, per-row largest bias) for a contiguous
+    prefill of ``cfg``; an upper bound of the library's own sizing."""
+    B, S, bs, K = cfg["B"], cfg["S"], cfg["bs"], cfg["K"]
+    rows = B * S
+    nblk = -(-S // bs)
+    lists = rows * K * 4 + 256
+    tiles = B * (-(-S // 128))
+    return lists * 3 + tiles * (-(-nblk // 32)) * 4 + 256 + rows * 4 + 4096
 
 
 def run_decode_setup(cfg, dev, seed):
@@ -639,33 +874,37 @@ def decode_bytes(cfg, d):
 # ---------------------------------------------------------------------------
 # CPU baseline (oracle port) on a bounded sample
 # ---------------------------------------------------------------------------
-def cpu_baseline(cfg, n_tokens=512, threads=None):
+def cpu_baseline(cfg, n_tokens=1024, threads=None):
+    """The reference's CPU inference path in its own arithmetic (fp32 torch:
+    head_cls k-bar of every block, scores and canonical selection of the sampled
+    query rows, dense masked attention of those rows over all keys, chunked by
+    512 queries; oracle/torch_path.py, checked against the reference's outputs)
+    on one sequence of the workload, all host threads.  Every query row of the
+    dense form costs the same (all keys, masked), so the sample's tokens/s is
+    the workload's."""
     import numpy as np
+    import torch
     from oracle import dash_oracle as O
+    from oracle import torch_path as TP
     threads = threads or os.cpu_count()
-    O.set_threads(threads)
+    torch.set_num_threads(threads)
     B, H, S, D, bs, lb, K = (cfg[x] for x in ("B", "H", "S", "D", "bs", "lb", "K"))
-    nseq = 1
-    q, k, v, iq, ik = O.make_prefill_inputs(99, nseq, H, S, D, cfg["n_pages"], cfg["page_tokens"],
-                                            cfg["off_std"])
-    rng = np.random.default_rng(0)
-    rows = np.sort(rng.choice(S, size=n_tokens, replace=False))
+    q, k, v, iq, ik = (torch.from_numpy(x) for x in O.make_prefill_inputs(
+        99, 1, H, S, D, cfg["n_pages"], cfg["page_tokens"], cfg["off_std"]))
+    q, k, v = (t.to(torch.bfloat16).float() for t in (q, k, v))
+    rows = torch.from_numpy(np.sort(np.random.default_rng(0).choice(S, size=n_tokens,
+                                                                     replace=False)))
     t0 = time.perf_counter()
-    kb = O.kbar_contig(ik, np.zeros(128, np.float32), bs)
-    nblk = kb.shape[1]
-    bt = np.arange(nblk, dtype=np.int32)[None]
-    sc = O.scores_paged(iq[0, rows], rows, np.zeros(len(rows), np.int64), np.array([S]), kb[0], bt,
-                        bs, lb, nblk)
-    idx, bias, _ = O.route_select(sc, None, IDX_SCALE, K, K, 1e-4, 1.0)
-    full_idx = np.full((nseq, S, K), -1, np.int32)
-    full_bias = np.zeros((nseq, S, K), np.float32)
-    full_idx[0, rows], full_bias[0, rows] = idx, bias
-    O.attend_contig(q, k, v, full_idx, full_bias, bs, lb * bs, 1.0 / math.sqrt(D), rows=rows)
+    with torch.no_grad():
+        TP.prefill_rows(q, k, v, iq, ik, rows, block_size=bs, local_blocks=lb, K=K,
+                        topm=cfg.get("topm", K), idx_scale=IDX_SCALE)
     dt = time.perf_counter() - t0
     return dict(value=n_tokens / dt, unit="tokens/s", cores=threads, kind="port",
-                sample=f"{n_tokens} query tokens x {H} heads of {cfg['name']} (k-bar of all blocks, "
-                       f"scores + selection + attention of the sampled tokens), oracle/dash_oracle.c",
-                seconds=dt)
+                sample=f"{n_tokens} query tokens x {H} heads of one {S}-token sequence of "
+                       f"{cfg['name']}: k-bar of all blocks, scores + selection + dense masked "
+                       f"fp32 attention of the sampled tokens (the reference's torch CPU form, "
+                       f"oracle/torch_path.py), {threads} threads",
+                seconds=dt, dtype="fp32")
 
 
 # ---------------------------------------------------------------------------
@@ -687,6 +926,15 @@ def main():
                     help="skip the training-backward measurement")
     ap.add_argument("--no-frontend", action="store_true",
                     help="skip the router front-end measurement")
+    ap.add_argument("--no-c4", action="store_true",
+                    help="skip the long-document (config 4) strong-scaling sub-object")
+    ap.add_argument("--no-c5", action="store_true",
+                    help="skip the end-to-end decoder (config 5) sub-object")
+    ap.add_argument("--no-block32", action="store_true",
+                    help="skip the prefill under the checkpoint's 32-token blocks")
+    ap.add_argument("--gather", default="fused", choices=["fused", "nccl", "none"],
+                    help="output gather at N > 1 inside the timed step: fused into the attention "
+                         "kernel (default), an NCCL all-gather after it, or none")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch eagerly instead of replaying captured CUDA graphs")
     ap.add_argument("--decode-rows", type=int, default=0,
@@ -704,17 +952,18 @@ def main():
             return
         ms = []
         res = None
+        n_tok = 1024
         for i in range(args.warmup + args.steps):
-            r = cpu_baseline(cfg, n_tokens=256)
+            r = cpu_baseline(cfg, n_tokens=n_tok)
             if i >= args.warmup:
                 ms.append(r["seconds"])
                 res = r
-        val = 256 / statistics.median(ms)
+        val = n_tok / statistics.median(ms)
         line = {"metric": "DASH attn tokens/s", "value": val, "unit": "tokens/s", "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.median(ms) * 1e3,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
                 "data": "synthetic", "impl": "reference",
-                "config": {"workload": cfg["name"], "sample_tokens": 256},
+                "config": {"workload": cfg["name"], "sample_tokens": n_tok},
                 "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": res["cores"],
                                  "kind": "port", "sample": res["sample"]},
                 "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -744,6 +993,28 @@ def main():
     from ananta_ocr_b200 import _lib
     _lib.load()
 
+    if args.workload == "c4":
+        # config 4 alone: strong scaling over the ranks, gather inside the step
+        clocks = ClockSampler(local_rank)
+        clocks.start()
+        r = run_c4(dev, rank, world, args.steps, max(3, args.warmup),
+                   args.gather if args.gather != "none" else "fused")
+        clk = clocks.stop()
+        if rank == 0:
+            peaks, peak_kind = load_peaks()
+            sub = c4_summary(r, world, args.gather, peaks, peak_kind)
+            print(json.dumps({"metric": "DASH attn tokens/s", "value": sub["tokens_per_s"],
+                              "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                              "warmup": max(3, args.warmup), "ms_per_step": r["ms"],
+                              "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                              "dtype": "bf16", "data": "synthetic (seeded, BASELINE distributions)",
+                              "config": {"workload": C4["name"], "parallelism": f"shard{world}",
+                                         "l2": "inputs exceed L2 (126 MB); no flush"},
+                              "roofline": sub["roofline"], "c4": sub, "clocks": clk}))
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.workload == "bwd":
         # the training backward alone (one GPU; ranks other than 0 run nothing)
         if rank != 0:
@@ -769,30 +1040,32 @@ def main():
         clocks.start()
         r = run_c5(dev, 512, max(3, args.warmup))
         clk = clocks.stop()
+        sub = c5_summary(r)
         line = {"metric": "C5 e2e prefill tokens/s", "value": r["B"] * r["S"] / (r["prefill_ms"] / 1e3),
                 "unit": "tokens/s", "n_gpus": 1, "steps": 1, "warmup": 1,
                 "ms_per_step": r["prefill_ms"], "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic (random-init weights, visual embeddings ~N(0,0.02))",
-                "config": {"workload": "config5_e2e_decoder", "layers": 12, "hidden": 1280,
-                           "heads": 10, "experts": "64 routed top-6 + 2 shared", "batch": r["B"],
-                           "prompt_tokens": r["S"], "decode_steps": r["decode_steps"],
-                           "block_size": 64, "local_blocks": 4, "routed_k": 16,
-                           "document": "100 pages x (marker + 272 image tokens) + 256 text",
-                           "candidates": "page-aware (PageIsolationState, once per forward)"},
-                "prefill": {"ms": r["prefill_ms"], "attention_ms": r["attn_ms"],
-                            "attention_fraction": r["attn_ms"] / r["prefill_ms"],
-                            "attention_scope": "per layer: RoPE + K/V store, index front end, "
-                                               "k-bar, routing, paged attention; page state "
-                                               "once per forward outside the layer events"},
-                "decode": {"ms_per_step": r["decode_ms"],
-                           "tokens_per_s": r["B"] / (r["decode_ms"] / 1e3),
-                           "graph": "one CUDA graph per step, 512 replays"},
+                "config": sub["config"], "prefill": sub["prefill"], "decode": sub["decode"],
                 "finite_logits": r["finite"], "clocks": clk}
         print(json.dumps(line))
         return
 
-    st = run_prefill(cfg, dev, args.steps, args.warmup, rank, world, not args.no_graph)
+    # the output gather of N > 1 runs inside the timed step: fused into the
+    # attention kernel (peer stores over NVLink, then one NCCL completion word),
+    # or as an NCCL all-gather after it (--gather nccl)
+    gather, full_out = None, None
+    if world > 1 and args.gather != "none":
+        full_out = torch.empty((world * cfg["B"], cfg["H"], cfg["S"], cfg["D"]),
+                               dtype=torch.bfloat16, device=dev)
+        if args.gather == "fused":
+            from ananta_ocr_b200.peer import PeerGather
+            gather = PeerGather(full_out)
+    st = run_prefill(cfg, dev, args.steps, args.warmup, rank, world, not args.no_graph,
+                     gather=gather)
+    if world > 1 and args.gather == "nccl":
+        shard = st["ws"]["out"]
+        st["step"].post = lambda: dist.all_gather_into_tensor(full_out, shard)
     dec = None
     if not args.no_decode:
         dec = run_decode_setup(C3, dev, 77 + rank)
@@ -854,9 +1127,9 @@ def main():
     tokens_per_rank = cfg["B"] * cfg["S"]
     value = tokens_per_rank * world / (t_step / 1e3)
 
-    # ---------------- the one collective: all-gather of the output shards -------------
-    # (outside the timed step, reported on its own; NCCL over NVLink)
-    gather = None
+    # ---------------- reference figure: the same gather as a plain NCCL all-gather ----
+    # (timed on its own, outside the step)
+    nccl_gather = None
     if world > 1:
         shard = st["ws"]["out"]
         full = torch.empty((world,) + tuple(shard.shape), dtype=shard.dtype, device=dev)
@@ -872,7 +1145,7 @@ def main():
         gt = torch.tensor([g0.elapsed_time(g1)], device=dev, dtype=torch.float64)
         dist.all_reduce(gt, op=dist.ReduceOp.MAX)
         gbytes = full.numel() * full.element_size()
-        gather = {"ms": float(gt[0]), "bytes": gbytes, "bus_gbs": gbytes * (world - 1) / world / float(gt[0]) / 1e6,
+        nccl_gather = {"ms": float(gt[0]), "bytes": gbytes, "bus_gbs": gbytes * (world - 1) / world / float(gt[0]) / 1e6,
                   "op": "all_gather_into_tensor (NCCL)"}
         del full
 
@@ -940,8 +1213,23 @@ def main():
     bw_res = None
     if not args.no_backward and args.workload == "c2":
         bw_res = run_backward(cfg, dev, args.steps, args.warmup)
+    b32_res = None
+    if not args.no_block32 and args.workload == "c2":
+        b32_res = run_prefill_on(C2_BS32, st, dev, args.steps, args.warmup)
+    c4_res = None
+    if not args.no_c4 and args.workload == "c2":
+        # every rank takes part (strong scaling of config 4 with the gather)
+        torch.cuda.empty_cache()
+        c4_res = run_c4(dev, rank, world, 3, 3, args.gather if args.gather != "none" else "fused")
+        torch.cuda.empty_cache()
+    c5_res = None
+    if not args.no_c5 and args.workload == "c2" and world == 1:
+        # the whole decoder on one GPU (replicas only at N > 1, not timed there)
+        c5_res = c5_summary(run_c5(dev, 64, max(3, args.warmup)))
 
     peaks, peak_kind = load_peaks()
+    if gather is not None:
+        gather.close()
     if rank != 0:
         if world > 1:
             dist.barrier()
@@ -962,7 +1250,14 @@ def main():
         "config": {"workload": cfg["name"], "sequences_per_gpu": cfg["B"], "heads": cfg["H"],
                    "seq_len": cfg["S"], "head_dim": cfg["D"], "block_size": cfg["bs"],
                    "local_blocks": cfg["lb"], "routed_k": cfg["K"], "parallelism": f"shard{world}",
-                   "l2": "inputs exceed L2 (126 MB); no flush"},
+                   "l2": "inputs exceed L2 (126 MB); no flush",
+                   "output_gather_in_step": (
+                       "none (one GPU)" if world == 1 else
+                       {"fused": "fused into the attention kernel: every output row stored into "
+                                 "every rank's gathered tensor over NVLink, then one NCCL "
+                                 "completion word",
+                        "nccl": "NCCL all_gather_into_tensor after the attention",
+                        "none": "none (excluded)"}[args.gather])},
         "breakdown_ms": {"route": route_ms, "attention": attn_ms},
         "prefill": {"alg_tflops": achieved, "executed_tflops": st["executed"] / (attn_ms / 1e3) / 1e12,
                     "alg_flops_per_step": st["alg"], "executed_flops_per_step": st["executed"]},
@@ -971,7 +1266,7 @@ def main():
                      "kernel": "prefill_kernel (+plan_kernel), algorithmic FLOPs / CUDA-event time",
                      "peak_source": f"{peak_kind} bf16_tflops"},
         "gpu_launches": launches,
-        "output_gather": gather,
+        "nccl_all_gather_alone": nccl_gather,
         "clocks": clk,
     }
     if dec_res is not None:
@@ -1031,10 +1326,32 @@ def main():
                                                      "bwd_tc_kernel (tcgen05) + bwd_dq_convert",
                          "flops_per_launch": bw_res["flops"],
                          "peak_source": f"{peak_kind} bf16_tflops"}}
+    if b32_res is not None:
+        peak = peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
+        c = C2_BS32
+        tf = b32_res["alg"] / (b32_res["attn_ms"] / 1e3) / 1e12
+        line["block32"] = {
+            "workload": c["name"], "block_size": c["bs"], "local_blocks": c["lb"],
+            "routed_k": c["K"], "entmax_window": c["topm"],
+            "tokens_per_s": b32_res["tokens"] / ((b32_res["route_ms"] + b32_res["attn_ms"]) / 1e3),
+            "route_ms": b32_res["route_ms"], "attn_ms": b32_res["attn_ms"],
+            "alg_tflops": tf, "executed_tflops": b32_res["executed"] / (b32_res["attn_ms"] / 1e3) / 1e12,
+            "alg_flops_per_step": b32_res["alg"], "executed_flops_per_step": b32_res["executed"],
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
+                         "frac": tf / peak,
+                         "kernel": "prefill_kernel (32-token blocks, two per key tile) + plan_kernel",
+                         "peak_source": f"{peak_kind} bf16_tflops"}}
+    if c4_res is not None:
+        line["c4"] = c4_summary(c4_res, world, args.gather, peaks, peak_kind)
+    if c5_res is not None:
+        line["c5"] = c5_res
     if e2e is not None:
         line["e2e"] = e2e
     if not args.no_cpu and world == 1:   # the CPU baseline is timed at N = 1 only
-        line["cpu_baseline"] = cpu_baseline(cfg, n_tokens=256)
+        runs = [cpu_baseline(cfg, n_tokens=4096) for _ in range(3)]
+        runs.sort(key=lambda r: r["value"])
+        line["cpu_baseline"] = runs[1]
+        line["cpu_baseline"]["sample"] += " (median of 3)"
         line["cpu_baseline"].pop("seconds", None)
     print(json.dumps(line))
     if world > 1:

@@ -474,9 +474,35 @@ typedef struct {
   void* workspace;
   size_t workspace_bytes;
   DashDeviceError* device_error;
+  /* fused output gather (optional): n_peers device pointers (a device array)
+   * to other ranks' copies of `out` (same strides, e.g. from dash_peer_import);
+   * every output row is also stored there (posted stores, complete when the
+   * grid completes).  The caller orders a cross-rank completion step after
+   * the call on the same stream. */
+  void* const* out_peers;
+  int32_t n_peers;
+  int32_t pad1;
 } DashPrefillArgs;
 size_t dash_prefill_workspace_size(const DashPrefillArgs* args);
 int dash_prefill_attn(const DashPrefillArgs* args, dash_stream_t stream);
+
+/* ---------------------------------------------------------------------- */
+/* Peer device memory for the fused output gather (no reference counterpart:
+ * the reference runs on one GPU; BASELINE's multi-GPU split gathers the output
+ * shards over NVLink).  A rank exports a device buffer as a CUDA IPC handle of
+ * the allocation holding it plus the buffer's offset; another rank of the same
+ * node imports it (the allocation is opened once per process) and gets a
+ * device pointer it may pass as a DashPrefillArgs.out_peers entry.  Handles are
+ * plain bytes and travel between processes through the host.  close releases
+ * one import; the mapping goes when its last import is closed.              */
+typedef struct {
+  char handle[64];       /* cudaIpcMemHandle_t of the allocation */
+  int64_t offset;        /* buffer start inside the allocation */
+  int64_t alloc_bytes;   /* allocation size (bounds check on import) */
+} DashPeerHandle;
+int dash_peer_export(const void* ptr, DashPeerHandle* out);
+int dash_peer_import(const DashPeerHandle* handle, void** ptr);
+int dash_peer_close(void* ptr);
 
 /* ---------------------------------------------------------------------- */
 /* Serving-step plans, computed on the device in one launch (no host sync).
@@ -696,7 +722,7 @@ int dash_count_launches(int reset);          /* kernels launched by this library
  * DashDecodeArgs, DashDeviceError, DashPageIdsArgs, DashPageStateArgs,
  * DashPageAllowArgs, DashPageDecodeArgs, DashBlockAnyArgs, DashPageBlocksArgs,
  * DashIndexProjArgs, DashRopeKVArgs, DashAttnBwdArgs, DashEntmaxArgs,
- * DashServingPlanArgs.  Lets a binding
+ * DashServingPlanArgs, DashPeerHandle.  Lets a binding
  * verify its struct layouts; returns the number of sizes available. */
 int dash_abi_sizes(int64_t* out, int n);
 /* Self-test of the bounded waits every kernel uses (no reference counterpart):

@@ -13,15 +13,31 @@ from ananta_ocr_b200.e2e_decoder import DashDecoder, DecoderConfig
 
 pytestmark = pytest.mark.gpu
 
-CFG = DecoderConfig(hidden=256, heads=2, kv_heads=2, layers=3, vocab=1000, dense_ffn=512,
-                    moe_ffn=128, experts=8, topk=2, shared=1, block_size=64, local_blocks=2, K=4)
+SMALL = dict(hidden=256, heads=2, kv_heads=2, layers=3, vocab=1000, dense_ffn=512, moe_ffn=128,
+             experts=8, topk=2, shared=1)
+CFGS = {
+    # 64-token blocks, 2-block window, 4 routed blocks
+    "bs64": DecoderConfig(**SMALL, block_size=64, local_blocks=2, K=4, topm=4, slots=4),
+    # the checkpoint's DASH settings: 32-token blocks (one page each), 4-block
+    # window, 12 routed blocks out of an entmax window of 16, 16 output slots
+    "bs32": DecoderConfig(**SMALL),
+}
+CFG = CFGS["bs64"]
+
+
+@pytest.fixture(params=sorted(CFGS))
+def cfg(request):
+    global CFG
+    CFG = CFGS[request.param]
+    yield CFG
+    CFG = CFGS["bs64"]
 
 
 def make(seed=3):
     return DashDecoder(CFG, batch=2, max_len=420, device=torch.device("cuda"), seed=seed)
 
 
-def test_prefill_plus_decode_equals_longer_prefill():
+def test_prefill_plus_decode_equals_longer_prefill(cfg):
     S = 333
     ids = torch.randint(0, CFG.vocab, (2, S + 1), generator=torch.Generator().manual_seed(0)).cuda()
     full = make()
@@ -36,7 +52,7 @@ def test_prefill_plus_decode_equals_longer_prefill():
     assert torch.equal(part.seq_lens, torch.full_like(part.seq_lens, S + 1))
 
 
-def test_graph_decode_equals_eager():
+def test_graph_decode_equals_eager(cfg):
     S = 200
     ids = torch.randint(0, CFG.vocab, (2, S), generator=torch.Generator().manual_seed(1)).cuda()
     a, b = make(5), make(5)
@@ -89,7 +105,7 @@ def make_paged(seed=3, max_len=420):
                        page_cfg=PAGE_CFG)
 
 
-def test_page_aware_prefill_plus_decode_equals_longer_prefill():
+def test_page_aware_prefill_plus_decode_equals_longer_prefill(cfg):
     S = 333
     ids = doc_ids(S + 1, 6, 4)
     full = make_paged()
@@ -111,7 +127,7 @@ def test_page_aware_prefill_plus_decode_equals_longer_prefill():
     assert torch.equal(part.pst._blk_hi, full.pst._blk_hi)
 
 
-def test_page_domain_equals_reference_allow_mask():
+def test_page_domain_equals_reference_allow_mask(cfg):
     """The compact page domain routes exactly as the reference's dense allow
     masks (``build_query_allow`` in prefill, ``decode_allow_fused`` in decode)
     through the whole model: equal routes, equal logits; and the page-aware

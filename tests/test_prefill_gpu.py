@@ -236,11 +236,13 @@ def test_paged_prefill_with_prefix(bs, lb):
     assert_close_bf16(out.float().cpu().numpy(), ref)
 
 
-def test_prefill_config4_geometry_sampled_rows():
+@pytest.mark.parametrize("H,S", [(16, 32768), (4, 131072)])
+def test_prefill_config4_geometry_sampled_rows(H, S):
     """BASELINE config 4 geometry (block 128, window 8 blocks = 1024 tokens,
-    k=64, 16 heads) on one 32,768-token sequence: router + attention on the GPU,
-    routes bit-exact, output vs the oracle on sampled rows."""
-    B, H, S, D, bs, lb, K = 1, 16, 32768, 128, 128, 8, 64
+    k=64) on one sequence of 32,768 tokens (16 heads) and of the full 131,072
+    tokens (4 heads, 1,024 blocks): router + attention on the GPU, routes
+    bit-exact, output vs the oracle on sampled rows."""
+    B, D, bs, lb, K = 1, 128, 128, 8, 64
     q, k, v, iq, ik = O.make_prefill_inputs(8, B, H, S, D, S // 273, 273, 0.2)
     out, idx, bias = MD.dash_prefill_forward(
         torch.from_numpy(q).cuda().bfloat16(), torch.from_numpy(k).cuda().bfloat16(),
