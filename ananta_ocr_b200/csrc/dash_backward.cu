@@ -296,11 +296,16 @@ __global__ void __launch_bounds__(kThreads) bwd_dkv_kernel(DashAttnBwdArgs a, in
 #pragma unroll
   for (int c = 0; c < 64; ++c) { dk[c] = 0.f; dv[c] = 0.f; }
 
+  // a 64-key tile holds at most two blocks (block sizes are multiples of 32):
+  // b and b2 (= b when the tile lies in one block); keys from j2 on are b2's
+  const int b2 = min(key0 + KT - 1, T - 1) / a.block_size;
+  const int j2 = b2 != b ? b2 * a.block_size - key0 : KT;
   const uint32_t* fl = a.flags + ((int64_t)s * nblk + b) * words;
+  const uint32_t* fl2 = a.flags + ((int64_t)s * nblk + b2) * words;
   // rows whose window reaches a key of the tile: [key0, key0 + KT - 1 + LW - 1]
   const int64_t loc_end = min((int64_t)key0 + KT - 1 + LW - 1, (int64_t)T - 1);
   for (int w = key0 >> 5; w < words; ++w) {
-    uint32_t m = fl[w];
+    uint32_t m = fl[w] | fl2[w];
     const int64_t r0 = (int64_t)w * 32;
     if (r0 <= loc_end) {
       const int64_t lo = max(r0, (int64_t)key0), hi = min(r0 + 31, loc_end);
@@ -317,6 +322,7 @@ __global__ void __launch_bounds__(kThreads) bwd_dkv_kernel(DashAttnBwdArgs a, in
       const int i = (int)(r0 + bit);
       if (i >= T) break;
       const bool routed = (fl[w] >> bit) & 1u;
+      const bool routed2 = b2 != b && ((fl2[w] >> bit) & 1u);
       const int64_t row = (int64_t)s * T + i;
       __syncthreads();
 #pragma unroll
@@ -329,18 +335,20 @@ __global__ void __launch_bounds__(kThreads) bwd_dkv_kernel(DashAttnBwdArgs a, in
         lse_s[tid] = a.lse[row * HQ + h * G + tid];
         del_s[tid] = a.delta[row * HQ + h * G + tid];
       }
-      if (tid < 32) {
-        // bias of the first slot holding b
+      if (tid < 64) {
+        // bias of the first slot holding b (warp 0) / b2 (warp 1)
+        const int bb = tid < 32 ? b : b2;
+        const bool rt = tid < 32 ? routed : routed2;
         float bias = 0.f;
-        if (routed && a.bias) {
+        if (rt && a.bias) {
           int first = INT_MAX;
           for (int jj = lane; jj < a.K; jj += 32)
-            if (a.idx[row * a.K + jj] == b) { first = jj; break; }
+            if (a.idx[row * a.K + jj] == bb) { first = jj; break; }
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) first = min(first, __shfl_xor_sync(0xffffffffu, first, o));
           if (first != INT_MAX) bias = a.bias[row * a.K + first];
         }
-        if (lane == 0) misc[0] = bias;
+        if (lane == 0) misc[tid >> 5] = bias;
       }
       __syncthreads();
       partial_scores<G>(Ks, Vs, Qs, Ds, part);
@@ -348,9 +356,10 @@ __global__ void __launch_bounds__(kThreads) bwd_dkv_kernel(DashAttnBwdArgs a, in
       if (tid < KT) {
         const int key = key0 + tid;
         const int64_t ls = (int64_t)i - LW + 1;
+        const bool second = tid >= j2;
         const bool local = key < T && key <= i && key >= ls;
-        const bool remote = routed && key < T && key < ls;
-        const float bias = remote ? misc[0] : 0.f;
+        const bool remote = (second ? routed2 : routed) && key < T && key < ls;
+        const float bias = remote ? misc[second ? 1 : 0] : 0.f;
 #pragma unroll
         for (int g = 0; g < G; ++g) {
           const float sc = part[g * KT + tid] + part[G * KT + g * KT + tid];

@@ -6,7 +6,7 @@
 // rows, so no query row is multiplied against a block it did not route:
 //
 // Work unit: one CTA per (128-key tile, kv head, sequence).  The tile's rows
-// are the query rows that routed one of its (at most two) blocks with a key
+// are the query rows that routed one of its (at most four) blocks with a key
 // below their local window (per-block row bitmask of bwd_flags_kernel) plus
 // the rows whose window reaches a key of the tile.  They are processed in
 // batches of 128 slots (a slot = a query row x one of the G query heads of
@@ -51,16 +51,19 @@ constexpr int OFF_Q = 65536;             // [2 halves][128 slots][128 B]
 constexpr int OFF_DO = 98304;
 constexpr int OFF_DS = 131072;           // dS^T MN-major: [2 slot halves][128 keys][128 B]
 constexpr int OFF_META = 163840;
+// A tile of 128 keys holds up to QB blocks (block sizes are multiples of 32,
+// so every 32-key warp quarter lies in one block).
+constexpr int QB = 4;
 // Per-batch slot meta, double-buffered (the producer fills batch b+1 while
-// batch b is computed): a = {pos, routed flags, cloc, delta} and b = {clA, clB}
-// (read by the softmax), global row, query head, slot of block A / B.
+// batch b is computed): a = {pos, routed bits (one per tile block) | seg << 4,
+// cloc, delta} and b = the remote logit offset of each tile block (read by
+// the softmax), global row, query head, routed-list slot of each tile block.
 struct SlotMeta {
   int4 a[NS];
-  float2 b[NS];
+  float4 b[NS];
   int row[NS];
   int hq[NS];
-  int sA[NS];
-  int sB[NS];
+  int4 sl[NS];
   int ns;
   int pad[3];
 };
@@ -181,8 +184,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int h = blockIdx.y;
   const int key0 = tl * TK;
   const int bs = a.block_size, LW = a.local_window;
-  const int bA = key0 / bs, bB = min(key0 + TK - 1, T - 1) / bs;
-  const int jB = bB != bA ? bB * bs - key0 : TK;        // first tile key of block B
+  const int bA = key0 / bs;                                  // first block of the tile
+  const int nbt = min(key0 + TK - 1, T - 1) / bs - bA + 1;  // blocks in the tile (<= QB)
   // index head of this kv head; its routes are rows (s*HI + ih)*T + t
   const int HI = a.n_index_heads > 1 ? a.n_index_heads : 1;
   const int ih = h * HI / H;
@@ -224,8 +227,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (warp == kProdWarp) {
     // ===================== producer: slot lists + per-slot meta =====================
-    const uint32_t* flA = a.flags + (((int64_t)s * HI + ih) * nblk + bA) * words;
-    const uint32_t* flB = a.flags + (((int64_t)s * HI + ih) * nblk + bB) * words;
+    const uint32_t* fl0 = a.flags + (((int64_t)s * HI + ih) * nblk + bA) * words;   // block bA + q at + q*words
     const int64_t loc_end = min((int64_t)key0 + TK - 1 + LW - 1, (int64_t)T - 1);
     int next_row = key0;                 // first row not yet taken (uniform)
     for (int b = 0;; ++b) {
@@ -238,7 +240,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int w = (next_row >> 5) + lane;
         uint32_t m = 0u;
         if (w < words) {
-          m = flA[w] | (bB != bA ? flB[w] : 0u);
+          for (int q = 0; q < nbt; ++q) m |= fl0[(int64_t)q * words + w];
           const int64_t r0 = (int64_t)w * 32;
           const int64_t lo = max(r0, (int64_t)key0), hi = min(r0 + 31, loc_end);
           if (lo <= hi) {
@@ -289,39 +291,46 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int hq = live ? M.hq[n] : 0;
         const int64_t row = (int64_t)s * T + i;
         const int64_t rr = row + rr_shift;     // row of this index head's routes
-        int routed = 0, sA = -1, sB = -1;
-        float lse = 0.f, delta = 0.f, biasA = 0.f, biasB = 0.f;
+        int routed = 0;
+        int slot[QB] = {-1, -1, -1, -1};
+        float bias[QB] = {0.f, 0.f, 0.f, 0.f};
+        float lse = 0.f, delta = 0.f;
         if (live) {
           lse = a.lse[row * HQ + hq];
           delta = a.delta[row * HQ + hq];
-          if ((flA[i >> 5] >> (i & 31)) & 1u) routed |= 1;
-          if (bB != bA && ((flB[i >> 5] >> (i & 31)) & 1u)) routed |= 2;
-          // first slot of bA / bB: 16 independent loads per step
+#pragma unroll
+          for (int q = 0; q < QB; ++q)
+            if (q < nbt && ((fl0[(int64_t)q * words + (i >> 5)] >> (i & 31)) & 1u)) routed |= 1 << q;
+          // first slot of each routed tile block: 16 independent loads per step
           const int32_t* ids = a.idx + rr * a.K;
-          for (int j0 = 0; j0 < a.K && (((routed & 1) && sA < 0) || ((routed & 2) && sB < 0)); j0 += 16) {
+          int found = 0;
+          for (int j0 = 0; j0 < a.K && found != routed; j0 += 16) {
             int v[16];
 #pragma unroll
             for (int u = 0; u < 16; ++u) v[u] = j0 + u < a.K ? ids[j0 + u] : -1;
 #pragma unroll
             for (int u = 0; u < 16; ++u) {
-              if ((routed & 1) && sA < 0 && v[u] == bA) sA = j0 + u;
-              if ((routed & 2) && sB < 0 && v[u] == bB) sB = j0 + u;
+              const int q = v[u] - bA;
+#pragma unroll
+              for (int qq = 0; qq < QB; ++qq)
+                if (q == qq && ((routed >> qq) & 1) && !((found >> qq) & 1)) { slot[qq] = j0 + u; found |= 1 << qq; }
             }
           }
           if (a.bias) {
-            if (sA >= 0) biasA = a.bias[rr * a.K + sA];
-            if (sB >= 0) biasB = a.bias[rr * a.K + sB];
+#pragma unroll
+            for (int q = 0; q < QB; ++q)
+              if (slot[q] >= 0) bias[q] = a.bias[rr * a.K + slot[q]];
           }
         }
         M.row[n] = (int)row;
         M.hq[n] = hq;
-        M.sA[n] = sA;
-        M.sB[n] = sB;
+        M.sl[n] = make_int4(slot[0], slot[1], slot[2], slot[3]);
         // a padding slot's position keeps every key out
         const int seg = (live && a.seg_start) ? a.seg_start[row] : 0;
-        M.a[n] = make_int4(live ? i : INT_MIN / 2, routed | (seg << 2), __float_as_int(-lse * LOG2E),
+        M.a[n] = make_int4(live ? i : INT_MIN / 2, routed | (seg << 4), __float_as_int(-lse * LOG2E),
                            __float_as_int(delta));
-        M.b[n] = make_float2((biasA - lse) * LOG2E, (biasB - lse) * LOG2E);
+        M.b[n] = make_float4((bias[0] - lse) * LOG2E, (bias[1] - lse) * LOG2E, (bias[2] - lse) * LOG2E,
+                             (bias[3] - lse) * LOG2E);
       }
       if (lane == 0) M.ns = ns;
       __threadfence_block();
@@ -370,8 +379,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
     const float sl2 = a.scale * LOG2E;
     const int key = key0 + kl;
-    const bool keyB = kl >= jB;
-    const int rmask = keyB ? 2 : 1;
+    const int kb = min(key, T - 1) / bs - bA;     // this key's block within the tile
+    const int rmask = 1 << kb;
     int nb = 0;
     bool alive = true;
     while (alive) {
@@ -441,12 +450,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int u = 0; u < 2; ++u) {
               const int n = col + e + u;
               const int4 ma = M.a[n];
-              const float2 mb = M.b[n];
+              const float mb = reinterpret_cast<const float*>(M.b)[n * QB + kb];
               const int d = ma.x - key;
-              const bool inseg = !SEG || key >= (ma.y >> 2);
+              const bool inseg = !SEG || key >= (ma.y >> 4);
               const bool local = d >= 0 && d < LW && inseg;
               const bool remote = d >= LW && (ma.y & rmask) && inseg;
-              const float c = remote ? (keyB ? mb.y : mb.x) : __int_as_float(ma.z);
+              const float c = remote ? mb : __int_as_float(ma.z);
               const float p = (local || remote) ? fast_exp2(fmaf(x[e + u], sl2, c)) : 0.f;
               const float ds = (local || remote) ? p * (y[e + u] - __int_as_float(ma.w)) : 0.f;
               pv[u] = p;
@@ -478,15 +487,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       math_bar();
       // ---- slot-bias gradient of slot tid ----
       if (tid < ns && a.d_bias) {
-        float sA_sum = 0.f, sB_sum = 0.f;
+        // warp quarter w (keys key0 + 32w ..) lies in tile block qb(w)
+        float sum[QB] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
-          if (w * 32 >= jB) sB_sum += m_dsum[w * NS + tid];
-          else sA_sum += m_dsum[w * NS + tid];
+          const int qb = min(key0 + 32 * w, T - 1) / bs - bA;
+          const float v = m_dsum[w * NS + tid];
+#pragma unroll
+          for (int q = 0; q < QB; ++q) sum[q] += q == qb ? v : 0.f;
         }
         const int64_t row = M.row[tid] + rr_shift;
-        if (M.sA[tid] >= 0) red_add(a.d_bias + row * a.K + M.sA[tid], sA_sum);
-        if (M.sB[tid] >= 0) red_add(a.d_bias + row * a.K + M.sB[tid], sB_sum);
+        const int4 sl = M.sl[tid];
+        const int slq[QB] = {sl.x, sl.y, sl.z, sl.w};
+#pragma unroll
+        for (int q = 0; q < QB; ++q)
+          if (slq[q] >= 0) red_add(a.d_bias + row * a.K + slq[q], sum[q]);
       }
       ++nb;
     }

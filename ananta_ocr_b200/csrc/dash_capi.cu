@@ -47,10 +47,12 @@ static int check_seqs(const DashSeqs& q) {
   return DASH_OK;
 }
 
-static int check_kv(const DashKV& kv, int n_heads, int block_size) {
+static int check_kv(const DashKV& kv, int n_heads, int block_size, bool allow_f32 = false) {
   if (!kv.k || !kv.v) return set_error(DASH_ERR_INVALID, "null K/V pointer");
-  if (kv.dtype != DASH_DTYPE_BF16 && kv.dtype != DASH_DTYPE_F16)
-    return set_error(DASH_ERR_UNSUPPORTED, "K/V dtype must be bf16 or fp16");
+  if (kv.dtype != DASH_DTYPE_BF16 && kv.dtype != DASH_DTYPE_F16 &&
+      !(allow_f32 && kv.dtype == DASH_DTYPE_F32 && !kv.block_table))
+    return set_error(DASH_ERR_UNSUPPORTED, allow_f32 ? "K/V dtype must be bf16 or fp16 (fp32: contiguous only)"
+                                                     : "K/V dtype must be bf16 or fp16");
   if (kv.head_dim != 128) return set_error(DASH_ERR_UNSUPPORTED, "head_dim %d != 128", kv.head_dim);
   if (kv.n_kv_heads <= 0 || n_heads % kv.n_kv_heads != 0)
     return set_error(DASH_ERR_INVALID, "n_heads %d not a multiple of n_kv_heads %d", n_heads, kv.n_kv_heads);
@@ -206,15 +208,20 @@ size_t dash_prefill_workspace_size(const DashPrefillArgs* a) {
 int dash_prefill_attn(const DashPrefillArgs* a, dash_stream_t stream) {
   if (!a) return set_error(DASH_ERR_INVALID, "null args");
   int rc = check_seqs(a->seqs);
-  if (!rc) rc = check_kv(a->kv, a->qo.n_heads, a->block_size);
+  if (!rc) rc = check_kv(a->kv, a->qo.n_heads, a->block_size, true);
   if (!rc) rc = check_routes(a->routes, a->qo.n_heads, a->kv.n_kv_heads);
   if (!rc) rc = check_qo(a->qo);
   if (rc) return rc;
   const int G = a->qo.n_heads / a->kv.n_kv_heads;
-  if (G != 1 && G != 2 && G != 4 && G != 8 && G != 16)
-    return set_error(DASH_ERR_UNSUPPORTED, "query heads per kv head %d not in {1,2,4,8,16}", G);
-  if (a->block_size != 32 && (a->block_size % 64 != 0 || a->block_size > 256))
-    return set_error(DASH_ERR_UNSUPPORTED, "prefill block_size %d not in {32,64,128,192,256}", a->block_size);
+  if (a->kv.dtype != DASH_DTYPE_F32) {
+    // tensor-core kernel: 128-row tiles of 128/G tokens, 64-key tiles
+    if (G != 1 && G != 2 && G != 4 && G != 8 && G != 16)
+      return set_error(DASH_ERR_UNSUPPORTED, "query heads per kv head %d not in {1,2,4,8,16}", G);
+    if (a->block_size != 32 && (a->block_size % 64 != 0 || a->block_size > 256))
+      return set_error(DASH_ERR_UNSUPPORTED, "prefill block_size %d not in {32,64,128,192,256}", a->block_size);
+  } else if (G > 128) {
+    return set_error(DASH_ERR_UNSUPPORTED, "query heads per kv head %d > 128", G);
+  }
   if (a->local_window < 0) return set_error(DASH_ERR_INVALID, "local_window must be >= 0");
   if (a->kv.block_table == nullptr && a->seqs.kv_len_fixed <= 0)
     return set_error(DASH_ERR_INVALID, "contiguous K/V needs kv_len_fixed (allocated length)");
@@ -382,8 +389,8 @@ static int check_attn_bwd(const DashAttnBwdArgs* a) {
   if (!a) return set_error(DASH_ERR_INVALID, "null args");
   if (a->n_seq < 0 || a->seq_len < 0) return set_error(DASH_ERR_INVALID, "negative size");
   if (a->head_dim != 128) return set_error(DASH_ERR_UNSUPPORTED, "head_dim %d != 128", a->head_dim);
-  if (a->block_size <= 0 || a->block_size % 64)
-    return set_error(DASH_ERR_UNSUPPORTED, "block_size %d must be a positive multiple of 64", a->block_size);
+  if (a->block_size <= 0 || a->block_size % 32)
+    return set_error(DASH_ERR_UNSUPPORTED, "block_size %d must be a positive multiple of 32", a->block_size);
   if (a->local_window <= 0) return set_error(DASH_ERR_INVALID, "local_window must be > 0");
   if (a->K < 0 || a->K > 256) return set_error(DASH_ERR_UNSUPPORTED, "K %d not in [0, 256]", a->K);
   if (a->n_kv_heads <= 0 || a->n_heads % a->n_kv_heads)

@@ -30,6 +30,7 @@
 #include <climits>
 #include "dash_common.cuh"
 #include "dash_internal.h"
+#include "dash_prefill_plan.cuh"
 
 namespace dash {
 
@@ -63,33 +64,6 @@ constexpr uint32_t TMEM_COLS = 512;               // per query tile: S0 | S1 | O
 constexpr float kGrowLog2 = 32.0f;
 constexpr float kGrowP = 4294967296.0f;
 constexpr int kPlanMaxK = 256;                    // routed slots per row
-
-struct PrefillPlan {
-  const int32_t* cidx;     // canonical lists [nih][n_rows][K]
-  const float* cbias;
-  const uint32_t* tmask;   // per-tile unions [nih][n_tiles][nwords]
-  const float* rowmax;     // largest kept bias per row [nih][n_rows] (-inf: none)
-  int64_t n_rows;
-  int32_t nwords;
-  int32_t tiles_per_seq;
-  int32_t G;               // query heads per kv head
-  int32_t TT;              // tokens per tile (= 128 / G)
-  int32_t paged;
-  int32_t nblk_cap;
-};
-
-__device__ __forceinline__ int kv_len_of(const DashSeqs& q, int s) {
-  return q.kv_len ? q.kv_len[s] : q.kv_len_fixed;
-}
-__device__ __forceinline__ int q_len_of(const DashSeqs& q, int s) {
-  return q.q_start ? q.q_start[s + 1] - q.q_start[s] : q.q_len_fixed;
-}
-__device__ __forceinline__ int pos0_of(const DashSeqs& q, int s) {
-  return q.pos0 ? q.pos0[s] : kv_len_of(q, s) - q_len_of(q, s);
-}
-__device__ __forceinline__ int64_t row_base(const DashSeqs& q, int s) {
-  return q.q_start ? (int64_t)q.q_start[s] : (int64_t)s * q.q_len_fixed;
-}
 
 // ---------------------------------------------------------------------------
 // plan_kernel: one CTA per (query tile, index head), one warp per token row
@@ -922,7 +896,7 @@ size_t prefill_workspace(const DashPrefillArgs& a, int64_t n_rows) {
   plan_geometry(a, n_rows, p);
   const int nih = a.routes.n_index_heads > 0 ? a.routes.n_index_heads : 1;
   const size_t lists = round256((size_t)nih * n_rows * a.routes.K * 4);
-  const size_t blists = a.block_size == 32 ? 2 * lists : lists;
+  const size_t blists = (a.block_size == 32 && a.kv.dtype != DASH_DTYPE_F32) ? 2 * lists : lists;
   size_t masks = (size_t)nih * a.seqs.n_seq * p.tiles_per_seq * p.nwords * 4;
   return lists + blists + round256(masks) + (size_t)nih * n_rows * 4;
 }
@@ -935,7 +909,10 @@ int launch_prefill(const DashPrefillArgs& a, int64_t n_rows, cudaStream_t st) {
     return set_error(DASH_ERR_UNSUPPORTED, "too many blocks per sequence (%d > %d)", p.nblk_cap,
                      MAX_MASK_WORDS * 32);
   const int nih = a.routes.n_index_heads > 0 ? a.routes.n_index_heads : 1;
-  const bool pair = a.block_size == 32;
+  // 32-token blocks pair up in the tensor-core kernel's 64-key tiles; the
+  // fp32 kernel reads plain per-block lists
+  const bool f32 = a.kv.dtype == DASH_DTYPE_F32;
+  const bool pair = a.block_size == 32 && !f32;
   const size_t lists = round256((size_t)nih * n_rows * a.routes.K * 4);
   const size_t blists = pair ? 2 * lists : lists;
   uint8_t* ws = reinterpret_cast<uint8_t*>(a.workspace);
@@ -966,6 +943,7 @@ int launch_prefill(const DashPrefillArgs& a, int64_t n_rows, cudaStream_t st) {
     int rc = check_launch("plan_kernel");
     if (rc) return rc;
   }
+  if (f32) return launch_prefill_f32(a, p, st);
   CUtensorMap mk, mv;
   int rc = make_kv_map(&mk, a.kv.k, a, p.paged);
   if (rc) return rc;

@@ -23,7 +23,13 @@ SPARSE_E2E_SENTINEL = 1
 
 
 def _as_kernel_dtype(t: torch.Tensor) -> torch.Tensor:
-    # the tensor-core path computes in bf16/fp16 with fp32 accumulation
+    # bf16/fp16 run on the tensor-core kernel (fp32 accumulation), fp32 on the
+    # fp32 CUDA-core kernel (every product and sum fp32); others compute in fp32
+    return t if t.dtype in (torch.bfloat16, torch.float16, torch.float32) else t.to(torch.float32)
+
+
+def _as_tc_dtype(t: torch.Tensor) -> torch.Tensor:
+    # tensor-core dtype (bf16 unless fp16), for paths that have no fp32 kernel
     return t if t.dtype in (torch.bfloat16, torch.float16) else t.to(torch.bfloat16)
 
 

@@ -18,7 +18,7 @@ from __future__ import annotations
 import torch
 
 from . import ops
-from .sparse_gather_e2e_triton import _as_kernel_dtype
+from .sparse_gather_e2e_triton import _as_kernel_dtype, _as_tc_dtype
 
 SPARSE_BLOCK_SIZE_SENTINEL = 128
 
@@ -72,11 +72,13 @@ class _TritonGatherAttnFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, sel, seg, block_size, scale, local_window):
         dt = q.dtype
-        qk = _as_kernel_dtype(q)
+        # the backward for several index heads / packed segments runs on tensor
+        # cores only: fp32 inputs compute forward and backward in bf16 here
+        qk = _as_tc_dtype(q)
         B, HQ, T, _ = q.shape
         HI = sel.shape[1]
         lse = torch.empty(B, HQ, T, dtype=torch.float32, device=q.device)
-        o = ops.gather_attention(qk, _as_kernel_dtype(k).to(qk.dtype), _as_kernel_dtype(v).to(qk.dtype),
+        o = ops.gather_attention(qk, _as_tc_dtype(k).to(qk.dtype), _as_tc_dtype(v).to(qk.dtype),
                                  sel, None, block_size=block_size, local_window=local_window,
                                  scale=scale, seg_start=seg, n_index_heads=HI, lse=lse)
         ctx.save_for_backward(q, k, v, sel, seg, o, lse)

@@ -661,7 +661,7 @@ int dash_rope_kv_write(const DashRopeKVArgs* args, dash_stream_t stream);
  * flags (dash_attn_bwd_flag_words() uint32 words) and, for bf16 / fp16,
  * dq_acc [n_seq, seq_len, n_heads, head_dim] fp32 (16-byte aligned).
  * bf16 / fp16 run on the tensor cores, fp32 on the CUDA cores.  head_dim
- * 128, block_size a multiple of 64, n_heads / n_kv_heads in {1, 2, 4, 8},
+ * 128, block_size a multiple of 32, n_heads / n_kv_heads in {1, 2, 4, 8},
  * K <= 256.                                                                 */
 typedef struct {
   const void* q; const void* k; const void* v; const void* o; const void* dout;

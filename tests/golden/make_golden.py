@@ -43,6 +43,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 from oracle.dash_oracle import make_prefill_inputs  # noqa: E402
+sys.path.insert(0, HERE)
+from golden_inputs import dash_attention_inputs  # noqa: E402
 
 REF = os.environ.get("DASH_REFERENCE", "")
 
@@ -283,6 +285,69 @@ def serving_plan_case(name, seed):
         res[f"row2req_{bs}"] = rt.prefill_row2req(cu_seqlens_q=torch.tensor(cu),
                                                   device="cpu").numpy()
         res[f"seq_{bs}"], res[f"ctx_{bs}"], res[f"bt_{bs}"], res[f"cu_{bs}"] = seq, ctx, bt, cu
+    np.savez_compressed(os.path.join(HERE, name + ".npz"), **res)
+    print(name, "saved")
+
+
+def dash_attention_case(da, name, seed):
+    """The reference's own DashAttention.forward (CPU: its dense path) and its
+    autograd backward, stage 0 head_cls and indexer, the checkpoint's block
+    size 32 with a 4-block window, K = 12, with and without a per-query
+    candidate domain."""
+    B, S, hidden, H, D = 1, 600, 256, 2, 128
+    w, x = dash_attention_inputs(seed, B, S, hidden, H, D, n_pages=3, page_tokens=150)
+    da._KS._k = 12                       # the schedule's hard top-k (eval: no anneal)
+    res = {"input_sha": sha(*w.values(), *x.values())}
+    nblk = -(-S // 32)
+    rng = np.random.default_rng(seed + 1)
+    cand = rng.random((B, S, nblk)) < 0.4
+    # scale 2.0 (the module default): smooth priors, every pick has prior > 0;
+    # scale 128 (the checkpoint's): narrow support, zero-prior picks whose
+    # order among equal priors is torch.topk's
+    for stage0, use_cand, scale in (("head_cls", False, 2.0), ("head_cls", True, 2.0),
+                                    ("indexer", False, 2.0), ("head_cls", False, 128.0)):
+        sp = dict(sparse_block_size=32, sparse_local_block=4, dash_scaling_factor=scale,
+                  dash_prior_floor=1e-2, sparse_topk_blocks=16, sparse_index_dim=128,
+                  dash_sigma=1.0)
+        cfg = types.SimpleNamespace(num_attention_heads=H, hidden_size=hidden, rms_norm_eps=1e-6,
+                                    sparse_attention_config=sp)
+        if True:
+            os.environ["DASH_STAGE0"] = stage0
+            m = da.DashAttention(cfg)
+            with torch.no_grad():
+                for n_, t in w.items():
+                    getattr(m, n_).copy_(torch.tensor(t)) if n_ == "head_cls" else \
+                        getattr(m, n_).weight.copy_(torch.tensor(t))
+            m.eval()
+            rec = {}
+            sel = m._select_and_bias
+
+            def hook(prior, cnd, nb, _sel=sel, _rec=rec):
+                out = _sel(prior, cnd, nb)
+                _rec["prior"], _rec["cand"] = prior.detach().clone(), cnd.clone()
+                _rec["topi"], _rec["bias"], _rec["valid"] = (t.detach().clone() for t in out)
+                return out
+            m._select_and_bias = hook
+            q, k, v = (torch.tensor(x[n_]).requires_grad_(True) for n_ in ("q", "k", "v"))
+            hs = torch.tensor(x["hidden"]).requires_grad_(True)
+            out = m(hs, q, k, v, position_embeddings=(torch.tensor(x["cos"]), torch.tensor(x["sin"])),
+                    block_cand=torch.tensor(cand) if use_cand else None)
+            (out * torch.tensor(x["dout"])).sum().backward()
+            tag = f"{stage0}_{int(use_cand)}_{int(scale)}"
+            rows = np.linspace(0, S - 1, 64).astype(np.int64)
+            res["rows"] = rows
+            res[f"out_{tag}"] = out.detach().numpy()[:, :, rows]
+            res[f"topi_{tag}"] = rec["topi"].numpy().astype(np.int32)
+            res[f"valid_{tag}"] = rec["valid"].numpy()
+            res[f"bias_{tag}"] = rec["bias"].numpy()
+            res[f"prior_{tag}"] = rec["prior"].numpy()
+            res[f"candm_{tag}"] = np.packbits(rec["cand"].numpy(), axis=-1)
+            res[f"dq_{tag}"] = q.grad.numpy()[:, :, rows]
+            res[f"dv_{tag}"] = v.grad.numpy()[:, :, rows]
+            res[f"dqproj_{tag}"] = m.q_proj.weight.grad.numpy()
+            res[f"dheadcls_{tag}"] = (m.head_cls.grad.numpy() if m.head_cls.grad is not None
+                                      else np.zeros(128, np.float32))
+    res["cand"] = np.packbits(cand, axis=-1)
     np.savez_compressed(os.path.join(HERE, name + ".npz"), **res)
     print(name, "saved")
 
@@ -653,6 +718,7 @@ def main(names=None):
                                                          T=256, bs=32, lb=4, K=3),
         "page_aware": lambda: page_aware_case("page_aware", seed=6),
         "serving_plan": lambda: serving_plan_case("serving_plan", seed=11),
+        "dash_attention": lambda: dash_attention_case(da, "dash_attention", seed=12),
         "frontend": lambda: frontend_case("frontend", seed=7),
         "backward": lambda: backward_case("backward", seed=8),
     }

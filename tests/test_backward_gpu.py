@@ -92,7 +92,12 @@ def routes(B, T, K, bs, LW, seed, dup=True):
 
 @pytest.mark.parametrize("B,HQ,H,T,bs,LW,K", [(2, 8, 2, 1000, 128, 256, 6),
                                                (1, 2, 2, 777, 64, 256, 16),
-                                               (1, 8, 1, 300, 64, 64, 3)])
+                                               (1, 8, 1, 300, 64, 64, 3),
+                                               # 32-token blocks: four per 128-key tile
+                                               (1, 2, 2, 700, 32, 128, 12),
+                                               # a window that ends inside a block
+                                               (2, 4, 2, 500, 32, 96, 8),
+                                               (1, 2, 2, 600, 64, 96, 5)])
 def test_bf16_forward_backward_matches_oracle(B, HQ, H, T, bs, LW, K):
     """Our tcgen05 forward (o, lse) + the backward vs fp32 autograd."""
     g = torch.Generator().manual_seed(T + HQ)
@@ -121,6 +126,8 @@ def test_bf16_forward_backward_matches_oracle(B, HQ, H, T, bs, LW, K):
     (torch.bfloat16, 2, 2, 2, 100, 64, 64, 3),     # shorter than one 128-key tile
     (torch.bfloat16, 1, 2, 1, 333, 64, 128, 0),    # no routed slots: local window only
     (torch.bfloat16, 1, 2, 2, 520, 192, 192, 4),   # blocks straddling the 128-key tiles
+    (torch.float32, 1, 2, 2, 600, 32, 128, 12),    # fp32 (CUDA cores), 32-token blocks
+    (torch.float32, 1, 4, 2, 400, 96, 100, 3),     # fp32, two blocks in a 64-key tile
 ])
 def test_backward_edge_cases_match_oracle(dt, B, HQ, H, T, bs, LW, K):
     g = torch.Generator().manual_seed(T * 7 + K)
@@ -141,11 +148,12 @@ def test_backward_edge_cases_match_oracle(dt, B, HQ, H, T, bs, LW, K):
     dq, dk, dv, db = ops.gather_attention_bwd(q, k, v, o, do, lse.transpose(1, 2), idx, bias,
                                               block_size=bs, local_window=LW, scale=scale)
     _, _, rdq, rdk, rdv, rdb = BO.gather_attention_grads(q, k, v, idx, bias, do, bs, LW, scale)
+    tol = (1e-4, None) if dt == torch.float32 else (0.02, 0.015)
     for got, ref in ((dq, rdq), (dk, rdk), (dv, rdv)):
         assert got.dtype == dt
-        close(got, ref, 0.02, 0.015)
+        close(got, ref, *tol)
     if K > 0:
-        close(db, rdb, 0.02, 0.015)
+        close(db, rdb, *tol)
 
 
 def test_autograd_mirror_matches_oracle():
@@ -231,7 +239,11 @@ def heads_routes(B, HI, T, K, bs, seed):
 
 
 @pytest.mark.parametrize("B,HQ,H,HI,T,bs,LW,K", [(2, 8, 4, 2, 600, 64, 128, 5),
-                                                  (1, 4, 2, 1, 450, 128, 128, 3)])
+                                                  (1, 4, 2, 1, 450, 128, 128, 3),
+                                                  # one index head per kv head, a window
+                                                  # ending inside a block
+                                                  (1, 4, 4, 4, 500, 64, 96, 4),
+                                                  (1, 4, 2, 2, 520, 32, 112, 6)])
 def test_multi_index_head_packed_backward_matches_oracle(B, HQ, H, HI, T, bs, LW, K):
     g = torch.Generator().manual_seed(T + HI)
     q = (torch.randn(B, T, HQ, 128, generator=g) * 0.5).to(torch.bfloat16).cuda()
@@ -286,3 +298,30 @@ def test_fp32_with_segments_is_rejected():
     with pytest.raises(L.DashError):
         ops.gather_attention_bwd(x, x, x, x, x, torch.zeros(1, T, 2, device="cuda"), idx, None,
                                  block_size=64, local_window=64, scale=0.1, seg_start=seg)
+
+
+def test_autograd_mirror_fp32_matches_oracle():
+    """fp32 inputs through triton_gather_attention_e2e with requires_grad: the
+    fp32 forward (CUDA cores) and the fp32 backward keep fp32 precision
+    (1e-4 of each tensor's largest magnitude against the fp32 autograd of the
+    dense restatement), like the reference's fp32 kernels."""
+    B, HQ, H, T, bs, LW, K = 1, 4, 2, 640, 64, 128, 5
+    g = torch.Generator().manual_seed(4)
+    q = (torch.randn(B, HQ, T, 128, generator=g) * 0.5).cuda().requires_grad_()
+    k = (torch.randn(B, H, T, 128, generator=g) * 0.5).cuda().requires_grad_()
+    v = (torch.randn(B, H, T, 128, generator=g) * 0.5).cuda().requires_grad_()
+    idx, bias = routes(B, T, K, bs, LW, 11, dup=False)
+    bias.requires_grad_()
+    do = torch.randn(B, HQ, T, 128, generator=g).cuda()
+    pos = torch.arange(T, device="cuda")[None]
+    o = E2E.triton_gather_attention_e2e(q, k, v, idx[:, None], bias, pos, None, bs,
+                                        1.0 / math.sqrt(128), LW)
+    assert o.dtype == torch.float32
+    o.backward(do)
+    tr = lambda t: t.detach().transpose(1, 2)     # noqa: E731
+    ro, _, rdq, rdk, rdv, rdb = BO.gather_attention_grads(tr(q), tr(k), tr(v), idx, bias.detach(),
+                                                          tr(do), bs, LW, 1.0 / math.sqrt(128))
+    close(o.detach().transpose(1, 2), ro, 1e-4)
+    for got, ref in ((q.grad, rdq), (k.grad, rdk), (v.grad, rdv)):
+        close(got.transpose(1, 2), ref, 1e-4)
+    close(bias.grad, rdb, 1e-4)

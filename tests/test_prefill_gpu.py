@@ -319,3 +319,78 @@ def test_two_streams_share_no_scratch():
         torch.cuda.synchronize()
         for j in range(2):
             assert torch.equal(outs[j], ref[j])
+
+
+# ---------------------------------------------------------------------------
+# fp32 inputs: the fp32 CUDA-core kernel (every product and sum in fp32)
+# ---------------------------------------------------------------------------
+F32_ATOL = 2e-5      # fp32 kernel vs fp32/fp64 references
+
+
+def test_c1_golden_fp32():
+    """BASELINE config 1 is fp32: with the reference's own routes the output
+    matches the reference's fp32 _forward_dense to fp32 rounding."""
+    g = np.load(os.path.join(GOLD, "c1_headcls.npz"))
+    q, k, v, iq, ik = O.make_prefill_inputs(0, 1, 10, 1348, 128, 0, 273, 0.0)
+    bi = np.where(g["valid"], g["topi"], -1).astype(np.int32)[:, None]
+    bias = np.where(g["valid"], g["bias"], 0).astype(np.float32)
+    out = triton_gather_attention_e2e(
+        torch.from_numpy(q).cuda(), torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda(),
+        torch.from_numpy(bi).cuda(), torch.from_numpy(bias).cuda(),
+        torch.arange(1348, device="cuda")[None], None, 64, 1.0 / math.sqrt(128), 256)
+    assert out.dtype == torch.float32
+    np.testing.assert_allclose(out.cpu().numpy()[:, :, g["rows"]], g["out_rows"], atol=F32_ATOL, rtol=0)
+
+
+F32_CASES = [
+    # B, H, Hkv, T, bs, LW, K
+    (2, 2, 2, 700, 64, 256, 4),
+    (1, 6, 2, 900, 32, 128, 12),      # G=3, 32-token blocks
+    (1, 2, 2, 333, 16, 48, 5),        # 16-token blocks, window of 3 blocks
+    (2, 4, 4, 500, 100, 200, 3),      # a block size no tile shape divides
+    (1, 1, 1, 40, 64, 256, 2),        # shorter than a block and the window
+]
+
+
+@pytest.mark.parametrize("B,H,Hkv,T,bs,LW,K", F32_CASES)
+def test_prefill_fp32_vs_oracle(B, H, Hkv, T, bs, LW, K):
+    rng = np.random.default_rng(B * 7 + T)
+    D = 128
+    q = (rng.standard_normal((B, H, T, D)) * 0.5).astype(np.float32)
+    k = (rng.standard_normal((B, Hkv, T, D)) * 0.5).astype(np.float32)
+    v = (rng.standard_normal((B, Hkv, T, D)) * 0.5).astype(np.float32)
+    idx, bias = random_routes(rng, B, T, K, bs, LW)
+    lse = torch.empty(B, H, T, device="cuda")
+    out = ops.gather_attention(torch.from_numpy(q).cuda(), torch.from_numpy(k).cuda(),
+                               torch.from_numpy(v).cuda(), torch.from_numpy(idx).cuda(),
+                               torch.from_numpy(bias).cuda(), block_size=bs, local_window=LW,
+                               scale=1.0 / math.sqrt(D), lse=lse)
+    ref, ref_lse = O.attend_contig(q, k, v, idx[:, 0], bias[:, 0], bs, LW, 1.0 / math.sqrt(D),
+                                   return_lse=True)
+    np.testing.assert_allclose(out.cpu().numpy(), ref, atol=F32_ATOL, rtol=0)
+    np.testing.assert_allclose(lse.cpu().numpy(), ref_lse, atol=1e-4, rtol=0)
+
+
+def test_prefill_fp32_index_heads_and_packing():
+    """fp32 through triton_gather_attention (no grad): two index heads, two
+    packed segments per row."""
+    rng = np.random.default_rng(41)
+    B, H, Hkv, T, D, bs, LW, K = 1, 4, 2, 640, 128, 64, 128, 3
+    q = (rng.standard_normal((B, H, T, D)) * 0.5).astype(np.float32)
+    k = (rng.standard_normal((B, Hkv, T, D)) * 0.5).astype(np.float32)
+    v = (rng.standard_normal((B, Hkv, T, D)) * 0.5).astype(np.float32)
+    idx, _ = random_routes(rng, B, T, K, bs, LW, n_index_heads=2)
+    split = 300
+    pos = np.concatenate([np.arange(split), np.arange(T - split)])[None]
+    with torch.no_grad():
+        out = triton_gather_attention(torch.from_numpy(q).cuda(), torch.from_numpy(k).cuda(),
+                                      torch.from_numpy(v).cuda(), torch.from_numpy(idx).cuda(),
+                                      torch.from_numpy(pos).cuda(), None, bs, 1.0 / math.sqrt(D), LW)
+    assert out.dtype == torch.float32
+    seg = (np.arange(T)[None] - pos)
+    got = out.cpu().numpy()
+    for ih in range(2):
+        hs = slice(ih * 2, ih * 2 + 2)
+        ref = O.attend_contig(q[:, hs], k[:, ih:ih + 1], v[:, ih:ih + 1], idx[:, ih], None, bs,
+                              LW, 1.0 / math.sqrt(D), seg=seg)
+        np.testing.assert_allclose(got[:, hs], ref, atol=F32_ATOL, rtol=0)
