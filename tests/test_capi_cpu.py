@@ -151,7 +151,7 @@ def test_attn_bwd_rejects_bad_arguments():
     a.n_seq, a.seq_len, a.n_heads, a.n_kv_heads, a.head_dim = 1, 128, 4, 2, 128
     a.dtype, a.block_size, a.local_window, a.K, a.scale = L.DTYPE_BF16, 64, 64, 4, 0.1
     assert L.load().dash_attn_bwd_flag_words(C.byref(a)) == 2 * 4
-    for field, bad in (("head_dim", 64), ("block_size", 32), ("K", 300), ("n_heads", 3),
+    for field, bad in (("head_dim", 64), ("block_size", 48), ("K", 300), ("n_heads", 3),
                        ("n_heads", 32), ("dtype", 9)):
         old = getattr(a, field)
         setattr(a, field, bad)
