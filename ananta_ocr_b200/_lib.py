@@ -171,7 +171,9 @@ class DashIndexProjArgs(C.Structure):
                 ("cs_stride", _i64), ("eps", _f32), ("norm_clamp", _i32), ("T", _i32),
                 ("hidden_dim", _i32), ("d", _i32), ("k_dtype", _i32), ("idx_q", _p),
                 ("q_stride", _i64), ("idx_k", _p), ("k_stride", _i64), ("slot_mapping", _p),
-                ("k_rows", _i64), ("device_error", _p)]
+                ("k_rows", _i64), ("device_error", _p),
+                ("kbar_page", _p), ("kbar_ntok", _p), ("kbar_head_cls", _p), ("kbar", _p),
+                ("kbar_row_stride", _i64), ("kbar_block_size", _i32), ("pad1", _i32)]
 
 
 class DashRopeKVArgs(C.Structure):
@@ -205,11 +207,28 @@ class DashServingPlanArgs(C.Structure):
                 ("row2req", _p)]
 
 
+class DashPageCoordArgs(C.Structure):
+    _fields_ = [("input_ids", _p), ("q_start", _p), ("start_pos", _p), ("gen_start", _p),
+                ("row_key", _p), ("image_token_id", _i64), ("page_token_id", _i64),
+                ("mm_pad_shift", _i64), ("num_tokens", _i32), ("num_reqs", _i32),
+                ("num_decode_tokens", _i32), ("has_page_token", _i32), ("max_rows", _i32),
+                ("max_pages", _i32), ("state_key", _p), ("state_stamp", _p), ("step", _p),
+                ("c_marker", _p), ("c_pp", _p), ("cnt", _p), ("rows", _p), ("tok_pos", _p),
+                ("page_pos", _p)]
+
+
+class DashCosSin2DArgs(C.Structure):
+    _fields_ = [("tok_pos", _p), ("page_pos", _p), ("inv_tok", _p), ("inv_page", _p),
+                ("cos", _p), ("sin", _p), ("stride", _i64), ("page_mod", _i64),
+                ("num_tokens", _i32), ("dim", _i32), ("n_tok", _i32), ("out_bf16", _i32)]
+
+
 ABI_ORDER = [DashSeqs, DashKV, DashRoutes, DashQO, DashKbarArgs, DashRouteArgs,
              DashBlockMaxArgs, DashPrefillArgs, DashDecodeArgs, DashDeviceError,
              DashPageIdsArgs, DashPageStateArgs, DashPageAllowArgs, DashPageDecodeArgs,
              DashBlockAnyArgs, DashPageBlocksArgs, DashIndexProjArgs, DashRopeKVArgs,
-             DashAttnBwdArgs, DashEntmaxArgs, DashServingPlanArgs, DashPeerHandle]
+             DashAttnBwdArgs, DashEntmaxArgs, DashServingPlanArgs, DashPeerHandle,
+             DashPageCoordArgs, DashCosSin2DArgs]
 
 # every function the header declares
 EXPORTS = [
@@ -221,6 +240,7 @@ EXPORTS = [
     "dash_block_any", "dash_page_blocks", "dash_index_proj", "dash_rope_kv_write",
     "dash_attn_bwd", "dash_attn_bwd_flag_words", "dash_entmax15_fwd", "dash_entmax15_bwd",
     "dash_serving_plan", "dash_peer_export", "dash_peer_import", "dash_peer_close",
+    "dash_page_coords", "dash_cos_sin_2d",
 ]
 
 
@@ -261,6 +281,8 @@ def load(path: str = LIB_PATH):
         ("dash_entmax15_fwd", [C.POINTER(DashEntmaxArgs), _p]),
         ("dash_entmax15_bwd", [C.POINTER(DashEntmaxArgs), _p]),
         ("dash_serving_plan", [C.POINTER(DashServingPlanArgs), _p]),
+        ("dash_page_coords", [C.POINTER(DashPageCoordArgs), _p]),
+        ("dash_cos_sin_2d", [C.POINTER(DashCosSin2DArgs), _p]),
     ]:
         f = getattr(L, name)
         f.argtypes = args

@@ -133,7 +133,7 @@ int dash_count_launches(int reset) {
 }
 
 int dash_abi_sizes(int64_t* out, int n) {
-  const int64_t s[22] = {(int64_t)sizeof(DashSeqs),           (int64_t)sizeof(DashKV),
+  const int64_t s[24] = {(int64_t)sizeof(DashSeqs),           (int64_t)sizeof(DashKV),
                          (int64_t)sizeof(DashRoutes),         (int64_t)sizeof(DashQO),
                          (int64_t)sizeof(DashKbarArgs),       (int64_t)sizeof(DashRouteArgs),
                          (int64_t)sizeof(DashBlockMaxArgs),   (int64_t)sizeof(DashPrefillArgs),
@@ -143,9 +143,10 @@ int dash_abi_sizes(int64_t* out, int n) {
                          (int64_t)sizeof(DashBlockAnyArgs),   (int64_t)sizeof(DashPageBlocksArgs),
                          (int64_t)sizeof(DashIndexProjArgs),  (int64_t)sizeof(DashRopeKVArgs),
                          (int64_t)sizeof(DashAttnBwdArgs),    (int64_t)sizeof(DashEntmaxArgs),
-                         (int64_t)sizeof(DashServingPlanArgs), (int64_t)sizeof(DashPeerHandle)};
-  for (int i = 0; i < n && i < 22; ++i) out[i] = s[i];
-  return 22;
+                         (int64_t)sizeof(DashServingPlanArgs), (int64_t)sizeof(DashPeerHandle),
+                         (int64_t)sizeof(DashPageCoordArgs),   (int64_t)sizeof(DashCosSin2DArgs)};
+  for (int i = 0; i < n && i < 24; ++i) out[i] = s[i];
+  return 24;
 }
 
 int dash_kbar_pool(const DashKbarArgs* a, dash_stream_t stream) {
@@ -338,6 +339,13 @@ int dash_index_proj(const DashIndexProjArgs* a, dash_stream_t stream) {
   if (a->k_dtype != DASH_DTYPE_F32 && a->k_dtype != DASH_DTYPE_BF16)
     return set_error(DASH_ERR_UNSUPPORTED, "idx_k dtype must be fp32 or bf16");
   if (a->slot_mapping && a->k_rows <= 0) return set_error(DASH_ERR_INVALID, "k_rows must be > 0 with slot_mapping");
+  if (a->kbar_page) {
+    if (!a->slot_mapping || !a->kbar_ntok || !a->kbar)
+      return set_error(DASH_ERR_INVALID, "the fused k-bar refresh needs slot_mapping, kbar_ntok and kbar");
+    if (a->kbar_block_size <= 0 || a->kbar_block_size > 256)
+      return set_error(DASH_ERR_UNSUPPORTED, "kbar_block_size %d not in (0, 256]", a->kbar_block_size);
+    if (a->kbar_row_stride < a->d) return set_error(DASH_ERR_INVALID, "kbar_row_stride < d");
+  }
   if (!aligned16(a->idx_q) || a->q_stride % 4 || a->q_stride < a->d)
     return set_error(DASH_ERR_INVALID, "idx_q must be 16-byte aligned with a row stride multiple of 4 >= d");
   if ((reinterpret_cast<uintptr_t>(a->idx_k) & (a->k_dtype == DASH_DTYPE_BF16 ? 7 : 15)) || a->k_stride % 4 ||
@@ -454,6 +462,32 @@ int dash_serving_plan(const DashServingPlanArgs* a, dash_stream_t stream) {
   }
   if (a->row2req && !a->cu_seqlens_q) return set_error(DASH_ERR_INVALID, "row2req needs cu_seqlens_q");
   return launch_serving_plan(*a, (cudaStream_t)stream);
+}
+
+int dash_page_coords(const DashPageCoordArgs* a, dash_stream_t stream) {
+  if (!a) return set_error(DASH_ERR_INVALID, "null args");
+  if (a->num_reqs < 0 || a->num_tokens < 0) return set_error(DASH_ERR_INVALID, "negative size");
+  if (a->num_reqs == 0) return DASH_OK;
+  if (!a->q_start && a->num_tokens != a->num_reqs)
+    return set_error(DASH_ERR_INVALID, "without q_start every request owns one token");
+  if (!a->input_ids || !a->start_pos || !a->row_key || !a->state_key || !a->state_stamp || !a->step ||
+      !a->c_marker || !a->c_pp || !a->cnt || !a->rows || !a->tok_pos || !a->page_pos)
+    return set_error(DASH_ERR_INVALID, "null pointer");
+  if (a->max_rows < a->num_reqs || a->max_pages < 1)
+    return set_error(DASH_ERR_INVALID, "need max_rows >= num_reqs and max_pages >= 1");
+  return launch_page_coords(*a, (cudaStream_t)stream);
+}
+
+int dash_cos_sin_2d(const DashCosSin2DArgs* a, dash_stream_t stream) {
+  if (!a) return set_error(DASH_ERR_INVALID, "null args");
+  if (a->num_tokens < 0) return set_error(DASH_ERR_INVALID, "num_tokens < 0");
+  if (a->num_tokens == 0) return DASH_OK;
+  if (a->dim <= 0 || a->dim % 2 || a->n_tok <= 0 || a->n_tok >= a->dim / 2)
+    return set_error(DASH_ERR_INVALID, "need an even dim and 0 < n_tok < dim / 2");
+  if (a->stride < a->dim || a->page_mod < 0) return set_error(DASH_ERR_INVALID, "bad stride / page_mod");
+  if (!a->tok_pos || !a->page_pos || !a->inv_tok || !a->inv_page || !a->cos || !a->sin)
+    return set_error(DASH_ERR_INVALID, "null pointer");
+  return launch_cos_sin_2d(*a, (cudaStream_t)stream);
 }
 
 int dash_entmax15_fwd(const DashEntmaxArgs* a, dash_stream_t stream) {

@@ -173,6 +173,67 @@ __device__ __forceinline__ void epilogue_unit(uint32_t tcol, const float* w1s,
   }
 }
 
+// k-bar of one page by one warp, in the arithmetic order of kbar_pool_kernel
+// (dash_router.cu): per key a sequential FMA chain over the feature index,
+// clamp, max, det_expf, a sequential sum, IEEE division, then per feature a
+// sequential FMA chain over the keys; non-finite -> 0.
+__device__ __noinline__ void kbar_refresh_warp(const DashIndexProjArgs& a, int64_t page, int n, int lane) {
+  if (n <= 0) return;
+  constexpr int D = 128, MAXJ = 8;                 // up to 256 keys per page
+  const bool b16 = a.k_dtype == DASH_DTYPE_BF16;
+  auto key = [&](int j, int c) -> float {
+    const int64_t row = page * a.kbar_block_size + j;
+    return b16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.idx_k)[row * a.k_stride + c])
+               : reinterpret_cast<const float*>(a.idx_k)[row * a.k_stride + c];
+  };
+  const float inv_sqrt_d = (float)(1.0 / sqrt((double)D));
+  float e[MAXJ];
+  float lmax = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < MAXJ; ++i) {
+    const int j = lane + 32 * i;
+    e[i] = 0.0f;
+    if (j < n) {
+      float acc = 0.0f;
+      for (int c = 0; c < D; ++c) acc = __fmaf_rn(key(j, c), a.kbar_head_cls ? a.kbar_head_cls[c] : 0.0f, acc);
+      e[i] = clamp_act(__fmul_rn(acc, inv_sqrt_d));
+      lmax = fmaxf(lmax, e[i]);
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+#pragma unroll
+  for (int i = 0; i < MAXJ; ++i)
+    if (lane + 32 * i < n) e[i] = det_expf(__fsub_rn(e[i], lmax));
+  float sum = 0.0f;
+#pragma unroll
+  for (int i = 0; i < MAXJ; ++i)
+    for (int l = 0; l < 32; ++l) {
+      const float v = __shfl_sync(0xffffffffu, e[i], l);
+      if (32 * i + l < n) sum = __fadd_rn(sum, v);
+    }
+  const float den = sum > 1e-6f ? sum : 1e-6f;
+#pragma unroll
+  for (int i = 0; i < MAXJ; ++i) e[i] = __fdiv_rn(e[i], den);
+  float acc[D / 32];
+#pragma unroll
+  for (int q = 0; q < D / 32; ++q) acc[q] = 0.0f;
+#pragma unroll
+  for (int i = 0; i < MAXJ; ++i)
+    for (int l = 0; l < 32; ++l) {
+      const int j = 32 * i + l;
+      if (j >= n) break;
+      const float w = __shfl_sync(0xffffffffu, e[i], l);
+#pragma unroll
+      for (int q = 0; q < D / 32; ++q) acc[q] = __fmaf_rn(w, key(j, lane + 32 * q), acc[q]);
+    }
+#pragma unroll
+  for (int q = 0; q < D / 32; ++q) {
+    float v = acc[q];
+    if (!(v == v) || isinf(v)) v = 0.0f;
+    a.kbar[page * a.kbar_row_stride + lane + 32 * q] = v;
+  }
+}
+
 __global__ void __launch_bounds__(fe::NTHREADS, 1)
     index_proj_kernel(const __grid_constant__ CUtensorMap tmH,
                       const __grid_constant__ CUtensorMap tmWq,
@@ -325,6 +386,18 @@ __global__ void __launch_bounds__(fe::NTHREADS, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+  // fused k-bar refresh: the barrier above made this CTA's idx_k rows visible
+  // to all its threads; a warp per token naming a page
+  if (a.kbar_page) {
+    const int nwarps = NTHREADS / 32;
+    for (int tl = warp; tl < 2 * 128; tl += nwarps) {
+      const int64_t t = (int64_t)m0 + tl;
+      if (t >= a.T) break;
+      const int64_t page = a.kbar_page[t];
+      if (page < 0) continue;
+      kbar_refresh_warp(a, page, min(a.kbar_ntok[t], a.kbar_block_size), lane);
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------

@@ -34,5 +34,7 @@ size_t attn_bwd_tc_acc_bytes(const DashAttnBwdArgs& a);
 int launch_attn_bwd_tc(const DashAttnBwdArgs& a, int nblk, int words, cudaStream_t st);
 int launch_entmax15(const DashEntmaxArgs& a, bool backward, cudaStream_t st);
 int launch_serving_plan(const DashServingPlanArgs& a, cudaStream_t st);
+int launch_page_coords(const DashPageCoordArgs& a, cudaStream_t st);
+int launch_cos_sin_2d(const DashCosSin2DArgs& a, cudaStream_t st);
 
 }  // namespace dash

@@ -307,11 +307,11 @@ class DashDecoder:
             qkv = F.linear(h, L["wqkv"])
             q, k, v = qkv[:, :H], qkv[:, H:2 * H], qkv[:, 2 * H:]
             IF.rope_and_store_kv(q, k, v, cos, sin, self.kc[li], self.vc[li], slots, c.head_dim)
+            # index projections + index-K write + k-bar refresh of the tail pages
             idx_q, _ = IF.index_qk_fused(h, L["wiq"], L["wik"], L["niq"], L["nik"], c.eps, cos, sin,
-                                         index_cache=self.ic[li], slot_mapping=slots)
-            RT.kbar_refresh_tail_triton(kv_cache=self.ic[li], k_bar=self.kbar[li],
-                                        block_table=self.block_table, seq_lens=sl,
-                                        head_cls=L["head_cls"], block_size=c.block_size, plan=tail)
+                                         index_cache=self.ic[li], slot_mapping=slots,
+                                         kbar_refresh=(self.kbar[li], tail, L["head_cls"],
+                                                       c.block_size))
             RT.route_decode_triton(idx_q=idx_q, k_bar=self.kbar[li], block_table=self.block_table,
                                    seq_lens=sl, image_allow=allow, out_idx=self.oi, out_bias=self.ob,
                                    max_block=self.pps, block_size=c.block_size,

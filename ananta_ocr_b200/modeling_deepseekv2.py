@@ -151,6 +151,20 @@ def _decode_attend(q, k_all, v_all, topi, bias, valid, q_pos, block_size, local_
     pos0 = torch.as_tensor(q_pos, device=q.device)[:, 0].to(torch.int32).contiguous()
     seqs = ops.Seqs(n_seq=B, q_len=Lq, kv_len=S, pos0=pos0, max_q_len=Lq)
     from . import _lib as L
+    if qq.dtype == torch.float32:
+        # fp32 (the reference computes this path in fp32): the fp32 prefill
+        # kernel with the Lq query rows at their positions over the whole cache
+        a = L.DashPrefillArgs()
+        a.seqs = seqs.c()
+        a.kv = ops._kv(kk, vv, None, Hkv, (kk.stride(0), kk.stride(2), kk.stride(1)))
+        idx2 = idx.view(B * Lq, -1)
+        bias2 = bias.view(B * Lq, -1)
+        a.routes = ops._routes(idx2, bias2, idx2.stride(0), 0, 1)
+        a.qo = ops._qo(qq, out, (qq.stride(0), qq.stride(2), qq.stride(1)),
+                       (out.stride(0), out.stride(2), out.stride(1)), H)
+        a.scale, a.block_size, a.local_window = float(scale), int(block_size), int(local_window)
+        ops.prefill_attn(a, q.device)
+        return out
     a = L.DashDecodeArgs()
     a.seqs = seqs.c()
     a.kv = ops._kv(kk, vv, None, Hkv, (kk.stride(0), kk.stride(2), kk.stride(1)))

@@ -453,7 +453,7 @@ def index_proj(hidden: torch.Tensor, w_q: torch.Tensor, w_k: torch.Tensor,
                cos: Optional[torch.Tensor] = None, sin: Optional[torch.Tensor] = None,
                norm_clamp: bool = False, idx_q: Optional[torch.Tensor] = None,
                idx_k: Optional[torch.Tensor] = None, slot_mapping: Optional[torch.Tensor] = None,
-               device_error: Optional[DeviceErrorWord] = None):
+               device_error: Optional[DeviceErrorWord] = None, kbar_refresh=None):
     """Index projections + RMSNorm + RoPE on tcgen05 (``dash_index_proj``).
 
     hidden [T, hidden_dim] bf16; w_q/w_k [128, hidden_dim] bf16 (nn.Linear
@@ -461,7 +461,9 @@ def index_proj(hidden: torch.Tensor, w_q: torch.Tensor, w_k: torch.Tensor,
     [T, >=128] bf16 or None.  Returns (idx_q [T, 128] fp32, idx_k): idx_k is
     [T, 128] fp32 unless ``idx_k`` is given -- with ``slot_mapping`` [T] int64
     it is a cache of rows [num_slots, 128] (fp32 or bf16) written at the
-    tokens' slots."""
+    tokens' slots.  ``kbar_refresh`` = (kbar [P, 128] fp32, pages [T] int64,
+    ntok [T] int32, head_cls or None, block_size) recomputes, after the write,
+    the k-bar row of each token's page (one token per page in this call)."""
     _need_cuda(hidden, w_q, w_k, cos, sin, idx_k, slot_mapping)
     if hidden.dtype != torch.bfloat16 or w_q.dtype != torch.bfloat16 or w_k.dtype != torch.bfloat16:
         raise NotImplementedError("index projections run on bf16 hidden states and weights")
@@ -499,7 +501,18 @@ def index_proj(hidden: torch.Tensor, w_q: torch.Tensor, w_k: torch.Tensor,
         sm = slot_mapping if slot_mapping.dtype == torch.int64 else slot_mapping.to(torch.int64)
         a.slot_mapping, a.k_rows = sm.contiguous().data_ptr(), idx_k.shape[0]
     a.device_error = device_error.ptr if device_error is not None else None
+    keep = None
+    if kbar_refresh is not None:
+        kbar, pages, ntok, head_cls, block_size = kbar_refresh
+        _need_cuda(kbar, pages, ntok)
+        pages = pages.to(torch.int64).contiguous()
+        ntok = ntok.to(torch.int32).contiguous()
+        hc = None if head_cls is None else head_cls.detach().to(dev, torch.float32).contiguous()
+        keep = (pages, ntok, hc)
+        a.kbar_page, a.kbar_ntok, a.kbar_head_cls = pages.data_ptr(), ntok.data_ptr(), _ptr(hc)
+        a.kbar, a.kbar_row_stride, a.kbar_block_size = kbar.data_ptr(), kbar.stride(0), int(block_size)
     L.call("dash_index_proj", a)
+    del keep
     return idx_q, idx_k
 
 

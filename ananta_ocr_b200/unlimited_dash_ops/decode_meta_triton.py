@@ -4,10 +4,11 @@ libdash_b200.so.
 
 ``decode_meta_fused`` runs the page bookkeeping of one decode token per request
 (``dash_page_state_step`` without a token layout: request r owns token r at
-position seq_lens[r] - 1); ``decode_allow_fused`` builds the candidate mask from
-the per-block page bounds that step maintains (``dash_page_allow``).  The
-Page2D coordinate state of the same reference kernel belongs to the rotary
-front end and is not part of this library: pass ``coord_state=None``.
+position seq_lens[r] - 1) and, with a ``coord_state`` (``page2d_rope.
+PageCoordState``), the Page2D coordinates of those tokens
+(``dash_page_coords``); ``cos_sin_2d_fused`` writes their cos/sin table
+(``dash_cos_sin_2d``); ``decode_allow_fused`` builds the candidate mask from
+the per-block page bounds the page step maintains (``dash_page_allow``).
 """
 from __future__ import annotations
 
@@ -21,9 +22,8 @@ from .page_state import _MM_PAD_SHIFT_VALUE, _i32, _i64
 def decode_meta_fused(*, input_ids, block_table, seq_lens, slot_mapping, page_state,
                       coord_state=None, num_slots: int, block_size: int, out_q_page=None,
                       out_tok=None, out_page=None):
-    """decode_meta_triton.py:247-315 (page part): returns (q_page int32 [R], None)."""
-    if coord_state is not None:
-        raise NotImplementedError("Page2D coordinates are not part of libdash_b200")
+    """decode_meta_triton.py:247-315: returns (q_page int32 [R], (tok_pos,
+    page_pos) int64 [R]) -- the coordinates are None without a coord_state."""
     R = int(seq_lens.shape[0])
     device = input_ids.device
     page_state._ensure(num_slots, device)
@@ -36,7 +36,22 @@ def decode_meta_fused(*, input_ids, block_table, seq_lens, slot_mapping, page_st
         page_token_id=page_state.page_token_id, slots=page_state._slots, q_page=q_page,
         seq_lens=_i32(seq_lens), num_decode_tokens=R, num_reqs=R, num_tokens=R,
         bounds=(page_state._blk_lo, page_state._blk_hi), mm_pad_shift=_MM_PAD_SHIFT_VALUE)
-    return q_page, None
+    if coord_state is None:
+        return q_page, None
+    sl = seq_lens[:R].to(torch.int64)
+    tok, page = coord_state.advance(input_ids=input_ids[:R], q_start=None, start_pos=sl - 1,
+                                    row_key=block_table[:R, 0], num_decode_tokens=R,
+                                    out_tok=out_tok, out_page=out_page)
+    return q_page, (tok, page)
+
+
+@torch.no_grad()
+def cos_sin_2d_fused(*, rope, tok_pos, page_pos, dtype, out_cos, out_sin):
+    """decode_meta_triton.py:354-389: the Page2D cos/sin table of the given
+    coordinates into the caller's fixed buffers."""
+    from .page2d_rope import cos_sin_table
+    T = int(tok_pos.shape[0])
+    return cos_sin_table(rope, tok_pos, page_pos, out_cos[:T], out_sin[:T])
 
 
 @torch.no_grad()

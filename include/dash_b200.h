@@ -530,6 +530,62 @@ typedef struct {
 int dash_serving_plan(const DashServingPlanArgs* args, dash_stream_t stream);
 
 /* ---------------------------------------------------------------------- */
+/* Page2D rotary coordinates of a serving step (two launches).
+ * Replaces: WHL page2d_rope.py:327-620 (PageCoordState._rows / step) and the
+ *           coordinate part of decode_meta_triton.py:89-104 (decode_meta_fused).
+ * Request r owns tokens [q_start[r], q_start[r+1]) (q_start NULL: token r),
+ * the first at position start_pos[r].  Its state row is the live row whose
+ * state_key equals row_key[r], else a free row (state_key -1) or the least
+ * recently stamped one (ties: lowest row), which is reset; a matched row is
+ * reset too when start_pos[r] <= 0.  Per token, in order: marker count
+ * mc = carry + markers so far; prompt pages pp = max(carry, mc at image tokens
+ * so far); generated iff flat index < num_decode_tokens or position >=
+ * gen_start[r]; page = clamp(!generated && (image || mc > pp) ? mc :
+ * min(max(mc - pp, 0), pp), 0, max_pages - 1); tok = the row's count of that
+ * page, then the count grows by one.  The row keeps mc, pp and the counts.
+ * State arrays are device memory the caller keeps across steps (state_key
+ * initialised to -1, step to 0); rows is scratch [num_reqs].
+ * No speculative-decoding rewind.                                          */
+typedef struct {
+  const int64_t* input_ids;    /* [num_tokens] */
+  const int64_t* q_start;      /* [num_reqs + 1] or NULL */
+  const int64_t* start_pos;    /* [num_reqs] */
+  const int64_t* gen_start;    /* [num_reqs] or NULL */
+  const int64_t* row_key;      /* [num_reqs], e.g. the first physical block */
+  int64_t image_token_id, page_token_id, mm_pad_shift;
+  int32_t num_tokens, num_reqs, num_decode_tokens, has_page_token, max_rows, max_pages;
+  int64_t* state_key;          /* [max_rows] */
+  int64_t* state_stamp;        /* [max_rows] */
+  int64_t* step;               /* [1] */
+  int32_t* c_marker;           /* [max_rows] */
+  int32_t* c_pp;               /* [max_rows] */
+  int32_t* cnt;                /* [max_rows, max_pages] */
+  int32_t* rows;               /* [num_reqs] scratch */
+  int64_t* tok_pos;            /* [num_tokens] out */
+  int64_t* page_pos;           /* [num_tokens] out */
+} DashPageCoordArgs;
+int dash_page_coords(const DashPageCoordArgs* args, dash_stream_t stream);
+
+/* Page2D cos/sin table: row t, column c (j = c mod dim/2):
+ *   angle = j < n_tok ? tok_pos[t] * inv_tok[j] : (page_pos[t] mod page_mod) * inv_page[j - n_tok]
+ * (fp32; page_mod 0 = no fold), cos/sin stored as fp32 or bf16 (round to
+ * nearest) with row stride `stride` elements.
+ * Replaces: WHL decode_meta_triton.py:166-209, :354-389 (cos_sin_2d_fused) and
+ *           page2d_rope.py:109-127 (PageRope2D.cos_sin).                    */
+typedef struct {
+  const int64_t* tok_pos;
+  const int64_t* page_pos;
+  const float* inv_tok;   /* [n_tok] */
+  const float* inv_page;  /* [dim/2 - n_tok] */
+  void* cos;
+  void* sin;
+  int64_t stride;
+  int64_t page_mod;
+  int32_t num_tokens, dim, n_tok, out_bf16;
+} DashCosSin2DArgs;
+int dash_cos_sin_2d(const DashCosSin2DArgs* args, dash_stream_t stream);
+
+/* ---------------------------------------------------------------------- */
 /* Decode gather attention over a block-paged (or contiguous) KV cache.
  * Replaces: WHL attend_triton.py:600-715 (dash_sparse_attn_decode) with the
  *           split-K merge of WHL common.py:40-89, and the decode attend of
@@ -614,6 +670,19 @@ typedef struct {
   const int64_t* slot_mapping;                 /* optional [T] */
   int64_t k_rows;                              /* rows addressable through slot_mapping */
   DashDeviceError* device_error;
+  /* Fused k-bar refresh (optional; replaces the separate dash_kbar_pool launch
+   * of WHL route_triton.py:707-726 on decode steps): after the idx_k write,
+   * the k-bar row kbar_page[t] (>= 0) is recomputed from the first
+   * kbar_ntok[t] cache rows of that page (rows kbar_page[t] * kbar_block_size
+   * + j), with dash_kbar_pool's arithmetic (bitwise the same result).  Needs
+   * slot_mapping; a page named by token t may receive no other token of this
+   * call (one token per request, as in a decode step). */
+  const int64_t* kbar_page;                    /* [T] or NULL */
+  const int32_t* kbar_ntok;                    /* [T] */
+  const float* kbar_head_cls;                  /* [d] or NULL (block mean) */
+  float* kbar; int64_t kbar_row_stride;
+  int32_t kbar_block_size;
+  int32_t pad1;
 } DashIndexProjArgs;
 int dash_index_proj(const DashIndexProjArgs* args, dash_stream_t stream);
 
@@ -722,7 +791,8 @@ int dash_count_launches(int reset);          /* kernels launched by this library
  * DashDecodeArgs, DashDeviceError, DashPageIdsArgs, DashPageStateArgs,
  * DashPageAllowArgs, DashPageDecodeArgs, DashBlockAnyArgs, DashPageBlocksArgs,
  * DashIndexProjArgs, DashRopeKVArgs, DashAttnBwdArgs, DashEntmaxArgs,
- * DashServingPlanArgs, DashPeerHandle.  Lets a binding
+ * DashServingPlanArgs, DashPeerHandle, DashPageCoordArgs, DashCosSin2DArgs.
+ * Lets a binding
  * verify its struct layouts; returns the number of sizes available. */
 int dash_abi_sizes(int64_t* out, int n);
 /* Self-test of the bounded waits every kernel uses (no reference counterpart):

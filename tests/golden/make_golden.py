@@ -544,6 +544,96 @@ def page_aware_case(name, seed):
     print(name, "saved")
 
 
+def page_coords_case(name, seed):
+    """Page2D coordinates of the sglang wheel over a serving trace: the torch
+    PageCoordState.step for prefill chunks, the fused one-token decode
+    (decode_meta_fused, Triton interpreted) for decode steps, a finished
+    request whose state row is reused by a new one, and the cos/sin tables
+    (PageRope2D.cos_sin in torch and cos_sin_2d_fused interpreted)."""
+    from sglang.srt.layers.attention.unlimited_dash_ops import page_state as ps
+    from sglang.srt.layers.attention.unlimited_dash_ops import decode_meta_triton as dm
+    from sglang.srt.layers.attention.unlimited_dash_ops import page2d_rope as pr
+    from oracle.page_oracle import make_document_ids, IMAGE_TOKEN_ID as IMG, PAGE_TOKEN_ID as PG
+    torch.cuda.is_current_stream_capturing = lambda: False
+    rng = np.random.default_rng(seed)
+    sbs, per, P, W = 16, 24, 128, 24
+    cfg = {"image_token_id": IMG, "page_token_id": PG, "per_page_image_tokens": per}
+    pst = ps.PageIsolationState(cfg, sbs)
+    coord = pr.PageCoordState(cfg, max_reqs=3, max_pages=6)
+    rope = pr.PageRope2D(128, 10000.0, 256.0, 1, "resample", page_mod=2)
+    num_slots = P * sbs
+    perm = rng.permutation(P)
+    bt = np.stack([perm[i * W:(i + 1) * W] for i in range(4)]).astype(np.int64)
+    docs = [make_document_ids(rng, 200, n_pages=4, page_tokens=30, text_in_page=2, response_pages=0),
+            make_document_ids(rng, 170, n_pages=3, page_tokens=40, markers=False),
+            make_document_ids(rng, 190, n_pages=5, page_tokens=25, empty_pages=1, lead_images=7,
+                              response_pages=0),
+            make_document_ids(rng, 120, n_pages=2, page_tokens=30, response_pages=0)]
+    lens = [0, 0, 0, 0]
+    # per step: (request, n_tokens) pairs; n == 1 after the prompt is a decode token
+    plan = [[(0, 120), (1, 170), (2, 150)], [(0, 80), (2, 40)],
+            [(0, 1), (1, 1), (2, 1)], [(0, 1), (1, 1), (2, 1)],
+            [(3, 90)],                                   # request 3 takes request 1's row
+            [(0, 1), (2, 1), (3, 1)], [(0, 1), (2, 1), (3, 1)]]
+    gen = rng.integers(0, 1000, size=(len(plan), 4))
+    gen[2, 0] = PG
+    gen[3, 2] = PG
+    gen[5, 3] = IMG
+    gen[6, 0] = PG
+    res = {"bt": bt}
+    prompt_len = [200, 170, 190, 90]
+    for si, st in enumerate(plan):
+        rows = [r for r, _ in st]
+        ns = [n for _, n in st]
+        toks, qs, starts = [], [0], []
+        for r, n in st:
+            if lens[r] >= prompt_len[r]:
+                toks.append(int(gen[si, r]))
+            else:
+                toks += docs[r][lens[r]:lens[r] + n].tolist()
+            starts.append(lens[r])
+            qs.append(qs[-1] + n)
+        T = qs[-1]
+        decode = all(lens[r] >= prompt_len[r] for r in rows)
+        q_start = torch.tensor(qs, dtype=torch.int64)
+        btab = torch.tensor(bt[rows])
+        slots = [int(bt[r, (starts[j] + i) // sbs]) * sbs + (starts[j] + i) % sbs
+                 for j, (r, n) in enumerate(st) for i in range(n)]
+        ids_t = torch.tensor(toks, dtype=torch.int64)
+        rec = {"rows": np.array(rows), "q_start": np.array(qs), "start_pos": np.array(starts),
+               "ids": np.array(toks), "slots": np.array(slots), "decode": int(decode)}
+        if decode:
+            seq = torch.tensor([lens[r] + 1 for r in rows], dtype=torch.int32)
+            q_page, (tok, page) = dm.decode_meta_fused(
+                input_ids=ids_t, block_table=btab, seq_lens=seq,
+                slot_mapping=torch.tensor(slots, dtype=torch.int64), page_state=pst,
+                coord_state=coord, num_slots=num_slots, block_size=sbs)
+            cos = torch.zeros(T, 128, dtype=torch.bfloat16)
+            sin = torch.zeros(T, 128, dtype=torch.bfloat16)
+            dm.cos_sin_2d_fused(rope=rope, tok_pos=tok, page_pos=page, dtype=torch.bfloat16,
+                                out_cos=cos, out_sin=sin)
+            rec["cos_fused"] = cos.view(torch.int16).numpy()
+            rec["sin_fused"] = sin.view(torch.int16).numpy()
+            rec["q_page"] = q_page.numpy().copy()
+        else:
+            layout = ps.BatchLayout(num_tokens=T, num_reqs=len(rows), q_start=q_start,
+                                    start_pos=torch.tensor(starts, dtype=torch.int64),
+                                    block_table=btab, req_of_token=ps._req_of_token(q_start, T),
+                                    num_decode_tokens=0, gen_start=None)
+            tok, page = coord.step(ids_t, layout)
+        c32, s32 = rope.cos_sin(tok, page, torch.float32)
+        rec["tok"], rec["page"] = tok.numpy().copy(), page.numpy().copy()
+        rec["cos32"], rec["sin32"] = c32.numpy(), s32.numpy()
+        for r, n in st:
+            lens[r] += n
+        for k, v in rec.items():
+            res[f"s{si}_{k}"] = np.asarray(v)
+    res["inv_tok"], res["inv_page"] = rope.inv_tok.numpy(), rope.inv_page.numpy()
+    np.savez_compressed(os.path.join(HERE, name + ".npz"), steps=len(plan), sbs=sbs, P=P, W=W,
+                        max_reqs=3, max_pages=6, page_mod=2, n_tok=rope.n_tok, **res)
+    print(name, "saved")
+
+
 def _gemma_forward_native():
     """GemmaRMSNorm.forward_native of the sglang wheel (WHL layernorm.py:1113-1131),
     compiled from the wheel's own source (the module's imports need a full
@@ -718,6 +808,7 @@ def main(names=None):
                                                          T=256, bs=32, lb=4, K=3),
         "page_aware": lambda: page_aware_case("page_aware", seed=6),
         "serving_plan": lambda: serving_plan_case("serving_plan", seed=11),
+        "page_coords": lambda: page_coords_case("page_coords", seed=13),
         "dash_attention": lambda: dash_attention_case(da, "dash_attention", seed=12),
         "frontend": lambda: frontend_case("frontend", seed=7),
         "backward": lambda: backward_case("backward", seed=8),

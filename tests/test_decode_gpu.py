@@ -28,7 +28,14 @@ def test_decode_golden_contiguous():
                             torch.from_numpy(v).cuda(), torch.from_numpy(g["topi"]).cuda(),
                             torch.from_numpy(g["bias"]).cuda(), torch.from_numpy(g["valid"]).cuda(),
                             pos, bs, lb * bs, 1.0 / math.sqrt(128))
-    assert_close_bf16(out.cpu().numpy(), g["out"])
+    # fp32 inputs: computed in fp32 (the reference's _decode_attend is fp32)
+    np.testing.assert_allclose(out.cpu().numpy(), g["out"], atol=2e-5, rtol=0)
+    # the same query in bf16 takes the split-KV decode kernel
+    bf = lambda x: torch.from_numpy(x).cuda().bfloat16()      # noqa: E731
+    out16 = MD._decode_attend(bf(g["qd"]), bf(k), bf(v), torch.from_numpy(g["topi"]).cuda(),
+                              torch.from_numpy(g["bias"]).cuda(), torch.from_numpy(g["valid"]).cuda(),
+                              pos, bs, lb * bs, 1.0 / math.sqrt(128))
+    assert_close_bf16(out16.cpu().numpy(), g["out"])
 
 
 def _paged_setup(rng, R, seq_lens, bs, Hkv, D, extra_pages=7):

@@ -181,3 +181,38 @@ def test_rope_and_store_kv_bitwise(Hq, Hkv):
     untouched = torch.ones(P * bs, dtype=torch.bool, device="cuda")
     untouched[slots] = False
     assert torch.all(kc[untouched] == 3.0) and torch.all(vc[untouched] == 5.0)
+
+
+@pytest.mark.parametrize("kdtype,bs,R", [(torch.float32, 32, 300), (torch.bfloat16, 64, 40)])
+def test_fused_kbar_refresh_equals_separate_refresh(kdtype, bs, R):
+    """A decode step's index-K write with the k-bar refresh of each token's
+    tail page in the same kernel gives k-bar rows bitwise equal to the separate
+    dash_kbar_pool launch (and to the oracle)."""
+    from ananta_ocr_b200.unlimited_dash_ops import route_triton as RT
+    from oracle import dash_oracle as O
+    Hd, W = 1280, 40
+    P = R * W
+    h, wq, wk, nq, nk, cos, sin = rand_inputs(9, R, Hd)
+    g = torch.Generator(device="cuda").manual_seed(2)
+    cache = (torch.randn(P, bs, 128, generator=g, device="cuda") * 0.5).to(kdtype)
+    bt = torch.randperm(P, generator=g, device="cuda").to(torch.int32).view(R, W)
+    seq = torch.randint(1, W * bs, (R,), generator=g, device="cuda").to(torch.int32)   # incl. this token
+    pos = seq.long() - 1
+    slots = bt.long().gather(1, (pos // bs)[:, None])[:, 0] * bs + pos % bs
+    hc = torch.randn(128, generator=g, device="cuda") * 0.3
+    plan = RT.kbar_tail_plan(block_table=bt, seq_lens=seq, block_size=bs, tail_pages=1, device="cuda")
+    k_fused = torch.full((P, 128), 3.0, device="cuda")
+    k_sep = k_fused.clone()
+    c1 = cache.clone()
+    index_qk_fused(h, wq, wk, nq, nk, 1e-6, cos, sin, index_cache=c1, slot_mapping=slots,
+                   kbar_refresh=(k_fused, plan, hc, bs))
+    c2 = cache.clone()
+    index_qk_fused(h, wq, wk, nq, nk, 1e-6, cos, sin, index_cache=c2, slot_mapping=slots)
+    RT.kbar_refresh_tail_triton(kv_cache=c2, k_bar=k_sep, block_table=bt, seq_lens=seq, head_cls=hc,
+                                block_size=bs, plan=plan)
+    assert torch.equal(c1, c2)
+    assert torch.equal(k_fused, k_sep)
+    pages, ntok = (t.cpu().numpy() for t in plan)
+    ref = np.full((P, 128), 3.0, np.float32)
+    O.kbar_paged(c2.float().cpu().numpy(), pages, ntok, hc.cpu().numpy(), ref)
+    assert np.array_equal(k_fused.cpu().numpy(), ref)

@@ -421,3 +421,60 @@ def test_serving_plans_match_reference_golden_and_oracle():
     np.testing.assert_array_equal(t.cpu().numpy(), rt_)
     r2r = RT.prefill_row2req(cu_seqlens_q=torch.from_numpy(cu).to(dev), device=dev)
     np.testing.assert_array_equal(r2r.cpu().numpy(), P.rows_to_requests(cu))
+
+
+def test_page2d_coordinates_match_reference_golden():
+    """Page2D coordinates over a serving trace (chunked prefills, decode
+    steps, a state row reused by a new request) against the wheel's
+    PageCoordState.step / decode_meta_fused, and the cos/sin tables against
+    PageRope2D.cos_sin (fp32) and cos_sin_2d_fused (bf16)."""
+    from ananta_ocr_b200.unlimited_dash_ops import page2d_rope as PR
+    from ananta_ocr_b200.unlimited_dash_ops import decode_meta_triton as DMT
+    from ananta_ocr_b200.unlimited_dash_ops import page_state as PSM
+    g = np.load(os.path.join(GOLD, "page_coords.npz"))
+    dev = torch.device("cuda")
+    IMG, PG = 128815, 128827
+    cfg = {"image_token_id": IMG, "page_token_id": PG, "per_page_image_tokens": 24}
+    sbs, P = int(g["sbs"]), int(g["P"])
+    coord = PR.PageCoordState(cfg, max_reqs=int(g["max_reqs"]), max_pages=int(g["max_pages"]))
+    pst = PSM.PageIsolationState(cfg, sbs)
+    rope = PR.PageRope2D(128, 10000.0, 256.0, 1, "resample", page_mod=int(g["page_mod"]))
+    np.testing.assert_array_equal(rope.inv_tok.numpy(), g["inv_tok"])
+    np.testing.assert_array_equal(rope.inv_page.numpy(), g["inv_page"])
+    bt = torch.from_numpy(g["bt"]).to(dev)
+    for i in range(int(g["steps"])):
+        rows = g[f"s{i}_rows"]
+        ids = torch.from_numpy(g[f"s{i}_ids"]).to(dev)
+        btab = bt[torch.from_numpy(rows).to(dev)]
+        if int(g[f"s{i}_decode"]):
+            seq = torch.from_numpy(g[f"s{i}_start_pos"] + 1).to(dev, torch.int32)
+            q_page, (tok, page) = DMT.decode_meta_fused(
+                input_ids=ids, block_table=btab, seq_lens=seq,
+                slot_mapping=torch.from_numpy(g[f"s{i}_slots"]).to(dev), page_state=pst,
+                coord_state=coord, num_slots=P * sbs, block_size=sbs)
+            np.testing.assert_array_equal(q_page.cpu().numpy(), g[f"s{i}_q_page"])
+            T = tok.shape[0]
+            cos = torch.zeros(T, 128, dtype=torch.bfloat16, device=dev)
+            sin = torch.zeros_like(cos)
+            DMT.cos_sin_2d_fused(rope=rope, tok_pos=tok, page_pos=page, dtype=torch.bfloat16,
+                                 out_cos=cos, out_sin=sin)
+            # the interpreted Triton golden truncates to bf16 (the CPU
+            # interpreter's conversion); the GPU kernel and torch round to
+            # nearest: compare with the torch fp32 table rounded to nearest
+            for got, key, k32 in ((cos, "cos_fused", "cos32"), (sin, "sin_fused", "sin32")):
+                a = got.view(torch.int16).cpu().numpy().astype(np.int32)
+                rn = torch.from_numpy(g[f"s{i}_{k32}"]).bfloat16().view(torch.int16).numpy()
+                assert np.abs(a - rn.astype(np.int32)).max() <= 1
+                assert (a == rn).mean() >= 0.99
+                assert np.abs(a - g[f"s{i}_{key}"].astype(np.int32)).max() <= 1
+        else:
+            layout = types.SimpleNamespace(
+                num_tokens=int(ids.shape[0]), q_start=torch.from_numpy(g[f"s{i}_q_start"]).to(dev),
+                start_pos=torch.from_numpy(g[f"s{i}_start_pos"]).to(dev), block_table=btab,
+                num_decode_tokens=0, gen_start=None)
+            tok, page = coord.step(ids, layout)
+        np.testing.assert_array_equal(tok.cpu().numpy(), g[f"s{i}_tok"])
+        np.testing.assert_array_equal(page.cpu().numpy(), g[f"s{i}_page"])
+        c32, s32 = rope.cos_sin(tok, page, torch.float32)
+        np.testing.assert_allclose(c32.cpu().numpy(), g[f"s{i}_cos32"], atol=2e-6, rtol=0)
+        np.testing.assert_allclose(s32.cpu().numpy(), g[f"s{i}_sin32"], atol=2e-6, rtol=0)
