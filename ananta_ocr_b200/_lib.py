@@ -96,9 +96,9 @@ class DashBlockMaxArgs(C.Structure):
 class DashPrefillArgs(C.Structure):
     _fields_ = [("seqs", DashSeqs), ("kv", DashKV), ("routes", DashRoutes), ("qo", DashQO),
                 ("seg_start", _p), ("scale", _f32), ("block_size", _i32),
-                ("local_window", _i32), ("pad0", _i32), ("workspace", _p),
+                ("local_window", _i32), ("mode", _i32), ("workspace", _p),
                 ("workspace_bytes", C.c_size_t), ("device_error", _p), ("out_peers", _p),
-                ("n_peers", _i32), ("pad1", _i32)]
+                ("n_peers", _i32), ("part_budget_mib", _i32)]
 
 
 class DashPeerHandle(C.Structure):

@@ -228,6 +228,12 @@ int dash_prefill_attn(const DashPrefillArgs* a, dash_stream_t stream) {
     return set_error(DASH_ERR_INVALID, "contiguous K/V needs kv_len_fixed (allocated length)");
   if (a->n_peers < 0 || a->n_peers > 64 || (a->n_peers > 0 && !a->out_peers))
     return set_error(DASH_ERR_INVALID, "n_peers must be in [0, 64] with an out_peers array");
+  if (a->mode < 0 || a->mode > 2) return set_error(DASH_ERR_INVALID, "mode %d not in {0,1,2}", a->mode);
+  if (a->part_budget_mib < 0) return set_error(DASH_ERR_INVALID, "part_budget_mib must be >= 0");
+  if (a->mode == 2 && !prefill_gathered_supported(*a))
+    return set_error(DASH_ERR_UNSUPPORTED, "gathered prefill needs bf16/fp16, block_size 32/64/128, "
+                     "1/2/4 query heads per kv head and 0 < K <= 256 (block_size %d, K %d)",
+                     a->block_size, a->routes.K);
   int64_t rows = seq_rows(a->seqs);
   size_t need = prefill_workspace(*a, rows);
   if (need && (!a->workspace || a->workspace_bytes < need))

@@ -17,6 +17,8 @@ int launch_block_max(const DashBlockMaxArgs& a, cudaStream_t st);
 int launch_decode(const DashDecodeArgs& a, int64_t n_rows, int splits, cudaStream_t st);
 int launch_prefill(const DashPrefillArgs& a, int64_t n_rows, cudaStream_t st);
 size_t prefill_workspace(const DashPrefillArgs& a, int64_t n_rows);
+// the routed part gathered by key block is implemented for these arguments
+bool prefill_gathered_supported(const DashPrefillArgs& a);
 size_t decode_workspace(const DashDecodeArgs& a, int64_t n_rows, int splits);
 int decode_auto_splits(const DashDecodeArgs& a, int64_t n_rows);
 int validate_decode(const DashDecodeArgs* a, int* splits);   // DASH_OK or a status with message

@@ -27,6 +27,7 @@
 // sparse_gather_triton.py:29-104 (_gather_attn_fwd_kernel, seg/packing),
 // WHL attend_triton.py:88-292 (_dash_sparse_fwd_kernel, paged).
 #include <cudaTypedefs.h>
+#include <algorithm>
 #include <climits>
 #include "dash_common.cuh"
 #include "dash_internal.h"
@@ -86,10 +87,13 @@ __global__ void __launch_bounds__(kPlanWarps * 32) plan_kernel(DashPrefillArgs a
                                                                int32_t* cidx, float* cbias,
                                                                uint32_t* tmask, float* rowmax) {
   __shared__ uint32_t s_mask[MAX_MASK_WORDS];
+  extern __shared__ uint32_t s_flags[];        // gathered mode: [nblk_cap][wpt]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, ih = blockIdx.y;
   const int s = tile / p.tiles_per_seq, t = tile - s * p.tiles_per_seq;
   for (int w = threadIdx.x; w < p.nwords; w += kPlanWarps * 32) s_mask[w] = 0u;
+  if (p.flags)
+    for (int w = threadIdx.x; w < p.nblk_cap * p.wpt; w += kPlanWarps * 32) s_flags[w] = 0u;
   __syncthreads();
   const int qlen = q_len_of(a.seqs, s);
   const int i_end = min(qlen, (t + 1) * p.TT);
@@ -218,6 +222,10 @@ __global__ void __launch_bounds__(kPlanWarps * 32) plan_kernel(DashPrefillArgs a
     for (int q = 0; q < PER; ++q) {
       if (keep[q]) {
         atomicOr(s_mask + (b[q] >> 5), 1u << (b[q] & 31));
+        if (p.flags) {
+          const int li = i - t * p.TT;                  // token within this tile
+          atomicOr(s_flags + b[q] * p.wpt + (li >> 5), 1u << (li & 31));
+        }
         if (a.routes.bias) bmax = fmaxf(bmax, bias[q]);
       }
     }
@@ -227,6 +235,14 @@ __global__ void __launch_bounds__(kPlanWarps * 32) plan_kernel(DashPrefillArgs a
   __syncthreads();
   uint32_t* tm = tmask + ((int64_t)ih * a.seqs.n_seq * p.tiles_per_seq + tile) * p.nwords;
   for (int w = threadIdx.x; w < p.nwords; w += kPlanWarps * 32) tm[w] = s_mask[w];
+  if (p.flags) {
+    // this tile owns words [t*wpt, (t+1)*wpt) of every block's row mask
+    uint32_t* fl = p.flags + ((int64_t)ih * a.seqs.n_seq + s) * p.nblk_cap * p.wps + (int64_t)t * p.wpt;
+    for (int e = threadIdx.x; e < p.nblk_cap * p.wpt; e += kPlanWarps * 32) {
+      const int bb = e / p.wpt, w = e - bb * p.wpt;
+      fl[(int64_t)bb * p.wps + w] = s_flags[e];
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -295,12 +311,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_seq = a.seqs.n_seq;
-  // two consecutive query tiles per CTA; heaviest (last) pairs first
-  const int pairs = (p.tiles_per_seq + 1) >> 1;
-  const int jj = blockIdx.x / n_seq;
-  const int s = blockIdx.x - jj * n_seq;
-  const int pj = pairs - 1 - jj;
-  const int hk = blockIdx.y;
+  // two consecutive query tiles per CTA; heaviest (last) pairs of the
+  // chunk first
+  const int jj = blockIdx.x / p.sn;
+  const int s = p.s0 + (blockIdx.x - jj * p.sn);
+  const int pj = p.pj0 + p.npj - 1 - jj;
+  const int hk = p.hk0 + blockIdx.y;
   const int qlen = q_len_of(a.seqs, s);
   const int i0A = 2 * pj * p.TT;
   if (i0A >= qlen) return;
@@ -342,7 +358,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int64_t lb0 = max((int64_t)0, (pmin - a.local_window + 1) / bs);
     const int64_t lb1 = pmax / bs;
     for (int w = tid; w < p.nwords; w += NTHREADS) {
-      uint32_t m = umA[w] | (umB ? umB[w] : 0u);
+      // gathered mode: the local window only (the routed keys are partials)
+      uint32_t m = p.flags ? 0u : (umA[w] | (umB ? umB[w] : 0u));
       int64_t b0 = (int64_t)w * 32;
       for (int k = 0; k < 32; ++k) {
         int64_t b = b0 + k;
@@ -539,8 +556,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(q_full);
       }
-      // routed list cursor
-      const int K = a.routes.K;
+      // routed list cursor (none in gathered mode: the routed keys arrive as
+      // partials merged in the epilogue)
+      const int K = p.flags ? 0 : a.routes.K;
       // rows past the end of the tile read row 0's list (never used)
       const int64_t lrow = (int64_t)ih * p.n_rows + (row_ok ? rglob : 0);
       const int32_t* rl = p.cidx + lrow * K;
@@ -779,10 +797,34 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         b21 = b21_next;
       }
       // ---- epilogue ----
-      float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
       bool have_o = alive && it > 0;
       if (have_o && !mbar_wait_warp(pv_done + ((it - 1) & 1), ((it - 1) >> 1) & 1, abort_flag, derr, 64)) have_o = false;
       tc_fence_after();
+      // Gathered mode: the row's routed keys arrive as normalised partials
+      // (log2-sum-exp lse_j) from the routed kernel; the output is the softmax
+      // merge of the window part (O, l relative to m_run) and the partials,
+      // all weights taken relative to their common max Mx.  Otherwise there
+      // are no partials and this is O / l.
+      const int Kf = a.routes.K;
+      const int64_t rsafe = row_ok ? rglob : 0;
+      const int32_t* rlist = p.cidx + ((int64_t)ih * p.n_rows + rsafe) * Kf;
+      const int64_t pbase =
+          ((((int64_t)(s - p.s0) * p.prows + (tok - 2 * p.pj0 * p.TT)) * p.hqn + (hq - p.hq0)) * Kf);
+      const bool win = have_o && l_run > 0.0f;
+      float Mx = win ? m_run : -INFINITY;
+      int npart = 0;
+      if (p.flags && row_ok) {
+        for (int j = 0; j < Kf && rlist[j] >= 0; ++j) {
+          Mx = fmaxf(Mx, p.part_lse[pbase + j]);
+          ++npart;
+        }
+      }
+      // every key masked (all weights 0): keep the weights finite
+      if (Mx == -INFINITY) Mx = 0.0f;
+      const float sL = win ? exp2f(m_run - Mx) : 0.0f;
+      float den = win ? l_run * sL : 0.0f;
+      for (int j = 0; j < npart; ++j) den += exp2f(p.part_lse[pbase + j] - Mx);
+      const float inv_den = den > 0.0f ? 1.0f / den : 0.0f;
       T* op = reinterpret_cast<T*>(a.qo.out) +
               (a.seqs.q_start ? rglob * a.qo.o_stride_tok
                               : (int64_t)s * a.qo.o_stride_seq + (int64_t)tok * a.qo.o_stride_tok) +
@@ -793,13 +835,27 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tmem_ld32(tO + q4 * 32 + lane_base, o);
         tmem_ld_wait();
         if (row_ok) {
+          float acc[32];
+  #pragma unroll
+          for (int c = 0; c < 32; ++c) acc[c] = win ? __uint_as_float(o[c]) * sL : 0.0f;
+          for (int j = 0; j < npart; ++j) {
+            const float w = exp2f(p.part_lse[pbase + j] - Mx);
+            const uint4* src = reinterpret_cast<const uint4*>(p.part_o + (pbase + j) * HD + q4 * 32);
+  #pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              const uint4 u = src[v];
+              const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
+  #pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = unpack2(uu[e], (T*)nullptr);
+                acc[8 * v + 2 * e] = fmaf(w, f.x, acc[8 * v + 2 * e]);
+                acc[8 * v + 2 * e + 1] = fmaf(w, f.y, acc[8 * v + 2 * e + 1]);
+              }
+            }
+          }
           uint32_t pko[16];
   #pragma unroll
-          for (int c = 0; c < 32; c += 2) {
-            float a0 = have_o ? __uint_as_float(o[c]) * inv_l : 0.0f;
-            float a1 = have_o ? __uint_as_float(o[c + 1]) * inv_l : 0.0f;
-            pko[c >> 1] = pack2(a0, a1, (T*)nullptr);
-          }
+          for (int c = 0; c < 32; c += 2) pko[c >> 1] = pack2(acc[c] * inv_den, acc[c + 1] * inv_den, (T*)nullptr);
   #pragma unroll
           for (int v = 0; v < 4; ++v)
             *reinterpret_cast<uint4*>(op + q4 * 32 + v * 8) = make_uint4(pko[4 * v], pko[4 * v + 1], pko[4 * v + 2], pko[4 * v + 3]);
@@ -818,7 +874,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       // of its writes are performed, and the caller's completion step is
       // stream-ordered after the grid, so it sees every row in place.
       if (row_ok && a.qo.lse) {
-        float lse = l_run > 0.0f ? (m_run + log2f(l_run)) * 0.6931471805599453f : -INFINITY;
+        float lse = den > 0.0f ? (Mx + log2f(den)) * 0.6931471805599453f : -INFINITY;
         a.qo.lse[(a.seqs.q_start ? rglob * a.qo.lse_stride_tok
                                  : (int64_t)s * a.qo.lse_stride_seq + (int64_t)tok * a.qo.lse_stride_tok) +
                  (int64_t)hq * a.qo.lse_stride_head] = lse;
@@ -846,7 +902,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
-static int make_kv_map(CUtensorMap* map, const void* base, const DashPrefillArgs& a, bool paged) {
+// K/V tensor map, boxes of 64 dims x `rows` tokens (128-byte swizzle)
+static int make_kv_map(CUtensorMap* map, const void* base, const DashPrefillArgs& a, bool paged, int rows) {
   auto enc = get_encode();
   if (!enc) return set_error(DASH_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
   const int esz = 2;
@@ -858,9 +915,7 @@ static int make_kv_map(CUtensorMap* map, const void* base, const DashPrefillArgs
   strides[0] = (cuuint64_t)a.kv.stride_tok * esz;
   strides[1] = (cuuint64_t)a.kv.stride_head * esz;
   strides[2] = (cuuint64_t)a.kv.stride_seq * esz;
-  // 32-token pages are loaded as two 32-row boxes per key tile
-  const cuuint32_t rows = (paged && a.block_size < BN) ? (cuuint32_t)a.block_size : (cuuint32_t)BN;
-  cuuint32_t box[4] = {64, rows, 1, 1};
+  cuuint32_t box[4] = {64, (cuuint32_t)rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   for (int k = 0; k < 3; ++k)
     if (strides[k] % 16 != 0 || strides[k] == 0)
@@ -885,20 +940,172 @@ static void plan_geometry(const DashPrefillArgs& a, int64_t n_rows, PrefillPlan&
                        : (a.seqs.kv_len_fixed + a.block_size - 1) / a.block_size;
   p.nwords = (p.nblk_cap + 31) / 32;
   p.n_rows = n_rows;
+  // one chunk: every sequence, tile pair and kv head
+  p.s0 = 0;
+  p.sn = a.seqs.n_seq;
+  p.pj0 = 0;
+  p.npj = (p.tiles_per_seq + 1) / 2;
+  p.hk0 = 0;
+  p.hq0 = 0;
+  p.hqn = a.qo.n_heads;
+}
+
+bool prefill_gathered_supported(const DashPrefillArgs& a) {
+  if (a.kv.dtype == DASH_DTYPE_F32 || a.kv.n_kv_heads <= 0) return false;
+  const int G = a.qo.n_heads / a.kv.n_kv_heads;
+  const int bs = a.block_size;
+  return (bs == 32 || bs == 64 || bs == 128) && (G == 1 || G == 2 || G == 4) && a.routes.K > 0 &&
+         a.routes.K <= kPlanMaxK;
+}
+
+// Mode 0 picks the gathered routed part when a tile's rows are unlikely to
+// share blocks: the remote span averaged over a causal sequence, in blocks,
+// is well above the routed slots per row.
+static bool use_gathered(const DashPrefillArgs& a) {
+  if (a.mode == 1 || !prefill_gathered_supported(a)) return false;
+  if (a.mode == 2) return true;
+  const int bs = a.block_size;
+  const double local_blocks = (double)(a.local_window + bs - 1) / bs;
+  const double remote = (double)a.seqs.max_q_len / 2.0 / bs - local_blocks;
+  return a.seqs.max_q_len >= 2048 && remote > 2.5 * a.routes.K;
+}
+
+// Gathered mode: chunks of sequences x tile pairs x kv heads whose partials
+// (bf16/fp16 output row + fp32 log2-sum-exp per list slot) fit the budget.
+struct GatherChunks {
+  int hcn, sn, npj;      // kv heads, sequences, tile pairs per chunk
+  int wpt, wps;          // flag words per tile / per (sequence, block)
+  size_t flags_bytes, lse_bytes, o_bytes;
+};
+constexpr size_t kPartBytes = HD * 2 + 4;        // one partial
+constexpr int kDefaultPartMiB = 2048;
+
+static GatherChunks gather_chunks(const DashPrefillArgs& a, const PrefillPlan& p) {
+  GatherChunks c{};
+  const int nih = a.routes.n_index_heads > 0 ? a.routes.n_index_heads : 1;
+  c.wpt = p.TT / 32;
+  c.wps = p.tiles_per_seq * c.wpt;
+  c.flags_bytes = (size_t)nih * a.seqs.n_seq * p.nblk_cap * c.wps * 4;
+  const int pairs = (p.tiles_per_seq + 1) / 2;
+  const int nkv = a.kv.n_kv_heads, ns = a.seqs.n_seq;
+  // one unit = (sequence, tile pair, kv head): 256 query rows x heads
+  const size_t unit = (size_t)2 * BM * a.routes.K * kPartBytes;
+  const size_t budget = (size_t)(a.part_budget_mib > 0 ? a.part_budget_mib : kDefaultPartMiB) << 20;
+  const size_t cap = budget / unit > 0 ? budget / unit : 1;
+  auto balance = [](int total, size_t per) -> int {
+    const int n = (int)((total + per - 1) / per);          // chunks
+    return (total + n - 1) / n;                            // even split
+  };
+  c.hcn = nkv;
+  c.sn = ns;
+  c.npj = pairs;
+  if ((size_t)ns * pairs * nkv > cap) {
+    if ((size_t)ns * pairs <= cap) {
+      c.hcn = balance(nkv, cap / ((size_t)ns * pairs));
+    } else if ((size_t)pairs <= cap) {
+      c.hcn = 1;
+      c.sn = balance(ns, cap / pairs);
+    } else {
+      c.hcn = 1;
+      c.sn = 1;
+      c.npj = balance(pairs, cap);
+    }
+  }
+  const size_t entries = (size_t)c.sn * (2 * c.npj * p.TT) * (c.hcn * p.G) * a.routes.K;
+  c.lse_bytes = entries * 4;
+  c.o_bytes = entries * HD * 2;
+  return c;
 }
 
 // Workspace: canonical block lists, their biases (two per entry with
-// 32-token blocks), per-tile unions, per-row largest bias.
+// 32-token blocks in the tile-major kernel), per-tile unions, per-row largest
+// bias; gathered mode adds the per-block row flags and the partials.
 static size_t round256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+struct PrefillWs {
+  size_t lists, blists, masks, rowmax;
+  size_t flags, lse, o;
+  size_t total() const { return lists + blists + masks + rowmax + flags + lse + o; }
+};
+
+static PrefillWs prefill_ws(const DashPrefillArgs& a, int64_t n_rows, const PrefillPlan& p, bool gathered) {
+  PrefillWs w{};
+  const int nih = a.routes.n_index_heads > 0 ? a.routes.n_index_heads : 1;
+  const bool pair = a.block_size == 32 && a.kv.dtype != DASH_DTYPE_F32 && !gathered;
+  w.lists = round256((size_t)nih * n_rows * a.routes.K * 4);
+  w.blists = pair ? 2 * w.lists : w.lists;
+  w.masks = round256((size_t)nih * a.seqs.n_seq * p.tiles_per_seq * p.nwords * 4);
+  w.rowmax = round256((size_t)nih * n_rows * 4);
+  if (gathered) {
+    const GatherChunks c = gather_chunks(a, p);
+    w.flags = round256(c.flags_bytes);
+    w.lse = round256(c.lse_bytes);
+    w.o = round256(c.o_bytes);
+  }
+  return w;
+}
 
 size_t prefill_workspace(const DashPrefillArgs& a, int64_t n_rows) {
   PrefillPlan p{};
   plan_geometry(a, n_rows, p);
+  return prefill_ws(a, n_rows, p, use_gathered(a)).total();
+}
+
+template <bool PAIR>
+static int launch_plan(const DashPrefillArgs& a, const PrefillPlan& p, int32_t* cidx, float* cbias,
+                       uint32_t* tmask, float* rowmax, cudaStream_t st) {
   const int nih = a.routes.n_index_heads > 0 ? a.routes.n_index_heads : 1;
-  const size_t lists = round256((size_t)nih * n_rows * a.routes.K * 4);
-  const size_t blists = (a.block_size == 32 && a.kv.dtype != DASH_DTYPE_F32) ? 2 * lists : lists;
-  size_t masks = (size_t)nih * a.seqs.n_seq * p.tiles_per_seq * p.nwords * 4;
-  return lists + blists + round256(masks) + (size_t)nih * n_rows * 4;
+  // every tile's union words (and flag words) are written, also with no lists
+  dim3 g1((unsigned)(a.seqs.n_seq * p.tiles_per_seq), nih);
+  const int K = a.routes.K;
+  const size_t dyn = p.flags ? (size_t)p.nblk_cap * p.wpt * 4 : 0;
+  auto plan = [&](auto kern) -> int {
+    if (dyn > 0 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) != cudaSuccess)
+      return set_error(DASH_ERR_CUDA, "cudaFuncSetAttribute(plan_kernel) failed");
+    kern<<<g1, kPlanWarps * 32, dyn, st>>>(a, p, cidx, cbias, tmask, rowmax);
+    count_launch();
+    return check_launch("plan_kernel");
+  };
+  if (K <= 32) return plan(plan_kernel<1, PAIR>);
+  if (K <= 64) return plan(plan_kernel<2, PAIR>);
+  return plan(plan_kernel<kPlanMaxK / 32, PAIR>);
+}
+
+template <typename T, bool PAGED, bool PAIR>
+static int launch_local(const DashPrefillArgs& a, const PrefillPlan& p, const CUtensorMap& mk,
+                        const CUtensorMap& mv, int hcn, cudaStream_t st) {
+  auto kern = prefill_kernel<T, PAGED, PAIR>;
+  // the in-kernel register growth waits until the pool covers it: launch
+  // only a build whose per-thread count matches the split
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess)
+    return set_error(DASH_ERR_CUDA, "cudaFuncGetAttributes(prefill_kernel) failed");
+  if (fa.numRegs != kLaunchRegs)
+    return set_error(DASH_ERR_UNSUPPORTED, "prefill_kernel built with %d registers per thread, "
+                     "the register split needs %d", fa.numRegs, kLaunchRegs);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
+    return set_error(DASH_ERR_CUDA, "cudaFuncSetAttribute(prefill_kernel) failed");
+  dim3 grid((unsigned)(p.sn * p.npj), (unsigned)hcn);
+  kern<<<grid, NTHREADS, SMEM_BYTES, st>>>(mk, mv, a, p);
+  count_launch();
+  return check_launch("prefill_kernel");
+}
+
+static int launch_local_any(const DashPrefillArgs& a, const PrefillPlan& p, const CUtensorMap& mk,
+                            const CUtensorMap& mv, bool pair, int hcn, cudaStream_t st) {
+  const bool paged = p.paged != 0;
+  if (a.kv.dtype == DASH_DTYPE_BF16) {
+    if (pair)
+      return paged ? launch_local<__nv_bfloat16, true, true>(a, p, mk, mv, hcn, st)
+                   : launch_local<__nv_bfloat16, false, true>(a, p, mk, mv, hcn, st);
+    return paged ? launch_local<__nv_bfloat16, true, false>(a, p, mk, mv, hcn, st)
+                 : launch_local<__nv_bfloat16, false, false>(a, p, mk, mv, hcn, st);
+  }
+  if (pair)
+    return paged ? launch_local<__half, true, true>(a, p, mk, mv, hcn, st)
+                 : launch_local<__half, false, true>(a, p, mk, mv, hcn, st);
+  return paged ? launch_local<__half, true, false>(a, p, mk, mv, hcn, st)
+               : launch_local<__half, false, false>(a, p, mk, mv, hcn, st);
 }
 
 int launch_prefill(const DashPrefillArgs& a, int64_t n_rows, cudaStream_t st) {
@@ -908,75 +1115,72 @@ int launch_prefill(const DashPrefillArgs& a, int64_t n_rows, cudaStream_t st) {
   if (p.nwords > MAX_MASK_WORDS)
     return set_error(DASH_ERR_UNSUPPORTED, "too many blocks per sequence (%d > %d)", p.nblk_cap,
                      MAX_MASK_WORDS * 32);
-  const int nih = a.routes.n_index_heads > 0 ? a.routes.n_index_heads : 1;
-  // 32-token blocks pair up in the tensor-core kernel's 64-key tiles; the
-  // fp32 kernel reads plain per-block lists
   const bool f32 = a.kv.dtype == DASH_DTYPE_F32;
-  const bool pair = a.block_size == 32 && !f32;
-  const size_t lists = round256((size_t)nih * n_rows * a.routes.K * 4);
-  const size_t blists = pair ? 2 * lists : lists;
+  const bool gathered = use_gathered(a);
+  // 32-token blocks pair up in the tile-major kernel's 64-key tiles (also
+  // for the window part in gathered mode); the fp32 kernel and the routed
+  // kernel read plain per-block lists
+  const bool pair_kernel = a.block_size == 32 && !f32;
+  const bool pair_plan = pair_kernel && !gathered;
+  const PrefillWs w = prefill_ws(a, n_rows, p, gathered);
   uint8_t* ws = reinterpret_cast<uint8_t*>(a.workspace);
   int32_t* cidx = reinterpret_cast<int32_t*>(ws);
-  float* cbias = reinterpret_cast<float*>(ws + lists);
-  uint32_t* tmask = reinterpret_cast<uint32_t*>(ws + lists + blists);
-  size_t masks = (size_t)nih * a.seqs.n_seq * p.tiles_per_seq * p.nwords * 4;
+  float* cbias = reinterpret_cast<float*>(ws + w.lists);
+  uint32_t* tmask = reinterpret_cast<uint32_t*>(ws + w.lists + w.blists);
+  float* rowmax = reinterpret_cast<float*>(ws + w.lists + w.blists + w.masks);
   p.cidx = cidx;
   p.cbias = cbias;
   p.tmask = tmask;
-  float* rowmax = reinterpret_cast<float*>(ws + lists + blists + round256(masks));
   p.rowmax = rowmax;
-  {
-    // every tile's union words are written (also with no routed lists)
-    dim3 g1((unsigned)(a.seqs.n_seq * p.tiles_per_seq), nih);
-    const int K = a.routes.K;
-    auto plan = [&](auto kern) { kern<<<g1, kPlanWarps * 32, 0, st>>>(a, p, cidx, cbias, tmask, rowmax); };
-    if (pair) {
-      if (K <= 32) plan(plan_kernel<1, true>);
-      else if (K <= 64) plan(plan_kernel<2, true>);
-      else plan(plan_kernel<kPlanMaxK / 32, true>);
-    } else {
-      if (K <= 32) plan(plan_kernel<1, false>);
-      else if (K <= 64) plan(plan_kernel<2, false>);
-      else plan(plan_kernel<kPlanMaxK / 32, false>);
-    }
-    count_launch();
-    int rc = check_launch("plan_kernel");
-    if (rc) return rc;
+  GatherChunks gc{};
+  if (gathered) {
+    gc = gather_chunks(a, p);
+    uint8_t* g = ws + w.lists + w.blists + w.masks + w.rowmax;
+    p.flags = reinterpret_cast<uint32_t*>(g);
+    p.wpt = gc.wpt;
+    p.wps = gc.wps;
+    p.part_lse = reinterpret_cast<const float*>(g + w.flags);
+    p.part_o = reinterpret_cast<const uint16_t*>(g + w.flags + w.lse);
   }
+  int rc = pair_plan ? launch_plan<true>(a, p, cidx, cbias, tmask, rowmax, st)
+                     : launch_plan<false>(a, p, cidx, cbias, tmask, rowmax, st);
+  if (rc) return rc;
   if (f32) return launch_prefill_f32(a, p, st);
   CUtensorMap mk, mv;
-  int rc = make_kv_map(&mk, a.kv.k, a, p.paged);
+  const int rows = (p.paged && a.block_size < BN) ? a.block_size : BN;
+  rc = make_kv_map(&mk, a.kv.k, a, p.paged, rows);
+  if (!rc) rc = make_kv_map(&mv, a.kv.v, a, p.paged, rows);
   if (rc) return rc;
-  rc = make_kv_map(&mv, a.kv.v, a, p.paged);
-  if (rc) return rc;
-  dim3 grid((unsigned)(a.seqs.n_seq * ((p.tiles_per_seq + 1) / 2)), a.kv.n_kv_heads);
-  auto launch = [&](auto kern) -> int {
-    // the in-kernel register growth waits until the pool covers it: launch
-    // only a build whose per-thread count matches the split
-    cudaFuncAttributes fa;
-    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess)
-      return set_error(DASH_ERR_CUDA, "cudaFuncGetAttributes(prefill_kernel) failed");
-    if (fa.numRegs != kLaunchRegs)
-      return set_error(DASH_ERR_UNSUPPORTED, "prefill_kernel built with %d registers per thread, "
-                       "the register split needs %d", fa.numRegs, kLaunchRegs);
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    kern<<<grid, NTHREADS, SMEM_BYTES, st>>>(mk, mv, a, p);
-    return DASH_OK;
-  };
-  if (a.kv.dtype == DASH_DTYPE_BF16) {
-    if (pair)
-      rc = p.paged ? launch(prefill_kernel<__nv_bfloat16, true, true>) : launch(prefill_kernel<__nv_bfloat16, false, true>);
-    else
-      rc = p.paged ? launch(prefill_kernel<__nv_bfloat16, true, false>) : launch(prefill_kernel<__nv_bfloat16, false, false>);
-  } else {
-    if (pair)
-      rc = p.paged ? launch(prefill_kernel<__half, true, true>) : launch(prefill_kernel<__half, false, true>);
-    else
-      rc = p.paged ? launch(prefill_kernel<__half, true, false>) : launch(prefill_kernel<__half, false, false>);
+  if (!gathered) return launch_local_any(a, p, mk, mv, pair_kernel, a.kv.n_kv_heads, st);
+  // gathered: the routed kernel's boxes hold min(block_size, 64) rows
+  CUtensorMap rk = mk, rv = mv;
+  const int rrows = a.block_size < BN ? a.block_size : BN;
+  if (rrows != rows) {
+    rc = make_kv_map(&rk, a.kv.k, a, p.paged, rrows);
+    if (!rc) rc = make_kv_map(&rv, a.kv.v, a, p.paged, rrows);
+    if (rc) return rc;
   }
-  if (rc) return rc;
-  count_launch();
-  return check_launch("prefill_kernel");
+  const int pairs = (p.tiles_per_seq + 1) / 2;
+  for (int hk0 = 0; hk0 < a.kv.n_kv_heads; hk0 += gc.hcn) {
+    const int hcn = std::min(gc.hcn, a.kv.n_kv_heads - hk0);
+    for (int s0 = 0; s0 < a.seqs.n_seq; s0 += gc.sn) {
+      for (int pj0 = 0; pj0 < pairs; pj0 += gc.npj) {
+        PrefillPlan c = p;
+        c.s0 = s0;
+        c.sn = std::min(gc.sn, a.seqs.n_seq - s0);
+        c.pj0 = pj0;
+        c.npj = std::min(gc.npj, pairs - pj0);
+        c.hk0 = hk0;
+        c.hq0 = hk0 * p.G;
+        c.hqn = hcn * p.G;
+        c.prows = 2 * c.npj * p.TT;
+        rc = launch_prefill_routed(a, c, rk, rv, hcn, st);
+        if (!rc) rc = launch_local_any(a, c, mk, mv, pair_kernel, hcn, st);
+        if (rc) return rc;
+      }
+    }
+  }
+  return DASH_OK;
 }
 
 }  // namespace dash

@@ -3,6 +3,7 @@
 // the sequence-layout helpers they share.
 #pragma once
 #include <cstdint>
+#include <cudaTypedefs.h>
 #include "../../include/dash_b200.h"
 
 namespace dash {
@@ -19,6 +20,25 @@ struct PrefillPlan {
   int32_t TT;              // tokens per tile (= 128 / G)
   int32_t paged;
   int32_t nblk_cap;
+  // gathered mode: per (index head, sequence, block) bitmask of the query
+  // tokens whose canonical list holds the block, [nih][n_seq][nblk_cap][wps]
+  // (bit i of word w: token 32w + i of the sequence); NULL in union mode
+  uint32_t* flags;
+  int32_t wps;             // words per (sequence, block)
+  int32_t wpt;             // words per query tile (TT / 32)
+  // Work chunk of the launch: sequences [s0, s0 + sn), query tile pairs
+  // [pj0, pj0 + npj) of each (pair j: tiles 2j, 2j+1, tokens [2j TT,
+  // 2(j+1) TT)), kv heads [hk0, hk0 + grid.y).  Union mode: everything.
+  int32_t s0, sn, pj0, npj;
+  int32_t hk0;
+  // gathered mode: the routed part's partials of this chunk, query heads
+  // [hq0, hq0 + hqn); entry ((((s - s0) * prows + i - 2 pj0 TT) * hqn + hq - hq0)
+  // * K + j) for token i, list slot j: the normalised output (bf16/fp16 bits,
+  // [.][128]) and its log2-sum-exp, merged in the local kernel's epilogue
+  int32_t hq0, hqn;
+  int32_t prows;           // partial rows per sequence (= 2 npj TT)
+  const uint16_t* part_o;
+  const float* part_lse;
 };
 
 __device__ __forceinline__ int kv_len_of(const DashSeqs& q, int s) {
@@ -36,5 +56,9 @@ __device__ __forceinline__ int64_t row_base(const DashSeqs& q, int s) {
 
 // Launches the fp32 CUDA-core kernel over plan_kernel's canonical lists.
 int launch_prefill_f32(const DashPrefillArgs& a, const PrefillPlan& p, cudaStream_t st);
+// Launches the routed (gathered) kernel over the plan's chunk (hcn kv heads
+// from p.hk0): K/V tensor maps with boxes of min(block_size, 64) rows.
+int launch_prefill_routed(const DashPrefillArgs& c, const PrefillPlan& p, const CUtensorMap& mk,
+                          const CUtensorMap& mv, int hcn, cudaStream_t st);
 
 }  // namespace dash

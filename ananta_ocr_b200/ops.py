@@ -4,6 +4,7 @@ any non-zero library status; there is no CPU path.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import math
 from dataclasses import dataclass
@@ -302,8 +303,37 @@ def _workspace(device, nbytes, key):
     return buf
 
 
+# Prefill work split (DashPrefillArgs.mode) for calls that leave it at 0:
+# 0 automatic, 1 tile-major, 2 routed part gathered by key block.
+PREFILL_MODE = 0
+
+
+@contextlib.contextmanager
+def prefill_mode(mode: int, part_budget_mib: int = 0):
+    """Within the block, prefill calls use ``mode`` (and the gathered mode's
+    partial scratch budget in MiB, 0 = the library default)."""
+    global PREFILL_MODE, PREFILL_PART_MIB
+    old = PREFILL_MODE, PREFILL_PART_MIB
+    PREFILL_MODE, PREFILL_PART_MIB = int(mode), int(part_budget_mib)
+    try:
+        yield
+    finally:
+        PREFILL_MODE, PREFILL_PART_MIB = old
+
+
+PREFILL_PART_MIB = 0
+
+
+def _apply_prefill_mode(args: L.DashPrefillArgs) -> None:
+    if args.mode == 0:
+        args.mode = PREFILL_MODE
+    if args.part_budget_mib == 0:
+        args.part_budget_mib = PREFILL_PART_MIB
+
+
 def prefill_attn(args: L.DashPrefillArgs, device, workspace: Optional[torch.Tensor] = None):
     L.load()
+    _apply_prefill_mode(args)
     need = L.load().dash_prefill_workspace_size(args)
     if workspace is None:
         workspace = _workspace(device, need, "prefill")
@@ -366,6 +396,22 @@ def gather_attention(q, k, v, idx, bias, *, block_size: int, local_window: int, 
         a.out_peers, a.n_peers = peers.data_ptr(), int(peers.numel())
     prefill_attn(a, q.device, workspace)
     return out
+
+
+def gather_attention_workspace_bytes(B: int, HQ: int, Hkv: int, T: int, K: int, *,
+                                     block_size: int, local_window: int,
+                                     n_index_heads: int = 1,
+                                     dtype: torch.dtype = torch.bfloat16) -> int:
+    """Scratch bytes ``gather_attention`` needs for these shapes (under the
+    current prefill mode), for callers that size a workspace once."""
+    a = L.DashPrefillArgs()
+    a.seqs = Seqs(n_seq=B, q_len=T, kv_len=T, max_q_len=T).c()
+    a.kv.dtype, a.kv.n_kv_heads, a.kv.head_dim = _DT[dtype], int(Hkv), 128
+    a.qo.n_heads = int(HQ)
+    a.routes.K, a.routes.n_index_heads = int(K), int(n_index_heads)
+    a.block_size, a.local_window = int(block_size), int(local_window)
+    _apply_prefill_mode(a)
+    return int(L.load().dash_prefill_workspace_size(a))
 
 
 # ---------------------------------------------------------------------------

@@ -785,15 +785,12 @@ def run_prefill_on(cfg, st, dev, steps, warmup):
 
 
 def _prefill_ws_bytes(cfg):
-    """Bytes of attention scratch (canonical lists, two biases per entry for
-    32-token blocks, per-tile unions, per-row largest bias) for a contiguous
-    prefill of ``cfg``; an upper bound of the library's own sizing."""
-    B, S, bs, K = cfg["B"], cfg["S"], cfg["bs"], cfg["K"]
-    rows = B * S
-    nblk = -(-S // bs)
-    lists = rows * K * 4 + 256
-    tiles = B * (-(-S // 128))
-    return lists * 3 + tiles * (-(-nblk // 32)) * 4 + 256 + rows * 4 + 4096
+    """Bytes of attention scratch for a contiguous prefill of ``cfg`` (the
+    library's own sizing under the current prefill mode)."""
+    from ananta_ocr_b200 import ops
+    return ops.gather_attention_workspace_bytes(
+        cfg["B"], cfg["H"], cfg.get("Hkv", cfg["H"]), cfg["S"], cfg["K"], block_size=cfg["bs"],
+        local_window=cfg["lb"] * cfg["bs"])
 
 
 def run_decode_setup(cfg, dev, seed):
@@ -939,6 +936,9 @@ def main():
                     help="launch eagerly instead of replaying captured CUDA graphs")
     ap.add_argument("--decode-rows", type=int, default=0,
                     help="decode batch override (small cases for profiler captures)")
+    ap.add_argument("--prefill-mode", type=int, default=0, choices=[0, 1, 2],
+                    help="prefill work split: 0 automatic, 1 tile-major, 2 routed part gathered "
+                         "by key block")
     args = ap.parse_args()
     cfg = C2 if args.workload == "c2" else C4
     if args.decode_rows > 0:
@@ -990,8 +990,9 @@ def main():
             sys.stdout.flush()
             os.dup2(saved_fd, 1)
             os.close(saved_fd)
-    from ananta_ocr_b200 import _lib
+    from ananta_ocr_b200 import _lib, ops as _ops
     _lib.load()
+    _ops.PREFILL_MODE = args.prefill_mode
 
     if args.workload == "c4":
         # config 4 alone: strong scaling over the ranks, gather inside the step

@@ -470,7 +470,12 @@ typedef struct {
   float scale;
   int32_t block_size;
   int32_t local_window;
-  int32_t pad0;
+  /* 0: automatic; 1: tile-major (each 128-row tile walks the union of its
+   * rows' blocks); 2: routed part gathered by key block (block sizes 32, 64,
+   * 128; 1, 2 or 4 query heads per kv head), merged into the window part.
+   * Automatic picks 2 when routes are sparse against the remote span
+   * (max_q_len / 2 / block_size - local blocks > 2.5 K, max_q_len >= 2048). */
+  int32_t mode;
   void* workspace;
   size_t workspace_bytes;
   DashDeviceError* device_error;
@@ -481,7 +486,9 @@ typedef struct {
    * the call on the same stream. */
   void* const* out_peers;
   int32_t n_peers;
-  int32_t pad1;
+  /* mode 2: scratch for the routed partials in MiB (0: 2048); the work runs
+   * in chunks of sequences x query tiles x kv heads whose partials fit it */
+  int32_t part_budget_mib;
 } DashPrefillArgs;
 size_t dash_prefill_workspace_size(const DashPrefillArgs* args);
 int dash_prefill_attn(const DashPrefillArgs* args, dash_stream_t stream);
