@@ -64,7 +64,6 @@ constexpr uint32_t TMEM_COLS = 512;               // per query tile: S0 | S1 | O
 // 2^kGrowLog2 (then p < 2^32: no bf16/fp32 overflow for any sequence length)
 constexpr float kGrowLog2 = 32.0f;
 constexpr float kGrowP = 4294967296.0f;
-constexpr int kPlanMaxK = 256;                    // routed slots per row
 
 // ---------------------------------------------------------------------------
 // plan_kernel: one CTA per (query tile, index head), one warp per token row
@@ -800,72 +799,43 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       bool have_o = alive && it > 0;
       if (have_o && !mbar_wait_warp(pv_done + ((it - 1) & 1), ((it - 1) >> 1) & 1, abort_flag, derr, 64)) have_o = false;
       tc_fence_after();
-      // Gathered mode: the row's routed keys arrive as normalised partials
-      // (log2-sum-exp lse_j) from the routed kernel; the output is the softmax
-      // merge of the window part (O, l relative to m_run) and the partials,
-      // all weights taken relative to their common max Mx.  Otherwise there
-      // are no partials and this is O / l.
-      const int Kf = a.routes.K;
-      const int64_t rsafe = row_ok ? rglob : 0;
-      const int32_t* rlist = p.cidx + ((int64_t)ih * p.n_rows + rsafe) * Kf;
-      const int64_t pbase =
-          ((((int64_t)(s - p.s0) * p.prows + (tok - 2 * p.pj0 * p.TT)) * p.hqn + (hq - p.hq0)) * Kf);
+      // Gathered mode: this kernel holds the row's window keys only; their
+      // normalised output and log2-sum-exp go to the row's partial slot K,
+      // merged with the routed partials by the merge kernel.
       const bool win = have_o && l_run > 0.0f;
-      float Mx = win ? m_run : -INFINITY;
-      int npart = 0;
-      if (p.flags && row_ok) {
-        for (int j = 0; j < Kf && rlist[j] >= 0; ++j) {
-          Mx = fmaxf(Mx, p.part_lse[pbase + j]);
-          ++npart;
-        }
-      }
-      // every key masked (all weights 0): keep the weights finite
-      if (Mx == -INFINITY) Mx = 0.0f;
-      const float sL = win ? exp2f(m_run - Mx) : 0.0f;
-      float den = win ? l_run * sL : 0.0f;
-      for (int j = 0; j < npart; ++j) den += exp2f(p.part_lse[pbase + j] - Mx);
-      const float inv_den = den > 0.0f ? 1.0f / den : 0.0f;
+      const float inv_l = win ? 1.0f / l_run : 0.0f;
+      const int Kf = a.routes.K;
+      const int64_t pent =
+          p.flags ? (((int64_t)(s - p.s0) * p.prows + (tok - 2 * p.pj0 * p.TT)) * p.hqn + (hq - p.hq0)) * (Kf + 1) + Kf
+                  : 0;
       T* op = reinterpret_cast<T*>(a.qo.out) +
               (a.seqs.q_start ? rglob * a.qo.o_stride_tok
                               : (int64_t)s * a.qo.o_stride_seq + (int64_t)tok * a.qo.o_stride_tok) +
               (int64_t)hq * a.qo.o_stride_head;
+      if (p.flags) op = reinterpret_cast<T*>(const_cast<uint16_t*>(p.part_o) + pent * HD);
   #pragma unroll
       for (int q4 = 0; q4 < 4; ++q4) {
         uint32_t o[32];
         tmem_ld32(tO + q4 * 32 + lane_base, o);
         tmem_ld_wait();
         if (row_ok) {
-          float acc[32];
-  #pragma unroll
-          for (int c = 0; c < 32; ++c) acc[c] = win ? __uint_as_float(o[c]) * sL : 0.0f;
-          for (int j = 0; j < npart; ++j) {
-            const float w = exp2f(p.part_lse[pbase + j] - Mx);
-            const uint4* src = reinterpret_cast<const uint4*>(p.part_o + (pbase + j) * HD + q4 * 32);
-  #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              const uint4 u = src[v];
-              const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
-  #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float2 f = unpack2(uu[e], (T*)nullptr);
-                acc[8 * v + 2 * e] = fmaf(w, f.x, acc[8 * v + 2 * e]);
-                acc[8 * v + 2 * e + 1] = fmaf(w, f.y, acc[8 * v + 2 * e + 1]);
-              }
-            }
-          }
           uint32_t pko[16];
   #pragma unroll
-          for (int c = 0; c < 32; c += 2) pko[c >> 1] = pack2(acc[c] * inv_den, acc[c + 1] * inv_den, (T*)nullptr);
+          for (int c = 0; c < 32; c += 2)
+            pko[c >> 1] = pack2(win ? __uint_as_float(o[c]) * inv_l : 0.0f,
+                                win ? __uint_as_float(o[c + 1]) * inv_l : 0.0f, (T*)nullptr);
   #pragma unroll
           for (int v = 0; v < 4; ++v)
             *reinterpret_cast<uint4*>(op + q4 * 32 + v * 8) = make_uint4(pko[4 * v], pko[4 * v + 1], pko[4 * v + 2], pko[4 * v + 3]);
           // fused output gather: the same row into every peer rank's copy of
           // the output (P2P stores over NVLink; same strides, same offset)
-          for (int pr = 0; pr < a.n_peers; ++pr) {
-            T* pop = reinterpret_cast<T*>(a.out_peers[pr]) + (op - reinterpret_cast<T*>(a.qo.out));
+          if (!p.flags) {
+            for (int pr = 0; pr < a.n_peers; ++pr) {
+              T* pop = reinterpret_cast<T*>(a.out_peers[pr]) + (op - reinterpret_cast<T*>(a.qo.out));
   #pragma unroll
-            for (int v = 0; v < 4; ++v)
-              *reinterpret_cast<uint4*>(pop + q4 * 32 + v * 8) = make_uint4(pko[4 * v], pko[4 * v + 1], pko[4 * v + 2], pko[4 * v + 3]);
+              for (int v = 0; v < 4; ++v)
+                *reinterpret_cast<uint4*>(pop + q4 * 32 + v * 8) = make_uint4(pko[4 * v], pko[4 * v + 1], pko[4 * v + 2], pko[4 * v + 3]);
+            }
           }
         }
       }
@@ -873,8 +843,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       // tile while they drain over NVLink.  The grid completes only once all
       // of its writes are performed, and the caller's completion step is
       // stream-ordered after the grid, so it sees every row in place.
-      if (row_ok && a.qo.lse) {
-        float lse = den > 0.0f ? (Mx + log2f(den)) * 0.6931471805599453f : -INFINITY;
+      if (row_ok && p.flags) {
+        const_cast<float*>(p.part_lse)[pent] = win ? m_run + log2f(l_run) : -INFINITY;
+      } else if (row_ok && a.qo.lse) {
+        const float lse = win ? (m_run + log2f(l_run)) * 0.6931471805599453f : -INFINITY;
         a.qo.lse[(a.seqs.q_start ? rglob * a.qo.lse_stride_tok
                                  : (int64_t)s * a.qo.lse_stride_seq + (int64_t)tok * a.qo.lse_stride_tok) +
                  (int64_t)hq * a.qo.lse_stride_head] = lse;
@@ -955,23 +927,17 @@ bool prefill_gathered_supported(const DashPrefillArgs& a) {
   const int G = a.qo.n_heads / a.kv.n_kv_heads;
   const int bs = a.block_size;
   return (bs == 32 || bs == 64 || bs == 128) && (G == 1 || G == 2 || G == 4) && a.routes.K > 0 &&
-         a.routes.K <= kPlanMaxK;
+         a.routes.K <= kPlanMaxSlots;
 }
 
-// Mode 0 picks the gathered routed part when a tile's rows are unlikely to
-// share blocks: the remote span averaged over a causal sequence, in blocks,
-// is well above the routed slots per row.
+// Mode 0 is tile-major: the gathered split is taken on request (mode 2).
 static bool use_gathered(const DashPrefillArgs& a) {
-  if (a.mode == 1 || !prefill_gathered_supported(a)) return false;
-  if (a.mode == 2) return true;
-  const int bs = a.block_size;
-  const double local_blocks = (double)(a.local_window + bs - 1) / bs;
-  const double remote = (double)a.seqs.max_q_len / 2.0 / bs - local_blocks;
-  return a.seqs.max_q_len >= 2048 && remote > 2.5 * a.routes.K;
+  return a.mode == 2 && prefill_gathered_supported(a);
 }
 
 // Gathered mode: chunks of sequences x tile pairs x kv heads whose partials
-// (bf16/fp16 output row + fp32 log2-sum-exp per list slot) fit the budget.
+// (bf16/fp16 output row + fp32 log2-sum-exp per list slot and one for the
+// window part) fit the budget.
 struct GatherChunks {
   int hcn, sn, npj;      // kv heads, sequences, tile pairs per chunk
   int wpt, wps;          // flag words per tile / per (sequence, block)
@@ -988,8 +954,9 @@ static GatherChunks gather_chunks(const DashPrefillArgs& a, const PrefillPlan& p
   c.flags_bytes = (size_t)nih * a.seqs.n_seq * p.nblk_cap * c.wps * 4;
   const int pairs = (p.tiles_per_seq + 1) / 2;
   const int nkv = a.kv.n_kv_heads, ns = a.seqs.n_seq;
-  // one unit = (sequence, tile pair, kv head): 256 query rows x heads
-  const size_t unit = (size_t)2 * BM * a.routes.K * kPartBytes;
+  // one unit = (sequence, tile pair, kv head): 256 query rows x heads, K
+  // routed slots + the window slot each
+  const size_t unit = (size_t)2 * BM * (a.routes.K + 1) * kPartBytes;
   const size_t budget = (size_t)(a.part_budget_mib > 0 ? a.part_budget_mib : kDefaultPartMiB) << 20;
   const size_t cap = budget / unit > 0 ? budget / unit : 1;
   auto balance = [](int total, size_t per) -> int {
@@ -1011,7 +978,7 @@ static GatherChunks gather_chunks(const DashPrefillArgs& a, const PrefillPlan& p
       c.npj = balance(pairs, cap);
     }
   }
-  const size_t entries = (size_t)c.sn * (2 * c.npj * p.TT) * (c.hcn * p.G) * a.routes.K;
+  const size_t entries = (size_t)c.sn * (2 * c.npj * p.TT) * (c.hcn * p.G) * (a.routes.K + 1);
   c.lse_bytes = entries * 4;
   c.o_bytes = entries * HD * 2;
   return c;
@@ -1068,7 +1035,7 @@ static int launch_plan(const DashPrefillArgs& a, const PrefillPlan& p, int32_t* 
   };
   if (K <= 32) return plan(plan_kernel<1, PAIR>);
   if (K <= 64) return plan(plan_kernel<2, PAIR>);
-  return plan(plan_kernel<kPlanMaxK / 32, PAIR>);
+  return plan(plan_kernel<kPlanMaxSlots / 32, PAIR>);
 }
 
 template <typename T, bool PAGED, bool PAIR>
@@ -1176,6 +1143,7 @@ int launch_prefill(const DashPrefillArgs& a, int64_t n_rows, cudaStream_t st) {
         c.prows = 2 * c.npj * p.TT;
         rc = launch_prefill_routed(a, c, rk, rv, hcn, st);
         if (!rc) rc = launch_local_any(a, c, mk, mv, pair_kernel, hcn, st);
+        if (!rc) rc = launch_prefill_merge(a, c, st);
         if (rc) return rc;
       }
     }

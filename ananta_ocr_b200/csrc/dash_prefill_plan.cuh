@@ -31,10 +31,11 @@ struct PrefillPlan {
   // 2(j+1) TT)), kv heads [hk0, hk0 + grid.y).  Union mode: everything.
   int32_t s0, sn, pj0, npj;
   int32_t hk0;
-  // gathered mode: the routed part's partials of this chunk, query heads
-  // [hq0, hq0 + hqn); entry ((((s - s0) * prows + i - 2 pj0 TT) * hqn + hq - hq0)
-  // * K + j) for token i, list slot j: the normalised output (bf16/fp16 bits,
-  // [.][128]) and its log2-sum-exp, merged in the local kernel's epilogue
+  // gathered mode: the partials of this chunk, query heads [hq0, hq0 + hqn);
+  // entry (((s - s0) * prows + i - 2 pj0 TT) * hqn + hq - hq0) * (K + 1) + j
+  // for token i: list slot j < K (the routed block's keys, no bias) or the
+  // window part (j = K); the normalised output (bf16/fp16 bits, [.][128]) and
+  // its log2-sum-exp, combined by the merge kernel
   int32_t hq0, hqn;
   int32_t prows;           // partial rows per sequence (= 2 npj TT)
   const uint16_t* part_o;
@@ -60,5 +61,11 @@ int launch_prefill_f32(const DashPrefillArgs& a, const PrefillPlan& p, cudaStrea
 // from p.hk0): K/V tensor maps with boxes of min(block_size, 64) rows.
 int launch_prefill_routed(const DashPrefillArgs& c, const PrefillPlan& p, const CUtensorMap& mk,
                           const CUtensorMap& mv, int hcn, cudaStream_t st);
+// Launches the merge of the chunk's partials into the output (and the peer
+// copies, lse).
+int launch_prefill_merge(const DashPrefillArgs& c, const PrefillPlan& p, cudaStream_t st);
+
+// Routed slots per row (K) the plan and the gathered kernels take.
+constexpr int kPlanMaxSlots = 256;
 
 }  // namespace dash

@@ -1,5 +1,5 @@
 // dash_prefill_routed.cu -- the routed part of the DASH prefill, gathered by
-// key block (sm_100a tensor cores).
+// key block (sm_100a tensor cores), and the merge of a row's partials.
 //
 // With noise-like routes, the 128 rows of a query tile route different blocks
 // and the tile-major kernel (dash_prefill.cu) multiplies every row against the
@@ -7,20 +7,31 @@
 // config 4.  Here the routed keys are taken block by block instead: one CTA
 // per (sequence, kv head, key block) gathers the query rows that routed the
 // block (the plan kernel's per-block row bitmask) into 128-slot batches (a
-// slot = a row x one query head of the kv head), so every product is useful:
-//   producer warp 5   enumerates the next batch's rows; per slot: q row
-//                     offset, the slot's list position, bias, key range
-//   slot warps 0-3    gather the slots' q rows into shared memory (cp.async,
-//                     128-byte swizzle); softmax of the slot's row (thread =
-//                     slot = TMEM lane) over the block's keys below its
-//                     window; epilogue: normalised partial output (bf16) and
-//                     its log2-sum-exp into the partial scratch
-//   MMA warp 4        S = Q K^T  (tcgen05 M=128 slots, N=block, K=128 dims)
-//                     O = P V    (M=128, N=128, K=block; P from TMEM)
-// The block's K and V (TMA) stay in shared memory for all its batches.  The
-// next batch's q rows are gathered while the current batch's PV runs.  The
-// local-window kernel (prefill_kernel, gathered mode) merges the partials of a
-// row with its window part in its epilogue.
+// slot = a row x one query head of the kv head), so every product is useful.
+// The block's K and V (TMA) stay in shared memory for all its batches.
+//
+//   enumerator (warp 5)     K/V of the block; the next batch's rows from the
+//                           bitmask into a 3-stage ring
+//   loaders (warps 6-13)    two groups, even / odd batches; thread = slot:
+//                           q row gathered into the stage (cp.async, 128-byte
+//                           swizzle), the slot's key range and partial entry
+//                           (list position of the block: one vector load of
+//                           the row's ascending list)
+//   MMA issuer (warp 4)     S = Q K^T (tcgen05 M=128, N=block, two TMEM S
+//                           buffers), O = P V (P from TMEM, two O buffers);
+//                           QK of batch n+2 is issued right after PV of n
+//   softmax (warps 0-3)     thread = slot = TMEM lane: softmax of batch n over
+//                           the block's keys below the row's window, P over S;
+//                           then the epilogue of batch n-1: normalised partial
+//                           output (bf16/fp16) and its log2-sum-exp
+// The block's bias of a row is constant over the block, so it only shifts the
+// partial's log-sum-exp: the merge adds it.
+//
+//   prefill_merge_kernel    one warp per (row, query head): the row's routed
+//                           partials and its window part (slot K, written by
+//                           the window kernel) merged with softmax weights
+//                           2^(lse_j + bias_j log2 e - max); coalesced 256-byte
+//                           partial rows; output (and peer copies) + lse
 //
 // Semantics: sparse_gather_e2e_triton.py:34-115 (keys of a routed block below
 // the query's local window, + the slot's bias), WHL attend_triton.py:88-292.
@@ -35,34 +46,37 @@ namespace {
 
 constexpr int NS = 128;                  // slots per batch
 constexpr int HD = 128;                  // head dim
-constexpr int kSlotWarps = 4;
 constexpr int kMmaWarp = 4;
-constexpr int kProdWarp = 5;
-constexpr int kThreads = 6 * 32;
-constexpr uint32_t TMEM_COLS = 256;      // S (<= 128 columns) | O (128)
+constexpr int kEnumWarp = 5;
+constexpr int kLoadWarp0 = 6;            // loader groups: warps 6-9, 10-13
+constexpr int kThreads = 14 * 32;
+constexpr uint32_t TMEM_COLS = 512;      // S0 | S1 | O0 | O1
 constexpr float LOG2E = 1.4426950408889634f;
 
-struct RMeta {
-  int64_t qoff[NS];    // element offset of the slot's q row
-  int64_t poff[NS];    // partial entry of the slot (chunk layout); -1: padding
-  float bias2[NS];     // bias * log2(e)
+struct RStage {
+  int rowtok[NS];      // token (within the sequence) of gathered row r (slots r*G+g)
+  int64_t poff[NS];    // partial entry of the slot; -1: padding
   int klo[NS];         // keys [klo, kcut) of the block count for the slot
   int kcut[NS];
-  int rowtok[NS];      // token index of each gathered row (slots row * G + g)
-  int ns;
-  int pad[3];
+  int ns;              // live slots; 0: no more batches
+  int s, b, hk;        // the batch's item: sequence, key block, kv head
+  int buf, kvpar;      // its K/V buffer and the parity of that buffer's load
+  int item;            // item ordinal within the CTA (a change marks the next item)
+  int pad;
 };
 
 template <int BS>
 struct RLayout {
-  static constexpr int OFF_Q = 0;                        // 2 halves x [128 slots][128 B]
-  static constexpr int OFF_K = 32768;                    // 2 halves x [BS keys][128 B]
-  static constexpr int OFF_V = OFF_K + BS * 256;
-  static constexpr int OFF_META = OFF_V + BS * 256;      // 2 x RMeta
-  static constexpr int OFF_BAR = OFF_META + 2 * (int)sizeof(RMeta);
-  // at most two CTAs per SM: each takes half of the SM's 512 TMEM columns
-  static constexpr int USED = OFF_BAR + 128 + 1024;
-  static constexpr int SMEM = USED > 80 * 1024 ? USED : 80 * 1024;
+  // batch stages: three, two with 128-token blocks (their K/V buffers are
+  // twice as large)
+  static constexpr int NQS = BS == 128 ? 2 : 3;
+  static constexpr int OFF_Q = 0;                           // NQS x 2 halves x [128 slots][128 B]
+  static constexpr int OFF_KV = NQS * 32768;                // 2 buffers x (K, V: 2 halves x [BS][128 B])
+  static constexpr int OFF_ST = OFF_KV + 2 * BS * 512;      // NQS x RStage
+  static constexpr int OFF_BAR = OFF_ST + NQS * (int)sizeof(RStage);
+  static constexpr int USED = OFF_BAR + 256 + 1024;
+  // one CTA per SM: it takes all 512 TMEM columns
+  static constexpr int SMEM = USED > 120 * 1024 ? USED : 120 * 1024;
 };
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
@@ -77,58 +91,48 @@ __device__ __forceinline__ void cp_async_wait_all_r() {
 template <typename T, bool PAGED, int BS>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_routed_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                          const DashPrefillArgs a, const PrefillPlan p) {
+                          const DashPrefillArgs a, const PrefillPlan p, const int hcn) {
   using L = RLayout<BS>;
+  constexpr int NQS = L::NQS;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  RMeta* meta = reinterpret_cast<RMeta*>(sm + L::OFF_META);
+  RStage* stg = reinterpret_cast<RStage*>(sm + L::OFF_ST);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
-  uint64_t* kv_full = bars + 0;
-  uint64_t* q_full = bars + 1;
-  uint64_t* s_full = bars + 2;
-  uint64_t* p_full = bars + 3;
-  uint64_t* o_full = bars + 4;
-  uint64_t* o_free = bars + 5;
-  uint64_t* meta_full = bars + 6;     // [2]
-  uint64_t* meta_empty = bars + 8;    // [2]
-  uint64_t* mma_done = bars + 10;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 11);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 12);
+  uint64_t* rows_full = bars + 0;       // [NQS] enumerator -> loaders, MMA, softmax
+  uint64_t* q_full = bars + 3;          // [NQS] loader group (4 warps) -> MMA
+  uint64_t* stage_free = bars + 6;      // [NQS] QK done (commit) + epilogue done (4 warps)
+  uint64_t* kv_ready = bars + 9;        // [2] K/V buffer loaded (and its tail zeroed)
+  uint64_t* kv_tail = bars + 11;        // [2] load of a sequence's last block (zeroed after)
+  uint64_t* kv_free = bars + 13;        // [2] every PV of the buffer's item issued + done
+  uint64_t* s_full = bars + 15;         // [2]
+  uint64_t* p_full = bars + 17;         // [2]
+  uint64_t* o_full = bars + 19;         // [2]
+  uint64_t* o_free = bars + 21;         // [2]
+  uint64_t* mma_done = bars + 23;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 24);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 25);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int sl = blockIdx.x / p.nblk_cap, b = blockIdx.x - sl * p.nblk_cap;
-  const int s = p.s0 + sl;
-  const int hk = p.hk0 + blockIdx.y;
-  const int kvl = kv_len_of(a.seqs, s);
-  if ((int64_t)b * BS >= kvl) return;
-  // query tokens of this chunk: [i_lo, i_hi), flag words [i_lo / 32, w_hi)
-  const int qlen = q_len_of(a.seqs, s);
-  const int i_lo = 2 * p.pj0 * p.TT;
-  const int i_hi = min(qlen, 2 * (p.pj0 + p.npj) * p.TT);
-  if (i_lo >= i_hi) return;
-  const int w_lo = i_lo >> 5, w_hi = (i_hi + 31) >> 5;
+  const int n_items = p.sn * p.nblk_cap * hcn;
   const int G = p.G, H = a.qo.n_heads, K = a.routes.K;
   const int nih = a.routes.n_index_heads > 0 ? a.routes.n_index_heads : 1;
-  const int ih = (hk * G) / (H / nih);
-  const uint32_t* fl = p.flags + (((int64_t)ih * a.seqs.n_seq + s) * p.nblk_cap + b) * p.wps;
-  // no row routed this block: nothing to do (uniform exit before any setup)
-  {
-    uint32_t any = 0u;
-    for (int w = w_lo + tid; w < w_hi; w += kThreads) any |= fl[w];
-    if (!__syncthreads_or(any != 0u)) return;
-  }
+  const int i_lo = 2 * p.pj0 * p.TT;       // a multiple of 64
   DeviceError* derr = a.device_error;
   if (tid == 0) {
-    mbar_init(kv_full, 1);
-    mbar_init(q_full, kSlotWarps);
-    mbar_init(s_full, 1);
-    mbar_init(p_full, kSlotWarps);
-    mbar_init(o_full, 1);
-    mbar_init(o_free, kSlotWarps);
-    mbar_init(meta_full + 0, 1);
-    mbar_init(meta_full + 1, 1);
-    mbar_init(meta_empty + 0, kSlotWarps);
-    mbar_init(meta_empty + 1, kSlotWarps);
+    for (int k = 0; k < NQS; ++k) {
+      mbar_init(rows_full + k, 1);
+      mbar_init(q_full + k, 4);
+      mbar_init(stage_free + k, 1 + 4);
+    }
+    for (int k = 0; k < 2; ++k) {
+      mbar_init(kv_ready + k, 1);
+      mbar_init(kv_tail + k, 1);
+      mbar_init(kv_free + k, 1);
+      mbar_init(s_full + k, 1);
+      mbar_init(p_full + k, 4);
+      mbar_init(o_full + k, 1);
+      mbar_init(o_free + k, 4);
+    }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     mbar_init_fence();
@@ -138,136 +142,178 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const uint32_t tS = tmem, tO = tmem + 128;
+  // TMEM columns: S buffer k at k*BS, O buffer k at 2*BS + k*128
+  auto tS_of = [&](int k) -> uint32_t { return tmem + (uint32_t)(k * BS); };
+  auto tO_of = [&](int k) -> uint32_t { return tmem + (uint32_t)(2 * BS + k * 128); };
+  auto sK_of = [&](int buf) -> uint8_t* { return sm + L::OFF_KV + buf * (BS * 512); };
+  auto sV_of = [&](int buf) -> uint8_t* { return sm + L::OFF_KV + buf * (BS * 512) + BS * 256; };
+  auto kv_head_of = [&](int hk) -> int { return (hk * G) / (H / nih); };
 
-  if (warp == kProdWarp) {
-    // ================= producer: K/V of the block, then slot batches =================
-    bool kv_issued = false;
+  if (warp == kEnumWarp) {
+    // ===== enumerator: items (sequence, key block, kv head) round robin over the
+    // grid; per item its K/V into a buffer, then its rows in batches =====
     if (lane == 0) {
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
-      constexpr int R = BS < 64 ? BS : 64;            // rows per TMA box
-      int c1 = b * BS, c3 = s;
-      bool ok = true;
-      if (PAGED) {
-        const int64_t page = a.kv.block_table[(int64_t)s * a.kv.bt_stride + b];
-        if (page < 0 || page >= a.kv.num_pages) {
-          record_error(derr, DASH_DEV_BAD_PAGE, 90, page);
-          ok = false;
-        }
-        c1 = 0;
-        c3 = (int)page;
-      }
-      if (ok) {
-        mbar_arrive_expect_tx(kv_full, 2 * BS * 256);
-#pragma unroll
-        for (int dh = 0; dh < 2; ++dh)
-#pragma unroll
-          for (int r0 = 0; r0 < BS; r0 += R) {
-            tma_load_4d(sm + L::OFF_K + dh * BS * 128 + r0 * 128, &tmK, kv_full, dh * 64, c1 + r0, hk, c3);
-            tma_load_4d(sm + L::OFF_V + dh * BS * 128 + r0 * 128, &tmV, kv_full, dh * 64, c1 + r0, hk, c3);
-          }
-        kv_issued = true;
-      } else {
-        mbar_arrive(kv_full);
-      }
     }
-    const int pos0 = pos0_of(a.seqs, s);
-    const int64_t rb = row_base(a.seqs, s);
     const int cap = NS / G;
-    // i_lo is a multiple of 64 and flag bits past qlen are zero, so whole
-    // words in [w_lo, w_hi) hold exactly this chunk's tokens
-    int next_row = i_lo;
-    for (int n = 0;; ++n) {
-      const int buf = n & 1;
-      RMeta& M = meta[buf];
-      if (n >= 2 && !mbar_wait_warp(meta_empty + buf, ((n >> 1) - 1) & 1, abort_flag, derr, 91)) break;
-      // rows of this batch: 32 bitmask words per step, one per lane
-      int cnt = 0;
-      while (cnt < cap && next_row < i_hi) {
-        const int w = (next_row >> 5) + lane;
-        uint32_t m = 0u;
-        if (w < w_hi) {
-          m = fl[w];
-          if (lane == 0) m &= 0xffffffffu << (next_row & 31);
-        }
-        const int c = __popc(m);
-        int incl = c;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-          const int o = __shfl_up_sync(0xffffffffu, incl, off);
-          if (lane >= off) incl += o;
-        }
-        const int excl = incl - c;
-        const int tot = __shfl_sync(0xffffffffu, incl, 31);
-        const int room = cap - cnt;
-        const int take = max(0, min(c, room - excl));
-        uint32_t mm = m;
-        for (int k = 0; k < take; ++k) {
-          const int bit = __ffs(mm) - 1;
-          mm &= mm - 1u;
-          M.rowtok[cnt + excl + k] = w * 32 + bit;
-        }
-        if (tot <= room) {
-          cnt += tot;
-          next_row = ((next_row >> 5) + 32) * 32;
-        } else {
-          // the lane holding the boundary: its first untaken row resumes the next batch
-          const bool bnd = excl <= room && excl + c > room;
-          const int src = __ffs(__ballot_sync(0xffffffffu, bnd)) - 1;
-          const int resume = w * 32 + (__ffs(mm) - 1);
-          next_row = __shfl_sync(0xffffffffu, resume, src);
-          cnt = cap;
-        }
+    int n = 0;                               // batches published
+    int uses[2] = {0, 0}, tail_uses[2] = {0, 0};
+    uint64_t* last_bar[2] = {nullptr, nullptr};
+    uint32_t last_par[2] = {0u, 0u};
+    int item_no = 0;
+    bool alive = true;
+    for (int it = blockIdx.x; alive && it < n_items; it += gridDim.x) {
+      const int hk = p.hk0 + it % hcn;
+      const int r = it / hcn;
+      const int b = r % p.nblk_cap, sl = r / p.nblk_cap;
+      const int s = p.s0 + sl;
+      const int kvl = kv_len_of(a.seqs, s);
+      if ((int64_t)b * BS >= kvl) continue;
+      const int i_hi = min(q_len_of(a.seqs, s), 2 * (p.pj0 + p.npj) * p.TT);
+      if (i_lo >= i_hi) continue;
+      const int w_hi = (i_hi + 31) >> 5;
+      const uint32_t* fl =
+          p.flags + (((int64_t)kv_head_of(hk) * a.seqs.n_seq + s) * p.nblk_cap + b) * p.wps;
+      // flag words of the chunk in windows of 32 (one per lane), the next
+      // window prefetched; flag bits past qlen are zero
+      int wb = i_lo >> 5;
+      uint32_t mc = wb + lane < w_hi ? fl[wb + lane] : 0u;
+      uint32_t mn = wb + 32 + lane < w_hi ? fl[wb + 32 + lane] : 0u;
+      while (!__any_sync(0xffffffffu, mc != 0u) && wb + 32 < w_hi) {
+        wb += 32;
+        mc = mn;
+        mn = wb + 32 + lane < w_hi ? fl[wb + 32 + lane] : 0u;
       }
-      __syncwarp();
-      const int ns = cnt * G;
-#pragma unroll 1
-      for (int q = 0; q < NS / 32; ++q) {
-        const int n2 = lane + 32 * q;
-        const bool live = n2 < ns;
-        const int i = live ? M.rowtok[n2 / G] : 0;
-        const int hq = hk * G + (n2 % G);
-        const int64_t rg = rb + i;
-        int kcut = 0, klo = 0, j = 0;
-        float bias2 = 0.0f;
-        int64_t qoff = 0, poff = -1;
-        if (live) {
-          const int lstart = pos0 + i - a.local_window + 1;
-          kcut = min(min(lstart, kvl) - b * BS, BS);
-          const int seg = a.seg_start ? a.seg_start[rg] : 0;
-          klo = max(seg - b * BS, 0);
-          // list position of the block: the row's list ascends with a -1 tail
-          const int32_t* cl = p.cidx + ((int64_t)ih * p.n_rows + rg) * K;
-          for (int j0 = 0; j0 < K; j0 += 16) {
-            int v[16];
-#pragma unroll
-            for (int u = 0; u < 16; ++u) v[u] = j0 + u < K ? cl[j0 + u] : -1;
-#pragma unroll
-            for (int u = 0; u < 16; ++u) j += (v[u] >= 0 && v[u] < b) ? 1 : 0;
+      if (!__any_sync(0xffffffffu, mc != 0u)) continue;      // no row routed the block
+      const int buf = item_no & 1;
+      // the buffer's previous item: every PV issued and complete
+      if (uses[buf] >= 1 && !mbar_wait_warp(kv_free + buf, (uint32_t)(uses[buf] - 1) & 1u, abort_flag, derr, 90)) {
+        alive = false;
+        break;
+      }
+      const bool tail = (int64_t)(b + 1) * BS > kvl;
+      uint64_t* lbar = tail ? kv_tail + buf : kv_ready + buf;
+      if (lane == 0) {
+        constexpr int R = BS < 64 ? BS : 64;          // rows per TMA box
+        int c1 = b * BS, c3 = s;
+        bool ok = true;
+        if (PAGED) {
+          const int64_t page = a.kv.block_table[(int64_t)s * a.kv.bt_stride + b];
+          if (page < 0 || page >= a.kv.num_pages) {
+            record_error(derr, DASH_DEV_BAD_PAGE, 91, page);
+            ok = false;
           }
-          if (a.routes.bias) bias2 = p.cbias[((int64_t)ih * p.n_rows + rg) * K + j] * LOG2E;
-          qoff = (a.seqs.q_start ? rg * a.qo.q_stride_tok
-                                 : (int64_t)s * a.qo.q_stride_seq + (int64_t)i * a.qo.q_stride_tok) +
-                 (int64_t)hq * a.qo.q_stride_head;
-          poff = ((((int64_t)sl * p.prows + (i - i_lo)) * p.hqn + (hq - p.hq0)) * K) + j;
+          c1 = 0;
+          c3 = (int)page;
         }
-        M.qoff[n2] = qoff;
-        M.poff[n2] = poff;
-        M.bias2[n2] = bias2;
-        M.klo[n2] = klo;
-        M.kcut[n2] = kcut;
+        if (ok) {
+          mbar_arrive_expect_tx(lbar, 2 * BS * 256);
+#pragma unroll
+          for (int dh = 0; dh < 2; ++dh)
+#pragma unroll
+            for (int r0 = 0; r0 < BS; r0 += R) {
+              tma_load_4d(sK_of(buf) + dh * BS * 128 + r0 * 128, &tmK, lbar, dh * 64, c1 + r0, hk, c3);
+              tma_load_4d(sV_of(buf) + dh * BS * 128 + r0 * 128, &tmV, lbar, dh * 64, c1 + r0, hk, c3);
+            }
+        } else {
+          mbar_arrive(lbar);
+        }
       }
-      if (lane == 0) M.ns = ns;
+      const int kvpar = uses[buf] & 1;
+      last_bar[buf] = lbar;
+      last_par[buf] = (uint32_t)(tail ? tail_uses[buf] : uses[buf]) & 1u;
+      ++uses[buf];
+      if (tail) {
+        // V rows past the end of the sequence are zeroed before any PV reads
+        // them (P is 0 there, never times garbage)
+        if (!mbar_wait_warp(kv_tail + buf, (uint32_t)tail_uses[buf] & 1u, abort_flag, derr, 92)) {
+          alive = false;
+          break;
+        }
+        ++tail_uses[buf];
+        const int r0 = kvl - b * BS;
+        uint8_t* dV = sV_of(buf);
+        for (int e = lane; e < (BS - r0) * 16; e += 32) {
+          const int row = r0 + e / 16, ch = e % 16;
+          *reinterpret_cast<uint4*>(dV + (ch >> 3) * (BS * 128) + row * 128 + ((ch & 7) << 4)) = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(kv_ready + buf);
+      }
+      // the item's batches
+      while (alive) {
+        const int st = n % NQS;
+        RStage& S = stg[st];
+        // (a stage reserved for a batch that turns out empty is reused by the
+        // next one: the completed wait passes again)
+        if (n >= NQS && !mbar_wait_warp(stage_free + st, (uint32_t)((n / NQS) - 1) & 1u, abort_flag, derr, 93)) {
+          alive = false;
+          break;
+        }
+        int cnt = 0;
+        bool exhausted = false;
+        while (cnt < cap) {
+          if (!__any_sync(0xffffffffu, mc != 0u)) {
+            if (wb + 32 >= w_hi) { exhausted = true; break; }
+            wb += 32;
+            mc = mn;
+            mn = wb + 32 + lane < w_hi ? fl[wb + 32 + lane] : 0u;
+            continue;
+          }
+          const int c = __popc(mc);
+          int incl = c;
+#pragma unroll
+          for (int off = 1; off < 32; off <<= 1) {
+            const int o = __shfl_up_sync(0xffffffffu, incl, off);
+            if (lane >= off) incl += o;
+          }
+          const int excl = incl - c;
+          const int tot = __shfl_sync(0xffffffffu, incl, 31);
+          const int room = cap - cnt;
+          const int take = max(0, min(c, room - excl));
+          for (int k = 0; k < take; ++k) {
+            const int bit = __ffs(mc) - 1;
+            mc &= mc - 1u;
+            S.rowtok[cnt + excl + k] = (wb + lane) * 32 + bit;
+          }
+          cnt += min(tot, room);
+        }
+        if (cnt > 0) {
+          if (lane == 0) {
+            S.ns = cnt * G;
+            S.s = s;
+            S.b = b;
+            S.hk = hk;
+            S.buf = buf;
+            S.kvpar = kvpar;
+            S.item = item_no;
+          }
+          __threadfence_block();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(rows_full + st);
+          ++n;
+        }
+        if (exhausted) break;
+      }
+      ++item_no;
+    }
+    // two empty batches end both loader groups, the MMA warp and the softmax
+    for (int z = 0; z < 2 && alive; ++z, ++n) {
+      const int st = n % NQS;
+      if (n >= NQS && !mbar_wait_warp(stage_free + st, (uint32_t)((n / NQS) - 1) & 1u, abort_flag, derr, 94)) break;
+      if (lane == 0) stg[st].ns = 0;
       __threadfence_block();
       __syncwarp();
-      if (lane == 0) mbar_arrive(meta_full + buf);
-      if (ns == 0) break;
+      if (lane == 0) mbar_arrive(rows_full + st);
     }
     // never leave the CTA with bulk copies in flight
-    if (kv_issued) {
-      volatile int no_abort = 0;
-      mbar_wait(kv_full, 0, &no_abort, nullptr, 92);
+    for (int k = 0; k < 2; ++k) {
+      if (last_bar[k] != nullptr) {
+        volatile int no_abort = 0;
+        mbar_wait(last_bar[k], last_par[k], &no_abort, nullptr, 95);
+      }
     }
   } else if (warp == kMmaWarp) {
     // ============================ MMA issuer ============================
@@ -275,86 +321,191 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t fmt = DType<T>::fmt;
       constexpr uint32_t idesc_qk = make_idesc(fmt, 0, 0, NS, BS);
       constexpr uint32_t idesc_pv = make_idesc(fmt, 0, 1, NS, HD);
-      const uint32_t sQ = smem_u32(sm + L::OFF_Q), sK = smem_u32(sm + L::OFF_K), sV = smem_u32(sm + L::OFF_V);
-      bool alive = mbar_wait(kv_full, 0, abort_flag, derr, 93);
-      for (int n = 0; alive; ++n) {
-        if (!mbar_wait(q_full, n & 1, abort_flag, derr, 94)) break;
+      bool alive = true;
+      int nq = 0;               // QKs issued (batches 0 .. nq-1 exist)
+      bool more = true;
+      // QK(n) into S buffer n % 2.  That buffer held P(n-2), read by PV(n-2):
+      // this thread issued PV(n-2) before, and its tcgen05.mma ops execute in
+      // issue order; softmax finished with S(n-2) before PV(n-2) was issued.
+      auto try_qk = [&]() {
+        if (!more) return;
+        const int n = nq, st = n % NQS;
+        const uint32_t par = (uint32_t)(n / NQS) & 1u;
+        if (!mbar_wait(rows_full + st, par, abort_flag, derr, 96)) { more = false; alive = false; return; }
+        const RStage& S = stg[st];
+        if (S.ns == 0) { more = false; return; }
+        if (!mbar_wait(q_full + st, par, abort_flag, derr, 97) ||
+            !mbar_wait(kv_ready + S.buf, (uint32_t)S.kvpar, abort_flag, derr, 98)) {
+          more = false;
+          alive = false;
+          return;
+        }
         tc_fence_after();
-        if (meta[n & 1].ns == 0) break;
-        // S(n) overwrites P(n-1), read by PV(n-1): this thread issued that PV
-        // first, and its tcgen05.mma ops execute in issue order
+        const uint32_t sQ = smem_u32(sm + L::OFF_Q + st * 32768);
+        const uint32_t sK = smem_u32(sK_of(S.buf));
+        const uint32_t tS = tS_of(n & 1);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint64_t ad = sw128_desc(sQ + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = sw128_desc(sK + (kk >> 2) * (BS * 128) + (kk & 3) * 32, 16, 1024);
           umma_ss(tS, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
         }
-        umma_commit(s_full);
-        if (!mbar_wait(p_full, n & 1, abort_flag, derr, 95)) break;
-        if (n >= 1 && !mbar_wait(o_free, (n - 1) & 1, abort_flag, derr, 96)) break;
+        umma_commit(s_full + (n & 1));
+        umma_commit(stage_free + st);           // the q rows of the stage are read
+        ++nq;
+      };
+      try_qk();
+      try_qk();
+      for (int n = 0; n < nq && alive; ++n) {
+        if (!mbar_wait(p_full + (n & 1), (uint32_t)(n >> 1) & 1u, abort_flag, derr, 99)) break;
+        if (n >= 2 && !mbar_wait(o_free + (n & 1), (uint32_t)((n - 2) >> 1) & 1u, abort_flag, derr, 100)) break;
         tc_fence_after();
+        const RStage& S = stg[n % NQS];
+        const int buf = S.buf;
+        const uint32_t sV = smem_u32(sV_of(buf));
+        const uint32_t tS = tS_of(n & 1), tO = tO_of(n & 1);
 #pragma unroll
         for (int kk = 0; kk < BS / 16; ++kk) {
           const uint64_t bd = sw128_desc(sV + kk * 2048, BS * 128, 1024);
           umma_ts(tO, tS + kk * 8, bd, idesc_pv, kk > 0 ? 1u : 0u);
         }
-        umma_commit(o_full);
+        umma_commit(o_full + (n & 1));
+        // the last PV of an item frees its K/V buffer for the item after next
+        // (batch n+1 is known: its QK was issued before this PV)
+        if (n + 1 < nq && stg[(n + 1) % NQS].item != S.item) umma_commit(kv_free + buf);
+        try_qk();
       }
       // every MMA completes before TMEM is released
       umma_commit(mma_done);
       volatile int no_abort = 0;
-      mbar_wait(mma_done, 0, &no_abort, nullptr, 97);
+      mbar_wait(mma_done, 0, &no_abort, nullptr, 101);
     }
     __syncwarp();
-  } else {
-    // ============ slot warps: gather, softmax, epilogue (thread = slot) ============
-    const int n_slot = tid;                        // 0..127, TMEM lane
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    const float sl2 = a.scale * LOG2E;
+  } else if (warp >= kLoadWarp0) {
+    // ============ loaders: q rows and slot data of every other batch ============
+    const int grp = (warp - kLoadWarp0) >> 2;
+    const int n2 = tid - (kLoadWarp0 + 4 * grp) * 32;        // slot 0..127
     const T* qbase = reinterpret_cast<const T*>(a.qo.q);
-    uint8_t* sQ = sm + L::OFF_Q;
-    auto gather = [&](const RMeta& M, int ns) {
-      const bool live = n_slot < ns;
-      const uint4* src = reinterpret_cast<const uint4*>(qbase + (live ? M.qoff[n_slot] : 0));
+    const bool vec = (K & 3) == 0;
+    for (int n = grp;; n += 2) {
+      const int st = n % NQS;
+      if (!mbar_wait_warp(rows_full + st, (uint32_t)(n / NQS) & 1u, abort_flag, derr, 102)) break;
+      RStage& S = stg[st];
+      const int ns = S.ns;
+      if (ns == 0) break;
+      const int s = S.s, b = S.b, hk = S.hk;
+      const bool live = n2 < ns;
+      const int i = live ? S.rowtok[n2 / G] : i_lo;
+      const int hq = hk * G + (n2 % G);
+      const int64_t rg = row_base(a.seqs, s) + i;
+      // q row -> stage (swizzled K-major); padding slots are zero
+      {
+        const int64_t qoff = (a.seqs.q_start ? rg * a.qo.q_stride_tok
+                                             : (int64_t)s * a.qo.q_stride_seq + (int64_t)i * a.qo.q_stride_tok) +
+                             (int64_t)hq * a.qo.q_stride_head;
+        const uint4* src = reinterpret_cast<const uint4*>(qbase + qoff);
+        uint8_t* sQ = sm + L::OFF_Q + st * 32768;
 #pragma unroll
-      for (int cc = 0; cc < 16; ++cc) {
-        const int region = cc >> 3, c8 = cc & 7;
-        uint8_t* dst = sQ + region * 16384 + n_slot * 128 + ((c8 ^ (n_slot & 7)) << 4);
-        if (live) cp_async16(dst, src + cc);
-        else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+        for (int cc = 0; cc < 16; ++cc) {
+          uint8_t* dst = sQ + (cc >> 3) * 16384 + n2 * 128 + (((cc & 7) ^ (n2 & 7)) << 4);
+          if (live) cp_async16(dst, src + cc);
+          else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+        }
       }
+      // key range and partial entry (list position of the block: the row's
+      // canonical list ascends with a -1 tail)
+      int64_t poff = -1;
+      int klo = 0, kcut = 0;
+      if (live) {
+        const int kvl = kv_len_of(a.seqs, s);
+        const int lstart = pos0_of(a.seqs, s) + i - a.local_window + 1;
+        kcut = min(min(lstart, kvl) - b * BS, BS);
+        const int seg = a.seg_start ? a.seg_start[rg] : 0;
+        klo = max(seg - b * BS, 0);
+        const int32_t* cl = p.cidx + ((int64_t)kv_head_of(hk) * p.n_rows + rg) * K;
+        int j = 0;
+        if (vec) {
+          for (int j0 = 0; j0 < K; j0 += 16) {
+            int4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              v[u] = j0 + 4 * u < K ? reinterpret_cast<const int4*>(cl + j0)[u] : make_int4(-1, -1, -1, -1);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              j += (v[u].x >= 0 && v[u].x < b) + (v[u].y >= 0 && v[u].y < b) + (v[u].z >= 0 && v[u].z < b) +
+                   (v[u].w >= 0 && v[u].w < b);
+          }
+        } else {
+          for (int j0 = 0; j0 < K; j0 += 16) {
+            int v[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) v[u] = j0 + u < K ? cl[j0 + u] : -1;
+#pragma unroll
+            for (int u = 0; u < 16; ++u) j += (v[u] >= 0 && v[u] < b) ? 1 : 0;
+          }
+        }
+        const int sl = s - p.s0;
+        poff = (((int64_t)sl * p.prows + (i - i_lo)) * p.hqn + (hq - p.hq0)) * (K + 1) + j;
+      }
+      S.poff[n2] = poff;
+      S.klo[n2] = klo;
+      S.kcut[n2] = kcut;
       cp_async_wait_all_r();
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(q_full);
-    };
-    bool alive = mbar_wait_warp(kv_full, 0, abort_flag, derr, 100);
-    // zero V rows past the end of the sequence (P is 0 there, never times garbage)
-    if (alive && (b + 1) * BS > kvl) {
-      const int r0 = kvl - b * BS;
-      uint8_t* dV = sm + L::OFF_V;
-      for (int e = n_slot; e < (BS - r0) * 16; e += NS) {
-        const int row = r0 + e / 16, ch = e % 16;
-        *reinterpret_cast<uint4*>(dV + (ch >> 3) * (BS * 128) + row * 128 + ((ch & 7) << 4)) = make_uint4(0, 0, 0, 0);
-      }
-      fence_proxy_async_smem();
+      if (lane == 0) mbar_arrive(q_full + st);
     }
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    int ns_cur = 0;
-    if (alive) {
-      alive = mbar_wait_warp(meta_full + 0, 0, abort_flag, derr, 101);
-      if (alive) {
-        ns_cur = meta[0].ns;
-        gather(meta[0], ns_cur);
-      }
-    }
-    for (int n = 0; alive && ns_cur > 0; ++n) {
-      const RMeta& M = meta[n & 1];
-      const int klo = M.klo[n_slot], kcut = M.kcut[n_slot];
-      const float bias2 = M.bias2[n_slot];
-      // ---- softmax of slot n_slot over the block's keys ----
-      if (!mbar_wait_warp(s_full, n & 1, abort_flag, derr, 102)) { alive = false; break; }
+  } else {
+    // ======== softmax of batch n, then the epilogue of batch n-1 (thread = slot) ========
+    const int n2 = tid;                             // 0..127, TMEM lane
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const float sl2 = a.scale * LOG2E;
+    bool alive = true;
+    // the batch whose epilogue is pending: its partial entry, max and sum
+    int64_t prev_poff = -1;
+    float prev_m = 0.0f, prev_l = 0.0f;
+    auto epilogue = [&](int m) -> bool {
+      if (!mbar_wait_warp(o_full + (m & 1), (uint32_t)(m >> 1) & 1u, abort_flag, derr, 103)) return false;
       tc_fence_after();
+      const uint32_t tO = tO_of(m & 1);
+      const float inv_l = prev_l > 0.0f ? 1.0f / prev_l : 0.0f;
+#pragma unroll 1
+      for (int q4 = 0; q4 < 4; ++q4) {
+        float o[32];
+        tmem_ld32f(tO + q4 * 32 + lane_base, o);
+        tmem_ld_wait();
+        if (prev_poff >= 0) {
+          uint32_t pko[16];
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) pko[c >> 1] = pack2(o[c] * inv_l, o[c + 1] * inv_l, (T*)nullptr);
+          uint4* dst = reinterpret_cast<uint4*>(const_cast<uint16_t*>(p.part_o) + prev_poff * HD + q4 * 32);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pko[4 * v], pko[4 * v + 1], pko[4 * v + 2], pko[4 * v + 3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(o_free + (m & 1));
+      if (prev_poff >= 0)
+        const_cast<float*>(p.part_lse)[prev_poff] = prev_l > 0.0f ? prev_m + log2f(prev_l) : -INFINITY;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(stage_free + (m % NQS));
+      return true;
+    };
+    int n = 0;
+    for (; alive; ++n) {
+      const int st = n % NQS;
+      const uint32_t par = (uint32_t)(n / NQS) & 1u;
+      if (!mbar_wait_warp(rows_full + st, par, abort_flag, derr, 104)) { alive = false; break; }
+      if (stg[st].ns == 0) break;
+      // the loaders' slot data of this stage (complete once q_full is)
+      if (!mbar_wait_warp(q_full + st, par, abort_flag, derr, 105)) { alive = false; break; }
+      const RStage& S = stg[st];
+      const int klo = S.klo[n2], kcut = S.kcut[n2];
+      const int64_t poff = S.poff[n2];
+      if (!mbar_wait_warp(s_full + (n & 1), (uint32_t)(n >> 1) & 1u, abort_flag, derr, 106)) { alive = false; break; }
+      tc_fence_after();
+      const uint32_t tS = tS_of(n & 1);
       // pass 1: the row max over the kept keys; pass 2: P (packed) over the
       // S columns already read (64 S columns per 32-column store)
       float mrow = -INFINITY, lrow = 0.0f;
@@ -365,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_wait();
 #pragma unroll
         for (int c = 0; c < 32; ++c)
-          if (c0 + c >= klo && c0 + c < kcut) mrow = fmaxf(mrow, fmaf(x[c], sl2, bias2));
+          if (c0 + c >= klo && c0 + c < kcut) mrow = fmaxf(mrow, x[c] * sl2);
       }
       const float mref = mrow == -INFINITY ? 0.0f : mrow;
 #pragma unroll 1
@@ -381,8 +532,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
               const int c = c0 + 2 * e;
-              const float p0 = (c >= klo && c < kcut) ? fast_exp2(fmaf(x[2 * e], sl2, bias2) - mref) : 0.0f;
-              const float p1 = (c + 1 >= klo && c + 1 < kcut) ? fast_exp2(fmaf(x[2 * e + 1], sl2, bias2) - mref) : 0.0f;
+              const float p0 = (c >= klo && c < kcut) ? fast_exp2(fmaf(x[2 * e], sl2, -mref)) : 0.0f;
+              const float p1 = (c + 1 >= klo && c + 1 < kcut) ? fast_exp2(fmaf(x[2 * e + 1], sl2, -mref)) : 0.0f;
               lrow += p0 + p1;
               pk[h * 16 + e] = pack2(p0, p1, (T*)nullptr);
             }
@@ -394,42 +545,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_st32(tS + sc * 32 + lane_base, pk);
       }
       tmem_st_wait();
-      mrow = mref;
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-      // ---- the next batch's q rows, gathered while PV(n) runs ----
-      int ns_next = 0;
-      if (!mbar_wait_warp(meta_full + ((n + 1) & 1), ((n + 1) >> 1) & 1, abort_flag, derr, 103)) { alive = false; break; }
-      ns_next = meta[(n + 1) & 1].ns;
-      gather(meta[(n + 1) & 1], ns_next);
-      // ---- epilogue: normalised partial output and its log2-sum-exp ----
-      if (!mbar_wait_warp(o_full, n & 1, abort_flag, derr, 104)) { alive = false; break; }
-      tc_fence_after();
-      const int64_t poff = M.poff[n_slot];
-      const float inv_l = lrow > 0.0f ? 1.0f / lrow : 0.0f;
-#pragma unroll 1
-      for (int q4 = 0; q4 < 4; ++q4) {
-        float o[32];
-        tmem_ld32f(tO + q4 * 32 + lane_base, o);
-        tmem_ld_wait();
-        if (poff >= 0) {
-          uint32_t pko[16];
-#pragma unroll
-          for (int c = 0; c < 32; c += 2) pko[c >> 1] = pack2(o[c] * inv_l, o[c + 1] * inv_l, (T*)nullptr);
-          uint4* dst = reinterpret_cast<uint4*>(const_cast<uint16_t*>(p.part_o) + poff * HD + q4 * 32);
-#pragma unroll
-          for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pko[4 * v], pko[4 * v + 1], pko[4 * v + 2], pko[4 * v + 3]);
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(o_free);
-      if (poff >= 0) const_cast<float*>(p.part_lse)[poff] = lrow > 0.0f ? mrow + log2f(lrow) : -INFINITY;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(meta_empty + (n & 1));
-      ns_cur = ns_next;
+      if (lane == 0) mbar_arrive(p_full + (n & 1));
+      // ---- epilogue of the previous batch while PV(n) runs ----
+      if (n >= 1 && !epilogue(n - 1)) { alive = false; break; }
+      prev_poff = poff;
+      prev_m = mref;
+      prev_l = lrow;
     }
+    if (alive && n >= 1) epilogue(n - 1);
   }
   tc_fence_before();
   __syncthreads();
@@ -438,8 +563,129 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// prefill_merge_kernel: one warp per (row, query head) of the chunk.  Slots:
+// the row's routed partials j < npart (its canonical list ascends with a -1
+// tail) and the window part at slot K.  Lane l owns dims [4l, 4l+4).
+// ---------------------------------------------------------------------------
+constexpr int kMergeWarps = 8;
+
+template <typename T>
+__global__ void __launch_bounds__(kMergeWarps * 32)
+    prefill_merge_kernel(const DashPrefillArgs a, const PrefillPlan p) {
+  __shared__ float s_w[kMergeWarps][kPlanMaxSlots + 1];
+  const int wl = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t wid = (int64_t)blockIdx.x * kMergeWarps + wl;
+  const int64_t per_seq = (int64_t)p.prows * p.hqn;
+  if (wid >= (int64_t)p.sn * per_seq) return;
+  const int sl = (int)(wid / per_seq);
+  const int64_t rem = wid - sl * per_seq;
+  const int il = (int)(rem / p.hqn), hl = (int)(rem - (int64_t)il * p.hqn);
+  const int s = p.s0 + sl;
+  const int i = 2 * p.pj0 * p.TT + il;
+  if (i >= q_len_of(a.seqs, s)) return;
+  const int hq = p.hq0 + hl;
+  const int64_t rg = row_base(a.seqs, s) + i;
+  const int H = a.qo.n_heads, K = a.routes.K;
+  const int nih = a.routes.n_index_heads > 0 ? a.routes.n_index_heads : 1;
+  const int ih = hq / (H / nih);
+  const int32_t* cl = p.cidx + ((int64_t)ih * p.n_rows + rg) * K;
+  const float* cb = p.cbias + ((int64_t)ih * p.n_rows + rg) * K;
+  const int64_t pbase = (((int64_t)sl * p.prows + il) * p.hqn + hl) * (K + 1);
+  const bool has_bias = a.routes.bias != nullptr;
+  // log2-domain weights of the slots: routed partial + its bias, window
+  float lv[(kPlanMaxSlots + 1 + 31) / 32];
+  int npart = 0;
+  float mx = -INFINITY;
+#pragma unroll
+  for (int u = 0; u < (kPlanMaxSlots + 1 + 31) / 32; ++u) {
+    const int j = lane + 32 * u;
+    float v = -INFINITY;
+    if (j < K) {
+      if (cl[j] >= 0) {
+        v = p.part_lse[pbase + j];
+        if (has_bias) v += cb[j] * LOG2E;
+        ++npart;
+      }
+    } else if (j == K) {
+      v = p.part_lse[pbase + K];
+    }
+    lv[u] = v;
+    mx = fmaxf(mx, v);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    npart += __shfl_xor_sync(0xffffffffu, npart, o);
+  }
+  // every key masked (all weights 0): keep the weights finite
+  if (mx == -INFINITY) mx = 0.0f;
+  float den = 0.0f;
+#pragma unroll
+  for (int u = 0; u < (kPlanMaxSlots + 1 + 31) / 32; ++u) {
+    const int j = lane + 32 * u;
+    if (j <= K) {
+      const float w = exp2f(lv[u] - mx);
+      s_w[wl][j] = w;
+      den += w;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+  __syncwarp();
+  // weighted sum over t = 0..npart (t < npart: routed slot t; t = npart: the
+  // window slot K), eight 256-byte partial rows in flight per step
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  const uint2* po = reinterpret_cast<const uint2*>(p.part_o);
+  for (int t0 = 0; t0 <= npart; t0 += 8) {
+    uint2 v[8];
+    float w[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int t = t0 + u;
+      const int j = t < npart ? t : K;
+      const bool ok = t <= npart;
+      w[u] = ok ? s_w[wl][j] : 0.0f;
+      v[u] = ok ? po[(pbase + j) * (HD / 4) + lane] : make_uint2(0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const float2 f0 = unpack2(v[u].x, (T*)nullptr), f1 = unpack2(v[u].y, (T*)nullptr);
+      acc[0] = fmaf(w[u], f0.x, acc[0]);
+      acc[1] = fmaf(w[u], f0.y, acc[1]);
+      acc[2] = fmaf(w[u], f1.x, acc[2]);
+      acc[3] = fmaf(w[u], f1.y, acc[3]);
+    }
+  }
+  const float inv = den > 0.0f ? 1.0f / den : 0.0f;
+  const uint2 ov = make_uint2(pack2(acc[0] * inv, acc[1] * inv, (T*)nullptr),
+                              pack2(acc[2] * inv, acc[3] * inv, (T*)nullptr));
+  const int64_t ooff = (a.seqs.q_start ? rg * a.qo.o_stride_tok
+                                       : (int64_t)s * a.qo.o_stride_seq + (int64_t)i * a.qo.o_stride_tok) +
+                       (int64_t)hq * a.qo.o_stride_head;
+  T* op = reinterpret_cast<T*>(a.qo.out) + ooff;
+  reinterpret_cast<uint2*>(op)[lane] = ov;
+  // fused output gather: the same row into every peer rank's copy of the
+  // output (posted P2P stores over NVLink; same strides, same offset)
+  for (int pr = 0; pr < a.n_peers; ++pr)
+    reinterpret_cast<uint2*>(reinterpret_cast<T*>(a.out_peers[pr]) + ooff)[lane] = ov;
+  if (lane == 0 && a.qo.lse) {
+    const float lse = den > 0.0f ? (mx + log2f(den)) * 0.6931471805599453f : -INFINITY;
+    a.qo.lse[(a.seqs.q_start ? rg * a.qo.lse_stride_tok
+                             : (int64_t)s * a.qo.lse_stride_seq + (int64_t)i * a.qo.lse_stride_tok) +
+             (int64_t)hq * a.qo.lse_stride_head] = lse;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
+static int sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
 template <typename T, bool PAGED, int BS>
 static int launch_routed_typed(const DashPrefillArgs& c, const PrefillPlan& p, const CUtensorMap& mk,
                                const CUtensorMap& mv, int hcn, cudaStream_t st) {
@@ -448,8 +694,10 @@ static int launch_routed_typed(const DashPrefillArgs& c, const PrefillPlan& p, c
   static_assert(smem <= 232448, "shared memory budget");
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return set_error(DASH_ERR_CUDA, "cudaFuncSetAttribute(prefill_routed_kernel) failed");
-  dim3 grid((unsigned)(p.sn * p.nblk_cap), (unsigned)hcn);
-  kern<<<grid, kThreads, smem, st>>>(mk, mv, c, p);
+  // persistent: one CTA per SM walks the (sequence, block, kv head) items
+  const int64_t items = (int64_t)p.sn * p.nblk_cap * hcn;
+  const unsigned grid = (unsigned)(items < sm_count() ? items : sm_count());
+  kern<<<grid, kThreads, smem, st>>>(mk, mv, c, p, hcn);
   count_launch();
   return check_launch("prefill_routed_kernel");
 }
@@ -473,6 +721,15 @@ int launch_prefill_routed(const DashPrefillArgs& c, const PrefillPlan& p, const 
       return set_error(DASH_ERR_UNSUPPORTED, "routed kernel: block_size %d", c.block_size);
   }
 #undef DASH_ROUTED
+}
+
+int launch_prefill_merge(const DashPrefillArgs& c, const PrefillPlan& p, cudaStream_t st) {
+  const int64_t warps = (int64_t)p.sn * p.prows * p.hqn;
+  const unsigned grid = (unsigned)((warps + kMergeWarps - 1) / kMergeWarps);
+  if (c.kv.dtype == DASH_DTYPE_BF16) prefill_merge_kernel<__nv_bfloat16><<<grid, kMergeWarps * 32, 0, st>>>(c, p);
+  else prefill_merge_kernel<__half><<<grid, kMergeWarps * 32, 0, st>>>(c, p);
+  count_launch();
+  return check_launch("prefill_merge_kernel");
 }
 
 }  // namespace dash

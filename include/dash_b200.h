@@ -472,9 +472,8 @@ typedef struct {
   int32_t local_window;
   /* 0: automatic; 1: tile-major (each 128-row tile walks the union of its
    * rows' blocks); 2: routed part gathered by key block (block sizes 32, 64,
-   * 128; 1, 2 or 4 query heads per kv head), merged into the window part.
-   * Automatic picks 2 when routes are sparse against the remote span
-   * (max_q_len / 2 / block_size - local blocks > 2.5 K, max_q_len >= 2048). */
+   * 128; 1, 2 or 4 query heads per kv head), merged with the window part.
+   * Automatic is tile-major. */
   int32_t mode;
   void* workspace;
   size_t workspace_bytes;

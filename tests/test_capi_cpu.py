@@ -69,6 +69,35 @@ def _prefill_args(head_dim=128, block_size=64, heads=10, kv_heads=10, K=4):
     return a
 
 
+def test_prefill_mode_checks_and_workspace():
+    """Mode 2 (routed part gathered by key block) is refused outside its
+    shapes; its workspace adds the per-block row flags and a partial scratch
+    that the budget bounds (one chunk's partials)."""
+    a = _prefill_args(heads=8, kv_heads=1)
+    a.mode = 2
+    assert _call_status("dash_prefill_attn", a) == L.DASH_ERR_UNSUPPORTED   # 8 heads per kv head
+    a = _prefill_args(block_size=192)
+    a.mode = 2
+    assert _call_status("dash_prefill_attn", a) == L.DASH_ERR_UNSUPPORTED
+    a = _prefill_args()
+    a.mode = 3
+    assert _call_status("dash_prefill_attn", a) == L.DASH_ERR_INVALID
+    lib = L.load()
+
+    def size(mode, budget=0, T=9248, K=16):
+        a = _prefill_args(K=K)
+        a.seqs.n_seq, a.seqs.q_len_fixed, a.seqs.kv_len_fixed, a.seqs.max_q_len = 4, T, T, T
+        a.mode, a.part_budget_mib = mode, budget
+        return lib.dash_prefill_workspace_size(C.byref(a))
+
+    union, full = size(1), size(2)
+    # every (row, head, slot) partial: 128 bf16 + one fp32
+    assert full - union >= 4 * 9248 * 10 * 16 * 260
+    assert size(0) == union                     # automatic: tile-major
+    small = size(2, budget=8)
+    assert union < small <= union + 8 * 2**20 + 4 * 145 * 292 * 4 + 3 * 256
+
+
 def test_prefill_rejects_unsupported_shapes():
     assert _call_status("dash_prefill_attn", _prefill_args(head_dim=64)) == L.DASH_ERR_UNSUPPORTED
     assert "head_dim" in L.last_error()
