@@ -240,7 +240,7 @@ EXPORTS = [
     "dash_block_any", "dash_page_blocks", "dash_index_proj", "dash_rope_kv_write",
     "dash_attn_bwd", "dash_attn_bwd_flag_words", "dash_entmax15_fwd", "dash_entmax15_bwd",
     "dash_serving_plan", "dash_peer_export", "dash_peer_import", "dash_peer_close",
-    "dash_page_coords", "dash_cos_sin_2d",
+    "dash_page_coords", "dash_cos_sin_2d", "dash_route_refresh",
 ]
 
 
@@ -287,6 +287,8 @@ def load(path: str = LIB_PATH):
         f = getattr(L, name)
         f.argtypes = args
         f.restype = C.c_int
+    L.dash_route_refresh.argtypes = [C.POINTER(DashRouteArgs), C.POINTER(DashKbarArgs), _p]
+    L.dash_route_refresh.restype = C.c_int
     L.dash_prefill_workspace_size.argtypes = [C.POINTER(DashPrefillArgs)]
     L.dash_prefill_workspace_size.restype = C.c_size_t
     L.dash_decode_workspace_size.argtypes = [C.POINTER(DashDecodeArgs)]

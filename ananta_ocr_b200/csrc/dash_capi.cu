@@ -149,7 +149,7 @@ int dash_abi_sizes(int64_t* out, int n) {
   return 24;
 }
 
-int dash_kbar_pool(const DashKbarArgs* a, dash_stream_t stream) {
+static int validate_kbar(const DashKbarArgs* a) {
   if (!a) return set_error(DASH_ERR_INVALID, "null args");
   if (!a->keys || !a->kbar) return set_error(DASH_ERR_INVALID, "null keys/kbar");
   if (a->dtype != DASH_DTYPE_F32 && a->dtype != DASH_DTYPE_BF16)
@@ -159,10 +159,15 @@ int dash_kbar_pool(const DashKbarArgs* a, dash_stream_t stream) {
     return set_error(DASH_ERR_UNSUPPORTED, "block_size %d not in (0, 256]", a->block_size);
   if (a->pages && !a->ntok) return set_error(DASH_ERR_INVALID, "paged plan needs ntok");
   if (!a->pages && (a->n_seq < 0 || a->seq_len < 0)) return set_error(DASH_ERR_INVALID, "bad n_seq/seq_len");
-  return launch_kbar(*a, (cudaStream_t)stream);
+  return DASH_OK;
 }
 
-int dash_route(const DashRouteArgs* a, dash_stream_t stream) {
+int dash_kbar_pool(const DashKbarArgs* a, dash_stream_t stream) {
+  const int rc = validate_kbar(a);
+  return rc != DASH_OK ? rc : launch_kbar(*a, (cudaStream_t)stream);
+}
+
+static int validate_route(const DashRouteArgs* a) {
   if (!a) return set_error(DASH_ERR_INVALID, "null args");
   int rc = check_seqs(a->seqs);
   if (rc) return rc;
@@ -188,7 +193,24 @@ int dash_route(const DashRouteArgs* a, dash_stream_t stream) {
       return set_error(DASH_ERR_INVALID, "page_seq_rows %lld < width %d", (long long)a->page_seq_rows,
                        a->width);
   }
-  return launch_route(*a, seq_rows(a->seqs), (cudaStream_t)stream);
+  return DASH_OK;
+}
+
+int dash_route(const DashRouteArgs* a, dash_stream_t stream) {
+  const int rc = validate_route(a);
+  return rc != DASH_OK ? rc : launch_route(*a, seq_rows(a->seqs), (cudaStream_t)stream);
+}
+
+int dash_route_refresh(const DashRouteArgs* a, const DashKbarArgs* refresh, dash_stream_t stream) {
+  int rc = validate_route(a);
+  if (rc != DASH_OK) return rc;
+  if (!refresh) return launch_route(*a, seq_rows(a->seqs), (cudaStream_t)stream);
+  rc = validate_kbar(refresh);
+  if (rc != DASH_OK) return rc;
+  if (!refresh->pages) return set_error(DASH_ERR_INVALID, "the folded refresh takes a paged plan");
+  if (refresh->kbar != a->kbar && a->kbar)
+    return set_error(DASH_ERR_INVALID, "the refresh must write the k-bar rows the routing reads");
+  return launch_route_refresh(*a, seq_rows(a->seqs), *refresh, (cudaStream_t)stream);
 }
 
 int dash_block_max(const DashBlockMaxArgs* a, dash_stream_t stream) {

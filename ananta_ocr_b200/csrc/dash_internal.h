@@ -13,6 +13,8 @@ void count_launch();
 
 int launch_kbar(const DashKbarArgs& a, cudaStream_t st);
 int launch_route(const DashRouteArgs& a, int64_t n_rows, cudaStream_t st);
+// the routing with a paged k-bar refresh folded into the decode launch where it can be
+int launch_route_refresh(const DashRouteArgs& a, int64_t n_rows, const DashKbarArgs& ka, cudaStream_t st);
 int launch_block_max(const DashBlockMaxArgs& a, cudaStream_t st);
 int launch_decode(const DashDecodeArgs& a, int64_t n_rows, int splits, cudaStream_t st);
 int launch_prefill(const DashPrefillArgs& a, int64_t n_rows, cudaStream_t st);

@@ -8,6 +8,7 @@
 // order as oracle/dash_oracle.c, so k-bar, block scores and the selected block
 // lists are bitwise equal to the CPU oracle.
 #include <cooperative_groups.h>
+#include <type_traits>
 #include "dash_common.cuh"
 #include "dash_internal.h"
 
@@ -25,9 +26,11 @@ constexpr float kEntmaxNeg = -1.0e4f;
 // operands are fetched ahead of the fixed-order FMA chains); VEC stages the
 // keys with 16-byte loads.  The arithmetic order is the same in every form.
 // ---------------------------------------------------------------------------
+// One k-bar row: the first n tokens at element offset `base` of a.keys ->
+// a.kbar row out_row.  All 128 threads of the CTA take part (barriers).
 template <typename KT, int DC, bool VEC>
-__global__ void __launch_bounds__(128) kbar_pool_kernel(DashKbarArgs a) {
-  extern __shared__ float sm[];
+__device__ __forceinline__ void kbar_pool_body(const DashKbarArgs& a, float* sm, int n, int64_t base,
+                                               int64_t out_row) {
   const int d = DC > 0 ? DC : a.d;
   const int ld = d + 1;                       // padded row, conflict-free column reads
   float* sk = sm;                             // [bs][d+1]
@@ -35,23 +38,6 @@ __global__ void __launch_bounds__(128) kbar_pool_kernel(DashKbarArgs a) {
   float* se = shc + d;                        // [bs]
   float* sred = se + a.block_size;            // [4]
   const KT* keys = reinterpret_cast<const KT*>(a.keys);
-
-  int n;
-  int64_t base, out_row;
-  if (a.pages == nullptr) {
-    int b = blockIdx.x, s = blockIdx.y;
-    n = a.seq_len - b * a.block_size;
-    if (n > a.block_size) n = a.block_size;
-    base = (int64_t)s * a.seq_stride + (int64_t)b * a.block_size * a.tok_stride;
-    out_row = (int64_t)s * a.kbar_seq_rows + b;
-  } else {
-    int i = blockIdx.x;
-    n = a.ntok[i];
-    if (n <= 0) return;                        // not a page slot (route_triton.py:69-72)
-    if (n > a.block_size) n = a.block_size;
-    base = a.pages[i] * a.page_stride;
-    out_row = a.pages[i];
-  }
   if constexpr (VEC) {
     // 16-byte vectors of W elements; every load of a thread is issued before
     // its first shared-memory store
@@ -109,6 +95,40 @@ __global__ void __launch_bounds__(128) kbar_pool_kernel(DashKbarArgs a) {
     if (!(acc == acc) || isinf(acc)) acc = 0.0f;
     a.kbar[out_row * a.kbar_row_stride + c] = acc;
   }
+}
+
+// Shared memory of kbar_pool_body, in floats.
+__host__ __device__ inline size_t kbar_pool_smem_floats(int block_size, int d) {
+  return (size_t)block_size * (d + 1) + d + block_size + 4;
+}
+
+// Plan entry i of a paged pool: false when it is not a page slot (ntok <= 0,
+// route_triton.py:69-72).
+__device__ __forceinline__ bool kbar_paged_entry(const DashKbarArgs& a, int i, int& n, int64_t& base,
+                                                 int64_t& out_row) {
+  n = a.ntok[i];
+  if (n <= 0) return false;
+  if (n > a.block_size) n = a.block_size;
+  base = a.pages[i] * a.page_stride;
+  out_row = a.pages[i];
+  return true;
+}
+
+template <typename KT, int DC, bool VEC>
+__global__ void __launch_bounds__(128) kbar_pool_kernel(const __grid_constant__ DashKbarArgs a) {
+  extern __shared__ float sm[];
+  int n;
+  int64_t base, out_row;
+  if (a.pages == nullptr) {
+    int b = blockIdx.x, s = blockIdx.y;
+    n = a.seq_len - b * a.block_size;
+    if (n > a.block_size) n = a.block_size;
+    base = (int64_t)s * a.seq_stride + (int64_t)b * a.block_size * a.tok_stride;
+    out_row = (int64_t)s * a.kbar_seq_rows + b;
+  } else if (!kbar_paged_entry(a, blockIdx.x, n, base, out_row)) {
+    return;
+  }
+  kbar_pool_body<KT, DC, VEC>(a, sm, n, base, out_row);
 }
 
 // ---------------------------------------------------------------------------
@@ -267,6 +287,137 @@ __device__ __forceinline__ bool page_block_holds(const DashRouteArgs& a, int qp,
   return page_desc_holds(a.page_lo, a.page_hi, a.page_bits, a.page_bits_words, i, qp);
 }
 
+// Second half of a row's selection, by one warp: the M top-M items are in
+// slots (mid_ = block id, mx = x) in ascending id order; ranks by (x desc, id
+// asc), the sort-based entmax threshold, the log prior of the first K ranks,
+// bias and the ascending pack.  scand holds the row's candidate bits.
+template <int PER>
+__device__ __forceinline__ void select_tail(const DashRouteArgs& a, const uint32_t* scand, const int* mid_,
+                                            float* mx, int* mval, int M, int64_t r, int lane) {
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  auto is_cand = [&](int b) -> bool { return (scand[b >> 5] >> (b & 31)) & 1u; };
+  // ---- rank of slot t = lane + 32u by (x desc, id asc); PER >= ceil(M / 32) ----
+  const int nper = (M + 31) >> 5;
+  float xt[PER];
+  int rk[PER];
+#pragma unroll
+  for (int u = 0; u < PER; ++u) {
+    const int t = lane + 32 * u;
+    xt[u] = (u < nper && t < M) ? mx[t] : -INFINITY;
+    rk[u] = 0;
+  }
+#pragma unroll 8
+  for (int v = 0; v < M; ++v) {
+    const float xv = mx[v];
+#pragma unroll
+    for (int u = 0; u < PER; ++u)
+      if (u < nper) rk[u] += (xv > xt[u] || (xv == xt[u] && v < lane + 32 * u)) ? 1 : 0;
+  }
+  float xmax = -INFINITY;
+#pragma unroll
+  for (int u = 0; u < PER; ++u) xmax = fmaxf(xmax, xt[u]);
+  for (int o = 16; o > 0; o >>= 1) xmax = fmaxf(xmax, __shfl_xor_sync(0xffffffffu, xmax, o));
+  int Kc = min(a.K, M);
+  if (Kc < 1) Kc = 1;
+  bool valid[PER];
+  __syncwarp();  // every lane has read mx by slot
+#pragma unroll
+  for (int u = 0; u < PER; ++u) {
+    const int t = lane + 32 * u;
+    valid[u] = false;
+    if (u < nper && t < M) {
+      valid[u] = rk[u] < Kc && is_cand(mid_[t]);
+      mx[rk[u]] = __fdiv_rn(__fsub_rn(xt[u], xmax), 2.0f);   // z by rank
+      mval[rk[u]] = valid[u] ? 1 : 0;
+    }
+  }
+  __syncwarp();
+
+  // ---- tau_k for rank k = lane + 32u; support; tau ----
+  float cs = 0.0f, cs2 = 0.0f;
+  float tau_r[PER];
+  int support = 0;
+#pragma unroll
+  for (int u = 0; u < PER; ++u) {
+    tau_r[u] = 0.0f;
+    if (u < nper) {
+      const int k = lane + 32 * u;
+      // add z_j for j = previous k + 1 .. k in ascending order (u = 0: 0 .. k)
+      const int jstart = u == 0 ? 32 - min(M, 32) : 0;
+#pragma unroll 8
+      for (int jj = jstart; jj < 32; ++jj) {
+        const int j = k - 31 + jj;
+        const float zj = mx[max(j, 0)];
+        if (j >= 0) {
+          cs = __fadd_rn(cs, zj);
+          cs2 = __fadd_rn(cs2, __fmul_rn(zj, zj));
+        }
+      }
+      bool in_support = false;
+      if (k < M) {
+        const float rho = (float)(k + 1);
+        const float mean = __fdiv_rn(cs, rho);
+        const float mean_sq = __fdiv_rn(cs2, rho);
+        const float ss = __fmul_rn(rho, __fsub_rn(mean_sq, __fmul_rn(mean, mean)));
+        const float delta = __fdiv_rn(__fsub_rn(1.0f, ss), rho);
+        const float tau = __fsub_rn(mean, __fsqrt_rn(delta > 0.0f ? delta : 0.0f));
+        tau_r[u] = tau;
+        in_support = tau <= mx[k];
+      }
+      support += __popc(__ballot_sync(0xffffffffu, in_support));
+    }
+  }
+  if (support < 1) support = 1;
+  float tsel = 0.0f;
+#pragma unroll
+  for (int u = 0; u < PER; ++u)
+    if (u == ((support - 1) >> 5)) tsel = tau_r[u];
+  const float tau = __shfl_sync(0xffffffffu, tsel, (support - 1) & 31);
+
+  // ---- log prior of the first Kc ranks; mean over the valid ones ----
+  __syncwarp();  // every lane has read z by rank
+  for (int k = lane; k < Kc; k += 32) {
+    float t = __fsub_rn(mx[k], tau);
+    t = t > 0.0f ? t : 0.0f;
+    const float p = __fmul_rn(t, t);
+    mx[k] = logf(p > a.prior_floor ? p : a.prior_floor);
+  }
+  __syncwarp();
+  float lsum = 0.0f;
+  int cnt = 0;
+#pragma unroll 8
+  for (int k = 0; k < Kc; ++k)
+    if (mval[k]) {
+      lsum = __fadd_rn(lsum, mx[k]);
+      ++cnt;
+    }
+  const float mu = __fdiv_rn(lsum, (float)(cnt > 0 ? cnt : 1));
+
+  // ---- ascending pack (slots ascend by id) ----
+  int32_t* oi = a.out_idx + r * a.out_stride;
+  float* ob = a.out_bias + r * a.out_stride;
+  int npos = 0;
+#pragma unroll
+  for (int u = 0; u < PER; ++u) {
+    if (u < nper) {
+      const uint32_t vb = __ballot_sync(0xffffffffu, valid[u]);
+      if (valid[u]) {
+        const int p = npos + __popc(vb & lt_mask);
+        if (p < a.out_width) {
+          oi[p] = mid_[lane + 32 * u];
+          ob[p] = __fmul_rn(__fsub_rn(mx[rk[u]], mu), a.inv_sigma);
+        }
+      }
+      npos += __popc(vb);
+    }
+  }
+  for (int j = npos + lane; j < a.out_width; j += 32) {
+    oi[j] = -1;
+    ob[j] = 0.0f;
+  }
+  if (a.out_count && lane == 0) a.out_count[r] = min(npos, a.out_width);
+}
+
 template <int KW, int PER>
 __device__ __noinline__ void select_row(const DashRouteArgs& a, float* sx, uint32_t* scand,
                                         int* mid_, float* mx, int* mval, int64_t r, int s,
@@ -414,126 +565,7 @@ __device__ __noinline__ void select_row(const DashRouteArgs& a, float* sx, uint3
   __syncwarp();
   M = n_items;  // == M
 
-  // ---- rank of slot t = lane + 32u by (x desc, id asc); PER >= ceil(M / 32) ----
-  const int nper = (M + 31) >> 5;
-  float xt[PER];
-  int rk[PER];
-#pragma unroll
-  for (int u = 0; u < PER; ++u) {
-    const int t = lane + 32 * u;
-    xt[u] = (u < nper && t < M) ? mx[t] : -INFINITY;
-    rk[u] = 0;
-  }
-#pragma unroll 8
-  for (int v = 0; v < M; ++v) {
-    const float xv = mx[v];
-#pragma unroll
-    for (int u = 0; u < PER; ++u)
-      if (u < nper) rk[u] += (xv > xt[u] || (xv == xt[u] && v < lane + 32 * u)) ? 1 : 0;
-  }
-  float xmax = -INFINITY;
-#pragma unroll
-  for (int u = 0; u < PER; ++u) xmax = fmaxf(xmax, xt[u]);
-  for (int o = 16; o > 0; o >>= 1) xmax = fmaxf(xmax, __shfl_xor_sync(0xffffffffu, xmax, o));
-  int Kc = min(a.K, M);
-  if (Kc < 1) Kc = 1;
-  bool valid[PER];
-  __syncwarp();  // every lane has read mx by slot
-#pragma unroll
-  for (int u = 0; u < PER; ++u) {
-    const int t = lane + 32 * u;
-    valid[u] = false;
-    if (u < nper && t < M) {
-      valid[u] = rk[u] < Kc && is_cand(mid_[t]);
-      mx[rk[u]] = __fdiv_rn(__fsub_rn(xt[u], xmax), 2.0f);   // z by rank
-      mval[rk[u]] = valid[u] ? 1 : 0;
-    }
-  }
-  __syncwarp();
-
-  // ---- tau_k for rank k = lane + 32u; support; tau ----
-  float cs = 0.0f, cs2 = 0.0f;
-  float tau_r[PER];
-  int support = 0;
-#pragma unroll
-  for (int u = 0; u < PER; ++u) {
-    tau_r[u] = 0.0f;
-    if (u < nper) {
-      const int k = lane + 32 * u;
-      // add z_j for j = previous k + 1 .. k in ascending order (u = 0: 0 .. k)
-      const int jstart = u == 0 ? 32 - min(M, 32) : 0;
-#pragma unroll 8
-      for (int jj = jstart; jj < 32; ++jj) {
-        const int j = k - 31 + jj;
-        const float zj = mx[max(j, 0)];
-        if (j >= 0) {
-          cs = __fadd_rn(cs, zj);
-          cs2 = __fadd_rn(cs2, __fmul_rn(zj, zj));
-        }
-      }
-      bool in_support = false;
-      if (k < M) {
-        const float rho = (float)(k + 1);
-        const float mean = __fdiv_rn(cs, rho);
-        const float mean_sq = __fdiv_rn(cs2, rho);
-        const float ss = __fmul_rn(rho, __fsub_rn(mean_sq, __fmul_rn(mean, mean)));
-        const float delta = __fdiv_rn(__fsub_rn(1.0f, ss), rho);
-        const float tau = __fsub_rn(mean, __fsqrt_rn(delta > 0.0f ? delta : 0.0f));
-        tau_r[u] = tau;
-        in_support = tau <= mx[k];
-      }
-      support += __popc(__ballot_sync(0xffffffffu, in_support));
-    }
-  }
-  if (support < 1) support = 1;
-  float tsel = 0.0f;
-#pragma unroll
-  for (int u = 0; u < PER; ++u)
-    if (u == ((support - 1) >> 5)) tsel = tau_r[u];
-  const float tau = __shfl_sync(0xffffffffu, tsel, (support - 1) & 31);
-
-  // ---- log prior of the first Kc ranks; mean over the valid ones ----
-  __syncwarp();  // every lane has read z by rank
-  for (int k = lane; k < Kc; k += 32) {
-    float t = __fsub_rn(mx[k], tau);
-    t = t > 0.0f ? t : 0.0f;
-    const float p = __fmul_rn(t, t);
-    mx[k] = logf(p > a.prior_floor ? p : a.prior_floor);
-  }
-  __syncwarp();
-  float lsum = 0.0f;
-  int cnt = 0;
-#pragma unroll 8
-  for (int k = 0; k < Kc; ++k)
-    if (mval[k]) {
-      lsum = __fadd_rn(lsum, mx[k]);
-      ++cnt;
-    }
-  const float mu = __fdiv_rn(lsum, (float)(cnt > 0 ? cnt : 1));
-
-  // ---- ascending pack (slots ascend by id) ----
-  int32_t* oi = a.out_idx + r * a.out_stride;
-  float* ob = a.out_bias + r * a.out_stride;
-  int npos = 0;
-#pragma unroll
-  for (int u = 0; u < PER; ++u) {
-    if (u < nper) {
-      const uint32_t vb = __ballot_sync(0xffffffffu, valid[u]);
-      if (valid[u]) {
-        const int p = npos + __popc(vb & lt_mask);
-        if (p < a.out_width) {
-          oi[p] = mid_[lane + 32 * u];
-          ob[p] = __fmul_rn(__fsub_rn(mx[rk[u]], mu), a.inv_sigma);
-        }
-      }
-      npos += __popc(vb);
-    }
-  }
-  for (int j = npos + lane; j < a.out_width; j += 32) {
-    oi[j] = -1;
-    ob[j] = 0.0f;
-  }
-  if (a.out_count && lane == 0) a.out_count[r] = min(npos, a.out_width);
+  select_tail<PER>(a, scand, mid_, mx, mval, M, r, lane);
 }
 
 template <int KW>
@@ -576,7 +608,7 @@ __host__ __device__ inline size_t route_tile_smem_floats(int W) {
          8 * ((size_t)Wp / 32 + 3 * kMaxM) + 8 * kPcCache;
 }
 
-__global__ void __launch_bounds__(256) route_tile_kernel(DashRouteArgs a, int tiles_per_seq) {
+__global__ void __launch_bounds__(256) route_tile_kernel(const __grid_constant__ DashRouteArgs a, int tiles_per_seq) {
   extern __shared__ float smt[];
   const int W = a.width, Wp = (W + 31) & ~31;
   float* qs = smt;                                  // [32][kLd]
@@ -674,7 +706,7 @@ __global__ void __launch_bounds__(256) route_tile_kernel(DashRouteArgs a, int ti
 // row, all its threads score the row's blocks, warp 0 selects (few rows,
 // e.g. decode).
 template <bool CTA_ROW>
-__global__ void __launch_bounds__(kRouteWarps * 32) route_rows_kernel(DashRouteArgs a,
+__global__ void __launch_bounds__(kRouteWarps * 32) route_rows_kernel(const __grid_constant__ DashRouteArgs a,
                                                                      int64_t n_rows) {
   extern __shared__ float smr[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -723,49 +755,200 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_rows_kernel(DashRouteA
 // Few rows (decode): a cluster of kClusterCtas CTAs per row.  CTA c scores a
 // contiguous slice of the row's blocks, one thread per block (its k-bar row is
 // loaded whole, then the same sequential FMA chain as score_blocks, so scores
-// are bitwise those of the other kernels); CTA 0 gathers the slices through
-// distributed shared memory and selects.  Every CTA reaches both cluster
-// barriers (no early exit).
+// are bitwise those of the other kernels).  After a cluster barrier CTA 0
+// pulls the row's W scores out of the slices (distributed shared memory)
+// straight into registers, EPT consecutive blocks per thread, and selects
+// with all its threads (select_head_cta); warp 0 finishes (select_tail).
+// The other CTAs are free after the barrier: with RK > 0 they refresh the
+// k-bar rows of a paged plan meanwhile (the tail refresh of a decode step,
+// folded into the routing launch).  A second, split barrier keeps every slice
+// alive until CTA 0 has read it.  Rows wider than 128 * kClusterEpt blocks
+// select with the one-warp select_row.
 // ---------------------------------------------------------------------------
 constexpr int kClusterCtas = 8;
+constexpr int kClusterEpt = 8;        // CTA-wide selection up to 1024 blocks
 
 __host__ __device__ inline int cluster_slice(int W) { return (W + kClusterCtas - 1) / kClusterCtas; }
-__host__ __device__ inline size_t route_cluster_smem_floats(int W) {
+// Shared memory, floats: q [128] | this CTA's slice | CTA 0's selection
+// scratch, or a helper CTA's k-bar refresh scratch (the larger of the two).
+__host__ __device__ inline size_t route_cluster_smem_floats(int W, size_t refresh_floats) {
   const int Wp = (W + 31) & ~31;
   const int per = (cluster_slice(W) + 31) & ~31;
-  return (size_t)128 + per + Wp + Wp / 32 + 3 * kMaxM;
+  const size_t sel = (size_t)Wp + Wp / 32 + 3 * kMaxM + 256 + 16;
+  return (size_t)128 + per + (sel > refresh_floats ? sel : refresh_floats);
 }
 
-__global__ void __launch_bounds__(128) route_cluster_kernel(DashRouteArgs a) {
-  extern __shared__ __align__(16) float smc[];
-  cg::cluster_group cl = cg::this_cluster();
-  const int rank = (int)cl.block_rank();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int W = a.width;
-  const int Wp = (W + 31) & ~31;
-  const int per = cluster_slice(W);
-  float* sq = smc;                                   // [128] router query
-  float* ssc = sq + 128;                             // [per] this CTA's slice of scores
-  float* sx = ssc + ((per + 31) & ~31);              // CTA 0: the row's W scores
-  uint32_t* scand = reinterpret_cast<uint32_t*>(sx + Wp);
-  int* mid_ = reinterpret_cast<int*>(scand + Wp / 32);
-  float* mx = reinterpret_cast<float*>(mid_ + kMaxM);
-  int* mval = reinterpret_cast<int*>(mx + kMaxM);
+// Blocks per thread of the CTA-wide selection: a power of two (a thread's
+// candidate bits then lie in one 32-bit word), 0 when W is too wide.
+__host__ __device__ inline int cluster_ept(int W) {
+  const int need = (W + 127) / 128;
+  return need <= 1 ? 1 : need <= 2 ? 2 : need <= 4 ? 4 : need <= kClusterEpt ? 8 : 0;
+}
 
-  const int64_t r = (int64_t)(blockIdx.x / kClusterCtas);
-  int s, i;
-  row_to_seq(a.seqs, r, s, i);
-  const int64_t pos = seq_pos(a.seqs, s, i);
-  const int kvl = seq_kv_len(a.seqs, s);
-  const int64_t qblk = pos >= 0 ? pos / a.block_size : -1;
-  sq[threadIdx.x] = a.idx_q[r * a.q_row_stride + threadIdx.x];
+// CTA-wide first half of a row's selection (all 128 threads; the row's scores
+// sc[e] of blocks b = EPT * tid + e, W <= 128 * EPT): candidates with the
+// per-row fallback, x = z * scale, the exact M-th largest order key by an
+// 8-bit radix over a shared histogram (stopping once a digit's keys are all
+// taken), then the top-M by (x desc, id asc) gathered into slots in ascending
+// id order through one packed (in, tie) prefix scan.  It takes the same set as
+// select_row's warp form: keys above the threshold, and ties at it from the
+// lowest id up.  Returns M.
+template <int EPT>
+__device__ int select_head_cta(const DashRouteArgs& a, const float (&sc)[EPT], int W, int64_t r, int s,
+                               uint32_t* scand, int* mid_, float* mx, uint32_t* hist, uint32_t* sred) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int b0 = tid * EPT;
+  const int Wp = (W + 31) & ~31;
+  // ---- candidates (with the per-row fallback to every remote block) ----
+  const uint8_t* cm = nullptr;
+  if (a.cand && !a.page_q) cm = a.cand + (a.cand_per_seq ? (int64_t)s : r) * a.cand_row_stride;
+  const int qp = a.page_q ? a.page_q[r] : -1;
+  uint32_t rem_bits = 0u, cand_bits = 0u;
+#pragma unroll
+  for (int e = 0; e < EPT; ++e) {
+    const int b = b0 + e;
+    const bool remote = b < W && sc[e] > kScoreNeg * 0.5f;
+    bool c = remote;
+    if (remote) {
+      if (a.page_q) c = page_block_holds(a, qp, s, b);
+      else if (cm) c = cm[b] != 0;
+    }
+    rem_bits |= (remote ? 1u : 0u) << e;
+    cand_bits |= (c ? 1u : 0u) << e;
+  }
+  for (int w = tid; w < Wp / 32; w += blockDim.x) scand[w] = 0u;
+  if (__syncthreads_or(cand_bits != 0u) == 0) cand_bits = rem_bits;
+  if (cand_bits) atomicOr(scand + (b0 >> 5), cand_bits << (b0 & 31));
+
+  // ---- x and order keys ----
+  float x[EPT];
+  uint32_t key[EPT];
+#pragma unroll
+  for (int e = 0; e < EPT; ++e) {
+    float v = ((cand_bits >> e) & 1u) ? __fmul_rn(sc[e], a.idx_scale) : kEntmaxNeg;
+    if (!(v == v) || isinf(v)) v = kEntmaxNeg;
+    x[e] = v;
+    key[e] = order_key(v);
+  }
+  int M = a.topm > 0 ? min(a.topm, W) : W;
+  if (M < 1) M = 1;
+  const bool all = M >= W;
+
+  // ---- threshold T: keys > T are in, keys == T are ties ----
+  uint32_t T = 0u;
+  if (!all) {
+    uint32_t prefix = 0u;
+    int need = M;                       // keys still to take among those matching prefix
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int j = tid; j < 256; j += blockDim.x) hist[j] = 0u;
+      __syncthreads();
+      const uint32_t hmask = shift == 24 ? 0u : (0xffffffffu << (shift + 8));
+#pragma unroll
+      for (int e = 0; e < EPT; ++e)
+        if (b0 + e < W && (key[e] & hmask) == prefix) atomicAdd(hist + ((key[e] >> shift) & 255u), 1u);
+      __syncthreads();
+      if (warp == 0) {
+        // lane l holds digits 8l .. 8l+7; suf = keys with digit >= 8l
+        uint32_t h[8], tot = 0u;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          h[k] = hist[lane * 8 + k];
+          tot += h[k];
+        }
+        uint32_t suf = tot;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t v = __shfl_down_sync(0xffffffffu, suf, o);
+          if (lane + o < 32) suf += v;
+        }
+        const uint32_t above = suf - tot;          // keys with digit >= 8(l+1)
+        // exactly one lane has above < need <= suf (suf of lane 0 = all >= need)
+        if (above < (uint32_t)need && (uint32_t)need <= suf) {
+          uint32_t acc = above, hsel = 0u;
+          int dsel = lane * 8;
+#pragma unroll
+          for (int k = 7; k >= 0; --k) {
+            if (hsel == 0u && acc + h[k] >= (uint32_t)need) {
+              dsel = lane * 8 + k;
+              hsel = h[k];
+            } else if (hsel == 0u) {
+              acc += h[k];
+            }
+          }
+          const uint32_t left = (uint32_t)need - acc;   // 1 .. hsel
+          sred[0] = prefix | ((uint32_t)dsel << shift);
+          sred[1] = left;
+          sred[2] = hsel == left ? 1u : 0u;             // every key of the digit is in
+        }
+      }
+      __syncthreads();
+      prefix = sred[0];
+      need = (int)sred[1];
+      if (sred[2]) break;
+    }
+    T = prefix;
+  }
+
+  // ---- gather: slot = #in with a lower id + #ties taken with a lower id ----
+  uint32_t in_bits = 0u, tie_bits = 0u;
+#pragma unroll
+  for (int e = 0; e < EPT; ++e) {
+    if (b0 + e < W) {
+      if (all || key[e] > T) in_bits |= 1u << e;
+      else if (key[e] == T) tie_bits |= 1u << e;
+    }
+  }
+  const uint32_t v = ((uint32_t)__popc(in_bits) << 16) | (uint32_t)__popc(tie_bits);
+  uint32_t inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += t;
+  }
+  if (lane == 31) sred[4 + warp] = inc;
   __syncthreads();
+  uint32_t before = inc - v, total = 0u;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+    const uint32_t t = sred[4 + w];
+    if (w < warp) before += t;
+    total += t;
+  }
+  const int ties_left = M - (int)(total >> 16);
+  int in_b = (int)(before >> 16), tie_b = (int)(before & 0xffffu);
+#pragma unroll
+  for (int e = 0; e < EPT; ++e) {
+    int slot = -1;
+    if ((in_bits >> e) & 1u) {
+      slot = in_b + min(tie_b, ties_left);
+      ++in_b;
+    } else if ((tie_bits >> e) & 1u) {
+      if (tie_b < ties_left) slot = in_b + tie_b;
+      ++tie_b;
+    }
+    if (slot >= 0) {
+      mid_[slot] = b0 + e;
+      mx[slot] = x[e];
+    }
+  }
+  __syncthreads();
+  return M;
+}
+
+template <int PER>
+__device__ __noinline__ void select_tail_warp(const DashRouteArgs& a, const uint32_t* scand, const int* mid_,
+                                              float* mx, int* mval, int M, int64_t r, int lane) {
+  select_tail<PER>(a, scand, mid_, mx, mval, M, r, lane);
+}
+
+// Scores of blocks [rank * per, rank * per + per) of the row into ssc.
+__device__ __forceinline__ void cluster_score_slice(const DashRouteArgs& a, const float* sq, float* ssc,
+                                                    int rank, int per, int s, int64_t qblk, int kvl) {
   const float inv_sqrt_d = (float)(1.0 / sqrt((double)a.d));
   const float4* sq4 = reinterpret_cast<const float4*>(sq);
-  for (int t = threadIdx.x; t < per; t += 128) {
+  for (int t = threadIdx.x; t < per; t += blockDim.x) {
     const int b = rank * per + t;
     float sc = kScoreNeg;
-    bool live = b < W && (int64_t)b <= qblk - a.local_blocks && (int64_t)b * a.block_size < kvl;
+    bool live = b < a.width && (int64_t)b <= qblk - a.local_blocks && (int64_t)b * a.block_size < kvl;
     int64_t kr = 0;
     if (live) {
       kr = a.block_table ? (int64_t)a.block_table[(int64_t)s * a.bt_stride + b]
@@ -793,13 +976,105 @@ __global__ void __launch_bounds__(128) route_cluster_kernel(DashRouteArgs a) {
     }
     ssc[t] = sc;
   }
+}
+
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// RK: 0 no refresh; 1 / 2 refresh with fp32 / bf16 index keys (d = 128,
+// 16-byte staging).  ka.n_plan entries spread over the helper CTAs (rank >= 1)
+// of every cluster.
+template <int RK>
+__global__ void __launch_bounds__(128) route_cluster_kernel(const __grid_constant__ DashRouteArgs a,
+                                                            const __grid_constant__ DashKbarArgs ka) {
+  extern __shared__ __align__(16) float smc[];
+  cg::cluster_group cl = cg::this_cluster();
+  const int rank = (int)cl.block_rank();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int W = a.width;
+  const int Wp = (W + 31) & ~31;
+  const int per = cluster_slice(W);
+  const int perp = (per + 31) & ~31;
+  float* sq = smc;                                   // [128] router query
+  float* ssc = sq + 128;                             // [per] this CTA's slice of scores
+  float* rest = ssc + perp;                          // CTA 0: selection; helpers: refresh
+
+  const int64_t r = (int64_t)(blockIdx.x / kClusterCtas);
+  int s, i;
+  row_to_seq(a.seqs, r, s, i);
+  const int64_t pos = seq_pos(a.seqs, s, i);
+  const int kvl = seq_kv_len(a.seqs, s);
+  const int64_t qblk = pos >= 0 ? pos / a.block_size : -1;
+  sq[threadIdx.x] = a.idx_q[r * a.q_row_stride + threadIdx.x];
+  __syncthreads();
+  cluster_score_slice(a, sq, ssc, rank, per, s, qblk, kvl);
   cl.sync();                                  // every slice written
-  if (rank == 0) {
-    for (int b = threadIdx.x; b < W; b += 128) {
-      const int src = b / per;
-      const float* remote = cl.map_shared_rank(ssc, src);
-      sx[b] = remote[b - src * per];
+
+  if (rank != 0) {
+    cluster_arrive_release();                 // nothing more for CTA 0 to wait on
+    if constexpr (RK > 0) {
+      using KT = typename std::conditional<RK == 1, float, __nv_bfloat16>::type;
+      const int helpers = (int)(gridDim.x / kClusterCtas) * (kClusterCtas - 1);
+      for (int e = (int)(blockIdx.x / kClusterCtas) * (kClusterCtas - 1) + rank - 1; e < ka.n_plan;
+           e += helpers) {
+        int n;
+        int64_t base, out_row;
+        if (kbar_paged_entry(ka, e, n, base, out_row)) kbar_pool_body<KT, 128, true>(ka, rest, n, base, out_row);
+      }
     }
+    cluster_wait_acquire();                   // CTA 0 has read this slice
+    return;
+  }
+
+  // ---- CTA 0: the row's scores, then its selection ----
+  uint32_t* scand = reinterpret_cast<uint32_t*>(rest);         // [Wp / 32]
+  int* mid_ = reinterpret_cast<int*>(scand + Wp / 32);         // [kMaxM]
+  float* mx = reinterpret_cast<float*>(mid_ + kMaxM);          // [kMaxM]
+  int* mval = reinterpret_cast<int*>(mx + kMaxM);              // [kMaxM]
+  uint32_t* hist = reinterpret_cast<uint32_t*>(mval + kMaxM);  // [256]
+  uint32_t* sred = hist + 256;                                 // [16]
+  float* sx = reinterpret_cast<float*>(sred + 16);             // [Wp] (rows wider than the CTA form)
+  auto pull = [&](int b) -> float {
+    const int src = b / per;
+    return cl.map_shared_rank(ssc, src)[b - src * per];
+  };
+  int M = 0;
+  auto cta_select = [&](auto ept_c) {
+    constexpr int E = decltype(ept_c)::value;
+    float sc[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const int b = (int)threadIdx.x * E + e;
+      sc[e] = b < W ? pull(b) : kScoreNeg;
+    }
+    cluster_arrive_release();                 // every slice has been read
+    if (a.scores_out) {
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const int b = (int)threadIdx.x * E + e;
+        if (b < W) a.scores_out[r * a.scores_out_stride + b] = sc[e];
+      }
+    }
+    M = select_head_cta<E>(a, sc, W, r, s, scand, mid_, mx, hist, sred);
+  };
+  const int ept = cluster_ept(W);
+  if (ept == 1) cta_select(std::integral_constant<int, 1>{});
+  else if (ept == 2) cta_select(std::integral_constant<int, 2>{});
+  else if (ept == 4) cta_select(std::integral_constant<int, 4>{});
+  else if (ept == 8) cta_select(std::integral_constant<int, 8>{});
+  if (ept > 0) {
+    if (warp == 0) {
+      if (M <= 32) select_tail_warp<1>(a, scand, mid_, mx, mval, M, r, lane);
+      else if (M <= 64) select_tail_warp<2>(a, scand, mid_, mx, mval, M, r, lane);
+      else select_tail_warp<kMaxM / 32>(a, scand, mid_, mx, mval, M, r, lane);
+    }
+  } else {
+    for (int b = threadIdx.x; b < W; b += blockDim.x) sx[b] = pull(b);
+    cluster_arrive_release();
     __syncthreads();
     if (warp == 0) {
       if (a.scores_out)
@@ -808,7 +1083,7 @@ __global__ void __launch_bounds__(128) route_cluster_kernel(DashRouteArgs a) {
       select_row_any(a, sx, scand, mid_, mx, mval, r, s, lane);
     }
   }
-  cl.sync();                                  // slices stay alive until CTA 0 has read them
+  cluster_wait_acquire();
 }
 
 // ---------------------------------------------------------------------------
@@ -870,6 +1145,49 @@ __global__ void __launch_bounds__(128) block_max_kernel(DashBlockMaxArgs a) {
 // ---------------------------------------------------------------------------
 // host launchers
 // ---------------------------------------------------------------------------
+// The decode form: a cluster of CTAs per row (few rows, scored here).
+static bool route_takes_cluster(const DashRouteArgs& a, int64_t n_rows) {
+  return !a.scores_in && a.d == 128 && n_rows < 148 * 16;
+}
+
+// 16-byte staging of a k-bar pool needs every row start 16-byte aligned.
+static bool kbar_vec_ok(const DashKbarArgs& a) {
+  const int w = a.dtype == DASH_DTYPE_F32 ? 4 : 8;
+  return (reinterpret_cast<uintptr_t>(a.keys) & 15) == 0 && a.d % w == 0 && a.tok_stride % w == 0 &&
+         (a.pages == nullptr ? a.seq_stride % w == 0 : a.page_stride % w == 0);
+}
+
+// ka: optional paged k-bar plan refreshed by the helper CTAs (d = 128, 16-byte
+// staging; the caller checked).
+static int launch_route_cluster(const DashRouteArgs& a, int64_t n_rows, const DashKbarArgs* ka,
+                                cudaStream_t st) {
+  DashKbarArgs none = {};
+  const int rk = ka == nullptr ? 0 : ka->dtype == DASH_DTYPE_F32 ? 1 : 2;
+  const size_t rf = rk ? kbar_pool_smem_floats(ka->block_size, 128) : 0;
+  const size_t smem = sizeof(float) * route_cluster_smem_floats(a.width, rf);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(n_rows * kClusterCtas));
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kClusterCtas;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  auto go = [&](auto kern) -> cudaError_t {
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    return cudaLaunchKernelEx(&cfg, kern, a, ka ? *ka : none);
+  };
+  const cudaError_t e = rk == 0 ? go(route_cluster_kernel<0>) : rk == 1 ? go(route_cluster_kernel<1>)
+                                                                        : go(route_cluster_kernel<2>);
+  if (e != cudaSuccess) return set_error(DASH_ERR_CUDA, "route_cluster_kernel launch: %s", cudaGetErrorString(e));
+  count_launch();
+  return check_launch("route_cluster_kernel");
+}
+
 int launch_kbar(const DashKbarArgs& a, cudaStream_t st) {
   dim3 grid;
   if (a.pages == nullptr) {
@@ -879,12 +1197,8 @@ int launch_kbar(const DashKbarArgs& a, cudaStream_t st) {
     grid = dim3(a.n_plan);
   }
   if (grid.x == 0 || grid.y == 0) return DASH_OK;
-  size_t smem = sizeof(float) * ((size_t)a.block_size * (a.d + 1) + a.d + a.block_size + 4);
-  // 16-byte staging needs every row start 16-byte aligned
-  const int w = a.dtype == DASH_DTYPE_F32 ? 4 : 8;
-  const bool vec = (reinterpret_cast<uintptr_t>(a.keys) & 15) == 0 && a.d % w == 0 &&
-                   a.tok_stride % w == 0 &&
-                   (a.pages == nullptr ? a.seq_stride % w == 0 : a.page_stride % w == 0);
+  size_t smem = sizeof(float) * kbar_pool_smem_floats(a.block_size, a.d);
+  const bool vec = kbar_vec_ok(a);
   auto go = [&](auto kern) {
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -903,6 +1217,15 @@ int launch_kbar(const DashKbarArgs& a, cudaStream_t st) {
   return check_launch("kbar_pool_kernel");
 }
 
+int launch_route_refresh(const DashRouteArgs& a, int64_t n_rows, const DashKbarArgs& ka, cudaStream_t st) {
+  if (ka.n_plan > 0 && ka.pages && n_rows > 0 && ka.d == 128 && kbar_vec_ok(ka) &&
+      route_takes_cluster(a, n_rows))
+    return launch_route_cluster(a, n_rows, &ka, st);
+  // any other form: the refresh, then the routing (two launches)
+  const int rc = ka.n_plan > 0 ? launch_kbar(ka, st) : DASH_OK;
+  return rc != DASH_OK ? rc : launch_route(a, n_rows, st);
+}
+
 int launch_route(const DashRouteArgs& a, int64_t n_rows, cudaStream_t st) {
   if (n_rows == 0) return DASH_OK;
   int Wp = (a.width + 31) & ~31;
@@ -917,27 +1240,7 @@ int launch_route(const DashRouteArgs& a, int64_t n_rows, cudaStream_t st) {
     return check_launch("route_tile_kernel");
   }
   // few rows (decode): a cluster of CTAs per row scores the blocks in parallel
-  if (!a.scores_in && a.d == 128 && n_rows < 148 * 16) {
-    const size_t smem = sizeof(float) * route_cluster_smem_floats(a.width);
-    if (smem > 48 * 1024)
-      cudaFuncSetAttribute(route_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(n_rows * kClusterCtas));
-    cfg.blockDim = dim3(128);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = kClusterCtas;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, route_cluster_kernel, a);
-    if (e != cudaSuccess) return set_error(DASH_ERR_CUDA, "route_cluster_kernel launch: %s", cudaGetErrorString(e));
-    count_launch();
-    return check_launch("route_cluster_kernel");
-  }
+  if (route_takes_cluster(a, n_rows)) return launch_route_cluster(a, n_rows, nullptr, st);
   // few rows otherwise: one CTA per row so all its threads score; else warp per row
   const bool cta_row = n_rows < 148 * 16;
   size_t smem = per_warp * (cta_row ? 1 : kRouteWarps);

@@ -126,9 +126,8 @@ def kbar_pool_contig(idx_k: torch.Tensor, head_cls: Optional[torch.Tensor], bloc
     return out
 
 
-def kbar_pool_paged(index_cache: torch.Tensor, pages: torch.Tensor, ntok: torch.Tensor,
-                    head_cls: Optional[torch.Tensor], kbar: torch.Tensor) -> torch.Tensor:
-    """Refresh kbar[page] from index_cache [P, bs, d] for each (page, ntok) entry."""
+def _kbar_paged_args(index_cache, pages, ntok, head_cls, kbar):
+    """DashKbarArgs of a paged refresh plan, with the tensors it points into."""
     _need_cuda(index_cache, pages, ntok, kbar)
     P, bs, d = index_cache.shape
     pages = pages.to(torch.int64).contiguous()
@@ -143,6 +142,13 @@ def kbar_pool_paged(index_cache: torch.Tensor, pages: torch.Tensor, ntok: torch.
     a.head_cls = _ptr(hc)
     a.pages, a.ntok = pages.data_ptr(), ntok.data_ptr()
     a.kbar, a.kbar_row_stride = kbar.data_ptr(), kbar.stride(0)
+    return a, (pages, ntok, hc)
+
+
+def kbar_pool_paged(index_cache: torch.Tensor, pages: torch.Tensor, ntok: torch.Tensor,
+                    head_cls: Optional[torch.Tensor], kbar: torch.Tensor) -> torch.Tensor:
+    """Refresh kbar[page] from index_cache [P, bs, d] for each (page, ntok) entry."""
+    a, keep = _kbar_paged_args(index_cache, pages, ntok, head_cls, kbar)
     if a.n_plan:
         L.call("dash_kbar_pool", a)
     return kbar
@@ -159,15 +165,19 @@ def route(seqs: Seqs, *, width: int, block_size: int, local_blocks: int, idx_sca
           out_idx: Optional[torch.Tensor] = None, out_bias: Optional[torch.Tensor] = None,
           out_width: Optional[int] = None, scores_out: Optional[torch.Tensor] = None,
           out_count: Optional[torch.Tensor] = None, device_error: Optional[DeviceErrorWord] = None,
-          page=None):
+          page=None, refresh=None):
     """Fused DASH routing for ``seqs.rows`` query rows.
 
     Either ``scores_in`` [rows, width] (precomputed block scores) or ``idx_q``
     [rows, d] + ``kbar`` (contiguous [n_seq, nblk, d] or a page cache [P, d]
     addressed through ``block_table`` [n_seq, W]).  ``page`` (a
     ``pages.PageDomain``) restricts the candidates to the blocks holding image
-    tokens of each row's page (instead of ``cand``).  Returns (idx int32 [rows,
-    out_width] ascending with -1 tail, bias fp32 [rows, out_width])."""
+    tokens of each row's page (instead of ``cand``).  ``refresh`` (index_cache
+    [P, bs, d], pages, ntok, head_cls) refreshes those k-bar rows of the page
+    cache in the same launch (``dash_route_refresh``); the rows must not be
+    scored by this call (a decode step's tail pages, inside every row's local
+    window).  Returns (idx int32 [rows, out_width] ascending with -1 tail, bias
+    fp32 [rows, out_width])."""
     ref = scores_in if scores_in is not None else idx_q
     _need_cuda(ref, kbar, block_table, cand)
     dev = ref.device
@@ -218,7 +228,16 @@ def route(seqs: Seqs, *, width: int, block_size: int, local_blocks: int, idx_sca
             a.page_bits, a.page_bits_words = page.bits.data_ptr(), page.bits.shape[-1]
         a.page_seq_rows = page.seq_rows if block_table is None else 0
         a.num_page_desc = page.lo.numel()
-    L.call("dash_route", a)
+    if refresh is None:
+        L.call("dash_route", a)
+        return out_idx, out_bias
+    if block_table is None:
+        raise ValueError("the folded k-bar refresh needs the paged k-bar cache (block_table)")
+    ka, keep = _kbar_paged_args(*refresh, kbar)
+    lib = L.load()
+    rc = lib.dash_route_refresh(ctypes.byref(a), ctypes.byref(ka) if ka.n_plan else None, L.current_stream())
+    if rc != L.DASH_OK:
+        raise L.DashError(rc, L.last_error())
     return out_idx, out_bias
 
 

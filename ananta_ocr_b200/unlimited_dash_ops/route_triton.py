@@ -160,12 +160,15 @@ def route_decode_triton(*, idx_q, k_bar, block_table, seq_lens, image_allow, out
                         decode_query_len: int, idx_scale: float, prior_floor: float,
                         sigma: float, topm: int, score_buf=None, budget=None, out_slots=None,
                         entmax_base=None, entmax_fit=None, entmax_width: int = 0,
-                        score_buf_win=None, bounds=None, page_domain=None):
+                        score_buf_win=None, bounds=None, page_domain=None, refresh=None):
     """Decode routing for ``nd = R * decode_query_len`` rows (the last
     ``decode_query_len`` tokens of each request).  The window-narrowing
     arguments of the reference are accepted; the fused kernel scans all
     ``max_block`` columns of a row in one pass.  ``page_domain`` as in
-    ``route_prefill_triton``.  Returns the slot width M."""
+    ``route_prefill_triton``.  ``refresh`` (extension): ``(kv_cache, head_cls,
+    plan)`` as given to ``kbar_refresh_tail_triton``, whose refresh then runs
+    inside this launch; the plan's pages must be tail pages inside every row's
+    local window (``tail_pages <= local_blocks``).  Returns the slot width M."""
     nd = int(idx_q.shape[0])
     dql = max(1, int(decode_query_len))
     W = min(int(max_block), int(block_table.shape[1]))
@@ -179,5 +182,14 @@ def route_decode_triton(*, idx_q, k_bar, block_table, seq_lens, image_allow, out
     ops.route(seqs, width=W, block_size=block_size, local_blocks=local_blocks,
               idx_scale=idx_scale, prior_floor=prior_floor, sigma=sigma, topm=int(topm), K=K,
               idx_q=idx_q, kbar=k_bar, block_table=bt, cand=cand,
-              out_idx=out_idx[:nd], out_bias=out_bias[:nd], out_width=M, page=page_domain)
+              out_idx=out_idx[:nd], out_bias=out_bias[:nd], out_width=M, page=page_domain,
+              refresh=_refresh_args(refresh, block_size))
     return M
+
+
+def _refresh_args(refresh, block_size):
+    if refresh is None:
+        return None
+    kv_cache, head_cls, plan = refresh
+    pages, tok = plan
+    return kv_cache.view(kv_cache.shape[0], block_size, -1), pages, tok, head_cls

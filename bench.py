@@ -820,15 +820,15 @@ def run_decode_setup(cfg, dev, seed):
 
 
 def decode_route(cfg, d):
-    """k-bar refresh of each sequence's tail page + decode routing."""
+    """k-bar refresh of each sequence's tail page + decode routing, one launch
+    (the refresh runs on the routing clusters' idle CTAs)."""
     from ananta_ocr_b200.unlimited_dash_ops import route_triton as RT
     bs, lb, K = cfg["bs"], cfg["lb"], cfg["K"]
-    RT.kbar_refresh_tail_triton(kv_cache=d["icache"], k_bar=d["kbar"], block_table=d["bt"],
-                                seq_lens=d["sl"], head_cls=None, block_size=bs, plan=d["tail"])
     RT.route_decode_triton(idx_q=d["iq"], k_bar=d["kbar"], block_table=d["bt"], seq_lens=d["sl"],
                            image_allow=None, out_idx=d["oi"], out_bias=d["ob"], max_block=d["nb"],
                            block_size=bs, local_blocks=lb, decode_query_len=1, idx_scale=IDX_SCALE,
-                           prior_floor=1e-4, sigma=1.0, topm=K, budget=K, out_slots=K)
+                           prior_floor=1e-4, sigma=1.0, topm=K, budget=K, out_slots=K,
+                           refresh=(d["icache"], None, d["tail"]))
 
 
 def decode_attend(cfg, d):

@@ -229,6 +229,18 @@ typedef struct {
 } DashRouteArgs;
 int dash_route(const DashRouteArgs* args, dash_stream_t stream);
 
+/* Decode routing with the k-bar tail refresh of the same step in one launch.
+ * Replaces the pair WHL route_triton.py:707-726 (kbar_refresh_tail_triton)
+ * then :730-847 (route_decode_triton), as called per decode step by
+ * WHL unlimited_ocr_v2_backend.py.  `refresh` is a paged DashKbarArgs plan
+ * (pages/ntok) writing the k-bar rows that `args` reads (NULL: dash_route).
+ * The rows it refreshes must not be rows this launch scores: the tail pages
+ * of a decode step lie in every row's local window when tail_pages <=
+ * local_blocks.  Few-row decode launches with d == 128 and 16-byte aligned
+ * keys run the refresh on the routing cluster's idle CTAs; any other form
+ * runs the refresh, then the routing, as two launches.                    */
+int dash_route_refresh(const DashRouteArgs* args, const DashKbarArgs* refresh, dash_stream_t stream);
+
 /* ---------------------------------------------------------------------- */
 /* Page-aware candidate domain (image pages of an OCR document).
  *
