@@ -318,7 +318,7 @@ static int decode_slots() {
 int decode_auto_splits(const DashDecodeArgs& a, int64_t n_rows) {
   const int64_t units = n_rows * a.qo.n_heads;
   const int items = a.routes.K + a.local_window / a.block_size + 1;
-  const int64_t slots = decode_slots();
+  const int64_t slots = decode_tma_supported(a) ? decode_tma_slots() : decode_slots();
   int best = 1;
   double best_cost = 1e300;
   for (int sp = 1; sp <= 16 && sp <= items; ++sp) {
@@ -350,6 +350,7 @@ int launch_decode(const DashDecodeArgs& a, int64_t n_rows, int splits, cudaStrea
     cudaError_t e = cudaMemsetAsync(counters, 0, (size_t)units * sizeof(int), st);
     if (e != cudaSuccess) return set_error(DASH_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
   }
+  if (decode_tma_supported(a)) return launch_decode_tma(a, n_rows, splits, part, counters, st);
   dim3 grid((unsigned)(n_rows * splits), a.qo.n_heads);
   if (a.kv.dtype == DASH_DTYPE_BF16)
     decode_kernel<__nv_bfloat16><<<grid, kDecWarps * 32, 0, st>>>(a, splits, part, counters);

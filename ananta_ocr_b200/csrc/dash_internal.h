@@ -23,6 +23,11 @@ size_t prefill_workspace(const DashPrefillArgs& a, int64_t n_rows);
 bool prefill_gathered_supported(const DashPrefillArgs& a);
 size_t decode_workspace(const DashDecodeArgs& a, int64_t n_rows, int splits);
 int decode_auto_splits(const DashDecodeArgs& a, int64_t n_rows);
+// paged bf16/fp16 caches with 128-dim heads: K/V streamed by TMA (dash_decode_tma.cu)
+bool decode_tma_supported(const DashDecodeArgs& a);
+int decode_tma_slots();
+int launch_decode_tma(const DashDecodeArgs& a, int64_t n_rows, int splits, float* part, int* counters,
+                      cudaStream_t st);
 int validate_decode(const DashDecodeArgs* a, int* splits);   // DASH_OK or a status with message
 int launch_page_ids(const DashPageIdsArgs& a, cudaStream_t st);
 int launch_page_state(const DashPageStateArgs& a, cudaStream_t st);
