@@ -837,15 +837,45 @@ __device__ int select_head_cta(const DashRouteArgs& a, const float (&sc)[EPT], i
   // ---- threshold T: keys > T are in, keys == T are ties ----
   uint32_t T = 0u;
   if (!all) {
-    uint32_t prefix = 0u;
+    // bits every key shares are decided at once (scores of a row sit in a
+    // narrow range, so their top bits agree): only the `lo` low bits below
+    // the highest differing bit are resolved digit by digit
+    uint32_t kand = 0xffffffffu, kor = 0u;
+#pragma unroll
+    for (int e = 0; e < EPT; ++e)
+      if (b0 + e < W) {
+        kand &= key[e];
+        kor |= key[e];
+      }
+    kand = __reduce_and_sync(0xffffffffu, kand);
+    kor = __reduce_or_sync(0xffffffffu, kor);
+    if (lane == 0) {
+      sred[8 + warp] = kand;
+      sred[12 + warp] = kor;
+    }
+    __syncthreads();
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+      kand &= sred[8 + w];
+      kor |= sred[12 + w];
+    }
+    const uint32_t diff = kand ^ kor;
+    int lo = diff ? 32 - __clz(diff) : 0;
+    uint32_t prefix = lo >= 32 ? 0u : (kand & (0xffffffffu << lo));
     int need = M;                       // keys still to take among those matching prefix
-    for (int shift = 24; shift >= 0; shift -= 8) {
+    while (lo > 0) {
+      const int shift = lo > 8 ? lo - 8 : 0;
+      const uint32_t hmask = lo >= 32 ? 0u : (0xffffffffu << lo);
+      const uint32_t dmask = (1u << (lo - shift)) - 1u;
       for (int j = tid; j < 256; j += blockDim.x) hist[j] = 0u;
       __syncthreads();
-      const uint32_t hmask = shift == 24 ? 0u : (0xffffffffu << (shift + 8));
 #pragma unroll
-      for (int e = 0; e < EPT; ++e)
-        if (b0 + e < W && (key[e] & hmask) == prefix) atomicAdd(hist + ((key[e] >> shift) & 255u), 1u);
+      for (int e = 0; e < EPT; ++e) {
+        const bool in = b0 + e < W && (key[e] & hmask) == prefix;
+        const uint32_t dg = in ? (key[e] >> shift) & dmask : 0xffffffffu;
+        // one increment per distinct digit of the warp
+        const uint32_t same = __match_any_sync(0xffffffffu, dg);
+        if (in && (same & ((1u << lane) - 1u)) == 0u) atomicAdd(hist + dg, (uint32_t)__popc(same));
+      }
       __syncthreads();
       if (warp == 0) {
         // lane l holds digits 8l .. 8l+7; suf = keys with digit >= 8l
@@ -884,6 +914,7 @@ __device__ int select_head_cta(const DashRouteArgs& a, const float (&sc)[EPT], i
       __syncthreads();
       prefix = sred[0];
       need = (int)sred[1];
+      lo = shift;
       if (sred[2]) break;
     }
     T = prefix;
