@@ -327,7 +327,7 @@ __device__ __forceinline__ void select_tail(const DashRouteArgs& a, const uint32
     valid[u] = false;
     if (u < nper && t < M) {
       valid[u] = rk[u] < Kc && is_cand(mid_[t]);
-      mx[rk[u]] = __fdiv_rn(__fsub_rn(xt[u], xmax), 2.0f);   // z by rank
+      mx[rk[u]] = __fmul_rn(__fsub_rn(xt[u], xmax), 0.5f);   // z by rank (x/2 exactly)
       mval[rk[u]] = valid[u] ? 1 : 0;
     }
   }
@@ -452,26 +452,52 @@ __device__ __noinline__ void select_row(const DashRouteArgs& a, float* sx, uint3
       }
     }
   }
-  bool any = false;
-  for (int b0 = 0; b0 < Wp; b0 += 32) {
-    int b = b0 + lane;
-    bool remote = b < W && sx[b] > kScoreNeg * 0.5f;
-    bool c = remote;
-    if (a.page_q) c = remote && (KW > 0 ? ((pcm >> (b0 >> 5)) & 1u) != 0 : page_block_holds(a, qp, s, b));
-    else if (cm) c = remote && cm[b] != 0;
-    uint32_t bal = __ballot_sync(0xffffffffu, c);
-    if (lane == 0) scand[b0 >> 5] = bal;
-    any |= bal != 0;
-  }
-  __syncwarp();
-  if (!any) {
+  // KW > 0: the row's scores of blocks lane + 32u come into registers once;
+  // candidate bit u of this lane in cbits
+  float sv[KW > 0 ? KW : 1];
+  uint32_t cbits = 0u;
+  if constexpr (KW > 0) {
+    uint32_t rbits = 0u;
+#pragma unroll
+    for (int u = 0; u < KW; ++u) {
+      const int b = lane + 32 * u;
+      sv[u] = b < W ? sx[b] : kScoreNeg;
+      const bool remote = b < W && sv[u] > kScoreNeg * 0.5f;
+      bool c = remote;
+      if (a.page_q) c = remote && ((pcm >> u) & 1u) != 0;
+      else if (cm) c = remote && cm[b] != 0;
+      rbits |= (remote ? 1u : 0u) << u;
+      cbits |= (c ? 1u : 0u) << u;
+    }
+    if (!__any_sync(0xffffffffu, cbits != 0u)) cbits = rbits;   // fallback: every remote block
+#pragma unroll
+    for (int u = 0; u < KW; ++u) {
+      const uint32_t bal = __ballot_sync(0xffffffffu, (cbits >> u) & 1u);
+      if (lane == 0 && 32 * u < Wp) scand[u] = bal;
+    }
+    __syncwarp();
+  } else {
+    bool any = false;
     for (int b0 = 0; b0 < Wp; b0 += 32) {
       int b = b0 + lane;
       bool remote = b < W && sx[b] > kScoreNeg * 0.5f;
-      uint32_t bal = __ballot_sync(0xffffffffu, remote);
+      bool c = remote;
+      if (a.page_q) c = remote && page_block_holds(a, qp, s, b);
+      else if (cm) c = remote && cm[b] != 0;
+      uint32_t bal = __ballot_sync(0xffffffffu, c);
       if (lane == 0) scand[b0 >> 5] = bal;
+      any |= bal != 0;
     }
     __syncwarp();
+    if (!any) {
+      for (int b0 = 0; b0 < Wp; b0 += 32) {
+        int b = b0 + lane;
+        bool remote = b < W && sx[b] > kScoreNeg * 0.5f;
+        uint32_t bal = __ballot_sync(0xffffffffu, remote);
+        if (lane == 0) scand[b0 >> 5] = bal;
+      }
+      __syncwarp();
+    }
   }
   auto is_cand = [&](int b) -> bool { return (scand[b >> 5] >> (b & 31)) & 1u; };
   auto xform = [&](int b) -> float {
@@ -507,7 +533,9 @@ __device__ __noinline__ void select_row(const DashRouteArgs& a, float* sx, uint3
 #pragma unroll
     for (int u = 0; u < KW; ++u) {
       const int b = lane + 32 * u;
-      xr[u] = b < W ? xform(b) : 0.0f;
+      float v = ((cbits >> u) & 1u) ? __fmul_rn(sv[u], a.idx_scale) : kEntmaxNeg;
+      if (!(v == v) || isinf(v)) v = kEntmaxNeg;
+      xr[u] = b < W ? v : 0.0f;
       kr[u] = b < W ? order_key(xr[u]) : 0u;
     }
     uint32_t T = 0;
@@ -523,7 +551,7 @@ __device__ __noinline__ void select_row(const DashRouteArgs& a, float* sx, uint3
 #pragma unroll
       for (int u = 0; u < KW; ++u) {
         const int b = lane + 32 * u;
-        if (b < W && is_cand(b)) {
+        if (b < W && ((cbits >> u) & 1u)) {
           ++nc;
           low |= !(xr[u] > kEntmaxNeg);
         }
@@ -600,20 +628,26 @@ __device__ __forceinline__ void select_row_any(const DashRouteArgs& a, float* sx
 constexpr int kTileRows = 32;
 constexpr int kPcCache = 33;   // per warp: page-candidacy mask per lane + the query page
 constexpr int kChunk = 64;
-constexpr int kLd = 132;   // padded fp32 row (conflict-free 16-byte loads)
+constexpr int kLd = 132;   // padded fp32 query row (conflict-free 16-byte loads by row)
+constexpr int kKLd = 128;  // k-bar chunk row (read by broadcast: no padding)
 
-__host__ __device__ inline size_t route_tile_smem_floats(int W) {
+// Per-warp selection scratch of a row: candidate bits [Wp / 32] and the
+// top-M items (id, x, rank flag) [3 * Mp], Mp = M rounded up to 32.
+__host__ __device__ inline int route_sel_floats(int W, int M) {
+  return (W + 31) / 32 + 3 * ((M + 31) & ~31);
+}
+__host__ __device__ inline size_t route_tile_smem_floats(int W, int M) {
   const int Wp = (W + 31) & ~31;
-  return (size_t)kTileRows * kLd + (size_t)kChunk * kLd + kChunk + (size_t)kTileRows * Wp +
-         8 * ((size_t)Wp / 32 + 3 * kMaxM) + 8 * kPcCache;
+  return (size_t)kTileRows * kLd + (size_t)kChunk * kKLd + kChunk + (size_t)kTileRows * Wp +
+         8 * (size_t)route_sel_floats(W, M) + 8 * kPcCache;
 }
 
-__global__ void __launch_bounds__(256) route_tile_kernel(const __grid_constant__ DashRouteArgs a, int tiles_per_seq) {
+__global__ void __launch_bounds__(256, 3) route_tile_kernel(const __grid_constant__ DashRouteArgs a, int tiles_per_seq) {
   extern __shared__ float smt[];
   const int W = a.width, Wp = (W + 31) & ~31;
   float* qs = smt;                                  // [32][kLd]
-  float* kbs = qs + kTileRows * kLd;                // [64][kLd]
-  int* kbad = reinterpret_cast<int*>(kbs + kChunk * kLd);   // [64]
+  float* kbs = qs + kTileRows * kLd;                // [64][kKLd]
+  int* kbad = reinterpret_cast<int*>(kbs + kChunk * kKLd);  // [64]
   float* scs = reinterpret_cast<float*>(kbad + kChunk);     // [32][Wp]
   float* selbase = scs + kTileRows * Wp;            // per warp: cand | ids | x | ranks
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -656,7 +690,7 @@ __global__ void __launch_bounds__(256) route_tile_kernel(const __grid_constant__
           bad = 0;
         }
       }
-      *reinterpret_cast<float4*>(kbs + bb * kLd + 4 * c4) = v;
+      *reinterpret_cast<float4*>(kbs + bb * kKLd + 4 * c4) = v;
       if (c4 == 0) kbad[bb] = bad;
     }
     __syncthreads();
@@ -667,7 +701,7 @@ __global__ void __launch_bounds__(256) route_tile_kernel(const __grid_constant__
       const float4 q4 = *reinterpret_cast<const float4*>(qs + rr * kLd + 4 * c4);
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        const float4 k4 = *reinterpret_cast<const float4*>(kbs + (warp + 8 * k) * kLd + 4 * c4);
+        const float4 k4 = *reinterpret_cast<const float4*>(kbs + (warp + 8 * k) * kKLd + 4 * c4);
         acc[k] = __fmaf_rn(q4.x, k4.x, acc[k]);
         acc[k] = __fmaf_rn(q4.y, k4.y, acc[k]);
         acc[k] = __fmaf_rn(q4.z, k4.z, acc[k]);
@@ -683,14 +717,18 @@ __global__ void __launch_bounds__(256) route_tile_kernel(const __grid_constant__
     }
     __syncthreads();
   }
-  float* sel = selbase + warp * (Wp / 32 + 3 * kMaxM);
-  uint32_t* pc_cache = reinterpret_cast<uint32_t*>(selbase + 8 * (Wp / 32 + 3 * kMaxM)) + warp * kPcCache;
+  // selection scratch sized by the entmax window M (every index it takes is < M)
+  const int Msel = a.topm > 0 ? min(a.topm, W) : W;
+  const int Mp = (max(Msel, 1) + 31) & ~31;
+  const int sel_floats = route_sel_floats(W, Msel);
+  float* sel = selbase + warp * sel_floats;
+  uint32_t* pc_cache = reinterpret_cast<uint32_t*>(selbase + 8 * sel_floats) + warp * kPcCache;
   if (lane == 0) pc_cache[32] = 0x80000000u;   // no page cached (pages are >= -1)
   __syncwarp();
   uint32_t* scand = reinterpret_cast<uint32_t*>(sel);
   int* mid_ = reinterpret_cast<int*>(scand + Wp / 32);
-  float* mx = reinterpret_cast<float*>(mid_ + kMaxM);
-  int* mrank = reinterpret_cast<int*>(mx + kMaxM);
+  float* mx = reinterpret_cast<float*>(mid_ + Mp);
+  int* mrank = reinterpret_cast<int*>(mx + Mp);
   for (int r2 = warp; r2 < nr; r2 += 8) {
     const int64_t r = rbase + r2;
     float* sx = scs + r2 * Wp;
@@ -1264,7 +1302,8 @@ int launch_route(const DashRouteArgs& a, int64_t n_rows, cudaStream_t st) {
   // many rows of few sequences: tiled kernel (k-bar chunks shared by 32 rows)
   if (!a.scores_in && a.width <= 1024 && a.d == 128 && n_rows >= 148 * 16) {
     const int tiles = (a.seqs.max_q_len + kTileRows - 1) / kTileRows;
-    const size_t sm = sizeof(float) * route_tile_smem_floats(a.width);
+    const int M = a.topm > 0 ? (a.topm < a.width ? a.topm : a.width) : a.width;
+    const size_t sm = sizeof(float) * route_tile_smem_floats(a.width, M);
     cudaFuncSetAttribute(route_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
     route_tile_kernel<<<(unsigned)((int64_t)a.seqs.n_seq * tiles), 256, sm, st>>>(a, tiles);
     count_launch();
