@@ -5,7 +5,9 @@ k-bar refresh, decode routing and decode attention consistent with the
 prefill path), and the decode step replayed from a CUDA graph equals the
 eager step bit for bit.  The two paths sum in different orders (prefill vs
 decode attention kernels, grouped vs dense MoE GEMMs), so the logits agree to
-2% of their largest magnitude."""
+2% of their largest magnitude.  One layer of the model is also checked
+against the CPU oracle in prefill and in the decode step: its k-bar rows
+(bitwise), routed lists (bit-exact) and attention output (bf16 tolerance)."""
 import pytest
 import torch
 
@@ -151,3 +153,99 @@ def test_page_domain_equals_reference_allow_mask(cfg):
     for _ in range(3):
         assert torch.equal(dom.decode_step(), ref.decode_step())
         assert torch.equal(dom.oi, ref.oi) and torch.equal(dom.ob, ref.ob)
+
+
+# ---------------------------------------------------------------------------
+# one layer of the decoder against the CPU oracle: the k-bar rows of the page
+# cache, the routed lists (bit-exact) and the attention output, in prefill and
+# in the decode step that follows
+# ---------------------------------------------------------------------------
+def _capture(monkeypatch):
+    """Record the last call's inputs / outputs of the routing and attention
+    functions the decoder calls (module attributes, restored after the test)."""
+    import ananta_ocr_b200.e2e_decoder as E
+    rec = {}
+
+    def wrap(mod, name, keys):
+        orig = getattr(mod, name)
+
+        def f(*args, **kw):
+            r = orig(*args, **kw)
+            rec[name] = {k: (v.clone() if torch.is_tensor(v) else v) for k, v in kw.items() if k in keys}
+            rec[name]["args"] = [a.clone() if torch.is_tensor(a) else a for a in args]
+            return r
+        monkeypatch.setattr(mod, name, f)
+
+    wrap(E.RT, "route_prefill_triton", ("idx_q", "out_idx", "out_bias"))
+    wrap(E.RT, "route_decode_triton", ("idx_q", "out_idx", "out_bias", "seq_lens"))
+    wrap(E.AT, "dash_sparse_attn", ())
+    wrap(E.AT, "dash_sparse_attn_decode", ())
+    return rec
+
+
+def _oracle_layer(d, li, idx_q, pos, req, seq_lens):
+    """k-bar rows of every page in use, routes and bias of the given rows."""
+    import numpy as np
+    from oracle import dash_oracle as O
+    c = d.cfg
+    bs = c.block_size
+    bt = d.block_table.cpu().numpy()
+    sl = seq_lens.cpu().numpy()
+    pages, ntok = [], []
+    for r in range(bt.shape[0]):
+        for b in range(-(-int(sl[r]) // bs)):
+            pages.append(bt[r, b])
+            ntok.append(min(bs, int(sl[r]) - b * bs))
+    kbar = np.zeros((d.num_pages, c.index_dim), np.float32)
+    O.kbar_paged(d.ic[li].cpu().numpy(), np.array(pages), np.array(ntok),
+                 d.layers[li]["head_cls"].cpu().numpy(), kbar)
+    sc = O.scores_paged(idx_q.cpu().numpy(), pos, req, sl, kbar, bt, bs, c.local_blocks, d.pps)
+    oi, ob, _ = O.route_select(sc, None, d.idx_scale, c.topm, c.K, c.prior_floor, c.sigma)
+    return np.array(pages), kbar, oi, ob
+
+
+def test_layer_vs_oracle_prefill_and_decode(cfg, monkeypatch):
+    import numpy as np
+    from oracle import dash_oracle as O
+    from dash_testutil import assert_close_bf16
+    rec = _capture(monkeypatch)
+    S, B = 301, 2
+    c = CFG
+    d = make(11)
+    ids = torch.randint(0, c.vocab, (B, S + 1), generator=torch.Generator().manual_seed(2)).cuda()
+    d.prefill(d.embed[ids[:, :S]])
+    li = c.layers - 1                       # every cache below is this layer's, after its call
+    K, bs = c.K, c.block_size
+    scale = 1.0 / np.sqrt(c.head_dim)
+    # ---- prefill ----
+    rp = rec["route_prefill_triton"]
+    pos = np.tile(np.arange(S), B)
+    req = np.repeat(np.arange(B), S)
+    pages, kbar, oi, ob = _oracle_layer(d, li, rp["idx_q"], pos, req, d.seq_lens)
+    assert np.array_equal(d.kbar[li].cpu().numpy()[pages], kbar[pages]), "prefill k-bar rows"
+    gi, gb = rp["out_idx"].cpu().numpy(), rp["out_bias"].cpu().numpy()
+    np.testing.assert_array_equal(gi[:, :K], oi)
+    assert (gi[:, K:] == -1).all()
+    np.testing.assert_allclose(gb[:, :K], ob, atol=1e-4, rtol=0)
+    q = rec["dash_sparse_attn"]["args"][0].float().cpu().numpy()
+    out = rec["dash_sparse_attn"]["args"][12].float().cpu().numpy()
+    kc, vc = d.kc[li].float().cpu().numpy(), d.vc[li].float().cpu().numpy()
+    bt = d.block_table.cpu().numpy()
+    ref = O.attend_paged(q, kc, vc, oi, ob, bt, req, pos, bs, c.local_blocks * bs, scale)
+    assert_close_bf16(out, ref)
+    # ---- the decode step that follows ----
+    d.tok.copy_(ids[:, S])
+    d.decode_step()
+    rd = rec["route_decode_triton"]
+    dpos = np.full(B, S)
+    _, kbar2, oi2, ob2 = _oracle_layer(d, li, rd["idx_q"], dpos, np.arange(B), rd["seq_lens"])
+    pages2 = bt[:, :-(-(S + 1) // bs)].reshape(-1)
+    assert np.array_equal(d.kbar[li].cpu().numpy()[pages2], kbar2[pages2]), "decode k-bar rows"
+    gi2, gb2 = rd["out_idx"].cpu().numpy(), rd["out_bias"].cpu().numpy()
+    np.testing.assert_array_equal(gi2[:, :K], oi2)
+    np.testing.assert_allclose(gb2[:, :K], ob2, atol=1e-4, rtol=0)
+    qd = rec["dash_sparse_attn_decode"]["args"][0].float().cpu().numpy()
+    outd = rec["dash_sparse_attn_decode"]["args"][9].float().cpu().numpy()
+    refd = O.attend_paged(qd, d.kc[li].float().cpu().numpy(), d.vc[li].float().cpu().numpy(), oi2, ob2,
+                          bt, np.arange(B), dpos, bs, c.local_blocks * bs, scale)
+    assert_close_bf16(outd, refd)
