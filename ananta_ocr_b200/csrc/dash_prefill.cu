@@ -930,9 +930,17 @@ bool prefill_gathered_supported(const DashPrefillArgs& a) {
          a.routes.K <= kPlanMaxSlots;
 }
 
-// Mode 0 is tile-major: the gathered split is taken on request (mode 2).
+// Mode 0 picks by the expected union waste.  A 128-row tile's union covers
+// nearly every candidate block when routes vary from row to row, so the
+// tile-major kernel executes about (candidates x block) keys per row against
+// K x block routed ones; the gathered split pays a 260-byte partial per
+// routed (row, head, block) instead.  Measured on B200: 128-token blocks
+// with K = 64 run 572 ms gathered vs 625 ms tile-major;
+// 64-token blocks with K = 16 (config 2) 2.25 ms vs 1.13 ms.  So the gathered
+// split is taken for blocks of 128 tokens with K >= 32, or on request (2).
 static bool use_gathered(const DashPrefillArgs& a) {
-  return a.mode == 2 && prefill_gathered_supported(a);
+  if (a.mode == 1 || !prefill_gathered_supported(a)) return false;
+  return a.mode == 2 || (a.block_size >= 128 && a.routes.K >= 32);
 }
 
 // Gathered mode: chunks of sequences x tile pairs x kv heads whose partials

@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
   uint64_t* rows_full = bars + 0;       // [NQS] enumerator -> loaders, MMA, softmax
   uint64_t* q_full = bars + 3;          // [NQS] loader group (4 warps) -> MMA
-  uint64_t* stage_free = bars + 6;      // [NQS] QK done (commit) + epilogue done (4 warps)
+  uint64_t* stage_free = bars + 6;      // [NQS] QK done (commit) + slot data read (4 softmax warps)
   uint64_t* kv_ready = bars + 9;        // [2] K/V buffer loaded (and its tail zeroed)
   uint64_t* kv_tail = bars + 11;        // [2] load of a sequence's last block (zeroed after)
   uint64_t* kv_free = bars + 13;        // [2] every PV of the buffer's item issued + done
@@ -324,6 +324,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool alive = true;
       int nq = 0;               // QKs issued (batches 0 .. nq-1 exist)
       bool more = true;
+      // K/V buffer and item of batches n and n + 1 (QK'd, PV pending): taken
+      // at QK time, since the stage may be reused once the softmax has read it
+      int qk_buf[2] = {0, 0}, qk_item[2] = {-1, -1};
       // QK(n) into S buffer n % 2.  That buffer held P(n-2), read by PV(n-2):
       // this thread issued PV(n-2) before, and its tcgen05.mma ops execute in
       // issue order; softmax finished with S(n-2) before PV(n-2) was issued.
@@ -334,6 +337,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(rows_full + st, par, abort_flag, derr, 96)) { more = false; alive = false; return; }
         const RStage& S = stg[st];
         if (S.ns == 0) { more = false; return; }
+        qk_buf[n & 1] = S.buf;
+        qk_item[n & 1] = S.item;
         if (!mbar_wait(q_full + st, par, abort_flag, derr, 97) ||
             !mbar_wait(kv_ready + S.buf, (uint32_t)S.kvpar, abort_flag, derr, 98)) {
           more = false;
@@ -360,8 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(p_full + (n & 1), (uint32_t)(n >> 1) & 1u, abort_flag, derr, 99)) break;
         if (n >= 2 && !mbar_wait(o_free + (n & 1), (uint32_t)((n - 2) >> 1) & 1u, abort_flag, derr, 100)) break;
         tc_fence_after();
-        const RStage& S = stg[n % NQS];
-        const int buf = S.buf;
+        const int buf = qk_buf[n & 1];
         const uint32_t sV = smem_u32(sV_of(buf));
         const uint32_t tS = tS_of(n & 1), tO = tO_of(n & 1);
 #pragma unroll
@@ -372,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(o_full + (n & 1));
         // the last PV of an item frees its K/V buffer for the item after next
         // (batch n+1 is known: its QK was issued before this PV)
-        if (n + 1 < nq && stg[(n + 1) % NQS].item != S.item) umma_commit(kv_free + buf);
+        if (n + 1 < nq && qk_item[(n + 1) & 1] != qk_item[n & 1]) umma_commit(kv_free + buf);
         try_qk();
       }
       // every MMA completes before TMEM is released
@@ -470,17 +474,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tO = tO_of(m & 1);
       const float inv_l = prev_l > 0.0f ? 1.0f / prev_l : 0.0f;
 #pragma unroll 1
-      for (int q4 = 0; q4 < 4; ++q4) {
-        float o[32];
-        tmem_ld32f(tO + q4 * 32 + lane_base, o);
+      for (int h = 0; h < 2; ++h) {
+        float o[64];
+        tmem_ld32f(tO + h * 64 + lane_base, o);
+        tmem_ld32f(tO + h * 64 + 32 + lane_base, o + 32);
         tmem_ld_wait();
         if (prev_poff >= 0) {
-          uint32_t pko[16];
+          uint32_t pko[32];
 #pragma unroll
-          for (int c = 0; c < 32; c += 2) pko[c >> 1] = pack2(o[c] * inv_l, o[c + 1] * inv_l, (T*)nullptr);
-          uint4* dst = reinterpret_cast<uint4*>(const_cast<uint16_t*>(p.part_o) + prev_poff * HD + q4 * 32);
+          for (int c = 0; c < 64; c += 2) pko[c >> 1] = pack2(o[c] * inv_l, o[c + 1] * inv_l, (T*)nullptr);
+          uint4* dst = reinterpret_cast<uint4*>(const_cast<uint16_t*>(p.part_o) + prev_poff * HD + h * 64);
 #pragma unroll
-          for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pko[4 * v], pko[4 * v + 1], pko[4 * v + 2], pko[4 * v + 3]);
+          for (int v = 0; v < 8; ++v) dst[v] = make_uint4(pko[4 * v], pko[4 * v + 1], pko[4 * v + 2], pko[4 * v + 3]);
         }
       }
       tc_fence_before();
@@ -488,8 +493,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(o_free + (m & 1));
       if (prev_poff >= 0)
         const_cast<float*>(p.part_lse)[prev_poff] = prev_l > 0.0f ? prev_m + log2f(prev_l) : -INFINITY;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(stage_free + (m % NQS));
       return true;
     };
     int n = 0;
@@ -503,44 +506,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       const RStage& S = stg[st];
       const int klo = S.klo[n2], kcut = S.kcut[n2];
       const int64_t poff = S.poff[n2];
+      // the stage is free for the enumerator once every slot's data is read
+      // (the epilogue works from registers)
+      __syncwarp();
+      if (lane == 0) mbar_arrive(stage_free + st);
       if (!mbar_wait_warp(s_full + (n & 1), (uint32_t)(n >> 1) & 1u, abort_flag, derr, 106)) { alive = false; break; }
       tc_fence_after();
       const uint32_t tS = tS_of(n & 1);
-      // pass 1: the row max over the kept keys; pass 2: P (packed) over the
-      // S columns already read (64 S columns per 32-column store)
+      // pass 1: the row max over the kept keys; pass 2: P (packed, 64 S
+      // columns per 32-column store).  S is read 64 columns per wait; with
+      // 64-key blocks pass 2 reuses the registers of pass 1.
       float mrow = -INFINITY, lrow = 0.0f;
+      float x[64];
 #pragma unroll 1
-      for (int c0 = 0; c0 < BS; c0 += 32) {
-        float x[32];
+      for (int c0 = 0; c0 < BS; c0 += 64) {
         tmem_ld32f(tS + c0 + lane_base, x);
+        if (c0 + 32 < BS) tmem_ld32f(tS + c0 + 32 + lane_base, x + 32);
         tmem_ld_wait();
 #pragma unroll
-        for (int c = 0; c < 32; ++c)
-          if (c0 + c >= klo && c0 + c < kcut) mrow = fmaxf(mrow, x[c] * sl2);
+        for (int c = 0; c < 64; ++c)
+          if (c0 + c < BS && c0 + c >= klo && c0 + c < kcut) mrow = fmaxf(mrow, x[c] * sl2);
       }
       const float mref = mrow == -INFINITY ? 0.0f : mrow;
 #pragma unroll 1
       for (int sc = 0; sc < (BS + 63) / 64; ++sc) {
+        const int c0 = sc * 64;
+        if (BS > 64) {
+          tmem_ld32f(tS + c0 + lane_base, x);
+          if (c0 + 32 < BS) tmem_ld32f(tS + c0 + 32 + lane_base, x + 32);
+          tmem_ld_wait();
+        }
         uint32_t pk[32];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int c0 = sc * 64 + h * 32;
-          if (c0 < BS) {
-            float x[32];
-            tmem_ld32f(tS + c0 + lane_base, x);
-            tmem_ld_wait();
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const int c = c0 + 2 * e;
-              const float p0 = (c >= klo && c < kcut) ? fast_exp2(fmaf(x[2 * e], sl2, -mref)) : 0.0f;
-              const float p1 = (c + 1 >= klo && c + 1 < kcut) ? fast_exp2(fmaf(x[2 * e + 1], sl2, -mref)) : 0.0f;
-              lrow += p0 + p1;
-              pk[h * 16 + e] = pack2(p0, p1, (T*)nullptr);
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) pk[h * 16 + e] = 0u;
-          }
+        for (int e = 0; e < 32; ++e) {
+          const int c = c0 + 2 * e;
+          const float p0 = (c < BS && c >= klo && c < kcut) ? fast_exp2(fmaf(x[2 * e], sl2, -mref)) : 0.0f;
+          const float p1 = (c + 1 < BS && c + 1 >= klo && c + 1 < kcut) ? fast_exp2(fmaf(x[2 * e + 1], sl2, -mref)) : 0.0f;
+          lrow += p0 + p1;
+          pk[e] = pack2(p0, p1, (T*)nullptr);
         }
         tmem_st32(tS + sc * 32 + lane_base, pk);
       }

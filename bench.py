@@ -577,9 +577,18 @@ def run_c4(dev, rank, world, steps, warmup, mode):
                 executed=float(fl[1]), tokens=B * S, shard=(sh.b0, sh.b1, sh.h0, sh.h1))
 
 
+def c4_gathered():
+    """Whether the library's automatic prefill split takes the gathered form
+    at config 4 (blocks of 128 tokens with K >= 32, or ``--prefill-mode 2``)."""
+    from ananta_ocr_b200 import ops as _ops
+    mode = _ops.PREFILL_MODE
+    return mode == 2 or (mode == 0 and C4["bs"] >= 128 and C4["K"] >= 32)
+
+
 def c4_summary(r, world, gather, peaks, peak_kind):
     """The config-4 figures of ``run_c4`` as a JSON object."""
     peak = peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
+    gathered = c4_gathered()
     tf = r["alg"] / (r["ms"] / 1e3) / 1e12
     return {
         "workload": C4["name"], "scaling": "strong", "n_gpus": world,
@@ -592,8 +601,12 @@ def c4_summary(r, world, gather, peaks, peak_kind):
                                   if gather != "nccl" else "in-place NCCL all-gather"),
         "ms_per_step": r["ms"], "tokens_per_s": r["tokens"] / (r["ms"] / 1e3),
         "attn_and_gather_ms": r["attn_gather_ms"],
-        "alg_tflops": tf, "executed_tflops": r["executed"] / (r["ms"] / 1e3) / 1e12,
-        "alg_flops_per_step": r["alg"], "executed_flops_per_step": r["executed"],
+        "prefill_split": ("routed keys gathered by key block (prefill_routed_kernel + "
+                          "prefill_merge_kernel; window part tile-major)" if gathered else
+                          "tile-major (each 128-row tile runs the union of its rows' blocks)"),
+        "alg_tflops": tf,
+        "executed_tflops": None if gathered else r["executed"] / (r["ms"] / 1e3) / 1e12,
+        "alg_flops_per_step": r["alg"], "executed_flops_per_step": None if gathered else r["executed"],
         "roofline": {"bound": "tensor", "achieved": tf, "peak": peak * world, "unit": "TFLOP/s",
                      "frac": tf / (peak * world),
                      "kernel": "whole step (routing + prefill_kernel + gather), algorithmic FLOPs, "

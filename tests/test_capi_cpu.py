@@ -93,7 +93,16 @@ def test_prefill_mode_checks_and_workspace():
     union, full = size(1), size(2)
     # every (row, head, slot) partial: 128 bf16 + one fp32
     assert full - union >= 4 * 9248 * 10 * 16 * 260
-    assert size(0) == union                     # automatic: tile-major
+    assert size(0) == union                     # automatic: tile-major for 64-token blocks, K = 16
+
+    def size128(mode, K):
+        a = _prefill_args(K=K, block_size=128)
+        a.seqs.n_seq, a.seqs.q_len_fixed, a.seqs.kv_len_fixed, a.seqs.max_q_len = 1, 16384, 16384, 16384
+        a.mode = mode
+        return lib.dash_prefill_workspace_size(C.byref(a))
+    # automatic: gathered for 128-token blocks with K >= 32 (the long-document shape)
+    assert size128(0, 64) == size128(2, 64) > size128(1, 64)
+    assert size128(0, 16) == size128(1, 16)
     small = size(2, budget=8)
     assert union < small <= union + 8 * 2**20 + 4 * 145 * 292 * 4 + 3 * 256
 
