@@ -37,6 +37,7 @@
 // the query's local window, + the slot's bias), WHL attend_triton.py:88-292.
 #include <cudaTypedefs.h>
 #include <climits>
+#include <cstring>
 #include "dash_common.cuh"
 #include "dash_internal.h"
 #include "dash_prefill_plan.cuh"
@@ -82,6 +83,20 @@ struct RLayout {
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
+// Four rows (any row indices) x 64 columns of a 2-D tensor into four
+// consecutive 128-byte rows of shared memory, with the map's swizzle.
+__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, uint64_t* bar, int col, int r0,
+                                            int r1, int r2, int r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(col), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+      : "memory");
+}
+// Bytes the current phase of an mbarrier waits for, without an arrival.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void cp_async_wait_all_r() {
   asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
 }
@@ -91,7 +106,8 @@ __device__ __forceinline__ void cp_async_wait_all_r() {
 template <typename T, bool PAGED, int BS>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_routed_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                          const DashPrefillArgs a, const PrefillPlan p, const int hcn) {
+                          const __grid_constant__ CUtensorMap tmQ, const DashPrefillArgs a, const PrefillPlan p,
+                          const int hcn, const int qmap) {
   using L = RLayout<BS>;
   constexpr int NQS = L::NQS;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -391,6 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int n2 = tid - (kLoadWarp0 + 4 * grp) * 32;        // slot 0..127
     const T* qbase = reinterpret_cast<const T*>(a.qo.q);
     const bool vec = (K & 3) == 0;
+    int last_n = -1;                  // the last batch this group gathered rows for
     for (int n = grp;; n += 2) {
       const int st = n % NQS;
       if (!mbar_wait_warp(rows_full + st, (uint32_t)(n / NQS) & 1u, abort_flag, derr, 102)) break;
@@ -402,18 +419,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int i = live ? S.rowtok[n2 / G] : i_lo;
       const int hq = hk * G + (n2 % G);
       const int64_t rg = row_base(a.seqs, s) + i;
-      // q row -> stage (swizzled K-major); padding slots are zero
+      // q row -> stage (swizzled K-major)
       {
         const int64_t qoff = (a.seqs.q_start ? rg * a.qo.q_stride_tok
                                              : (int64_t)s * a.qo.q_stride_seq + (int64_t)i * a.qo.q_stride_tok) +
                              (int64_t)hq * a.qo.q_stride_head;
-        const uint4* src = reinterpret_cast<const uint4*>(qbase + qoff);
         uint8_t* sQ = sm + L::OFF_Q + st * 32768;
+        if (qmap) {
+          // TMA row gather: 4 slots x 64 columns per instruction into the
+          // swizzled halves, 16 instructions for the warp's 32 slots (lanes
+          // 0-15), instead of 512 lane copies through the load/store unit.
+          // q rows are whole 128-element rows of the map (the host checked
+          // the strides); a padding slot takes row 0 (its P is masked to 0
+          // and it writes no partial).
+          const int wq = n2 >> 5;
+          const int row = live ? (int)(qoff >> 7) : 0;
+          const int quad = lane >> 1, h = lane & 1;
+          const int r0 = __shfl_sync(0xffffffffu, row, 4 * quad), r1 = __shfl_sync(0xffffffffu, row, 4 * quad + 1);
+          const int r2 = __shfl_sync(0xffffffffu, row, 4 * quad + 2), r3 = __shfl_sync(0xffffffffu, row, 4 * quad + 3);
+          if (lane == 0) mbar_expect_tx(q_full + st, 32 * 256);
+          __syncwarp();
+          if (lane < 16)
+            tma_gather4(sQ + h * 16384 + (wq * 32 + 4 * quad) * 128, &tmQ, q_full + st, h * 64, r0, r1, r2, r3);
+        } else {
+          // padding slots are zero
+          const uint4* src = reinterpret_cast<const uint4*>(qbase + qoff);
 #pragma unroll
-        for (int cc = 0; cc < 16; ++cc) {
-          uint8_t* dst = sQ + (cc >> 3) * 16384 + n2 * 128 + (((cc & 7) ^ (n2 & 7)) << 4);
-          if (live) cp_async16(dst, src + cc);
-          else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+          for (int cc = 0; cc < 16; ++cc) {
+            uint8_t* dst = sQ + (cc >> 3) * 16384 + n2 * 128 + (((cc & 7) ^ (n2 & 7)) << 4);
+            if (live) cp_async16(dst, src + cc);
+            else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+          }
         }
       }
       // key range and partial entry (list position of the block: the row's
@@ -454,11 +490,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       S.poff[n2] = poff;
       S.klo[n2] = klo;
       S.kcut[n2] = kcut;
-      cp_async_wait_all_r();
-      fence_proxy_async_smem();
+      if (!qmap) {
+        cp_async_wait_all_r();
+        fence_proxy_async_smem();
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(q_full + st);
+      last_n = n;
     }
+    // never leave the CTA with row gathers in flight: the last batch's rows
+    // have landed (its MMA waited for them, unless the CTA gave up early)
+    if (qmap && last_n >= 0 && lane == 0) {
+      volatile int no_abort = 0;
+      mbar_wait(q_full + last_n % NQS, (uint32_t)(last_n / NQS) & 1u, &no_abort, nullptr, 108);
+    }
+    __syncwarp();
   } else {
     // ======== softmax of batch n, then the epilogue of batch n-1 (thread = slot) ========
     const int n2 = tid;                             // 0..127, TMEM lane
@@ -689,9 +735,53 @@ static int sm_count() {
   return n > 0 ? n : 148;
 }
 
+static PFN_cuTensorMapEncodeTiled_v12000 routed_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }
+  return fn;
+}
+
+// The queries as a 2-D tensor of 128-element rows for the TMA row gather:
+// possible when every q stride is a whole number of rows (the [B, H, T, D],
+// [B, T, H, D] and packed [T, H, D] layouts).  Returns false otherwise (the
+// loaders then copy rows with cp.async).
+static bool make_q_rows_map(CUtensorMap* map, const DashPrefillArgs& c) {
+  auto enc = routed_encode_fn();
+  const DashQO& qo = c.qo;
+  if (!enc || (reinterpret_cast<uintptr_t>(qo.q) & 15) != 0) return false;
+  const bool packed = c.seqs.q_start != nullptr;
+  if (qo.q_stride_tok < 0 || qo.q_stride_head < 0 || qo.q_stride_tok % 128 || qo.q_stride_head % 128) return false;
+  if (!packed && (qo.q_stride_seq < 0 || qo.q_stride_seq % 128)) return false;
+  const int64_t rows_of_seq = packed ? (int64_t)c.seqs.q_len_fixed : (int64_t)c.seqs.max_q_len;
+  if (rows_of_seq <= 0 || c.seqs.n_seq <= 0 || qo.n_heads <= 0) return false;
+  const int64_t max_off = (packed ? 0 : (int64_t)(c.seqs.n_seq - 1) * qo.q_stride_seq) +
+                          (rows_of_seq - 1) * qo.q_stride_tok + (int64_t)(qo.n_heads - 1) * qo.q_stride_head;
+  const int64_t rows = max_off / 128 + 1;
+  if (rows >= ((int64_t)1 << 31)) return false;
+  cuuint64_t dims[2] = {128, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {256};
+  cuuint32_t box[2] = {64, 1};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, c.kv.dtype == DASH_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                         2, const_cast<void*>(qo.q), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 template <typename T, bool PAGED, int BS>
 static int launch_routed_typed(const DashPrefillArgs& c, const PrefillPlan& p, const CUtensorMap& mk,
                                const CUtensorMap& mv, int hcn, cudaStream_t st) {
+  CUtensorMap mq;
+  memset(&mq, 0, sizeof(mq));
+  const int qmap = make_q_rows_map(&mq, c) ? 1 : 0;
   auto kern = prefill_routed_kernel<T, PAGED, BS>;
   constexpr int smem = RLayout<BS>::SMEM;
   static_assert(smem <= 232448, "shared memory budget");
@@ -700,7 +790,7 @@ static int launch_routed_typed(const DashPrefillArgs& c, const PrefillPlan& p, c
   // persistent: one CTA per SM walks the (sequence, block, kv head) items
   const int64_t items = (int64_t)p.sn * p.nblk_cap * hcn;
   const unsigned grid = (unsigned)(items < sm_count() ? items : sm_count());
-  kern<<<grid, kThreads, smem, st>>>(mk, mv, c, p, hcn);
+  kern<<<grid, kThreads, smem, st>>>(mk, mv, mq, c, p, hcn, qmap);
   count_launch();
   return check_launch("prefill_routed_kernel");
 }
