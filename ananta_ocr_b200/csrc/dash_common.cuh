@@ -131,17 +131,33 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that may park the thread until the phase completes, for up to
+// `hint_ns` (the hardware wakes it when the phase completes): a waiting warp
+// does not spin on the issue slots its sub-partition shares with the others.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait: returns false when the CTA abort flag is up or the wait ran
 // past `limit_ns`; in the latter case it raises the abort flag and records
-// DASH_DEV_TIMEOUT in the device error word.
+// DASH_DEV_TIMEOUT in the device error word.  After a few polls the thread
+// parks in the hinted try_wait (20 us at most per try) instead of spinning.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile int* abort_flag, DeviceError* err,
                                           int where, uint64_t limit_ns = 2000000000ull) {
-  for (int i = 0; i < 256; ++i)
+  for (int i = 0; i < 32; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   uint64_t t0 = globaltimer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
     if (*abort_flag) return false;
     if (globaltimer_ns() - t0 > limit_ns) {
       *abort_flag = 1;

@@ -949,6 +949,10 @@ def main():
                     help="launch eagerly instead of replaying captured CUDA graphs")
     ap.add_argument("--decode-rows", type=int, default=0,
                     help="decode batch override (small cases for profiler captures)")
+    ap.add_argument("--c4-seqs", type=int, default=0,
+                    help="config-4 sequence count override (small cases for profiler captures)")
+    ap.add_argument("--c4-len", type=int, default=0,
+                    help="config-4 sequence length override (small cases for profiler captures)")
     ap.add_argument("--prefill-mode", type=int, default=0, choices=[0, 1, 2],
                     help="prefill work split: 0 automatic, 1 tile-major, 2 routed part gathered "
                          "by key block")
@@ -956,6 +960,11 @@ def main():
     cfg = C2 if args.workload == "c2" else C4
     if args.decode_rows > 0:
         C3["R"] = args.decode_rows
+    if args.c4_seqs > 0:
+        C4["B"] = args.c4_seqs
+    if args.c4_len > 0:
+        C4["S"] = args.c4_len
+        C4["n_pages"] = max(1, args.c4_len // C4["page_tokens"])
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
