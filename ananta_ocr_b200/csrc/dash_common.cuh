@@ -148,12 +148,12 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parit
 
 // Bounded wait: returns false when the CTA abort flag is up or the wait ran
 // past `limit_ns`; in the latter case it raises the abort flag and records
-// DASH_DEV_TIMEOUT in the device error word.  After a few polls the thread
+// DASH_DEV_TIMEOUT in the device error word.  After 8 polls the thread
 // parks in the hinted try_wait (20 us at most per try) instead of spinning.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile int* abort_flag, DeviceError* err,
                                           int where, uint64_t limit_ns = 2000000000ull) {
-  for (int i = 0; i < 32; ++i)
+  for (int i = 0; i < 8; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   uint64_t t0 = globaltimer_ns();
   while (true) {
