@@ -813,29 +813,47 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                               : (int64_t)s * a.qo.o_stride_seq + (int64_t)tok * a.qo.o_stride_tok) +
               (int64_t)hq * a.qo.o_stride_head;
       if (p.flags) op = reinterpret_cast<T*>(const_cast<uint16_t*>(p.part_o) + pent * HD);
+      // The group's Q buffer is free (its last QK completed before the last
+      // PV): the rows are staged there (16-byte chunk c of row m at
+      // ((c ^ (m & 15)) << 4)), then every warp writes its 32 rows two per
+      // instruction (lanes 0-15 one row, 16-31 the next: 512 contiguous
+      // bytes per instruction instead of 32 scattered 16-byte pieces), to
+      // the output and, fused output gather, to every peer rank's copy of it
+      // (P2P stores over NVLink; same strides, same offset).
+      uint8_t* stg = sm + OFF_Q + g * 32768;
   #pragma unroll
       for (int q4 = 0; q4 < 4; ++q4) {
         uint32_t o[32];
         tmem_ld32(tO + q4 * 32 + lane_base, o);
         tmem_ld_wait();
-        if (row_ok) {
-          uint32_t pko[16];
+        uint32_t pko[16];
   #pragma unroll
-          for (int c = 0; c < 32; c += 2)
-            pko[c >> 1] = pack2(win ? __uint_as_float(o[c]) * inv_l : 0.0f,
-                                win ? __uint_as_float(o[c + 1]) * inv_l : 0.0f, (T*)nullptr);
+        for (int c = 0; c < 32; c += 2)
+          pko[c >> 1] = pack2(win ? __uint_as_float(o[c]) * inv_l : 0.0f,
+                              win ? __uint_as_float(o[c + 1]) * inv_l : 0.0f, (T*)nullptr);
   #pragma unroll
-          for (int v = 0; v < 4; ++v)
-            *reinterpret_cast<uint4*>(op + q4 * 32 + v * 8) = make_uint4(pko[4 * v], pko[4 * v + 1], pko[4 * v + 2], pko[4 * v + 3]);
-          // fused output gather: the same row into every peer rank's copy of
-          // the output (P2P stores over NVLink; same strides, same offset)
-          if (!p.flags) {
-            for (int pr = 0; pr < a.n_peers; ++pr) {
-              T* pop = reinterpret_cast<T*>(a.out_peers[pr]) + (op - reinterpret_cast<T*>(a.qo.out));
-  #pragma unroll
-              for (int v = 0; v < 4; ++v)
-                *reinterpret_cast<uint4*>(pop + q4 * 32 + v * 8) = make_uint4(pko[4 * v], pko[4 * v + 1], pko[4 * v + 2], pko[4 * v + 3]);
-            }
+        for (int v = 0; v < 4; ++v) {
+          const int c = q4 * 4 + v;
+          *reinterpret_cast<uint4*>(stg + m * 256 + ((c ^ (m & 15)) << 4)) =
+              make_uint4(pko[4 * v], pko[4 * v + 1], pko[4 * v + 2], pko[4 * v + 3]);
+        }
+      }
+      __syncwarp();
+      {
+        T* obase = p.flags ? reinterpret_cast<T*>(const_cast<uint16_t*>(p.part_o)) : reinterpret_cast<T*>(a.qo.out);
+        const int64_t myoff = row_ok ? (int64_t)(op - obase) : -1;
+        const int npeer = p.flags ? 0 : a.n_peers;
+        const int c = lane & 15;
+  #pragma unroll 4
+        for (int j = 0; j < 16; ++j) {
+          const int rr = 2 * j + (lane >> 4);                 // row of the warp
+          const int64_t off = __shfl_sync(0xffffffffu, myoff, rr);
+          const int mr = (warp & 3) * 32 + rr;
+          const uint4 val = *reinterpret_cast<const uint4*>(stg + mr * 256 + ((c ^ (mr & 15)) << 4));
+          if (off >= 0) {
+            *reinterpret_cast<uint4*>(obase + off + c * 8) = val;
+            for (int pr = 0; pr < npeer; ++pr)
+              *reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.out_peers[pr]) + off + c * 8) = val;
           }
         }
       }
