@@ -564,14 +564,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       // 64-key blocks pass 2 reuses the registers of pass 1.
       float mrow = -INFINITY, lrow = 0.0f;
       float x[64];
+      // Slots that keep every key of the block (no window cut and no segment
+      // start inside it; the scale is positive): the warp takes a mask-free
+      // path, max(x) * scale (the same value: rounding is monotonic) and
+      // packed f32x2 arithmetic for P.
+      const bool full = __all_sync(0xffffffffu, klo <= 0 && kcut >= BS) && sl2 > 0.0f;
 #pragma unroll 1
       for (int c0 = 0; c0 < BS; c0 += 64) {
         tmem_ld32f(tS + c0 + lane_base, x);
         if (c0 + 32 < BS) tmem_ld32f(tS + c0 + 32 + lane_base, x + 32);
         tmem_ld_wait();
+        if (full) {
+          float mx = x[0];
 #pragma unroll
-        for (int c = 0; c < 64; ++c)
-          if (c0 + c < BS && c0 + c >= klo && c0 + c < kcut) mrow = fmaxf(mrow, x[c] * sl2);
+          for (int c = 1; c < 64; ++c)
+            if (c0 + c < BS) mx = fmaxf(mx, x[c]);
+          mrow = fmaxf(mrow, mx * sl2);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (c0 + c < BS && c0 + c >= klo && c0 + c < kcut) mrow = fmaxf(mrow, x[c] * sl2);
+        }
       }
       const float mref = mrow == -INFINITY ? 0.0f : mrow;
 #pragma unroll 1
@@ -583,13 +596,33 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_wait();
         }
         uint32_t pk[32];
+        if (full) {
+          const uint64_t sv = f2_pack(sl2, sl2), mv = f2_pack(-mref, -mref);
+          uint64_t lsv = f2_pack(0.0f, 0.0f);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int c = c0 + 2 * e;
-          const float p0 = (c < BS && c >= klo && c < kcut) ? fast_exp2(fmaf(x[2 * e], sl2, -mref)) : 0.0f;
-          const float p1 = (c + 1 < BS && c + 1 >= klo && c + 1 < kcut) ? fast_exp2(fmaf(x[2 * e + 1], sl2, -mref)) : 0.0f;
-          lrow += p0 + p1;
-          pk[e] = pack2(p0, p1, (T*)nullptr);
+          for (int e = 0; e < 32; ++e) {
+            if (c0 + 2 * e < BS) {
+              float y0, y1;
+              f2_unpack(ffma2(f2_pack(x[2 * e], x[2 * e + 1]), sv, mv), y0, y1);
+              const float p0 = fast_exp2(y0), p1 = fast_exp2(y1);
+              lsv = fadd2(lsv, f2_pack(p0, p1));
+              pk[e] = pack2(p0, p1, (T*)nullptr);
+            } else {
+              pk[e] = 0u;
+            }
+          }
+          float l0, l1;
+          f2_unpack(lsv, l0, l1);
+          lrow += l0 + l1;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int c = c0 + 2 * e;
+            const float p0 = (c < BS && c >= klo && c < kcut) ? fast_exp2(fmaf(x[2 * e], sl2, -mref)) : 0.0f;
+            const float p1 = (c + 1 < BS && c + 1 >= klo && c + 1 < kcut) ? fast_exp2(fmaf(x[2 * e + 1], sl2, -mref)) : 0.0f;
+            lrow += p0 + p1;
+            pk[e] = pack2(p0, p1, (T*)nullptr);
+          }
         }
         tmem_st32(tS + sc * 32 + lane_base, pk);
       }
