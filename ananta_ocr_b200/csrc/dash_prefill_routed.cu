@@ -75,7 +75,9 @@ struct RLayout {
   static constexpr int OFF_KV = NQS * 32768;                // 2 buffers x (K, V: 2 halves x [BS][128 B])
   static constexpr int OFF_ST = OFF_KV + 2 * BS * 512;      // NQS x RStage
   static constexpr int OFF_BAR = OFF_ST + NQS * (int)sizeof(RStage);
-  static constexpr int USED = OFF_BAR + 256 + 1024;
+  // epilogue staging: one 64-column half of the batch's partial rows
+  static constexpr int OFF_OSTG = OFF_BAR + 256;             // [128 slots][128 B]
+  static constexpr int USED = OFF_OSTG + 16384 + 1024;
   // one CTA per SM: it takes all 512 TMEM columns
   static constexpr int SMEM = USED > 120 * 1024 ? USED : 120 * 1024;
 };
@@ -514,6 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the batch whose epilogue is pending: its partial entry, max and sum
     int64_t prev_poff = -1;
     float prev_m = 0.0f, prev_l = 0.0f;
+    uint8_t* ostg = sm + L::OFF_OSTG;
     auto epilogue = [&](int m) -> bool {
       if (!mbar_wait_warp(o_full + (m & 1), (uint32_t)(m >> 1) & 1u, abort_flag, derr, 103)) return false;
       tc_fence_after();
@@ -525,14 +528,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32f(tO + h * 64 + lane_base, o);
         tmem_ld32f(tO + h * 64 + 32 + lane_base, o + 32);
         tmem_ld_wait();
-        if (prev_poff >= 0) {
-          uint32_t pko[32];
+        // the half-row goes through shared memory (16-byte chunk c of slot
+        // n2 at ((c ^ (n2 & 7)) << 4)), then the warp writes its 32 slots'
+        // half-rows four per instruction (8 lanes x 16 bytes each) instead
+        // of 32 scattered 16-byte pieces
+        uint32_t pko[32];
 #pragma unroll
-          for (int c = 0; c < 64; c += 2) pko[c >> 1] = pack2(o[c] * inv_l, o[c + 1] * inv_l, (T*)nullptr);
-          uint4* dst = reinterpret_cast<uint4*>(const_cast<uint16_t*>(p.part_o) + prev_poff * HD + h * 64);
+        for (int c = 0; c < 64; c += 2) pko[c >> 1] = pack2(o[c] * inv_l, o[c + 1] * inv_l, (T*)nullptr);
 #pragma unroll
-          for (int v = 0; v < 8; ++v) dst[v] = make_uint4(pko[4 * v], pko[4 * v + 1], pko[4 * v + 2], pko[4 * v + 3]);
+        for (int v = 0; v < 8; ++v)
+          *reinterpret_cast<uint4*>(ostg + n2 * 128 + ((v ^ (n2 & 7)) << 4)) =
+              make_uint4(pko[4 * v], pko[4 * v + 1], pko[4 * v + 2], pko[4 * v + 3]);
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int rr = 4 * j + (lane >> 3), cc = lane & 7;
+          const int64_t off = __shfl_sync(0xffffffffu, prev_poff, rr);
+          const int mr = warp * 32 + rr;
+          const uint4 val = *reinterpret_cast<const uint4*>(ostg + mr * 128 + ((cc ^ (mr & 7)) << 4));
+          if (off >= 0)
+            *reinterpret_cast<uint4*>(const_cast<uint16_t*>(p.part_o) + off * HD + h * 64 + cc * 8) = val;
         }
+        __syncwarp();
       }
       tc_fence_before();
       __syncwarp();
