@@ -69,7 +69,9 @@ struct SlotMeta {
 };
 constexpr int META_BYTES = 2 * (int)sizeof(SlotMeta) + 4 * NS * 4;   // + dsum [4][NS]
 constexpr int OFF_BAR = (OFF_META + META_BYTES + 15) & ~15;
-constexpr int SMEM_TC = OFF_BAR + 128 + 1024;    // + alignment slack
+// dQ staging: per math warp, 32 slots x 32 fp32 (one quarter of a row)
+constexpr int OFF_DQSTG = (OFF_BAR + 128 + 127) & ~127;   // [8 warps][32 slots][128 B]
+constexpr int SMEM_TC = OFF_DQSTG + 8 * 4096 + 1024;       // + alignment slack
 static_assert(SMEM_TC <= 232448, "shared memory budget");
 constexpr uint32_t TMEM_COLS = 512;
 
@@ -390,16 +392,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc_fence_after();
         const SlotMeta& P = meta[(nb - 1) & 1];
         const int ns_prev = P.ns;
+        uint8_t* dstg = sm + OFF_DQSTG + warp * 4096;
 #pragma unroll 1
         for (int q2 = 0; q2 < 2; ++q2) {
           float v[32];
           tmem_ld32f(tDP + sh * 64 + q2 * 32 + lane_base, v);
           tmem_ld_wait();
-          if (kl < ns_prev) {
-            float* dst = dq_acc + ((int64_t)P.row[kl] * HQ + P.hq[kl]) * 128 + sh * 64 + q2 * 32;
+          // through shared memory (16-byte chunk c of slot `lane` at
+          // ((c ^ (lane & 7)) << 4)): the warp then reduces its 32 slots'
+          // 128-byte pieces four per instruction (8 lanes each) instead of
+          // 32 scattered 16-byte pieces
 #pragma unroll
-            for (int c = 0; c < 8; ++c) red_add_v4(dst + 4 * c, v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<float4*>(dstg + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+                make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int rr = 4 * j + (lane >> 3), cc = lane & 7;
+            const int slot = wq * 32 + rr;
+            if (slot < ns_prev) {
+              const float4 w = *reinterpret_cast<const float4*>(dstg + rr * 128 + ((cc ^ (rr & 7)) << 4));
+              float* dst = dq_acc + ((int64_t)P.row[slot] * HQ + P.hq[slot]) * 128 + sh * 64 + q2 * 32 + cc * 4;
+              red_add_v4(dst, w.x, w.y, w.z, w.w);
+            }
           }
+          __syncwarp();
         }
         // the producer may refill this meta buffer
         __syncwarp();
