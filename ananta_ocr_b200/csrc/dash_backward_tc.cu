@@ -32,7 +32,9 @@
 // Every wait is bounded (abort flag + time limit, DASH_DEV_TIMEOUT).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cudaTypedefs.h>
 #include <climits>
+#include <cstring>
 #include "dash_common.cuh"
 #include "dash_internal.h"
 
@@ -164,7 +166,8 @@ __device__ __forceinline__ float reduce_scatter32(float (&v)[32], int lane) {
 // segment test is compiled out
 template <typename E, bool SEG>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    bwd_tc_kernel(const DashAttnBwdArgs a, int nblk, int words, int ntiles, float* dq_acc) {
+    bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+                  const DashAttnBwdArgs a, int nblk, int words, int ntiles, float* dq_acc, const int qmap) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   SlotMeta* meta = reinterpret_cast<SlotMeta*>(sm + OFF_META);   // [2], batch b uses meta[b & 1]
@@ -433,7 +436,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         break;
       }
       // ---- gather slot n: threads 0-127 its q row, 128-255 its dout row ----
-      {
+      if (qmap) {
+        // TMA row gather: lane l < 16 of warp w brings slots (w&3)*32 + 4(l&7)
+        // .. +3, column half l>>3, of q (warps 0-3) or dout (warps 4-7).  A
+        // padding slot reads row 0: its position keeps every key out, so its
+        // P and dS are 0 whatever the row holds.
+        const int wq4 = warp & 3;
+        const bool isdo = warp >= 4;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_expect_tx(rows_full, 32 * 256);
+        __syncwarp();
+        if (lane < 16) {
+          const int quad = lane & 7, hf = lane >> 3;
+          const int n0 = wq4 * 32 + 4 * quad;
+          int r[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) r[j] = n0 + j < ns ? M.row[n0 + j] * HQ + M.hq[n0 + j] : 0;
+          tma_gather4(sm + (isdo ? OFF_DO : OFF_Q) + hf * 16384 + n0 * 128, isdo ? &tmDO : &tmQ, rows_full,
+                      hf * 64, r[0], r[1], r[2], r[3]);
+        }
+      } else {
         const int n = tid & (NS - 1);
         const bool live = n < ns;
         const int64_t off = ((int64_t)(live ? M.row[n] : 0) * HQ + (live ? M.hq[n] : 0)) * 128;
@@ -443,11 +466,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           cp_row_sw128(sm + OFF_Q, n, reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(a.q) + off), !live);
         cp_async_wait_all();
         fence_proxy_async_smem();
+        math_bar();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(rows_full);
       }
-      math_bar();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(rows_full);
       // ---- P^T and dS^T for key `key` (TMEM lane kl), slots sh*64 .. +63 ----
       if (!math_all(mbar_wait_warp(s_full, nb & 1, abort_flag, derr, 84))) { alive = false; break; }
       tc_fence_after();
@@ -584,6 +607,39 @@ __global__ void __launch_bounds__(256) bwd_dq_convert_kernel(const float* acc, E
   reinterpret_cast<uint2*>(dq)[i] = r;
 }
 
+static PFN_cuTensorMapEncodeTiled_v12000 bwd_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }
+  return fn;
+}
+
+// q or dout [n_seq, seq_len, n_heads, 128] as a 2-D tensor of 128-element
+// rows for the TMA row gather (box: one row x 64 columns, 128-byte swizzle).
+// Returns false when the rows do not fit the gather's int coordinates; the
+// kernel then copies rows with cp.async.
+static bool make_rows_map(CUtensorMap* map, const void* base, const DashAttnBwdArgs& a) {
+  auto enc = bwd_encode_fn();
+  if (!enc || (reinterpret_cast<uintptr_t>(base) & 15) != 0) return false;
+  const int64_t rows = (int64_t)a.n_seq * a.seq_len * a.n_heads;
+  if (rows <= 0 || rows >= ((int64_t)1 << 31)) return false;
+  cuuint64_t dims[2] = {128, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {256};
+  cuuint32_t box[2] = {64, 1};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, a.dtype == DASH_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                         2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 template <typename E>
 int launch_tc_typed(const DashAttnBwdArgs& a, int nblk, int words, float* dq_acc, cudaStream_t st) {
   const int64_t rows = (int64_t)a.n_seq * a.seq_len;
@@ -594,12 +650,16 @@ int launch_tc_typed(const DashAttnBwdArgs& a, int nblk, int words, float* dq_acc
   if (rc) return rc;
   const int ntiles = (a.seq_len + TK - 1) / TK;
   const dim3 grid((unsigned)(a.n_seq * ntiles), (unsigned)a.n_kv_heads);
+  CUtensorMap mq, mdo;
+  memset(&mq, 0, sizeof(mq));
+  memset(&mdo, 0, sizeof(mdo));
+  const int qmap = make_rows_map(&mq, a.q, a) && make_rows_map(&mdo, a.dout, a) ? 1 : 0;
   if (a.seg_start) {
     cudaFuncSetAttribute(bwd_tc_kernel<E, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_TC);
-    bwd_tc_kernel<E, true><<<grid, kTcThreads, SMEM_TC, st>>>(a, nblk, words, ntiles, dq_acc);
+    bwd_tc_kernel<E, true><<<grid, kTcThreads, SMEM_TC, st>>>(mq, mdo, a, nblk, words, ntiles, dq_acc, qmap);
   } else {
     cudaFuncSetAttribute(bwd_tc_kernel<E, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_TC);
-    bwd_tc_kernel<E, false><<<grid, kTcThreads, SMEM_TC, st>>>(a, nblk, words, ntiles, dq_acc);
+    bwd_tc_kernel<E, false><<<grid, kTcThreads, SMEM_TC, st>>>(mq, mdo, a, nblk, words, ntiles, dq_acc, qmap);
   }
   count_launch();
   rc = check_launch("bwd_tc_kernel");

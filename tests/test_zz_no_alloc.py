@@ -106,3 +106,34 @@ def test_noalloc_rejects_requests_beyond_the_fixed_scratch():
     rc = lib.dash_decode_attn_noalloc(C.byref(a), L.current_stream())
     assert rc == L.DASH_ERR_WORKSPACE
     assert "fixed" in L.last_error()
+
+
+def test_noalloc_decode_replays_in_a_cuda_graph():
+    """The documented serving pattern: one call on the device first (outside
+    any capture), then the call captured in a CUDA graph and replayed with new
+    queries written in place; each replay equals the workspace entry point on
+    the same queries."""
+    lib = L.load()
+    q, kc, vc, bt, sl, idx, bias, H, bs, lw = _problem()
+    out = torch.empty_like(q)
+    a = _decode_args(q, kc, vc, bt, sl, idx, bias, out, H, H, bs, lw, 0)
+    assert lib.dash_decode_attn_noalloc(C.byref(a), L.current_stream()) == L.DASH_OK, L.last_error()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        rc = lib.dash_decode_attn_noalloc(C.byref(a), L.current_stream())
+    assert rc == L.DASH_OK, L.last_error()
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    for _ in range(2):
+        q.copy_(torch.randn(q.shape, generator=gen, device="cuda").bfloat16())
+        out.fill_(float("nan"))
+        g.replay()
+        ref = torch.empty_like(q)
+        b = _decode_args(q, kc, vc, bt, sl, idx, bias, ref, H, H, bs, lw, 0)
+        need = lib.dash_decode_workspace_size(C.byref(b))
+        ws = torch.empty(max(need, 256), dtype=torch.uint8, device="cuda")
+        b.workspace, b.workspace_bytes = ws.data_ptr(), ws.numel()
+        assert lib.dash_decode_attn(C.byref(b), L.current_stream()) == L.DASH_OK, L.last_error()
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref), "graph replay differs from the workspace entry point"
+    del g
