@@ -128,7 +128,9 @@ __global__ void __launch_bounds__(kPlanWarps * 32) plan_kernel(DashPrefillArgs a
     const int lstart = pos0 + i - a.local_window + 1;
     // keep ids with a remote key for this row; drop later duplicates (the
     // validity test depends only on the id, so a duplicate of a dropped id is
-    // dropped by the same test)
+    // dropped by the same test).  The shuffle loops below visit the K live
+    // slots only: a slot j >= K holds -1, which is never kept and never
+    // matches or ranks below a kept id.
     bool keep[PER];
 #pragma unroll
     for (int q = 0; q < PER; ++q) {
@@ -138,7 +140,7 @@ __global__ void __launch_bounds__(kPlanWarps * 32) plan_kernel(DashPrefillArgs a
     }
 #pragma unroll
     for (int qs = 0; qs < PER; ++qs) {
-      for (int src = 0; src < 32; ++src) {
+      for (int src = 0; src < min(32, K - 32 * qs); ++src) {
         const int bu = __shfl_sync(0xffffffffu, b[qs], src);
         const int u = src + 32 * qs;
 #pragma unroll
@@ -153,7 +155,7 @@ __global__ void __launch_bounds__(kPlanWarps * 32) plan_kernel(DashPrefillArgs a
 #pragma unroll
     for (int qs = 0; qs < PER; ++qs) {
       const int key = keep[qs] ? b[qs] : INT_MAX;
-      for (int src = 0; src < 32; ++src) {
+      for (int src = 0; src < min(32, K - 32 * qs); ++src) {
         const int ku = __shfl_sync(0xffffffffu, key, src);
 #pragma unroll
         for (int q = 0; q < PER; ++q) rank[q] += ku < b[q] ? 1 : 0;
@@ -183,7 +185,7 @@ __global__ void __launch_bounds__(kPlanWarps * 32) plan_kernel(DashPrefillArgs a
 #pragma unroll
       for (int qs = 0; qs < PER; ++qs) {
         const int key = keep[qs] ? b[qs] : -2;
-        for (int src = 0; src < 32; ++src) {
+        for (int src = 0; src < min(32, K - 32 * qs); ++src) {
           const int ku = __shfl_sync(0xffffffffu, key, src);
           const float bu = __shfl_sync(0xffffffffu, bias[qs], src);
 #pragma unroll
@@ -199,7 +201,7 @@ __global__ void __launch_bounds__(kPlanWarps * 32) plan_kernel(DashPrefillArgs a
 #pragma unroll
       for (int qs = 0; qs < PER; ++qs) {
         const int key = lead[qs] ? (b[qs] >> 1) : INT_MAX;
-        for (int src = 0; src < 32; ++src) {
+        for (int src = 0; src < min(32, K - 32 * qs); ++src) {
           const int ku = __shfl_sync(0xffffffffu, key, src);
 #pragma unroll
           for (int q = 0; q < PER; ++q) prank[q] += ku < (b[q] >> 1) ? 1 : 0;
