@@ -697,15 +697,35 @@ __global__ void __launch_bounds__(256, 3) route_tile_kernel(const __grid_constan
     float acc[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) acc[k] = 0.0f;
-    for (int c4 = 0; c4 < 32; ++c4) {
-      const float4 q4 = *reinterpret_cast<const float4*>(qs + rr * kLd + 4 * c4);
+    // blocks warp + 8k of the chunk that exist (warp-uniform): a chunk past
+    // the tile's last block skips the rest
+    const int64_t dlast = bmax - cb0 - warp;
+    const int nk = dlast < 0 ? 0 : (int)min((int64_t)8, dlast / 8 + 1);
+    if (nk == 8) {
+      for (int c4 = 0; c4 < 32; ++c4) {
+        const float4 q4 = *reinterpret_cast<const float4*>(qs + rr * kLd + 4 * c4);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float4 k4 = *reinterpret_cast<const float4*>(kbs + (warp + 8 * k) * kKLd + 4 * c4);
-        acc[k] = __fmaf_rn(q4.x, k4.x, acc[k]);
-        acc[k] = __fmaf_rn(q4.y, k4.y, acc[k]);
-        acc[k] = __fmaf_rn(q4.z, k4.z, acc[k]);
-        acc[k] = __fmaf_rn(q4.w, k4.w, acc[k]);
+        for (int k = 0; k < 8; ++k) {
+          const float4 k4 = *reinterpret_cast<const float4*>(kbs + (warp + 8 * k) * kKLd + 4 * c4);
+          acc[k] = __fmaf_rn(q4.x, k4.x, acc[k]);
+          acc[k] = __fmaf_rn(q4.y, k4.y, acc[k]);
+          acc[k] = __fmaf_rn(q4.z, k4.z, acc[k]);
+          acc[k] = __fmaf_rn(q4.w, k4.w, acc[k]);
+        }
+      }
+    } else if (nk > 0) {
+      for (int c4 = 0; c4 < 32; ++c4) {
+        const float4 q4 = *reinterpret_cast<const float4*>(qs + rr * kLd + 4 * c4);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if (k < nk) {
+            const float4 k4 = *reinterpret_cast<const float4*>(kbs + (warp + 8 * k) * kKLd + 4 * c4);
+            acc[k] = __fmaf_rn(q4.x, k4.x, acc[k]);
+            acc[k] = __fmaf_rn(q4.y, k4.y, acc[k]);
+            acc[k] = __fmaf_rn(q4.z, k4.z, acc[k]);
+            acc[k] = __fmaf_rn(q4.w, k4.w, acc[k]);
+          }
+        }
       }
     }
 #pragma unroll
